@@ -1,0 +1,256 @@
+/*
+ * snl_b200.h - C ABI of the B200 (sm_100a) decode/prefill path of sensenova-loop.
+ *
+ * This library replaces the wgpu layer of the reference (src/gpu.rs) and the WGSL
+ * kernels it dispatches (src/shaders/{matmul,linear,attention,layers}.wgsl). Two
+ * levels are exported:
+ *
+ *   - Kernel level: one entry point per WGSL entry point, taking the same parameter
+ *     structs as the reference's uniforms (byte-identical to the #[repr(C)] structs of
+ *     src/engine.rs:24-82) plus device pointers and a cudaStream_t (passed as void*).
+ *     A caller such as src/vision.rs, which records Kernels::matmul itself, binds here.
+ *   - Engine level: an opaque snl_engine owning all device memory (weights, caches,
+ *     activations), with the methods of the reference's Engine (src/engine.rs:229-949).
+ *
+ * Conventions
+ *   - Every function returns 0 (SNL_OK) or a negative SNL_E_* code. The message of the
+ *     last failure on the calling thread is returned by snl_last_error().
+ *   - Device pointers are CUDA global-memory addresses on the current device; host
+ *     pointers are plain process memory. No function keeps a caller pointer after it
+ *     returns.
+ *   - An snl_engine is not thread-safe: one owner thread drives it (the reference's
+ *     Engine is !Sync and lives on the "generation" thread, src/worker.rs:76-106).
+ */
+#ifndef SNL_B200_H
+#define SNL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* The library is built with hidden visibility; everything declared here is exported. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* ---- codes ------------------------------------------------------------------ */
+
+/* Weight dtypes, in the order of weights.rs:25-30 (DType::{F32, Q8_0, Q4_0}). */
+enum { SNL_F32 = 0, SNL_Q8_0 = 1, SNL_Q4_0 = 2 };
+
+enum {
+  SNL_OK = 0,
+  SNL_E_INVALID = -1,     /* bad argument or unsupported request                  */
+  SNL_E_RANGE = -2,       /* token id / context / row out of range               */
+  SNL_E_CUDA = -3,        /* a CUDA runtime error                                */
+  SNL_E_OOM = -4,         /* device allocation failed                            */
+  SNL_E_STATE = -5,       /* call not valid in the engine's current state        */
+  SNL_E_TIMEOUT = -6,     /* a bounded device-side wait gave up                  */
+  SNL_E_UNSUPPORTED = -7, /* model configuration the kernels are not built for   */
+  SNL_E_NCCL = -8         /* a tensor-parallel collective failed                 */
+};
+
+/* ---- parameter structs (byte-identical to src/engine.rs) ---------------------- */
+
+/* StepU, src/engine.rs:24-32: rows in this step, first cache position, split-K
+ * parts of decode attention, and ckpt > 0 = save linear state after token ckpt-1. */
+typedef struct snl_step_u {
+  uint32_t m, pos0, parts, ckpt;
+} snl_step_u;
+
+/* MatP, src/engine.rs:34-45 (matmul.wgsl:18-27). Offsets/strides in floats. */
+typedef struct snl_mat_p {
+  uint32_t n, k, x_off, x_stride, y_off, y_stride, n_off, m_one;
+} snl_mat_p;
+
+/* LayerP, src/engine.rs:47-58 (layers.wgsl:154-163). */
+typedef struct snl_layer_p {
+  uint32_t h, mode, last_row;
+  float eps, weight_one;
+  uint32_t iterations, inter, x_stride;
+} snl_layer_p;
+
+/* AttnP, src/engine.rs:60-71 (attention.wgsl:17-29). */
+typedef struct snl_attn_p {
+  uint32_t n_heads, n_kv, rot_dim, proj_stride;
+  float rope_theta, eps, scale;
+  uint32_t mrope;
+} snl_attn_p;
+
+/* LinP, src/engine.rs:73-82 (linear.wgsl:13-22). */
+typedef struct snl_lin_p {
+  uint32_t conv_dim, proj_stride, n_k, n_v;
+  float eps;
+  uint32_t pad[3];
+} snl_lin_p;
+
+/* ModelConfig, src/config.rs:7-37 (text part). mhc_start < 0 means no mHC.
+ * full_attention[i] != 0 marks layer i as a gated full-attention layer. */
+#define SNL_MAX_LAYERS 256
+typedef struct snl_model_config {
+  uint32_t hidden, intermediate, vocab, n_layers;
+  uint8_t full_attention[SNL_MAX_LAYERS];
+  uint32_t n_heads, n_kv_heads, head_dim, rot_dim;
+  float rope_theta;
+  uint32_t mrope_section[3];
+  uint32_t lin_k_heads, lin_v_heads, lin_k_dim, lin_v_dim, conv_kernel;
+  float eps;
+  uint32_t loop_start, loop_end, loop_count;
+  int32_t mhc_start, mhc_end;
+  uint32_t mhc_streams, mhc_iterations;
+  uint32_t max_position;
+} snl_model_config;
+
+/* ---- errors ------------------------------------------------------------------ */
+
+/* Message of the last failed call on this thread ("" if none). Replaces the
+ * anyhow::bail! strings of engine.rs (e.g. "context length exceeded (a > b)"). */
+const char* snl_last_error(void);
+
+/* Library version string, and the number of kernel launches the library has issued
+ * on the calling process (a launch counter for measurement). */
+const char* snl_version(void);
+uint64_t snl_launch_count(void);
+
+/* ModelConfig::validate (src/config.rs:194-240). */
+int snl_config_validate(const snl_model_config* cfg);
+
+/* ---- kernel level: matmul.wgsl ------------------------------------------------ */
+
+/* y[m, y_off + m*y_stride + n_off + row] = sum_k x[x_off + m*x_stride + k] * W[row, k]
+ * for m < rows_m (m_one > 0 ? m_one : step->m). Replaces the 8 pipelines of
+ * Kernels::mat (src/gpu.rs:221-234, :377-382) with the MatKind choice of
+ * src/gpu.rs:211-218 made on the host. wq/ws are the reference layout
+ * (weights.rs:48-55): Q8_0 int8 [n, k] + f32 scales [n, k/32]; Q4_0 packed u32
+ * [n, k/8] + f32 scales [n, k/32]. */
+int snl_mat(int dtype, const snl_step_u* step, const snl_mat_p* p, const float* x, const void* wq,
+            const float* ws, float* y, void* stream);
+
+/* ---- kernel level: layers.wgsl ------------------------------------------------- */
+
+/* branch_norm (layers.wgsl:186-213): n_groups workgroups (step->m, or 1 for the
+ * final-row norm). x, coef, w, out as the WGSL bindings. */
+int snl_branch_norm(const snl_step_u* step, const snl_layer_p* p, const float* x, const float* coef,
+                    const float* w, float* out, uint32_t n_groups, void* stream);
+/* mhc_dots (layers.wgsl:215-232): grid (9, step->m); writes raw[m*9 + o]. */
+int snl_mhc_dots(const snl_step_u* step, const snl_layer_p* p, const float* x, const float* w,
+                 float* raw, void* stream);
+/* mhc_finish (layers.wgsl:234-266): coef[m*8 + 0..8] from raw and the router bias. */
+int snl_mhc_finish(const snl_step_u* step, const snl_layer_p* p, const float* raw, const float* w,
+                   float* coef, void* stream);
+/* merge (layers.wgsl:268-302): width = h; modes 0..3. */
+int snl_merge(const snl_step_u* step, const snl_layer_p* p, float* x, const float* coef,
+              const float* branch, void* stream);
+/* swiglu (layers.wgsl:304-315): act[m, i] = silu(gate_up[m, i]) * gate_up[m, I + i]. */
+int snl_swiglu(const snl_step_u* step, const snl_layer_p* p, const float* gate_up, float* act,
+               void* stream);
+
+/* ---- kernel level: attention.wgsl ---------------------------------------------- */
+
+/* prep (attention.wgsl:59-127): q/k RMSNorm(1+w), partial rotate-half M-RoPE, q to
+ * qbuf [m, n_heads*256], k/v as f16 pairs into the caches at position pos0+m.
+ * rpos is [m][4] u32 (t, h, w, 0). */
+int snl_attn_prep(const snl_step_u* step, const snl_attn_p* p, const float* proj, float* qbuf,
+                  uint32_t* kcache, uint32_t* vcache, const float* norms, const uint32_t* rpos,
+                  void* stream);
+/* attend (attention.wgsl:129-246): causal GQA (4 query heads per KV head) over the f16
+ * cache, split into step->parts parts. parts == 1: gated output to out [m, q_dim];
+ * otherwise partials [(m*n_heads + h)*parts + part][258] to partial. */
+int snl_attend(const snl_step_u* step, const snl_attn_p* p, const float* proj, const float* qbuf,
+               const uint32_t* kcache, const uint32_t* vcache, float* out, float* partial,
+               void* stream);
+/* combine (attention.wgsl:248-269): merge split-K partials and apply the gate. */
+int snl_attn_combine(const snl_step_u* step, const snl_attn_p* p, const float* proj,
+                     const float* partial, float* out, void* stream);
+
+/* ---- kernel level: linear.wgsl -------------------------------------------------- */
+
+/* conv (linear.wgsl:38-66): causal depthwise conv(4) + SiLU over the qkv channels of
+ * proj, carrying conv_state [3, conv_dim]; step->ckpt > 0 also saves the state after
+ * token ckpt-1 into conv_ckpt. lw = conv w [conv_dim*4] | A_log | dt_bias | norm. */
+int snl_conv(const snl_step_u* step, const snl_lin_p* p, const float* proj, float* conv_out,
+             float* conv_state, const float* lw, float* conv_ckpt, void* stream);
+/* delta (linear.wgsl:84-140): gated delta rule over the tokens of the step plus the
+ * gated RMSNorm; state [n_v, 128, 128] f32 (row i = key dim, column j = value dim). */
+int snl_delta(const snl_step_u* step, const snl_lin_p* p, const float* proj, const float* conv_out,
+              float* state, const float* lw, float* out, float* state_ckpt, void* stream);
+
+/* ---- kernel level: sampling ----------------------------------------------------- */
+
+/* Greedy argmax of each of `rows` rows of `n` logits (sampler.rs:169-177: the first
+ * maximum wins); out_idx is a device u32[rows]. */
+int snl_argmax(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_idx, void* stream);
+
+/* ---- engine level (src/engine.rs) ----------------------------------------------- */
+
+typedef struct snl_engine snl_engine;
+
+/* Engine::load without the file part (src/engine.rs:230-644): validate cfg, pick the
+ * device, record the configuration. Weights are then given tensor by tensor
+ * (snl_engine_set_tensor, the upload_q/upload_f of engine.rs:91-113) or generated
+ * (snl_engine_fill_synthetic), and snl_engine_finalize allocates caches and
+ * activations and builds the op graph. ctx is clamped to cfg->max_position.
+ * flags: SNL_ENGINE_MTP = also expect the MTP head tensors ("mtp.*"). */
+#define SNL_ENGINE_MTP 1u
+#define SNL_ENGINE_F16_SCALES 2u /* store fp16 block scales where every scale is fp16-exact */
+int snl_engine_create(const snl_model_config* cfg, size_t ctx, int device, uint32_t flags,
+                      snl_engine** out);
+
+/* One tensor of a .snl file (weights.rs:76-104 names and layout): dtype SNL_F32 with
+ * rows*cols floats in q (s unused), or Q8_0/Q4_0 with the packed quants in q and the
+ * f32 scales in s. Host pointers. */
+int snl_engine_set_tensor(snl_engine* e, const char* name, int dtype, size_t rows, size_t cols,
+                          const void* q, const void* s);
+
+/* Generate every tensor of the configuration from `seed` on the device (the seeded
+ * synthetic model of the benchmarks). quant = SNL_Q8_0 or SNL_Q4_0 for the projections
+ * that follow the file quantization (embed, lm_head, in_proj and the MTP head stay
+ * Q8_0, as convert.rs:232-234, :286-298, :205-226 lay them out). */
+int snl_engine_fill_synthetic(snl_engine* e, uint64_t seed, int quant);
+
+int snl_engine_finalize(snl_engine* e);
+void snl_engine_destroy(snl_engine* e);
+
+/* Engine::forward_mm (src/engine.rs:801-936). tokens[n]; pos = NULL (rotary position
+ * = cache position) or [n][3] u32; embeds = NULL or n_embeds rows of `hidden` floats
+ * replacing the embedding of token embed_idx[i]; logit_rows <= 2; ckpt only with n == 2.
+ * With logit_rows > 0, logits_out (host) receives logit_rows * vocab floats. */
+int snl_engine_forward_mm(snl_engine* e, const uint32_t* tokens, size_t n, const uint32_t* pos,
+                          const uint32_t* embed_idx, const float* embeds, size_t n_embeds,
+                          size_t logit_rows, int ckpt, float* logits_out);
+
+/* forward_mm followed by the greedy choice on the device: argmax_out (host) receives
+ * logit_rows token ids (sampler.rs:169-177), and only those cross to the host. */
+int snl_engine_forward_greedy(snl_engine* e, const uint32_t* tokens, size_t n, const uint32_t* pos,
+                              size_t logit_rows, int ckpt, uint32_t* argmax_out);
+
+/* Engine::mtp (src/engine.rs:708-774). With draft != 0, *draft_out = argmax of the
+ * MTP head's logits. Returns SNL_E_STATE when the engine has no MTP head. */
+int snl_engine_mtp(snl_engine* e, size_t r0, const uint32_t* tokens, size_t n, const uint32_t* pos,
+                   size_t slot0, int draft, uint32_t* draft_out);
+
+int snl_engine_reset(snl_engine* e);                             /* engine.rs:652-660 */
+int snl_engine_snapshot(snl_engine* e, size_t slot);             /* engine.rs:662-670 */
+int snl_engine_restore(snl_engine* e, size_t slot, size_t pos);  /* engine.rs:672-683 */
+int snl_engine_rollback(snl_engine* e);                          /* engine.rs:685-697 */
+size_t snl_engine_hid_rows(const snl_engine* e);                 /* engine.rs:699-702 */
+int snl_engine_has_mtp(const snl_engine* e);                     /* engine.rs:704-706 */
+size_t snl_engine_pos(const snl_engine* e);                      /* pub pos, engine.rs:185 */
+size_t snl_engine_ctx(const snl_engine* e);                      /* pub ctx, engine.rs:154 */
+/* Bytes of device memory the engine holds (Gpu::allocated, gpu.rs:17-18). */
+size_t snl_engine_device_bytes(const snl_engine* e);
+/* Copy `rows` rows of the last step's normed hidden states (row 0 = the token before
+ * the step) to host memory; for tests of the hidden-row bookkeeping. */
+int snl_engine_read_hidden(const snl_engine* e, size_t row0, size_t rows, float* out);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SNL_B200_H */

@@ -1,0 +1,314 @@
+// Gated GQA attention with partial M-RoPE over an f16 KV cache
+// (attention.wgsl: prep :59-127, attend :129-246, combine :248-269).
+//
+// Layouts are the reference's: proj rows hold per query head [q 256 | gate 256],
+// then k [n_kv*256], then v [n_kv*256]; the caches hold f16 pairs packed in u32,
+// cache[(pos * kv_dim + kh*256 + d) / 2]; split-K partials are
+// [(m*n_heads + h)*parts + part][256 acc | max | sum].
+#include "common.cuh"
+
+namespace snl {
+namespace {
+
+constexpr uint32_t HD = 256;
+constexpr uint32_t G = 4;  // query heads per KV head (config.rs:202)
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// prep: CTA (head slot, token), thread d = head dim. Slots [0, n_heads) queries,
+// [n_heads, n_heads+n_kv) keys, then values.
+__global__ void __launch_bounds__(256) prep_kernel(StepRef sr, snl_attn_p p, const float* __restrict__ proj,
+                                                   float* __restrict__ qbuf, uint32_t* __restrict__ kc,
+                                                   uint32_t* __restrict__ vc, const float* __restrict__ norms,
+                                                   const uint32_t* __restrict__ rpos) {
+  __shared__ float sh[HD];
+  __shared__ float red[32];
+  const snl_step_u st = load_step(sr);
+  const uint32_t slot = blockIdx.x, m = blockIdx.y, d = threadIdx.x;
+  if (m >= st.m) return;
+  const uint64_t pos = (uint64_t)st.pos0 + m;
+  const uint32_t q_dim = p.n_heads * HD, kv_dim = p.n_kv * HD;
+  const uint64_t row = (uint64_t)m * p.proj_stride;
+  if (slot >= p.n_heads + p.n_kv) {
+    const uint32_t kh = slot - p.n_heads - p.n_kv;
+    sh[d] = proj[row + 2 * q_dim + kv_dim + kh * HD + d];
+    __syncthreads();
+    if ((d & 1) == 0) vc[(pos * kv_dim + kh * HD + d) / 2] = pack_h2(sh[d], sh[d + 1]);
+    return;
+  }
+  const bool is_q = slot < p.n_heads;
+  float v = is_q ? proj[row + slot * 2 * HD + d] : proj[row + 2 * q_dim + (slot - p.n_heads) * HD + d];
+  const float total = block_sum(v * v, red);
+  v = v * rsqrtf(total / (float)HD + p.eps) * (1.0f + norms[(is_q ? 0 : HD) + d]);
+  sh[d] = v;
+  __syncthreads();
+  const uint32_t half_rot = p.rot_dim / 2;
+  if (d < p.rot_dim) {
+    const uint32_t fi = d % half_rot;
+    const float inv_freq = powf(p.rope_theta, -(float)(2 * fi) / (float)p.rot_dim);
+    const uint32_t* rp = rpos + 4 * m;
+    uint32_t rot_pos = rp[0];
+    if (fi % 3 == 1 && fi < (p.mrope >> 16)) rot_pos = rp[1];
+    else if (fi % 3 == 2 && fi < (p.mrope & 0xFFFFu)) rot_pos = rp[2];
+    float sn, cs;
+    sincosf((float)rot_pos * inv_freq, &sn, &cs);
+    v = d < half_rot ? v * cs - sh[d + half_rot] * sn : v * cs + sh[d - half_rot] * sn;
+  }
+  if (is_q) {
+    qbuf[(uint64_t)m * q_dim + slot * HD + d] = v;
+  } else {
+    __syncthreads();
+    sh[d] = v;
+    __syncthreads();
+    const uint32_t kh = slot - p.n_heads;
+    if ((d & 1) == 0) kc[(pos * kv_dim + kh * HD + d) / 2] = pack_h2(sh[d], sh[d + 1]);
+  }
+}
+
+// 32 per-lane values -> lane L holds the warp-wide sum of value L (butterfly
+// reduce-scatter, 31 shuffles).
+__device__ __forceinline__ float reduce_scatter32(float v[32], int lane) {
+#pragma unroll
+  for (int o = 16, n = 16; o > 0; o >>= 1, n >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < n; i++) {
+      const float send = up ? v[i] : v[i + n];
+      const float keep = up ? v[i + n] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  return v[0];
+}
+
+__device__ __forceinline__ void h8_to_f(const uint4 w, float f[8]) {
+  const __half2* h = reinterpret_cast<const __half2*>(&w);
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const float2 t = __half22float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+constexpr int kAttWarps = 8;
+constexpr int kKeysPerGroup = 8;
+
+// attend: CTA (KV head, token, part); 8 warps each take 8-key groups round-robin and
+// keep their own online softmax for the G = 4 query heads; lane l owns head dims
+// [8l, 8l+8). The warps' states are merged at the end.
+__global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, const float* __restrict__ proj,
+                                                     const float* __restrict__ qbuf, const uint32_t* __restrict__ kc,
+                                                     const uint32_t* __restrict__ vc, float* __restrict__ out,
+                                                     float* __restrict__ partial) {
+  __shared__ float s_acc[kAttWarps][G][HD];  // 32 KB
+  __shared__ float s_ml[kAttWarps][G][2];
+  __shared__ float s_p[kAttWarps][32];
+  const snl_step_u st = load_step(sr);
+  const uint32_t kh = blockIdx.x, m = blockIdx.y, part = blockIdx.z;
+  if (m >= st.m || part >= st.parts) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t q_dim = p.n_heads * HD, kv_dim = p.n_kv * HD;
+  const uint32_t total = st.pos0 + m + 1;
+  const uint32_t chunk = (total + st.parts - 1) / st.parts;
+  const uint32_t start = min(total, part * chunk);
+  const uint32_t end = min(total, start + chunk);
+
+  float q[G][8];
+#pragma unroll
+  for (int g = 0; g < (int)G; g++) {
+    const float4* qp = reinterpret_cast<const float4*>(qbuf + (uint64_t)m * q_dim + (kh * G + g) * HD + lane * 8);
+    const float4 a = qp[0], b = qp[1];
+    q[g][0] = a.x * p.scale; q[g][1] = a.y * p.scale; q[g][2] = a.z * p.scale; q[g][3] = a.w * p.scale;
+    q[g][4] = b.x * p.scale; q[g][5] = b.y * p.scale; q[g][6] = b.z * p.scale; q[g][7] = b.w * p.scale;
+  }
+  float acc[G][8];
+#pragma unroll
+  for (int g = 0; g < (int)G; g++)
+#pragma unroll
+    for (int e = 0; e < 8; e++) acc[g][e] = 0.f;
+  const int my_g = lane & 3;       // score lane -> (key lane/4, head lane%4)
+  float m_run = -1e30f, l_run = 0.f;  // for head my_g (replicated over lanes with that g)
+
+  const uint64_t kbase = (uint64_t)kh * HD;  // in halves
+  for (uint32_t t0 = start + warp * kKeysPerGroup; t0 < end; t0 += kAttWarps * kKeysPerGroup) {
+    const uint32_t nk = min((uint32_t)kKeysPerGroup, end - t0);
+    float part_s[32];
+#pragma unroll
+    for (int j = 0; j < kKeysPerGroup; j++) {
+      const uint32_t t = t0 + min((uint32_t)j, nk - 1);
+      const uint4 w = *reinterpret_cast<const uint4*>(kc + ((uint64_t)t * kv_dim + kbase) / 2 + lane * 4);
+      float k8[8];
+      h8_to_f(w, k8);
+#pragma unroll
+      for (int g = 0; g < (int)G; g++) {
+        float s = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; e++) s = fmaf(q[g][e], k8[e], s);
+        part_s[j * 4 + g] = s;
+      }
+    }
+    float sc = reduce_scatter32(part_s, lane);
+    const uint32_t my_key = lane >> 2;
+    if (my_key >= nk) sc = -1e30f;
+    float mx = sc;
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+    const float m_new = fmaxf(m_run, mx);
+    const float pe = my_key < nk ? __expf(sc - m_new) : 0.f;
+    float ls = pe;
+    ls += __shfl_xor_sync(0xffffffffu, ls, 4);
+    ls += __shfl_xor_sync(0xffffffffu, ls, 8);
+    ls += __shfl_xor_sync(0xffffffffu, ls, 16);
+    const float corr = __expf(m_run - m_new);
+    l_run = l_run * corr + ls;
+    m_run = m_new;
+    s_p[warp][lane] = pe;
+    float cg[G];
+#pragma unroll
+    for (int g = 0; g < (int)G; g++) cg[g] = __shfl_sync(0xffffffffu, corr, g);
+    __syncwarp();
+#pragma unroll
+    for (int g = 0; g < (int)G; g++)
+#pragma unroll
+      for (int e = 0; e < 8; e++) acc[g][e] *= cg[g];
+    for (uint32_t j = 0; j < nk; j++) {
+      const uint4 w = *reinterpret_cast<const uint4*>(vc + ((uint64_t)(t0 + j) * kv_dim + kbase) / 2 + lane * 4);
+      float v8[8];
+      h8_to_f(w, v8);
+      const float4 pj = *reinterpret_cast<const float4*>(&s_p[warp][j * 4]);
+      const float pg[G] = {pj.x, pj.y, pj.z, pj.w};
+#pragma unroll
+      for (int g = 0; g < (int)G; g++)
+#pragma unroll
+        for (int e = 0; e < 8; e++) acc[g][e] = fmaf(pg[g], v8[e], acc[g][e]);
+    }
+    __syncwarp();
+  }
+  // Publish this warp's state.
+#pragma unroll
+  for (int g = 0; g < (int)G; g++) {
+#pragma unroll
+    for (int e = 0; e < 8; e++) s_acc[warp][g][lane * 8 + e] = acc[g][e];
+  }
+  if (lane < (int)G) {
+    s_ml[warp][lane][0] = m_run;
+    s_ml[warp][lane][1] = l_run;
+  }
+  __syncthreads();
+  // Merge: thread d owns head dim d for the G heads.
+  const uint32_t d = threadIdx.x;
+#pragma unroll
+  for (int g = 0; g < (int)G; g++) {
+    float M = -1e30f;
+#pragma unroll
+    for (int w = 0; w < kAttWarps; w++) M = fmaxf(M, s_ml[w][g][0]);
+    float L = 0.f, A = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttWarps; w++) {
+      const float f = __expf(s_ml[w][g][0] - M);
+      L = fmaf(s_ml[w][g][1], f, L);
+      A = fmaf(s_acc[w][g][d], f, A);
+    }
+    const uint32_t h = kh * G + g;
+    if (st.parts == 1) {
+      const float gate = proj[(uint64_t)m * p.proj_stride + h * 2 * HD + HD + d];
+      out[(uint64_t)m * q_dim + h * HD + d] = A / L / (1.0f + __expf(-gate));
+    } else {
+      const uint64_t pi = ((uint64_t)m * p.n_heads + h) * st.parts + part;
+      partial[pi * (HD + 2) + d] = A;
+      if (d == 0) {
+        partial[pi * (HD + 2) + HD] = M;
+        partial[pi * (HD + 2) + HD + 1] = L;
+      }
+    }
+  }
+}
+
+// combine: CTA (head, token), thread = head dim.
+// skip_single: the step's attend already wrote `out` (parts == 1); used by captured
+// graphs, whose launch list is fixed while parts changes between replays.
+__global__ void __launch_bounds__(256) combine_kernel(StepRef sr, snl_attn_p p, const float* __restrict__ proj,
+                                                      const float* __restrict__ partial, float* __restrict__ out,
+                                                      int skip_single) {
+  const snl_step_u st = load_step(sr);
+  const uint32_t h = blockIdx.x, m = blockIdx.y, d = threadIdx.x;
+  if (m >= st.m || (skip_single && st.parts <= 1)) return;
+  const uint32_t q_dim = p.n_heads * HD;
+  const uint64_t base = ((uint64_t)m * p.n_heads + h) * st.parts;
+  float mx = -1e30f;
+  for (uint32_t i = 0; i < st.parts; i++) mx = fmaxf(mx, partial[(base + i) * (HD + 2) + HD]);
+  float l = 0.f, acc = 0.f;
+  for (uint32_t i = 0; i < st.parts; i++) {
+    const uint64_t o = (base + i) * (HD + 2);
+    const float f = __expf(partial[o + HD] - mx);
+    l = fmaf(partial[o + HD + 1], f, l);
+    acc = fmaf(partial[o + d], f, acc);
+  }
+  const float gate = proj[(uint64_t)m * p.proj_stride + h * 2 * HD + HD + d];
+  out[(uint64_t)m * q_dim + h * HD + d] = acc / l / (1.0f + __expf(-gate));
+}
+
+}  // namespace
+
+static int check_attn(const snl_attn_p& p) {
+  if (p.n_heads != G * p.n_kv || p.n_kv == 0) return fail(SNL_E_UNSUPPORTED, "attention: need 4 query heads per KV head");
+  if (p.rot_dim > HD || (p.rot_dim & 1) || p.rot_dim == 0) return fail(SNL_E_UNSUPPORTED, "attention: invalid rotary dim");
+  return SNL_OK;
+}
+
+int launch_attn_prep(StepRef st, const snl_attn_p& p, const float* proj, float* qbuf, uint32_t* kc, uint32_t* vc,
+                     const float* norms, const uint32_t* rpos, uint32_t m, cudaStream_t s) {
+  if (int rc = check_attn(p)) return rc;
+  if (m == 0) return SNL_OK;
+  prep_kernel<<<dim3(p.n_heads + 2 * p.n_kv, m), HD, 0, s>>>(st, p, proj, qbuf, kc, vc, norms, rpos);
+  SNL_LAUNCH_CHECK("attn_prep");
+  return SNL_OK;
+}
+
+int launch_attend(StepRef st, const snl_attn_p& p, const float* proj, const float* qbuf, const uint32_t* kc,
+                  const uint32_t* vc, float* out, float* partial, uint32_t m, uint32_t parts_grid, cudaStream_t s) {
+  if (int rc = check_attn(p)) return rc;
+  if (m == 0 || parts_grid == 0) return SNL_OK;
+  attend_kernel<<<dim3(p.n_kv, m, parts_grid), kAttWarps * 32, 0, s>>>(st, p, proj, qbuf, kc, vc, out, partial);
+  SNL_LAUNCH_CHECK("attend");
+  return SNL_OK;
+}
+
+int launch_attn_combine(StepRef st, const snl_attn_p& p, const float* proj, const float* partial, float* out,
+                        uint32_t m, cudaStream_t s, int skip_single) {
+  if (int rc = check_attn(p)) return rc;
+  if (m == 0) return SNL_OK;
+  combine_kernel<<<dim3(p.n_heads, m), HD, 0, s>>>(st, p, proj, partial, out, skip_single);
+  SNL_LAUNCH_CHECK("attn_combine");
+  return SNL_OK;
+}
+
+}  // namespace snl
+
+extern "C" int snl_attn_prep(const snl_step_u* step, const snl_attn_p* p, const float* proj, float* qbuf,
+                             uint32_t* kcache, uint32_t* vcache, const float* norms, const uint32_t* rpos,
+                             void* stream) {
+  if (!step || !p || !proj || !qbuf || !kcache || !vcache || !norms || !rpos)
+    return snl::fail(SNL_E_INVALID, "snl_attn_prep: null argument");
+  return snl::launch_attn_prep(snl::step_val(*step), *p, proj, qbuf, kcache, vcache, norms, rpos, step->m,
+                               (cudaStream_t)stream);
+}
+extern "C" int snl_attend(const snl_step_u* step, const snl_attn_p* p, const float* proj, const float* qbuf,
+                          const uint32_t* kcache, const uint32_t* vcache, float* out, float* partial, void* stream) {
+  if (!step || !p || !proj || !qbuf || !kcache || !vcache) return snl::fail(SNL_E_INVALID, "snl_attend: null argument");
+  if (step->parts == 0) return snl::fail(SNL_E_INVALID, "snl_attend: parts must be >= 1");
+  if (step->parts == 1 ? !out : !partial) return snl::fail(SNL_E_INVALID, "snl_attend: missing output buffer");
+  return snl::launch_attend(snl::step_val(*step), *p, proj, qbuf, kcache, vcache, out, partial, step->m, step->parts,
+                            (cudaStream_t)stream);
+}
+extern "C" int snl_attn_combine(const snl_step_u* step, const snl_attn_p* p, const float* proj, const float* partial,
+                                float* out, void* stream) {
+  if (!step || !p || !proj || !partial || !out) return snl::fail(SNL_E_INVALID, "snl_attn_combine: null argument");
+  if (step->parts == 0) return snl::fail(SNL_E_INVALID, "snl_attn_combine: parts must be >= 1");
+  return snl::launch_attn_combine(snl::step_val(*step), *p, proj, partial, out, step->m, (cudaStream_t)stream, 0);
+}

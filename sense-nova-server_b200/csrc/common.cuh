@@ -1,0 +1,117 @@
+// Shared definitions of the sm_100a kernels and the C ABI.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "snl_b200.h"
+
+namespace snl {
+
+// Error reporting: a thread-local message behind snl_last_error().
+void set_error(const std::string& msg);
+int fail(int code, const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what);
+void count_launch(uint64_t n = 1);
+
+#define SNL_CUDA_TRY(expr)                                       \
+  do {                                                           \
+    cudaError_t _e = (expr);                                     \
+    if (_e != cudaSuccess) return ::snl::cuda_fail(_e, #expr);   \
+  } while (0)
+
+// Checks the launch that was just issued and counts it.
+#define SNL_LAUNCH_CHECK(what)                                   \
+  do {                                                           \
+    cudaError_t _e = cudaGetLastError();                         \
+    if (_e != cudaSuccess) return ::snl::cuda_fail(_e, what);    \
+    ::snl::count_launch();                                       \
+  } while (0)
+
+// A step descriptor passed to kernels: either by value (kernel-level C ABI) or
+// through a device pointer (engine graphs, where pos0/parts change between replays
+// while the captured launch stays the same, like the reference's `step` uniform).
+struct StepRef {
+  const snl_step_u* dev;
+  snl_step_u val;
+};
+__device__ __forceinline__ snl_step_u load_step(const StepRef& s) {
+  if (s.dev) {
+    snl_step_u v;
+    v.m = s.dev->m;
+    v.pos0 = s.dev->pos0;
+    v.parts = s.dev->parts;
+    v.ckpt = s.dev->ckpt;
+    return v;
+  }
+  return s.val;
+}
+inline StepRef step_val(const snl_step_u& v) { return StepRef{nullptr, v}; }
+inline StepRef step_dev(const snl_step_u* d, const snl_step_u& host_copy) { return StepRef{d, host_copy}; }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide sum for blockDim.x a multiple of 32 (<= 1024); every thread gets the sum.
+__device__ __forceinline__ float block_sum(float v, float* sh32) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) sh32[wid] = v;
+  __syncthreads();
+  float t = lane < nw ? sh32[lane] : 0.f;
+  return warp_sum(t);
+}
+
+__device__ __forceinline__ float sigmoidf_(float v) { return 1.0f / (1.0f + __expf(-v)); }
+
+// 16-byte streaming load that does not allocate in L1 (weights are read once).
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// Launch helpers implemented per kernel family (internal, not part of the C ABI).
+int launch_mat(int dtype, StepRef st, const snl_mat_p& p, const float* x, const void* wq, const void* ws,
+               int scale_f16, float* y, cudaStream_t s, uint32_t rows_m_host);
+int launch_branch_norm(StepRef st, const snl_layer_p& p, const float* x, const float* coef, const float* w,
+                       float* out, uint32_t n_groups, cudaStream_t s);
+int launch_mhc_dots(StepRef st, const snl_layer_p& p, const float* x, const float* w, float* raw, uint32_t m,
+                    cudaStream_t s);
+int launch_mhc_finish(StepRef st, const snl_layer_p& p, const float* raw, const float* w, float* coef, uint32_t m,
+                      cudaStream_t s);
+int launch_merge(StepRef st, const snl_layer_p& p, float* x, const float* coef, const float* br, uint32_t m,
+                 cudaStream_t s);
+int launch_swiglu(StepRef st, const snl_layer_p& p, const float* gu, float* act, uint32_t m, cudaStream_t s);
+int launch_attn_prep(StepRef st, const snl_attn_p& p, const float* proj, float* qbuf, uint32_t* kc, uint32_t* vc,
+                     const float* norms, const uint32_t* rpos, uint32_t m, cudaStream_t s);
+int launch_attend(StepRef st, const snl_attn_p& p, const float* proj, const float* qbuf, const uint32_t* kc,
+                  const uint32_t* vc, float* out, float* partial, uint32_t m, uint32_t parts_grid, cudaStream_t s);
+int launch_attn_combine(StepRef st, const snl_attn_p& p, const float* proj, const float* partial, float* out,
+                        uint32_t m, cudaStream_t s, int skip_single);
+int launch_conv(StepRef st, const snl_lin_p& p, const float* proj, float* conv_out, float* conv_state,
+                const float* lw, float* conv_ckpt, cudaStream_t s);
+int launch_delta(StepRef st, const snl_lin_p& p, const float* proj, const float* conv_out, float* state,
+                 const float* lw, float* out, float* state_ckpt, cudaStream_t s);
+int launch_argmax(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_idx, cudaStream_t s);
+int launch_embed(const uint32_t* tokens, uint32_t m, const int8_t* q, const float* s_, uint32_t h, uint32_t vocab,
+                 float* x, int* err_flag, cudaStream_t s);
+int launch_gen_quant(uint64_t seed, const char* name, int dtype, size_t rows, size_t cols, void* q, float* s,
+                     cudaStream_t st);
+int launch_gen_f32(uint64_t seed, const char* name, uint32_t sub, size_t n, float mult, float offset, float* out,
+                   cudaStream_t st);
+
+}  // namespace snl

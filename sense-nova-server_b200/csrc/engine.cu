@@ -1,0 +1,829 @@
+// The engine: the reference's Engine (src/engine.rs) on one B200.
+//
+// It owns every device buffer (weights, KV caches, DeltaNet states, activations),
+// runs the op graph of engine.rs:383-493 in the same order, and keeps the same
+// bookkeeping (pos, hid rows, hlast, checkpoints, snapshots). Differences by design:
+//   * the embedding rows are dequantized on the device from token ids (the reference
+//     does it on the host and uploads x);
+//   * steps of 1 and 2 token rows (decode, speculative verify) are captured once into
+//     CUDA graphs that read the step descriptor from device memory, so a decode token
+//     is one graph launch plus a 4-byte (greedy) or vocab-float logits read-back;
+//   * greedy callers get the argmax on the device (snl_engine_forward_greedy).
+#include <algorithm>
+#include <atomic>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "synth.h"
+#include "synth_model.h"
+
+namespace snl {
+
+static thread_local std::string g_err;
+static std::atomic<uint64_t> g_launches{0};
+
+void set_error(const std::string& msg) { g_err = msg; }
+int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+int cuda_fail(cudaError_t e, const char* what) {
+  g_err = std::string(what) + ": " + cudaGetErrorString(e);
+  if (e == cudaErrorMemoryAllocation) return SNL_E_OOM;
+  return SNL_E_CUDA;
+}
+void count_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+int launch_argmax_with(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_idx, unsigned long long* part,
+                       cudaStream_t s);
+
+namespace {
+
+constexpr size_t MAX_M = 512;      // engine.rs:18
+constexpr size_t SNAPSHOTS = 4;    // engine.rs:20
+constexpr size_t LOGIT_ROWS = 2;   // engine.rs:22
+constexpr uint32_t MAX_PARTS = 64;  // engine.rs:827 clamp
+
+struct QT {
+  int dtype = 0;
+  size_t rows = 0, cols = 0;
+  void* q = nullptr;
+  void* s = nullptr;
+  int s_f16 = 0;
+};
+struct FT {
+  float* p = nullptr;
+  size_t n = 0;
+};
+
+uint32_t parts_for(size_t m, size_t total) {
+  // engine.rs:827: split-K attention only for short steps.
+  if (m > 4) return 1;
+  size_t p = (total + 255) / 256;
+  return (uint32_t)std::min<size_t>(std::max<size_t>(p, 1), MAX_PARTS);
+}
+
+}  // namespace
+}  // namespace snl
+
+struct snl_engine {
+  snl_model_config cfg;
+  size_t ctx = 0;
+  int device = 0;
+  uint32_t flags = 0;
+  bool has_mtp = false;
+  bool finalized = false;
+  cudaStream_t stream = nullptr;
+  std::map<std::string, snl::QT> qw;
+  std::map<std::string, snl::FT> fv;
+  std::vector<size_t> plan;
+  std::vector<void*> allocs;
+  size_t bytes = 0;
+
+  // activations (engine.rs:243-273)
+  float *x = nullptr, *xn = nullptr, *proj = nullptr, *act = nullptr, *attn_out = nullptr, *branch = nullptr,
+        *qbuf = nullptr, *coef = nullptr, *partial = nullptr, *logits = nullptr, *hid = nullptr, *hlast = nullptr,
+        *mhc_raw = nullptr;
+  uint32_t *rpos = nullptr, *tokens = nullptr, *amax = nullptr;
+  unsigned long long* amax_part = nullptr;
+  snl_step_u *step_d = nullptr, *mstep_d = nullptr;
+  // caches (engine.rs:275-297)
+  float *lin_state = nullptr, *conv_state = nullptr, *lin_ckpt = nullptr, *conv_ckpt = nullptr;
+  size_t state_elems = 0, conv_elems = 0, n_lin = 0, n_full = 0;
+  std::vector<uint32_t*> kc, vc;
+  std::vector<float*> snap_lin, snap_conv, snap_h;
+  // MTP (engine.rs:495-580)
+  float *mx = nullptr, *hn = nullptr, *m_logits = nullptr;
+  uint32_t *m_kc = nullptr, *m_vc = nullptr;
+  // pinned host staging
+  uint32_t* h_tokens = nullptr;
+  uint32_t* h_rpos = nullptr;
+  snl_step_u* h_step = nullptr;
+  float* h_logits = nullptr;
+  uint32_t* h_amax = nullptr;
+
+  size_t pos = 0, hid_rows = 0, head_rows = 1;
+  // captured step graphs keyed by (m, head rows, ckpt, greedy)
+  struct Graph {
+    cudaGraphExec_t exec = nullptr;
+    uint64_t launches = 0;
+  };
+  std::map<uint32_t, Graph> graphs;
+  bool use_graphs = true;
+
+  size_t h() const { return cfg.hidden; }
+};
+
+namespace snl {
+namespace {
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+template <class T>
+int dalloc(snl_engine* e, T** p, size_t count) {
+  void* ptr = nullptr;
+  const size_t nbytes = std::max<size_t>(count * sizeof(T), 256);
+  cudaError_t err = cudaMalloc(&ptr, nbytes);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaMalloc");
+  err = cudaMemsetAsync(ptr, 0, nbytes, e->stream);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaMemsetAsync");
+  e->allocs.push_back(ptr);
+  e->bytes += nbytes;
+  *p = static_cast<T*>(ptr);
+  return SNL_OK;
+}
+
+snl_layer_p layer_p(const snl_engine* e, uint32_t mode, bool last_row) {
+  snl_layer_p p;
+  p.h = e->cfg.hidden;
+  p.mode = mode;
+  p.last_row = last_row ? 1 : 0;
+  p.eps = e->cfg.eps;
+  p.weight_one = 1.0f;
+  p.iterations = e->cfg.mhc_start >= 0 ? e->cfg.mhc_iterations : 0;
+  p.inter = e->cfg.intermediate;
+  p.x_stride = 0;
+  return p;
+}
+
+snl_attn_p attn_p(const snl_engine* e) {
+  snl_attn_p a;
+  a.n_heads = e->cfg.n_heads;
+  a.n_kv = e->cfg.n_kv_heads;
+  a.rot_dim = e->cfg.rot_dim;
+  a.proj_stride = (uint32_t)snl_synth::attn_proj_rows(e->cfg);
+  a.rope_theta = e->cfg.rope_theta;
+  a.eps = e->cfg.eps;
+  a.scale = 1.0f / sqrtf((float)e->cfg.head_dim);
+  a.mrope = ((3 * e->cfg.mrope_section[1]) << 16) | (3 * e->cfg.mrope_section[2]);
+  return a;
+}
+
+snl_lin_p lin_p(const snl_engine* e) {
+  snl_lin_p l;
+  l.conv_dim = (uint32_t)snl_synth::conv_dim(e->cfg);
+  l.proj_stride = (uint32_t)snl_synth::lin_proj_rows(e->cfg);
+  l.n_k = e->cfg.lin_k_heads;
+  l.n_v = e->cfg.lin_v_heads;
+  l.eps = e->cfg.eps;
+  l.pad[0] = l.pad[1] = l.pad[2] = 0;
+  return l;
+}
+
+const QT* find_q(const snl_engine* e, const std::string& n) {
+  auto it = e->qw.find(n);
+  return it == e->qw.end() ? nullptr : &it->second;
+}
+const float* find_f(const snl_engine* e, const std::string& n) {
+  auto it = e->fv.find(n);
+  return it == e->fv.end() ? nullptr : it->second.p;
+}
+
+// One matrix op (engine.rs:336-363): y[r, y_stride] for rows_m token rows.
+int mat(snl_engine* e, StepRef st, const QT& w, const float* x, size_t x_stride, float* y, size_t y_stride,
+        uint32_t rows_m, uint32_t m_one = 0, uint32_t x_off = 0) {
+  snl_mat_p p;
+  p.n = (uint32_t)w.rows;
+  p.k = (uint32_t)w.cols;
+  p.x_off = x_off;
+  p.x_stride = (uint32_t)x_stride;
+  p.y_off = 0;
+  p.y_stride = (uint32_t)y_stride;
+  p.n_off = 0;
+  p.m_one = m_one;
+  return launch_mat(w.dtype, st, p, x, w.q, w.s, w.s_f16, y, e->stream, rows_m);
+}
+
+#define SNL_TRY(expr)          \
+  do {                         \
+    int _rc = (expr);          \
+    if (_rc) return _rc;       \
+  } while (0)
+
+int push_norm(snl_engine* e, StepRef st, uint32_t m, const float* router, const float* norm_w) {
+  if (router) {
+    snl_layer_p p0 = layer_p(e, 0, false);
+    SNL_TRY(launch_mhc_dots(st, p0, e->x, router, e->mhc_raw, m, e->stream));
+    SNL_TRY(launch_mhc_finish(st, p0, e->mhc_raw, router, e->coef, m, e->stream));
+  }
+  snl_layer_p p = layer_p(e, router ? 1 : 0, false);
+  return launch_branch_norm(st, p, e->x, e->coef, norm_w, e->xn, m, e->stream);
+}
+
+// The layer loop of engine.rs:389-481 for one step of m rows.
+int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
+  const auto& c = e->cfg;
+  const size_t h = c.hidden;
+  size_t lin_slot = 0, full_slot = 0;
+  const snl_attn_p ap = attn_p(e);
+  const snl_lin_p lp = lin_p(e);
+  for (size_t li : e->plan) {
+    const std::string L = "l" + std::to_string(li) + ".";
+    const bool mhc = snl_synth::is_mhc(c, li);
+    if (mhc && (int32_t)li == c.mhc_start) SNL_TRY(launch_merge(st, layer_p(e, 3, false), e->x, e->coef, e->branch, m, e->stream));
+    SNL_TRY(push_norm(e, st, m, mhc ? find_f(e, L + "mhc_attn") : nullptr, find_f(e, L + "in_ln")));
+    if (c.full_attention[li]) {
+      SNL_TRY(mat(e, st, *find_q(e, L + "qkv"), e->xn, h, e->proj, ap.proj_stride, m));
+      SNL_TRY(launch_attn_prep(st, ap, e->proj, e->qbuf, e->kc[full_slot], e->vc[full_slot], find_f(e, L + "qk_norm"),
+                               e->rpos, m, e->stream));
+      SNL_TRY(launch_attend(st, ap, e->proj, e->qbuf, e->kc[full_slot], e->vc[full_slot], e->attn_out, e->partial, m,
+                            parts_grid, e->stream));
+      if (parts_grid > 1) SNL_TRY(launch_attn_combine(st, ap, e->proj, e->partial, e->attn_out, m, e->stream, 1));
+      SNL_TRY(mat(e, st, *find_q(e, L + "o_proj"), e->attn_out, snl_synth::q_dim(c), e->branch, h, m));
+      full_slot++;
+    } else {
+      SNL_TRY(mat(e, st, *find_q(e, L + "in_proj"), e->xn, h, e->proj, lp.proj_stride, m));
+      float* cs = e->conv_state + lin_slot * e->conv_elems;
+      float* ss = e->lin_state + lin_slot * e->state_elems;
+      float* cc = e->conv_ckpt + lin_slot * e->conv_elems;
+      float* sc = e->lin_ckpt + lin_slot * e->state_elems;
+      const float* lw = find_f(e, L + "lin");
+      SNL_TRY(launch_conv(st, lp, e->proj, e->act, cs, lw, cc, e->stream));
+      SNL_TRY(launch_delta(st, lp, e->proj, e->act, ss, lw, e->attn_out, sc, e->stream));
+      SNL_TRY(mat(e, st, *find_q(e, L + "out_proj"), e->attn_out, snl_synth::lin_value_dim(c), e->branch, h, m));
+      lin_slot++;
+    }
+    SNL_TRY(launch_merge(st, layer_p(e, mhc ? 1 : 0, false), e->x, e->coef, e->branch, m, e->stream));
+    SNL_TRY(push_norm(e, st, m, mhc ? find_f(e, L + "mhc_ffn") : nullptr, find_f(e, L + "post_ln")));
+    SNL_TRY(mat(e, st, *find_q(e, L + "gate_up"), e->xn, h, e->proj, 2 * (size_t)c.intermediate, m));
+    SNL_TRY(launch_swiglu(st, layer_p(e, 0, false), e->proj, e->act, m, e->stream));
+    SNL_TRY(mat(e, st, *find_q(e, L + "down"), e->act, c.intermediate, e->branch, h, m));
+    const uint32_t mode = !mhc ? 0 : ((int32_t)(li + 1) == c.mhc_end ? 2 : 1);
+    SNL_TRY(launch_merge(st, layer_p(e, mode, false), e->x, e->coef, e->branch, m, e->stream));
+  }
+  return SNL_OK;
+}
+
+// Everything a step does on the device after its inputs (tokens, rpos, step) are
+// resident: embedding, layers, final norm, optional head and argmax, hlast update.
+int device_step(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid, uint32_t rows, bool greedy) {
+  const size_t h = e->h();
+  const QT* emb = find_q(e, "embed");
+  SNL_TRY(launch_embed(e->tokens, m, (const int8_t*)emb->q, (const float*)emb->s, (uint32_t)h, e->cfg.vocab, e->x,
+                       nullptr, e->stream));
+  // Row 0 of hid is the hidden state of the token before this step (engine.rs:889-890).
+  SNL_CUDA_TRY(cudaMemcpyAsync(e->hid, e->hlast, h * sizeof(float), cudaMemcpyDeviceToDevice, e->stream));
+  SNL_TRY(run_layers(e, st, m, parts_grid));
+  SNL_TRY(launch_branch_norm(st, layer_p(e, 0, false), e->x, e->coef, find_f(e, "norm"), e->hid + h, m, e->stream));
+  if (rows > 0) {
+    SNL_TRY(mat(e, st, *find_q(e, "lm_head"), e->hid, h, e->logits, e->cfg.vocab, rows, rows,
+                (uint32_t)((m - rows + 1) * h)));
+    if (greedy) SNL_TRY(launch_argmax_with(e->logits, rows, e->cfg.vocab, e->amax, e->amax_part, e->stream));
+  }
+  SNL_CUDA_TRY(cudaMemcpyAsync(e->hlast, e->hid + (size_t)m * h, h * sizeof(float), cudaMemcpyDeviceToDevice, e->stream));
+  return SNL_OK;
+}
+
+// Run one step, through a captured graph for m <= 2.
+int run_step(snl_engine* e, const snl_step_u& sh, uint32_t m, uint32_t rows, bool greedy) {
+  StepRef st = step_dev(e->step_d, sh);
+  const bool graphable = e->use_graphs && m <= 2;
+  if (!graphable) {
+    const uint32_t parts_grid = sh.parts;
+    return device_step(e, st, m, parts_grid, rows, greedy);
+  }
+  const uint32_t key = (m << 8) | (rows << 4) | ((sh.ckpt ? 1u : 0u) << 1) | (greedy ? 1u : 0u);
+  auto it = e->graphs.find(key);
+  if (it == e->graphs.end()) {
+    const uint64_t before = g_launches.load();
+    SNL_CUDA_TRY(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = device_step(e, st, m, MAX_PARTS, rows, greedy);
+    cudaGraph_t graph = nullptr;
+    cudaError_t ce = cudaStreamEndCapture(e->stream, &graph);
+    if (rc) {
+      if (graph) cudaGraphDestroy(graph);
+      return rc;
+    }
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamEndCapture");
+    snl_engine::Graph g;
+    ce = cudaGraphInstantiate(&g.exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaGraphInstantiate");
+    g.launches = g_launches.load() - before;
+    g_launches.fetch_sub(g.launches);  // captured, not executed
+    it = e->graphs.emplace(key, g).first;
+  }
+  SNL_CUDA_TRY(cudaGraphLaunch(it->second.exec, e->stream));
+  count_launch(it->second.launches);
+  return SNL_OK;
+}
+
+int check_tokens(const snl_engine* e, const uint32_t* toks, size_t n) {
+  for (size_t i = 0; i < n; i++)
+    if (toks[i] >= e->cfg.vocab) return fail(SNL_E_RANGE, "token id " + std::to_string(toks[i]) + " out of range");
+  return SNL_OK;
+}
+
+// forward_mm (engine.rs:801-936), leaving the logits (or the argmax) on the device.
+int forward_impl(snl_engine* e, const uint32_t* tokens, size_t n, const uint32_t* pos3, const uint32_t* embed_idx,
+                 const float* embeds, size_t n_embeds, size_t logit_rows, int ckpt, bool greedy, size_t* rows_out) {
+  if (!e->finalized) return fail(SNL_E_STATE, "engine not finalized");
+  if (logit_rows > LOGIT_ROWS || (ckpt && n != 2)) return fail(SNL_E_INVALID, "forward: unsupported logits or checkpoint request");
+  if (n == 0 || !tokens) return fail(SNL_E_INVALID, "forward called with no tokens");
+  for (size_t i = 0; i < n_embeds; i++)
+    if (embed_idx[i] >= n) return fail(SNL_E_INVALID, "forward: positions or embeddings do not match the tokens");
+  if (e->pos + n > e->ctx)
+    return fail(SNL_E_RANGE, "context length exceeded (" + std::to_string(e->pos + n) + " > " + std::to_string(e->ctx) + ")");
+  SNL_TRY(check_tokens(e, tokens, n));
+  const size_t h = e->h();
+  const size_t chunk = MAX_M;
+  const size_t n_chunks = (n + chunk - 1) / chunk;
+  *rows_out = 0;
+  for (size_t ci = 0; ci < n_chunks; ci++) {
+    const bool last = ci + 1 == n_chunks;
+    const size_t c0 = ci * chunk;
+    const size_t m = std::min(chunk, n - c0);
+    const size_t total = e->pos + m;
+    snl_step_u sh = {(uint32_t)m, (uint32_t)e->pos, parts_for(m, total), (uint32_t)(ckpt ? 1 : 0)};
+    const size_t rows = (last && logit_rows > 0) ? std::min(logit_rows, m) : 0;
+    if (rows) e->head_rows = rows;
+    // Stage the step inputs through pinned memory.
+    *e->h_step = sh;
+    memcpy(e->h_tokens, tokens + c0, m * sizeof(uint32_t));
+    for (size_t i = 0; i < m; i++)
+      for (int k = 0; k < 4; k++)
+        e->h_rpos[i * 4 + k] = pos3 ? (k < 3 ? pos3[(c0 + i) * 3 + k] : 0u) : (uint32_t)(e->pos + i);
+    SNL_CUDA_TRY(cudaMemcpyAsync(e->step_d, e->h_step, sizeof(snl_step_u), cudaMemcpyHostToDevice, e->stream));
+    SNL_CUDA_TRY(cudaMemcpyAsync(e->tokens, e->h_tokens, m * sizeof(uint32_t), cudaMemcpyHostToDevice, e->stream));
+    SNL_CUDA_TRY(cudaMemcpyAsync(e->rpos, e->h_rpos, m * 4 * sizeof(uint32_t), cudaMemcpyHostToDevice, e->stream));
+    bool has_embeds = false;
+    for (size_t i = 0; i < n_embeds; i++) has_embeds |= embed_idx[i] >= c0 && embed_idx[i] < c0 + m;
+    if (has_embeds) {
+      // Vision features replace embedding rows: run the embedding first, then
+      // overwrite, outside any graph.
+      StepRef st = step_dev(e->step_d, sh);
+      const QT* emb = find_q(e, "embed");
+      SNL_TRY(launch_embed(e->tokens, (uint32_t)m, (const int8_t*)emb->q, (const float*)emb->s, (uint32_t)h,
+                           e->cfg.vocab, e->x, nullptr, e->stream));
+      for (size_t i = 0; i < n_embeds; i++) {
+        const size_t r = embed_idx[i];
+        if (r < c0 || r >= c0 + m) continue;
+        SNL_CUDA_TRY(cudaMemcpyAsync(e->x + (r - c0) * 2 * h, embeds + i * h, h * sizeof(float), cudaMemcpyHostToDevice,
+                                     e->stream));
+      }
+      SNL_CUDA_TRY(cudaMemcpyAsync(e->hid, e->hlast, h * sizeof(float), cudaMemcpyDeviceToDevice, e->stream));
+      SNL_TRY(run_layers(e, st, (uint32_t)m, sh.parts));
+      SNL_TRY(launch_branch_norm(st, layer_p(e, 0, false), e->x, e->coef, find_f(e, "norm"), e->hid + h, (uint32_t)m,
+                                 e->stream));
+      if (rows) {
+        SNL_TRY(mat(e, st, *find_q(e, "lm_head"), e->hid, h, e->logits, e->cfg.vocab, (uint32_t)rows, (uint32_t)rows,
+                    (uint32_t)((m - rows + 1) * h)));
+        if (greedy) SNL_TRY(launch_argmax_with(e->logits, (uint32_t)rows, e->cfg.vocab, e->amax, e->amax_part, e->stream));
+      }
+      SNL_CUDA_TRY(cudaMemcpyAsync(e->hlast, e->hid + m * h, h * sizeof(float), cudaMemcpyDeviceToDevice, e->stream));
+    } else {
+      SNL_TRY(run_step(e, sh, (uint32_t)m, (uint32_t)rows, greedy));
+    }
+    if (!last) SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));  // pinned staging is reused by the next chunk
+    e->pos += m;
+    e->hid_rows = m;
+    if (rows) *rows_out = rows;
+  }
+  return SNL_OK;
+}
+
+}  // namespace
+}  // namespace snl
+
+using namespace snl;
+
+// ---------------------------------------------------------------------------
+// C ABI: errors, config
+// ---------------------------------------------------------------------------
+
+extern "C" const char* snl_last_error(void) { return snl::g_err.c_str(); }
+extern "C" const char* snl_version(void) { return "snl_b200 0.1 (sm_100a)"; }
+extern "C" uint64_t snl_launch_count(void) { return snl::g_launches.load(); }
+
+extern "C" int snl_config_validate(const snl_model_config* c) {
+  if (!c) return fail(SNL_E_INVALID, "null config");
+  // ModelConfig::validate (config.rs:194-240)
+  if (c->head_dim != 256) return fail(SNL_E_UNSUPPORTED, "unsupported model configuration: head_dim must be 256");
+  if (c->lin_k_dim != 128 || c->lin_v_dim != 128)
+    return fail(SNL_E_UNSUPPORTED, "unsupported model configuration: linear head dims must be 128");
+  if (c->conv_kernel != 4) return fail(SNL_E_UNSUPPORTED, "unsupported model configuration: linear conv kernel must be 4");
+  if (c->hidden == 0 || c->hidden % 256)
+    return fail(SNL_E_UNSUPPORTED, "unsupported model configuration: hidden size must be a multiple of 256");
+  if (c->n_layers == 0 || c->n_layers > SNL_MAX_LAYERS)
+    return fail(SNL_E_UNSUPPORTED, "unsupported model configuration: layer_types length mismatch");
+  if (c->n_kv_heads == 0 || c->n_heads != 4 * c->n_kv_heads)
+    return fail(SNL_E_UNSUPPORTED, "unsupported model configuration: attention must have 4 query heads per KV head");
+  if (c->lin_k_heads == 0 || c->lin_v_heads % c->lin_k_heads)
+    return fail(SNL_E_UNSUPPORTED, "unsupported model configuration: linear value heads must be a multiple of key heads");
+  if (c->rot_dim % 2 || c->rot_dim > c->head_dim || c->rot_dim == 0)
+    return fail(SNL_E_UNSUPPORTED, "unsupported model configuration: invalid rotary dim");
+  if (c->mrope_section[0] + c->mrope_section[1] + c->mrope_section[2] != c->rot_dim / 2)
+    return fail(SNL_E_UNSUPPORTED, "unsupported model configuration: M-RoPE sections must cover the rotary dims");
+  if (!(c->loop_start < c->loop_end && c->loop_end <= c->n_layers && c->loop_count >= 1))
+    return fail(SNL_E_UNSUPPORTED, "unsupported model configuration: invalid loop range");
+  if (c->intermediate == 0 || c->intermediate % 32 || c->vocab == 0)
+    return fail(SNL_E_UNSUPPORTED, "unsupported model configuration: intermediate/vocab");
+  if (c->mhc_start >= 0) {
+    if (c->mhc_streams != 2)
+      return fail(SNL_E_UNSUPPORTED, "unsupported model configuration: only 2 mHC streams are supported");
+    auto inside = [&](uint32_t a, uint32_t b) { return a <= (uint32_t)c->mhc_start && (uint32_t)c->mhc_end <= b; };
+    if (!(inside(0, c->loop_start) || inside(c->loop_start, c->loop_end) || inside(c->loop_end, c->n_layers)))
+      return fail(SNL_E_UNSUPPORTED, "mHC range crosses a loop boundary");
+  }
+  return SNL_OK;
+}
+
+// ---------------------------------------------------------------------------
+// C ABI: engine
+// ---------------------------------------------------------------------------
+
+extern "C" int snl_engine_create(const snl_model_config* cfg, size_t ctx, int device, uint32_t flags, snl_engine** out) {
+  if (!out) return fail(SNL_E_INVALID, "snl_engine_create: null out");
+  *out = nullptr;
+  if (int rc = snl_config_validate(cfg)) return rc;
+  int ndev = 0;
+  cudaError_t ce = cudaGetDeviceCount(&ndev);
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaGetDeviceCount");
+  if (device < 0 || device >= ndev) return fail(SNL_E_INVALID, "snl_engine_create: no such device");
+  DeviceGuard dg(device);
+  snl_engine* e = new snl_engine();
+  e->cfg = *cfg;
+  e->ctx = std::min<size_t>(ctx, cfg->max_position);
+  e->device = device;
+  e->flags = flags;
+  e->has_mtp = (flags & SNL_ENGINE_MTP) != 0;
+  if (getenv("SNL_NO_GRAPHS")) e->use_graphs = false;
+  ce = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
+  if (ce != cudaSuccess) {
+    delete e;
+    return cuda_fail(ce, "cudaStreamCreate");
+  }
+  const auto& c = e->cfg;
+  for (size_t i = 0; i < c.loop_start; i++) e->plan.push_back(i);
+  for (size_t r = 0; r < c.loop_count; r++)
+    for (size_t i = c.loop_start; i < c.loop_end; i++) e->plan.push_back(i);
+  for (size_t i = c.loop_end; i < c.n_layers; i++) e->plan.push_back(i);
+  *out = e;
+  return SNL_OK;
+}
+
+static int store_q(snl_engine* e, const std::string& name, int dtype, size_t rows, size_t cols) {
+  snl::QT t;
+  t.dtype = dtype;
+  t.rows = rows;
+  t.cols = cols;
+  const size_t n = rows * cols;
+  const size_t qbytes = dtype == SNL_Q8_0 ? n : n / 2;
+  void* q = nullptr;
+  float* s = nullptr;
+  SNL_TRY(dalloc(e, (uint8_t**)&q, qbytes));
+  SNL_TRY(dalloc(e, &s, n / 32));
+  t.q = q;
+  t.s = s;
+  e->qw[name] = t;
+  return SNL_OK;
+}
+
+extern "C" int snl_engine_set_tensor(snl_engine* e, const char* name, int dtype, size_t rows, size_t cols, const void* q,
+                                     const void* s) {
+  if (!e || !name || !q) return fail(SNL_E_INVALID, "snl_engine_set_tensor: null argument");
+  if (e->finalized) return fail(SNL_E_STATE, "snl_engine_set_tensor: engine already finalized");
+  DeviceGuard dg(e->device);
+  const std::string nm(name);
+  if (dtype == SNL_F32) {
+    snl::FT f;
+    f.n = rows * cols;
+    SNL_TRY(dalloc(e, &f.p, f.n));
+    SNL_CUDA_TRY(cudaMemcpyAsync(f.p, q, f.n * sizeof(float), cudaMemcpyHostToDevice, e->stream));
+    e->fv[nm] = f;
+  } else if (dtype == SNL_Q8_0 || dtype == SNL_Q4_0) {
+    if (!s) return fail(SNL_E_INVALID, "snl_engine_set_tensor: quantized tensor without scales");
+    if (cols % 32) return fail(SNL_E_INVALID, std::string(name) + ": columns not divisible by 32");
+    SNL_TRY(store_q(e, nm, dtype, rows, cols));
+    const snl::QT& t = e->qw[nm];
+    const size_t n = rows * cols;
+    SNL_CUDA_TRY(cudaMemcpyAsync(t.q, q, dtype == SNL_Q8_0 ? n : n / 2, cudaMemcpyHostToDevice, e->stream));
+    SNL_CUDA_TRY(cudaMemcpyAsync(t.s, s, n / 32 * sizeof(float), cudaMemcpyHostToDevice, e->stream));
+  } else {
+    return fail(SNL_E_INVALID, "snl_engine_set_tensor: unknown dtype");
+  }
+  SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));  // host buffers may go away after return
+  return SNL_OK;
+}
+
+extern "C" int snl_engine_fill_synthetic(snl_engine* e, uint64_t seed, int quant) {
+  if (!e) return fail(SNL_E_INVALID, "null engine");
+  if (e->finalized) return fail(SNL_E_STATE, "snl_engine_fill_synthetic: engine already finalized");
+  if (quant != SNL_Q8_0 && quant != SNL_Q4_0) return fail(SNL_E_INVALID, "snl_engine_fill_synthetic: quant");
+  DeviceGuard dg(e->device);
+  int rc = SNL_OK;
+  snl_synth::for_each_tensor(
+      e->cfg, e->has_mtp, quant,
+      [&](const std::string& name, int dtype, size_t rows, size_t cols) {
+        if (rc) return;
+        rc = store_q(e, name, dtype, rows, cols);
+        if (rc) return;
+        const snl::QT& t = e->qw[name];
+        rc = launch_gen_quant(seed, name.c_str(), dtype, rows, cols, t.q, (float*)t.s, e->stream);
+      },
+      [&](const std::string& name, const snl_synth::Seg* segs, int nseg) {
+        if (rc) return;
+        snl::FT f;
+        for (int i = 0; i < nseg; i++) f.n += segs[i].n;
+        rc = dalloc(e, &f.p, f.n);
+        if (rc) return;
+        size_t off = 0;
+        for (int i = 0; i < nseg && !rc; i++) {
+          rc = launch_gen_f32(seed, name.c_str(), segs[i].sub, segs[i].n, segs[i].mult, segs[i].offset, f.p + off,
+                              e->stream);
+          off += segs[i].n;
+        }
+        e->fv[name] = f;
+      });
+  if (rc) return rc;
+  SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));
+  return SNL_OK;
+}
+
+extern "C" int snl_engine_finalize(snl_engine* e) {
+  if (!e) return fail(SNL_E_INVALID, "null engine");
+  if (e->finalized) return SNL_OK;
+  DeviceGuard dg(e->device);
+  const auto& c = e->cfg;
+  const size_t h = c.hidden, I = c.intermediate;
+  // Every tensor the op graph binds must be present (WeightFile::info, weights.rs:108-113).
+  std::string missing;
+  snl_synth::for_each_tensor(
+      c, e->has_mtp, SNL_Q8_0,
+      [&](const std::string& name, int, size_t rows, size_t cols) {
+        auto it = e->qw.find(name);
+        if (it == e->qw.end()) {
+          if (missing.empty()) missing = name;
+        } else if (it->second.rows != rows || it->second.cols != cols) {
+          if (missing.empty()) missing = name + " (shape)";
+        }
+      },
+      [&](const std::string& name, const snl_synth::Seg* segs, int nseg) {
+        size_t n = 0;
+        for (int i = 0; i < nseg; i++) n += segs[i].n;
+        auto it = e->fv.find(name);
+        if (it == e->fv.end()) {
+          if (missing.empty()) missing = name;
+        } else if (it->second.n != n) {
+          if (missing.empty()) missing = name + " (shape)";
+        }
+      });
+  if (!missing.empty()) return fail(SNL_E_INVALID, "weight file is missing tensor `" + missing + "`");
+  const size_t proj_w = std::max({2 * I, snl_synth::lin_proj_rows(c), snl_synth::attn_proj_rows(c)});
+  const size_t act_w = std::max(I, snl_synth::conv_dim(c));
+  const size_t attn_w = std::max(snl_synth::q_dim(c), snl_synth::lin_value_dim(c));
+  SNL_TRY(dalloc(e, &e->x, MAX_M * 2 * h));
+  SNL_TRY(dalloc(e, &e->xn, MAX_M * h));
+  SNL_TRY(dalloc(e, &e->proj, MAX_M * proj_w));
+  SNL_TRY(dalloc(e, &e->act, MAX_M * act_w));
+  SNL_TRY(dalloc(e, &e->attn_out, MAX_M * attn_w));
+  SNL_TRY(dalloc(e, &e->branch, MAX_M * h));
+  SNL_TRY(dalloc(e, &e->qbuf, MAX_M * snl_synth::q_dim(c)));
+  SNL_TRY(dalloc(e, &e->coef, MAX_M * 8));
+  SNL_TRY(dalloc(e, &e->partial, std::max<size_t>((size_t)c.n_heads * MAX_M, (size_t)c.n_heads * 4 * MAX_PARTS) *
+                                         (c.head_dim + 2)));
+  SNL_TRY(dalloc(e, &e->rpos, MAX_M * 4));
+  SNL_TRY(dalloc(e, &e->tokens, MAX_M));
+  SNL_TRY(dalloc(e, &e->logits, LOGIT_ROWS * (size_t)c.vocab));
+  SNL_TRY(dalloc(e, &e->hid, (MAX_M + 1) * h));
+  SNL_TRY(dalloc(e, &e->hlast, h));
+  SNL_TRY(dalloc(e, &e->mhc_raw, MAX_M * 9));
+  SNL_TRY(dalloc(e, &e->amax, LOGIT_ROWS));
+  SNL_TRY(dalloc(e, &e->amax_part, LOGIT_ROWS * 128));
+  SNL_TRY(dalloc(e, &e->step_d, 1));
+  SNL_TRY(dalloc(e, &e->mstep_d, 1));
+  for (size_t l : e->plan) (c.full_attention[l] ? e->n_full : e->n_lin)++;
+  e->state_elems = (size_t)c.lin_v_heads * c.lin_k_dim * c.lin_v_dim;
+  e->conv_elems = (3 * snl_synth::conv_dim(c) + 63) / 64 * 64;  // 256-byte aligned slots (engine.rs:284)
+  SNL_TRY(dalloc(e, &e->lin_state, e->state_elems * std::max<size_t>(e->n_lin, 1)));
+  SNL_TRY(dalloc(e, &e->conv_state, e->conv_elems * std::max<size_t>(e->n_lin, 1)));
+  SNL_TRY(dalloc(e, &e->lin_ckpt, e->state_elems * std::max<size_t>(e->n_lin, 1)));
+  SNL_TRY(dalloc(e, &e->conv_ckpt, e->conv_elems * std::max<size_t>(e->n_lin, 1)));
+  const size_t kv_words = e->ctx * snl_synth::kv_dim(c) / 2;
+  e->kc.resize(e->n_full);
+  e->vc.resize(e->n_full);
+  for (size_t i = 0; i < e->n_full; i++) {
+    SNL_TRY(dalloc(e, &e->kc[i], kv_words));
+    SNL_TRY(dalloc(e, &e->vc[i], kv_words));
+  }
+  e->snap_lin.resize(SNAPSHOTS);
+  e->snap_conv.resize(SNAPSHOTS);
+  e->snap_h.resize(SNAPSHOTS);
+  for (size_t i = 0; i < SNAPSHOTS; i++) {
+    SNL_TRY(dalloc(e, &e->snap_lin[i], e->state_elems * std::max<size_t>(e->n_lin, 1)));
+    SNL_TRY(dalloc(e, &e->snap_conv[i], e->conv_elems * std::max<size_t>(e->n_lin, 1)));
+    SNL_TRY(dalloc(e, &e->snap_h[i], h));
+  }
+  if (e->has_mtp) {
+    SNL_TRY(dalloc(e, &e->mx, MAX_M * 2 * h));
+    SNL_TRY(dalloc(e, &e->hn, MAX_M * h));
+    SNL_TRY(dalloc(e, &e->m_logits, (size_t)c.vocab));
+    SNL_TRY(dalloc(e, &e->m_kc, kv_words));
+    SNL_TRY(dalloc(e, &e->m_vc, kv_words));
+  }
+  SNL_CUDA_TRY(cudaMallocHost(&e->h_tokens, MAX_M * sizeof(uint32_t)));
+  SNL_CUDA_TRY(cudaMallocHost(&e->h_rpos, MAX_M * 4 * sizeof(uint32_t)));
+  SNL_CUDA_TRY(cudaMallocHost(&e->h_step, sizeof(snl_step_u)));
+  SNL_CUDA_TRY(cudaMallocHost(&e->h_logits, LOGIT_ROWS * (size_t)c.vocab * sizeof(float)));
+  SNL_CUDA_TRY(cudaMallocHost(&e->h_amax, LOGIT_ROWS * sizeof(uint32_t)));
+  SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));
+  e->finalized = true;
+  e->pos = 0;
+  e->hid_rows = 0;
+  return SNL_OK;
+}
+
+extern "C" void snl_engine_destroy(snl_engine* e) {
+  if (!e) return;
+  {
+    DeviceGuard dg(e->device);
+    if (e->stream) cudaStreamSynchronize(e->stream);
+    for (auto& kv : e->graphs)
+      if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    for (void* p : e->allocs) cudaFree(p);
+    if (e->h_tokens) cudaFreeHost(e->h_tokens);
+    if (e->h_rpos) cudaFreeHost(e->h_rpos);
+    if (e->h_step) cudaFreeHost(e->h_step);
+    if (e->h_logits) cudaFreeHost(e->h_logits);
+    if (e->h_amax) cudaFreeHost(e->h_amax);
+    if (e->stream) cudaStreamDestroy(e->stream);
+  }
+  delete e;
+}
+
+extern "C" int snl_engine_forward_mm(snl_engine* e, const uint32_t* tokens, size_t n, const uint32_t* pos,
+                                     const uint32_t* embed_idx, const float* embeds, size_t n_embeds, size_t logit_rows,
+                                     int ckpt, float* logits_out) {
+  if (!e) return fail(SNL_E_INVALID, "null engine");
+  if (n_embeds && (!embed_idx || !embeds)) return fail(SNL_E_INVALID, "forward: embeds without rows");
+  if (logit_rows && !logits_out) return fail(SNL_E_INVALID, "forward: logits requested without an output buffer");
+  DeviceGuard dg(e->device);
+  size_t rows = 0;
+  SNL_TRY(forward_impl(e, tokens, n, pos, embed_idx, embeds, n_embeds, logit_rows, ckpt, false, &rows));
+  if (rows) {
+    const size_t nbytes = rows * e->cfg.vocab * sizeof(float);
+    SNL_CUDA_TRY(cudaMemcpyAsync(e->h_logits, e->logits, nbytes, cudaMemcpyDeviceToHost, e->stream));
+    SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    memcpy(logits_out, e->h_logits, nbytes);
+  } else {
+    // Keep the host from running far ahead of the device (engine.rs:933-934).
+    SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));
+  }
+  return SNL_OK;
+}
+
+extern "C" int snl_engine_forward_greedy(snl_engine* e, const uint32_t* tokens, size_t n, const uint32_t* pos,
+                                         size_t logit_rows, int ckpt, uint32_t* argmax_out) {
+  if (!e) return fail(SNL_E_INVALID, "null engine");
+  if (logit_rows == 0 || !argmax_out) return fail(SNL_E_INVALID, "forward_greedy: needs logit_rows >= 1 and an output");
+  DeviceGuard dg(e->device);
+  size_t rows = 0;
+  SNL_TRY(forward_impl(e, tokens, n, pos, nullptr, nullptr, 0, logit_rows, ckpt, true, &rows));
+  SNL_CUDA_TRY(cudaMemcpyAsync(e->h_amax, e->amax, rows * sizeof(uint32_t), cudaMemcpyDeviceToHost, e->stream));
+  SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));
+  memcpy(argmax_out, e->h_amax, rows * sizeof(uint32_t));
+  return SNL_OK;
+}
+
+// mtp (engine.rs:708-774).
+extern "C" int snl_engine_mtp(snl_engine* e, size_t r0, const uint32_t* tokens, size_t n, const uint32_t* pos, size_t slot0,
+                              int draft, uint32_t* draft_out) {
+  if (!e) return fail(SNL_E_INVALID, "null engine");
+  if (!e->has_mtp) return fail(SNL_E_STATE, "mtp: the model has no MTP head");
+  if (n == 0 || !tokens || !pos || r0 + n > e->hid_rows + 1) return fail(SNL_E_RANGE, "mtp: rows out of range");
+  if (slot0 + n > e->ctx) return fail(SNL_E_RANGE, "mtp: rows out of range");
+  SNL_TRY(check_tokens(e, tokens, n));
+  DeviceGuard dg(e->device);
+  const size_t h = e->h();
+  const auto& c = e->cfg;
+  const snl_attn_p ap = attn_p(e);
+  for (size_t c0 = 0; c0 < n; c0 += MAX_M) {
+    const size_t c1 = std::min(c0 + MAX_M, n);
+    const uint32_t m = (uint32_t)(c1 - c0);
+    snl_step_u sh = {m, (uint32_t)(slot0 + c0), parts_for(m, slot0 + c1), 0};
+    *e->h_step = sh;
+    memcpy(e->h_tokens, tokens + c0, m * sizeof(uint32_t));
+    for (size_t i = 0; i < m; i++) {
+      for (int k = 0; k < 3; k++) e->h_rpos[i * 4 + k] = pos[(c0 + i) * 3 + k];
+      e->h_rpos[i * 4 + 3] = 0;
+    }
+    SNL_CUDA_TRY(cudaMemcpyAsync(e->mstep_d, e->h_step, sizeof(snl_step_u), cudaMemcpyHostToDevice, e->stream));
+    SNL_CUDA_TRY(cudaMemcpyAsync(e->tokens, e->h_tokens, m * sizeof(uint32_t), cudaMemcpyHostToDevice, e->stream));
+    SNL_CUDA_TRY(cudaMemcpyAsync(e->rpos, e->h_rpos, m * 4 * sizeof(uint32_t), cudaMemcpyHostToDevice, e->stream));
+    StepRef st = step_dev(e->mstep_d, sh);
+    const bool last = c1 == n;
+    const QT* emb = find_q(e, "embed");
+    SNL_TRY(launch_embed(e->tokens, m, (const int8_t*)emb->q, (const float*)emb->s, (uint32_t)h, c.vocab, e->mx, nullptr,
+                         e->stream));
+    snl_layer_p p0 = layer_p(e, 0, false);
+    SNL_TRY(launch_branch_norm(st, p0, e->mx, e->coef, find_f(e, "mtp.norm_e"), e->xn, m, e->stream));
+    snl_layer_p ph = p0;
+    ph.x_stride = (uint32_t)h;
+    SNL_TRY(launch_branch_norm(st, ph, e->hid + (r0 + c0) * h, e->coef, find_f(e, "mtp.norm_h"), e->hn, m, e->stream));
+    SNL_TRY(mat(e, st, *find_q(e, "mtp.fc_e"), e->xn, h, e->mx, 2 * h, m));
+    SNL_TRY(mat(e, st, *find_q(e, "mtp.fc_h"), e->hn, h, e->branch, h, m));
+    SNL_TRY(launch_merge(st, p0, e->mx, e->coef, e->branch, m, e->stream));
+    SNL_TRY(launch_branch_norm(st, p0, e->mx, e->coef, find_f(e, "mtp.in_ln"), e->xn, m, e->stream));
+    SNL_TRY(mat(e, st, *find_q(e, "mtp.qkv"), e->xn, h, e->proj, ap.proj_stride, m));
+    SNL_TRY(launch_attn_prep(st, ap, e->proj, e->qbuf, e->m_kc, e->m_vc, find_f(e, "mtp.qk_norm"), e->rpos, m, e->stream));
+    SNL_TRY(launch_attend(st, ap, e->proj, e->qbuf, e->m_kc, e->m_vc, e->attn_out, e->partial, m, sh.parts, e->stream));
+    if (sh.parts > 1) SNL_TRY(launch_attn_combine(st, ap, e->proj, e->partial, e->attn_out, m, e->stream, 1));
+    SNL_TRY(mat(e, st, *find_q(e, "mtp.o_proj"), e->attn_out, snl_synth::q_dim(c), e->branch, h, m));
+    SNL_TRY(launch_merge(st, p0, e->mx, e->coef, e->branch, m, e->stream));
+    SNL_TRY(launch_branch_norm(st, p0, e->mx, e->coef, find_f(e, "mtp.post_ln"), e->xn, m, e->stream));
+    SNL_TRY(mat(e, st, *find_q(e, "mtp.gate_up"), e->xn, h, e->proj, 2 * (size_t)c.intermediate, m));
+    SNL_TRY(launch_swiglu(st, p0, e->proj, e->act, m, e->stream));
+    SNL_TRY(mat(e, st, *find_q(e, "mtp.down"), e->act, c.intermediate, e->branch, h, m));
+    SNL_TRY(launch_merge(st, p0, e->mx, e->coef, e->branch, m, e->stream));
+    if (last && draft) {
+      snl_layer_p pl = layer_p(e, 0, true);
+      SNL_TRY(launch_branch_norm(st, pl, e->mx, e->coef, find_f(e, "mtp.norm"), e->xn, 1, e->stream));
+      SNL_TRY(mat(e, st, *find_q(e, "lm_head"), e->xn, h, e->m_logits, c.vocab, 1, 1));
+      SNL_TRY(launch_argmax_with(e->m_logits, 1, c.vocab, e->amax, e->amax_part, e->stream));
+    }
+    SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));
+  }
+  if (draft && draft_out) {
+    SNL_CUDA_TRY(cudaMemcpy(draft_out, e->amax, sizeof(uint32_t), cudaMemcpyDeviceToHost));
+  }
+  return SNL_OK;
+}
+
+extern "C" int snl_engine_reset(snl_engine* e) {
+  if (!e || !e->finalized) return fail(SNL_E_STATE, "reset: engine not finalized");
+  DeviceGuard dg(e->device);
+  const size_t nl = std::max<size_t>(e->n_lin, 1);
+  SNL_CUDA_TRY(cudaMemsetAsync(e->lin_state, 0, e->state_elems * nl * sizeof(float), e->stream));
+  SNL_CUDA_TRY(cudaMemsetAsync(e->conv_state, 0, e->conv_elems * nl * sizeof(float), e->stream));
+  SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));
+  e->pos = 0;
+  e->hid_rows = 0;
+  return SNL_OK;
+}
+
+static int copy_state(snl_engine* e, float* dl, const float* sl, float* dc, const float* sc, float* dh, const float* sh_) {
+  const size_t nl = std::max<size_t>(e->n_lin, 1);
+  SNL_CUDA_TRY(cudaMemcpyAsync(dl, sl, e->state_elems * nl * sizeof(float), cudaMemcpyDeviceToDevice, e->stream));
+  SNL_CUDA_TRY(cudaMemcpyAsync(dc, sc, e->conv_elems * nl * sizeof(float), cudaMemcpyDeviceToDevice, e->stream));
+  SNL_CUDA_TRY(cudaMemcpyAsync(dh, sh_, e->h() * sizeof(float), cudaMemcpyDeviceToDevice, e->stream));
+  SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));
+  return SNL_OK;
+}
+
+extern "C" int snl_engine_snapshot(snl_engine* e, size_t slot) {
+  if (!e || !e->finalized) return fail(SNL_E_STATE, "snapshot: engine not finalized");
+  if (slot >= SNAPSHOTS) return fail(SNL_E_RANGE, "snapshot slot out of range");
+  DeviceGuard dg(e->device);
+  return copy_state(e, e->snap_lin[slot], e->lin_state, e->snap_conv[slot], e->conv_state, e->snap_h[slot], e->hlast);
+}
+
+extern "C" int snl_engine_restore(snl_engine* e, size_t slot, size_t pos) {
+  if (!e || !e->finalized) return fail(SNL_E_STATE, "restore: engine not finalized");
+  if (slot >= SNAPSHOTS) return fail(SNL_E_RANGE, "snapshot slot out of range");
+  if (pos > e->ctx) return fail(SNL_E_RANGE, "restore: position beyond the context");
+  DeviceGuard dg(e->device);
+  SNL_TRY(copy_state(e, e->lin_state, e->snap_lin[slot], e->conv_state, e->snap_conv[slot], e->hlast, e->snap_h[slot]));
+  e->pos = pos;
+  e->hid_rows = 0;
+  return SNL_OK;
+}
+
+extern "C" int snl_engine_rollback(snl_engine* e) {
+  if (!e || !e->finalized) return fail(SNL_E_STATE, "rollback: engine not finalized");
+  if (e->pos == 0) return fail(SNL_E_STATE, "rollback: nothing to undo");
+  DeviceGuard dg(e->device);
+  SNL_TRY(copy_state(e, e->lin_state, e->lin_ckpt, e->conv_state, e->conv_ckpt, e->hlast, e->hid + e->h()));
+  e->pos -= 1;
+  e->hid_rows = 1;
+  return SNL_OK;
+}
+
+extern "C" size_t snl_engine_hid_rows(const snl_engine* e) { return e ? e->hid_rows : 0; }
+extern "C" int snl_engine_has_mtp(const snl_engine* e) { return e && e->has_mtp ? 1 : 0; }
+extern "C" size_t snl_engine_pos(const snl_engine* e) { return e ? e->pos : 0; }
+extern "C" size_t snl_engine_ctx(const snl_engine* e) { return e ? e->ctx : 0; }
+extern "C" size_t snl_engine_device_bytes(const snl_engine* e) { return e ? e->bytes : 0; }
+
+extern "C" int snl_engine_read_hidden(const snl_engine* e, size_t row0, size_t rows, float* out) {
+  if (!e || !e->finalized || !out) return fail(SNL_E_INVALID, "read_hidden: bad argument");
+  if (row0 + rows > MAX_M + 1) return fail(SNL_E_RANGE, "read_hidden: rows out of range");
+  DeviceGuard dg(e->device);
+  SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));
+  SNL_CUDA_TRY(cudaMemcpy(out, e->hid + row0 * e->h(), rows * e->h() * sizeof(float), cudaMemcpyDeviceToHost));
+  return SNL_OK;
+}

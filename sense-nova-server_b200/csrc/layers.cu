@@ -1,0 +1,380 @@
+// Norm / mHC / residual / SwiGLU kernels (layers.wgsl), greedy argmax
+// (sampler.rs:169-177), the device-side embedding dequant (engine.rs:777-790,
+// weights.rs:155-162) and the seeded synthetic-weight generators.
+#include <algorithm>
+
+#include "common.cuh"
+#include "synth.h"
+
+namespace snl {
+namespace {
+
+// branch_norm (layers.wgsl:186-213): one CTA per output row.
+__global__ void __launch_bounds__(256) branch_norm_kernel(StepRef sr, snl_layer_p p, const float* __restrict__ x,
+                                                          const float* __restrict__ coef, const float* __restrict__ w,
+                                                          float* __restrict__ out) {
+  __shared__ float sh[32];
+  const snl_step_u st = load_step(sr);
+  const uint32_t g = blockIdx.x;
+  const uint32_t m = g + (p.last_row == 1 ? st.m - 1 : 0);
+  const uint64_t base = (uint64_t)m * (p.x_stride != 0 ? p.x_stride : 2 * p.h);
+  float pre0 = 1.f, pre1 = 0.f;
+  if (p.mode == 1) {
+    pre0 = coef[m * 8];
+    pre1 = coef[m * 8 + 1];
+  }
+  float ss = 0.f;
+  for (uint32_t i = threadIdx.x; i < p.h; i += blockDim.x) {
+    float v = pre0 * x[base + i];
+    if (p.mode == 1) v = fmaf(pre1, x[base + p.h + i], v);
+    ss = fmaf(v, v, ss);
+  }
+  const float total = block_sum(ss, sh);
+  const float rinv = rsqrtf(total / (float)p.h + p.eps);
+  const uint64_t ob = (uint64_t)g * p.h;
+  for (uint32_t i = threadIdx.x; i < p.h; i += blockDim.x) {
+    float v = pre0 * x[base + i];
+    if (p.mode == 1) v = fmaf(pre1, x[base + p.h + i], v);
+    out[ob + i] = v * rinv * (p.weight_one + w[i]);
+  }
+}
+
+// The 9 router sums of mhc_dots (layers.wgsl:215-232) for one token, in one pass
+// over its two streams.
+__device__ __forceinline__ void mhc_sums(const float* __restrict__ x, const float* __restrict__ w, uint32_t d,
+                                         float out9[9], float* sh) {
+  float acc[9];
+#pragma unroll
+  for (int o = 0; o < 9; o++) acc[o] = 0.f;
+  for (uint32_t i = threadIdx.x; i < d; i += blockDim.x) {
+    const float v = x[i];
+#pragma unroll
+    for (int o = 0; o < 8; o++) acc[o] = fmaf(__ldg(w + (uint64_t)o * d + i), v, acc[o]);
+    acc[8] = fmaf(v, v, acc[8]);
+  }
+#pragma unroll
+  for (int o = 0; o < 9; o++) out9[o] = block_sum(acc[o], sh);
+}
+
+__device__ __forceinline__ float lse2(float a, float b) {
+  const float mx = fmaxf(a, b);
+  return mx + __logf(__expf(a - mx) + __expf(b - mx));
+}
+
+// mhc_finish (layers.wgsl:234-266) for one token.
+__device__ __forceinline__ void mhc_coef(const float raw[9], const float* __restrict__ w, uint32_t d,
+                                         uint32_t iterations, float* __restrict__ cb) {
+  const float rinv = rsqrtf(raw[8] / (float)d + 1e-6f);
+  float lg[8];
+#pragma unroll
+  for (int o = 0; o < 8; o++) lg[o] = fmaf(raw[o], rinv, w[(uint64_t)8 * d + o]);
+  float a = lg[4], b = lg[5], c = lg[6], e = lg[7];
+  for (uint32_t it = 0; it < iterations; it++) {
+    const float r0 = lse2(a, b), r1 = lse2(c, e);
+    a -= r0;
+    b -= r0;
+    c -= r1;
+    e -= r1;
+    const float c0 = lse2(a, c), c1 = lse2(b, e);
+    a -= c0;
+    c -= c0;
+    b -= c1;
+    e -= c1;
+  }
+  cb[0] = 1.0f / (1.0f + __expf(-lg[0]));
+  cb[1] = 1.0f / (1.0f + __expf(-lg[1]));
+  cb[2] = 2.0f / (1.0f + __expf(-lg[2]));
+  cb[3] = 2.0f / (1.0f + __expf(-lg[3]));
+  cb[4] = __expf(a);
+  cb[5] = __expf(b);
+  cb[6] = __expf(c);
+  cb[7] = __expf(e);
+}
+
+__global__ void __launch_bounds__(256) mhc_dots_kernel(snl_layer_p p, const float* __restrict__ x,
+                                                       const float* __restrict__ w, float* __restrict__ raw) {
+  __shared__ float sh[32];
+  const uint32_t m = blockIdx.x, d = 2 * p.h;
+  float r[9];
+  mhc_sums(x + (uint64_t)m * d, w, d, r, sh);
+  if (threadIdx.x == 0)
+    for (int o = 0; o < 9; o++) raw[m * 9 + o] = r[o];
+}
+
+__global__ void mhc_finish_kernel(StepRef sr, snl_layer_p p, const float* __restrict__ raw,
+                                  const float* __restrict__ w, float* __restrict__ coef) {
+  const snl_step_u st = load_step(sr);
+  const uint32_t m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= st.m) return;
+  float r[9];
+  for (int o = 0; o < 9; o++) r[o] = raw[m * 9 + o];
+  mhc_coef(r, w, 2 * p.h, p.iterations, coef + m * 8);
+}
+
+// merge (layers.wgsl:268-302).
+__global__ void merge_kernel(snl_layer_p p, uint32_t m_rows, float* __restrict__ x, const float* __restrict__ coef,
+                             const float* __restrict__ br) {
+  const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (uint64_t)m_rows * p.h) return;
+  const uint64_t m = idx / p.h, i = idx % p.h;
+  const uint64_t b0 = m * 2 * p.h + i, b1 = b0 + p.h;
+  if (p.mode == 0) {
+    x[b0] += br[idx];
+    return;
+  }
+  if (p.mode == 3) {
+    x[b1] = x[b0];
+    return;
+  }
+  const float* c = coef + m * 8;
+  const float x0 = x[b0], x1 = x[b1], b = br[idx];
+  const float n0 = fmaf(c[4], x0, fmaf(c[5], x1, c[2] * b));
+  const float n1 = fmaf(c[6], x0, fmaf(c[7], x1, c[3] * b));
+  if (p.mode == 2) {
+    x[b0] = 0.5f * (n0 + n1);
+  } else {
+    x[b0] = n0;
+    x[b1] = n1;
+  }
+}
+
+// swiglu (layers.wgsl:304-315).
+__global__ void swiglu_kernel(snl_layer_p p, uint32_t m_rows, const float* __restrict__ gu, float* __restrict__ act) {
+  const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (uint64_t)m_rows * p.inter) return;
+  const uint64_t m = idx / p.inter, i = idx % p.inter;
+  const float g = gu[m * 2 * p.inter + i], u = gu[m * 2 * p.inter + p.inter + i];
+  act[idx] = g / (1.0f + __expf(-g)) * u;
+}
+
+// Greedy argmax, two passes. Key = (ordered float bits << 32) | ~index so that the
+// largest key is the largest value with the smallest index (the first maximum, as
+// sampler.rs:169-177). NaN never wins (the reference's `x > v[best]` is false for it).
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t i) {
+  uint32_t b = __float_as_uint(v);
+  if (v != v) b = 0xFF800000u;  // NaN -> -inf
+  const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((unsigned long long)ord << 32) | (unsigned long long)(~i);
+}
+
+constexpr int kArgBlocks = 128;
+__global__ void __launch_bounds__(512) argmax_pass1(const float* __restrict__ v, uint32_t n,
+                                                    unsigned long long* __restrict__ part) {
+  const uint32_t row = blockIdx.y;
+  const float* r = v + (uint64_t)row * n;
+  unsigned long long best = 0;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const unsigned long long k = argmax_key(__ldg(r + i), i);
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
+    best = t > best ? t : best;
+  }
+  __shared__ unsigned long long sh[16];
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++) best = sh[w] > best ? sh[w] : best;
+    part[(uint64_t)row * gridDim.x + blockIdx.x] = best;
+  }
+}
+__global__ void argmax_pass2(const unsigned long long* __restrict__ part, uint32_t nparts, uint32_t* __restrict__ out) {
+  const uint32_t row = blockIdx.x;
+  unsigned long long best = 0;
+  for (uint32_t i = threadIdx.x; i < nparts; i += 32) {
+    const unsigned long long k = part[(uint64_t)row * nparts + i];
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
+    best = t > best ? t : best;
+  }
+  if (threadIdx.x == 0) out[row] = ~(uint32_t)(best & 0xFFFFFFFFull);
+}
+
+// Embedding rows (engine.rs:777-790): stream 0 = q * s of the token's Q8_0 row,
+// stream 1 = 0. Ids >= vocab raise err_flag and write zeros (the host checks first).
+__global__ void embed_kernel(const uint32_t* __restrict__ toks, uint32_t h, uint32_t vocab,
+                             const int8_t* __restrict__ q, const float* __restrict__ s, float* __restrict__ x,
+                             int* __restrict__ err) {
+  const uint32_t m = blockIdx.x;
+  const uint32_t t = toks[m];
+  const bool ok = t < vocab;
+  if (!ok && threadIdx.x == 0 && err) *err = 1;
+  for (uint32_t i = threadIdx.x; i < h; i += blockDim.x) {
+    const float v = ok ? (float)q[(uint64_t)t * h + i] * s[((uint64_t)t * h + i) / 32] : 0.f;
+    x[(uint64_t)m * 2 * h + i] = v;
+    x[(uint64_t)m * 2 * h + h + i] = 0.f;
+  }
+}
+
+__global__ void gen_q8_kernel(uint64_t kq, uint64_t ks, uint64_t n, int8_t* __restrict__ q, float* __restrict__ s) {
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n / 4; i += (uint64_t)gridDim.x * blockDim.x) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int e = 0; e < 4; e++) w |= (uint32_t)(uint8_t)snl_q8(snl_draw(kq, i * 4 + e)) << (8 * e);
+    reinterpret_cast<uint32_t*>(q)[i] = w;
+    if ((i & 7) == 0) s[i / 8] = snl_q8_scale(snl_draw(ks, i / 8));
+  }
+}
+__global__ void gen_q4_kernel(uint64_t kq, uint64_t ks, uint64_t n, uint32_t* __restrict__ q, float* __restrict__ s) {
+  for (uint64_t wi = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; wi < n / 8; wi += (uint64_t)gridDim.x * blockDim.x) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int e = 0; e < 8; e++) w |= snl_nib(snl_draw(kq, wi * 8 + e)) << (4 * e);
+    q[wi] = w;
+    if ((wi & 3) == 0) s[wi / 4] = snl_q4_scale(snl_draw(ks, wi / 4));
+  }
+}
+__global__ void gen_f32_kernel(uint64_t k, uint64_t n, float mult, float offset, float* __restrict__ out) {
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+    out[i] = snl_param(snl_draw(k, i), mult, offset);
+}
+
+}  // namespace
+
+int launch_branch_norm(StepRef st, const snl_layer_p& p, const float* x, const float* coef, const float* w, float* out,
+                       uint32_t n_groups, cudaStream_t s) {
+  if (n_groups == 0) return SNL_OK;
+  branch_norm_kernel<<<n_groups, 256, 0, s>>>(st, p, x, coef, w, out);
+  SNL_LAUNCH_CHECK("branch_norm");
+  return SNL_OK;
+}
+int launch_mhc_dots(StepRef st, const snl_layer_p& p, const float* x, const float* w, float* raw, uint32_t m,
+                    cudaStream_t s) {
+  (void)st;
+  if (m == 0) return SNL_OK;
+  mhc_dots_kernel<<<m, 256, 0, s>>>(p, x, w, raw);
+  SNL_LAUNCH_CHECK("mhc_dots");
+  return SNL_OK;
+}
+int launch_mhc_finish(StepRef st, const snl_layer_p& p, const float* raw, const float* w, float* coef, uint32_t m,
+                      cudaStream_t s) {
+  if (m == 0) return SNL_OK;
+  mhc_finish_kernel<<<(m + 127) / 128, 128, 0, s>>>(st, p, raw, w, coef);
+  SNL_LAUNCH_CHECK("mhc_finish");
+  return SNL_OK;
+}
+int launch_merge(StepRef st, const snl_layer_p& p, float* x, const float* coef, const float* br, uint32_t m,
+                 cudaStream_t s) {
+  (void)st;
+  const uint64_t n = (uint64_t)m * p.h;
+  if (n == 0) return SNL_OK;
+  merge_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(p, m, x, coef, br);
+  SNL_LAUNCH_CHECK("merge");
+  return SNL_OK;
+}
+int launch_swiglu(StepRef st, const snl_layer_p& p, const float* gu, float* act, uint32_t m, cudaStream_t s) {
+  (void)st;
+  const uint64_t n = (uint64_t)m * p.inter;
+  if (n == 0) return SNL_OK;
+  swiglu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(p, m, gu, act);
+  SNL_LAUNCH_CHECK("swiglu");
+  return SNL_OK;
+}
+
+// Per-device scratch of the two-pass argmax: rows * kArgBlocks keys, grown on demand.
+static unsigned long long* argmax_scratch(uint32_t rows) {
+  static thread_local unsigned long long* buf[64] = {nullptr};
+  static thread_local uint32_t cap[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (cap[dev] < rows) {
+    if (buf[dev]) cudaFree(buf[dev]);
+    buf[dev] = nullptr;
+    if (cudaMalloc(&buf[dev], sizeof(unsigned long long) * kArgBlocks * rows) != cudaSuccess) {
+      cap[dev] = 0;
+      return nullptr;
+    }
+    cap[dev] = rows;
+  }
+  return buf[dev];
+}
+
+int launch_argmax_with(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_idx, unsigned long long* part,
+                       cudaStream_t s) {
+  if (rows == 0) return SNL_OK;
+  argmax_pass1<<<dim3(kArgBlocks, rows), 512, 0, s>>>(logits, n, part);
+  SNL_LAUNCH_CHECK("argmax_pass1");
+  argmax_pass2<<<rows, 32, 0, s>>>(part, kArgBlocks, out_idx);
+  SNL_LAUNCH_CHECK("argmax_pass2");
+  return SNL_OK;
+}
+
+int launch_argmax(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_idx, cudaStream_t s) {
+  unsigned long long* part = argmax_scratch(rows);
+  if (!part) return fail(SNL_E_OOM, "argmax: scratch allocation failed");
+  return launch_argmax_with(logits, rows, n, out_idx, part, s);
+}
+
+int launch_embed(const uint32_t* tokens, uint32_t m, const int8_t* q, const float* s_, uint32_t h, uint32_t vocab,
+                 float* x, int* err_flag, cudaStream_t s) {
+  if (m == 0) return SNL_OK;
+  embed_kernel<<<m, 256, 0, s>>>(tokens, h, vocab, q, s_, x, err_flag);
+  SNL_LAUNCH_CHECK("embed");
+  return SNL_OK;
+}
+
+int launch_gen_quant(uint64_t seed, const char* name, int dtype, size_t rows, size_t cols, void* q, float* s,
+                     cudaStream_t st) {
+  const uint64_t nh = snl_fnv1a(name);
+  const uint64_t kq = snl_key(seed, nh, 0), ks = snl_key(seed, nh, 1);
+  const uint64_t n = (uint64_t)rows * cols;
+  if (n % 32) return fail(SNL_E_INVALID, "gen_quant: size must be a multiple of 32");
+  const unsigned grid = (unsigned)std::min<uint64_t>((n / 8 + 255) / 256, 148 * 64);
+  if (dtype == SNL_Q8_0) gen_q8_kernel<<<grid, 256, 0, st>>>(kq, ks, n, (int8_t*)q, s);
+  else gen_q4_kernel<<<grid, 256, 0, st>>>(kq, ks, n, (uint32_t*)q, s);
+  SNL_LAUNCH_CHECK("gen_quant");
+  return SNL_OK;
+}
+
+int launch_gen_f32(uint64_t seed, const char* name, uint32_t sub, size_t n, float mult, float offset, float* out,
+                   cudaStream_t st) {
+  const uint64_t k = snl_key(seed, snl_fnv1a(name), sub);
+  if (n == 0) return SNL_OK;
+  const unsigned grid = (unsigned)std::min<uint64_t>((n + 255) / 256, 148 * 16);
+  gen_f32_kernel<<<grid, 256, 0, st>>>(k, n, mult, offset, out);
+  SNL_LAUNCH_CHECK("gen_f32");
+  return SNL_OK;
+}
+
+}  // namespace snl
+
+// ---- kernel-level C ABI (layers.wgsl entry points) ----
+
+extern "C" int snl_branch_norm(const snl_step_u* step, const snl_layer_p* p, const float* x, const float* coef,
+                               const float* w, float* out, uint32_t n_groups, void* stream) {
+  if (!step || !p || !x || !w || !out) return snl::fail(SNL_E_INVALID, "snl_branch_norm: null argument");
+  if (p->mode == 1 && !coef) return snl::fail(SNL_E_INVALID, "snl_branch_norm: mode 1 needs coef");
+  return snl::launch_branch_norm(snl::step_val(*step), *p, x, coef, w, out, n_groups, (cudaStream_t)stream);
+}
+extern "C" int snl_mhc_dots(const snl_step_u* step, const snl_layer_p* p, const float* x, const float* w, float* raw,
+                            void* stream) {
+  if (!step || !p || !x || !w || !raw) return snl::fail(SNL_E_INVALID, "snl_mhc_dots: null argument");
+  return snl::launch_mhc_dots(snl::step_val(*step), *p, x, w, raw, step->m, (cudaStream_t)stream);
+}
+extern "C" int snl_mhc_finish(const snl_step_u* step, const snl_layer_p* p, const float* raw, const float* w,
+                              float* coef, void* stream) {
+  if (!step || !p || !raw || !w || !coef) return snl::fail(SNL_E_INVALID, "snl_mhc_finish: null argument");
+  return snl::launch_mhc_finish(snl::step_val(*step), *p, raw, w, coef, step->m, (cudaStream_t)stream);
+}
+extern "C" int snl_merge(const snl_step_u* step, const snl_layer_p* p, float* x, const float* coef, const float* branch,
+                         void* stream) {
+  if (!step || !p || !x) return snl::fail(SNL_E_INVALID, "snl_merge: null argument");
+  if (p->mode > 3) return snl::fail(SNL_E_INVALID, "snl_merge: mode must be 0..3");
+  if ((p->mode == 1 || p->mode == 2) && !coef) return snl::fail(SNL_E_INVALID, "snl_merge: modes 1 and 2 need coef");
+  if (p->mode != 3 && !branch) return snl::fail(SNL_E_INVALID, "snl_merge: branch is null");
+  return snl::launch_merge(snl::step_val(*step), *p, x, coef, branch, step->m, (cudaStream_t)stream);
+}
+extern "C" int snl_swiglu(const snl_step_u* step, const snl_layer_p* p, const float* gate_up, float* act, void* stream) {
+  if (!step || !p || !gate_up || !act) return snl::fail(SNL_E_INVALID, "snl_swiglu: null argument");
+  return snl::launch_swiglu(snl::step_val(*step), *p, gate_up, act, step->m, (cudaStream_t)stream);
+}
+extern "C" int snl_argmax(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_idx, void* stream) {
+  if (!logits || !out_idx || n == 0) return snl::fail(SNL_E_INVALID, "snl_argmax: bad argument");
+  return snl::launch_argmax(logits, rows, n, out_idx, (cudaStream_t)stream);
+}

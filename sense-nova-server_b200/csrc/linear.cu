@@ -1,0 +1,141 @@
+// Gated DeltaNet linear attention (linear.wgsl: conv :38-66, delta :84-140).
+//
+// proj rows: qkv[conv_dim] | z[n_v*128] | b[n_v] | a[n_v]; after the causal conv,
+// qkv splits as q[n_k*128] | k[n_k*128] | v[n_v*128]. lw = conv w [conv_dim*4] |
+// A_log[n_v] | dt_bias[n_v] | norm w[128]. The recurrent state of value head h is a
+// [128 (key dim i), 128 (value dim j)] f32 matrix; column j evolves independently of
+// the other columns given the head's q, k, beta and decay.
+#include "common.cuh"
+
+namespace snl {
+namespace {
+
+constexpr uint32_t DK = 128, DV = 128;
+
+// conv: one thread per channel walking the tokens of the step.
+__global__ void conv_kernel(StepRef sr, snl_lin_p p, const float* __restrict__ proj, float* __restrict__ conv_out,
+                            float* __restrict__ cs, const float* __restrict__ lw, float* __restrict__ ck) {
+  const snl_step_u st = load_step(sr);
+  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t cd = p.conv_dim;
+  if (c >= cd) return;
+  const float4 w = *reinterpret_cast<const float4*>(lw + (uint64_t)c * 4);
+  float r0 = cs[c], r1 = cs[cd + c], r2 = cs[2 * cd + c];
+  for (uint32_t m = 0; m < st.m; m++) {
+    const float cur = proj[(uint64_t)m * p.proj_stride + c];
+    const float o = fmaf(w.w, cur, fmaf(w.z, r2, fmaf(w.y, r1, w.x * r0)));
+    conv_out[(uint64_t)m * cd + c] = o / (1.0f + __expf(-o));
+    r0 = r1;
+    r1 = r2;
+    r2 = cur;
+    if (m + 1 == st.ckpt) {
+      ck[c] = r0;
+      ck[cd + c] = r1;
+      ck[2 * cd + c] = r2;
+    }
+  }
+  cs[c] = r0;
+  cs[cd + c] = r1;
+  cs[2 * cd + c] = r2;
+}
+
+// delta: CTA per value head, thread j owns state column j (128 floats in registers).
+__global__ void __launch_bounds__(128) delta_kernel(StepRef sr, snl_lin_p p, const float* __restrict__ proj,
+                                                    const float* __restrict__ conv_out, float* __restrict__ state,
+                                                    const float* __restrict__ lw, float* __restrict__ out,
+                                                    float* __restrict__ state_ckpt) {
+  __shared__ float qs[DK], ks[DK];
+  __shared__ float red[32];
+  const snl_step_u st = load_step(sr);
+  const uint32_t h = blockIdx.x, j = threadIdx.x;
+  const uint32_t kh = h / (p.n_v / p.n_k);
+  const uint32_t cd = p.conv_dim, key_dim = p.n_k * DK;
+  const uint64_t sbase = (uint64_t)h * DK * DV;
+  const float a_log = lw[(uint64_t)cd * 4 + h];
+  const float dt_bias = lw[(uint64_t)cd * 4 + p.n_v + h];
+  const float norm_w = lw[(uint64_t)cd * 4 + 2 * p.n_v + j];
+  const float neg_a = -__expf(a_log);
+  const uint32_t z_off = cd, b_off = cd + p.n_v * DV, a_off = b_off + p.n_v;
+  float S[DK];
+#pragma unroll
+  for (uint32_t i = 0; i < DK; i++) S[i] = state[sbase + i * DV + j];
+  for (uint32_t m = 0; m < st.m; m++) {
+    const uint64_t crow = (uint64_t)m * cd;
+    const float qv = conv_out[crow + kh * DK + j];
+    const float kv = conv_out[crow + key_dim + kh * DK + j];
+    const float vv = conv_out[crow + 2 * key_dim + h * DV + j];
+    const float sq = block_sum(qv * qv, red);
+    const float sk = block_sum(kv * kv, red);
+    qs[j] = qv * rsqrtf(sq + 1e-6f) * rsqrtf((float)DK);
+    ks[j] = kv * rsqrtf(sk + 1e-6f);
+    __syncthreads();
+    const uint64_t prow = (uint64_t)m * p.proj_stride;
+    const float beta = 1.0f / (1.0f + __expf(-proj[prow + b_off + h]));
+    const float araw = proj[prow + a_off + h] + dt_bias;
+    const float sp = araw <= 20.0f ? log1pf(__expf(araw)) : araw;
+    const float decay = __expf(neg_a * sp);
+    float kv_mem = 0.f;
+#pragma unroll
+    for (uint32_t i = 0; i < DK; i++) {
+      S[i] *= decay;
+      kv_mem = fmaf(S[i], ks[i], kv_mem);
+    }
+    const float dlt = (vv - kv_mem) * beta;
+    float o = 0.f;
+#pragma unroll
+    for (uint32_t i = 0; i < DK; i++) {
+      S[i] = fmaf(ks[i], dlt, S[i]);
+      o = fmaf(S[i], qs[i], o);
+    }
+    const float var_o = block_sum(o * o, red) / (float)DV;
+    const float z = proj[prow + z_off + h * DV + j];
+    out[(uint64_t)m * p.n_v * DV + h * DV + j] = o * rsqrtf(var_o + p.eps) * norm_w * (z / (1.0f + __expf(-z)));
+    if (m + 1 == st.ckpt) {
+#pragma unroll
+      for (uint32_t i = 0; i < DK; i++) state_ckpt[sbase + i * DV + j] = S[i];
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (uint32_t i = 0; i < DK; i++) state[sbase + i * DV + j] = S[i];
+}
+
+}  // namespace
+
+static int check_lin(const snl_lin_p& p) {
+  if (p.n_k == 0 || p.n_v == 0 || p.n_v % p.n_k) return fail(SNL_E_UNSUPPORTED, "linear: n_v must be a multiple of n_k");
+  if (p.conv_dim != 2 * p.n_k * DK + p.n_v * DV) return fail(SNL_E_UNSUPPORTED, "linear: conv_dim mismatch");
+  return SNL_OK;
+}
+
+int launch_conv(StepRef st, const snl_lin_p& p, const float* proj, float* conv_out, float* conv_state, const float* lw,
+                float* conv_ckpt, cudaStream_t s) {
+  if (int rc = check_lin(p)) return rc;
+  conv_kernel<<<(p.conv_dim + 255) / 256, 256, 0, s>>>(st, p, proj, conv_out, conv_state, lw, conv_ckpt);
+  SNL_LAUNCH_CHECK("conv");
+  return SNL_OK;
+}
+
+int launch_delta(StepRef st, const snl_lin_p& p, const float* proj, const float* conv_out, float* state,
+                 const float* lw, float* out, float* state_ckpt, cudaStream_t s) {
+  if (int rc = check_lin(p)) return rc;
+  delta_kernel<<<p.n_v, DV, 0, s>>>(st, p, proj, conv_out, state, lw, out, state_ckpt);
+  SNL_LAUNCH_CHECK("delta");
+  return SNL_OK;
+}
+
+}  // namespace snl
+
+extern "C" int snl_conv(const snl_step_u* step, const snl_lin_p* p, const float* proj, float* conv_out,
+                        float* conv_state, const float* lw, float* conv_ckpt, void* stream) {
+  if (!step || !p || !proj || !conv_out || !conv_state || !lw) return snl::fail(SNL_E_INVALID, "snl_conv: null argument");
+  if (step->ckpt > 0 && !conv_ckpt) return snl::fail(SNL_E_INVALID, "snl_conv: ckpt needs conv_ckpt");
+  return snl::launch_conv(snl::step_val(*step), *p, proj, conv_out, conv_state, lw, conv_ckpt, (cudaStream_t)stream);
+}
+extern "C" int snl_delta(const snl_step_u* step, const snl_lin_p* p, const float* proj, const float* conv_out,
+                         float* state, const float* lw, float* out, float* state_ckpt, void* stream) {
+  if (!step || !p || !proj || !conv_out || !state || !lw || !out)
+    return snl::fail(SNL_E_INVALID, "snl_delta: null argument");
+  if (step->ckpt > 0 && !state_ckpt) return snl::fail(SNL_E_INVALID, "snl_delta: ckpt needs state_ckpt");
+  return snl::launch_delta(snl::step_val(*step), *p, proj, conv_out, state, lw, out, state_ckpt, (cudaStream_t)stream);
+}

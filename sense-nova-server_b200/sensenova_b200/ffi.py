@@ -1,0 +1,145 @@
+"""ctypes binding of include/snl_b200.h (the C ABI of libsnl_b200.so).
+
+The library is the only compute path: if it is missing this module raises at import
+time instead of falling back to anything else.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+PKG_DIR = Path(__file__).resolve().parent.parent
+LIB_PATH = Path(os.environ.get("SNL_LIB", PKG_DIR / "libsnl_b200.so"))
+
+SNL_F32, SNL_Q8_0, SNL_Q4_0 = 0, 1, 2
+SNL_OK = 0
+ERRORS = {
+    -1: "SNL_E_INVALID", -2: "SNL_E_RANGE", -3: "SNL_E_CUDA", -4: "SNL_E_OOM",
+    -5: "SNL_E_STATE", -6: "SNL_E_TIMEOUT", -7: "SNL_E_UNSUPPORTED", -8: "SNL_E_NCCL",
+}
+SNL_ENGINE_MTP = 1
+SNL_ENGINE_F16_SCALES = 2
+MAX_LAYERS = 256
+
+
+class StepU(C.Structure):
+    """StepU (engine.rs:24-32)."""
+    _fields_ = [("m", C.c_uint32), ("pos0", C.c_uint32), ("parts", C.c_uint32), ("ckpt", C.c_uint32)]
+
+
+class MatP(C.Structure):
+    """MatP (engine.rs:34-45)."""
+    _fields_ = [(n, C.c_uint32) for n in ("n", "k", "x_off", "x_stride", "y_off", "y_stride", "n_off", "m_one")]
+
+
+class LayerP(C.Structure):
+    """LayerP (engine.rs:47-58)."""
+    _fields_ = [("h", C.c_uint32), ("mode", C.c_uint32), ("last_row", C.c_uint32), ("eps", C.c_float),
+                ("weight_one", C.c_float), ("iterations", C.c_uint32), ("inter", C.c_uint32), ("x_stride", C.c_uint32)]
+
+
+class AttnP(C.Structure):
+    """AttnP (engine.rs:60-71)."""
+    _fields_ = [("n_heads", C.c_uint32), ("n_kv", C.c_uint32), ("rot_dim", C.c_uint32), ("proj_stride", C.c_uint32),
+                ("rope_theta", C.c_float), ("eps", C.c_float), ("scale", C.c_float), ("mrope", C.c_uint32)]
+
+
+class LinP(C.Structure):
+    """LinP (engine.rs:73-82)."""
+    _fields_ = [("conv_dim", C.c_uint32), ("proj_stride", C.c_uint32), ("n_k", C.c_uint32), ("n_v", C.c_uint32),
+                ("eps", C.c_float), ("pad", C.c_uint32 * 3)]
+
+
+class ModelConfigC(C.Structure):
+    """snl_model_config (the text part of ModelConfig, config.rs:7-37)."""
+    _fields_ = [
+        ("hidden", C.c_uint32), ("intermediate", C.c_uint32), ("vocab", C.c_uint32), ("n_layers", C.c_uint32),
+        ("full_attention", C.c_uint8 * MAX_LAYERS),
+        ("n_heads", C.c_uint32), ("n_kv_heads", C.c_uint32), ("head_dim", C.c_uint32), ("rot_dim", C.c_uint32),
+        ("rope_theta", C.c_float), ("mrope_section", C.c_uint32 * 3),
+        ("lin_k_heads", C.c_uint32), ("lin_v_heads", C.c_uint32), ("lin_k_dim", C.c_uint32), ("lin_v_dim", C.c_uint32),
+        ("conv_kernel", C.c_uint32), ("eps", C.c_float),
+        ("loop_start", C.c_uint32), ("loop_end", C.c_uint32), ("loop_count", C.c_uint32),
+        ("mhc_start", C.c_int32), ("mhc_end", C.c_int32), ("mhc_streams", C.c_uint32), ("mhc_iterations", C.c_uint32),
+        ("max_position", C.c_uint32),
+    ]
+
+
+class SnlError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(msg)
+        self.code = code
+        self.kind = ERRORS.get(code, str(code))
+
+
+vp = C.c_void_p
+u32 = C.c_uint32
+u64 = C.c_uint64
+sz = C.c_size_t
+i32 = C.c_int
+P = C.POINTER
+
+# name -> (restype, argtypes); mirrors include/snl_b200.h.
+SIGNATURES = {
+    "snl_last_error": (C.c_char_p, []),
+    "snl_version": (C.c_char_p, []),
+    "snl_launch_count": (u64, []),
+    "snl_config_validate": (i32, [P(ModelConfigC)]),
+    "snl_mat": (i32, [i32, P(StepU), P(MatP), vp, vp, vp, vp, vp]),
+    "snl_branch_norm": (i32, [P(StepU), P(LayerP), vp, vp, vp, vp, u32, vp]),
+    "snl_mhc_dots": (i32, [P(StepU), P(LayerP), vp, vp, vp, vp]),
+    "snl_mhc_finish": (i32, [P(StepU), P(LayerP), vp, vp, vp, vp]),
+    "snl_merge": (i32, [P(StepU), P(LayerP), vp, vp, vp, vp]),
+    "snl_swiglu": (i32, [P(StepU), P(LayerP), vp, vp, vp]),
+    "snl_attn_prep": (i32, [P(StepU), P(AttnP), vp, vp, vp, vp, vp, vp, vp]),
+    "snl_attend": (i32, [P(StepU), P(AttnP), vp, vp, vp, vp, vp, vp, vp]),
+    "snl_attn_combine": (i32, [P(StepU), P(AttnP), vp, vp, vp, vp]),
+    "snl_conv": (i32, [P(StepU), P(LinP), vp, vp, vp, vp, vp, vp]),
+    "snl_delta": (i32, [P(StepU), P(LinP), vp, vp, vp, vp, vp, vp, vp]),
+    "snl_argmax": (i32, [vp, u32, u32, vp, vp]),
+    "snl_engine_create": (i32, [P(ModelConfigC), sz, i32, u32, P(vp)]),
+    "snl_engine_set_tensor": (i32, [vp, C.c_char_p, i32, sz, sz, vp, vp]),
+    "snl_engine_fill_synthetic": (i32, [vp, u64, i32]),
+    "snl_engine_finalize": (i32, [vp]),
+    "snl_engine_destroy": (None, [vp]),
+    "snl_engine_forward_mm": (i32, [vp, vp, sz, vp, vp, vp, sz, sz, i32, vp]),
+    "snl_engine_forward_greedy": (i32, [vp, vp, sz, vp, sz, i32, vp]),
+    "snl_engine_mtp": (i32, [vp, sz, vp, sz, vp, sz, i32, vp]),
+    "snl_engine_reset": (i32, [vp]),
+    "snl_engine_snapshot": (i32, [vp, sz]),
+    "snl_engine_restore": (i32, [vp, sz, sz]),
+    "snl_engine_rollback": (i32, [vp]),
+    "snl_engine_hid_rows": (sz, [vp]),
+    "snl_engine_has_mtp": (i32, [vp]),
+    "snl_engine_pos": (sz, [vp]),
+    "snl_engine_ctx": (sz, [vp]),
+    "snl_engine_device_bytes": (sz, [vp]),
+    "snl_engine_read_hidden": (i32, [vp, sz, sz, vp]),
+}
+
+_lib: C.CDLL | None = None
+
+
+def load(path: Path | str | None = None) -> C.CDLL:
+    """Load libsnl_b200.so (once) and declare every exported function."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = Path(path) if path else LIB_PATH
+    if not p.exists():
+        raise FileNotFoundError(f"{p} is missing: build it with `python sense-nova-server_b200/build.py --lib`")
+    lib = C.CDLL(str(p))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def check(rc: int) -> None:
+    if rc != SNL_OK:
+        msg = load().snl_last_error().decode(errors="replace")
+        raise SnlError(rc, msg or ERRORS.get(rc, f"error {rc}"))
