@@ -1,0 +1,433 @@
+#!/usr/bin/env python
+"""Benchmark: decode tok/s at batch 1 on the synthetic 9B-shape Q8_0 model, with the
+Q8_0 GEMV's achieved HBM bandwidth against the measured peak.
+
+One step = one greedy decode token of the 9B-shape model (56 layer visits + the
+248320-row LM head) after a 2048-token prefill of uniform random ids (BASELINE.json
+configs[2]). `value` is device-timed (CUDA events on the engine stream) with every
+step's inputs resident in HBM and the argmax fed back on the device; `e2e` is the same
+metric through the public API with the token crossing host->device and the next token
+device->host every step. The weights (14.8 GB streamed per token) are far larger than
+L2, so no L2 flush is needed between steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Under torchrun (N > 1) every rank runs its own replica of the model on its GPU
+("replicas"; weak scaling); time is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "sense-nova-server_b200"))
+
+METRIC = "decode tok/s @bs1 Q8_0 9B-shape; Q8 GEMV achieved HBM GB/s vs peak"
+PUBLISHED_DECODE_TOK_S = 38.0  # ~38 tok/s decode, batch 1, Q8_0 (RTX 5080, README.md:218)
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--prompt", type=int, default=2048)
+    ap.add_argument("--quant", default="q8_0", choices=["q8_0", "q4_0"])
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--e2e-steps", type=int, default=64)
+    ap.add_argument("--e2e-logits-steps", type=int, default=16)
+    ap.add_argument("--no-gemv", action="store_true", help="skip the standalone config-1 GEMV timing")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget-s", type=float, default=25.0)
+    ap.add_argument("--profile", action="store_true", help="print the per-op table of one decode step")
+    ap.add_argument("--workload", choices=["decode", "gemv"], default="decode",
+                    help="gemv: only BASELINE configs[0], the one-token Q8_0 GEMV 12288x4096")
+    ap.add_argument("--iters", type=int, default=40)
+    return ap.parse_args()
+
+
+def peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def env_rank():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, phys_index: int):
+        self.idx = phys_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.idx)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in self.lines:
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def phys_gpu_index(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if local_rank < len(ids) and ids[local_rank].isdigit():
+            return int(ids[local_rank])
+    return local_rank
+
+
+def traffic_from_profiles() -> float | None:
+    """DRAM bytes per launch of the decode GEMV from the committed ncu summary."""
+    f = ROOT / "profiles" / "gemv_q8_decode.md"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.strip().startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# ---- CPU side (oracle): the reference's algorithm restated in C++ ------------------------------
+
+
+def cpu_decode(cfg, quant: int, budget_s: float, max_steps: int, warmup: int = 1, seed: int = 0):
+    """Greedy decode with the CPU restatement of the reference's kernels (oracle/),
+    all host threads. Returns (tok/s, steps timed, build seconds)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as orc  # test/baseline infrastructure only
+
+    t0 = time.perf_counter()
+    m = orc.OracleModel(cfg, 64, seed=seed, quant=quant)
+    build_s = time.perf_counter() - t0
+    prompt = [int(v) for v in np.random.default_rng(seed).integers(0, cfg.vocab, 4)]
+    lg = m.forward(prompt, True)
+    tok = orc.argmax(lg)
+    for _ in range(warmup):
+        tok = orc.argmax(m.forward([tok], True))
+    steps, t = 0, 0.0
+    while steps < max_steps and (steps == 0 or t < budget_s):
+        t1 = time.perf_counter()
+        tok = orc.argmax(m.forward([tok], True))
+        t += time.perf_counter() - t1
+        steps += 1
+    m.close()
+    return steps / t, steps, build_s
+
+
+def weight_bytes_per_token(cfg, quant: str) -> int:
+    """Quant + f32-scale bytes of every matrix one decode token streams (56 layer
+    visits + LM head); in_proj and lm_head stay Q8_0 (convert.rs:232-234, :286-298)."""
+    h, inter = cfg.hidden, cfg.intermediate
+    q8 = lambda r, k: r * k * 1.125
+    qq = (lambda r, k: r * k * 1.125) if quant == "q8_0" else (lambda r, k: r * k * 0.625)
+    tot = q8(cfg.vocab, h)
+    for l in cfg.execution_plan():
+        if cfg.full_attention[l]:
+            tot += qq(cfg.attn_proj_rows, h) + qq(h, cfg.q_dim)
+        else:
+            tot += q8(cfg.lin_proj_rows, h) + qq(h, cfg.lin_value_dim)
+        tot += qq(2 * inter, h) + qq(h, inter)
+    return int(tot)
+
+
+def gemv_config1(lib, quant: str, copies: int = 8, iters: int = 40) -> dict:
+    """one-token Q8_0 GEMV, W [12288 x 4096], x fp32 ~N(0,1),
+    timed alone with CUDA events on the launching stream. `copies` weight copies
+    (8 x 56.7 MB > L2) rotate so every launch reads its weights from HBM."""
+    import ctypes as C
+
+    import torch
+
+    from sensenova_b200 import ffi
+
+    n, k = 12288, 4096
+    dt = ffi.SNL_Q8_0 if quant == "q8_0" else ffi.SNL_Q4_0
+    qb = n * k if dt == ffi.SNL_Q8_0 else n * k // 2
+    ws = [torch.empty(qb, dtype=torch.uint8, device="cuda") for _ in range(copies)]
+    ss = [torch.empty(n * k // 32, dtype=torch.float32, device="cuda") for _ in range(copies)]
+    for i in range(copies):
+        ffi.check(lib.snl_synth_quant(100 + i, b"gemv", dt, n, k, C.c_void_p(ws[i].data_ptr()),
+                                      C.c_void_p(ss[i].data_ptr()), None))
+    x = torch.randn(k, device="cuda")
+    y = torch.empty(n, device="cuda")
+    st, p = ffi.StepU(1, 0, 1, 0), ffi.MatP(n, k, 0, k, 0, n, 0, 0)
+
+    def run(i):
+        ffi.check(lib.snl_mat(dt, C.byref(st), C.byref(p), C.c_void_p(x.data_ptr()), C.c_void_p(ws[i].data_ptr()),
+                              C.c_void_p(ss[i].data_ptr()), C.c_void_p(y.data_ptr()), None))
+
+    for i in range(2 * copies):
+        run(i % copies)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(iters):
+        run(i % copies)
+    b.record()
+    torch.cuda.synchronize()
+    us = a.elapsed_time(b) * 1000.0 / iters
+    nbytes = qb + n * k // 32 * 4 + 4 * k + 4 * n
+    return {"shape": [n, k], "quant": quant, "scales": "f32", "us_per_launch": us, "bytes_per_launch": nbytes,
+            "achieved_gbs": nbytes / (us * 1e3), "copies_rotated": copies}
+
+
+def cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def run_reference(args):
+    rank, world, _ = env_rank()
+    if rank != 0:
+        return 0
+    from sensenova_b200.config import nine_b
+
+    cfg = nine_b()
+    quant = {"q8_0": 1, "q4_0": 2}[args.quant]
+    budget = max(30.0, min(150.0, 4.0 * args.steps))
+    v, n, build_s = cpu_decode(cfg, quant, budget, args.steps, warmup=min(args.warmup, 1), seed=args.seed)
+    sample = (f"9B-shape {args.quant} greedy decode, 4-token prompt, {n} timed tokens (of --steps {args.steps}; "
+              f"capped to ~{budget:.0f} s of CPU work), weights generated in {build_s:.0f} s")
+    line = {
+        "metric": METRIC, "value": v, "unit": "tok/s", "impl": "reference", "n_gpus": world, "steps": n,
+        "warmup": min(args.warmup, 1), "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": v / PUBLISHED_DECODE_TOK_S, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "9B-shape Q8_0 decode bs1", "quant": args.quant},
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores(), "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference = CPU restatement of the reference's WGSL kernels (oracle/); the Rust/wgpu reference "
+                "cannot be built or run here (no Rust toolchain, no graphics stack)",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+
+    rank, world, local_rank = env_rank()
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+
+    from sensenova_b200 import ffi
+    from sensenova_b200.config import nine_b
+    from sensenova_b200.engine import Engine
+
+    lib = ffi.load()
+    cfg = nine_b()
+    K, W = args.steps, max(args.warmup, 3)
+    ctx = args.prompt + W + K + args.e2e_steps + 40
+    t0 = time.perf_counter()
+    eng = Engine.synthetic(cfg, ctx, args.seed, args.quant, device=local_rank)
+    build_s = time.perf_counter() - t0
+    rng = np.random.default_rng(args.seed + rank)
+    prompt = rng.integers(0, cfg.vocab, args.prompt).tolist()
+
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    tok = eng.forward_greedy(prompt, None, 1)[0]
+    prefill_s = time.perf_counter() - t0
+
+    toks, _ = eng.generate(tok, W)  # warm-up (also captures the decode graph)
+    tok = toks[-1]
+
+    def barrier():
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    clocks = ClockSampler(phys_gpu_index(local_rank))
+    l0 = lib.snl_launch_count()
+    barrier()
+    clocks.start()
+    gen, ms = eng.generate(tok, K)
+    barrier()
+    clk = clocks.stop()
+    launches = lib.snl_launch_count() - l0
+    tok = gen[-1]
+    ms_t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    value = world * K / (ms_max / 1000.0)
+
+    # e2e through the public API: token in from host memory, token out to host memory.
+    E = args.e2e_steps
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(E):
+        tok = eng.forward_greedy([tok], None, 1)[0]
+    barrier()
+    e2e_s = time.perf_counter() - t0
+    e2e_t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e = world * E / float(e2e_t.item())
+    # the reference's own call returns the full logits row every token (engine.rs:917-931)
+    El = max(args.e2e_logits_steps, 1)
+    t0 = time.perf_counter()
+    for _ in range(El):
+        lg = eng.forward([tok], True)
+        tok = int(np.argmax(lg))
+    torch.cuda.synchronize()
+    e2e_logits = El / (time.perf_counter() - t0)
+
+    # Roofline of the dominant kernel: the Q8_0 GEMVs of one decode step, each bracketed by
+    # CUDA events on the engine stream.
+    prof = eng.profile(tok)
+    mats = [r for r in prof if r["label"].startswith("mat")]
+    gb = sum(r["bytes"] for r in mats)
+    gms = sum(r["ms"] for r in mats)
+    step_ms = sum(r["ms"] for r in prof)
+    peak, peak_kind = peaks()
+    achieved = gb / (gms * 1e6)
+    n_mat = sum(r["calls"] for r in mats)
+    traffic = traffic_from_profiles()
+
+    if rank == 0 and args.profile:
+        eng.print_profile(prof)
+    g1 = None if args.no_gemv else gemv_config1(lib, args.quant)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        quant = {"q8_0": 1, "q4_0": 2}[args.quant]
+        v, n, bs = cpu_decode(cfg, quant, args.cpu_budget_s, 8, warmup=0, seed=args.seed)
+        cpu = {"value": v, "unit": "tok/s", "cores": cores(), "kind": "port",
+               "sample": f"oracle/ (C++ restatement of the WGSL kernels, OpenMP) greedy decode of the same "
+                         f"9B-shape {args.quant} model after a 4-token prompt, {n} tokens timed; KV reads at "
+                         f"2K context are <1% of the 14.8 GB weight stream, so a short context stands in"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": value / PUBLISHED_DECODE_TOK_S, "dtype": "f32 (int8 weights, fp32 accumulate)",
+            "data": "synthetic (seeded random-init weights, uniform random prompt ids)",
+            "config": {"workload": f"9B-shape {args.quant} greedy decode bs1 after a {args.prompt}-token prefill",
+                       "prompt_tokens": args.prompt, "decode_tokens": K, "quant": args.quant, "scales": "f32",
+                       "weight_bytes_per_token": weight_bytes_per_token(cfg, args.quant),
+                       "l2": "inputs larger than L2 (14.8 GB of weights streamed per token)",
+                       "parallelism": "replicas" if world > 1 else "single"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "kernel": f"Q8_0 GEMV (all {n_mat} matrix launches of one decode step, "
+                                   f"{gb / 1e9:.2f} GB algorithmic)", "peak_kind": f"{peak_kind} hbm_gbs (burst)"},
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4 + 16 + 16, "d2h_bytes_per_step": 4,
+                    "api": "snl_engine_forward_greedy"},
+            "e2e_logits": {"value": e2e_logits, "unit": "tok/s", "d2h_bytes_per_step": 4 * cfg.vocab,
+                           "api": "snl_engine_forward_mm (full logits row, as engine.rs:917-931)"},
+            "gpu_launches": int(launches),
+            "clocks": clk,
+            "prefill_tok_s": args.prompt / prefill_s,
+            "step_profile_ms": step_ms,
+            "build_s": build_s,
+        }
+        if g1:
+            g1["frac"] = g1["achieved_gbs"] / peak
+            line["gemv_config1"] = g1
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def run_gemv_only(args):
+    import torch
+
+    from sensenova_b200 import ffi
+
+    torch.cuda.set_device(0)
+    lib = ffi.load()
+    g = gemv_config1(lib, args.quant, iters=args.iters)
+    peak, kind = peaks()
+    g["frac"] = g["achieved_gbs"] / peak
+    g["peak"] = peak
+    print(json.dumps({"workload": "gemv config1", **g}), flush=True)
+    return 0
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    if args.workload == "gemv":
+        return run_gemv_only(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

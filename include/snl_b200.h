@@ -115,6 +115,11 @@ const char* snl_last_error(void);
 const char* snl_version(void);
 uint64_t snl_launch_count(void);
 
+/* Device error word of the current device: bit 0 = a bounded device-side wait gave up
+ * (the kernel returned instead of hanging). Returns the word (>= 0), clearing it when
+ * clear != 0, or a negative code. */
+int snl_device_error(int clear);
+
 /* ModelConfig::validate (src/config.rs:194-240). */
 int snl_config_validate(const snl_model_config* cfg);
 
@@ -184,6 +189,16 @@ int snl_delta(const snl_step_u* step, const snl_lin_p* p, const float* proj, con
  * maximum wins); out_idx is a device u32[rows]. */
 int snl_argmax(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_idx, void* stream);
 
+/* ---- seeded synthetic tensors ------------------------------------------------------- */
+
+/* Fill device buffers with tensor `name` of the seeded synthetic model (the benchmark
+ * weights; no reference counterpart): quants (Q8_0: rows*cols bytes, Q4_0: rows*cols/2)
+ * and f32 scales (rows*cols/32), or f32 values offset + mult * z for segment `sub`. */
+int snl_synth_quant(uint64_t seed, const char* name, int dtype, size_t rows, size_t cols, void* q,
+                    float* s, void* stream);
+int snl_synth_f32(uint64_t seed, const char* name, uint32_t sub, size_t n, float mult, float offset,
+                  float* out, void* stream);
+
 /* ---- engine level (src/engine.rs) ----------------------------------------------- */
 
 typedef struct snl_engine snl_engine;
@@ -231,6 +246,24 @@ int snl_engine_forward_greedy(snl_engine* e, const uint32_t* tokens, size_t n, c
  * MTP head's logits. Returns SNL_E_STATE when the engine has no MTP head. */
 int snl_engine_mtp(snl_engine* e, size_t r0, const uint32_t* tokens, size_t n, const uint32_t* pos,
                    size_t slot0, int draft, uint32_t* draft_out);
+
+/* Greedy generation of n tokens after `first_token` entirely on the device: each
+ * step's argmax is the next step's input without a host round trip (the loop of
+ * main.rs:561-565 / worker.rs:207-213 at temperature 0). out_tokens (host) receives the
+ * n generated ids; *device_ms (optional) the CUDA-event time of the n steps. */
+int snl_engine_generate(snl_engine* e, uint32_t first_token, size_t n, uint32_t* out_tokens,
+                        float* device_ms);
+
+/* Per-op timing of one decode step (the SENSENOVA_PROFILE table of engine.rs:859-886,
+ * :939-949): runs forward([token], logits) op by op with CUDA events around each and
+ * fills up to `cap` records, aggregated by label. bytes = algorithmic bytes moved. */
+typedef struct snl_op_stat {
+  char label[32];
+  uint32_t calls;
+  double ms;
+  double bytes;
+} snl_op_stat;
+int snl_engine_profile(snl_engine* e, uint32_t token, snl_op_stat* out, size_t cap, size_t* n_out);
 
 int snl_engine_reset(snl_engine* e);                             /* engine.rs:652-660 */
 int snl_engine_snapshot(snl_engine* e, size_t slot);             /* engine.rs:662-670 */

@@ -93,6 +93,9 @@ int launch_mhc_dots(StepRef st, const snl_layer_p& p, const float* x, const floa
                     cudaStream_t s);
 int launch_mhc_finish(StepRef st, const snl_layer_p& p, const float* raw, const float* w, float* coef, uint32_t m,
                       cudaStream_t s);
+// Engine mHC router: part holds m * 16 * 9 floats of scratch.
+int launch_mhc_router(const snl_layer_p& p, const float* x, const float* w, float* part, float* coef, uint32_t m,
+                      cudaStream_t s);
 int launch_merge(StepRef st, const snl_layer_p& p, float* x, const float* coef, const float* br, uint32_t m,
                  cudaStream_t s);
 int launch_swiglu(StepRef st, const snl_layer_p& p, const float* gu, float* act, uint32_t m, cudaStream_t s);

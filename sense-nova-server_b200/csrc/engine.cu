@@ -115,6 +115,14 @@ struct snl_engine {
   std::map<uint32_t, Graph> graphs;
   bool use_graphs = true;
 
+  // Per-op timing of one eager step (snl_engine_profile).
+  struct ProfRec {
+    std::string label;
+    double bytes;
+    cudaEvent_t a, b;
+  };
+  std::vector<ProfRec>* prof = nullptr;
+
   size_t h() const { return cfg.hidden; }
 };
 
@@ -194,6 +202,26 @@ const float* find_f(const snl_engine* e, const std::string& n) {
   return it == e->fv.end() ? nullptr : it->second.p;
 }
 
+// Runs `fn` (one launch) and, while profiling, brackets it with CUDA events on the
+// engine stream under `label` with its algorithmic byte count.
+template <class F>
+int timed(snl_engine* e, const std::string& label, double bytes, F&& fn) {
+  if (!e->prof) return fn();
+  snl_engine::ProfRec r{label, bytes, nullptr, nullptr};
+  cudaEventCreate(&r.a);
+  cudaEventCreate(&r.b);
+  cudaEventRecord(r.a, e->stream);
+  int rc = fn();
+  cudaEventRecord(r.b, e->stream);
+  e->prof->push_back(r);
+  return rc;
+}
+
+double qbytes(const QT& w) {
+  const double n = (double)w.rows * w.cols;
+  return (w.dtype == SNL_Q8_0 ? n : n / 2) + n / 32 * (w.s_f16 ? 2 : 4);
+}
+
 // One matrix op (engine.rs:336-363): y[r, y_stride] for rows_m token rows.
 int mat(snl_engine* e, StepRef st, const QT& w, const float* x, size_t x_stride, float* y, size_t y_stride,
         uint32_t rows_m, uint32_t m_one = 0, uint32_t x_off = 0) {
@@ -206,7 +234,9 @@ int mat(snl_engine* e, StepRef st, const QT& w, const float* x, size_t x_stride,
   p.y_stride = (uint32_t)y_stride;
   p.n_off = 0;
   p.m_one = m_one;
-  return launch_mat(w.dtype, st, p, x, w.q, w.s, w.s_f16, y, e->stream, rows_m);
+  const double bytes = qbytes(w) + 4.0 * rows_m * (w.cols + w.rows);
+  const std::string label = "mat n=" + std::to_string(w.rows) + (m_one ? " (head)" : "");
+  return timed(e, label, bytes, [&] { return launch_mat(w.dtype, st, p, x, w.q, w.s, w.s_f16, y, e->stream, rows_m); });
 }
 
 #define SNL_TRY(expr)          \
@@ -216,13 +246,15 @@ int mat(snl_engine* e, StepRef st, const QT& w, const float* x, size_t x_stride,
   } while (0)
 
 int push_norm(snl_engine* e, StepRef st, uint32_t m, const float* router, const float* norm_w) {
+  const double h = e->cfg.hidden;
   if (router) {
     snl_layer_p p0 = layer_p(e, 0, false);
-    SNL_TRY(launch_mhc_dots(st, p0, e->x, router, e->mhc_raw, m, e->stream));
-    SNL_TRY(launch_mhc_finish(st, p0, e->mhc_raw, router, e->coef, m, e->stream));
+    SNL_TRY(timed(e, "MhcRouter", 4.0 * (16 * h + 8 + m * 2 * h),
+                  [&] { return launch_mhc_router(p0, e->x, router, e->mhc_raw, e->coef, m, e->stream); }));
   }
   snl_layer_p p = layer_p(e, router ? 1 : 0, false);
-  return launch_branch_norm(st, p, e->x, e->coef, norm_w, e->xn, m, e->stream);
+  return timed(e, "BranchNorm", 4.0 * (m * 3 * h + h),
+               [&] { return launch_branch_norm(st, p, e->x, e->coef, norm_w, e->xn, m, e->stream); });
 }
 
 // The layer loop of engine.rs:389-481 for one step of m rows.
@@ -235,15 +267,26 @@ int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
   for (size_t li : e->plan) {
     const std::string L = "l" + std::to_string(li) + ".";
     const bool mhc = snl_synth::is_mhc(c, li);
-    if (mhc && (int32_t)li == c.mhc_start) SNL_TRY(launch_merge(st, layer_p(e, 3, false), e->x, e->coef, e->branch, m, e->stream));
+    const double hb = 4.0 * m * h;
+    if (mhc && (int32_t)li == c.mhc_start)
+      SNL_TRY(timed(e, "Merge", 2 * hb, [&] { return launch_merge(st, layer_p(e, 3, false), e->x, e->coef, e->branch, m, e->stream); }));
     SNL_TRY(push_norm(e, st, m, mhc ? find_f(e, L + "mhc_attn") : nullptr, find_f(e, L + "in_ln")));
     if (c.full_attention[li]) {
       SNL_TRY(mat(e, st, *find_q(e, L + "qkv"), e->xn, h, e->proj, ap.proj_stride, m));
-      SNL_TRY(launch_attn_prep(st, ap, e->proj, e->qbuf, e->kc[full_slot], e->vc[full_slot], find_f(e, L + "qk_norm"),
-                               e->rpos, m, e->stream));
-      SNL_TRY(launch_attend(st, ap, e->proj, e->qbuf, e->kc[full_slot], e->vc[full_slot], e->attn_out, e->partial, m,
-                            parts_grid, e->stream));
-      if (parts_grid > 1) SNL_TRY(launch_attn_combine(st, ap, e->proj, e->partial, e->attn_out, m, e->stream, 1));
+      const double kvd = (double)snl_synth::kv_dim(c), qd = (double)snl_synth::q_dim(c);
+      SNL_TRY(timed(e, "AttnPrep", 4.0 * m * (qd + 2 * kvd) + 4.0 * m * qd + 2.0 * m * 2 * kvd, [&] {
+        return launch_attn_prep(st, ap, e->proj, e->qbuf, e->kc[full_slot], e->vc[full_slot], find_f(e, L + "qk_norm"),
+                                e->rpos, m, e->stream);
+      }));
+      const double keys = (double)st.val.pos0 + m;
+      SNL_TRY(timed(e, "Attend", 2.0 * 2 * kvd * keys + 4.0 * m * 2 * qd, [&] {
+        return launch_attend(st, ap, e->proj, e->qbuf, e->kc[full_slot], e->vc[full_slot], e->attn_out, e->partial, m,
+                             parts_grid, e->stream);
+      }));
+      if (parts_grid > 1)
+        SNL_TRY(timed(e, "Combine", 4.0 * m * qd * 2, [&] {
+          return launch_attn_combine(st, ap, e->proj, e->partial, e->attn_out, m, e->stream, 1);
+        }));
       SNL_TRY(mat(e, st, *find_q(e, L + "o_proj"), e->attn_out, snl_synth::q_dim(c), e->branch, h, m));
       full_slot++;
     } else {
@@ -253,18 +296,22 @@ int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
       float* cc = e->conv_ckpt + lin_slot * e->conv_elems;
       float* sc = e->lin_ckpt + lin_slot * e->state_elems;
       const float* lw = find_f(e, L + "lin");
-      SNL_TRY(launch_conv(st, lp, e->proj, e->act, cs, lw, cc, e->stream));
-      SNL_TRY(launch_delta(st, lp, e->proj, e->act, ss, lw, e->attn_out, sc, e->stream));
+      const double cdim = (double)lp.conv_dim;
+      SNL_TRY(timed(e, "Conv", 4.0 * (2 * m * cdim + 6 * cdim + 4 * cdim),
+                    [&] { return launch_conv(st, lp, e->proj, e->act, cs, lw, cc, e->stream); }));
+      SNL_TRY(timed(e, "Delta", 4.0 * (2.0 * e->state_elems + m * (cdim + 2 * 4096.0)),
+                    [&] { return launch_delta(st, lp, e->proj, e->act, ss, lw, e->attn_out, sc, e->stream); }));
       SNL_TRY(mat(e, st, *find_q(e, L + "out_proj"), e->attn_out, snl_synth::lin_value_dim(c), e->branch, h, m));
       lin_slot++;
     }
-    SNL_TRY(launch_merge(st, layer_p(e, mhc ? 1 : 0, false), e->x, e->coef, e->branch, m, e->stream));
+    SNL_TRY(timed(e, "Merge", 5 * hb, [&] { return launch_merge(st, layer_p(e, mhc ? 1 : 0, false), e->x, e->coef, e->branch, m, e->stream); }));
     SNL_TRY(push_norm(e, st, m, mhc ? find_f(e, L + "mhc_ffn") : nullptr, find_f(e, L + "post_ln")));
     SNL_TRY(mat(e, st, *find_q(e, L + "gate_up"), e->xn, h, e->proj, 2 * (size_t)c.intermediate, m));
-    SNL_TRY(launch_swiglu(st, layer_p(e, 0, false), e->proj, e->act, m, e->stream));
+    SNL_TRY(timed(e, "Swiglu", 12.0 * m * c.intermediate,
+                  [&] { return launch_swiglu(st, layer_p(e, 0, false), e->proj, e->act, m, e->stream); }));
     SNL_TRY(mat(e, st, *find_q(e, L + "down"), e->act, c.intermediate, e->branch, h, m));
     const uint32_t mode = !mhc ? 0 : ((int32_t)(li + 1) == c.mhc_end ? 2 : 1);
-    SNL_TRY(launch_merge(st, layer_p(e, mode, false), e->x, e->coef, e->branch, m, e->stream));
+    SNL_TRY(timed(e, "Merge", 5 * hb, [&] { return launch_merge(st, layer_p(e, mode, false), e->x, e->coef, e->branch, m, e->stream); }));
   }
   return SNL_OK;
 }
@@ -274,16 +321,23 @@ int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
 int device_step(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid, uint32_t rows, bool greedy) {
   const size_t h = e->h();
   const QT* emb = find_q(e, "embed");
-  SNL_TRY(launch_embed(e->tokens, m, (const int8_t*)emb->q, (const float*)emb->s, (uint32_t)h, e->cfg.vocab, e->x,
-                       nullptr, e->stream));
+  SNL_TRY(timed(e, "Embed", (double)m * h * 13, [&] {
+    return launch_embed(e->tokens, m, (const int8_t*)emb->q, (const float*)emb->s, (uint32_t)h, e->cfg.vocab, e->x,
+                        nullptr, e->stream);
+  }));
   // Row 0 of hid is the hidden state of the token before this step (engine.rs:889-890).
   SNL_CUDA_TRY(cudaMemcpyAsync(e->hid, e->hlast, h * sizeof(float), cudaMemcpyDeviceToDevice, e->stream));
   SNL_TRY(run_layers(e, st, m, parts_grid));
-  SNL_TRY(launch_branch_norm(st, layer_p(e, 0, false), e->x, e->coef, find_f(e, "norm"), e->hid + h, m, e->stream));
+  SNL_TRY(timed(e, "BranchNorm", 12.0 * m * h, [&] {
+    return launch_branch_norm(st, layer_p(e, 0, false), e->x, e->coef, find_f(e, "norm"), e->hid + h, m, e->stream);
+  }));
   if (rows > 0) {
     SNL_TRY(mat(e, st, *find_q(e, "lm_head"), e->hid, h, e->logits, e->cfg.vocab, rows, rows,
                 (uint32_t)((m - rows + 1) * h)));
-    if (greedy) SNL_TRY(launch_argmax_with(e->logits, rows, e->cfg.vocab, e->amax, e->amax_part, e->stream));
+    if (greedy)
+      SNL_TRY(timed(e, "Argmax", 4.0 * rows * e->cfg.vocab, [&] {
+        return launch_argmax_with(e->logits, rows, e->cfg.vocab, e->amax, e->amax_part, e->stream);
+      }));
   }
   SNL_CUDA_TRY(cudaMemcpyAsync(e->hlast, e->hid + (size_t)m * h, h * sizeof(float), cudaMemcpyDeviceToDevice, e->stream));
   return SNL_OK;
@@ -602,7 +656,7 @@ extern "C" int snl_engine_finalize(snl_engine* e) {
   SNL_TRY(dalloc(e, &e->logits, LOGIT_ROWS * (size_t)c.vocab));
   SNL_TRY(dalloc(e, &e->hid, (MAX_M + 1) * h));
   SNL_TRY(dalloc(e, &e->hlast, h));
-  SNL_TRY(dalloc(e, &e->mhc_raw, MAX_M * 9));
+  SNL_TRY(dalloc(e, &e->mhc_raw, MAX_M * 16 * 9));
   SNL_TRY(dalloc(e, &e->amax, LOGIT_ROWS));
   SNL_TRY(dalloc(e, &e->amax_part, LOGIT_ROWS * 128));
   SNL_TRY(dalloc(e, &e->step_d, 1));
@@ -761,6 +815,123 @@ extern "C" int snl_engine_mtp(snl_engine* e, size_t r0, const uint32_t* tokens, 
   if (draft && draft_out) {
     SNL_CUDA_TRY(cudaMemcpy(draft_out, e->amax, sizeof(uint32_t), cudaMemcpyDeviceToHost));
   }
+  return SNL_OK;
+}
+
+extern "C" int snl_engine_generate(snl_engine* e, uint32_t first_token, size_t n, uint32_t* out_tokens, float* device_ms) {
+  if (!e || !e->finalized) return fail(SNL_E_STATE, "generate: engine not finalized");
+  if (!out_tokens || n == 0) return fail(SNL_E_INVALID, "generate: needs n >= 1 and an output buffer");
+  if (e->pos + n > e->ctx)
+    return fail(SNL_E_RANGE, "context length exceeded (" + std::to_string(e->pos + n) + " > " + std::to_string(e->ctx) + ")");
+  if (first_token >= e->cfg.vocab) return fail(SNL_E_RANGE, "token id " + std::to_string(first_token) + " out of range");
+  DeviceGuard dg(e->device);
+  // Every step's descriptor and rotary positions go to device memory first, so the
+  // timed loop reads only device-resident inputs.
+  std::vector<snl_step_u> steps(n);
+  std::vector<uint32_t> rp(4 * n);
+  for (size_t i = 0; i < n; i++) {
+    const size_t p = e->pos + i;
+    steps[i] = snl_step_u{1u, (uint32_t)p, parts_for(1, p + 1), 0u};
+    for (int k = 0; k < 4; k++) rp[4 * i + k] = (uint32_t)p;
+  }
+  snl_step_u* steps_d = nullptr;
+  uint32_t *rp_d = nullptr, *gen_d = nullptr;
+  SNL_CUDA_TRY(cudaMalloc(&steps_d, n * sizeof(snl_step_u)));
+  SNL_CUDA_TRY(cudaMalloc(&rp_d, 4 * n * sizeof(uint32_t)));
+  SNL_CUDA_TRY(cudaMalloc(&gen_d, n * sizeof(uint32_t)));
+  int rc = SNL_OK;
+  cudaEvent_t t0 = nullptr, t1 = nullptr;
+  do {
+    cudaError_t ce;
+    if ((ce = cudaMemcpy(steps_d, steps.data(), n * sizeof(snl_step_u), cudaMemcpyHostToDevice)) != cudaSuccess ||
+        (ce = cudaMemcpy(rp_d, rp.data(), 4 * n * sizeof(uint32_t), cudaMemcpyHostToDevice)) != cudaSuccess ||
+        (ce = cudaMemcpy(e->tokens, &first_token, sizeof(uint32_t), cudaMemcpyHostToDevice)) != cudaSuccess) {
+      rc = cuda_fail(ce, "generate: staging");
+      break;
+    }
+    cudaEventCreate(&t0);
+    cudaEventCreate(&t1);
+    cudaEventRecord(t0, e->stream);
+    for (size_t i = 0; i < n && !rc; i++) {
+      if ((ce = cudaMemcpyAsync(e->step_d, steps_d + i, sizeof(snl_step_u), cudaMemcpyDeviceToDevice, e->stream)) ||
+          (ce = cudaMemcpyAsync(e->rpos, rp_d + 4 * i, 4 * sizeof(uint32_t), cudaMemcpyDeviceToDevice, e->stream))) {
+        rc = cuda_fail(ce, "generate: step copy");
+        break;
+      }
+      rc = run_step(e, steps[i], 1, 1, true);
+      if (rc) break;
+      if ((ce = cudaMemcpyAsync(e->tokens, e->amax, sizeof(uint32_t), cudaMemcpyDeviceToDevice, e->stream)) ||
+          (ce = cudaMemcpyAsync(gen_d + i, e->amax, sizeof(uint32_t), cudaMemcpyDeviceToDevice, e->stream))) {
+        rc = cuda_fail(ce, "generate: token copy");
+        break;
+      }
+      e->pos += 1;
+      e->hid_rows = 1;
+    }
+    cudaEventRecord(t1, e->stream);
+    if ((ce = cudaStreamSynchronize(e->stream)) != cudaSuccess) {
+      rc = cuda_fail(ce, "generate");
+      break;
+    }
+    if (!rc && device_ms) cudaEventElapsedTime(device_ms, t0, t1);
+    if (!rc && (ce = cudaMemcpy(out_tokens, gen_d, n * sizeof(uint32_t), cudaMemcpyDeviceToHost)) != cudaSuccess)
+      rc = cuda_fail(ce, "generate: read-back");
+  } while (0);
+  if (t0) cudaEventDestroy(t0);
+  if (t1) cudaEventDestroy(t1);
+  cudaFree(steps_d);
+  cudaFree(rp_d);
+  cudaFree(gen_d);
+  return rc;
+}
+
+extern "C" int snl_engine_profile(snl_engine* e, uint32_t token, snl_op_stat* out, size_t cap, size_t* n_out) {
+  if (!e || !e->finalized) return fail(SNL_E_STATE, "profile: engine not finalized");
+  if (e->pos + 1 > e->ctx) return fail(SNL_E_RANGE, "context length exceeded");
+  if (token >= e->cfg.vocab) return fail(SNL_E_RANGE, "token id " + std::to_string(token) + " out of range");
+  DeviceGuard dg(e->device);
+  std::vector<snl_engine::ProfRec> recs;
+  snl_step_u sh = {1u, (uint32_t)e->pos, parts_for(1, e->pos + 1), 0u};
+  *e->h_step = sh;
+  *e->h_tokens = token;
+  for (int k = 0; k < 4; k++) e->h_rpos[k] = (uint32_t)e->pos;
+  SNL_CUDA_TRY(cudaMemcpyAsync(e->step_d, e->h_step, sizeof(snl_step_u), cudaMemcpyHostToDevice, e->stream));
+  SNL_CUDA_TRY(cudaMemcpyAsync(e->tokens, e->h_tokens, sizeof(uint32_t), cudaMemcpyHostToDevice, e->stream));
+  SNL_CUDA_TRY(cudaMemcpyAsync(e->rpos, e->h_rpos, 4 * sizeof(uint32_t), cudaMemcpyHostToDevice, e->stream));
+  e->prof = &recs;
+  int rc = device_step(e, step_dev(e->step_d, sh), 1, sh.parts, 1, true);
+  e->prof = nullptr;
+  cudaError_t ce = cudaStreamSynchronize(e->stream);
+  std::map<std::string, snl_op_stat> agg;
+  std::vector<std::string> order;
+  for (auto& r : recs) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, r.a, r.b);
+    cudaEventDestroy(r.a);
+    cudaEventDestroy(r.b);
+    auto it = agg.find(r.label);
+    if (it == agg.end()) {
+      snl_op_stat z;
+      memset(&z, 0, sizeof(z));
+      snprintf(z.label, sizeof(z.label), "%s", r.label.c_str());
+      it = agg.emplace(r.label, z).first;
+      order.push_back(r.label);
+    }
+    it->second.calls += 1;
+    it->second.ms += ms;
+    it->second.bytes += r.bytes;
+  }
+  if (rc) return rc;
+  if (ce != cudaSuccess) return cuda_fail(ce, "profile");
+  e->pos += 1;
+  e->hid_rows = 1;
+  size_t k = 0;
+  for (auto& l : order) {
+    if (k >= cap) break;
+    if (out) out[k] = agg[l];
+    k++;
+  }
+  if (n_out) *n_out = k;
   return SNL_OK;
 }
 

@@ -111,6 +111,43 @@ __global__ void mhc_finish_kernel(StepRef sr, snl_layer_p p, const float* __rest
   mhc_coef(r, w, 2 * p.h, p.iterations, coef + m * 8);
 }
 
+// Engine-side mHC router in two launches that use many SMs: slice s of the 2H inputs
+// of token m -> part[(m * slices + s) * 9 + o]; then one warp per token sums the
+// slices and finishes the Sinkhorn step (mhc_coef).
+constexpr int kMhcSlices = 16;
+__global__ void __launch_bounds__(256) mhc_part_kernel(snl_layer_p p, const float* __restrict__ x,
+                                                       const float* __restrict__ w, float* __restrict__ part) {
+  __shared__ float sh[32];
+  const uint32_t sl = blockIdx.x, m = blockIdx.y, d = 2 * p.h;
+  const uint32_t len = d / kMhcSlices, i0 = sl * len;
+  float acc[9];
+#pragma unroll
+  for (int o = 0; o < 9; o++) acc[o] = 0.f;
+  for (uint32_t i = i0 + threadIdx.x; i < i0 + len; i += blockDim.x) {
+    const float v = x[(uint64_t)m * d + i];
+#pragma unroll
+    for (int o = 0; o < 8; o++) acc[o] = fmaf(__ldg(w + (uint64_t)o * d + i), v, acc[o]);
+    acc[8] = fmaf(v, v, acc[8]);
+  }
+#pragma unroll
+  for (int o = 0; o < 9; o++) {
+    const float t = block_sum(acc[o], sh);
+    if (threadIdx.x == 0) part[((uint64_t)m * kMhcSlices + sl) * 9 + o] = t;
+  }
+}
+__global__ void mhc_coef_kernel(snl_layer_p p, uint32_t m_rows, const float* __restrict__ part,
+                                const float* __restrict__ w, float* __restrict__ coef) {
+  const uint32_t m = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
+  if (m >= m_rows) return;
+  float r[9];
+#pragma unroll
+  for (int o = 0; o < 9; o++) {
+    float v = lane < kMhcSlices ? part[((uint64_t)m * kMhcSlices + lane) * 9 + o] : 0.f;
+    r[o] = warp_sum(v);
+  }
+  if (lane == 0) mhc_coef(r, w, 2 * p.h, p.iterations, coef + m * 8);
+}
+
 // merge (layers.wgsl:268-302).
 __global__ void merge_kernel(snl_layer_p p, uint32_t m_rows, float* __restrict__ x, const float* __restrict__ coef,
                              const float* __restrict__ br) {
@@ -258,6 +295,17 @@ int launch_mhc_finish(StepRef st, const snl_layer_p& p, const float* raw, const 
   SNL_LAUNCH_CHECK("mhc_finish");
   return SNL_OK;
 }
+int launch_mhc_router(const snl_layer_p& p, const float* x, const float* w, float* part, float* coef, uint32_t m,
+                      cudaStream_t s) {
+  if (m == 0) return SNL_OK;
+  if ((2 * p.h) % kMhcSlices) return fail(SNL_E_INVALID, "mhc: 2H must divide into slices");
+  mhc_part_kernel<<<dim3(kMhcSlices, m), 256, 0, s>>>(p, x, w, part);
+  SNL_LAUNCH_CHECK("mhc_part");
+  mhc_coef_kernel<<<(m + 3) / 4, 128, 0, s>>>(p, m, part, w, coef);
+  SNL_LAUNCH_CHECK("mhc_coef");
+  return SNL_OK;
+}
+
 int launch_merge(StepRef st, const snl_layer_p& p, float* x, const float* coef, const float* br, uint32_t m,
                  cudaStream_t s) {
   (void)st;
@@ -377,4 +425,16 @@ extern "C" int snl_swiglu(const snl_step_u* step, const snl_layer_p* p, const fl
 extern "C" int snl_argmax(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_idx, void* stream) {
   if (!logits || !out_idx || n == 0) return snl::fail(SNL_E_INVALID, "snl_argmax: bad argument");
   return snl::launch_argmax(logits, rows, n, out_idx, (cudaStream_t)stream);
+}
+
+extern "C" int snl_synth_quant(uint64_t seed, const char* name, int dtype, size_t rows, size_t cols, void* q, float* s,
+                               void* stream) {
+  if (!name || !q || !s) return snl::fail(SNL_E_INVALID, "snl_synth_quant: null argument");
+  if (dtype != SNL_Q8_0 && dtype != SNL_Q4_0) return snl::fail(SNL_E_INVALID, "snl_synth_quant: dtype");
+  return snl::launch_gen_quant(seed, name, dtype, rows, cols, q, s, (cudaStream_t)stream);
+}
+extern "C" int snl_synth_f32(uint64_t seed, const char* name, uint32_t sub, size_t n, float mult, float offset,
+                             float* out, void* stream) {
+  if (!name || !out) return snl::fail(SNL_E_INVALID, "snl_synth_f32: null argument");
+  return snl::launch_gen_f32(seed, name, sub, n, mult, offset, out, (cudaStream_t)stream);
 }

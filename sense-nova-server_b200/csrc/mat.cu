@@ -11,9 +11,18 @@
 // non-allocating loads of whole weight chunks, converts int8/nibbles to f32 with a
 // byte-permute into the mantissa of 2^23 (exact), and the per-row sums are reduced
 // with warp shuffles. Larger m goes to a tiled GEMM.
+#include <algorithm>
+#include <cstdlib>
+
 #include "common.cuh"
+#include "ptx.cuh"
 
 namespace snl {
+
+// Device error word of this library's bounded waits (no allocation). Read and cleared
+// by snl_device_error().
+__device__ int g_dev_error;
+
 namespace {
 
 constexpr int kRowsPerWarp = 4;
@@ -233,10 +242,255 @@ __global__ void __launch_bounds__(256) gemm_kernel(snl_mat_p p, uint32_t m_rows,
   }
 }
 
+
+// ---------------------------------------------------------------------------------
+// Streaming GEMV (1-2 token rows) with bulk async copies.
+//
+// Each warp is an independent streaming unit: it owns groups of kSRows weight rows
+// (group g = global warp id + i * total warps) and walks each group's K range in chunks
+// of `chunk` bytes per row. Lanes 0..2*kSRows-1 issue one cp.async.bulk each per stage
+// (a row's weight chunk, a row's scale chunk) into a per-warp ring of `stages` stages
+// that completes on that stage's mbarrier, so stages * kSRows * (chunk + scales) bytes
+// are in flight per warp whatever the register budget. x is staged once per CTA in
+// shared memory. Weights carry an L2 evict-first policy: they are read once per token,
+// while x, the KV cache and the recurrent state should stay in L2.
+// ---------------------------------------------------------------------------------
+constexpr int kSWarps = 8;
+constexpr int kSRows = 4;
+constexpr int kSMaxStages = 4;
+
+__host__ __device__ constexpr uint32_t align16u(uint32_t v) { return (v + 15u) & ~15u; }
+
+template <int DT, int M, typename ST>
+__global__ void __launch_bounds__(kSWarps * 32, 1)
+    gemv_stream_kernel(snl_mat_p p, const float* __restrict__ x, const uint8_t* __restrict__ wq,
+                       const ST* __restrict__ ws, float* __restrict__ y, uint32_t chunk, uint32_t stages) {
+  constexpr uint32_t EPB = DT == SNL_Q8_0 ? 1 : 2;  // elements per weight byte
+  constexpr uint32_t EPC = 16 * EPB;                // elements per 16-byte chunk
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t K = p.k;
+  const uint32_t row_bytes = K / EPB;
+  const uint32_t nchunk = row_bytes / chunk;
+  const uint32_t chunk_elems = chunk * EPB;
+  const uint32_t sc_bytes = chunk_elems / 32 * (uint32_t)sizeof(ST);
+  const uint32_t stage_bytes = kSRows * (chunk + sc_bytes);
+  const uint32_t x_bytes = align16u(M * K * 4);
+  float* xs = reinterpret_cast<float*>(smem);
+  uint8_t* ring = smem + x_bytes + (uint32_t)warp * stages * stage_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + x_bytes + kSWarps * stages * stage_bytes) + warp * kSMaxStages;
+
+  const uint32_t groups = (p.n + kSRows - 1) / kSRows;
+  const uint32_t gw = blockIdx.x * kSWarps + warp;
+  const uint32_t nw = gridDim.x * kSWarps;
+  const uint32_t my_groups = gw < groups ? (groups - gw + nw - 1) / nw : 0;
+  const uint32_t njobs = my_groups * nchunk;
+
+  if (lane == 0)
+    for (uint32_t s = 0; s < stages; s++) mbar_init(&bars[s], 1);
+  fence_mbar_init();
+  __syncwarp();
+  const uint64_t pol = l2_policy_evict_first();
+
+  auto issue = [&](uint32_t j) {
+    const uint32_t s = j % stages;
+    const uint32_t row0 = (gw + (j / nchunk) * nw) * kSRows;
+    const uint32_t c = j % nchunk;
+    const uint32_t rows = min((uint32_t)kSRows, p.n - row0);
+    uint8_t* st = ring + s * stage_bytes;
+    if (lane == 0) mbar_arrive_expect_tx(&bars[s], rows * (chunk + sc_bytes));
+    __syncwarp();
+    if ((uint32_t)lane < rows) {
+      const uint32_t r = lane;
+      bulk_g2s(st + r * chunk, wq + (uint64_t)(row0 + r) * row_bytes + (uint64_t)c * chunk, chunk, &bars[s], pol);
+    } else if (lane >= kSRows && (uint32_t)(lane - kSRows) < rows) {
+      const uint32_t r = lane - kSRows;
+      const uint8_t* src = reinterpret_cast<const uint8_t*>(ws) +
+                           ((uint64_t)(row0 + r) * (K / 32) + (uint64_t)c * (chunk_elems / 32)) * sizeof(ST);
+      bulk_g2s(st + kSRows * chunk + r * sc_bytes, src, sc_bytes, &bars[s], pol);
+    }
+  };
+
+  const uint32_t pre = min(stages, njobs);
+  for (uint32_t j = 0; j < pre; j++) issue(j);
+
+  // Stage x (M rows of K floats) while the first weight chunks are in flight.
+  {
+    float4* xs4 = reinterpret_cast<float4*>(xs);
+    const uint32_t k4 = K / 4;
+    for (uint32_t i = threadIdx.x; i < M * k4; i += blockDim.x) {
+      const uint32_t t = i / k4, e = i % k4;
+      xs4[i] = __ldg(reinterpret_cast<const float4*>(x + p.x_off + (uint64_t)t * p.x_stride) + e);
+    }
+  }
+  __syncthreads();
+
+  float acc[M][kSRows];
+#pragma unroll
+  for (int t = 0; t < M; t++)
+#pragma unroll
+    for (int r = 0; r < kSRows; r++) acc[t][r] = 0.f;
+
+  uint32_t j = 0;
+  bool ok = true;
+  for (; j < njobs; j++) {
+    const uint32_t s = j % stages;
+    if (!mbar_wait_bounded(&bars[s], (j / stages) & 1)) {
+      ok = false;
+      break;
+    }
+    const uint32_t row0 = (gw + (j / nchunk) * nw) * kSRows;
+    const uint32_t c = j % nchunk;
+    const uint32_t rows = min((uint32_t)kSRows, p.n - row0);
+    const uint8_t* st = ring + s * stage_bytes;
+    for (uint32_t q = lane; q < chunk / 16; q += 32) {
+      const uint32_t e0 = c * chunk_elems + q * EPC;
+      float xv[M][EPC];
+#pragma unroll
+      for (int t = 0; t < M; t++) {
+        const float4* xp = reinterpret_cast<const float4*>(xs + t * K + e0);
+#pragma unroll
+        for (uint32_t i = 0; i < EPC / 4; i++) {
+          const float4 v = xp[i];
+          xv[t][4 * i] = v.x;
+          xv[t][4 * i + 1] = v.y;
+          xv[t][4 * i + 2] = v.z;
+          xv[t][4 * i + 3] = v.w;
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < kSRows; r++) {
+        if ((uint32_t)r >= rows) break;
+        const uint4 w = *reinterpret_cast<const uint4*>(st + r * chunk + q * 16);
+        const ST* scp = reinterpret_cast<const ST*>(st + kSRows * chunk + r * sc_bytes);
+        float sc;
+        if constexpr (sizeof(ST) == 4) sc = scp[q * EPC / 32];
+        else sc = __half2float(scp[q * EPC / 32]);
+        const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+        float d[M];
+#pragma unroll
+        for (int t = 0; t < M; t++) d[t] = 0.f;
+#pragma unroll
+        for (int qq = 0; qq < 4; qq++) {
+          if constexpr (DT == SNL_Q8_0) {
+            float f[4];
+            q8_word(wv[qq], f);
+#pragma unroll
+            for (int t = 0; t < M; t++)
+#pragma unroll
+              for (int e = 0; e < 4; e++) d[t] = fmaf(f[e], xv[t][4 * qq + e], d[t]);
+          } else {
+            float f[8];
+            q4_word(wv[qq], f);
+#pragma unroll
+            for (int t = 0; t < M; t++)
+#pragma unroll
+              for (int e = 0; e < 8; e++) d[t] = fmaf(f[e], xv[t][8 * qq + e], d[t]);
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < M; t++) acc[t][r] = fmaf(sc, d[t], acc[t][r]);
+      }
+    }
+    // Stage s is consumed: order the reads before the async refill, then refill it.
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (j + stages < njobs) issue(j + stages);
+    if (c == nchunk - 1) {
+#pragma unroll
+      for (int t = 0; t < M; t++)
+#pragma unroll
+        for (int r = 0; r < kSRows; r++) acc[t][r] = warp_sum(acc[t][r]);
+      if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < kSRows; r++) {
+          if ((uint32_t)r < rows) {
+#pragma unroll
+            for (int t = 0; t < M; t++) y[p.y_off + (uint64_t)t * p.y_stride + p.n_off + row0 + r] = acc[t][r];
+          }
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < M; t++)
+#pragma unroll
+        for (int r = 0; r < kSRows; r++) acc[t][r] = 0.f;
+    }
+  }
+  if (!ok) {
+    // Drain the copies this warp still has in flight (bounded) before exiting.
+    if (lane == 0) report_timeout(&g_dev_error);
+    const uint32_t last = min(njobs, j + stages);
+    for (uint32_t k = j; k < last; k++) (void)mbar_wait_bounded(&bars[k % stages], (k / stages) & 1);
+  }
+}
+
+struct StreamCfg {
+  uint32_t chunk, stages, smem;
+};
+
+// Chooses chunk bytes and stages for the streaming kernel, or returns false if the
+// shape cannot use it (row bytes not a multiple of 256, x not fitting next to 2 stages).
+template <typename ST>
+bool stream_cfg(int dtype, uint32_t k, int M, StreamCfg* c) {
+  const uint32_t epb = dtype == SNL_Q8_0 ? 1 : 2;
+  const uint32_t row_bytes = k / epb;
+  if (row_bytes % 256) return false;
+  uint32_t chunk = 1024;
+  while (row_bytes % chunk) chunk /= 2;
+  const uint32_t sc = chunk * epb / 32 * sizeof(ST);
+  const uint32_t stage = kSRows * (chunk + sc);
+  const uint32_t xb = align16u(M * k * 4);
+  const uint32_t limit = 227 * 1024;
+  for (uint32_t s = kSMaxStages; s >= 2; s--) {
+    const uint32_t total = xb + kSWarps * s * stage + kSWarps * kSMaxStages * 8;
+    if (total <= limit) {
+      *c = StreamCfg{chunk, s, total};
+      return true;
+    }
+  }
+  return false;
+}
+
+int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!cached[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+template <int DT, int M, typename ST>
+int launch_stream(const snl_mat_p& p, const float* x, const void* wq, const ST* ws, float* y, const StreamCfg& c,
+                  cudaStream_t s) {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto kern = gemv_stream_kernel<DT, M, ST>;
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return cuda_fail(e, "gemv_stream: smem attribute");
+    attr_set[dev] = true;
+  }
+  const uint32_t groups = (p.n + kSRows - 1) / kSRows;
+  const uint32_t grid = std::min<uint32_t>((groups + kSWarps - 1) / kSWarps, (uint32_t)num_sms());
+  kern<<<grid, kSWarps * 32, c.smem, s>>>(p, x, static_cast<const uint8_t*>(wq), ws, y, c.chunk, c.stages);
+  SNL_LAUNCH_CHECK("gemv_stream");
+  return SNL_OK;
+}
+
 template <int DT, typename ST>
 int launch_mat_t(const snl_mat_p& p, uint32_t rows_m, const float* x, const void* wq, const ST* ws, float* y,
                  cudaStream_t s) {
   const uint8_t* w = static_cast<const uint8_t*>(wq);
+  StreamCfg sc;
+  if (rows_m <= 2 && !getenv("SNL_GEMV_DIRECT") && stream_cfg<ST>(DT, p.k, (int)rows_m, &sc)) {
+    return rows_m == 1 ? launch_stream<DT, 1, ST>(p, x, wq, ws, y, sc, s) : launch_stream<DT, 2, ST>(p, x, wq, ws, y, sc, s);
+  }
   if (rows_m == 1) {
     dim3 grid((p.n + kWarps * kRowsPerWarp - 1) / (kWarps * kRowsPerWarp));
     gemv_kernel<DT, 1, ST><<<grid, 256, 0, s>>>(p, x, w, ws, y);
@@ -270,6 +524,17 @@ int launch_mat(int dtype, StepRef st, const snl_mat_p& p, const float* x, const 
 }
 
 }  // namespace snl
+
+extern "C" int snl_device_error(int clear) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, snl::g_dev_error, sizeof(int));
+  if (e != cudaSuccess) return snl::cuda_fail(e, "snl_device_error");
+  if (clear && v) {
+    const int z = 0;
+    cudaMemcpyToSymbol(snl::g_dev_error, &z, sizeof(int));
+  }
+  return v;
+}
 
 extern "C" int snl_mat(int dtype, const snl_step_u* step, const snl_mat_p* p, const float* x, const void* wq,
                        const float* ws, float* y, void* stream) {

@@ -168,6 +168,31 @@ class Engine:
         rows = min(logit_rows, n - (max(n - 1, 0) // 512) * 512)
         return [int(v) for v in out[:rows]]
 
+    def generate(self, first_token: int, n: int) -> tuple[list[int], float]:
+        """Greedy generation of n tokens with the argmax fed back on the device.
+        Returns (tokens, device milliseconds of the n steps)."""
+        out = np.zeros(n, dtype=np.uint32)
+        ms = C.c_float(0.0)
+        ffi.check(self.lib.snl_engine_generate(self._h, first_token, n, out.ctypes.data, C.byref(ms)))
+        return [int(v) for v in out], float(ms.value)
+
+    def profile(self, token: int) -> list[dict]:
+        """One decode step op by op (engine.rs:859-886): [{label, calls, ms, bytes}]."""
+        cap = 64
+        arr = (ffi.OpStat * cap)()
+        n = C.c_size_t(0)
+        ffi.check(self.lib.snl_engine_profile(self._h, token, arr, cap, C.byref(n)))
+        return [{"label": arr[i].label.decode(), "calls": arr[i].calls, "ms": arr[i].ms, "bytes": arr[i].bytes}
+                for i in range(n.value)]
+
+    def print_profile(self, rows: list[dict]) -> None:
+        """The table of Engine::print_profile (engine.rs:938-949)."""
+        total = sum(r["ms"] for r in rows) or 1.0
+        print(f"{'op':<28} {'total ms':>10} {'share':>8} {'calls':>10} {'GB/s':>8}")
+        for r in sorted(rows, key=lambda r: -r["ms"]):
+            gbs = r["bytes"] / (r["ms"] * 1e6) if r["ms"] > 0 else 0.0
+            print(f"{r['label']:<28} {r['ms']:>10.3f} {100 * r['ms'] / total:>7.1f}% {r['calls']:>10} {gbs:>8.0f}")
+
     def mtp(self, r0: int, tokens: Sequence[int], pos: Sequence[Sequence[int]], slot0: int,
             draft: bool) -> int | None:
         """engine.rs:708-774: None without an MTP head or without `draft`."""

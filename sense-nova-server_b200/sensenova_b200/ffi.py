@@ -66,6 +66,11 @@ class ModelConfigC(C.Structure):
     ]
 
 
+class OpStat(C.Structure):
+    """snl_op_stat: one row of the per-op profile."""
+    _fields_ = [("label", C.c_char * 32), ("calls", C.c_uint32), ("ms", C.c_double), ("bytes", C.c_double)]
+
+
 class SnlError(RuntimeError):
     def __init__(self, code: int, msg: str):
         super().__init__(msg)
@@ -85,6 +90,7 @@ SIGNATURES = {
     "snl_last_error": (C.c_char_p, []),
     "snl_version": (C.c_char_p, []),
     "snl_launch_count": (u64, []),
+    "snl_device_error": (i32, [i32]),
     "snl_config_validate": (i32, [P(ModelConfigC)]),
     "snl_mat": (i32, [i32, P(StepU), P(MatP), vp, vp, vp, vp, vp]),
     "snl_branch_norm": (i32, [P(StepU), P(LayerP), vp, vp, vp, vp, u32, vp]),
@@ -98,6 +104,8 @@ SIGNATURES = {
     "snl_conv": (i32, [P(StepU), P(LinP), vp, vp, vp, vp, vp, vp]),
     "snl_delta": (i32, [P(StepU), P(LinP), vp, vp, vp, vp, vp, vp, vp]),
     "snl_argmax": (i32, [vp, u32, u32, vp, vp]),
+    "snl_synth_quant": (i32, [u64, C.c_char_p, i32, sz, sz, vp, vp, vp]),
+    "snl_synth_f32": (i32, [u64, C.c_char_p, u32, sz, C.c_float, C.c_float, vp, vp]),
     "snl_engine_create": (i32, [P(ModelConfigC), sz, i32, u32, P(vp)]),
     "snl_engine_set_tensor": (i32, [vp, C.c_char_p, i32, sz, sz, vp, vp]),
     "snl_engine_fill_synthetic": (i32, [vp, u64, i32]),
@@ -106,6 +114,8 @@ SIGNATURES = {
     "snl_engine_forward_mm": (i32, [vp, vp, sz, vp, vp, vp, sz, sz, i32, vp]),
     "snl_engine_forward_greedy": (i32, [vp, vp, sz, vp, sz, i32, vp]),
     "snl_engine_mtp": (i32, [vp, sz, vp, sz, vp, sz, i32, vp]),
+    "snl_engine_generate": (i32, [vp, u32, sz, vp, P(C.c_float)]),
+    "snl_engine_profile": (i32, [vp, u32, P(OpStat), sz, P(sz)]),
     "snl_engine_reset": (i32, [vp]),
     "snl_engine_snapshot": (i32, [vp, sz]),
     "snl_engine_restore": (i32, [vp, sz, sz]),

@@ -1,0 +1,343 @@
+"""Parity of every CUDA kernel with the CPU oracle, through the C ABI.
+
+Inputs are seeded; device buffers are torch tensors (plumbing only). The bar is the
+one BASELINE.json states: fp32 results within 1e-3 relative error per kernel
+(max |gpu - oracle| / max |oracle|); quantized values and argmax indices bit-exact.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from sensenova_b200 import ffi
+from sensenova_b200.ffi import AttnP, LayerP, LinP, MatP, StepU, SNL_Q4_0, SNL_Q8_0
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3  # fp32 accumulate within 1e-3 relative error per kernel
+
+
+def rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def T(torch_cuda):
+    return torch_cuda
+
+
+_keep = []  # device tensors stay alive until the test's kernels have run
+
+
+@pytest.fixture(autouse=True)
+def _release_buffers():
+    yield
+    import torch
+
+    torch.cuda.synchronize()
+    _keep.clear()
+
+
+def dev(T, a):
+    t = T.from_numpy(np.ascontiguousarray(a)).cuda()
+    _keep.append(t)
+    return t
+
+
+def host(t):
+    import torch
+
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def ptr(t):
+    return C.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def call(rc):
+    ffi.check(rc)
+
+
+# ---- synthetic generator: device == host, bit for bit --------------------------------
+
+
+@pytest.mark.parametrize("dtype", [SNL_Q8_0, SNL_Q4_0])
+def test_synth_quant_bit_exact(T, lib, orc, dtype):
+    rows, cols = 300, 1024
+    q_ref, s_ref = orc.gen_quant(42, "l3.gate_up", dtype, rows, cols)
+    q = T.empty(q_ref.size, dtype=T.uint8, device="cuda")
+    s = T.empty(s_ref.size, dtype=T.float32, device="cuda")
+    call(lib.snl_synth_quant(42, b"l3.gate_up", dtype, rows, cols, ptr(q), ptr(s), None))
+    assert np.array_equal(host(q), q_ref)
+    assert np.array_equal(host(s).view(np.uint32), s_ref.view(np.uint32))
+    # fp16-exact scales (the benchmark's "fp16 scale per block")
+    assert np.array_equal(s_ref.astype(np.float16).astype(np.float32), s_ref)
+
+
+def test_synth_f32_bit_exact(T, lib, orc):
+    ref = orc.gen_f32(9, "l0.lin", 3, 5000, 0.1, 1.0)
+    out = T.empty(5000, dtype=T.float32, device="cuda")
+    call(lib.snl_synth_f32(9, b"l0.lin", 3, 5000, 0.1, 1.0, ptr(out), None))
+    assert np.array_equal(host(out).view(np.uint32), ref.view(np.uint32))
+
+
+# ---- matmul.wgsl -------------------------------------------------------------------
+
+
+def run_mat(T, lib, orc, dtype, n, k, m, x_stride=None, y_stride=None, x_off=0, m_one=0, seed=0):
+    rng = np.random.default_rng(seed)
+    q, s = orc.gen_quant(seed + 1, "w", dtype, n, k)
+    xs = x_stride or k
+    ys = y_stride or n
+    rows = m_one or m
+    x = rng.standard_normal(x_off + max(rows, 1) * xs).astype(np.float32)
+    y_ref = np.zeros(rows * ys, dtype=np.float32)
+    p = MatP(n, k, x_off, xs, 0, ys, 0, m_one)
+    st = StepU(m, 0, 1, 0)
+    orc.mat(dtype, st, p, x, q, s, y_ref)
+    yd = T.zeros(rows * ys, dtype=T.float32, device="cuda")
+    call(lib.snl_mat(dtype, C.byref(st), C.byref(p), ptr(dev(T, x)), ptr(dev(T, q)), ptr(dev(T, s)), ptr(yd), None))
+    return host(yd), y_ref
+
+
+@pytest.mark.parametrize("dtype", [SNL_Q8_0, SNL_Q4_0])
+@pytest.mark.parametrize("m", [1, 2, 3, 8, 9, 64, 130])
+def test_mat_rows(T, lib, orc, dtype, m):
+    y, ref = run_mat(T, lib, orc, dtype, 200, 1024, m, seed=m)
+    assert rel(y, ref) < TOL
+
+
+@pytest.mark.parametrize("dtype", [SNL_Q8_0, SNL_Q4_0])
+def test_mat_config1_shape(T, lib, orc, dtype):
+    # The benchmark GEMV: W [12288 x 4096], one token.
+    y, ref = run_mat(T, lib, orc, dtype, 12288, 4096, 1, seed=5)
+    assert rel(y, ref) < TOL
+    assert rel(y, ref) < 1e-5  # well inside the bar: same fp32 math, another order
+
+
+@pytest.mark.parametrize("n", [1, 5, 33, 127])
+def test_mat_ragged_rows(T, lib, orc, n):
+    for m in (1, 2, 11):
+        y, ref = run_mat(T, lib, orc, SNL_Q8_0, n, 96, m, seed=n)
+        assert rel(y, ref) < TOL
+
+
+def test_mat_strides_offsets(T, lib, orc):
+    # head-style call: x_off picks the last rows, m_one fixes the count, y strided
+    y, ref = run_mat(T, lib, orc, SNL_Q8_0, 64, 256, 5, x_stride=256, y_stride=80, x_off=4 * 256, m_one=2, seed=3)
+    assert rel(y, ref) < TOL
+
+
+def test_mat_rejects_misaligned(T, lib):
+    st, p = StepU(1, 0, 1, 0), MatP(8, 32, 2, 32, 0, 8, 0, 0)
+    buf = T.zeros(1024, device="cuda")
+    rc = lib.snl_mat(SNL_Q8_0, C.byref(st), C.byref(p), ptr(buf), ptr(buf), ptr(buf), ptr(buf), None)
+    assert rc == -1 and b"multiples of 4" in lib.snl_last_error()
+
+
+# ---- layers.wgsl --------------------------------------------------------------------
+
+
+def lp(h, mode=0, last_row=0, inter=0, x_stride=0):
+    return LayerP(h, mode, last_row, 1e-6, 1.0, 20, inter, x_stride)
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_branch_norm(T, lib, orc, mode):
+    rng = np.random.default_rng(mode)
+    m, h = 7, 4096
+    x = rng.standard_normal((m, 2 * h)).astype(np.float32)
+    coef = rng.uniform(0.1, 1, (m, 8)).astype(np.float32)
+    w = (0.1 * rng.standard_normal(h)).astype(np.float32)
+    ref = np.zeros((m, h), np.float32)
+    st, p = StepU(m, 0, 1, 0), lp(h, mode)
+    orc.branch_norm(st, p, x, coef, w, ref, m)
+    out = T.zeros((m, h), device="cuda")
+    call(lib.snl_branch_norm(C.byref(st), C.byref(p), ptr(dev(T, x)), ptr(dev(T, coef)), ptr(dev(T, w)), ptr(out), m, None))
+    assert rel(host(out), ref) < TOL
+
+
+def test_branch_norm_last_row(T, lib, orc):
+    rng = np.random.default_rng(2)
+    m, h = 5, 512
+    x = rng.standard_normal((m, h)).astype(np.float32)
+    w = (0.1 * rng.standard_normal(h)).astype(np.float32)
+    st, p = StepU(m, 0, 1, 0), lp(h, 0, last_row=1, x_stride=h)
+    ref = np.zeros(h, np.float32)
+    orc.branch_norm(st, p, x, None, w, ref, 1)
+    out = T.zeros(h, device="cuda")
+    call(lib.snl_branch_norm(C.byref(st), C.byref(p), ptr(dev(T, x)), None, ptr(dev(T, w)), ptr(out), 1, None))
+    assert rel(host(out), ref) < TOL
+
+
+def test_mhc(T, lib, orc):
+    rng = np.random.default_rng(3)
+    m, h = 3, 4096
+    d = 2 * h
+    x = rng.standard_normal((m, d)).astype(np.float32)
+    w = np.concatenate([0.02 * rng.standard_normal(8 * d), 0.1 * rng.standard_normal(8)]).astype(np.float32)
+    st, p = StepU(m, 0, 1, 0), lp(h)
+    raw_ref = np.zeros((m, 9), np.float32)
+    coef_ref = np.zeros((m, 8), np.float32)
+    orc.mhc_dots(st, p, x, w, raw_ref)
+    orc.mhc_finish(st, p, raw_ref, w, coef_ref)
+    raw = T.zeros((m, 9), device="cuda")
+    coef = T.zeros((m, 8), device="cuda")
+    xd, wd = dev(T, x), dev(T, w)
+    call(lib.snl_mhc_dots(C.byref(st), C.byref(p), ptr(xd), ptr(wd), ptr(raw), None))
+    call(lib.snl_mhc_finish(C.byref(st), C.byref(p), ptr(raw), ptr(wd), ptr(coef), None))
+    assert rel(host(raw), raw_ref) < TOL
+    assert rel(host(coef), coef_ref) < TOL
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2, 3])
+def test_merge(T, lib, orc, mode):
+    rng = np.random.default_rng(mode)
+    m, h = 3, 4096
+    x = rng.standard_normal((m, 2 * h)).astype(np.float32)
+    coef = rng.uniform(0, 1, (m, 8)).astype(np.float32)
+    br = rng.standard_normal((m, h)).astype(np.float32)
+    st, p = StepU(m, 0, 1, 0), lp(h, mode)
+    xr = x.copy()
+    orc.merge(st, p, xr, coef, br)
+    xd = dev(T, x)
+    call(lib.snl_merge(C.byref(st), C.byref(p), ptr(xd), ptr(dev(T, coef)), ptr(dev(T, br)), None))
+    assert rel(host(xd), xr) < TOL
+
+
+def test_swiglu(T, lib, orc):
+    rng = np.random.default_rng(4)
+    m, inter = 4, 12288
+    gu = rng.standard_normal((m, 2 * inter)).astype(np.float32)
+    st, p = StepU(m, 0, 1, 0), lp(4096, inter=inter)
+    ref = np.zeros((m, inter), np.float32)
+    orc.swiglu(st, p, gu, ref)
+    out = T.zeros((m, inter), device="cuda")
+    call(lib.snl_swiglu(C.byref(st), C.byref(p), ptr(dev(T, gu)), ptr(out), None))
+    assert rel(host(out), ref) < TOL
+
+
+@pytest.mark.parametrize("n", [1, 7, 1000, 248320])
+def test_argmax_exact(T, lib, orc, n):
+    rng = np.random.default_rng(n)
+    v = rng.standard_normal((2, n)).astype(np.float32)
+    if n > 10:
+        v[0, n // 3] = v[0, n // 2] = 10.0  # tie: the first wins
+    out = T.zeros(2, dtype=T.int32, device="cuda")
+    call(lib.snl_argmax(ptr(dev(T, v)), 2, n, ptr(out), None))
+    got = host(out).view(np.uint32)
+    assert list(got) == [orc.argmax(v[0]), orc.argmax(v[1])]
+
+
+# ---- attention.wgsl -------------------------------------------------------------------
+
+
+def attn_case(rng, m, pos0, n_kv=4, ctx=None):
+    nh = 4 * n_kv
+    HD = 256
+    q_dim, kv_dim = nh * HD, n_kv * HD
+    stride = 2 * q_dim + 2 * kv_dim
+    ctx = ctx or pos0 + m + 8
+    p = AttnP(nh, n_kv, 64, stride, 1e7, 1e-6, 1 / 16, (33 << 16) | 30)
+    proj = rng.standard_normal((m, stride)).astype(np.float32)
+    norms = (0.1 * rng.standard_normal(2 * HD)).astype(np.float32)
+    kc = np.zeros(ctx * kv_dim // 2, np.uint32)
+    vc = np.zeros_like(kc)
+    kc[: pos0 * kv_dim // 2] = rng.standard_normal(pos0 * kv_dim).astype(np.float16).view(np.uint32)
+    vc[: pos0 * kv_dim // 2] = rng.standard_normal(pos0 * kv_dim).astype(np.float16).view(np.uint32)
+    rpos = np.stack([np.arange(pos0, pos0 + m), np.arange(pos0, pos0 + m) + 3, np.arange(pos0, pos0 + m) + 7,
+                     np.zeros(m)], 1).astype(np.uint32)
+    return p, proj, norms, kc, vc, rpos
+
+
+@pytest.mark.parametrize("m,pos0", [(1, 0), (1, 300), (3, 17), (40, 100)])
+def test_attn_prep(T, lib, orc, m, pos0):
+    rng = np.random.default_rng(m + pos0)
+    p, proj, norms, kc, vc, rpos = attn_case(rng, m, pos0)
+    st = StepU(m, pos0, 1, 0)
+    q_ref = np.zeros((m, p.n_heads * 256), np.float32)
+    kr, vr = kc.copy(), vc.copy()
+    orc.attn_prep(st, p, proj, q_ref, kr, vr, norms, rpos)
+    qd = T.zeros((m, p.n_heads * 256), device="cuda")
+    kd, vd = dev(T, kc.view(np.int32)), dev(T, vc.view(np.int32))
+    call(lib.snl_attn_prep(C.byref(st), C.byref(p), ptr(dev(T, proj)), ptr(qd), ptr(kd), ptr(vd), ptr(dev(T, norms)),
+                           ptr(dev(T, rpos.view(np.int32))), None))
+    assert rel(host(qd), q_ref) < TOL
+    kg = host(kd).view(np.uint32).view(np.float16).astype(np.float32)
+    assert rel(kg, kr.view(np.float16).astype(np.float32)) < TOL
+    assert np.array_equal(host(vd).view(np.uint32), vr)  # V is stored without math: bit-exact
+
+
+@pytest.mark.parametrize("m,pos0,parts", [(1, 0, 1), (1, 255, 1), (1, 1000, 4), (1, 2047, 8), (2, 5000, 20),
+                                          (4, 700, 64), (9, 50, 1), (64, 200, 1)])
+def test_attend_combine(T, lib, orc, m, pos0, parts):
+    rng = np.random.default_rng(pos0 + m)
+    p, proj, norms, kc, vc, rpos = attn_case(rng, m, pos0)
+    kv_dim = p.n_kv * 256
+    n = (pos0 + m) * kv_dim // 2
+    kc[:n] = rng.standard_normal(2 * n).astype(np.float16).view(np.uint32)
+    vc[:n] = rng.standard_normal(2 * n).astype(np.float16).view(np.uint32)
+    qbuf = rng.standard_normal((m, p.n_heads * 256)).astype(np.float32)
+    st = StepU(m, pos0, parts, 0)
+    out_ref = np.zeros((m, p.n_heads * 256), np.float32)
+    part_ref = np.zeros((m * p.n_heads * parts, 258), np.float32)
+    orc.attend(st, p, proj, qbuf, kc, vc, out_ref, part_ref)
+    if parts > 1:
+        orc.attn_combine(st, p, proj, part_ref, out_ref)
+    out = T.zeros((m, p.n_heads * 256), device="cuda")
+    part = T.zeros((m * p.n_heads * parts, 258), device="cuda")
+    projd = dev(T, proj)
+    call(lib.snl_attend(C.byref(st), C.byref(p), ptr(projd), ptr(dev(T, qbuf)), ptr(dev(T, kc.view(np.int32))),
+                        ptr(dev(T, vc.view(np.int32))), ptr(out), ptr(part), None))
+    if parts > 1:
+        call(lib.snl_attn_combine(C.byref(st), C.byref(p), ptr(projd), ptr(part), ptr(out), None))
+    assert rel(host(out), out_ref) < TOL
+
+
+# ---- linear.wgsl --------------------------------------------------------------------
+
+
+def lin_case(rng, m, n_k=16, n_v=32):
+    cd = 2 * n_k * 128 + n_v * 128
+    stride = cd + n_v * 128 + 2 * n_v
+    lpp = LinP(cd, stride, n_k, n_v, 1e-6, (0, 0, 0))
+    proj = rng.standard_normal((m, stride)).astype(np.float32)
+    lw = np.concatenate([0.5 * rng.standard_normal(cd * 4), 0.1 * rng.standard_normal(n_v),
+                         0.1 * rng.standard_normal(n_v), 1 + 0.1 * rng.standard_normal(128)]).astype(np.float32)
+    return lpp, proj, lw, cd
+
+
+@pytest.mark.parametrize("m,ckpt", [(1, 0), (2, 1), (37, 0)])
+def test_conv(T, lib, orc, m, ckpt):
+    rng = np.random.default_rng(m)
+    lpp, proj, lw, cd = lin_case(rng, m)
+    cs = rng.standard_normal((3, cd)).astype(np.float32)
+    st = StepU(m, 0, 1, ckpt)
+    out_ref, cs_ref, ck_ref = np.zeros((m, cd), np.float32), cs.copy(), np.zeros((3, cd), np.float32)
+    orc.conv(st, lpp, proj, out_ref, cs_ref, lw, ck_ref)
+    out, csd, ckd = T.zeros((m, cd), device="cuda"), dev(T, cs), T.zeros((3, cd), device="cuda")
+    call(lib.snl_conv(C.byref(st), C.byref(lpp), ptr(dev(T, proj)), ptr(out), ptr(csd), ptr(dev(T, lw)), ptr(ckd), None))
+    assert rel(host(out), out_ref) < TOL
+    assert np.array_equal(host(csd), cs_ref)  # the carried state is copied, not computed
+    if ckpt:
+        assert np.array_equal(host(ckd), ck_ref)
+
+
+@pytest.mark.parametrize("m,ckpt", [(1, 0), (2, 1), (24, 0)])
+def test_delta(T, lib, orc, m, ckpt):
+    rng = np.random.default_rng(10 + m)
+    lpp, proj, lw, cd = lin_case(rng, m)
+    conv_out = rng.standard_normal((m, cd)).astype(np.float32)
+    S = (0.05 * rng.standard_normal((32, 128, 128))).astype(np.float32)
+    st = StepU(m, 0, 1, ckpt)
+    out_ref, S_ref, ck_ref = np.zeros((m, 4096), np.float32), S.copy(), np.zeros_like(S)
+    orc.delta(st, lpp, proj, conv_out, S_ref, lw, out_ref, ck_ref)
+    out, Sd, ckd = T.zeros((m, 4096), device="cuda"), dev(T, S), T.zeros(S.shape, device="cuda")
+    call(lib.snl_delta(C.byref(st), C.byref(lpp), ptr(dev(T, proj)), ptr(dev(T, conv_out)), ptr(Sd), ptr(dev(T, lw)),
+                       ptr(out), ptr(ckd), None))
+    assert rel(host(out), out_ref) < TOL
+    assert rel(host(Sd), S_ref) < TOL
+    if ckpt:
+        assert rel(host(ckd), ck_ref) < TOL
