@@ -55,6 +55,7 @@ def parse_args():
     ap.add_argument("--workload", choices=["decode", "gemv"], default="decode",
                     help="gemv: only BASELINE configs[0], the one-token Q8_0 GEMV 12288x4096")
     ap.add_argument("--iters", type=int, default=40)
+    ap.add_argument("--gemv-kernel", choices=["tile", "tc", "simt"], default="tile")
     return ap.parse_args()
 
 
@@ -191,7 +192,7 @@ def weight_bytes_per_token(cfg, quant: str) -> int:
     return int(tot)
 
 
-def gemv_config1(lib, quant: str, copies: int = 8, iters: int = 40) -> dict:
+def gemv_config1(lib, quant: str, copies: int = 8, iters: int = 40, kernel: str = "tile") -> dict:
     """one-token Q8_0 GEMV, W [12288 x 4096], x fp32 ~N(0,1),
     timed alone with CUDA events on the launching stream. `copies` weight copies
     (8 x 56.7 MB > L2) rotate so every launch reads its weights from HBM."""
@@ -212,10 +213,28 @@ def gemv_config1(lib, quant: str, copies: int = 8, iters: int = 40) -> dict:
     x = torch.randn(k, device="cuda")
     y = torch.empty(n, device="cuda")
     st, p = ffi.StepU(1, 0, 1, 0), ffi.MatP(n, k, 0, k, 0, n, 0, 0)
+    planes = torch.empty(2 * k, dtype=torch.float16, device="cuda")
+    ffi.check(lib.snl_xpack(C.c_void_p(x.data_ptr()), 1, k, k, C.c_void_p(planes.data_ptr()), None))
+    tiles, tsc = [], []
+    if kernel == "tile":
+        tb, sf = C.c_size_t(), C.c_size_t()
+        ffi.check(lib.snl_tile_sizes(dt, n, k, C.byref(tb), C.byref(sf)))
+        for i in range(copies):
+            tiles.append(torch.empty(tb.value, dtype=torch.uint8, device="cuda"))
+            tsc.append(torch.empty(sf.value, dtype=torch.float32, device="cuda"))
+            ffi.check(lib.snl_tile_repack(dt, n, k, C.c_void_p(ws[i].data_ptr()), C.c_void_p(ss[i].data_ptr()),
+                                          C.c_void_p(tiles[i].data_ptr()), C.c_void_p(tsc[i].data_ptr()), None))
 
     def run(i):
-        ffi.check(lib.snl_mat(dt, C.byref(st), C.byref(p), C.c_void_p(x.data_ptr()), C.c_void_p(ws[i].data_ptr()),
-                              C.c_void_p(ss[i].data_ptr()), C.c_void_p(y.data_ptr()), None))
+        if kernel == "tile":  # the decode path: tile layout, tensor-core GEMV over packed x
+            ffi.check(lib.snl_mat_tiles(dt, C.byref(p), 1, C.c_void_p(planes.data_ptr()), C.c_void_p(tiles[i].data_ptr()),
+                                        C.c_void_p(tsc[i].data_ptr()), C.c_void_p(y.data_ptr()), None))
+        elif kernel == "tc":  # tensor-core GEMV on the file layout
+            ffi.check(lib.snl_mat_xpack(dt, C.byref(p), 1, C.c_void_p(planes.data_ptr()), C.c_void_p(ws[i].data_ptr()),
+                                        C.c_void_p(ss[i].data_ptr()), C.c_void_p(y.data_ptr()), None))
+        else:  # snl_mat: the SIMT kernels of the kernel-level entry point
+            ffi.check(lib.snl_mat(dt, C.byref(st), C.byref(p), C.c_void_p(x.data_ptr()), C.c_void_p(ws[i].data_ptr()),
+                                  C.c_void_p(ss[i].data_ptr()), C.c_void_p(y.data_ptr()), None))
 
     for i in range(2 * copies):
         run(i % copies)
@@ -228,7 +247,8 @@ def gemv_config1(lib, quant: str, copies: int = 8, iters: int = 40) -> dict:
     torch.cuda.synchronize()
     us = a.elapsed_time(b) * 1000.0 / iters
     nbytes = qb + n * k // 32 * 4 + 4 * k + 4 * n
-    return {"shape": [n, k], "quant": quant, "scales": "f32", "us_per_launch": us, "bytes_per_launch": nbytes,
+    return {"shape": [n, k], "quant": quant, "scales": "f32", "kernel": kernel, "us_per_launch": us,
+            "bytes_per_launch": nbytes,
             "achieved_gbs": nbytes / (us * 1e3), "copies_rotated": copies}
 
 
@@ -412,7 +432,7 @@ def run_gemv_only(args):
 
     torch.cuda.set_device(0)
     lib = ffi.load()
-    g = gemv_config1(lib, args.quant, iters=args.iters)
+    g = gemv_config1(lib, args.quant, iters=args.iters, kernel=args.gemv_kernel)
     peak, kind = peaks()
     g["frac"] = g["achieved_gbs"] / peak
     g["peak"] = peak

@@ -134,6 +134,25 @@ int snl_config_validate(const snl_model_config* cfg);
 int snl_mat(int dtype, const snl_step_u* step, const snl_mat_p* p, const float* x, const void* wq,
             const float* ws, float* y, void* stream);
 
+/* The same product on the tensor cores for 1..4 token rows, with x given as "x planes":
+ * [2*rows_m][k] fp16, plane 2t = hi and 2t+1 = lo of x[t]/16 (written by snl_xpack or by
+ * the engine's producer kernels). y as snl_mat (y_off, y_stride, n_off); x_off and
+ * x_stride of p are unused. */
+int snl_xpack(const float* x, uint32_t m, uint32_t k, uint32_t x_stride, void* planes, void* stream);
+int snl_mat_xpack(int dtype, const snl_mat_p* p, uint32_t rows_m, const void* planes, const void* wq,
+                  const float* ws, float* y, void* stream);
+
+/* Tile layout of a Q8_0/Q4_0 matrix for the decode GEMV: 16-row groups, one 512-byte
+ * (Q8) or 256-byte (Q4) tile per 32-element block holding each MMA lane's fragment
+ * bytes contiguously, plus grouped f32 scales. The same values as the file layout in
+ * another order (weights.rs:48-55 is the source). snl_tile_sizes gives the buffer
+ * sizes; snl_tile_repack converts on the device; snl_mat_tiles is snl_mat_xpack on it. */
+int snl_tile_sizes(int dtype, uint32_t n, uint32_t k, size_t* tile_bytes, size_t* scale_floats);
+int snl_tile_repack(int dtype, uint32_t n, uint32_t k, const void* q, const float* s, void* tiles,
+                    float* tile_scales, void* stream);
+int snl_mat_tiles(int dtype, const snl_mat_p* p, uint32_t rows_m, const void* planes, const void* tiles,
+                  const float* tile_scales, float* y, void* stream);
+
 /* ---- kernel level: layers.wgsl ------------------------------------------------- */
 
 /* branch_norm (layers.wgsl:186-213): n_groups workgroups (step->m, or 1 for the
@@ -188,7 +207,6 @@ int snl_delta(const snl_step_u* step, const snl_lin_p* p, const float* proj, con
 /* Greedy argmax of each of `rows` rows of `n` logits (sampler.rs:169-177: the first
  * maximum wins); out_idx is a device u32[rows]. */
 int snl_argmax(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_idx, void* stream);
-
 /* ---- seeded synthetic tensors ------------------------------------------------------- */
 
 /* Fill device buffers with tensor `name` of the seeded synthetic model (the benchmark

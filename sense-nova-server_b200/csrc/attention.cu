@@ -103,7 +103,7 @@ constexpr int kKeysPerGroup = 8;
 __global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, const float* __restrict__ proj,
                                                      const float* __restrict__ qbuf, const uint32_t* __restrict__ kc,
                                                      const uint32_t* __restrict__ vc, float* __restrict__ out,
-                                                     float* __restrict__ partial) {
+                                                     float* __restrict__ partial, XOut xo) {
   __shared__ float s_acc[kAttWarps][G][HD];  // 32 KB
   __shared__ float s_ml[kAttWarps][G][2];
   __shared__ float s_p[kAttWarps][32];
@@ -217,7 +217,9 @@ __global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, c
     const uint32_t h = kh * G + g;
     if (st.parts == 1) {
       const float gate = proj[(uint64_t)m * p.proj_stride + h * 2 * HD + HD + d];
-      out[(uint64_t)m * q_dim + h * HD + d] = A / L / (1.0f + __expf(-gate));
+      const float o = A / L / (1.0f + __expf(-gate));
+      out[(uint64_t)m * q_dim + h * HD + d] = o;
+      if (xo.planes) xout_store(xo, m, h * HD + d, o);
     } else {
       const uint64_t pi = ((uint64_t)m * p.n_heads + h) * st.parts + part;
       partial[pi * (HD + 2) + d] = A;
@@ -234,7 +236,7 @@ __global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, c
 // graphs, whose launch list is fixed while parts changes between replays.
 __global__ void __launch_bounds__(256) combine_kernel(StepRef sr, snl_attn_p p, const float* __restrict__ proj,
                                                       const float* __restrict__ partial, float* __restrict__ out,
-                                                      int skip_single) {
+                                                      int skip_single, XOut xo) {
   const snl_step_u st = load_step(sr);
   const uint32_t h = blockIdx.x, m = blockIdx.y, d = threadIdx.x;
   if (m >= st.m || (skip_single && st.parts <= 1)) return;
@@ -250,7 +252,9 @@ __global__ void __launch_bounds__(256) combine_kernel(StepRef sr, snl_attn_p p, 
     acc = fmaf(partial[o + d], f, acc);
   }
   const float gate = proj[(uint64_t)m * p.proj_stride + h * 2 * HD + HD + d];
-  out[(uint64_t)m * q_dim + h * HD + d] = acc / l / (1.0f + __expf(-gate));
+  const float o = acc / l / (1.0f + __expf(-gate));
+  out[(uint64_t)m * q_dim + h * HD + d] = o;
+  if (xo.planes) xout_store(xo, m, h * HD + d, o);
 }
 
 }  // namespace
@@ -271,19 +275,20 @@ int launch_attn_prep(StepRef st, const snl_attn_p& p, const float* proj, float* 
 }
 
 int launch_attend(StepRef st, const snl_attn_p& p, const float* proj, const float* qbuf, const uint32_t* kc,
-                  const uint32_t* vc, float* out, float* partial, uint32_t m, uint32_t parts_grid, cudaStream_t s) {
+                  const uint32_t* vc, float* out, float* partial, uint32_t m, uint32_t parts_grid, cudaStream_t s,
+                  XOut xo) {
   if (int rc = check_attn(p)) return rc;
   if (m == 0 || parts_grid == 0) return SNL_OK;
-  attend_kernel<<<dim3(p.n_kv, m, parts_grid), kAttWarps * 32, 0, s>>>(st, p, proj, qbuf, kc, vc, out, partial);
+  attend_kernel<<<dim3(p.n_kv, m, parts_grid), kAttWarps * 32, 0, s>>>(st, p, proj, qbuf, kc, vc, out, partial, xo);
   SNL_LAUNCH_CHECK("attend");
   return SNL_OK;
 }
 
 int launch_attn_combine(StepRef st, const snl_attn_p& p, const float* proj, const float* partial, float* out,
-                        uint32_t m, cudaStream_t s, int skip_single) {
+                        uint32_t m, cudaStream_t s, int skip_single, XOut xo) {
   if (int rc = check_attn(p)) return rc;
   if (m == 0) return SNL_OK;
-  combine_kernel<<<dim3(p.n_heads, m), HD, 0, s>>>(st, p, proj, partial, out, skip_single);
+  combine_kernel<<<dim3(p.n_heads, m), HD, 0, s>>>(st, p, proj, partial, out, skip_single, xo);
   SNL_LAUNCH_CHECK("attn_combine");
   return SNL_OK;
 }

@@ -84,11 +84,33 @@ __device__ __forceinline__ uint4 ld_stream16(const void* p) {
   return r;
 }
 
+// Optional second output of a kernel that produces a GEMV input: the x planes of the
+// tensor-core GEMV (hi/lo fp16 halves of x / 16, plane 2t = hi, 2t+1 = lo of token t).
+struct XOut {
+  __half* planes = nullptr;
+  uint32_t stride = 0;
+};
+__device__ __forceinline__ void xout_store(const XOut& xo, uint32_t t, uint32_t i, float v) {
+  const float vs = v * (1.0f / 16.0f);
+  const __half hi = __float2half_rn(vs);
+  const __half lo = __float2half_rn(vs - __half2float(hi));
+  xo.planes[(uint64_t)(2 * t) * xo.stride + i] = hi;
+  xo.planes[(uint64_t)(2 * t + 1) * xo.stride + i] = lo;
+}
+
+// Device address of the library's device error word (bit 0: a bounded wait gave up).
+int device_error_word(int** out);
+
 // Launch helpers implemented per kernel family (internal, not part of the C ABI).
 int launch_mat(int dtype, StepRef st, const snl_mat_p& p, const float* x, const void* wq, const void* ws,
                int scale_f16, float* y, cudaStream_t s, uint32_t rows_m_host);
 int launch_branch_norm(StepRef st, const snl_layer_p& p, const float* x, const float* coef, const float* w,
-                       float* out, uint32_t n_groups, cudaStream_t s);
+                       float* out, uint32_t n_groups, cudaStream_t s, XOut xo = XOut());
+// branch_norm mode 1 that first finishes the mHC router from nparts partial sums per
+// token (written by the residual-merging GEMV) and writes coef.
+int launch_branch_norm_router(StepRef st, const snl_layer_p& p, const float* x, float* coef, const float* w,
+                              float* out, uint32_t n_groups, cudaStream_t s, XOut xo, const float* rpart,
+                              uint32_t nparts, const float* router);
 int launch_mhc_dots(StepRef st, const snl_layer_p& p, const float* x, const float* w, float* raw, uint32_t m,
                     cudaStream_t s);
 int launch_mhc_finish(StepRef st, const snl_layer_p& p, const float* raw, const float* w, float* coef, uint32_t m,
@@ -98,17 +120,23 @@ int launch_mhc_router(const snl_layer_p& p, const float* x, const float* w, floa
                       cudaStream_t s);
 int launch_merge(StepRef st, const snl_layer_p& p, float* x, const float* coef, const float* br, uint32_t m,
                  cudaStream_t s);
-int launch_swiglu(StepRef st, const snl_layer_p& p, const float* gu, float* act, uint32_t m, cudaStream_t s);
+int launch_swiglu(StepRef st, const snl_layer_p& p, const float* gu, float* act, uint32_t m, cudaStream_t s,
+                  XOut xo = XOut());
 int launch_attn_prep(StepRef st, const snl_attn_p& p, const float* proj, float* qbuf, uint32_t* kc, uint32_t* vc,
                      const float* norms, const uint32_t* rpos, uint32_t m, cudaStream_t s);
 int launch_attend(StepRef st, const snl_attn_p& p, const float* proj, const float* qbuf, const uint32_t* kc,
-                  const uint32_t* vc, float* out, float* partial, uint32_t m, uint32_t parts_grid, cudaStream_t s);
+                  const uint32_t* vc, float* out, float* partial, uint32_t m, uint32_t parts_grid, cudaStream_t s,
+                  XOut xo = XOut());
 int launch_attn_combine(StepRef st, const snl_attn_p& p, const float* proj, const float* partial, float* out,
-                        uint32_t m, cudaStream_t s, int skip_single);
+                        uint32_t m, cudaStream_t s, int skip_single, XOut xo = XOut());
 int launch_conv(StepRef st, const snl_lin_p& p, const float* proj, float* conv_out, float* conv_state,
                 const float* lw, float* conv_ckpt, cudaStream_t s);
 int launch_delta(StepRef st, const snl_lin_p& p, const float* proj, const float* conv_out, float* state,
-                 const float* lw, float* out, float* state_ckpt, cudaStream_t s);
+                 const float* lw, float* out, float* state_ckpt, cudaStream_t s, XOut xo = XOut());
+// conv + delta fused (engine path): no conv_out buffer.
+int launch_conv_delta(StepRef st, const snl_lin_p& p, const float* proj, float* conv_state, float* state,
+                      const float* lw, float* out, float* conv_ckpt, float* state_ckpt, cudaStream_t s,
+                      XOut xo = XOut());
 int launch_argmax(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_idx, cudaStream_t s);
 int launch_embed(const uint32_t* tokens, uint32_t m, const int8_t* q, const float* s_, uint32_t h, uint32_t vocab,
                  float* x, int* err_flag, cudaStream_t s);

@@ -18,6 +18,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "gemv_mma.cuh"
 #include "synth.h"
 #include "synth_model.h"
 
@@ -54,6 +55,9 @@ struct QT {
   void* q = nullptr;
   void* s = nullptr;
   int s_f16 = 0;
+  // the same matrix in the tile layout of the decode GEMV (gemv_mma.cu)
+  void* tiles = nullptr;
+  float* tscales = nullptr;
 };
 struct FT {
   float* p = nullptr;
@@ -114,6 +118,14 @@ struct snl_engine {
   };
   std::map<uint32_t, Graph> graphs;
   bool use_graphs = true;
+  // Steps of <= 4 rows run their projections on the tensor-core GEMV, whose x operand is
+  // these planes ([8][pstride] halves), written by the kernel that produces each input.
+  bool use_tc = true;
+  __half* xpl = nullptr;
+  uint32_t pstride = 0;
+  // Router partial sums written by the residual-merging GEMV for the next mHC norm.
+  float* rpart = nullptr;
+  bool rpart_ready = false;
 
   // Per-op timing of one eager step (snl_engine_profile).
   struct ProfRec {
@@ -245,8 +257,18 @@ int mat(snl_engine* e, StepRef st, const QT& w, const float* x, size_t x_stride,
     if (_rc) return _rc;       \
   } while (0)
 
-int push_norm(snl_engine* e, StepRef st, uint32_t m, const float* router, const float* norm_w) {
+int push_norm(snl_engine* e, StepRef st, uint32_t m, const float* router, const float* norm_w, XOut xo = XOut()) {
   const double h = e->cfg.hidden;
+  if (router && e->rpart_ready) {
+    // The router sums were produced by the GEMV that merged the residual.
+    e->rpart_ready = false;
+    snl_layer_p p = layer_p(e, 1, false);
+    const uint32_t nparts = (e->cfg.hidden + 15) / 16;
+    return timed(e, "BranchNorm+Router", 4.0 * (m * 3 * h + h + 9.0 * nparts * m), [&] {
+      return launch_branch_norm_router(st, p, e->x, e->coef, norm_w, e->xn, m, e->stream, xo, e->rpart, nparts, router);
+    });
+  }
+  e->rpart_ready = false;
   if (router) {
     snl_layer_p p0 = layer_p(e, 0, false);
     SNL_TRY(timed(e, "MhcRouter", 4.0 * (16 * h + 8 + m * 2 * h),
@@ -254,7 +276,38 @@ int push_norm(snl_engine* e, StepRef st, uint32_t m, const float* router, const 
   }
   snl_layer_p p = layer_p(e, router ? 1 : 0, false);
   return timed(e, "BranchNorm", 4.0 * (m * 3 * h + h),
-               [&] { return launch_branch_norm(st, p, e->x, e->coef, norm_w, e->xn, m, e->stream); });
+               [&] { return launch_branch_norm(st, p, e->x, e->coef, norm_w, e->xn, m, e->stream, xo); });
+}
+
+// One projection on the tensor-core GEMV (x = the planes). mode 0 writes y; mode 1
+// merges into the residual x like `merge` (engine.rs:471-480) and can expand stream 0
+// into stream 1 (the merge mode 3 that opens an mHC range).
+int matx(snl_engine* e, const QT& w, uint32_t rows, int mode, float* y, size_t y_stride, uint32_t merge_mode = 0,
+         int expand = 0, const float* rnext = nullptr) {
+  GemvArgs a{};
+  a.n = (uint32_t)w.rows;
+  a.k = (uint32_t)w.cols;
+  a.xplanes = e->xpl;
+  a.plane_stride = e->pstride;
+  a.wq = static_cast<const uint8_t*>(w.q);
+  a.mode = mode;
+  a.y = y;
+  a.y_stride = (uint32_t)y_stride;
+  a.resid = e->x;
+  a.coef = e->coef;
+  a.h = e->cfg.hidden;
+  a.merge_mode = (int)merge_mode;
+  a.expand = expand;
+  a.rnext = rnext;
+  a.rpart = e->rpart;
+  const double bytes = qbytes(w) + 4.0 * rows * (w.cols + w.rows);
+  const std::string label = "mat n=" + std::to_string(w.rows) + (y == e->logits ? " (head)" : "");
+  SNL_TRY(timed(e, label, bytes, [&] {
+    if (w.tiles) return launch_gemv_tile(w.dtype, a, rows, w.tiles, w.tscales, e->stream);
+    return launch_gemv_mma(w.dtype, a, rows, w.s, w.s_f16, e->stream);
+  }));
+  e->rpart_ready = rnext != nullptr;
+  return SNL_OK;
 }
 
 // The layer loop of engine.rs:389-481 for one step of m rows.
@@ -264,15 +317,37 @@ int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
   size_t lin_slot = 0, full_slot = 0;
   const snl_attn_p ap = attn_p(e);
   const snl_lin_p lp = lin_p(e);
-  for (size_t li : e->plan) {
+  const bool tc = e->use_tc && m <= 4;
+  const XOut xo = tc ? XOut{e->xpl, e->pstride} : XOut{};
+  const double hb = 4.0 * m * h;
+  // in-projection (x = normed residual) into y
+  auto proj_in = [&](const QT& w, float* y, size_t y_stride) -> int {
+    if (tc) return matx(e, w, m, 0, y, y_stride);
+    return mat(e, st, w, e->xn, h, y, y_stride, m);
+  };
+  // out-projection of `src` (K = src_dim) merged into the residual
+  auto proj_out = [&](const QT& w, const float* src, size_t src_dim, uint32_t merge_mode, bool expand,
+                      const float* rnext) -> int {
+    if (tc) return matx(e, w, m, 1, nullptr, 0, merge_mode, expand ? 1 : 0, rnext);
+    SNL_TRY(mat(e, st, w, src, src_dim, e->branch, h, m));
+    SNL_TRY(timed(e, "Merge", 5 * hb, [&] {
+      return launch_merge(st, layer_p(e, merge_mode, false), e->x, e->coef, e->branch, m, e->stream);
+    }));
+    if (expand)
+      SNL_TRY(timed(e, "Merge", 2 * hb, [&] { return launch_merge(st, layer_p(e, 3, false), e->x, e->coef, e->branch, m, e->stream); }));
+    return SNL_OK;
+  };
+  bool expanded = false;  // the previous visit's last merge already opened the mHC range
+  e->rpart_ready = false;
+  for (size_t vi = 0; vi < e->plan.size(); vi++) {
+    const size_t li = e->plan[vi];
     const std::string L = "l" + std::to_string(li) + ".";
     const bool mhc = snl_synth::is_mhc(c, li);
-    const double hb = 4.0 * m * h;
-    if (mhc && (int32_t)li == c.mhc_start)
+    if (mhc && (int32_t)li == c.mhc_start && !expanded)
       SNL_TRY(timed(e, "Merge", 2 * hb, [&] { return launch_merge(st, layer_p(e, 3, false), e->x, e->coef, e->branch, m, e->stream); }));
-    SNL_TRY(push_norm(e, st, m, mhc ? find_f(e, L + "mhc_attn") : nullptr, find_f(e, L + "in_ln")));
+    SNL_TRY(push_norm(e, st, m, mhc ? find_f(e, L + "mhc_attn") : nullptr, find_f(e, L + "in_ln"), xo));
     if (c.full_attention[li]) {
-      SNL_TRY(mat(e, st, *find_q(e, L + "qkv"), e->xn, h, e->proj, ap.proj_stride, m));
+      SNL_TRY(proj_in(*find_q(e, L + "qkv"), e->proj, ap.proj_stride));
       const double kvd = (double)snl_synth::kv_dim(c), qd = (double)snl_synth::q_dim(c);
       SNL_TRY(timed(e, "AttnPrep", 4.0 * m * (qd + 2 * kvd) + 4.0 * m * qd + 2.0 * m * 2 * kvd, [&] {
         return launch_attn_prep(st, ap, e->proj, e->qbuf, e->kc[full_slot], e->vc[full_slot], find_f(e, L + "qk_norm"),
@@ -281,37 +356,41 @@ int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
       const double keys = (double)st.val.pos0 + m;
       SNL_TRY(timed(e, "Attend", 2.0 * 2 * kvd * keys + 4.0 * m * 2 * qd, [&] {
         return launch_attend(st, ap, e->proj, e->qbuf, e->kc[full_slot], e->vc[full_slot], e->attn_out, e->partial, m,
-                             parts_grid, e->stream);
+                             parts_grid, e->stream, xo);
       }));
       if (parts_grid > 1)
         SNL_TRY(timed(e, "Combine", 4.0 * m * qd * 2, [&] {
-          return launch_attn_combine(st, ap, e->proj, e->partial, e->attn_out, m, e->stream, 1);
+          return launch_attn_combine(st, ap, e->proj, e->partial, e->attn_out, m, e->stream, 1, xo);
         }));
-      SNL_TRY(mat(e, st, *find_q(e, L + "o_proj"), e->attn_out, snl_synth::q_dim(c), e->branch, h, m));
+      SNL_TRY(proj_out(*find_q(e, L + "o_proj"), e->attn_out, snl_synth::q_dim(c), mhc ? 1 : 0, false,
+                       mhc ? find_f(e, L + "mhc_ffn") : nullptr));
       full_slot++;
     } else {
-      SNL_TRY(mat(e, st, *find_q(e, L + "in_proj"), e->xn, h, e->proj, lp.proj_stride, m));
+      SNL_TRY(proj_in(*find_q(e, L + "in_proj"), e->proj, lp.proj_stride));
       float* cs = e->conv_state + lin_slot * e->conv_elems;
       float* ss = e->lin_state + lin_slot * e->state_elems;
       float* cc = e->conv_ckpt + lin_slot * e->conv_elems;
       float* sc = e->lin_ckpt + lin_slot * e->state_elems;
       const float* lw = find_f(e, L + "lin");
       const double cdim = (double)lp.conv_dim;
-      SNL_TRY(timed(e, "Conv", 4.0 * (2 * m * cdim + 6 * cdim + 4 * cdim),
-                    [&] { return launch_conv(st, lp, e->proj, e->act, cs, lw, cc, e->stream); }));
-      SNL_TRY(timed(e, "Delta", 4.0 * (2.0 * e->state_elems + m * (cdim + 2 * 4096.0)),
-                    [&] { return launch_delta(st, lp, e->proj, e->act, ss, lw, e->attn_out, sc, e->stream); }));
-      SNL_TRY(mat(e, st, *find_q(e, L + "out_proj"), e->attn_out, snl_synth::lin_value_dim(c), e->branch, h, m));
+      SNL_TRY(timed(e, "ConvDelta", 4.0 * (2.0 * e->state_elems + 10.0 * cdim + m * (cdim + 2 * 4096.0)), [&] {
+        return launch_conv_delta(st, lp, e->proj, cs, ss, lw, e->attn_out, cc, sc, e->stream, xo);
+      }));
+      SNL_TRY(proj_out(*find_q(e, L + "out_proj"), e->attn_out, snl_synth::lin_value_dim(c), mhc ? 1 : 0, false,
+                       mhc ? find_f(e, L + "mhc_ffn") : nullptr));
       lin_slot++;
     }
-    SNL_TRY(timed(e, "Merge", 5 * hb, [&] { return launch_merge(st, layer_p(e, mhc ? 1 : 0, false), e->x, e->coef, e->branch, m, e->stream); }));
-    SNL_TRY(push_norm(e, st, m, mhc ? find_f(e, L + "mhc_ffn") : nullptr, find_f(e, L + "post_ln")));
-    SNL_TRY(mat(e, st, *find_q(e, L + "gate_up"), e->xn, h, e->proj, 2 * (size_t)c.intermediate, m));
+    SNL_TRY(push_norm(e, st, m, mhc ? find_f(e, L + "mhc_ffn") : nullptr, find_f(e, L + "post_ln"), xo));
+    SNL_TRY(proj_in(*find_q(e, L + "gate_up"), e->proj, 2 * (size_t)c.intermediate));
     SNL_TRY(timed(e, "Swiglu", 12.0 * m * c.intermediate,
-                  [&] { return launch_swiglu(st, layer_p(e, 0, false), e->proj, e->act, m, e->stream); }));
-    SNL_TRY(mat(e, st, *find_q(e, L + "down"), e->act, c.intermediate, e->branch, h, m));
+                  [&] { return launch_swiglu(st, layer_p(e, 0, false), e->proj, e->act, m, e->stream, xo); }));
     const uint32_t mode = !mhc ? 0 : ((int32_t)(li + 1) == c.mhc_end ? 2 : 1);
-    SNL_TRY(timed(e, "Merge", 5 * hb, [&] { return launch_merge(st, layer_p(e, mode, false), e->x, e->coef, e->branch, m, e->stream); }));
+    const bool expand_next = vi + 1 < e->plan.size() && snl_synth::is_mhc(c, e->plan[vi + 1]) &&
+                             (int32_t)e->plan[vi + 1] == c.mhc_start;
+    const bool next_mhc = vi + 1 < e->plan.size() && snl_synth::is_mhc(c, e->plan[vi + 1]);
+    const float* rnext = next_mhc ? find_f(e, "l" + std::to_string(e->plan[vi + 1]) + ".mhc_attn") : nullptr;
+    SNL_TRY(proj_out(*find_q(e, L + "down"), e->act, c.intermediate, mode, expand_next, rnext));
+    expanded = expand_next;
   }
   return SNL_OK;
 }
@@ -328,12 +407,22 @@ int device_step(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid, uint
   // Row 0 of hid is the hidden state of the token before this step (engine.rs:889-890).
   SNL_CUDA_TRY(cudaMemcpyAsync(e->hid, e->hlast, h * sizeof(float), cudaMemcpyDeviceToDevice, e->stream));
   SNL_TRY(run_layers(e, st, m, parts_grid));
+  const bool tc = e->use_tc && m <= 4 && rows > 0;
+  const XOut xo = (tc && rows == m) ? XOut{e->xpl, e->pstride} : XOut{};
   SNL_TRY(timed(e, "BranchNorm", 12.0 * m * h, [&] {
-    return launch_branch_norm(st, layer_p(e, 0, false), e->x, e->coef, find_f(e, "norm"), e->hid + h, m, e->stream);
+    return launch_branch_norm(st, layer_p(e, 0, false), e->x, e->coef, find_f(e, "norm"), e->hid + h, m, e->stream, xo);
   }));
   if (rows > 0) {
-    SNL_TRY(mat(e, st, *find_q(e, "lm_head"), e->hid, h, e->logits, e->cfg.vocab, rows, rows,
-                (uint32_t)((m - rows + 1) * h)));
+    if (tc) {
+      // The head reads the last `rows` hidden rows (engine.rs:835-842).
+      if (rows != m)
+        SNL_TRY(launch_xpack(e->hid + (size_t)(m - rows + 1) * h, rows, (uint32_t)h, (uint32_t)h, e->xpl, e->pstride,
+                             e->stream));
+      SNL_TRY(matx(e, *find_q(e, "lm_head"), rows, 0, e->logits, e->cfg.vocab));
+    } else {
+      SNL_TRY(mat(e, st, *find_q(e, "lm_head"), e->hid, h, e->logits, e->cfg.vocab, rows, rows,
+                  (uint32_t)((m - rows + 1) * h)));
+    }
     if (greedy)
       SNL_TRY(timed(e, "Argmax", 4.0 * rows * e->cfg.vocab, [&] {
         return launch_argmax_with(e->logits, rows, e->cfg.vocab, e->amax, e->amax_part, e->stream);
@@ -638,6 +727,23 @@ extern "C" int snl_engine_finalize(snl_engine* e) {
         }
       });
   if (!missing.empty()) return fail(SNL_E_INVALID, "weight file is missing tensor `" + missing + "`");
+  // Tile-layout copies for the decode GEMV (embed is only gathered, not multiplied).
+  if (!getenv("SNL_NO_TILES")) {
+    for (auto& kv : e->qw) {
+      if (kv.first == "embed") continue;
+      snl::QT& t = kv.second;
+      size_t tb = 0, sf = 0;
+      tile_sizes(t.dtype, (uint32_t)t.rows, (uint32_t)t.cols, &tb, &sf);
+      uint8_t* tiles = nullptr;
+      float* ts = nullptr;
+      SNL_TRY(dalloc(e, &tiles, tb));
+      SNL_TRY(dalloc(e, &ts, sf));
+      SNL_TRY(launch_repack_tiles(t.dtype, (uint32_t)t.rows, (uint32_t)t.cols, t.q, (const float*)t.s, tiles, ts,
+                                  e->stream));
+      t.tiles = tiles;
+      t.tscales = ts;
+    }
+  }
   const size_t proj_w = std::max({2 * I, snl_synth::lin_proj_rows(c), snl_synth::attn_proj_rows(c)});
   const size_t act_w = std::max(I, snl_synth::conv_dim(c));
   const size_t attn_w = std::max(snl_synth::q_dim(c), snl_synth::lin_value_dim(c));
@@ -659,6 +765,10 @@ extern "C" int snl_engine_finalize(snl_engine* e) {
   SNL_TRY(dalloc(e, &e->mhc_raw, MAX_M * 16 * 9));
   SNL_TRY(dalloc(e, &e->amax, LOGIT_ROWS));
   SNL_TRY(dalloc(e, &e->amax_part, LOGIT_ROWS * 128));
+  e->pstride = (uint32_t)((std::max({h, I, snl_synth::q_dim(c), snl_synth::lin_value_dim(c)}) + 7) / 8 * 8);
+  SNL_TRY(dalloc(e, &e->xpl, (size_t)8 * e->pstride));
+  SNL_TRY(dalloc(e, &e->rpart, (size_t)4 * ((h + 15) / 16) * 9));
+  if (getenv("SNL_NO_TC")) e->use_tc = false;
   SNL_TRY(dalloc(e, &e->step_d, 1));
   SNL_TRY(dalloc(e, &e->mstep_d, 1));
   for (size_t l : e->plan) (c.full_attention[l] ? e->n_full : e->n_lin)++;

@@ -1,0 +1,707 @@
+// Block-quantized GEMV on the tensor cores (decode and 2-row verify).
+//
+// y[t, n] = sum_k x[t, k] * q[n, k] * s[n, k/32] for t < M <= 4 token rows.
+//
+// The dot products run as mma.sync m16n8k16 (f16 inputs, f32 accumulation):
+//   * A = 16 weight rows x 16 k. Q8_0 codes and Q4_0 nibbles are exact in fp16: a byte
+//     permute builds 1024 + (code + 128) (or 1024 + nibble) in the mantissa of fp16 and
+//     one packed subtract removes the offset.
+//   * B = 16 k x 8 columns: column 2t holds x_hi of token t and column 2t+1 its x_lo,
+//     where x = 16 * (x_hi + x_lo) with x_hi = fp16(x / 16), x_lo = fp16(x / 16 - x_hi).
+//     The pair carries ~22 significant bits, so the products match an fp32 dot product
+//     well inside the 1e-3 bar; the 1/16 pre-scale keeps |x| up to 10^6 in fp16 range.
+//   * Each 32-element block is two MMAs; its f32 result is scaled by the block's scale
+//     and added to an f32 accumulator in registers, so the per-block scale of the
+//     reference layout (weights.rs:48-55) is applied exactly as in matmul.wgsl.
+// k placement inside a block: thread (group g, lane-in-group t) loads bytes [8t, 8t+8)
+// of its two rows (Q8: one 8-byte load per row; Q4: the 4-byte word t). Any bijection
+// of k onto the MMA's k slots gives the same sum as long as A and B use the same one;
+// here MMA 0 takes k in {8t..8t+3} and MMA 1 k in {8t+4..8t+7} (Q4 pairs (8t+i, 8t+i+4)).
+//
+// The x operand arrives packed ("x planes", [2M][K] halves, natural k order), written
+// by the kernel that produced x, so a GEMV CTA starts streaming weights immediately.
+#include <algorithm>
+#include <cstdlib>
+
+#include "common.cuh"
+#include "gemv_mma.cuh"
+#include "ptx.cuh"
+
+namespace snl {
+namespace {
+
+constexpr int kWarpsK = 4;  // warps of a CTA split K into 4 contiguous ranges
+constexpr int kUnroll = 8;  // blocks (32 k) per iteration: 16 8-byte weight loads in flight per thread
+
+__device__ __forceinline__ void mma16816(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
+  __half2 r = __hsub2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// 4 int8 codes of w -> two half2 (codes 0,1) and (2,3), exact.
+__device__ __forceinline__ void q8_half2(uint32_t w, uint32_t& h01, uint32_t& h23) {
+  const uint32_t u = w ^ 0x80808080u;                   // code + 128 as unsigned bytes
+  const uint32_t off = 0x64806480u;                     // half2(1152, 1152)
+  h01 = hsub2_u32(__byte_perm(u, 0x64646464u, 0x4140), off);  // [b0, 0x64, b1, 0x64]
+  h23 = hsub2_u32(__byte_perm(u, 0x64646464u, 0x4342), off);
+}
+// 8 nibbles of w (element i = nibble i, value nibble - 8) -> half2 pairs (i, i+4), i < 4.
+__device__ __forceinline__ void q4_half2(uint32_t w, uint32_t h[4]) {
+  const uint32_t off = 0x64086408u;  // half2(1032, 1032)
+#pragma unroll
+  for (int i = 0; i < 4; i++) h[i] = hsub2_u32(((w >> (4 * i)) & 0x000F000Fu) | 0x64006400u, off);
+}
+
+template <typename ST>
+__device__ __forceinline__ float scale_at(const ST* s, uint64_t i) {
+  if constexpr (sizeof(ST) == 4) return __ldg(reinterpret_cast<const float*>(s) + i);
+  else return __half2float(__ldg(reinterpret_cast<const __half*>(s) + i));
+}
+
+// Streaming 8-byte weight load (read once per token: no L1 allocation).
+__device__ __forceinline__ uint2 ld_w8(const uint8_t* p) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint32_t ld_w4(const uint8_t* p) {
+  uint32_t r;
+  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
+  return r;
+}
+
+template <int DT, int M, typename ST>
+__global__ void __launch_bounds__(kWarpsK * 32) gemv_mma_kernel(GemvArgs a, const ST* __restrict__ ws) {
+  static_assert(M >= 1 && M <= 4, "2M B columns must fit the MMA's 8");
+  __shared__ float red[kWarpsK][M][16];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const uint32_t K = a.k, nb = K / 32;
+  const uint32_t row0 = blockIdx.x * 16;
+  const uint32_t rA = min(row0 + g, a.n - 1), rB = min(row0 + g + 8, a.n - 1);
+  constexpr uint32_t BPB = DT == SNL_Q8_0 ? 32 : 16;  // weight bytes per block per row
+  const uint8_t* wA = a.wq + (uint64_t)rA * nb * BPB;
+  const uint8_t* wB = a.wq + (uint64_t)rB * nb * BPB;
+  const ST* sA = ws + (uint64_t)rA * nb;
+  const ST* sB = ws + (uint64_t)rB * nb;
+  // This warp's K range, in blocks.
+  const uint32_t per = (nb + kWarpsK - 1) / kWarpsK;
+  const uint32_t b_begin = min(nb, warp * per), b_end = min(nb, b_begin + per);
+  // x planes: thread loads plane g (< 2M) at k = 32 b + 8 t.
+  const bool has_x = g < 2 * M;
+  const __half* xp = a.xplanes + (uint64_t)(has_x ? g : 0) * a.plane_stride + 8 * t;
+
+  float accA = 0.f, accB = 0.f;  // rows g and g+8 for token t (t < M)
+  for (uint32_t b0 = b_begin; b0 < b_end; b0 += kUnroll) {
+    uint32_t wa[kUnroll][2], wb[kUnroll][2];
+    float sa[kUnroll], sb[kUnroll];
+    uint4 xv[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; u++) {
+      const uint32_t b = min(b0 + u, b_end - 1);  // tail: reload the last block, masked below
+      if constexpr (DT == SNL_Q8_0) {
+        const uint2 va = ld_w8(wA + (uint64_t)b * 32 + 8 * t), vb = ld_w8(wB + (uint64_t)b * 32 + 8 * t);
+        wa[u][0] = va.x; wa[u][1] = va.y; wb[u][0] = vb.x; wb[u][1] = vb.y;
+      } else {
+        wa[u][0] = ld_w4(wA + (uint64_t)b * 16 + 4 * t);
+        wb[u][0] = ld_w4(wB + (uint64_t)b * 16 + 4 * t);
+      }
+      sa[u] = scale_at(sA, b);
+      sb[u] = scale_at(sB, b);
+      xv[u] = has_x ? __ldg(reinterpret_cast<const uint4*>(xp + (uint64_t)b * 32)) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; u++) {
+      if (b0 + u >= b_end) break;
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      if constexpr (DT == SNL_Q8_0) {
+        uint32_t A0[4], A1[4];
+        q8_half2(wa[u][0], A0[0], A0[2]);
+        q8_half2(wb[u][0], A0[1], A0[3]);
+        q8_half2(wa[u][1], A1[0], A1[2]);
+        q8_half2(wb[u][1], A1[1], A1[3]);
+        mma16816(d, A0, xv[u].x, xv[u].y);
+        mma16816(d, A1, xv[u].z, xv[u].w);
+      } else {
+        uint32_t ha[4], hb[4];
+        q4_half2(wa[u][0], ha);
+        q4_half2(wb[u][0], hb);
+        // B pairs (8t+i, 8t+i+4) from the natural-order halves x[8t..8t+8).
+        const uint32_t x01 = xv[u].x, x23 = xv[u].y, x45 = xv[u].z, x67 = xv[u].w;
+        const uint32_t p04 = __byte_perm(x01, x45, 0x5410), p15 = __byte_perm(x01, x45, 0x7632);
+        const uint32_t p26 = __byte_perm(x23, x67, 0x5410), p37 = __byte_perm(x23, x67, 0x7632);
+        const uint32_t A0[4] = {ha[0], hb[0], ha[1], hb[1]};
+        const uint32_t A1[4] = {ha[2], hb[2], ha[3], hb[3]};
+        mma16816(d, A0, p04, p15);
+        mma16816(d, A1, p26, p37);
+      }
+      // d0/d1: row g, columns 2t (hi) and 2t+1 (lo); d2/d3: row g+8.
+      accA = fmaf(sa[u], d[0] + d[1], accA);
+      accB = fmaf(sb[u], d[2] + d[3], accB);
+    }
+  }
+  if (t < M) {
+    red[warp][t][g] = accA;
+    red[warp][t][g + 8] = accB;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // lanes 0..15: token 0 rows, 16..31: token 1 rows; tokens 2, 3 in a second pass.
+#pragma unroll
+    for (int pass = 0; pass < (M + 1) / 2; pass++) {
+      const int tt = pass * 2 + lane / 16, r = lane % 16;
+      const uint32_t row = row0 + r;
+      const bool live = tt < M && row < a.n;
+      float2 nx = make_float2(0.f, 0.f);
+      if (live) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarpsK; w++) v += red[w][tt][r];
+        nx = gemv_epilogue(a, tt, row, v * kXPlaneScale);
+      }
+      if (a.rnext) {  // warp-uniform
+        float rs[9];
+        const uint32_t d = 2 * a.h;
+#pragma unroll
+        for (int o = 0; o < 8; o++)
+          rs[o] = live ? fmaf(__ldg(a.rnext + (uint64_t)o * d + row), nx.x, __ldg(a.rnext + (uint64_t)o * d + a.h + row) * nx.y)
+                       : 0.f;
+        rs[8] = live ? fmaf(nx.x, nx.x, nx.y * nx.y) : 0.f;
+#pragma unroll
+        for (int o = 0; o < 9; o++) {
+#pragma unroll
+          for (int off = 8; off > 0; off >>= 1) rs[o] += __shfl_xor_sync(0xffffffffu, rs[o], off);
+        }
+        if (r == 0 && tt < M) {
+#pragma unroll
+          for (int o = 0; o < 9; o++) a.rpart[((uint64_t)tt * gridDim.x + blockIdx.x) * 9 + o] = rs[o];
+        }
+      }
+    }
+  }
+}
+
+template <int DT, int M, typename ST>
+int launch_t(const GemvArgs& a, const void* ws, cudaStream_t s) {
+  const unsigned grid = (a.n + 15) / 16;
+  gemv_mma_kernel<DT, M, ST><<<grid, kWarpsK * 32, 0, s>>>(a, static_cast<const ST*>(ws));
+  SNL_LAUNCH_CHECK("gemv_mma");
+  return SNL_OK;
+}
+
+template <int DT, typename ST>
+int launch_m(const GemvArgs& a, uint32_t m, const void* ws, cudaStream_t s) {
+  switch (m) {
+    case 1: return launch_t<DT, 1, ST>(a, ws, s);
+    case 2: return launch_t<DT, 2, ST>(a, ws, s);
+    case 3: return launch_t<DT, 3, ST>(a, ws, s);
+    case 4: return launch_t<DT, 4, ST>(a, ws, s);
+  }
+  return fail(SNL_E_INVALID, "gemv_mma: 1..4 token rows");
+}
+
+// x [m, x_stride] f32 -> planes [2m][plane_stride] halves (hi, lo per token).
+__global__ void xpack_kernel(const float* __restrict__ x, uint32_t k, uint32_t x_stride, uint32_t m,
+                             __half* __restrict__ planes, uint32_t plane_stride) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t t = blockIdx.y;
+  if (i >= k || t >= m) return;
+  xplane_store(planes, plane_stride, t, i, x[(uint64_t)t * x_stride + i]);
+}
+
+}  // namespace
+
+int launch_gemv_mma(int dtype, const GemvArgs& a, uint32_t m, const void* ws, int scale_f16, cudaStream_t s) {
+  if (dtype != SNL_Q8_0 && dtype != SNL_Q4_0) return fail(SNL_E_INVALID, "gemv_mma: dtype");
+  if (a.k == 0 || a.k % 32) return fail(SNL_E_INVALID, "gemv_mma: k must be a multiple of 32");
+  if (a.plane_stride % 8 || ((uintptr_t)a.xplanes % 16)) return fail(SNL_E_INVALID, "gemv_mma: planes must be 16-byte aligned");
+  if (a.n == 0) return SNL_OK;
+  if (dtype == SNL_Q8_0)
+    return scale_f16 ? launch_m<SNL_Q8_0, __half>(a, m, ws, s) : launch_m<SNL_Q8_0, float>(a, m, ws, s);
+  return scale_f16 ? launch_m<SNL_Q4_0, __half>(a, m, ws, s) : launch_m<SNL_Q4_0, float>(a, m, ws, s);
+}
+
+int launch_xpack(const float* x, uint32_t m, uint32_t k, uint32_t x_stride, __half* planes, uint32_t plane_stride,
+                 cudaStream_t s) {
+  if (m == 0 || k == 0) return SNL_OK;
+  xpack_kernel<<<dim3((k + 255) / 256, m), 256, 0, s>>>(x, k, x_stride, m, planes, plane_stride);
+  SNL_LAUNCH_CHECK("xpack");
+  return SNL_OK;
+}
+
+}  // namespace snl
+
+extern "C" int snl_xpack(const float* x, uint32_t m, uint32_t k, uint32_t x_stride, void* planes, void* stream) {
+  if (!x || !planes || m == 0 || m > 4) return snl::fail(SNL_E_INVALID, "snl_xpack: bad argument");
+  if (k % 32 || x_stride < k) return snl::fail(SNL_E_INVALID, "snl_xpack: k must be a multiple of 32");
+  return snl::launch_xpack(x, m, k, x_stride, static_cast<__half*>(planes), k, (cudaStream_t)stream);
+}
+
+extern "C" int snl_mat_xpack(int dtype, const snl_mat_p* p, uint32_t rows_m, const void* planes, const void* wq,
+                             const float* ws, float* y, void* stream) {
+  if (!p || !planes || !wq || !ws || !y) return snl::fail(SNL_E_INVALID, "snl_mat_xpack: null argument");
+  if (rows_m == 0 || rows_m > 4) return snl::fail(SNL_E_INVALID, "snl_mat_xpack: 1..4 token rows");
+  snl::GemvArgs a = snl::gemv_args_plain(*p, static_cast<const __half*>(planes), p->k, wq, y);
+  return snl::launch_gemv_mma(dtype, a, rows_m, ws, 0, (cudaStream_t)stream);
+}
+
+// =====================================================================================
+// Tile layout and the tile GEMV (the engine's decode path).
+//
+// The decode GEMV is issue-bound on the reference layout: every 16-row x 32-k tile
+// costs ~60 warp instructions (two 8-byte loads per thread at row stride, an xor,
+// address arithmetic). The engine therefore keeps a second copy of each matrix in a
+// "tile layout" made for the MMA fragments:
+//   * rows are grouped by 16 (padded with zero rows); within a group, block b (32 k)
+//     is one 512-byte Q8_0 tile (256 bytes for Q4_0) and the tiles of a group follow
+//     each other along k;
+//   * in a Q8_0 tile, lane L = 4g + t owns bytes [16L, 16L + 16): bytes [8t, 8t + 8) of
+//     the block of row g, then the same bytes of row g + 8, each code stored as
+//     code + 128 (offset binary), so a warp reads 512 contiguous bytes with one 16-byte
+//     load per thread and the fp16 conversion needs no xor;
+//   * in a Q4_0 tile, lane L owns 8 bytes: word t of row g, then word t of row g + 8,
+//     with nibble i of word t holding element 8t + 2(i % 4) + (i / 4) (nibbles i and
+//     i + 4 form the pair (8t + 2j, 8t + 2j + 1) that matches the natural-order x halves);
+//   * scales: per row group, blocks in fours: [group][b / 4][16 rows][4 blocks] f32.
+// The values are the file's, bit for bit; only their order changes.
+// =====================================================================================
+
+namespace snl {
+namespace {
+
+constexpr int kTileWarps = 4;
+constexpr int kTileUnroll = 8;
+
+__global__ void repack_tiles_kernel(int dtype, uint32_t n, uint32_t k, const uint8_t* __restrict__ q,
+                                    const float* __restrict__ s, uint8_t* __restrict__ tiles, float* __restrict__ ts) {
+  // one thread per (group, block, lane)
+  const uint32_t nb = k / 32, groups = (n + 15) / 16;
+  const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (uint64_t)groups * nb * 32) return;
+  const uint32_t lane = (uint32_t)(idx % 32), b = (uint32_t)((idx / 32) % nb), grp = (uint32_t)(idx / 32 / nb);
+  const uint32_t g = lane >> 2, t = lane & 3;
+  const uint32_t rA = grp * 16 + g, rB = rA + 8;
+  const uint64_t tile = (uint64_t)grp * nb + b;
+  if (dtype == SNL_Q8_0) {
+    uint8_t* dst = tiles + tile * 512 + lane * 16;
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      dst[e] = rA < n ? (uint8_t)(q[(uint64_t)rA * k + b * 32 + 8 * t + e] ^ 0x80u) : (uint8_t)0x80u;
+      dst[8 + e] = rB < n ? (uint8_t)(q[(uint64_t)rB * k + b * 32 + 8 * t + e] ^ 0x80u) : (uint8_t)0x80u;
+    }
+  } else {
+    uint32_t* dst = reinterpret_cast<uint32_t*>(tiles + tile * 256 + lane * 8);
+    for (int r = 0; r < 2; r++) {
+      const uint32_t row = r ? rB : rA;
+      uint32_t word = 0x88888888u;  // padding rows: nibble 8 = value 0
+      if (row < n) {
+        const uint32_t src = reinterpret_cast<const uint32_t*>(q + (uint64_t)row * (k / 2))[b * 4 + t];
+        word = 0;
+        for (int i = 0; i < 8; i++) {
+          const uint32_t e = 2 * (i % 4) + (i / 4);  // element 8t + e goes to nibble i
+          word |= ((src >> (4 * e)) & 0xFu) << (4 * i);
+        }
+      }
+      dst[r] = word;
+    }
+  }
+  // scales: lanes 0..15 of each (group, block) write row `lane`'s scale.
+  if (lane < 16) {
+    const uint32_t row = grp * 16 + lane;
+    const uint32_t nb4 = (nb + 3) / 4;
+    ts[(((uint64_t)grp * nb4 + b / 4) * 16 + lane) * 4 + b % 4] = row < n ? s[(uint64_t)row * nb + b] : 0.f;
+  }
+}
+
+__device__ __forceinline__ uint4 ld_tile16(const uint8_t* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// Q8 codes stored as code + 128: half2(code_a, code_b) with one permute and one subtract.
+__device__ __forceinline__ uint32_t u8pair(uint32_t w, uint32_t sel) {
+  return hsub2_u32(__byte_perm(w, 0x64646464u, sel), 0x64806480u);
+}
+// Q4 (tile nibble order): half2 of nibbles (j, j + 4) of w, j = 0..3.
+__device__ __forceinline__ uint32_t u4pair(uint32_t w, int j) {
+  return hsub2_u32(((w >> (4 * j)) & 0x000F000Fu) | 0x64006400u, 0x64086408u);
+}
+
+template <int DT, int M>
+__global__ void __launch_bounds__(kTileWarps * 32) gemv_tile_kernel(GemvArgs a, const uint8_t* __restrict__ tiles,
+                                                                    const float* __restrict__ ts) {
+  __shared__ float red[kTileWarps][M][16];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const uint32_t nb = a.k / 32, nb4 = (nb + 3) / 4;
+  const uint32_t grp = blockIdx.x;
+  constexpr uint32_t TB = DT == SNL_Q8_0 ? 512 : 256;  // tile bytes
+  // This warp's blocks: a multiple-of-4 aligned range so scale loads stay whole.
+  const uint32_t per = ((nb4 + kTileWarps - 1) / kTileWarps) * 4;
+  const uint32_t b_begin = min(nb, warp * per), b_end = min(nb, b_begin + per);
+  const uint8_t* tp = tiles + ((uint64_t)grp * nb + b_begin) * TB + lane * (TB / 32);
+  const float* sp = ts + ((uint64_t)grp * nb4 + b_begin / 4) * 64;
+  const bool has_x = g < 2 * M;
+  const __half* xp = a.xplanes + (uint64_t)(has_x ? g : 0) * a.plane_stride + 8 * t + (uint64_t)b_begin * 32;
+
+  float accA = 0.f, accB = 0.f;
+  for (uint32_t b0 = b_begin; b0 < b_end; b0 += kTileUnroll) {
+    const uint32_t nu = min((uint32_t)kTileUnroll, b_end - b0);
+    uint4 w[kTileUnroll];
+    uint4 xv[kTileUnroll];
+    float4 sa[kTileUnroll / 4], sb[kTileUnroll / 4];
+#pragma unroll
+    for (int u = 0; u < kTileUnroll; u++) {
+      const uint32_t uu = min((uint32_t)u, nu - 1);
+      if constexpr (DT == SNL_Q8_0) {
+        w[u] = ld_tile16(tp + (uint64_t)uu * TB);
+      } else {
+        const uint2 v = *reinterpret_cast<const uint2*>(tp + (uint64_t)uu * TB);
+        w[u] = make_uint4(v.x, v.y, 0, 0);
+      }
+      xv[u] = has_x ? __ldg(reinterpret_cast<const uint4*>(xp + (uint64_t)uu * 32)) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int q = 0; q < kTileUnroll / 4; q++) {
+      const uint32_t qq = min((uint32_t)q, (nu - 1) / 4);
+      sa[q] = __ldg(reinterpret_cast<const float4*>(sp + (uint64_t)qq * 64 + g * 4));
+      sb[q] = __ldg(reinterpret_cast<const float4*>(sp + (uint64_t)qq * 64 + (g + 8) * 4));
+    }
+#pragma unroll
+    for (int u = 0; u < kTileUnroll; u++) {
+      if ((uint32_t)u >= nu) break;
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      if constexpr (DT == SNL_Q8_0) {
+        // w.x/w.y: row g bytes 8t..8t+7; w.z/w.w: row g+8.
+        const uint32_t A0[4] = {u8pair(w[u].x, 0x4140), u8pair(w[u].z, 0x4140), u8pair(w[u].x, 0x4342),
+                                u8pair(w[u].z, 0x4342)};
+        const uint32_t A1[4] = {u8pair(w[u].y, 0x4140), u8pair(w[u].w, 0x4140), u8pair(w[u].y, 0x4342),
+                                u8pair(w[u].w, 0x4342)};
+        mma16816(d, A0, xv[u].x, xv[u].y);
+        mma16816(d, A1, xv[u].z, xv[u].w);
+      } else {
+        // w.x: row g word t, w.y: row g+8 word t; pair j = elements (8t+2j, 8t+2j+1).
+        const uint32_t A0[4] = {u4pair(w[u].x, 0), u4pair(w[u].y, 0), u4pair(w[u].x, 1), u4pair(w[u].y, 1)};
+        const uint32_t A1[4] = {u4pair(w[u].x, 2), u4pair(w[u].y, 2), u4pair(w[u].x, 3), u4pair(w[u].y, 3)};
+        mma16816(d, A0, xv[u].x, xv[u].y);
+        mma16816(d, A1, xv[u].z, xv[u].w);
+      }
+      const float4 s4a = sa[u / 4], s4b = sb[u / 4];
+      const int r = u % 4;
+      const float scA = r == 0 ? s4a.x : r == 1 ? s4a.y : r == 2 ? s4a.z : s4a.w;
+      const float scB = r == 0 ? s4b.x : r == 1 ? s4b.y : r == 2 ? s4b.z : s4b.w;
+      accA = fmaf(scA, d[0] + d[1], accA);
+      accB = fmaf(scB, d[2] + d[3], accB);
+    }
+    tp += (uint64_t)kTileUnroll * TB;
+    sp += (uint64_t)(kTileUnroll / 4) * 64;
+    xp += (uint64_t)kTileUnroll * 32;
+  }
+  if (t < M) {
+    red[warp][t][g] = accA;
+    red[warp][t][g + 8] = accB;
+  }
+  __syncthreads();
+  if (warp == 0) {
+#pragma unroll
+    for (int pass = 0; pass < (M + 1) / 2; pass++) {
+      const int tt = pass * 2 + lane / 16, r = lane % 16;
+      const uint32_t row = grp * 16 + r;
+      const bool live = tt < M && row < a.n;
+      float2 nx = make_float2(0.f, 0.f);
+      if (live) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kTileWarps; w++) v += red[w][tt][r];
+        nx = gemv_epilogue(a, tt, row, v * kXPlaneScale);
+      }
+      if (a.rnext) {
+        float rs[9];
+        const uint32_t d = 2 * a.h;
+#pragma unroll
+        for (int o = 0; o < 8; o++)
+          rs[o] = live ? fmaf(__ldg(a.rnext + (uint64_t)o * d + row), nx.x, __ldg(a.rnext + (uint64_t)o * d + a.h + row) * nx.y)
+                       : 0.f;
+        rs[8] = live ? fmaf(nx.x, nx.x, nx.y * nx.y) : 0.f;
+#pragma unroll
+        for (int o = 0; o < 9; o++) {
+#pragma unroll
+          for (int off = 8; off > 0; off >>= 1) rs[o] += __shfl_xor_sync(0xffffffffu, rs[o], off);
+        }
+        if (r == 0 && tt < M) {
+#pragma unroll
+          for (int o = 0; o < 9; o++) a.rpart[((uint64_t)tt * gridDim.x + blockIdx.x) * 9 + o] = rs[o];
+        }
+      }
+    }
+  }
+}
+
+
+// Tile GEMV fed by bulk async copies: each warp streams its K range of a row group
+// through a ring of kBulkStages stages of 8 tiles (one contiguous copy of 4 KB (Q8) or
+// 2 KB (Q4) of tiles plus one of their grouped scales), so up to 4 stages are in flight
+// per warp whatever the consumer is doing. The consumer reads each lane's 16 (8) bytes
+// of a tile back from shared memory (contiguous, conflict-free) and runs the MMAs.
+constexpr int kBulkStages = 4;
+constexpr int kStageTiles = 8;
+
+template <int DT>
+struct BulkGeom {
+  static constexpr uint32_t TB = DT == SNL_Q8_0 ? 512 : 256;
+  static constexpr uint32_t kStageW = kStageTiles * TB;         // tile bytes per stage
+  static constexpr uint32_t kStageS = kStageTiles / 4 * 256;    // scale bytes per stage (2 groups of 4 blocks)
+  static constexpr uint32_t kStage = kStageW + kStageS;
+  static constexpr uint32_t kWarpBytes = kBulkStages * kStage;
+  static constexpr uint32_t kSmem = kTileWarps * kWarpBytes + kTileWarps * kBulkStages * 8;
+};
+
+template <int DT, int M>
+__global__ void __launch_bounds__(kTileWarps * 32) gemv_tile_bulk_kernel(GemvArgs a, const uint8_t* __restrict__ tiles,
+                                                                         const float* __restrict__ ts, int* err) {
+  using G = BulkGeom<DT>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ float red[kTileWarps][M][16];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const uint32_t nb = a.k / 32, nb4 = (nb + 3) / 4;
+  const uint32_t grp = blockIdx.x;
+  // Warp ranges are multiples of a stage (8 blocks) so every stage's scales are whole groups.
+  const uint32_t per = ((nb + kTileWarps * kStageTiles - 1) / (kTileWarps * kStageTiles)) * kStageTiles;
+  const uint32_t b_begin = min(nb, warp * per), b_end = min(nb, b_begin + per);
+  const uint32_t njobs = (b_end - b_begin + kStageTiles - 1) / kStageTiles;
+  uint8_t* ring = smem + warp * G::kWarpBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTileWarps * G::kWarpBytes) + warp * kBulkStages;
+  const uint8_t* tsrc = tiles + ((uint64_t)grp * nb + b_begin) * G::TB;
+  const uint8_t* ssrc = reinterpret_cast<const uint8_t*>(ts + ((uint64_t)grp * nb4 + b_begin / 4) * 64);
+
+  if (lane == 0)
+    for (int s = 0; s < kBulkStages; s++) mbar_init(&bars[s], 1);
+  fence_mbar_init();
+  __syncwarp();
+  const uint64_t pol = l2_policy_evict_first();
+  auto issue = [&](uint32_t j) {
+    if (lane != 0) return;
+    const uint32_t s = j % kBulkStages;
+    const uint32_t nt = min((uint32_t)kStageTiles, b_end - b_begin - j * kStageTiles);
+    const uint32_t wbytes = nt * G::TB, sbytes = (nt + 3) / 4 * 256;
+    uint8_t* st = ring + s * G::kStage;
+    mbar_arrive_expect_tx(&bars[s], wbytes + sbytes);
+    bulk_g2s(st, tsrc + (uint64_t)j * G::kStageW, wbytes, &bars[s], pol);
+    bulk_g2s(st + G::kStageW, ssrc + (uint64_t)j * G::kStageS, sbytes, &bars[s], pol);
+  };
+  for (uint32_t j = 0; j < min((uint32_t)kBulkStages, njobs); j++) issue(j);
+
+  const bool has_x = g < 2 * M;
+  const __half* xp = a.xplanes + (uint64_t)(has_x ? g : 0) * a.plane_stride + 8 * t + (uint64_t)b_begin * 32;
+  float accA = 0.f, accB = 0.f;
+  uint32_t j = 0;
+  bool ok = true;
+  for (; j < njobs; j++) {
+    const uint32_t s = j % kBulkStages;
+    const uint32_t nt = min((uint32_t)kStageTiles, b_end - b_begin - j * kStageTiles);
+    uint4 xv[kStageTiles];
+#pragma unroll
+    for (int u = 0; u < kStageTiles; u++) {
+      const uint32_t uu = min((uint32_t)u, nt - 1);
+      xv[u] = has_x ? __ldg(reinterpret_cast<const uint4*>(xp + ((uint64_t)j * kStageTiles + uu) * 32))
+                    : make_uint4(0, 0, 0, 0);
+    }
+    if (!mbar_wait_bounded(&bars[s], (j / kBulkStages) & 1)) {
+      ok = false;
+      break;
+    }
+    const uint8_t* st = ring + s * G::kStage;
+    const float* sc = reinterpret_cast<const float*>(st + G::kStageW);
+#pragma unroll
+    for (int u = 0; u < kStageTiles; u++) {
+      if ((uint32_t)u >= nt) break;
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      if constexpr (DT == SNL_Q8_0) {
+        const uint4 w = *reinterpret_cast<const uint4*>(st + u * G::TB + lane * 16);
+        const uint32_t A0[4] = {u8pair(w.x, 0x4140), u8pair(w.z, 0x4140), u8pair(w.x, 0x4342), u8pair(w.z, 0x4342)};
+        const uint32_t A1[4] = {u8pair(w.y, 0x4140), u8pair(w.w, 0x4140), u8pair(w.y, 0x4342), u8pair(w.w, 0x4342)};
+        mma16816(d, A0, xv[u].x, xv[u].y);
+        mma16816(d, A1, xv[u].z, xv[u].w);
+      } else {
+        const uint2 w = *reinterpret_cast<const uint2*>(st + u * G::TB + lane * 8);
+        const uint32_t A0[4] = {u4pair(w.x, 0), u4pair(w.y, 0), u4pair(w.x, 1), u4pair(w.y, 1)};
+        const uint32_t A1[4] = {u4pair(w.x, 2), u4pair(w.y, 2), u4pair(w.x, 3), u4pair(w.y, 3)};
+        mma16816(d, A0, xv[u].x, xv[u].y);
+        mma16816(d, A1, xv[u].z, xv[u].w);
+      }
+      // scales: [group of 4 blocks][16 rows][4]
+      const float scA = sc[(u / 4) * 64 + g * 4 + (u % 4)];
+      const float scB = sc[(u / 4) * 64 + (g + 8) * 4 + (u % 4)];
+      accA = fmaf(scA, d[0] + d[1], accA);
+      accB = fmaf(scB, d[2] + d[3], accB);
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (j + kBulkStages < njobs) issue(j + kBulkStages);
+  }
+  if (!ok) {
+    if (lane == 0) report_timeout(err);
+    const uint32_t last = min(njobs, j + kBulkStages);
+    for (uint32_t k2 = j; k2 < last; k2++) (void)mbar_wait_bounded(&bars[k2 % kBulkStages], (k2 / kBulkStages) & 1);
+  }
+  if (t < M) {
+    red[warp][t][g] = accA;
+    red[warp][t][g + 8] = accB;
+  }
+  __syncthreads();
+  if (warp == 0) {
+#pragma unroll
+    for (int pass = 0; pass < (M + 1) / 2; pass++) {
+      const int tt = pass * 2 + lane / 16, r = lane % 16;
+      const uint32_t row = grp * 16 + r;
+      const bool live = tt < M && row < a.n;
+      float2 nx = make_float2(0.f, 0.f);
+      if (live) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kTileWarps; w++) v += red[w][tt][r];
+        nx = gemv_epilogue(a, tt, row, v * kXPlaneScale);
+      }
+      if (a.rnext) {
+        float rs[9];
+        const uint32_t d = 2 * a.h;
+#pragma unroll
+        for (int o = 0; o < 8; o++)
+          rs[o] = live ? fmaf(__ldg(a.rnext + (uint64_t)o * d + row), nx.x, __ldg(a.rnext + (uint64_t)o * d + a.h + row) * nx.y)
+                       : 0.f;
+        rs[8] = live ? fmaf(nx.x, nx.x, nx.y * nx.y) : 0.f;
+#pragma unroll
+        for (int o = 0; o < 9; o++) {
+#pragma unroll
+          for (int off = 8; off > 0; off >>= 1) rs[o] += __shfl_xor_sync(0xffffffffu, rs[o], off);
+        }
+        if (r == 0 && tt < M) {
+#pragma unroll
+          for (int o = 0; o < 9; o++) a.rpart[((uint64_t)tt * gridDim.x + blockIdx.x) * 9 + o] = rs[o];
+        }
+      }
+    }
+  }
+}
+
+template <int DT, int M>
+int launch_tile_bulk_t(const GemvArgs& a, const void* tiles, const float* ts, int* err, cudaStream_t s) {
+  using G = BulkGeom<DT>;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto kern = gemv_tile_bulk_kernel<DT, M>;
+  if (dev >= 0 && dev < 64 && !attr[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
+    if (e != cudaSuccess) return cuda_fail(e, "gemv_tile_bulk: smem attribute");
+    attr[dev] = true;
+  }
+  kern<<<(a.n + 15) / 16, kTileWarps * 32, G::kSmem, s>>>(a, static_cast<const uint8_t*>(tiles), ts, err);
+  SNL_LAUNCH_CHECK("gemv_tile_bulk");
+  return SNL_OK;
+}
+
+template <int DT, int M>
+int launch_tile_t(const GemvArgs& a, const void* tiles, const float* ts, cudaStream_t s) {
+  gemv_tile_kernel<DT, M><<<(a.n + 15) / 16, kTileWarps * 32, 0, s>>>(a, static_cast<const uint8_t*>(tiles), ts);
+  SNL_LAUNCH_CHECK("gemv_tile");
+  return SNL_OK;
+}
+
+}  // namespace
+
+void tile_sizes(int dtype, uint32_t n, uint32_t k, size_t* tile_bytes, size_t* scale_floats) {
+  const size_t groups = (n + 15) / 16, nb = k / 32, nb4 = (nb + 3) / 4;
+  *tile_bytes = groups * nb * (dtype == SNL_Q8_0 ? 512 : 256);
+  *scale_floats = groups * nb4 * 64;
+}
+
+int launch_repack_tiles(int dtype, uint32_t n, uint32_t k, const void* q, const float* s, void* tiles, float* ts,
+                        cudaStream_t st) {
+  if (k % 32 || n == 0) return fail(SNL_E_INVALID, "repack: k must be a multiple of 32");
+  size_t tb, sf;
+  tile_sizes(dtype, n, k, &tb, &sf);
+  cudaError_t e = cudaMemsetAsync(ts, 0, sf * sizeof(float), st);  // scales of blocks past k in the last four
+  if (e != cudaSuccess) return cuda_fail(e, "repack: memset");
+  const uint64_t threads = (uint64_t)((n + 15) / 16) * (k / 32) * 32;
+  repack_tiles_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(dtype, n, k, static_cast<const uint8_t*>(q), s,
+                                                                         static_cast<uint8_t*>(tiles), ts);
+  SNL_LAUNCH_CHECK("repack_tiles");
+  return SNL_OK;
+}
+
+int launch_gemv_tile(int dtype, const GemvArgs& a, uint32_t m, const void* tiles, const float* ts, cudaStream_t s) {
+  if (a.k == 0 || a.k % 32) return fail(SNL_E_INVALID, "gemv_tile: k must be a multiple of 32");
+  if (a.plane_stride % 8 || ((uintptr_t)a.xplanes % 16)) return fail(SNL_E_INVALID, "gemv_tile: planes alignment");
+  if (a.n == 0) return SNL_OK;
+  static const bool direct = getenv("SNL_GEMV_TILE_DIRECT") != nullptr;
+  if (!direct) {
+    int* err = nullptr;
+    if (int rc = device_error_word(&err)) return rc;
+    if (dtype == SNL_Q8_0) {
+      switch (m) {
+        case 1: return launch_tile_bulk_t<SNL_Q8_0, 1>(a, tiles, ts, err, s);
+        case 2: return launch_tile_bulk_t<SNL_Q8_0, 2>(a, tiles, ts, err, s);
+        case 3: return launch_tile_bulk_t<SNL_Q8_0, 3>(a, tiles, ts, err, s);
+        case 4: return launch_tile_bulk_t<SNL_Q8_0, 4>(a, tiles, ts, err, s);
+      }
+    } else if (dtype == SNL_Q4_0) {
+      switch (m) {
+        case 1: return launch_tile_bulk_t<SNL_Q4_0, 1>(a, tiles, ts, err, s);
+        case 2: return launch_tile_bulk_t<SNL_Q4_0, 2>(a, tiles, ts, err, s);
+        case 3: return launch_tile_bulk_t<SNL_Q4_0, 3>(a, tiles, ts, err, s);
+        case 4: return launch_tile_bulk_t<SNL_Q4_0, 4>(a, tiles, ts, err, s);
+      }
+    }
+    return fail(SNL_E_INVALID, "gemv_tile: dtype / rows");
+  }
+  if (dtype == SNL_Q8_0) {
+    switch (m) {
+      case 1: return launch_tile_t<SNL_Q8_0, 1>(a, tiles, ts, s);
+      case 2: return launch_tile_t<SNL_Q8_0, 2>(a, tiles, ts, s);
+      case 3: return launch_tile_t<SNL_Q8_0, 3>(a, tiles, ts, s);
+      case 4: return launch_tile_t<SNL_Q8_0, 4>(a, tiles, ts, s);
+    }
+  } else if (dtype == SNL_Q4_0) {
+    switch (m) {
+      case 1: return launch_tile_t<SNL_Q4_0, 1>(a, tiles, ts, s);
+      case 2: return launch_tile_t<SNL_Q4_0, 2>(a, tiles, ts, s);
+      case 3: return launch_tile_t<SNL_Q4_0, 3>(a, tiles, ts, s);
+      case 4: return launch_tile_t<SNL_Q4_0, 4>(a, tiles, ts, s);
+    }
+  }
+  return fail(SNL_E_INVALID, "gemv_tile: dtype / rows");
+}
+
+}  // namespace snl
+
+extern "C" int snl_tile_sizes(int dtype, uint32_t n, uint32_t k, size_t* tile_bytes, size_t* scale_floats) {
+  if (!tile_bytes || !scale_floats || (dtype != SNL_Q8_0 && dtype != SNL_Q4_0)) return snl::fail(SNL_E_INVALID, "snl_tile_sizes");
+  snl::tile_sizes(dtype, n, k, tile_bytes, scale_floats);
+  return SNL_OK;
+}
+extern "C" int snl_tile_repack(int dtype, uint32_t n, uint32_t k, const void* q, const float* s, void* tiles,
+                               float* tile_scales, void* stream) {
+  if (!q || !s || !tiles || !tile_scales || (dtype != SNL_Q8_0 && dtype != SNL_Q4_0))
+    return snl::fail(SNL_E_INVALID, "snl_tile_repack: bad argument");
+  return snl::launch_repack_tiles(dtype, n, k, q, s, tiles, tile_scales, (cudaStream_t)stream);
+}
+extern "C" int snl_mat_tiles(int dtype, const snl_mat_p* p, uint32_t rows_m, const void* planes, const void* tiles,
+                             const float* tile_scales, float* y, void* stream) {
+  if (!p || !planes || !tiles || !tile_scales || !y) return snl::fail(SNL_E_INVALID, "snl_mat_tiles: null argument");
+  if (rows_m == 0 || rows_m > 4) return snl::fail(SNL_E_INVALID, "snl_mat_tiles: 1..4 token rows");
+  snl::GemvArgs a = snl::gemv_args_plain(*p, static_cast<const __half*>(planes), p->k, tiles, y);
+  return snl::launch_gemv_tile(dtype, a, rows_m, tiles, tile_scales, (cudaStream_t)stream);
+}

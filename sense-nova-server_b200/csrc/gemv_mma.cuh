@@ -1,0 +1,103 @@
+// Tensor-core GEMV interface: the packed x operand ("x planes") and the epilogues.
+#pragma once
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+
+namespace snl {
+
+// x planes hold x / kXPlaneScale split as hi + lo fp16 halves: plane 2t = hi, plane 2t+1
+// = lo for token row t, natural k order, plane_stride halves apart (multiple of 8).
+constexpr float kXPlaneScale = 16.0f;
+
+__device__ __forceinline__ void xplane_store(__half* planes, uint32_t plane_stride, uint32_t t, uint32_t i, float v) {
+  const float vs = v * (1.0f / kXPlaneScale);
+  const __half hi = __float2half_rn(vs);
+  const __half lo = __float2half_rn(vs - __half2float(hi));
+  planes[(uint64_t)(2 * t) * plane_stride + i] = hi;
+  planes[(uint64_t)(2 * t + 1) * plane_stride + i] = lo;
+}
+
+// Epilogue of one output element (token t, output row n):
+//   mode 0: y[y_off + t*y_stride + n_off + n] = v
+//   mode 1: residual merge into x [t, 2H] (layers.wgsl:268-302 `merge` mode `merge_mode`),
+//           then optionally copy stream 0 into stream 1 (`expand`, merge mode 3).
+struct GemvArgs {
+  uint32_t n, k;
+  const __half* xplanes;
+  uint32_t plane_stride;
+  const uint8_t* wq;
+  // epilogue
+  int mode;
+  float* y;
+  uint32_t y_off, y_stride, n_off;
+  float* resid;         // mode 1: x [t, 2H]
+  const float* coef;    // mode 1, merge modes 1/2: coef [t, 8]
+  uint32_t h;           // mode 1: hidden size H (= n)
+  int merge_mode;       // 0, 1, 2
+  int expand;           // also x1 = x0 afterwards
+  // mode 1, optional: the mHC router of the next norm ([8, 2H] weights, then 8 biases).
+  // Each CTA writes the 9 router sums over its rows of the merged (x0 | x1) to
+  // rpart[(t * gridDim.x + blockIdx.x) * 9 + o] (8 dots, then the sum of squares).
+  const float* rnext;
+  float* rpart;
+};
+
+// Returns the merged (x0, x1) of element n (mode 1), for the router partials.
+__device__ __forceinline__ float2 gemv_epilogue(const GemvArgs& a, uint32_t t, uint32_t n, float v) {
+  if (a.mode == 0) {
+    a.y[a.y_off + (uint64_t)t * a.y_stride + a.n_off + n] = v;
+    return make_float2(0.f, 0.f);
+  }
+  float* x0 = a.resid + (uint64_t)t * 2 * a.h + n;
+  float* x1 = x0 + a.h;
+  float n0, n1 = *x1;
+  if (a.merge_mode == 0) {
+    n0 = *x0 + v;
+    *x0 = n0;
+  } else {
+    const float* c = a.coef + t * 8;
+    const float a0 = *x0, a1 = n1;
+    n0 = fmaf(c[4], a0, fmaf(c[5], a1, c[2] * v));
+    const float m1 = fmaf(c[6], a0, fmaf(c[7], a1, c[3] * v));
+    if (a.merge_mode == 2) {
+      n0 = 0.5f * (n0 + m1);
+      *x0 = n0;
+    } else {
+      *x0 = n0;
+      *x1 = m1;
+      n1 = m1;
+    }
+  }
+  if (a.expand) {
+    *x1 = n0;
+    n1 = n0;
+  }
+  return make_float2(n0, n1);
+}
+
+inline GemvArgs gemv_args_plain(const snl_mat_p& p, const __half* planes, uint32_t plane_stride, const void* wq, float* y) {
+  GemvArgs a{};
+  a.n = p.n;
+  a.k = p.k;
+  a.xplanes = planes;
+  a.plane_stride = plane_stride;
+  a.wq = static_cast<const uint8_t*>(wq);
+  a.mode = 0;
+  a.y = y;
+  a.y_off = p.y_off;
+  a.y_stride = p.y_stride;
+  a.n_off = p.n_off;
+  return a;
+}
+
+int launch_gemv_mma(int dtype, const GemvArgs& a, uint32_t m, const void* ws, int scale_f16, cudaStream_t s);
+// Tile layout (see gemv_mma.cu): sizes, device repack from the reference layout, GEMV.
+void tile_sizes(int dtype, uint32_t n, uint32_t k, size_t* tile_bytes, size_t* scale_floats);
+int launch_repack_tiles(int dtype, uint32_t n, uint32_t k, const void* q, const float* s, void* tiles, float* ts,
+                        cudaStream_t st);
+int launch_gemv_tile(int dtype, const GemvArgs& a, uint32_t m, const void* tiles, const float* ts, cudaStream_t s);
+int launch_xpack(const float* x, uint32_t m, uint32_t k, uint32_t x_stride, __half* planes, uint32_t plane_stride,
+                 cudaStream_t s);
+
+}  // namespace snl

@@ -10,9 +10,10 @@ namespace snl {
 namespace {
 
 // branch_norm (layers.wgsl:186-213): one CTA per output row.
-__global__ void __launch_bounds__(256) branch_norm_kernel(StepRef sr, snl_layer_p p, const float* __restrict__ x,
-                                                          const float* __restrict__ coef, const float* __restrict__ w,
-                                                          float* __restrict__ out) {
+// Generic form (any h): strided loops.
+__global__ void __launch_bounds__(256) branch_norm_loop_kernel(StepRef sr, snl_layer_p p, const float* __restrict__ x,
+                                                               const float* __restrict__ coef, const float* __restrict__ w,
+                                                               float* __restrict__ out, XOut xo) {
   __shared__ float sh[32];
   const snl_step_u st = load_step(sr);
   const uint32_t g = blockIdx.x;
@@ -35,7 +36,105 @@ __global__ void __launch_bounds__(256) branch_norm_kernel(StepRef sr, snl_layer_
   for (uint32_t i = threadIdx.x; i < p.h; i += blockDim.x) {
     float v = pre0 * x[base + i];
     if (p.mode == 1) v = fmaf(pre1, x[base + p.h + i], v);
-    out[ob + i] = v * rinv * (p.weight_one + w[i]);
+    const float o = v * rinv * (p.weight_one + w[i]);
+    out[ob + i] = o;
+    if (xo.planes) xout_store(xo, g, i, o);
+  }
+}
+
+__device__ __forceinline__ void mhc_coef(const float raw[9], const float* __restrict__ w, uint32_t d,
+                                         uint32_t iterations, float* __restrict__ cb);
+
+// Router finished inside the norm: rpart holds nparts partial router sums per token (from
+// the GEMV that merged the residual); they are summed in a fixed order, the Sinkhorn
+// step runs on thread 0, and coef[m] is written for the later merge.
+struct NormRouter {
+  const float* rpart = nullptr;
+  uint32_t nparts = 0;
+  const float* router = nullptr;  // [8, 2H] weights then 8 biases
+  float* coef_out = nullptr;
+};
+
+// Register form (h % 4 == 0, h <= 1024 * VPT): every float4 of the row is loaded up front
+// into registers, so the row costs one memory latency instead of one per loop trip.
+template <int VPT>
+__global__ void __launch_bounds__(256) branch_norm_kernel(StepRef sr, snl_layer_p p, const float* __restrict__ x,
+                                                          const float* __restrict__ coef, const float* __restrict__ w,
+                                                          float* __restrict__ out, XOut xo, NormRouter nr) {
+  __shared__ float sh[32];
+  __shared__ float pre_sh[2];
+  const snl_step_u st = load_step(sr);
+  const uint32_t g = blockIdx.x;
+  const uint32_t m = g + (p.last_row == 1 ? st.m - 1 : 0);
+  const uint64_t base = (uint64_t)m * (p.x_stride != 0 ? p.x_stride : 2 * p.h);
+  float pre0 = 1.f, pre1 = 0.f;
+  if (p.mode == 1 && nr.rpart) {
+    float acc[9];
+#pragma unroll
+    for (int o = 0; o < 9; o++) acc[o] = 0.f;
+    for (uint32_t i = threadIdx.x; i < nr.nparts; i += blockDim.x) {
+#pragma unroll
+      for (int o = 0; o < 9; o++) acc[o] += nr.rpart[((uint64_t)m * nr.nparts + i) * 9 + o];
+    }
+    float tot[9];
+#pragma unroll
+    for (int o = 0; o < 9; o++) tot[o] = block_sum(acc[o], sh);
+    if (threadIdx.x == 0) {
+      float* cb = nr.coef_out + m * 8;
+      mhc_coef(tot, nr.router, 2 * p.h, p.iterations, cb);
+      pre_sh[0] = cb[0];
+      pre_sh[1] = cb[1];
+    }
+    __syncthreads();
+    pre0 = pre_sh[0];
+    pre1 = pre_sh[1];
+  } else if (p.mode == 1) {
+    pre0 = coef[m * 8];
+    pre1 = coef[m * 8 + 1];
+  }
+  const uint32_t h4 = p.h / 4;
+  const float4* x4 = reinterpret_cast<const float4*>(x + base);
+  float4 v[VPT];
+#pragma unroll
+  for (int c = 0; c < VPT; c++) {
+    const uint32_t i4 = threadIdx.x + c * 256;
+    v[c] = i4 < h4 ? x4[i4] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if (p.mode == 1) {
+#pragma unroll
+    for (int c = 0; c < VPT; c++) {
+      const uint32_t i4 = threadIdx.x + c * 256;
+      const float4 b = i4 < h4 ? x4[h4 + i4] : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[c].x = fmaf(pre1, b.x, pre0 * v[c].x);
+      v[c].y = fmaf(pre1, b.y, pre0 * v[c].y);
+      v[c].z = fmaf(pre1, b.z, pre0 * v[c].z);
+      v[c].w = fmaf(pre1, b.w, pre0 * v[c].w);
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < VPT; c++) ss += v[c].x * v[c].x + v[c].y * v[c].y + v[c].z * v[c].z + v[c].w * v[c].w;
+  const float total = block_sum(ss, sh);
+  const float rinv = rsqrtf(total / (float)p.h + p.eps);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  float4* o4 = reinterpret_cast<float4*>(out + (uint64_t)g * p.h);
+#pragma unroll
+  for (int c = 0; c < VPT; c++) {
+    const uint32_t i4 = threadIdx.x + c * 256;
+    if (i4 >= h4) break;
+    const float4 ww = w4[i4];
+    float4 o;
+    o.x = v[c].x * rinv * (p.weight_one + ww.x);
+    o.y = v[c].y * rinv * (p.weight_one + ww.y);
+    o.z = v[c].z * rinv * (p.weight_one + ww.z);
+    o.w = v[c].w * rinv * (p.weight_one + ww.w);
+    o4[i4] = o;
+    if (xo.planes) {
+      xout_store(xo, g, 4 * i4, o.x);
+      xout_store(xo, g, 4 * i4 + 1, o.y);
+      xout_store(xo, g, 4 * i4 + 2, o.z);
+      xout_store(xo, g, 4 * i4 + 3, o.w);
+    }
   }
 }
 
@@ -176,12 +275,15 @@ __global__ void merge_kernel(snl_layer_p p, uint32_t m_rows, float* __restrict__
 }
 
 // swiglu (layers.wgsl:304-315).
-__global__ void swiglu_kernel(snl_layer_p p, uint32_t m_rows, const float* __restrict__ gu, float* __restrict__ act) {
+__global__ void swiglu_kernel(snl_layer_p p, uint32_t m_rows, const float* __restrict__ gu, float* __restrict__ act,
+                              XOut xo) {
   const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (uint64_t)m_rows * p.inter) return;
   const uint64_t m = idx / p.inter, i = idx % p.inter;
   const float g = gu[m * 2 * p.inter + i], u = gu[m * 2 * p.inter + p.inter + i];
-  act[idx] = g / (1.0f + __expf(-g)) * u;
+  const float a = g / (1.0f + __expf(-g)) * u;
+  act[idx] = a;
+  if (xo.planes) xout_store(xo, (uint32_t)m, (uint32_t)i, a);
 }
 
 // Greedy argmax, two passes. Key = (ordered float bits << 32) | ~index so that the
@@ -273,10 +375,40 @@ __global__ void gen_f32_kernel(uint64_t k, uint64_t n, float mult, float offset,
 
 }  // namespace
 
-int launch_branch_norm(StepRef st, const snl_layer_p& p, const float* x, const float* coef, const float* w, float* out,
-                       uint32_t n_groups, cudaStream_t s) {
+int launch_branch_norm_router(StepRef st, const snl_layer_p& p, const float* x, float* coef, const float* w, float* out,
+                              uint32_t n_groups, cudaStream_t s, XOut xo, const float* rpart, uint32_t nparts,
+                              const float* router) {
   if (n_groups == 0) return SNL_OK;
-  branch_norm_kernel<<<n_groups, 256, 0, s>>>(st, p, x, coef, w, out);
+  const uint32_t stride = p.x_stride != 0 ? p.x_stride : 2 * p.h;
+  const bool vec = p.h % 4 == 0 && stride % 4 == 0 && ((uintptr_t)x % 16) == 0 && ((uintptr_t)w % 16) == 0 &&
+                   ((uintptr_t)out % 16) == 0;
+  const uint32_t vpt = (p.h / 4 + 255) / 256;
+  if (!vec || vpt > 8 || p.mode != 1) return fail(SNL_E_INVALID, "branch_norm_router: unsupported shape");
+  NormRouter nr;
+  nr.rpart = rpart;
+  nr.nparts = nparts;
+  nr.router = router;
+  nr.coef_out = coef;
+  if (vpt <= 1) branch_norm_kernel<1><<<n_groups, 256, 0, s>>>(st, p, x, coef, w, out, xo, nr);
+  else if (vpt <= 2) branch_norm_kernel<2><<<n_groups, 256, 0, s>>>(st, p, x, coef, w, out, xo, nr);
+  else if (vpt <= 4) branch_norm_kernel<4><<<n_groups, 256, 0, s>>>(st, p, x, coef, w, out, xo, nr);
+  else branch_norm_kernel<8><<<n_groups, 256, 0, s>>>(st, p, x, coef, w, out, xo, nr);
+  SNL_LAUNCH_CHECK("branch_norm_router");
+  return SNL_OK;
+}
+
+int launch_branch_norm(StepRef st, const snl_layer_p& p, const float* x, const float* coef, const float* w, float* out,
+                       uint32_t n_groups, cudaStream_t s, XOut xo) {
+  if (n_groups == 0) return SNL_OK;
+  const uint32_t stride = p.x_stride != 0 ? p.x_stride : 2 * p.h;
+  const bool vec = p.h % 4 == 0 && stride % 4 == 0 && ((uintptr_t)x % 16) == 0 && ((uintptr_t)w % 16) == 0 &&
+                   ((uintptr_t)out % 16) == 0;
+  const uint32_t vpt = (p.h / 4 + 255) / 256;
+  if (vec && vpt <= 1) branch_norm_kernel<1><<<n_groups, 256, 0, s>>>(st, p, x, coef, w, out, xo, NormRouter());
+  else if (vec && vpt <= 2) branch_norm_kernel<2><<<n_groups, 256, 0, s>>>(st, p, x, coef, w, out, xo, NormRouter());
+  else if (vec && vpt <= 4) branch_norm_kernel<4><<<n_groups, 256, 0, s>>>(st, p, x, coef, w, out, xo, NormRouter());
+  else if (vec && vpt <= 8) branch_norm_kernel<8><<<n_groups, 256, 0, s>>>(st, p, x, coef, w, out, xo, NormRouter());
+  else branch_norm_loop_kernel<<<n_groups, 256, 0, s>>>(st, p, x, coef, w, out, xo);
   SNL_LAUNCH_CHECK("branch_norm");
   return SNL_OK;
 }
@@ -315,11 +447,11 @@ int launch_merge(StepRef st, const snl_layer_p& p, float* x, const float* coef, 
   SNL_LAUNCH_CHECK("merge");
   return SNL_OK;
 }
-int launch_swiglu(StepRef st, const snl_layer_p& p, const float* gu, float* act, uint32_t m, cudaStream_t s) {
+int launch_swiglu(StepRef st, const snl_layer_p& p, const float* gu, float* act, uint32_t m, cudaStream_t s, XOut xo) {
   (void)st;
   const uint64_t n = (uint64_t)m * p.inter;
   if (n == 0) return SNL_OK;
-  swiglu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(p, m, gu, act);
+  swiglu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(p, m, gu, act, xo);
   SNL_LAUNCH_CHECK("swiglu");
   return SNL_OK;
 }

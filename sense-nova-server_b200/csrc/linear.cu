@@ -43,7 +43,7 @@ __global__ void conv_kernel(StepRef sr, snl_lin_p p, const float* __restrict__ p
 __global__ void __launch_bounds__(128) delta_kernel(StepRef sr, snl_lin_p p, const float* __restrict__ proj,
                                                     const float* __restrict__ conv_out, float* __restrict__ state,
                                                     const float* __restrict__ lw, float* __restrict__ out,
-                                                    float* __restrict__ state_ckpt) {
+                                                    float* __restrict__ state_ckpt, XOut xo) {
   __shared__ float qs[DK], ks[DK];
   __shared__ float red[32];
   const snl_step_u st = load_step(sr);
@@ -89,12 +89,115 @@ __global__ void __launch_bounds__(128) delta_kernel(StepRef sr, snl_lin_p p, con
     }
     const float var_o = block_sum(o * o, red) / (float)DV;
     const float z = proj[prow + z_off + h * DV + j];
-    out[(uint64_t)m * p.n_v * DV + h * DV + j] = o * rsqrtf(var_o + p.eps) * norm_w * (z / (1.0f + __expf(-z)));
+    const float ov = o * rsqrtf(var_o + p.eps) * norm_w * (z / (1.0f + __expf(-z)));
+    out[(uint64_t)m * p.n_v * DV + h * DV + j] = ov;
+    if (xo.planes) xout_store(xo, m, h * DV + j, ov);
     if (m + 1 == st.ckpt) {
 #pragma unroll
       for (uint32_t i = 0; i < DK; i++) state_ckpt[sbase + i * DV + j] = S[i];
     }
     __syncthreads();
+  }
+#pragma unroll
+  for (uint32_t i = 0; i < DK; i++) state[sbase + i * DV + j] = S[i];
+}
+
+// conv + delta in one kernel (the engine's form of linear.wgsl:38-140): CTA per value
+// head h, thread j owns the head's q, k and v channels j (conv weights and the 3-token
+// conv state of each in registers) and state column j. The causal conv + SiLU of the
+// three channels is computed token by token in registers, so no conv_out buffer is
+// written. The q/k channels of key head kh are shared by the n_v/n_k value heads of its
+// group; the first of them owns their conv state and checkpoint writes.
+__global__ void __launch_bounds__(128) conv_delta_kernel(StepRef sr, snl_lin_p p, const float* __restrict__ proj,
+                                                         float* __restrict__ conv_state, float* __restrict__ state,
+                                                         const float* __restrict__ lw, float* __restrict__ out,
+                                                         float* __restrict__ conv_ckpt, float* __restrict__ state_ckpt,
+                                                         XOut xo) {
+  __shared__ float qs[DK], ks[DK];
+  __shared__ float red[32];
+  const snl_step_u st = load_step(sr);
+  const uint32_t h = blockIdx.x, j = threadIdx.x;
+  const uint32_t group = p.n_v / p.n_k;
+  const uint32_t kh = h / group;
+  const bool owns_qk = (h % group) == 0;
+  const uint32_t cd = p.conv_dim, key_dim = p.n_k * DK;
+  const uint32_t ch[3] = {kh * DK + j, key_dim + kh * DK + j, 2 * key_dim + h * DV + j};  // q, k, v channels
+  float4 cw[3];
+  float r[3][3];
+#pragma unroll
+  for (int c = 0; c < 3; c++) {
+    cw[c] = *reinterpret_cast<const float4*>(lw + (uint64_t)ch[c] * 4);
+#pragma unroll
+    for (int k = 0; k < 3; k++) r[c][k] = conv_state[(uint64_t)k * cd + ch[c]];
+  }
+  const uint64_t sbase = (uint64_t)h * DK * DV;
+  const float a_log = lw[(uint64_t)cd * 4 + h];
+  const float dt_bias = lw[(uint64_t)cd * 4 + p.n_v + h];
+  const float norm_w = lw[(uint64_t)cd * 4 + 2 * p.n_v + j];
+  const float neg_a = -__expf(a_log);
+  const uint32_t z_off = cd, b_off = cd + p.n_v * DV, a_off = b_off + p.n_v;
+  float S[DK];
+#pragma unroll
+  for (uint32_t i = 0; i < DK; i++) S[i] = state[sbase + i * DV + j];
+  for (uint32_t m = 0; m < st.m; m++) {
+    const uint64_t prow = (uint64_t)m * p.proj_stride;
+    float cv[3];
+#pragma unroll
+    for (int c = 0; c < 3; c++) {
+      const float cur = proj[prow + ch[c]];
+      const float o = fmaf(cw[c].w, cur, fmaf(cw[c].z, r[c][2], fmaf(cw[c].y, r[c][1], cw[c].x * r[c][0])));
+      cv[c] = o / (1.0f + __expf(-o));
+      r[c][0] = r[c][1];
+      r[c][1] = r[c][2];
+      r[c][2] = cur;
+    }
+    if (m + 1 == st.ckpt) {
+#pragma unroll
+      for (int c = 0; c < 3; c++) {
+        if (c < 2 && !owns_qk) continue;
+#pragma unroll
+        for (int k = 0; k < 3; k++) conv_ckpt[(uint64_t)k * cd + ch[c]] = r[c][k];
+      }
+    }
+    const float qv = cv[0], kv = cv[1], vv = cv[2];
+    const float sq = block_sum(qv * qv, red);
+    const float sk = block_sum(kv * kv, red);
+    qs[j] = qv * rsqrtf(sq + 1e-6f) * rsqrtf((float)DK);
+    ks[j] = kv * rsqrtf(sk + 1e-6f);
+    __syncthreads();
+    const float beta = 1.0f / (1.0f + __expf(-proj[prow + b_off + h]));
+    const float araw = proj[prow + a_off + h] + dt_bias;
+    const float sp = araw <= 20.0f ? log1pf(__expf(araw)) : araw;
+    const float decay = __expf(neg_a * sp);
+    float kv_mem = 0.f;
+#pragma unroll
+    for (uint32_t i = 0; i < DK; i++) {
+      S[i] *= decay;
+      kv_mem = fmaf(S[i], ks[i], kv_mem);
+    }
+    const float dlt = (vv - kv_mem) * beta;
+    float o = 0.f;
+#pragma unroll
+    for (uint32_t i = 0; i < DK; i++) {
+      S[i] = fmaf(ks[i], dlt, S[i]);
+      o = fmaf(S[i], qs[i], o);
+    }
+    const float var_o = block_sum(o * o, red) / (float)DV;
+    const float z = proj[prow + z_off + h * DV + j];
+    const float ov = o * rsqrtf(var_o + p.eps) * norm_w * (z / (1.0f + __expf(-z)));
+    out[(uint64_t)m * p.n_v * DV + h * DV + j] = ov;
+    if (xo.planes) xout_store(xo, m, h * DV + j, ov);
+    if (m + 1 == st.ckpt) {
+#pragma unroll
+      for (uint32_t i = 0; i < DK; i++) state_ckpt[sbase + i * DV + j] = S[i];
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int c = 0; c < 3; c++) {
+    if (c < 2 && !owns_qk) continue;
+#pragma unroll
+    for (int k = 0; k < 3; k++) conv_state[(uint64_t)k * cd + ch[c]] = r[c][k];
   }
 #pragma unroll
   for (uint32_t i = 0; i < DK; i++) state[sbase + i * DV + j] = S[i];
@@ -117,10 +220,18 @@ int launch_conv(StepRef st, const snl_lin_p& p, const float* proj, float* conv_o
 }
 
 int launch_delta(StepRef st, const snl_lin_p& p, const float* proj, const float* conv_out, float* state,
-                 const float* lw, float* out, float* state_ckpt, cudaStream_t s) {
+                 const float* lw, float* out, float* state_ckpt, cudaStream_t s, XOut xo) {
   if (int rc = check_lin(p)) return rc;
-  delta_kernel<<<p.n_v, DV, 0, s>>>(st, p, proj, conv_out, state, lw, out, state_ckpt);
+  delta_kernel<<<p.n_v, DV, 0, s>>>(st, p, proj, conv_out, state, lw, out, state_ckpt, xo);
   SNL_LAUNCH_CHECK("delta");
+  return SNL_OK;
+}
+
+int launch_conv_delta(StepRef st, const snl_lin_p& p, const float* proj, float* conv_state, float* state,
+                      const float* lw, float* out, float* conv_ckpt, float* state_ckpt, cudaStream_t s, XOut xo) {
+  if (int rc = check_lin(p)) return rc;
+  conv_delta_kernel<<<p.n_v, DV, 0, s>>>(st, p, proj, conv_state, state, lw, out, conv_ckpt, state_ckpt, xo);
+  SNL_LAUNCH_CHECK("conv_delta");
   return SNL_OK;
 }
 

@@ -23,6 +23,24 @@ namespace snl {
 // by snl_device_error().
 __device__ int g_dev_error;
 
+// Device address of g_dev_error on the current device, for kernels in other files
+// (looked up once per device).
+int device_error_word(int** out) {
+  static int* addr[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(SNL_E_INVALID, "device ordinal out of range");
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_dev_error);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_dev_error)");
+    addr[dev] = static_cast<int*>(p);
+  }
+  *out = addr[dev];
+  return SNL_OK;
+}
+
 namespace {
 
 constexpr int kRowsPerWarp = 4;

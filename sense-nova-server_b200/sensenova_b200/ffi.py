@@ -93,6 +93,11 @@ SIGNATURES = {
     "snl_device_error": (i32, [i32]),
     "snl_config_validate": (i32, [P(ModelConfigC)]),
     "snl_mat": (i32, [i32, P(StepU), P(MatP), vp, vp, vp, vp, vp]),
+    "snl_xpack": (i32, [vp, u32, u32, u32, vp, vp]),
+    "snl_mat_xpack": (i32, [i32, P(MatP), u32, vp, vp, vp, vp, vp]),
+    "snl_tile_sizes": (i32, [i32, u32, u32, P(sz), P(sz)]),
+    "snl_tile_repack": (i32, [i32, u32, u32, vp, vp, vp, vp, vp]),
+    "snl_mat_tiles": (i32, [i32, P(MatP), u32, vp, vp, vp, vp, vp]),
     "snl_branch_norm": (i32, [P(StepU), P(LayerP), vp, vp, vp, vp, u32, vp]),
     "snl_mhc_dots": (i32, [P(StepU), P(LayerP), vp, vp, vp, vp]),
     "snl_mhc_finish": (i32, [P(StepU), P(LayerP), vp, vp, vp, vp]),

@@ -66,6 +66,22 @@ def test_greedy_256_steps_identical(torch_cuda, orc, cfg):
     e.close()
 
 
+def test_simt_fallback_path_matches_oracle(torch_cuda, orc, cfg, monkeypatch):
+    """SNL_NO_TC: the same engine on the SIMT GEMVs and separate merge kernels."""
+    monkeypatch.setenv("SNL_NO_TC", "1")
+    e = Engine.synthetic(cfg, 320, 21)
+    monkeypatch.delenv("SNL_NO_TC")
+    o = orc.OracleModel(cfg, 320, seed=21)
+    prompt = [(3 + i * 101) % cfg.vocab for i in range(9)]
+    le, lo = e.forward(prompt, True), o.forward(prompt, True)
+    assert rel(le, lo) < TOL
+    for _ in range(8):
+        t = int(np.argmax(lo))
+        le, lo = e.forward([t], True), o.forward([t], True)
+        assert rel(le, lo) < TOL and int(np.argmax(le)) == int(np.argmax(lo))
+    e.close()
+
+
 def test_forward_greedy_matches_logits(torch_cuda, orc, cfg):
     e, _ = pair(orc, cfg, seed=13)
     e2 = Engine.synthetic(cfg, 320, 13)

@@ -130,6 +130,65 @@ def test_mat_strides_offsets(T, lib, orc):
     assert rel(y, ref) < TOL
 
 
+@pytest.mark.parametrize("dtype", [SNL_Q8_0, SNL_Q4_0])
+@pytest.mark.parametrize("m", [1, 2, 3, 4])
+@pytest.mark.parametrize("n,k", [(200, 1024), (37, 96), (12288, 4096), (4096, 12288)])
+def test_mat_tensor_core(T, lib, orc, dtype, m, n, k):
+    """The tensor-core GEMV (x as fp16 hi/lo planes) against the oracle's matvec."""
+    rng = np.random.default_rng(n + k + m)
+    q, s = orc.gen_quant(n + m, "wtc", dtype, n, k)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    ref = np.zeros((m, n), np.float32)
+    orc.mat(dtype, StepU(m, 0, 1, 0), MatP(n, k, 0, k, 0, n, 0, 0), x, q, s, ref)
+    planes = T.empty(2 * m * k, dtype=T.float16, device="cuda")
+    call(lib.snl_xpack(ptr(dev(T, x)), m, k, k, ptr(planes), None))
+    y = T.zeros((m, n), device="cuda")
+    p = MatP(n, k, 0, k, 0, n, 0, 0)
+    call(lib.snl_mat_xpack(dtype, C.byref(p), m, ptr(planes), ptr(dev(T, q)), ptr(dev(T, s)), ptr(y), None))
+    err = rel(host(y), ref)
+    assert err < TOL and err < 2e-5, err
+
+
+@pytest.mark.parametrize("dtype", [SNL_Q8_0, SNL_Q4_0])
+@pytest.mark.parametrize("m", [1, 2, 3, 4])
+@pytest.mark.parametrize("n,k", [(200, 1024), (37, 96), (12288, 4096), (4096, 12288), (33, 160)])
+def test_mat_tiles(T, lib, orc, dtype, m, n, k):
+    """Tile-layout repack + the tile GEMV (the engine's decode path) against the oracle."""
+    rng = np.random.default_rng(n * 3 + k + m)
+    q, s = orc.gen_quant(n + 7 * m, "wtile", dtype, n, k)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    ref = np.zeros((m, n), np.float32)
+    orc.mat(dtype, StepU(m, 0, 1, 0), MatP(n, k, 0, k, 0, n, 0, 0), x, q, s, ref)
+    tb, sf = C.c_size_t(), C.c_size_t()
+    call(lib.snl_tile_sizes(dtype, n, k, C.byref(tb), C.byref(sf)))
+    tiles = T.empty(tb.value, dtype=T.uint8, device="cuda")
+    ts = T.empty(sf.value, dtype=T.float32, device="cuda")
+    call(lib.snl_tile_repack(dtype, n, k, ptr(dev(T, q)), ptr(dev(T, s)), ptr(tiles), ptr(ts), None))
+    planes = T.empty(2 * m * k, dtype=T.float16, device="cuda")
+    call(lib.snl_xpack(ptr(dev(T, x)), m, k, k, ptr(planes), None))
+    y = T.zeros((m, n), device="cuda")
+    p = MatP(n, k, 0, k, 0, n, 0, 0)
+    call(lib.snl_mat_tiles(dtype, C.byref(p), m, ptr(planes), ptr(tiles), ptr(ts), ptr(y), None))
+    err = rel(host(y), ref)
+    assert err < TOL and err < 2e-5, err
+
+
+def test_mat_tensor_core_wide_range(T, lib, orc):
+    # |x| up to ~5e4: the 1/16 pre-scale keeps the fp16 planes finite and accurate.
+    rng = np.random.default_rng(77)
+    n, k = 256, 2048
+    q, s = orc.gen_quant(5, "wide", SNL_Q8_0, n, k)
+    x = (rng.standard_normal((1, k)) * np.exp(rng.uniform(-8, 10, (1, k)))).astype(np.float32)
+    ref = np.zeros((1, n), np.float32)
+    orc.mat(SNL_Q8_0, StepU(1, 0, 1, 0), MatP(n, k, 0, k, 0, n, 0, 0), x, q, s, ref)
+    planes = T.empty(2 * k, dtype=T.float16, device="cuda")
+    call(lib.snl_xpack(ptr(dev(T, x)), 1, k, k, ptr(planes), None))
+    y = T.zeros((1, n), device="cuda")
+    p = MatP(n, k, 0, k, 0, n, 0, 0)
+    call(lib.snl_mat_xpack(SNL_Q8_0, C.byref(p), 1, ptr(planes), ptr(dev(T, q)), ptr(dev(T, s)), ptr(y), None))
+    assert rel(host(y), ref) < TOL
+
+
 def test_mat_rejects_misaligned(T, lib):
     st, p = StepU(1, 0, 1, 0), MatP(8, 32, 2, 32, 0, 8, 0, 0)
     buf = T.zeros(1024, device="cuda")
