@@ -207,6 +207,17 @@ int snl_delta(const snl_step_u* step, const snl_lin_p* p, const float* proj, con
 /* Greedy argmax of each of `rows` rows of `n` logits (sampler.rs:169-177: the first
  * maximum wins); out_idx is a device u32[rows]. */
 int snl_argmax(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_idx, void* stream);
+
+/* snl_argmax for callers that must not allocate device memory when they call it (no
+ * counterpart in the reference): a host whose device memory is reserved by its own
+ * pool allocator, or a serving loop that cannot take the device-wide wait of a free.
+ * Same arguments and results as snl_argmax; it calls no cudaMalloc, cudaFree or other
+ * allocating routine. Its scratch is a static 16 KB device array per GPU, so rows must
+ * be <= 16 (SNL_E_RANGE otherwise). The first call on a device looks up that array's
+ * address (cudaGetSymbolAddress) with the device current; make that first call before
+ * any stream capture. All calls share the array: calls that overlap on the GPU (for
+ * example on two streams at once) race and must be serialised by the caller. */
+int snl_argmax_noalloc(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_idx, void* stream);
 /* ---- seeded synthetic tensors ------------------------------------------------------- */
 
 /* Fill device buffers with tensor `name` of the seeded synthetic model (the benchmark

@@ -2,6 +2,7 @@
 // (sampler.rs:169-177), the device-side embedding dequant (engine.rs:777-790,
 // weights.rs:155-162) and the seeded synthetic-weight generators.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "synth.h"
@@ -569,4 +570,55 @@ extern "C" int snl_synth_f32(uint64_t seed, const char* name, uint32_t sub, size
                              float* out, void* stream) {
   if (!name || !out) return snl::fail(SNL_E_INVALID, "snl_synth_f32: null argument");
   return snl::launch_gen_f32(seed, name, sub, n, mult, offset, out, (cudaStream_t)stream);
+}
+
+// ---- argmax without allocation ------------------------------------------------------
+//
+// snl_argmax keeps its per-block partial keys in a buffer it cudaMalloc's on first use
+// (and frees and re-allocates when more rows are asked for; cudaFree waits for the whole
+// device). snl_argmax_noalloc serves callers that must not allocate or free device
+// memory at that point: a host whose device memory is all reserved by its own pool
+// allocator, or a per-token serving loop that shares the GPU and cannot afford the
+// device-wide wait of a free. Its scratch is this file-scope array, sized for
+// kNoAllocRows rows (16 KB), held by every GPU that loads the library until exit.
+namespace snl {
+namespace {
+constexpr uint32_t kNoAllocRows = 16;
+__device__ __align__(256) unsigned long long g_argmax_noalloc_scratch[kNoAllocRows * kArgBlocks];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+unsigned long long* g_noalloc_addr[kMaxDevices] = {nullptr};
+
+// Device address of the scratch array on the current device. In host code the array's
+// name only stands in for it, so the address is looked up once per device (with that
+// device current) and cached.
+int noalloc_scratch(unsigned long long** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return snl::cuda_fail(e, "snl_argmax_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return snl::fail(SNL_E_INVALID, "snl_argmax_noalloc: device ordinal out of range");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_argmax_noalloc_scratch);
+    if (e != cudaSuccess) return snl::cuda_fail(e, "snl_argmax_noalloc: cudaGetSymbolAddress");
+    g_noalloc_addr[dev] = static_cast<unsigned long long*>(p);
+  }
+  *out = g_noalloc_addr[dev];
+  return SNL_OK;
+}
+}  // namespace
+}  // namespace snl
+
+extern "C" int snl_argmax_noalloc(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_idx, void* stream) {
+  if (!logits || !out_idx || n == 0) return snl::fail(SNL_E_INVALID, "snl_argmax_noalloc: bad argument");
+  if (rows > snl::kNoAllocRows)
+    return snl::fail(SNL_E_RANGE, "snl_argmax_noalloc: " + std::to_string(rows) + " rows exceed the static scratch of " +
+                                      std::to_string(snl::kNoAllocRows) + " rows");
+  unsigned long long* part = nullptr;
+  if (int rc = snl::noalloc_scratch(&part)) return rc;
+  // Every partial slot the second pass reads is written by the first pass of the same
+  // call, so nothing in the shared scratch has to be cleared between calls.
+  return snl::launch_argmax_with(logits, rows, n, out_idx, part, (cudaStream_t)stream);
 }

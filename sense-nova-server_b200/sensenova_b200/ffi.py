@@ -109,6 +109,7 @@ SIGNATURES = {
     "snl_conv": (i32, [P(StepU), P(LinP), vp, vp, vp, vp, vp, vp]),
     "snl_delta": (i32, [P(StepU), P(LinP), vp, vp, vp, vp, vp, vp, vp]),
     "snl_argmax": (i32, [vp, u32, u32, vp, vp]),
+    "snl_argmax_noalloc": (i32, [vp, u32, u32, vp, vp]),
     "snl_synth_quant": (i32, [u64, C.c_char_p, i32, sz, sz, vp, vp, vp]),
     "snl_synth_f32": (i32, [u64, C.c_char_p, u32, sz, C.c_float, C.c_float, vp, vp]),
     "snl_engine_create": (i32, [P(ModelConfigC), sz, i32, u32, P(vp)]),
