@@ -6,6 +6,7 @@
 // cache[(pos * kv_dim + kh*256 + d) / 2]; split-K partials are
 // [(m*n_heads + h)*parts + part][256 acc | max | sum].
 #include "common.cuh"
+#include "ptx.cuh"
 
 namespace snl {
 namespace {
@@ -24,6 +25,8 @@ __global__ void __launch_bounds__(256) prep_kernel(StepRef sr, snl_attn_p p, con
                                                    float* __restrict__ qbuf, uint32_t* __restrict__ kc,
                                                    uint32_t* __restrict__ vc, const float* __restrict__ norms,
                                                    const uint32_t* __restrict__ rpos) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float sh[HD];
   __shared__ float red[32];
   const snl_step_u st = load_step(sr);
@@ -104,6 +107,8 @@ __global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, c
                                                      const float* __restrict__ qbuf, const uint32_t* __restrict__ kc,
                                                      const uint32_t* __restrict__ vc, float* __restrict__ out,
                                                      float* __restrict__ partial, XOut xo) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float s_acc[kAttWarps][G][HD];  // 32 KB
   __shared__ float s_ml[kAttWarps][G][2];
   __shared__ float s_p[kAttWarps][32];
@@ -237,6 +242,8 @@ __global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, c
 __global__ void __launch_bounds__(256) combine_kernel(StepRef sr, snl_attn_p p, const float* __restrict__ proj,
                                                       const float* __restrict__ partial, float* __restrict__ out,
                                                       int skip_single, XOut xo) {
+  pdl_trigger();
+  pdl_wait();
   const snl_step_u st = load_step(sr);
   const uint32_t h = blockIdx.x, m = blockIdx.y, d = threadIdx.x;
   if (m >= st.m || (skip_single && st.parts <= 1)) return;
@@ -269,8 +276,7 @@ int launch_attn_prep(StepRef st, const snl_attn_p& p, const float* proj, float* 
                      const float* norms, const uint32_t* rpos, uint32_t m, cudaStream_t s) {
   if (int rc = check_attn(p)) return rc;
   if (m == 0) return SNL_OK;
-  prep_kernel<<<dim3(p.n_heads + 2 * p.n_kv, m), HD, 0, s>>>(st, p, proj, qbuf, kc, vc, norms, rpos);
-  SNL_LAUNCH_CHECK("attn_prep");
+  SNL_PDL_LAUNCH("prep_kernel", prep_kernel, dim3(dim3(p.n_heads + 2 * p.n_kv, m)), dim3(HD), (size_t)(0), s, st, p, proj, qbuf, kc, vc, norms, rpos);
   return SNL_OK;
 }
 
@@ -279,8 +285,7 @@ int launch_attend(StepRef st, const snl_attn_p& p, const float* proj, const floa
                   XOut xo) {
   if (int rc = check_attn(p)) return rc;
   if (m == 0 || parts_grid == 0) return SNL_OK;
-  attend_kernel<<<dim3(p.n_kv, m, parts_grid), kAttWarps * 32, 0, s>>>(st, p, proj, qbuf, kc, vc, out, partial, xo);
-  SNL_LAUNCH_CHECK("attend");
+  SNL_PDL_LAUNCH("attend_kernel", attend_kernel, dim3(dim3(p.n_kv, m, parts_grid)), dim3(kAttWarps * 32), (size_t)(0), s, st, p, proj, qbuf, kc, vc, out, partial, xo);
   return SNL_OK;
 }
 
@@ -288,8 +293,7 @@ int launch_attn_combine(StepRef st, const snl_attn_p& p, const float* proj, cons
                         uint32_t m, cudaStream_t s, int skip_single, XOut xo) {
   if (int rc = check_attn(p)) return rc;
   if (m == 0) return SNL_OK;
-  combine_kernel<<<dim3(p.n_heads, m), HD, 0, s>>>(st, p, proj, partial, out, skip_single, xo);
-  SNL_LAUNCH_CHECK("attn_combine");
+  SNL_PDL_LAUNCH("combine_kernel", combine_kernel, dim3(dim3(p.n_heads, m)), dim3(HD), (size_t)(0), s, st, p, proj, partial, out, skip_single, xo);
   return SNL_OK;
 }
 

@@ -101,6 +101,32 @@ __device__ __forceinline__ void xout_store(const XOut& xo, uint32_t t, uint32_t 
 // Device address of the library's device error word (bit 0: a bounded wait gave up).
 int device_error_word(int** out);
 
+// Launches with programmatic stream serialization (unless SNL_NO_PDL is set): the
+// kernel may begin while the previous kernel on the stream finishes. Every kernel
+// launched this way calls pdl_wait() before it touches anything an earlier kernel wrote.
+bool pdl_on();
+int sm_count();  // SMs of the current device (cached per device)
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_on() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+#define SNL_PDL_LAUNCH(what, ...)                                \
+  do {                                                           \
+    cudaError_t _e = ::snl::launch_pdl(__VA_ARGS__);             \
+    if (_e != cudaSuccess) return ::snl::cuda_fail(_e, what);    \
+    ::snl::count_launch();                                       \
+  } while (0)
+
 // Launch helpers implemented per kernel family (internal, not part of the C ABI).
 int launch_mat(int dtype, StepRef st, const snl_mat_p& p, const float* x, const void* wq, const void* ws,
                int scale_f16, float* y, cudaStream_t s, uint32_t rows_m_host);

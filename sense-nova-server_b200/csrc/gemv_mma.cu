@@ -211,6 +211,8 @@ int launch_m(const GemvArgs& a, uint32_t m, const void* ws, cudaStream_t s) {
 // x [m, x_stride] f32 -> planes [2m][plane_stride] halves (hi, lo per token).
 __global__ void xpack_kernel(const float* __restrict__ x, uint32_t k, uint32_t x_stride, uint32_t m,
                              __half* __restrict__ planes, uint32_t plane_stride) {
+  pdl_trigger();
+  pdl_wait();
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
   const uint32_t t = blockIdx.y;
   if (i >= k || t >= m) return;
@@ -232,8 +234,7 @@ int launch_gemv_mma(int dtype, const GemvArgs& a, uint32_t m, const void* ws, in
 int launch_xpack(const float* x, uint32_t m, uint32_t k, uint32_t x_stride, __half* planes, uint32_t plane_stride,
                  cudaStream_t s) {
   if (m == 0 || k == 0) return SNL_OK;
-  xpack_kernel<<<dim3((k + 255) / 256, m), 256, 0, s>>>(x, k, x_stride, m, planes, plane_stride);
-  SNL_LAUNCH_CHECK("xpack");
+  SNL_PDL_LAUNCH("xpack_kernel", xpack_kernel, dim3(dim3((k + 255) / 256, m)), dim3(256), (size_t)(0), s, x, k, x_stride, m, planes, plane_stride);
   return SNL_OK;
 }
 
@@ -596,6 +597,197 @@ __global__ void __launch_bounds__(kTileWarps * 32) gemv_tile_bulk_kernel(GemvArg
   }
 }
 
+// ---------------------------------------------------------------------------
+// Persistent row-group tile GEMV (the default decode GEMV).
+//
+// A grid of up to kPgCtasPerSm CTAs per SM; CTA b owns the contiguous row groups
+// [b*G/grid, (b+1)*G/grid). The kPgWarps warps of a CTA split every group's K range
+// into equal runs of stages (kPgTiles tiles plus their scales, one contiguous bulk copy
+// each), stream them through a per-warp ring of kStages stages, and meet once per group
+// in shared memory, where warp 0 adds the warp partials in warp order and runs the
+// epilogue (double-buffered, so the other warps go on streaming the next group).
+// The first stages are issued before pdl_wait(): the weights are constant during a
+// step, so their copies overlap the tail of the kernel before.
+// ---------------------------------------------------------------------------
+constexpr int kPgWarps = 4;
+constexpr int kPgTiles = 16;
+constexpr int kPgCtasPerSm = 3;
+
+template <int DT>
+struct PgGeom {
+  static constexpr uint32_t TB = DT == SNL_Q8_0 ? 512 : 256;
+  static constexpr int kStages = DT == SNL_Q8_0 ? 2 : 3;
+  static constexpr uint32_t kStageW = kPgTiles * TB;
+  static constexpr uint32_t kStageS = kPgTiles / 4 * 256;
+  static constexpr uint32_t kStage = kStageW + kStageS;
+  static constexpr uint32_t kWarpBytes = kStages * kStage;
+  static constexpr uint32_t kSmem = kPgWarps * kWarpBytes + kPgWarps * kStages * 8;
+};
+
+// The epilogue of one finished row group, run by one warp: val(tt, r) is the dot of
+// token tt, row 16*grp + r (lanes 16*j + r handle token 2*pass + j). Router partials
+// go to rpart[(tt * groups + grp) * 9 + o].
+template <int M, class V>
+__device__ __forceinline__ void group_finish(const GemvArgs& a, uint32_t grp, uint32_t groups, int lane, V&& val) {
+#pragma unroll
+  for (int pass = 0; pass < (M + 1) / 2; pass++) {
+    const int tt = pass * 2 + lane / 16, r = lane % 16;
+    const uint32_t row = grp * 16 + r;
+    const bool live = tt < M && row < a.n;
+    float2 nx = make_float2(0.f, 0.f);
+    if (live) nx = gemv_epilogue(a, tt, row, val(tt, r) * kXPlaneScale);
+    if (a.rnext) {
+      float rs[9];
+      const uint32_t d = 2 * a.h;
+#pragma unroll
+      for (int o = 0; o < 8; o++)
+        rs[o] = live ? fmaf(__ldg(a.rnext + (uint64_t)o * d + row), nx.x, __ldg(a.rnext + (uint64_t)o * d + a.h + row) * nx.y)
+                     : 0.f;
+      rs[8] = live ? fmaf(nx.x, nx.x, nx.y * nx.y) : 0.f;
+#pragma unroll
+      for (int o = 0; o < 9; o++) {
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) rs[o] += __shfl_xor_sync(0xffffffffu, rs[o], off);
+      }
+      if (r == 0 && tt < M) {
+#pragma unroll
+        for (int o = 0; o < 9; o++) a.rpart[((uint64_t)tt * groups + grp) * 9 + o] = rs[o];
+      }
+    }
+  }
+}
+
+template <int DT, int M>
+__global__ void __launch_bounds__(kPgWarps * 32) gemv_pg_kernel(GemvArgs a, const uint8_t* __restrict__ tiles,
+                                                                const float* __restrict__ ts, uint32_t groups, int* err) {
+  using G = PgGeom<DT>;
+  constexpr int S = G::kStages;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ float red[2][kPgWarps][M][16];
+  pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const uint32_t nb = a.k / 32, nb4 = (nb + 3) / 4;
+  const uint32_t spg = (nb + kPgTiles - 1) / kPgTiles;
+  const uint32_t per = (spg + kPgWarps - 1) / kPgWarps;
+  const uint32_t st0 = min(spg, warp * per), nst = min(spg, st0 + per) - st0;
+  const uint32_t g0 = (uint32_t)((uint64_t)blockIdx.x * groups / gridDim.x);
+  const uint32_t g1 = (uint32_t)((uint64_t)(blockIdx.x + 1) * groups / gridDim.x);
+  const uint32_t njobs = (g1 - g0) * nst;
+  uint8_t* ring = smem + warp * G::kWarpBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPgWarps * G::kWarpBytes) + warp * S;
+
+  if (lane == 0)
+    for (int s = 0; s < S; s++) mbar_init(&bars[s], 1);
+  fence_mbar_init();
+  __syncwarp();
+  const uint64_t pol = l2_policy_evict_first();
+  auto issue = [&](uint32_t j) {
+    if (lane != 0) return;
+    const uint32_t grp = g0 + j / nst, sg = st0 + j % nst;
+    const uint32_t nt = min((uint32_t)kPgTiles, nb - sg * kPgTiles);
+    const uint32_t wbytes = nt * G::TB, sbytes = (nt + 3) / 4 * 256;
+    uint8_t* st = ring + (j % S) * G::kStage;
+    mbar_arrive_expect_tx(&bars[j % S], wbytes + sbytes);
+    bulk_g2s(st, tiles + ((uint64_t)grp * nb + sg * kPgTiles) * G::TB, wbytes, &bars[j % S], pol);
+    bulk_g2s(st + G::kStageW, ts + ((uint64_t)grp * nb4 + sg * (kPgTiles / 4)) * 64, sbytes, &bars[j % S], pol);
+  };
+  for (uint32_t j = 0; j < min((uint32_t)S, njobs); j++) issue(j);
+  pdl_wait();
+
+  const bool has_x = g < 2 * M;
+  const __half* xbase = a.xplanes + (uint64_t)(has_x ? g : 0) * a.plane_stride + 8 * t;
+  bool ok = true;
+  uint32_t j_fail = 0, j = 0;
+  for (uint32_t gi = 0; gi < g1 - g0; gi++) {
+    float accA = 0.f, accB = 0.f;
+    for (uint32_t si = 0; si < nst; si++, j++) {
+      if (!ok) continue;
+      const uint32_t sg = st0 + si;
+      const uint32_t nt = min((uint32_t)kPgTiles, nb - sg * kPgTiles);
+      uint4 xv[kPgTiles];
+#pragma unroll
+      for (int u = 0; u < kPgTiles; u++) {
+        const uint32_t uu = min((uint32_t)u, nt - 1);
+        xv[u] = has_x ? __ldg(reinterpret_cast<const uint4*>(xbase + ((uint64_t)sg * kPgTiles + uu) * 32))
+                      : make_uint4(0, 0, 0, 0);
+      }
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&bars[j % S], (j / S) & 1))) {
+        ok = false;
+        j_fail = j;
+        continue;
+      }
+      const uint8_t* st = ring + (j % S) * G::kStage;
+      const float* sc = reinterpret_cast<const float*>(st + G::kStageW);
+#pragma unroll
+      for (int u = 0; u < kPgTiles; u++) {
+        if ((uint32_t)u >= nt) break;
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        if constexpr (DT == SNL_Q8_0) {
+          const uint4 w = *reinterpret_cast<const uint4*>(st + u * G::TB + lane * 16);
+          const uint32_t A0[4] = {u8pair(w.x, 0x4140), u8pair(w.z, 0x4140), u8pair(w.x, 0x4342), u8pair(w.z, 0x4342)};
+          const uint32_t A1[4] = {u8pair(w.y, 0x4140), u8pair(w.w, 0x4140), u8pair(w.y, 0x4342), u8pair(w.w, 0x4342)};
+          mma16816(d, A0, xv[u].x, xv[u].y);
+          mma16816(d, A1, xv[u].z, xv[u].w);
+        } else {
+          const uint2 w = *reinterpret_cast<const uint2*>(st + u * G::TB + lane * 8);
+          const uint32_t A0[4] = {u4pair(w.x, 0), u4pair(w.y, 0), u4pair(w.x, 1), u4pair(w.y, 1)};
+          const uint32_t A1[4] = {u4pair(w.x, 2), u4pair(w.y, 2), u4pair(w.x, 3), u4pair(w.y, 3)};
+          mma16816(d, A0, xv[u].x, xv[u].y);
+          mma16816(d, A1, xv[u].z, xv[u].w);
+        }
+        const float scA = sc[(u / 4) * 64 + g * 4 + (u % 4)];
+        const float scB = sc[(u / 4) * 64 + (g + 8) * 4 + (u % 4)];
+        accA = fmaf(scA, d[0] + d[1], accA);
+        accB = fmaf(scB, d[2] + d[3], accB);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (j + S < njobs) issue(j + S);
+    }
+    // All warps meet once per group; warp 0 sums the partials in warp order.
+    const int buf = gi & 1;
+    if (t < M) {
+      red[buf][warp][t][g] = accA;
+      red[buf][warp][t][g + 8] = accB;
+    }
+    __syncthreads();
+    if (warp == 0)
+      group_finish<M>(a, g0 + gi, groups, lane, [&](int tt, int r) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kPgWarps; w++) v += red[buf][w][tt][r];
+        return v;
+      });
+  }
+  if (!ok) {
+    // A bounded wait gave up: flag it and let the copies still in flight land before
+    // the CTA exits.
+    if (lane == 0) report_timeout(err);
+    const uint32_t last = min(njobs, j_fail + S);
+    for (uint32_t k2 = j_fail; k2 < last; k2++) (void)mbar_wait_bounded(&bars[k2 % S], (k2 / S) & 1);
+  }
+}
+
+template <int DT, int M>
+int launch_pg_t(const GemvArgs& a, const void* tiles, const float* ts, int* err, cudaStream_t s) {
+  using G = PgGeom<DT>;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto kern = gemv_pg_kernel<DT, M>;
+  if (dev >= 0 && dev < 64 && !attr[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
+    if (e != cudaSuccess) return cuda_fail(e, "gemv_pg: smem attribute");
+    attr[dev] = true;
+  }
+  const uint32_t groups = (a.n + 15) / 16;
+  const uint32_t grid = std::min<uint32_t>(groups, (uint32_t)sm_count() * kPgCtasPerSm);
+  SNL_PDL_LAUNCH("gemv_pg", kern, dim3(grid), dim3(kPgWarps * 32), (size_t)G::kSmem, s, a,
+                 static_cast<const uint8_t*>(tiles), ts, groups, err);
+  return SNL_OK;
+}
+
 template <int DT, int M>
 int launch_tile_bulk_t(const GemvArgs& a, const void* tiles, const float* ts, int* err, cudaStream_t s) {
   using G = BulkGeom<DT>;
@@ -647,6 +839,27 @@ int launch_gemv_tile(int dtype, const GemvArgs& a, uint32_t m, const void* tiles
   if (a.plane_stride % 8 || ((uintptr_t)a.xplanes % 16)) return fail(SNL_E_INVALID, "gemv_tile: planes alignment");
   if (a.n == 0) return SNL_OK;
   static const bool direct = getenv("SNL_GEMV_TILE_DIRECT") != nullptr;
+  static const bool bulk = getenv("SNL_GEMV_BULK") != nullptr;
+  if (!direct && !bulk) {
+    int* err = nullptr;
+    if (int rc = device_error_word(&err)) return rc;
+    if (dtype == SNL_Q8_0) {
+      switch (m) {
+        case 1: return launch_pg_t<SNL_Q8_0, 1>(a, tiles, ts, err, s);
+        case 2: return launch_pg_t<SNL_Q8_0, 2>(a, tiles, ts, err, s);
+        case 3: return launch_pg_t<SNL_Q8_0, 3>(a, tiles, ts, err, s);
+        case 4: return launch_pg_t<SNL_Q8_0, 4>(a, tiles, ts, err, s);
+      }
+    } else if (dtype == SNL_Q4_0) {
+      switch (m) {
+        case 1: return launch_pg_t<SNL_Q4_0, 1>(a, tiles, ts, err, s);
+        case 2: return launch_pg_t<SNL_Q4_0, 2>(a, tiles, ts, err, s);
+        case 3: return launch_pg_t<SNL_Q4_0, 3>(a, tiles, ts, err, s);
+        case 4: return launch_pg_t<SNL_Q4_0, 4>(a, tiles, ts, err, s);
+      }
+    }
+    return fail(SNL_E_INVALID, "gemv_tile: dtype / rows");
+  }
   if (!direct) {
     int* err = nullptr;
     if (int rc = device_error_word(&err)) return rc;

@@ -5,6 +5,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "ptx.cuh"
 #include "synth.h"
 
 namespace snl {
@@ -15,6 +16,8 @@ namespace {
 __global__ void __launch_bounds__(256) branch_norm_loop_kernel(StepRef sr, snl_layer_p p, const float* __restrict__ x,
                                                                const float* __restrict__ coef, const float* __restrict__ w,
                                                                float* __restrict__ out, XOut xo) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float sh[32];
   const snl_step_u st = load_step(sr);
   const uint32_t g = blockIdx.x;
@@ -62,6 +65,8 @@ template <int VPT>
 __global__ void __launch_bounds__(256) branch_norm_kernel(StepRef sr, snl_layer_p p, const float* __restrict__ x,
                                                           const float* __restrict__ coef, const float* __restrict__ w,
                                                           float* __restrict__ out, XOut xo, NormRouter nr) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float sh[32];
   __shared__ float pre_sh[2];
   const snl_step_u st = load_step(sr);
@@ -251,6 +256,8 @@ __global__ void mhc_coef_kernel(snl_layer_p p, uint32_t m_rows, const float* __r
 // merge (layers.wgsl:268-302).
 __global__ void merge_kernel(snl_layer_p p, uint32_t m_rows, float* __restrict__ x, const float* __restrict__ coef,
                              const float* __restrict__ br) {
+  pdl_trigger();
+  pdl_wait();
   const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (uint64_t)m_rows * p.h) return;
   const uint64_t m = idx / p.h, i = idx % p.h;
@@ -278,6 +285,8 @@ __global__ void merge_kernel(snl_layer_p p, uint32_t m_rows, float* __restrict__
 // swiglu (layers.wgsl:304-315).
 __global__ void swiglu_kernel(snl_layer_p p, uint32_t m_rows, const float* __restrict__ gu, float* __restrict__ act,
                               XOut xo) {
+  pdl_trigger();
+  pdl_wait();
   const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (uint64_t)m_rows * p.inter) return;
   const uint64_t m = idx / p.inter, i = idx % p.inter;
@@ -300,6 +309,8 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t i) {
 constexpr int kArgBlocks = 128;
 __global__ void __launch_bounds__(512) argmax_pass1(const float* __restrict__ v, uint32_t n,
                                                     unsigned long long* __restrict__ part) {
+  pdl_trigger();
+  pdl_wait();
   const uint32_t row = blockIdx.y;
   const float* r = v + (uint64_t)row * n;
   unsigned long long best = 0;
@@ -321,6 +332,8 @@ __global__ void __launch_bounds__(512) argmax_pass1(const float* __restrict__ v,
   }
 }
 __global__ void argmax_pass2(const unsigned long long* __restrict__ part, uint32_t nparts, uint32_t* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const uint32_t row = blockIdx.x;
   unsigned long long best = 0;
   for (uint32_t i = threadIdx.x; i < nparts; i += 32) {
@@ -340,6 +353,8 @@ __global__ void argmax_pass2(const unsigned long long* __restrict__ part, uint32
 __global__ void embed_kernel(const uint32_t* __restrict__ toks, uint32_t h, uint32_t vocab,
                              const int8_t* __restrict__ q, const float* __restrict__ s, float* __restrict__ x,
                              int* __restrict__ err) {
+  pdl_trigger();
+  pdl_wait();
   const uint32_t m = blockIdx.x;
   const uint32_t t = toks[m];
   const bool ok = t < vocab;
@@ -390,11 +405,10 @@ int launch_branch_norm_router(StepRef st, const snl_layer_p& p, const float* x, 
   nr.nparts = nparts;
   nr.router = router;
   nr.coef_out = coef;
-  if (vpt <= 1) branch_norm_kernel<1><<<n_groups, 256, 0, s>>>(st, p, x, coef, w, out, xo, nr);
-  else if (vpt <= 2) branch_norm_kernel<2><<<n_groups, 256, 0, s>>>(st, p, x, coef, w, out, xo, nr);
-  else if (vpt <= 4) branch_norm_kernel<4><<<n_groups, 256, 0, s>>>(st, p, x, coef, w, out, xo, nr);
-  else branch_norm_kernel<8><<<n_groups, 256, 0, s>>>(st, p, x, coef, w, out, xo, nr);
-  SNL_LAUNCH_CHECK("branch_norm_router");
+  if (vpt <= 1) SNL_PDL_LAUNCH("branch_norm_kernel", branch_norm_kernel<1>, dim3(n_groups), dim3(256), (size_t)(0), s, st, p, x, coef, w, out, xo, nr);
+  else if (vpt <= 2) SNL_PDL_LAUNCH("branch_norm_kernel", branch_norm_kernel<2>, dim3(n_groups), dim3(256), (size_t)(0), s, st, p, x, coef, w, out, xo, nr);
+  else if (vpt <= 4) SNL_PDL_LAUNCH("branch_norm_kernel", branch_norm_kernel<4>, dim3(n_groups), dim3(256), (size_t)(0), s, st, p, x, coef, w, out, xo, nr);
+  else SNL_PDL_LAUNCH("branch_norm_kernel", branch_norm_kernel<8>, dim3(n_groups), dim3(256), (size_t)(0), s, st, p, x, coef, w, out, xo, nr);
   return SNL_OK;
 }
 
@@ -405,12 +419,11 @@ int launch_branch_norm(StepRef st, const snl_layer_p& p, const float* x, const f
   const bool vec = p.h % 4 == 0 && stride % 4 == 0 && ((uintptr_t)x % 16) == 0 && ((uintptr_t)w % 16) == 0 &&
                    ((uintptr_t)out % 16) == 0;
   const uint32_t vpt = (p.h / 4 + 255) / 256;
-  if (vec && vpt <= 1) branch_norm_kernel<1><<<n_groups, 256, 0, s>>>(st, p, x, coef, w, out, xo, NormRouter());
-  else if (vec && vpt <= 2) branch_norm_kernel<2><<<n_groups, 256, 0, s>>>(st, p, x, coef, w, out, xo, NormRouter());
-  else if (vec && vpt <= 4) branch_norm_kernel<4><<<n_groups, 256, 0, s>>>(st, p, x, coef, w, out, xo, NormRouter());
-  else if (vec && vpt <= 8) branch_norm_kernel<8><<<n_groups, 256, 0, s>>>(st, p, x, coef, w, out, xo, NormRouter());
-  else branch_norm_loop_kernel<<<n_groups, 256, 0, s>>>(st, p, x, coef, w, out, xo);
-  SNL_LAUNCH_CHECK("branch_norm");
+  if (vec && vpt <= 1) SNL_PDL_LAUNCH("branch_norm_kernel", branch_norm_kernel<1>, dim3(n_groups), dim3(256), (size_t)(0), s, st, p, x, coef, w, out, xo, NormRouter());
+  else if (vec && vpt <= 2) SNL_PDL_LAUNCH("branch_norm_kernel", branch_norm_kernel<2>, dim3(n_groups), dim3(256), (size_t)(0), s, st, p, x, coef, w, out, xo, NormRouter());
+  else if (vec && vpt <= 4) SNL_PDL_LAUNCH("branch_norm_kernel", branch_norm_kernel<4>, dim3(n_groups), dim3(256), (size_t)(0), s, st, p, x, coef, w, out, xo, NormRouter());
+  else if (vec && vpt <= 8) SNL_PDL_LAUNCH("branch_norm_kernel", branch_norm_kernel<8>, dim3(n_groups), dim3(256), (size_t)(0), s, st, p, x, coef, w, out, xo, NormRouter());
+  else SNL_PDL_LAUNCH("branch_norm_loop_kernel", branch_norm_loop_kernel, dim3(n_groups), dim3(256), (size_t)(0), s, st, p, x, coef, w, out, xo);
   return SNL_OK;
 }
 int launch_mhc_dots(StepRef st, const snl_layer_p& p, const float* x, const float* w, float* raw, uint32_t m,
@@ -444,16 +457,14 @@ int launch_merge(StepRef st, const snl_layer_p& p, float* x, const float* coef, 
   (void)st;
   const uint64_t n = (uint64_t)m * p.h;
   if (n == 0) return SNL_OK;
-  merge_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(p, m, x, coef, br);
-  SNL_LAUNCH_CHECK("merge");
+  SNL_PDL_LAUNCH("merge_kernel", merge_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), (size_t)(0), s, p, m, x, coef, br);
   return SNL_OK;
 }
 int launch_swiglu(StepRef st, const snl_layer_p& p, const float* gu, float* act, uint32_t m, cudaStream_t s, XOut xo) {
   (void)st;
   const uint64_t n = (uint64_t)m * p.inter;
   if (n == 0) return SNL_OK;
-  swiglu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(p, m, gu, act, xo);
-  SNL_LAUNCH_CHECK("swiglu");
+  SNL_PDL_LAUNCH("swiglu_kernel", swiglu_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), (size_t)(0), s, p, m, gu, act, xo);
   return SNL_OK;
 }
 
@@ -479,10 +490,8 @@ static unsigned long long* argmax_scratch(uint32_t rows) {
 int launch_argmax_with(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_idx, unsigned long long* part,
                        cudaStream_t s) {
   if (rows == 0) return SNL_OK;
-  argmax_pass1<<<dim3(kArgBlocks, rows), 512, 0, s>>>(logits, n, part);
-  SNL_LAUNCH_CHECK("argmax_pass1");
-  argmax_pass2<<<rows, 32, 0, s>>>(part, kArgBlocks, out_idx);
-  SNL_LAUNCH_CHECK("argmax_pass2");
+  SNL_PDL_LAUNCH("argmax_pass1", argmax_pass1, dim3(dim3(kArgBlocks, rows)), dim3(512), (size_t)(0), s, logits, n, part);
+  SNL_PDL_LAUNCH("argmax_pass2", argmax_pass2, dim3(rows), dim3(32), (size_t)(0), s, part, kArgBlocks, out_idx);
   return SNL_OK;
 }
 
@@ -495,8 +504,7 @@ int launch_argmax(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_
 int launch_embed(const uint32_t* tokens, uint32_t m, const int8_t* q, const float* s_, uint32_t h, uint32_t vocab,
                  float* x, int* err_flag, cudaStream_t s) {
   if (m == 0) return SNL_OK;
-  embed_kernel<<<m, 256, 0, s>>>(tokens, h, vocab, q, s_, x, err_flag);
-  SNL_LAUNCH_CHECK("embed");
+  SNL_PDL_LAUNCH("embed_kernel", embed_kernel, dim3(m), dim3(256), (size_t)(0), s, tokens, h, vocab, q, s_, x, err_flag);
   return SNL_OK;
 }
 

@@ -6,6 +6,7 @@
 // [128 (key dim i), 128 (value dim j)] f32 matrix; column j evolves independently of
 // the other columns given the head's q, k, beta and decay.
 #include "common.cuh"
+#include "ptx.cuh"
 
 namespace snl {
 namespace {
@@ -113,6 +114,8 @@ __global__ void __launch_bounds__(128) conv_delta_kernel(StepRef sr, snl_lin_p p
                                                          const float* __restrict__ lw, float* __restrict__ out,
                                                          float* __restrict__ conv_ckpt, float* __restrict__ state_ckpt,
                                                          XOut xo) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float qs[DK], ks[DK];
   __shared__ float red[32];
   const snl_step_u st = load_step(sr);
@@ -230,8 +233,7 @@ int launch_delta(StepRef st, const snl_lin_p& p, const float* proj, const float*
 int launch_conv_delta(StepRef st, const snl_lin_p& p, const float* proj, float* conv_state, float* state,
                       const float* lw, float* out, float* conv_ckpt, float* state_ckpt, cudaStream_t s, XOut xo) {
   if (int rc = check_lin(p)) return rc;
-  conv_delta_kernel<<<p.n_v, DV, 0, s>>>(st, p, proj, conv_state, state, lw, out, conv_ckpt, state_ckpt, xo);
-  SNL_LAUNCH_CHECK("conv_delta");
+  SNL_PDL_LAUNCH("conv_delta_kernel", conv_delta_kernel, dim3(p.n_v), dim3(DV), (size_t)(0), s, st, p, proj, conv_state, state, lw, out, conv_ckpt, state_ckpt, xo);
   return SNL_OK;
 }
 

@@ -41,6 +41,23 @@ int device_error_word(int** out) {
   return SNL_OK;
 }
 
+bool pdl_on() {
+  static const bool on = getenv("SNL_NO_PDL") == nullptr;
+  return on;
+}
+
+int sm_count() {
+  static int sms[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
+  if (!sms[dev]) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 1;
+    sms[dev] = v;
+  }
+  return sms[dev];
+}
+
 namespace {
 
 constexpr int kRowsPerWarp = 4;

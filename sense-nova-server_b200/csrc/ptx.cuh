@@ -63,4 +63,13 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 // Bit 0 of a device error word: a bounded wait gave up (read back by the host).
 __device__ __forceinline__ void report_timeout(int* err) { atomicOr(err, 1); }
 
+// Programmatic dependent launch. A kernel launched with programmatic stream
+// serialization may start while its predecessor in the stream still runs:
+// pdl_wait() blocks until the predecessor grid has completed and its memory is
+// visible (a no-op for a kernel launched without the attribute); pdl_trigger() lets
+// the successor launch before this grid ends. Work before pdl_wait() may read only
+// data no earlier kernel of the step writes (the weights).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 }  // namespace snl
