@@ -58,6 +58,7 @@ struct QT {
   // the same matrix in the tile layout of the decode GEMV (gemv_mma.cu)
   void* tiles = nullptr;
   float* tscales = nullptr;
+  uint32_t pair_half = 0;  // tiles pair gate row i with up row i (a layer's gate_up)
 };
 struct FT {
   float* p = nullptr;
@@ -122,6 +123,7 @@ struct snl_engine {
   // these planes ([8][pstride] halves), written by the kernel that produces each input.
   bool use_tc = true;
   __half* xpl = nullptr;
+  __half* xpl_act = nullptr;  // planes of the SwiGLU output, written by the gate_up GEMV
   uint32_t pstride = 0;
   // Router partial sums written by the residual-merging GEMV for the next mHC norm.
   float* rpart = nullptr;
@@ -283,11 +285,13 @@ int push_norm(snl_engine* e, StepRef st, uint32_t m, const float* router, const 
 // merges into the residual x like `merge` (engine.rs:471-480) and can expand stream 0
 // into stream 1 (the merge mode 3 that opens an mHC range).
 int matx(snl_engine* e, const QT& w, uint32_t rows, int mode, float* y, size_t y_stride, uint32_t merge_mode = 0,
-         int expand = 0, const float* rnext = nullptr) {
+         int expand = 0, const float* rnext = nullptr, const __half* planes = nullptr) {
   GemvArgs a{};
   a.n = (uint32_t)w.rows;
   a.k = (uint32_t)w.cols;
-  a.xplanes = e->xpl;
+  a.xplanes = planes ? planes : e->xpl;
+  a.act_planes = e->xpl_act;
+  a.act_stride = e->pstride;
   a.plane_stride = e->pstride;
   a.wq = static_cast<const uint8_t*>(w.q);
   a.mode = mode;
@@ -327,8 +331,8 @@ int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
   };
   // out-projection of `src` (K = src_dim) merged into the residual
   auto proj_out = [&](const QT& w, const float* src, size_t src_dim, uint32_t merge_mode, bool expand,
-                      const float* rnext) -> int {
-    if (tc) return matx(e, w, m, 1, nullptr, 0, merge_mode, expand ? 1 : 0, rnext);
+                      const float* rnext, const __half* planes = nullptr) -> int {
+    if (tc) return matx(e, w, m, 1, nullptr, 0, merge_mode, expand ? 1 : 0, rnext, planes);
     SNL_TRY(mat(e, st, w, src, src_dim, e->branch, h, m));
     SNL_TRY(timed(e, "Merge", 5 * hb, [&] {
       return launch_merge(st, layer_p(e, merge_mode, false), e->x, e->coef, e->branch, m, e->stream);
@@ -381,15 +385,23 @@ int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
       lin_slot++;
     }
     SNL_TRY(push_norm(e, st, m, mhc ? find_f(e, L + "mhc_ffn") : nullptr, find_f(e, L + "post_ln"), xo));
-    SNL_TRY(proj_in(*find_q(e, L + "gate_up"), e->proj, 2 * (size_t)c.intermediate));
-    SNL_TRY(timed(e, "Swiglu", 12.0 * m * c.intermediate,
-                  [&] { return launch_swiglu(st, layer_p(e, 0, false), e->proj, e->act, m, e->stream, xo); }));
+    const QT& gu = *find_q(e, L + "gate_up");
+    const bool fused_swiglu = tc && gu.tiles && gu.pair_half;
+    if (fused_swiglu) {
+      // The gate_up GEMV finishes SwiGLU in its epilogue and writes the planes of act.
+      SNL_TRY(matx(e, gu, m, 2, nullptr, c.intermediate));
+    } else {
+      SNL_TRY(proj_in(gu, e->proj, 2 * (size_t)c.intermediate));
+      SNL_TRY(timed(e, "Swiglu", 12.0 * m * c.intermediate,
+                    [&] { return launch_swiglu(st, layer_p(e, 0, false), e->proj, e->act, m, e->stream, xo); }));
+    }
     const uint32_t mode = !mhc ? 0 : ((int32_t)(li + 1) == c.mhc_end ? 2 : 1);
     const bool expand_next = vi + 1 < e->plan.size() && snl_synth::is_mhc(c, e->plan[vi + 1]) &&
                              (int32_t)e->plan[vi + 1] == c.mhc_start;
     const bool next_mhc = vi + 1 < e->plan.size() && snl_synth::is_mhc(c, e->plan[vi + 1]);
     const float* rnext = next_mhc ? find_f(e, "l" + std::to_string(e->plan[vi + 1]) + ".mhc_attn") : nullptr;
-    SNL_TRY(proj_out(*find_q(e, L + "down"), e->act, c.intermediate, mode, expand_next, rnext));
+    SNL_TRY(proj_out(*find_q(e, L + "down"), e->act, c.intermediate, mode, expand_next, rnext,
+                     fused_swiglu ? e->xpl_act : nullptr));
     expanded = expand_next;
   }
   return SNL_OK;
@@ -738,8 +750,13 @@ extern "C" int snl_engine_finalize(snl_engine* e) {
       float* ts = nullptr;
       SNL_TRY(dalloc(e, &tiles, tb));
       SNL_TRY(dalloc(e, &ts, sf));
+      // A layer's [gate; up] matrix pairs gate row i with up row i for the SwiGLU epilogue.
+      const std::string& nm = kv.first;
+      const bool pair = nm.size() > 8 && nm[0] == 'l' && nm.compare(nm.size() - 8, 8, ".gate_up") == 0 &&
+                        t.rows % 16 == 0;
+      t.pair_half = pair ? (uint32_t)(t.rows / 2) : 0;
       SNL_TRY(launch_repack_tiles(t.dtype, (uint32_t)t.rows, (uint32_t)t.cols, t.q, (const float*)t.s, tiles, ts,
-                                  e->stream));
+                                  e->stream, t.pair_half));
       t.tiles = tiles;
       t.tscales = ts;
     }
@@ -767,6 +784,7 @@ extern "C" int snl_engine_finalize(snl_engine* e) {
   SNL_TRY(dalloc(e, &e->amax_part, LOGIT_ROWS * 128));
   e->pstride = (uint32_t)((std::max({h, I, snl_synth::q_dim(c), snl_synth::lin_value_dim(c)}) + 7) / 8 * 8);
   SNL_TRY(dalloc(e, &e->xpl, (size_t)8 * e->pstride));
+  SNL_TRY(dalloc(e, &e->xpl_act, (size_t)8 * e->pstride));
   SNL_TRY(dalloc(e, &e->rpart, (size_t)4 * ((h + 15) / 16) * 9));
   if (getenv("SNL_NO_TC")) e->use_tc = false;
   SNL_TRY(dalloc(e, &e->step_d, 1));

@@ -281,15 +281,23 @@ namespace {
 constexpr int kTileWarps = 4;
 constexpr int kTileUnroll = 8;
 
+// pair_half != 0 (n = 2 * pair_half, pair_half % 8 == 0): group grp holds rows
+// 8*grp .. 8*grp+7 in its first 8 rows and pair_half + 8*grp .. +7 in the last 8, so a
+// [gate; up] matrix puts each gate row in the group of its up row (the SwiGLU epilogue).
+__device__ __forceinline__ uint32_t tile_row(uint32_t grp, uint32_t r, uint32_t pair_half) {
+  return pair_half ? (r < 8 ? 8 * grp + r : pair_half + 8 * grp + (r - 8)) : grp * 16 + r;
+}
+
 __global__ void repack_tiles_kernel(int dtype, uint32_t n, uint32_t k, const uint8_t* __restrict__ q,
-                                    const float* __restrict__ s, uint8_t* __restrict__ tiles, float* __restrict__ ts) {
+                                    const float* __restrict__ s, uint8_t* __restrict__ tiles, float* __restrict__ ts,
+                                    uint32_t pair_half) {
   // one thread per (group, block, lane)
   const uint32_t nb = k / 32, groups = (n + 15) / 16;
   const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (uint64_t)groups * nb * 32) return;
   const uint32_t lane = (uint32_t)(idx % 32), b = (uint32_t)((idx / 32) % nb), grp = (uint32_t)(idx / 32 / nb);
   const uint32_t g = lane >> 2, t = lane & 3;
-  const uint32_t rA = grp * 16 + g, rB = rA + 8;
+  const uint32_t rA = tile_row(grp, g, pair_half), rB = tile_row(grp, g + 8, pair_half);
   const uint64_t tile = (uint64_t)grp * nb + b;
   if (dtype == SNL_Q8_0) {
     uint8_t* dst = tiles + tile * 512 + lane * 16;
@@ -316,7 +324,7 @@ __global__ void repack_tiles_kernel(int dtype, uint32_t n, uint32_t k, const uin
   }
   // scales: lanes 0..15 of each (group, block) write row `lane`'s scale.
   if (lane < 16) {
-    const uint32_t row = grp * 16 + lane;
+    const uint32_t row = tile_row(grp, lane, pair_half);
     const uint32_t nb4 = (nb + 3) / 4;
     ts[(((uint64_t)grp * nb4 + b / 4) * 16 + lane) * 4 + b % 4] = row < n ? s[(uint64_t)row * nb + b] : 0.f;
   }
@@ -629,6 +637,23 @@ struct PgGeom {
 // go to rpart[(tt * groups + grp) * 9 + o].
 template <int M, class V>
 __device__ __forceinline__ void group_finish(const GemvArgs& a, uint32_t grp, uint32_t groups, int lane, V&& val) {
+  if (a.mode == 2) {
+    // SwiGLU (layers.wgsl `swiglu`): rows 0-7 of the group are gate rows 8*grp + r,
+    // rows 8-15 the matching up rows (tiles repacked with pair_half).
+#pragma unroll
+    for (int pass = 0; pass < (M + 1) / 2; pass++) {
+      const int tt = pass * 2 + lane / 16, r = lane % 16;
+      const float v = tt < M ? val(tt, r) * kXPlaneScale : 0.f;
+      const float up = __shfl_down_sync(0xffffffffu, v, 8);
+      if (tt < M && r < 8) {
+        const uint32_t i = grp * 8 + r;
+        const float act = v / (1.0f + __expf(-v)) * up;
+        if (a.y) a.y[(uint64_t)tt * a.y_stride + i] = act;
+        xplane_store(a.act_planes, a.act_stride, tt, i, act);
+      }
+    }
+    return;
+  }
 #pragma unroll
   for (int pass = 0; pass < (M + 1) / 2; pass++) {
     const int tt = pass * 2 + lane / 16, r = lane % 16;
@@ -821,15 +846,16 @@ void tile_sizes(int dtype, uint32_t n, uint32_t k, size_t* tile_bytes, size_t* s
 }
 
 int launch_repack_tiles(int dtype, uint32_t n, uint32_t k, const void* q, const float* s, void* tiles, float* ts,
-                        cudaStream_t st) {
+                        cudaStream_t st, uint32_t pair_half) {
   if (k % 32 || n == 0) return fail(SNL_E_INVALID, "repack: k must be a multiple of 32");
+  if (pair_half && (n != 2 * pair_half || pair_half % 8)) return fail(SNL_E_INVALID, "repack: bad row pairing");
   size_t tb, sf;
   tile_sizes(dtype, n, k, &tb, &sf);
   cudaError_t e = cudaMemsetAsync(ts, 0, sf * sizeof(float), st);  // scales of blocks past k in the last four
   if (e != cudaSuccess) return cuda_fail(e, "repack: memset");
   const uint64_t threads = (uint64_t)((n + 15) / 16) * (k / 32) * 32;
   repack_tiles_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(dtype, n, k, static_cast<const uint8_t*>(q), s,
-                                                                         static_cast<uint8_t*>(tiles), ts);
+                                                                         static_cast<uint8_t*>(tiles), ts, pair_half);
   SNL_LAUNCH_CHECK("repack_tiles");
   return SNL_OK;
 }
@@ -840,7 +866,8 @@ int launch_gemv_tile(int dtype, const GemvArgs& a, uint32_t m, const void* tiles
   if (a.n == 0) return SNL_OK;
   static const bool direct = getenv("SNL_GEMV_TILE_DIRECT") != nullptr;
   static const bool bulk = getenv("SNL_GEMV_BULK") != nullptr;
-  if (!direct && !bulk) {
+  if (a.mode == 2 && (!a.act_planes || a.n % 16)) return fail(SNL_E_INVALID, "gemv_tile: swiglu epilogue arguments");
+  if ((!direct && !bulk) || a.mode == 2) {
     int* err = nullptr;
     if (int rc = device_error_word(&err)) return rc;
     if (dtype == SNL_Q8_0) {

@@ -22,6 +22,7 @@ __device__ __forceinline__ void xplane_store(__half* planes, uint32_t plane_stri
 //   mode 0: y[y_off + t*y_stride + n_off + n] = v
 //   mode 1: residual merge into x [t, 2H] (layers.wgsl:268-302 `merge` mode `merge_mode`),
 //           then optionally copy stream 0 into stream 1 (`expand`, merge mode 3).
+//   mode 2: SwiGLU of gate/up row pairs (tile GEMV only, see group_finish).
 struct GemvArgs {
   uint32_t n, k;
   const __half* xplanes;
@@ -41,6 +42,10 @@ struct GemvArgs {
   // rpart[(t * gridDim.x + blockIdx.x) * 9 + o] (8 dots, then the sum of squares).
   const float* rnext;
   float* rpart;
+  // mode 2 (SwiGLU of a pair-repacked [gate; up] matrix): the x planes of act
+  // (act_stride halves per plane) and, if y is set, act itself at y[t * y_stride + i].
+  __half* act_planes;
+  uint32_t act_stride;
 };
 
 // Returns the merged (x0, x1) of element n (mode 1), for the router partials.
@@ -95,7 +100,7 @@ int launch_gemv_mma(int dtype, const GemvArgs& a, uint32_t m, const void* ws, in
 // Tile layout (see gemv_mma.cu): sizes, device repack from the reference layout, GEMV.
 void tile_sizes(int dtype, uint32_t n, uint32_t k, size_t* tile_bytes, size_t* scale_floats);
 int launch_repack_tiles(int dtype, uint32_t n, uint32_t k, const void* q, const float* s, void* tiles, float* ts,
-                        cudaStream_t st);
+                        cudaStream_t st, uint32_t pair_half = 0);
 int launch_gemv_tile(int dtype, const GemvArgs& a, uint32_t m, const void* tiles, const float* ts, cudaStream_t s);
 int launch_xpack(const float* x, uint32_t m, uint32_t k, uint32_t x_stride, __half* planes, uint32_t plane_stride,
                  cudaStream_t s);

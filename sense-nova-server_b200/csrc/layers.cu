@@ -46,8 +46,8 @@ __global__ void __launch_bounds__(256) branch_norm_loop_kernel(StepRef sr, snl_l
   }
 }
 
-__device__ __forceinline__ void mhc_coef(const float raw[9], const float* __restrict__ w, uint32_t d,
-                                         uint32_t iterations, float* __restrict__ cb);
+__device__ __forceinline__ void mhc_coef_b(const float raw[9], const float bias[8], uint32_t d, uint32_t iterations,
+                                           float* __restrict__ cb);
 
 // Router finished inside the norm: rpart holds nparts partial router sums per token (from
 // the GEMV that merged the residual); they are summed in a fixed order, the Sinkhorn
@@ -59,8 +59,10 @@ struct NormRouter {
   float* coef_out = nullptr;
 };
 
-// Register form (h % 4 == 0, h <= 1024 * VPT): every float4 of the row is loaded up front
-// into registers, so the row costs one memory latency instead of one per loop trip.
+// Register form (h % 4 == 0, h <= 1024 * VPT). Every load of the CTA (both streams of
+// the row, the norm weight, the router partials and biases) is issued first, so the
+// row costs one memory latency; the router sums take one block reduction (fixed warp
+// order), the Sinkhorn step runs on thread 0, and the mixed row one more reduction.
 template <int VPT>
 __global__ void __launch_bounds__(256) branch_norm_kernel(StepRef sr, snl_layer_p p, const float* __restrict__ x,
                                                           const float* __restrict__ coef, const float* __restrict__ w,
@@ -68,13 +70,32 @@ __global__ void __launch_bounds__(256) branch_norm_kernel(StepRef sr, snl_layer_
   pdl_trigger();
   pdl_wait();
   __shared__ float sh[32];
+  __shared__ float rsh[8][9];
   __shared__ float pre_sh[2];
-  const snl_step_u st = load_step(sr);
   const uint32_t g = blockIdx.x;
-  const uint32_t m = g + (p.last_row == 1 ? st.m - 1 : 0);
+  const uint32_t m = p.last_row == 1 ? g + load_step(sr).m - 1 : g;
   const uint64_t base = (uint64_t)m * (p.x_stride != 0 ? p.x_stride : 2 * p.h);
+  const uint32_t h4 = p.h / 4;
+  const float4* x4 = reinterpret_cast<const float4*>(x + base);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  const bool mix = p.mode == 1;
+  const bool route = mix && nr.rpart;
+  float4 v[VPT], b[VPT], ww[VPT];
+#pragma unroll
+  for (int c = 0; c < VPT; c++) {
+    const uint32_t i4 = threadIdx.x + c * 256;
+    const bool in = i4 < h4;
+    v[c] = in ? x4[i4] : make_float4(0.f, 0.f, 0.f, 0.f);
+    b[c] = in && mix ? x4[h4 + i4] : make_float4(0.f, 0.f, 0.f, 0.f);
+    ww[c] = in ? w4[i4] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   float pre0 = 1.f, pre1 = 0.f;
-  if (p.mode == 1 && nr.rpart) {
+  if (route) {
+    float bias[8];
+    if (threadIdx.x == 0) {
+#pragma unroll
+      for (int o = 0; o < 8; o++) bias[o] = nr.router[(uint64_t)16 * p.h + o];
+    }
     float acc[9];
 #pragma unroll
     for (int o = 0; o < 9; o++) acc[o] = 0.f;
@@ -82,39 +103,41 @@ __global__ void __launch_bounds__(256) branch_norm_kernel(StepRef sr, snl_layer_
 #pragma unroll
       for (int o = 0; o < 9; o++) acc[o] += nr.rpart[((uint64_t)m * nr.nparts + i) * 9 + o];
     }
-    float tot[9];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
 #pragma unroll
-    for (int o = 0; o < 9; o++) tot[o] = block_sum(acc[o], sh);
+    for (int o = 0; o < 9; o++) acc[o] = warp_sum(acc[o]);
+    if (lane == 0) {
+#pragma unroll
+      for (int o = 0; o < 9; o++) rsh[wid][o] = acc[o];
+    }
+    __syncthreads();
     if (threadIdx.x == 0) {
+      float tot[9];
+#pragma unroll
+      for (int o = 0; o < 9; o++) {
+        float t = 0.f;
+        for (int k = 0; k < 8; k++) t += rsh[k][o];
+        tot[o] = t;
+      }
       float* cb = nr.coef_out + m * 8;
-      mhc_coef(tot, nr.router, 2 * p.h, p.iterations, cb);
+      mhc_coef_b(tot, bias, 2 * p.h, p.iterations, cb);
       pre_sh[0] = cb[0];
       pre_sh[1] = cb[1];
     }
     __syncthreads();
     pre0 = pre_sh[0];
     pre1 = pre_sh[1];
-  } else if (p.mode == 1) {
+  } else if (mix) {
     pre0 = coef[m * 8];
     pre1 = coef[m * 8 + 1];
   }
-  const uint32_t h4 = p.h / 4;
-  const float4* x4 = reinterpret_cast<const float4*>(x + base);
-  float4 v[VPT];
-#pragma unroll
-  for (int c = 0; c < VPT; c++) {
-    const uint32_t i4 = threadIdx.x + c * 256;
-    v[c] = i4 < h4 ? x4[i4] : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  if (p.mode == 1) {
+  if (mix) {
 #pragma unroll
     for (int c = 0; c < VPT; c++) {
-      const uint32_t i4 = threadIdx.x + c * 256;
-      const float4 b = i4 < h4 ? x4[h4 + i4] : make_float4(0.f, 0.f, 0.f, 0.f);
-      v[c].x = fmaf(pre1, b.x, pre0 * v[c].x);
-      v[c].y = fmaf(pre1, b.y, pre0 * v[c].y);
-      v[c].z = fmaf(pre1, b.z, pre0 * v[c].z);
-      v[c].w = fmaf(pre1, b.w, pre0 * v[c].w);
+      v[c].x = fmaf(pre1, b[c].x, pre0 * v[c].x);
+      v[c].y = fmaf(pre1, b[c].y, pre0 * v[c].y);
+      v[c].z = fmaf(pre1, b[c].z, pre0 * v[c].z);
+      v[c].w = fmaf(pre1, b[c].w, pre0 * v[c].w);
     }
   }
   float ss = 0.f;
@@ -122,18 +145,16 @@ __global__ void __launch_bounds__(256) branch_norm_kernel(StepRef sr, snl_layer_
   for (int c = 0; c < VPT; c++) ss += v[c].x * v[c].x + v[c].y * v[c].y + v[c].z * v[c].z + v[c].w * v[c].w;
   const float total = block_sum(ss, sh);
   const float rinv = rsqrtf(total / (float)p.h + p.eps);
-  const float4* w4 = reinterpret_cast<const float4*>(w);
   float4* o4 = reinterpret_cast<float4*>(out + (uint64_t)g * p.h);
 #pragma unroll
   for (int c = 0; c < VPT; c++) {
     const uint32_t i4 = threadIdx.x + c * 256;
     if (i4 >= h4) break;
-    const float4 ww = w4[i4];
     float4 o;
-    o.x = v[c].x * rinv * (p.weight_one + ww.x);
-    o.y = v[c].y * rinv * (p.weight_one + ww.y);
-    o.z = v[c].z * rinv * (p.weight_one + ww.z);
-    o.w = v[c].w * rinv * (p.weight_one + ww.w);
+    o.x = v[c].x * rinv * (p.weight_one + ww[c].x);
+    o.y = v[c].y * rinv * (p.weight_one + ww[c].y);
+    o.z = v[c].z * rinv * (p.weight_one + ww[c].z);
+    o.w = v[c].w * rinv * (p.weight_one + ww[c].w);
     o4[i4] = o;
     if (xo.planes) {
       xout_store(xo, g, 4 * i4, o.x);
@@ -166,34 +187,71 @@ __device__ __forceinline__ float lse2(float a, float b) {
   return mx + __logf(__expf(a - mx) + __expf(b - mx));
 }
 
-// mhc_finish (layers.wgsl:234-266) for one token.
-__device__ __forceinline__ void mhc_coef(const float raw[9], const float* __restrict__ w, uint32_t d,
-                                         uint32_t iterations, float* __restrict__ cb) {
+// mhc_finish (layers.wgsl:234-266) for one token, with the 8 router biases given.
+// The Sinkhorn normalisation of the 2x2 mixing matrix runs on exp(logits - max), where
+// each half-step is a sum, one reciprocal and two products (the same iterates as the
+// log-domain form, without a log per step); if any row or column sum underflows, it is
+// redone in the log domain.
+__device__ __forceinline__ void mhc_coef_b(const float raw[9], const float bias[8], uint32_t d, uint32_t iterations,
+                                           float* __restrict__ cb) {
   const float rinv = rsqrtf(raw[8] / (float)d + 1e-6f);
   float lg[8];
 #pragma unroll
-  for (int o = 0; o < 8; o++) lg[o] = fmaf(raw[o], rinv, w[(uint64_t)8 * d + o]);
-  float a = lg[4], b = lg[5], c = lg[6], e = lg[7];
+  for (int o = 0; o < 8; o++) lg[o] = fmaf(raw[o], rinv, bias[o]);
+  const float mx = fmaxf(fmaxf(lg[4], lg[5]), fmaxf(lg[6], lg[7]));
+  float A = __expf(lg[4] - mx), B = __expf(lg[5] - mx), C = __expf(lg[6] - mx), E = __expf(lg[7] - mx);
+  bool ok = true;
   for (uint32_t it = 0; it < iterations; it++) {
-    const float r0 = lse2(a, b), r1 = lse2(c, e);
-    a -= r0;
-    b -= r0;
-    c -= r1;
-    e -= r1;
-    const float c0 = lse2(a, c), c1 = lse2(b, e);
-    a -= c0;
-    c -= c0;
-    b -= c1;
-    e -= c1;
+    const float r0 = A + B, r1 = C + E;
+    ok &= r0 > 1e-30f && r1 > 1e-30f;
+    const float i0 = __fdividef(1.0f, r0), i1 = __fdividef(1.0f, r1);
+    A *= i0;
+    B *= i0;
+    C *= i1;
+    E *= i1;
+    const float c0 = A + C, c1 = B + E;
+    ok &= c0 > 1e-30f && c1 > 1e-30f;
+    const float j0 = __fdividef(1.0f, c0), j1 = __fdividef(1.0f, c1);
+    A *= j0;
+    C *= j0;
+    B *= j1;
+    E *= j1;
+  }
+  if (!ok) {
+    float a = lg[4], b = lg[5], c = lg[6], e = lg[7];
+    for (uint32_t it = 0; it < iterations; it++) {
+      const float r0 = lse2(a, b), r1 = lse2(c, e);
+      a -= r0;
+      b -= r0;
+      c -= r1;
+      e -= r1;
+      const float c0 = lse2(a, c), c1 = lse2(b, e);
+      a -= c0;
+      c -= c0;
+      b -= c1;
+      e -= c1;
+    }
+    A = __expf(a);
+    B = __expf(b);
+    C = __expf(c);
+    E = __expf(e);
   }
   cb[0] = 1.0f / (1.0f + __expf(-lg[0]));
   cb[1] = 1.0f / (1.0f + __expf(-lg[1]));
   cb[2] = 2.0f / (1.0f + __expf(-lg[2]));
   cb[3] = 2.0f / (1.0f + __expf(-lg[3]));
-  cb[4] = __expf(a);
-  cb[5] = __expf(b);
-  cb[6] = __expf(c);
-  cb[7] = __expf(e);
+  cb[4] = A;
+  cb[5] = B;
+  cb[6] = C;
+  cb[7] = E;
+}
+
+__device__ __forceinline__ void mhc_coef(const float raw[9], const float* __restrict__ w, uint32_t d,
+                                         uint32_t iterations, float* __restrict__ cb) {
+  float bias[8];
+#pragma unroll
+  for (int o = 0; o < 8; o++) bias[o] = w[(uint64_t)8 * d + o];
+  mhc_coef_b(raw, bias, d, iterations, cb);
 }
 
 __global__ void __launch_bounds__(256) mhc_dots_kernel(snl_layer_p p, const float* __restrict__ x,
