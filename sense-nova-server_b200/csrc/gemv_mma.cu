@@ -609,7 +609,7 @@ __global__ void __launch_bounds__(kTileWarps * 32) gemv_tile_bulk_kernel(GemvArg
 // Persistent row-group tile GEMV (the default decode GEMV).
 //
 // A grid of up to kPgCtasPerSm CTAs per SM; CTA b owns the contiguous row groups
-// [b*G/grid, (b+1)*G/grid). The kPgWarps warps of a CTA split every group's K range
+// [b*G/grid, (b+1)*G/grid). The warps of a CTA split every group's K range
 // into equal runs of stages (kPgTiles tiles plus their scales, one contiguous bulk copy
 // each), stream them through a per-warp ring of kStages stages, and meet once per group
 // in shared memory, where warp 0 adds the warp partials in warp order and runs the
@@ -617,19 +617,21 @@ __global__ void __launch_bounds__(kTileWarps * 32) gemv_tile_bulk_kernel(GemvArg
 // The first stages are issued before pdl_wait(): the weights are constant during a
 // step, so their copies overlap the tail of the kernel before.
 // ---------------------------------------------------------------------------
-constexpr int kPgWarps = 4;
-constexpr int kPgTiles = 16;
+// Two shapes of CTA: matrices with many row groups use 8 warps with 2 stages each, 3
+// CTAs per SM (registers capped for that); matrices with few groups (n <= 16 * 2 * SMs,
+// the 4096-row projections) get one 16-warp CTA per group, 2 per SM, each warp one
+// stage of its 1/16 of K, so more bytes are in flight per group.
+constexpr int kPgTiles = 8;
 constexpr int kPgCtasPerSm = 3;
 
-template <int DT>
+template <int DT, int WARPS, int S>
 struct PgGeom {
   static constexpr uint32_t TB = DT == SNL_Q8_0 ? 512 : 256;
-  static constexpr int kStages = DT == SNL_Q8_0 ? 2 : 3;
   static constexpr uint32_t kStageW = kPgTiles * TB;
   static constexpr uint32_t kStageS = kPgTiles / 4 * 256;
   static constexpr uint32_t kStage = kStageW + kStageS;
-  static constexpr uint32_t kWarpBytes = kStages * kStage;
-  static constexpr uint32_t kSmem = kPgWarps * kWarpBytes + kPgWarps * kStages * 8;
+  static constexpr uint32_t kWarpBytes = S * kStage;
+  static constexpr uint32_t kSmem = WARPS * kWarpBytes + WARPS * S * 8;
 };
 
 // The epilogue of one finished row group, run by one warp: val(tt, r) is the dot of
@@ -682,25 +684,24 @@ __device__ __forceinline__ void group_finish(const GemvArgs& a, uint32_t grp, ui
   }
 }
 
-template <int DT, int M>
-__global__ void __launch_bounds__(kPgWarps * 32) gemv_pg_kernel(GemvArgs a, const uint8_t* __restrict__ tiles,
-                                                                const float* __restrict__ ts, uint32_t groups, int* err) {
-  using G = PgGeom<DT>;
-  constexpr int S = G::kStages;
+template <int DT, int M, int WARPS, int S>
+__global__ void __launch_bounds__(WARPS * 32, WARPS >= 16 ? 2 : 3) gemv_pg_kernel(GemvArgs a, const uint8_t* __restrict__ tiles,
+                                                             const float* __restrict__ ts, uint32_t groups, int* err) {
+  using G = PgGeom<DT, WARPS, S>;
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ float red[2][kPgWarps][M][16];
+  __shared__ float red[2][WARPS][M][16];
   pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const uint32_t nb = a.k / 32, nb4 = (nb + 3) / 4;
   const uint32_t spg = (nb + kPgTiles - 1) / kPgTiles;
-  const uint32_t per = (spg + kPgWarps - 1) / kPgWarps;
+  const uint32_t per = (spg + WARPS - 1) / WARPS;
   const uint32_t st0 = min(spg, warp * per), nst = min(spg, st0 + per) - st0;
   const uint32_t g0 = (uint32_t)((uint64_t)blockIdx.x * groups / gridDim.x);
   const uint32_t g1 = (uint32_t)((uint64_t)(blockIdx.x + 1) * groups / gridDim.x);
   const uint32_t njobs = (g1 - g0) * nst;
   uint8_t* ring = smem + warp * G::kWarpBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPgWarps * G::kWarpBytes) + warp * S;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + WARPS * G::kWarpBytes) + warp * S;
 
   if (lane == 0)
     for (int s = 0; s < S; s++) mbar_init(&bars[s], 1);
@@ -781,7 +782,7 @@ __global__ void __launch_bounds__(kPgWarps * 32) gemv_pg_kernel(GemvArgs a, cons
       group_finish<M>(a, g0 + gi, groups, lane, [&](int tt, int r) {
         float v = 0.f;
 #pragma unroll
-        for (int w = 0; w < kPgWarps; w++) v += red[buf][w][tt][r];
+        for (int w = 0; w < WARPS; w++) v += red[buf][w][tt][r];
         return v;
       });
   }
@@ -794,23 +795,31 @@ __global__ void __launch_bounds__(kPgWarps * 32) gemv_pg_kernel(GemvArgs a, cons
   }
 }
 
-template <int DT, int M>
-int launch_pg_t(const GemvArgs& a, const void* tiles, const float* ts, int* err, cudaStream_t s) {
-  using G = PgGeom<DT>;
+template <int DT, int M, int WARPS, int S>
+int launch_pg_cfg(const GemvArgs& a, const void* tiles, const float* ts, uint32_t groups, int* err, cudaStream_t s) {
+  using G = PgGeom<DT, WARPS, S>;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
-  auto kern = gemv_pg_kernel<DT, M>;
+  auto kern = gemv_pg_kernel<DT, M, WARPS, S>;
   if (dev >= 0 && dev < 64 && !attr[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
     if (e != cudaSuccess) return cuda_fail(e, "gemv_pg: smem attribute");
     attr[dev] = true;
   }
-  const uint32_t groups = (a.n + 15) / 16;
   const uint32_t grid = std::min<uint32_t>(groups, (uint32_t)sm_count() * kPgCtasPerSm);
-  SNL_PDL_LAUNCH("gemv_pg", kern, dim3(grid), dim3(kPgWarps * 32), (size_t)G::kSmem, s, a,
+  SNL_PDL_LAUNCH("gemv_pg", kern, dim3(grid), dim3(WARPS * 32), (size_t)G::kSmem, s, a,
                  static_cast<const uint8_t*>(tiles), ts, groups, err);
   return SNL_OK;
+}
+
+template <int DT, int M>
+int launch_pg_t(const GemvArgs& a, const void* tiles, const float* ts, int* err, cudaStream_t s) {
+  const uint32_t groups = (a.n + 15) / 16;
+  const bool few = groups <= 2u * (uint32_t)sm_count();
+  constexpr int kSA = DT == SNL_Q8_0 ? 2 : 3;  // stages per warp, 8-warp CTA
+  if (few) return launch_pg_cfg<DT, M, 16, 1>(a, tiles, ts, groups, err, s);
+  return launch_pg_cfg<DT, M, 8, kSA>(a, tiles, ts, groups, err, s);
 }
 
 template <int DT, int M>
