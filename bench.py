@@ -135,8 +135,12 @@ def phys_gpu_index(local_rank: int) -> int:
     return local_rank
 
 
+CONFIG1_BYTES = 12288 * 4096 + 12288 * 4096 // 32 * 4 + 4 * 4096 + 4 * 12288
+
+
 def traffic_from_profiles() -> float | None:
-    """DRAM bytes per launch of the decode GEMV from the committed ncu summary."""
+    """DRAM bytes per launch of the config-1 GEMV from the committed ncu summary
+    (profiles/gemv_q8_decode.md, `dram_bytes_per_launch:`)."""
     f = ROOT / "profiles" / "gemv_q8_decode.md"
     if not f.exists():
         return None
@@ -372,7 +376,10 @@ def run_ours(args):
     peak, peak_kind = peaks()
     achieved = gb / (gms * 1e6)
     n_mat = sum(r["calls"] for r in mats)
-    traffic = traffic_from_profiles()
+    # ncu traffic of config 1 scaled to this step's average matrix launch (same kernel,
+    # every weight byte read once at every shape).
+    t1 = traffic_from_profiles()
+    traffic = None if t1 is None or n_mat == 0 else (gb / n_mat) * (t1 / CONFIG1_BYTES)
 
     if rank == 0 and args.profile:
         eng.print_profile(prof)
