@@ -243,6 +243,40 @@ typedef struct snl_engine snl_engine;
 int snl_engine_create(const snl_model_config* cfg, size_t ctx, int device, uint32_t flags,
                       snl_engine** out);
 
+/* Tensor parallelism over 2, 4 or 8 GPUs of one node: one process (and one engine) per
+ * GPU, all driven through the same call sequence, as the reference's single Engine is.
+ * (The reference has no tensor parallelism. SURVEY §8e proposes `snl_engine_create(...,
+ * tp_rank, tp_size, nccl_id)`; the rendezvous here is CUDA IPC instead of an NCCL id.)
+ * The in-projections and the LM head are split by output rows (qkv by head, in_proj by
+ * key/value head, gate_up by intermediate slice, lm_head by vocabulary). The
+ * out-projections are split by K, and their partial sums are added across GPUs over
+ * NVLink inside the projection kernel. Norms, mHC and the embedding are replicated.
+ * Steps:
+ *   1. snl_engine_create_tp on every rank;
+ *   2. snl_engine_tp_handle; all-gather the SNL_TP_HANDLE_BYTES-byte handles in rank
+ *      order (e.g. with torch.distributed);
+ *   3. snl_engine_tp_connect with the gathered handles;
+ *   4. set_tensor / fill_synthetic with the FULL tensors; finalize keeps this rank's
+ *      shard.
+ * forward_mm returns the full logits row on every rank; forward_greedy returns the same
+ * token on every rank. With tp_size == 1 this is snl_engine_create. MTP is not supported
+ * under tensor parallelism (finalize fails with SNL_E_UNSUPPORTED). */
+#define SNL_TP_HANDLE_BYTES 64
+/* The shard a rank keeps of one named tensor (what finalize applies): kind
+ * SNL_TP_FULL (replicated), SNL_TP_ROWS (the listed row ranges of a matrix, in order),
+ * SNL_TP_COLS (one column range) or SNL_TP_ELEMS (element ranges of an f32 vector).
+ * ranges receives n_ranges (start, count) pairs; cap is its capacity in pairs. */
+#define SNL_TP_FULL 0
+#define SNL_TP_ROWS 1
+#define SNL_TP_COLS 2
+#define SNL_TP_ELEMS 3
+int snl_tp_plan(const snl_model_config* cfg, int tp_rank, int tp_size, const char* name, int* kind, size_t* ranges,
+                size_t cap, size_t* n_ranges);
+int snl_engine_create_tp(const snl_model_config* cfg, size_t ctx, int device, uint32_t flags, int tp_rank,
+                         int tp_size, snl_engine** out);
+int snl_engine_tp_handle(snl_engine* e, void* handle_out);
+int snl_engine_tp_connect(snl_engine* e, const void* handles);
+
 /* One tensor of a .snl file (weights.rs:76-104 names and layout): dtype SNL_F32 with
  * rows*cols floats in q (s unused), or Q8_0/Q4_0 with the packed quants in q and the
  * f32 scales in s. Host pointers. */

@@ -165,7 +165,7 @@ int launch_conv_delta(StepRef st, const snl_lin_p& p, const float* proj, float* 
                       XOut xo = XOut());
 int launch_argmax(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_idx, cudaStream_t s);
 int launch_embed(const uint32_t* tokens, uint32_t m, const int8_t* q, const float* s_, uint32_t h, uint32_t vocab,
-                 float* x, int* err_flag, cudaStream_t s);
+                 float* x, int* err_flag, cudaStream_t s, unsigned long long* step_ctr = nullptr);
 int launch_gen_quant(uint64_t seed, const char* name, int dtype, size_t rows, size_t cols, void* q, float* s,
                      cudaStream_t st);
 int launch_gen_f32(uint64_t seed, const char* name, uint32_t sub, size_t n, float mult, float offset, float* out,

@@ -20,6 +20,7 @@
 #include "common.cuh"
 #include "gemv_mma.cuh"
 #include "synth.h"
+#include "tp.cuh"
 #include "synth_model.h"
 
 namespace snl {
@@ -77,6 +78,15 @@ uint32_t parts_for(size_t m, size_t total) {
 
 struct snl_engine {
   snl_model_config cfg;
+  // This rank's shard of the model: cfg with the head counts and intermediate size
+  // divided by the tensor-parallel size (cfg itself when it is 1).
+  snl_model_config lc;
+  uint32_t vocab_l = 0;  // LM-head rows on this rank
+  snl::TpHost tp;
+  unsigned long long* step_ctr = nullptr;  // steps run (exchange epochs), bumped by the embedding
+  float* logits_full = nullptr;            // tensor parallel: gathered logits [2][vocab]
+  float* head_out = nullptr;               // where the LM head writes [rows][vocab_l]
+  uint32_t tp_sites = 0;                   // exchanges per step: 2 per layer visit + 2 (head)
   size_t ctx = 0;
   int device = 0;
   uint32_t flags = 0;
@@ -178,17 +188,17 @@ snl_layer_p layer_p(const snl_engine* e, uint32_t mode, bool last_row) {
   p.eps = e->cfg.eps;
   p.weight_one = 1.0f;
   p.iterations = e->cfg.mhc_start >= 0 ? e->cfg.mhc_iterations : 0;
-  p.inter = e->cfg.intermediate;
+  p.inter = e->lc.intermediate;
   p.x_stride = 0;
   return p;
 }
 
 snl_attn_p attn_p(const snl_engine* e) {
   snl_attn_p a;
-  a.n_heads = e->cfg.n_heads;
-  a.n_kv = e->cfg.n_kv_heads;
+  a.n_heads = e->lc.n_heads;
+  a.n_kv = e->lc.n_kv_heads;
   a.rot_dim = e->cfg.rot_dim;
-  a.proj_stride = (uint32_t)snl_synth::attn_proj_rows(e->cfg);
+  a.proj_stride = (uint32_t)snl_synth::attn_proj_rows(e->lc);
   a.rope_theta = e->cfg.rope_theta;
   a.eps = e->cfg.eps;
   a.scale = 1.0f / sqrtf((float)e->cfg.head_dim);
@@ -198,10 +208,10 @@ snl_attn_p attn_p(const snl_engine* e) {
 
 snl_lin_p lin_p(const snl_engine* e) {
   snl_lin_p l;
-  l.conv_dim = (uint32_t)snl_synth::conv_dim(e->cfg);
-  l.proj_stride = (uint32_t)snl_synth::lin_proj_rows(e->cfg);
-  l.n_k = e->cfg.lin_k_heads;
-  l.n_v = e->cfg.lin_v_heads;
+  l.conv_dim = (uint32_t)snl_synth::conv_dim(e->lc);
+  l.proj_stride = (uint32_t)snl_synth::lin_proj_rows(e->lc);
+  l.n_k = e->lc.lin_k_heads;
+  l.n_v = e->lc.lin_v_heads;
   l.eps = e->cfg.eps;
   l.pad[0] = l.pad[1] = l.pad[2] = 0;
   return l;
@@ -285,13 +295,17 @@ int push_norm(snl_engine* e, StepRef st, uint32_t m, const float* router, const 
 // merges into the residual x like `merge` (engine.rs:471-480) and can expand stream 0
 // into stream 1 (the merge mode 3 that opens an mHC range).
 int matx(snl_engine* e, const QT& w, uint32_t rows, int mode, float* y, size_t y_stride, uint32_t merge_mode = 0,
-         int expand = 0, const float* rnext = nullptr, const __half* planes = nullptr) {
+         int expand = 0, const float* rnext = nullptr, const __half* planes = nullptr, int tp_site = -1) {
   GemvArgs a{};
   a.n = (uint32_t)w.rows;
   a.k = (uint32_t)w.cols;
   a.xplanes = planes ? planes : e->xpl;
   a.act_planes = e->xpl_act;
   a.act_stride = e->pstride;
+  if (tp_site >= 0 && e->tp.size > 1) {
+    a.tp = e->tp.comm;
+    a.tp_site = (uint32_t)tp_site;
+  }
   a.plane_stride = e->pstride;
   a.wq = static_cast<const uint8_t*>(w.q);
   a.mode = mode;
@@ -305,7 +319,7 @@ int matx(snl_engine* e, const QT& w, uint32_t rows, int mode, float* y, size_t y
   a.rnext = rnext;
   a.rpart = e->rpart;
   const double bytes = qbytes(w) + 4.0 * rows * (w.cols + w.rows);
-  const std::string label = "mat n=" + std::to_string(w.rows) + (y == e->logits ? " (head)" : "");
+  const std::string label = "mat n=" + std::to_string(w.rows) + (y == e->head_out ? " (head)" : "");
   SNL_TRY(timed(e, label, bytes, [&] {
     if (w.tiles) return launch_gemv_tile(w.dtype, a, rows, w.tiles, w.tscales, e->stream);
     return launch_gemv_mma(w.dtype, a, rows, w.s, w.s_f16, e->stream);
@@ -314,9 +328,19 @@ int matx(snl_engine* e, const QT& w, uint32_t rows, int mode, float* y, size_t y
   return SNL_OK;
 }
 
+// Element offset of this rank's o_proj input inside the attention output (non-zero
+// only when ranks outnumber KV heads and a rank computes a whole GQA group).
+size_t o_proj_offset(const snl_engine* e) {
+  const auto& c = e->cfg;
+  const size_t N = (size_t)e->tp.size;
+  if (N <= c.n_kv_heads) return 0;
+  const size_t nq = c.n_heads / N;
+  return ((size_t)e->tp.rank % (N / c.n_kv_heads)) * nq * c.head_dim;
+}
+
 // The layer loop of engine.rs:389-481 for one step of m rows.
 int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
-  const auto& c = e->cfg;
+  const auto& c = e->lc;
   const size_t h = c.hidden;
   size_t lin_slot = 0, full_slot = 0;
   const snl_attn_p ap = attn_p(e);
@@ -330,10 +354,21 @@ int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
     return mat(e, st, w, e->xn, h, y, y_stride, m);
   };
   // out-projection of `src` (K = src_dim) merged into the residual
+  // Under tensor parallelism the out-projections are row-parallel: the tensor-core GEMV
+  // trades partials with the peers in its epilogue; the prefill GEMM writes this rank's
+  // partial into the exchange region and an allreduce kernel sums the ranks' partials.
   auto proj_out = [&](const QT& w, const float* src, size_t src_dim, uint32_t merge_mode, bool expand,
-                      const float* rnext, const __half* planes = nullptr) -> int {
-    if (tc) return matx(e, w, m, 1, nullptr, 0, merge_mode, expand ? 1 : 0, rnext, planes);
-    SNL_TRY(mat(e, st, w, src, src_dim, e->branch, h, m));
+                      const float* rnext, const __half* planes, uint32_t site) -> int {
+    if (tc) return matx(e, w, m, 1, nullptr, 0, merge_mode, expand ? 1 : 0, rnext, planes, (int)site);
+    if (e->tp.size > 1) {
+      const uint64_t par = (((uint64_t)site + 1) & 1) * e->tp.comm.bp_elems;  // tp_sites is even
+      float* part = e->tp.comm.bparts[e->tp.rank] + par;
+      SNL_TRY(mat(e, st, w, src, src_dim, part, h, m));
+      SNL_TRY(timed(e, "TpAllreduce", 4.0 * m * h * e->tp.size,
+                    [&] { return launch_tp_allreduce(e->tp.comm, site, (uint64_t)m * h, e->branch, e->stream); }));
+    } else {
+      SNL_TRY(mat(e, st, w, src, src_dim, e->branch, h, m));
+    }
     SNL_TRY(timed(e, "Merge", 5 * hb, [&] {
       return launch_merge(st, layer_p(e, merge_mode, false), e->x, e->coef, e->branch, m, e->stream);
     }));
@@ -366,8 +401,10 @@ int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
         SNL_TRY(timed(e, "Combine", 4.0 * m * qd * 2, [&] {
           return launch_attn_combine(st, ap, e->proj, e->partial, e->attn_out, m, e->stream, 1, xo);
         }));
-      SNL_TRY(proj_out(*find_q(e, L + "o_proj"), e->attn_out, snl_synth::q_dim(c), mhc ? 1 : 0, false,
-                       mhc ? find_f(e, L + "mhc_ffn") : nullptr));
+      // o_proj's K shard: this rank's query heads within the attention it computed.
+      const size_t xo_off = o_proj_offset(e);
+      SNL_TRY(proj_out(*find_q(e, L + "o_proj"), e->attn_out + xo_off, snl_synth::q_dim(c), mhc ? 1 : 0, false,
+                       mhc ? find_f(e, L + "mhc_ffn") : nullptr, tc ? e->xpl + xo_off : nullptr, (uint32_t)(2 * vi)));
       full_slot++;
     } else {
       SNL_TRY(proj_in(*find_q(e, L + "in_proj"), e->proj, lp.proj_stride));
@@ -381,7 +418,7 @@ int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
         return launch_conv_delta(st, lp, e->proj, cs, ss, lw, e->attn_out, cc, sc, e->stream, xo);
       }));
       SNL_TRY(proj_out(*find_q(e, L + "out_proj"), e->attn_out, snl_synth::lin_value_dim(c), mhc ? 1 : 0, false,
-                       mhc ? find_f(e, L + "mhc_ffn") : nullptr));
+                       mhc ? find_f(e, L + "mhc_ffn") : nullptr, nullptr, (uint32_t)(2 * vi)));
       lin_slot++;
     }
     SNL_TRY(push_norm(e, st, m, mhc ? find_f(e, L + "mhc_ffn") : nullptr, find_f(e, L + "post_ln"), xo));
@@ -401,7 +438,7 @@ int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
     const bool next_mhc = vi + 1 < e->plan.size() && snl_synth::is_mhc(c, e->plan[vi + 1]);
     const float* rnext = next_mhc ? find_f(e, "l" + std::to_string(e->plan[vi + 1]) + ".mhc_attn") : nullptr;
     SNL_TRY(proj_out(*find_q(e, L + "down"), e->act, c.intermediate, mode, expand_next, rnext,
-                     fused_swiglu ? e->xpl_act : nullptr));
+                     fused_swiglu ? e->xpl_act : nullptr, (uint32_t)(2 * vi + 1)));
     expanded = expand_next;
   }
   return SNL_OK;
@@ -409,13 +446,16 @@ int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
 
 // Everything a step does on the device after its inputs (tokens, rpos, step) are
 // resident: embedding, layers, final norm, optional head and argmax, hlast update.
-int device_step(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid, uint32_t rows, bool greedy) {
+int device_step(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid, uint32_t rows, bool greedy,
+                bool embed = true) {
   const size_t h = e->h();
-  const QT* emb = find_q(e, "embed");
-  SNL_TRY(timed(e, "Embed", (double)m * h * 13, [&] {
-    return launch_embed(e->tokens, m, (const int8_t*)emb->q, (const float*)emb->s, (uint32_t)h, e->cfg.vocab, e->x,
-                        nullptr, e->stream);
-  }));
+  if (embed) {
+    const QT* emb = find_q(e, "embed");
+    SNL_TRY(timed(e, "Embed", (double)m * h * 13, [&] {
+      return launch_embed(e->tokens, m, (const int8_t*)emb->q, (const float*)emb->s, (uint32_t)h, e->cfg.vocab, e->x,
+                          nullptr, e->stream, e->step_ctr);
+    }));
+  }
   // Row 0 of hid is the hidden state of the token before this step (engine.rs:889-890).
   SNL_CUDA_TRY(cudaMemcpyAsync(e->hid, e->hlast, h * sizeof(float), cudaMemcpyDeviceToDevice, e->stream));
   SNL_TRY(run_layers(e, st, m, parts_grid));
@@ -424,21 +464,34 @@ int device_step(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid, uint
   SNL_TRY(timed(e, "BranchNorm", 12.0 * m * h, [&] {
     return launch_branch_norm(st, layer_p(e, 0, false), e->x, e->coef, find_f(e, "norm"), e->hid + h, m, e->stream, xo);
   }));
+  const uint32_t vl = e->vocab_l;
   if (rows > 0) {
     if (tc) {
       // The head reads the last `rows` hidden rows (engine.rs:835-842).
       if (rows != m)
         SNL_TRY(launch_xpack(e->hid + (size_t)(m - rows + 1) * h, rows, (uint32_t)h, (uint32_t)h, e->xpl, e->pstride,
                              e->stream));
-      SNL_TRY(matx(e, *find_q(e, "lm_head"), rows, 0, e->logits, e->cfg.vocab));
+      SNL_TRY(matx(e, *find_q(e, "lm_head"), rows, 0, e->head_out, vl));
     } else {
-      SNL_TRY(mat(e, st, *find_q(e, "lm_head"), e->hid, h, e->logits, e->cfg.vocab, rows, rows,
+      SNL_TRY(mat(e, st, *find_q(e, "lm_head"), e->hid, h, e->head_out, vl, rows, rows,
                   (uint32_t)((m - rows + 1) * h)));
     }
-    if (greedy)
-      SNL_TRY(timed(e, "Argmax", 4.0 * rows * e->cfg.vocab, [&] {
-        return launch_argmax_with(e->logits, rows, e->cfg.vocab, e->amax, e->amax_part, e->stream);
-      }));
+  }
+  if (e->tp.size > 1) {
+    // Two exchanges close every step (the site count stays even and fixed): the logits
+    // shards are gathered when the caller wants logits, and the greedy token is the
+    // largest of the ranks' shard maxima (first index on ties, as one scan would find).
+    const uint32_t site = e->tp_sites - 2;
+    const uint32_t grows = (rows > 0 && !greedy) ? rows : 0;
+    SNL_TRY(timed(e, "TpGather", 4.0 * grows * e->cfg.vocab,
+                  [&] { return launch_tp_gather_logits(e->tp.comm, site, grows, vl, e->logits_full, e->stream); }));
+    const uint32_t krows = (rows > 0 && greedy) ? rows : 0;
+    SNL_TRY(timed(e, "Argmax", 4.0 * krows * vl, [&] {
+      return launch_argmax_tp(e->head_out, krows, vl, e->amax, e->amax_part, e->tp.comm, site + 1, e->stream);
+    }));
+  } else if (rows > 0 && greedy) {
+    SNL_TRY(timed(e, "Argmax", 4.0 * rows * vl,
+                  [&] { return launch_argmax_with(e->head_out, rows, vl, e->amax, e->amax_part, e->stream); }));
   }
   SNL_CUDA_TRY(cudaMemcpyAsync(e->hlast, e->hid + (size_t)m * h, h * sizeof(float), cudaMemcpyDeviceToDevice, e->stream));
   return SNL_OK;
@@ -524,23 +577,14 @@ int forward_impl(snl_engine* e, const uint32_t* tokens, size_t n, const uint32_t
       StepRef st = step_dev(e->step_d, sh);
       const QT* emb = find_q(e, "embed");
       SNL_TRY(launch_embed(e->tokens, (uint32_t)m, (const int8_t*)emb->q, (const float*)emb->s, (uint32_t)h,
-                           e->cfg.vocab, e->x, nullptr, e->stream));
+                           e->cfg.vocab, e->x, nullptr, e->stream, e->step_ctr));
       for (size_t i = 0; i < n_embeds; i++) {
         const size_t r = embed_idx[i];
         if (r < c0 || r >= c0 + m) continue;
         SNL_CUDA_TRY(cudaMemcpyAsync(e->x + (r - c0) * 2 * h, embeds + i * h, h * sizeof(float), cudaMemcpyHostToDevice,
                                      e->stream));
       }
-      SNL_CUDA_TRY(cudaMemcpyAsync(e->hid, e->hlast, h * sizeof(float), cudaMemcpyDeviceToDevice, e->stream));
-      SNL_TRY(run_layers(e, st, (uint32_t)m, sh.parts));
-      SNL_TRY(launch_branch_norm(st, layer_p(e, 0, false), e->x, e->coef, find_f(e, "norm"), e->hid + h, (uint32_t)m,
-                                 e->stream));
-      if (rows) {
-        SNL_TRY(mat(e, st, *find_q(e, "lm_head"), e->hid, h, e->logits, e->cfg.vocab, (uint32_t)rows, (uint32_t)rows,
-                    (uint32_t)((m - rows + 1) * h)));
-        if (greedy) SNL_TRY(launch_argmax_with(e->logits, (uint32_t)rows, e->cfg.vocab, e->amax, e->amax_part, e->stream));
-      }
-      SNL_CUDA_TRY(cudaMemcpyAsync(e->hlast, e->hid + m * h, h * sizeof(float), cudaMemcpyDeviceToDevice, e->stream));
+      SNL_TRY(device_step(e, st, (uint32_t)m, sh.parts, (uint32_t)rows, greedy, false));
     } else {
       SNL_TRY(run_step(e, sh, (uint32_t)m, (uint32_t)rows, greedy));
     }
@@ -613,6 +657,8 @@ extern "C" int snl_engine_create(const snl_model_config* cfg, size_t ctx, int de
   DeviceGuard dg(device);
   snl_engine* e = new snl_engine();
   e->cfg = *cfg;
+  e->lc = *cfg;
+  e->vocab_l = cfg->vocab;
   e->ctx = std::min<size_t>(ctx, cfg->max_position);
   e->device = device;
   e->flags = flags;
@@ -629,6 +675,262 @@ extern "C" int snl_engine_create(const snl_model_config* cfg, size_t ctx, int de
     for (size_t i = c.loop_start; i < c.loop_end; i++) e->plan.push_back(i);
   for (size_t i = c.loop_end; i < c.n_layers; i++) e->plan.push_back(i);
   *out = e;
+  return SNL_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Tensor parallelism (Megatron split): column-parallel in-projections
+// (qkv by head, in_proj by key/value head, gate_up by intermediate slice) and LM head
+// (by vocabulary rows); row-parallel out-projections (o_proj, out_proj, down: K split)
+// whose partial sums are exchanged over NVLink peer memory (tp.cuh). Norms, mHC and the
+// embedding are replicated.
+// ---------------------------------------------------------------------------
+namespace {
+
+struct RowRange {
+  size_t a, n;
+};
+
+void dfree(snl_engine* e, void* p) {
+  if (!p) return;
+  auto it = std::find(e->allocs.begin(), e->allocs.end(), p);
+  if (it != e->allocs.end()) e->allocs.erase(it);
+  cudaFree(p);
+}
+
+// Keeps the rows `rs` (in order) of a quantized matrix.
+int shard_rows(snl_engine* e, snl::QT& t, const std::vector<RowRange>& rs) {
+  size_t rows = 0;
+  for (const auto& r : rs) rows += r.n;
+  const size_t qrow = t.dtype == SNL_Q8_0 ? t.cols : t.cols / 2, srow = t.cols / 32;
+  uint8_t* q = nullptr;
+  float* sc = nullptr;
+  SNL_TRY(snl::dalloc(e, &q, rows * qrow));
+  SNL_TRY(snl::dalloc(e, &sc, rows * srow));
+  size_t o = 0;
+  for (const auto& r : rs) {
+    SNL_CUDA_TRY(cudaMemcpyAsync(q + o * qrow, (const uint8_t*)t.q + r.a * qrow, r.n * qrow, cudaMemcpyDeviceToDevice,
+                                 e->stream));
+    SNL_CUDA_TRY(cudaMemcpyAsync(sc + o * srow, (const float*)t.s + r.a * srow, r.n * srow * sizeof(float),
+                                 cudaMemcpyDeviceToDevice, e->stream));
+    o += r.n;
+  }
+  SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));
+  dfree(e, t.q);
+  dfree(e, t.s);
+  t.q = q;
+  t.s = sc;
+  t.rows = rows;
+  return SNL_OK;
+}
+
+// Keeps columns [c0, c0 + cn) (multiples of 32) of a quantized matrix.
+int shard_cols(snl_engine* e, snl::QT& t, size_t c0, size_t cn) {
+  const bool q8 = t.dtype == SNL_Q8_0;
+  const size_t qrow = q8 ? t.cols : t.cols / 2, qw = q8 ? cn : cn / 2, qo = q8 ? c0 : c0 / 2;
+  uint8_t* q = nullptr;
+  float* sc = nullptr;
+  SNL_TRY(snl::dalloc(e, &q, t.rows * qw));
+  SNL_TRY(snl::dalloc(e, &sc, t.rows * (cn / 32)));
+  SNL_CUDA_TRY(cudaMemcpy2DAsync(q, qw, (const uint8_t*)t.q + qo, qrow, qw, t.rows, cudaMemcpyDeviceToDevice, e->stream));
+  SNL_CUDA_TRY(cudaMemcpy2DAsync(sc, cn / 32 * sizeof(float), (const float*)t.s + c0 / 32, t.cols / 32 * sizeof(float),
+                                 cn / 32 * sizeof(float), t.rows, cudaMemcpyDeviceToDevice, e->stream));
+  SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));
+  dfree(e, t.q);
+  dfree(e, t.s);
+  t.q = q;
+  t.s = sc;
+  t.cols = cn;
+  return SNL_OK;
+}
+
+// Keeps the element ranges `rs` of an f32 vector.
+int shard_f32(snl_engine* e, snl::FT& f, const std::vector<RowRange>& rs) {
+  size_t n = 0;
+  for (const auto& r : rs) n += r.n;
+  float* p = nullptr;
+  SNL_TRY(snl::dalloc(e, &p, n));
+  size_t o = 0;
+  for (const auto& r : rs) {
+    SNL_CUDA_TRY(cudaMemcpyAsync(p + o, f.p + r.a, r.n * sizeof(float), cudaMemcpyDeviceToDevice, e->stream));
+    o += r.n;
+  }
+  SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));
+  dfree(e, f.p);
+  f.p = p;
+  f.n = n;
+  return SNL_OK;
+}
+
+bool ends_with(const std::string& s, const char* suf) {
+  const size_t n = strlen(suf);
+  return s.size() >= n && s.compare(s.size() - n, n, suf) == 0;
+}
+
+// The shard plan of one tensor for rank r of N: kind SNL_TP_ROWS keeps the listed row
+// ranges of a matrix (in order), SNL_TP_COLS one column range, SNL_TP_ELEMS the listed
+// element ranges of an f32 vector, SNL_TP_FULL the whole tensor.
+int tp_plan(const snl_model_config& c, size_t r, size_t N, const std::string& nm, int* kind,
+            std::vector<RowRange>* rs) {
+  rs->clear();
+  *kind = SNL_TP_FULL;
+  if (N <= 1 || nm == "embed" || nm.compare(0, 4, "mtp.") == 0) return SNL_OK;
+  const size_t HD = c.head_dim;
+  const size_t nq = c.n_heads / N, q0 = r * nq;  // the query heads whose o_proj columns this rank holds
+  const size_t nkv = N <= c.n_kv_heads ? c.n_kv_heads / N : 1;
+  const size_t G = c.n_heads / c.n_kv_heads;
+  const size_t kv0 = N <= c.n_kv_heads ? r * nkv : q0 / G;
+  // With more ranks than KV heads, a rank computes the attention of its whole GQA group
+  // (G query heads over one KV head) and keeps its nq heads' share for o_proj.
+  const size_t aq = N <= c.n_kv_heads ? nq : G, aq0 = N <= c.n_kv_heads ? q0 : kv0 * G;
+  const size_t q_dim = (size_t)c.n_heads * HD, kv_dim = (size_t)c.n_kv_heads * HD;
+  const size_t nk = c.lin_k_heads / N, nv = c.lin_v_heads / N, k0 = r * nk, v0 = r * nv;
+  const size_t key_dim = (size_t)c.lin_k_heads * c.lin_k_dim, cdim = snl_synth::conv_dim(c);
+  const size_t DKh = c.lin_k_dim, DVh = c.lin_v_dim;
+  const size_t Il = c.intermediate / N, I = c.intermediate, vl = c.vocab / N;
+  if (ends_with(nm, ".qkv")) {
+    *kind = SNL_TP_ROWS;
+    *rs = {{aq0 * 2 * HD, aq * 2 * HD}, {2 * q_dim + kv0 * HD, nkv * HD}, {2 * q_dim + kv_dim + kv0 * HD, nkv * HD}};
+  } else if (ends_with(nm, ".in_proj")) {
+    const size_t zb = cdim, bb = cdim + (size_t)c.lin_v_heads * DVh, ab = bb + c.lin_v_heads;
+    *kind = SNL_TP_ROWS;
+    *rs = {{k0 * DKh, nk * DKh}, {key_dim + k0 * DKh, nk * DKh}, {2 * key_dim + v0 * DVh, nv * DVh},
+           {zb + v0 * DVh, nv * DVh}, {bb + v0, nv}, {ab + v0, nv}};
+  } else if (ends_with(nm, ".gate_up")) {
+    *kind = SNL_TP_ROWS;
+    *rs = {{r * Il, Il}, {I + r * Il, Il}};
+  } else if (nm == "lm_head") {
+    *kind = SNL_TP_ROWS;
+    *rs = {{r * vl, vl}};
+  } else if (ends_with(nm, ".o_proj")) {
+    *kind = SNL_TP_COLS;
+    *rs = {{q0 * HD, nq * HD}};
+  } else if (ends_with(nm, ".out_proj")) {
+    *kind = SNL_TP_COLS;
+    *rs = {{v0 * DVh, nv * DVh}};
+  } else if (ends_with(nm, ".down")) {
+    *kind = SNL_TP_COLS;
+    *rs = {{r * Il, Il}};
+  } else if (ends_with(nm, ".lin")) {
+    // conv w [conv_dim][4] | A_log [n_v] | dt_bias [n_v] | norm w [128] (linear.wgsl bindings)
+    const size_t tail = cdim * 4;
+    *kind = SNL_TP_ELEMS;
+    *rs = {{k0 * DKh * 4, nk * DKh * 4},        {(key_dim + k0 * DKh) * 4, nk * DKh * 4},
+           {(2 * key_dim + v0 * DVh) * 4, nv * DVh * 4}, {tail + v0, nv},
+           {tail + c.lin_v_heads + v0, nv},     {tail + 2 * (size_t)c.lin_v_heads, DVh}};
+  }
+  return SNL_OK;
+}
+
+// Replaces every tensor by this rank's shard (the global shapes were checked before).
+int shard_weights(snl_engine* e) {
+  const size_t N = (size_t)e->tp.size, r = (size_t)e->tp.rank;
+  std::vector<RowRange> rs;
+  int kind = 0;
+  for (auto& kv : e->qw) {
+    SNL_TRY(tp_plan(e->cfg, r, N, kv.first, &kind, &rs));
+    if (kind == SNL_TP_ROWS) SNL_TRY(shard_rows(e, kv.second, rs));
+    else if (kind == SNL_TP_COLS) SNL_TRY(shard_cols(e, kv.second, rs[0].a, rs[0].n));
+  }
+  for (auto& kv : e->fv) {
+    SNL_TRY(tp_plan(e->cfg, r, N, kv.first, &kind, &rs));
+    if (kind == SNL_TP_ELEMS) SNL_TRY(shard_f32(e, kv.second, rs));
+  }
+  return SNL_OK;
+}
+
+}  // namespace
+
+extern "C" int snl_engine_create_tp(const snl_model_config* cfg, size_t ctx, int device, uint32_t flags, int tp_rank,
+                                    int tp_size, snl_engine** out) {
+  if (!out) return fail(SNL_E_INVALID, "snl_engine_create_tp: null out");
+  *out = nullptr;
+  if (tp_size < 1 || tp_size > snl::kTpMax || (tp_size & (tp_size - 1)) || tp_rank < 0 || tp_rank >= tp_size)
+    return fail(SNL_E_INVALID, "snl_engine_create_tp: tp_size must be 1, 2, 4 or 8 and 0 <= tp_rank < tp_size");
+  if (int rc = snl_config_validate(cfg)) return rc;
+  const uint32_t N = (uint32_t)tp_size;
+  if (cfg->n_heads % N || cfg->lin_k_heads % N || cfg->lin_v_heads % N || cfg->intermediate % (32 * N) ||
+      cfg->vocab % N || (N > cfg->n_kv_heads && N % cfg->n_kv_heads) ||
+      (N > cfg->n_kv_heads && (cfg->n_heads / cfg->n_kv_heads) % (cfg->n_heads / N)))
+    return fail(SNL_E_UNSUPPORTED, "tensor parallel: heads, intermediate and vocab must divide by tp_size");
+  snl_engine* e = nullptr;
+  SNL_TRY(snl_engine_create(cfg, ctx, device, flags, &e));
+  if (tp_size == 1) {
+    *out = e;
+    return SNL_OK;
+  }
+  DeviceGuard dg(device);
+  e->tp.rank = tp_rank;
+  e->tp.size = tp_size;
+  e->lc.n_heads = N <= cfg->n_kv_heads ? cfg->n_heads / N : cfg->n_heads / cfg->n_kv_heads;
+  e->lc.n_kv_heads = N <= cfg->n_kv_heads ? cfg->n_kv_heads / N : 1;
+  e->lc.lin_k_heads = cfg->lin_k_heads / N;
+  e->lc.lin_v_heads = cfg->lin_v_heads / N;
+  e->lc.intermediate = cfg->intermediate / N;
+  e->vocab_l = cfg->vocab / N;
+  // The exchange region: flags, GEMV partials, bulk partials, argmax keys, LM-head shard.
+  const size_t h = cfg->hidden;
+  auto al = [](size_t v) { return (v + 255) / 256 * 256; };
+  TpHost& t = e->tp;
+  t.off_flags = 0;
+  t.off_gparts = al(t.off_flags + (size_t)snl::kTpSlots * snl::kTpMax * 8);
+  t.off_bparts = al(t.off_gparts + 2 * 4 * h * sizeof(float));
+  t.off_keys = al(t.off_bparts + 2 * MAX_M * h * sizeof(float));
+  t.off_logits = al(t.off_keys + LOGIT_ROWS * snl::kTpMax * 8);
+  t.region_bytes = al(t.off_logits + LOGIT_ROWS * (size_t)e->vocab_l * sizeof(float));
+  cudaError_t ce = cudaMalloc(&t.region, t.region_bytes);
+  if (ce == cudaSuccess) ce = cudaMemset(t.region, 0, t.region_bytes);
+  if (ce != cudaSuccess) {
+    snl_engine_destroy(e);
+    return cuda_fail(ce, "tensor parallel: exchange region");
+  }
+  e->bytes += t.region_bytes;
+  t.peer_base[tp_rank] = t.region;
+  *out = e;
+  return SNL_OK;
+}
+
+extern "C" int snl_tp_plan(const snl_model_config* cfg, int tp_rank, int tp_size, const char* name, int* kind,
+                           size_t* ranges, size_t cap, size_t* n_ranges) {
+  if (!cfg || !name || !kind || !n_ranges) return fail(SNL_E_INVALID, "snl_tp_plan: null argument");
+  if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size) return fail(SNL_E_INVALID, "snl_tp_plan: bad rank");
+  std::vector<RowRange> rs;
+  SNL_TRY(tp_plan(*cfg, (size_t)tp_rank, (size_t)tp_size, name, kind, &rs));
+  *n_ranges = rs.size();
+  if (rs.size() > cap || (!ranges && !rs.empty())) return fail(SNL_E_RANGE, "snl_tp_plan: ranges buffer too small");
+  for (size_t i = 0; i < rs.size(); i++) {
+    ranges[2 * i] = rs[i].a;
+    ranges[2 * i + 1] = rs[i].n;
+  }
+  return SNL_OK;
+}
+
+extern "C" int snl_engine_tp_handle(snl_engine* e, void* handle_out) {
+  if (!e || !handle_out) return fail(SNL_E_INVALID, "snl_engine_tp_handle: null argument");
+  if (e->tp.size < 2) return fail(SNL_E_STATE, "snl_engine_tp_handle: not a tensor parallel engine");
+  DeviceGuard dg(e->device);
+  cudaIpcMemHandle_t hd;
+  SNL_CUDA_TRY(cudaIpcGetMemHandle(&hd, e->tp.region));
+  memcpy(handle_out, &hd, sizeof(hd));
+  return SNL_OK;
+}
+
+extern "C" int snl_engine_tp_connect(snl_engine* e, const void* handles) {
+  if (!e || !handles) return fail(SNL_E_INVALID, "snl_engine_tp_connect: null argument");
+  if (e->tp.size < 2) return fail(SNL_E_STATE, "snl_engine_tp_connect: not a tensor parallel engine");
+  if (e->tp.connected) return SNL_OK;
+  DeviceGuard dg(e->device);
+  const uint8_t* hs = static_cast<const uint8_t*>(handles);
+  for (int q = 0; q < e->tp.size; q++) {
+    if (q == e->tp.rank) continue;
+    cudaIpcMemHandle_t hd;
+    memcpy(&hd, hs + (size_t)q * SNL_TP_HANDLE_BYTES, sizeof(hd));
+    void* p = nullptr;
+    cudaError_t ce = cudaIpcOpenMemHandle(&p, hd, cudaIpcMemLazyEnablePeerAccess);
+    if (ce != cudaSuccess) return cuda_fail(ce, "tensor parallel: cudaIpcOpenMemHandle");
+    e->tp.peer_base[q] = p;
+  }
+  e->tp.connected = true;
   return SNL_OK;
 }
 
@@ -714,12 +1016,12 @@ extern "C" int snl_engine_finalize(snl_engine* e) {
   if (!e) return fail(SNL_E_INVALID, "null engine");
   if (e->finalized) return SNL_OK;
   DeviceGuard dg(e->device);
-  const auto& c = e->cfg;
+  const auto& c = e->lc;  // this rank's shard of the model
   const size_t h = c.hidden, I = c.intermediate;
   // Every tensor the op graph binds must be present (WeightFile::info, weights.rs:108-113).
   std::string missing;
   snl_synth::for_each_tensor(
-      c, e->has_mtp, SNL_Q8_0,
+      e->cfg, e->has_mtp, SNL_Q8_0,
       [&](const std::string& name, int, size_t rows, size_t cols) {
         auto it = e->qw.find(name);
         if (it == e->qw.end()) {
@@ -739,6 +1041,11 @@ extern "C" int snl_engine_finalize(snl_engine* e) {
         }
       });
   if (!missing.empty()) return fail(SNL_E_INVALID, "weight file is missing tensor `" + missing + "`");
+  if (e->tp.size > 1) {
+    if (!e->tp.connected) return fail(SNL_E_STATE, "tensor parallel engine: snl_engine_tp_connect first");
+    if (e->has_mtp) return fail(SNL_E_UNSUPPORTED, "tensor parallel engine: MTP is not supported");
+    SNL_TRY(shard_weights(e));
+  }
   // Tile-layout copies for the decode GEMV (embed is only gathered, not multiplied).
   if (!getenv("SNL_NO_TILES")) {
     for (auto& kv : e->qw) {
@@ -823,6 +1130,31 @@ extern "C" int snl_engine_finalize(snl_engine* e) {
   SNL_CUDA_TRY(cudaMallocHost(&e->h_step, sizeof(snl_step_u)));
   SNL_CUDA_TRY(cudaMallocHost(&e->h_logits, LOGIT_ROWS * (size_t)c.vocab * sizeof(float)));
   SNL_CUDA_TRY(cudaMallocHost(&e->h_amax, LOGIT_ROWS * sizeof(uint32_t)));
+  SNL_TRY(dalloc(e, &e->step_ctr, 1));
+  e->tp_sites = (uint32_t)(2 * e->plan.size() + 2);
+  e->head_out = e->logits;
+  if (e->tp.size > 1) {
+    SNL_TRY(dalloc(e, &e->logits_full, LOGIT_ROWS * (size_t)e->cfg.vocab));
+    int* err = nullptr;
+    SNL_TRY(device_error_word(&err));
+    snl::TpComm& cm = e->tp.comm;
+    cm.rank = e->tp.rank;
+    cm.size = e->tp.size;
+    for (int q = 0; q < e->tp.size; q++) {
+      uint8_t* b = static_cast<uint8_t*>(e->tp.peer_base[q]);
+      cm.flags[q] = reinterpret_cast<uint64_t*>(b + e->tp.off_flags);
+      cm.gparts[q] = reinterpret_cast<float*>(b + e->tp.off_gparts);
+      cm.bparts[q] = reinterpret_cast<float*>(b + e->tp.off_bparts);
+      cm.keys[q] = reinterpret_cast<unsigned long long*>(b + e->tp.off_keys);
+      cm.logits[q] = reinterpret_cast<float*>(b + e->tp.off_logits);
+    }
+    cm.gp_rows = (uint32_t)h;
+    cm.bp_elems = MAX_M * h;
+    cm.step = e->step_ctr;
+    cm.sites = e->tp_sites;
+    cm.err = err;
+    e->head_out = cm.logits[e->tp.rank];
+  }
   SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));
   e->finalized = true;
   e->pos = 0;
@@ -838,6 +1170,9 @@ extern "C" void snl_engine_destroy(snl_engine* e) {
     for (auto& kv : e->graphs)
       if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
     for (void* p : e->allocs) cudaFree(p);
+    for (int q = 0; q < e->tp.size; q++)
+      if (q != e->tp.rank && e->tp.peer_base[q]) cudaIpcCloseMemHandle(e->tp.peer_base[q]);
+    if (e->tp.region) cudaFree(e->tp.region);
     if (e->h_tokens) cudaFreeHost(e->h_tokens);
     if (e->h_rpos) cudaFreeHost(e->h_rpos);
     if (e->h_step) cudaFreeHost(e->h_step);
@@ -859,7 +1194,8 @@ extern "C" int snl_engine_forward_mm(snl_engine* e, const uint32_t* tokens, size
   SNL_TRY(forward_impl(e, tokens, n, pos, embed_idx, embeds, n_embeds, logit_rows, ckpt, false, &rows));
   if (rows) {
     const size_t nbytes = rows * e->cfg.vocab * sizeof(float);
-    SNL_CUDA_TRY(cudaMemcpyAsync(e->h_logits, e->logits, nbytes, cudaMemcpyDeviceToHost, e->stream));
+    const float* src = e->tp.size > 1 ? e->logits_full : e->head_out;
+    SNL_CUDA_TRY(cudaMemcpyAsync(e->h_logits, src, nbytes, cudaMemcpyDeviceToHost, e->stream));
     SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));
     memcpy(logits_out, e->h_logits, nbytes);
   } else {

@@ -656,6 +656,56 @@ __device__ __forceinline__ void group_finish(const GemvArgs& a, uint32_t grp, ui
     }
     return;
   }
+  if (a.tp.size > 1) {
+    // Row-parallel projection: publish this rank's partials of the group, signal the
+    // group's flag slot to every rank, wait for the peers' signals, then merge the sum
+    // of all ranks' partials in rank order (identical on every rank).
+    const uint64_t epoch = tp_epoch(a.tp, a.tp_site);
+    const uint64_t par = (epoch & 1) * 4ull * a.tp.gp_rows;
+#pragma unroll
+    for (int pass = 0; pass < (M + 1) / 2; pass++) {
+      const int tt = pass * 2 + lane / 16, r = lane % 16;
+      const uint32_t row = grp * 16 + r;
+      if (tt < M && row < a.n) a.tp.gparts[a.tp.rank][par + (uint64_t)tt * a.tp.gp_rows + row] = val(tt, r);
+    }
+    __threadfence_system();
+    __syncwarp();
+    if (lane == 0) tp_signal(a.tp, grp, epoch);
+    bool ok = true;
+    if (lane < a.tp.size && lane != a.tp.rank) ok = tp_wait_one(a.tp, grp, lane, epoch);
+    ok = __all_sync(0xffffffffu, ok);
+#pragma unroll
+    for (int pass = 0; pass < (M + 1) / 2; pass++) {
+      const int tt = pass * 2 + lane / 16, r = lane % 16;
+      const uint32_t row = grp * 16 + r;
+      const bool live = tt < M && row < a.n;
+      float2 nx = make_float2(0.f, 0.f);
+      if (live && ok) {
+        float v = 0.f;
+        for (int q = 0; q < a.tp.size; q++) v += ld_cv(a.tp.gparts[q] + par + (uint64_t)tt * a.tp.gp_rows + row);
+        nx = gemv_epilogue(a, tt, row, v * kXPlaneScale);
+      }
+      if (a.rnext) {
+        float rs[9];
+        const uint32_t d = 2 * a.h;
+#pragma unroll
+        for (int o = 0; o < 8; o++)
+          rs[o] = live ? fmaf(__ldg(a.rnext + (uint64_t)o * d + row), nx.x, __ldg(a.rnext + (uint64_t)o * d + a.h + row) * nx.y)
+                       : 0.f;
+        rs[8] = live ? fmaf(nx.x, nx.x, nx.y * nx.y) : 0.f;
+#pragma unroll
+        for (int o = 0; o < 9; o++) {
+#pragma unroll
+          for (int off = 8; off > 0; off >>= 1) rs[o] += __shfl_xor_sync(0xffffffffu, rs[o], off);
+        }
+        if (r == 0 && tt < M) {
+#pragma unroll
+          for (int o = 0; o < 9; o++) a.rpart[((uint64_t)tt * groups + grp) * 9 + o] = rs[o];
+        }
+      }
+    }
+    return;
+  }
 #pragma unroll
   for (int pass = 0; pass < (M + 1) / 2; pass++) {
     const int tt = pass * 2 + lane / 16, r = lane % 16;

@@ -3,6 +3,7 @@
 #include <cuda_fp16.h>
 
 #include "common.cuh"
+#include "tp.cuh"
 
 namespace snl {
 
@@ -46,6 +47,11 @@ struct GemvArgs {
   // (act_stride halves per plane) and, if y is set, act itself at y[t * y_stride + i].
   __half* act_planes;
   uint32_t act_stride;
+  // mode 1 under tensor parallelism (tp.size > 1): the dot is this rank's partial over
+  // its K shard; each finished group trades partials with the peers (exchange site
+  // tp_site, flag slot = group) and merges the rank-ordered sum.
+  TpComm tp;
+  uint32_t tp_site;
 };
 
 // Returns the merged (x0, x1) of element n (mode 1), for the router partials.

@@ -7,6 +7,7 @@
 #include "common.cuh"
 #include "ptx.cuh"
 #include "synth.h"
+#include "tp.cuh"
 
 namespace snl {
 namespace {
@@ -406,14 +407,61 @@ __global__ void argmax_pass2(const unsigned long long* __restrict__ part, uint32
   if (threadIdx.x == 0) out[row] = ~(uint32_t)(best & 0xFFFFFFFFull);
 }
 
+// Tensor-parallel pass 2: the row's best key over this rank's vocabulary shard, rebased
+// to the global index, is written into every rank's key slot; after the exchange each
+// rank takes the largest key, so all ranks agree on the token (first index on ties).
+// With rows == 0 the CTA only takes part in the exchange.
+__global__ void argmax_tp_pass2(const unsigned long long* __restrict__ part, uint32_t nparts, uint32_t rows,
+                                uint32_t vl, TpComm c, uint32_t site, uint32_t* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  const uint32_t row = blockIdx.x;
+  const uint64_t epoch = tp_epoch(c, site);
+  const uint32_t slot = kSlotKeys - row;
+  unsigned long long best = 0;
+  if (row < rows) {
+    for (uint32_t i = threadIdx.x; i < nparts; i += 32) {
+      const unsigned long long k = part[(uint64_t)row * nparts + i];
+      best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
+      best = t > best ? t : best;
+    }
+  }
+  if (threadIdx.x == 0) {
+    if (row < rows) {
+      const uint32_t gidx = (uint32_t)c.rank * vl + ~(uint32_t)(best & 0xFFFFFFFFull);
+      const unsigned long long key = (best & 0xFFFFFFFF00000000ull) | (unsigned long long)(~gidx);
+      for (int q = 0; q < c.size; q++) c.keys[q][(uint64_t)row * kTpMax + c.rank] = key;
+    }
+    tp_signal(c, slot, epoch);
+    bool ok = true;
+    for (int q = 0; q < c.size; q++)
+      if (q != c.rank) ok &= tp_wait_one(c, slot, q, epoch);
+    if (row < rows && ok) {
+      unsigned long long g = 0;
+      for (int q = 0; q < c.size; q++) {
+        const unsigned long long k = ld_cv_u64(c.keys[c.rank] + (uint64_t)row * kTpMax + q);
+        g = k > g ? k : g;
+      }
+      out[row] = ~(uint32_t)(g & 0xFFFFFFFFull);
+    }
+  }
+}
+
 // Embedding rows (engine.rs:777-790): stream 0 = q * s of the token's Q8_0 row,
 // stream 1 = 0. Ids >= vocab raise err_flag and write zeros (the host checks first).
 __global__ void embed_kernel(const uint32_t* __restrict__ toks, uint32_t h, uint32_t vocab,
                              const int8_t* __restrict__ q, const float* __restrict__ s, float* __restrict__ x,
-                             int* __restrict__ err) {
+                             int* __restrict__ err, unsigned long long* __restrict__ step_ctr) {
   pdl_trigger();
   pdl_wait();
   const uint32_t m = blockIdx.x;
+  // The embedding is the first kernel of every step: it advances the step counter that
+  // numbers the step's tensor-parallel exchanges.
+  if (step_ctr && m == 0 && threadIdx.x == 0) *step_ctr += 1;
   const uint32_t t = toks[m];
   const bool ok = t < vocab;
   if (!ok && threadIdx.x == 0 && err) *err = 1;
@@ -553,6 +601,15 @@ int launch_argmax_with(const float* logits, uint32_t rows, uint32_t n, uint32_t*
   return SNL_OK;
 }
 
+int launch_argmax_tp(const float* logits, uint32_t rows, uint32_t vl, uint32_t* out_idx, unsigned long long* part,
+                     const TpComm& c, uint32_t site, cudaStream_t s) {
+  if (rows > 0)
+    SNL_PDL_LAUNCH("argmax_pass1", argmax_pass1, dim3(dim3(kArgBlocks, rows)), dim3(512), (size_t)(0), s, logits, vl, part);
+  SNL_PDL_LAUNCH("argmax_tp_pass2", argmax_tp_pass2, dim3(std::max(rows, 1u)), dim3(32), (size_t)(0), s, part, kArgBlocks,
+                 rows, vl, c, site, out_idx);
+  return SNL_OK;
+}
+
 int launch_argmax(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_idx, cudaStream_t s) {
   unsigned long long* part = argmax_scratch(rows);
   if (!part) return fail(SNL_E_OOM, "argmax: scratch allocation failed");
@@ -560,9 +617,10 @@ int launch_argmax(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_
 }
 
 int launch_embed(const uint32_t* tokens, uint32_t m, const int8_t* q, const float* s_, uint32_t h, uint32_t vocab,
-                 float* x, int* err_flag, cudaStream_t s) {
+                 float* x, int* err_flag, cudaStream_t s, unsigned long long* step_ctr) {
   if (m == 0) return SNL_OK;
-  SNL_PDL_LAUNCH("embed_kernel", embed_kernel, dim3(m), dim3(256), (size_t)(0), s, tokens, h, vocab, q, s_, x, err_flag);
+  SNL_PDL_LAUNCH("embed_kernel", embed_kernel, dim3(m), dim3(256), (size_t)(0), s, tokens, h, vocab, q, s_, x, err_flag,
+                 step_ctr);
   return SNL_OK;
 }
 

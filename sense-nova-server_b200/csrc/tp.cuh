@@ -1,0 +1,113 @@
+// Tensor parallelism over NVLink peer memory (one process per GPU, Megatron split).
+//
+// Each rank allocates one region of device memory and exports it with a CUDA IPC handle;
+// every rank maps every peer's region. The region holds:
+//   flags[slot][src]  u64, the epoch at which rank `src` last signalled `slot`
+//                     (written by the peer with a system-scope release store);
+//   gemv parts        [2 parities][4 tokens][rows] f32: a row-parallel GEMV's partial
+//                     sums, read by the peers' same GEMV;
+//   bulk parts        [2 parities][MAX_M * hidden] f32: the prefill allreduce's input;
+//   keys              [src] u64: the greedy argmax candidates;
+//   logits            [2 rows][vocab / N] f32: this rank's LM-head shard.
+// An exchange at site s of step t uses epoch t * sites + s + 1, so flags only grow and
+// never need resetting. Data buffers alternate by epoch parity: a rank rewrites a buffer
+// two exchanges later, and by then every peer has signalled the exchange in between,
+// which it does only after it has finished reading. Every wait is bounded by clock64;
+// one that runs out sets bit 1 of the device error word and the kernel carries on.
+#pragma once
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace snl {
+
+constexpr int kTpMax = 8;
+constexpr uint32_t kTpSlots = 1024;  // flag slots per rank (>= row groups of a 4096-row GEMV)
+constexpr long long kTpWaitCycles = 4000000000LL;
+
+// Device view of the communicator (passed by value to kernels).
+struct TpComm {
+  int rank = 0, size = 1;
+  uint64_t* flags[kTpMax] = {};     // each rank's flag array, [kTpSlots][kTpMax]
+  float* gparts[kTpMax] = {};       // each rank's GEMV partials, [2][4][gp_rows]
+  float* bparts[kTpMax] = {};       // each rank's bulk partials, [2][bp_elems]
+  unsigned long long* keys[kTpMax] = {};  // each rank's argmax key slots, [2 rows][kTpMax]
+  float* logits[kTpMax] = {};       // each rank's LM-head shard, [2][vocab_local]
+  uint32_t gp_rows = 0;
+  uint64_t bp_elems = 0;
+  const unsigned long long* step = nullptr;  // device step counter (this rank)
+  uint32_t sites = 1;                        // exchanges per step
+  int* err = nullptr;
+};
+
+__device__ __forceinline__ uint64_t tp_epoch(const TpComm& c, uint32_t site) {
+  return *(volatile const unsigned long long*)c.step * c.sites + site + 1;
+}
+
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ float ld_cv(const float* p) {
+  float v;
+  asm volatile("ld.global.cv.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long ld_cv_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.global.cv.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Signal `slot` at `epoch` to every rank (including this one). Call after this thread's
+// data stores, from one thread; preceded by a system-scope fence.
+__device__ __forceinline__ void tp_signal(const TpComm& c, uint32_t slot, uint64_t epoch) {
+  __threadfence_system();
+  for (int q = 0; q < c.size; q++) st_release_sys(c.flags[q] + (uint64_t)slot * kTpMax + c.rank, epoch);
+}
+
+// Wait until rank `src` has signalled `slot` at `epoch` or later. False if the bound ran out.
+__device__ __forceinline__ bool tp_wait_one(const TpComm& c, uint32_t slot, int src, uint64_t epoch) {
+  const uint64_t* f = c.flags[c.rank] + (uint64_t)slot * kTpMax + src;
+  if (ld_acquire_sys(f) >= epoch) return true;
+  const long long t0 = clock64();
+  while (ld_acquire_sys(f) < epoch) {
+    if (clock64() - t0 > kTpWaitCycles) {
+      atomicOr(c.err, 2);
+      return false;
+    }
+  }
+  return true;
+}
+
+// Host side.
+struct TpHost {
+  int rank = 0, size = 1;
+  void* region = nullptr;       // this rank's exported region
+  size_t region_bytes = 0;
+  void* peer_base[kTpMax] = {};  // mapped regions (own at [rank])
+  bool connected = false;
+  // offsets inside a region
+  size_t off_flags = 0, off_gparts = 0, off_bparts = 0, off_keys = 0, off_logits = 0;
+  TpComm comm;
+};
+
+// Flag slots: [0, row groups) for the row-parallel GEMVs, then these (from the top).
+constexpr uint32_t kSlotBulk = kTpSlots - 1;
+constexpr uint32_t kSlotLogits = kTpSlots - 2;
+constexpr uint32_t kSlotKeys = kTpSlots - 3;  // minus the logits row
+
+// Exchange kernels (tp.cu).
+// Sums every rank's bulk partial [n] (parity of the site's epoch) in rank order into out.
+int launch_tp_allreduce(const TpComm& c, uint32_t site, uint64_t n, float* out, cudaStream_t s);
+// Copies every rank's LM-head shard [rows][vl] into full[rows][vl * size].
+int launch_tp_gather_logits(const TpComm& c, uint32_t site, uint32_t rows, uint32_t vl, float* full, cudaStream_t s);
+// Greedy argmax over an LM-head shard [rows][vl] agreed by all ranks (layers.cu).
+int launch_argmax_tp(const float* logits, uint32_t rows, uint32_t vl, uint32_t* out_idx, unsigned long long* part,
+                     const TpComm& c, uint32_t site, cudaStream_t s);
+
+}  // namespace snl

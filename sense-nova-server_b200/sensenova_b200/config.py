@@ -158,3 +158,18 @@ def small() -> ModelConfig:
         loop_start=2, loop_end=6, loop_count=2, mhc=MhcConfig(start=2, end=6, streams=2, iterations=20),
         mrope_section=[11, 11, 10], max_position=262144,
     )
+
+
+def tp_test() -> ModelConfig:
+    """A reduced model whose head counts and sizes divide by 8 (the 9B shape's 16 Q / 4
+    KV heads and 16 / 32 DeltaNet heads, narrower layers), so tensor parallelism over
+    2, 4 and 8 GPUs can be checked against the CPU restatement."""
+    n = 8
+    return ModelConfig(
+        hidden=512, intermediate=2048, vocab=8192, n_layers=n,
+        full_attention=[(i + 1) % 4 == 0 for i in range(n)],
+        n_heads=16, n_kv_heads=4, head_dim=256, rot_dim=64, rope_theta=1e7,
+        lin_k_heads=16, lin_v_heads=32, lin_k_dim=128, lin_v_dim=128, conv_kernel=4, eps=1e-6,
+        loop_start=2, loop_end=6, loop_count=2, mhc=MhcConfig(start=2, end=6, streams=2, iterations=20),
+        mrope_section=[11, 11, 10], max_position=262144,
+    )

@@ -26,26 +26,57 @@ def _u32(a) -> np.ndarray:
     return np.ascontiguousarray(np.asarray(a, dtype=np.uint32))
 
 
+def gather_tp_handles(rank: int, size: int, mine: bytes, group) -> bytes:
+    """All-gathers every rank's exchange-region handle over torch.distributed and returns
+    them concatenated in rank order (what snl_engine_tp_connect takes)."""
+    import torch.distributed as dist
+
+    handles: list = [None] * size
+    dist.all_gather_object(handles, (rank, mine), group=group)
+    by_rank = dict(handles)
+    if sorted(by_rank) != list(range(size)):
+        raise ffi.SnlError(ffi.SNL_E_INVALID, "tensor parallel: ranks of the group do not match tp")
+    return b"".join(by_rank[r] for r in range(size))
+
+
 class Engine:
     """One model on one GPU. Not thread-safe (one owner thread, like the reference)."""
 
-    def __init__(self, cfg: ModelConfig, ctx: int, *, device: int = 0, mtp: bool = False, flags: int = 0):
+    def __init__(self, cfg: ModelConfig, ctx: int, *, device: int = 0, mtp: bool = False, flags: int = 0,
+                 tp: tuple[int, int] | None = None, tp_group=None):
+        """tp = (rank, size) builds one tensor-parallel shard; every rank of the group
+        constructs its Engine with the same arguments (one process per GPU), and the
+        ranks' exchange handles are all-gathered over `tp_group` (a torch.distributed
+        process group; None = the default group)."""
         self.lib = ffi.load()
         self.cfg = cfg
         self._h = C.c_void_p()
         cc = cfg.to_c()
         fl = flags | (ffi.SNL_ENGINE_MTP if mtp else 0)
-        ffi.check(self.lib.snl_engine_create(C.byref(cc), ctx, device, fl, C.byref(self._h)))
+        self.tp = tp if tp is not None else (0, 1)
+        if self.tp[1] > 1:
+            ffi.check(self.lib.snl_engine_create_tp(C.byref(cc), ctx, device, fl, self.tp[0], self.tp[1],
+                                                    C.byref(self._h)))
+            self._tp_connect(tp_group)
+        else:
+            ffi.check(self.lib.snl_engine_create(C.byref(cc), ctx, device, fl, C.byref(self._h)))
         self.quant = "q8_0"
         self.device = device
+
+    def _tp_connect(self, group) -> None:
+        buf = (C.c_uint8 * ffi.SNL_TP_HANDLE_BYTES)()
+        ffi.check(self.lib.snl_engine_tp_handle(self._h, C.cast(buf, C.c_void_p)))
+        allh = gather_tp_handles(self.tp[0], self.tp[1], bytes(buf), group)
+        arr = (C.c_uint8 * len(allh)).from_buffer_copy(allh)
+        ffi.check(self.lib.snl_engine_tp_connect(self._h, C.cast(arr, C.c_void_p)))
 
     # ---- construction -------------------------------------------------------------
 
     @classmethod
     def synthetic(cls, cfg: ModelConfig, ctx: int, seed: int = 0, quant: str = "q8_0", *, mtp: bool = False,
-                  device: int = 0, flags: int = 0) -> "Engine":
+                  device: int = 0, flags: int = 0, tp: tuple[int, int] | None = None, tp_group=None) -> "Engine":
         """The seeded random-init model of the benchmarks, generated on the device."""
-        e = cls(cfg, ctx, device=device, mtp=mtp, flags=flags)
+        e = cls(cfg, ctx, device=device, mtp=mtp, flags=flags, tp=tp, tp_group=tp_group)
         q = {"q8_0": ffi.SNL_Q8_0, "q4_0": ffi.SNL_Q4_0}[quant]
         ffi.check(e.lib.snl_engine_fill_synthetic(e._h, seed, q))
         ffi.check(e.lib.snl_engine_finalize(e._h))

@@ -18,6 +18,8 @@ ERRORS = {
     -1: "SNL_E_INVALID", -2: "SNL_E_RANGE", -3: "SNL_E_CUDA", -4: "SNL_E_OOM",
     -5: "SNL_E_STATE", -6: "SNL_E_TIMEOUT", -7: "SNL_E_UNSUPPORTED", -8: "SNL_E_NCCL",
 }
+SNL_TP_HANDLE_BYTES = 64
+SNL_TP_FULL, SNL_TP_ROWS, SNL_TP_COLS, SNL_TP_ELEMS = 0, 1, 2, 3
 SNL_ENGINE_MTP = 1
 SNL_ENGINE_F16_SCALES = 2
 MAX_LAYERS = 256
@@ -113,6 +115,10 @@ SIGNATURES = {
     "snl_synth_quant": (i32, [u64, C.c_char_p, i32, sz, sz, vp, vp, vp]),
     "snl_synth_f32": (i32, [u64, C.c_char_p, u32, sz, C.c_float, C.c_float, vp, vp]),
     "snl_engine_create": (i32, [P(ModelConfigC), sz, i32, u32, P(vp)]),
+    "snl_engine_create_tp": (i32, [P(ModelConfigC), sz, i32, u32, i32, i32, P(vp)]),
+    "snl_engine_tp_handle": (i32, [vp, vp]),
+    "snl_tp_plan": (i32, [P(ModelConfigC), i32, i32, C.c_char_p, P(i32), P(sz), sz, P(sz)]),
+    "snl_engine_tp_connect": (i32, [vp, vp]),
     "snl_engine_set_tensor": (i32, [vp, C.c_char_p, i32, sz, sz, vp, vp]),
     "snl_engine_fill_synthetic": (i32, [vp, u64, i32]),
     "snl_engine_finalize": (i32, [vp]),
