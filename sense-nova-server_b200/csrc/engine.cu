@@ -477,18 +477,18 @@ int device_step(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid, uint
                   (uint32_t)((m - rows + 1) * h)));
     }
   }
-  if (e->tp.size > 1) {
-    // Two exchanges close every step (the site count stays even and fixed): the logits
-    // shards are gathered when the caller wants logits, and the greedy token is the
-    // largest of the ranks' shard maxima (first index on ties, as one scan would find).
+  if (e->tp.size > 1 && rows > 0) {
+    // The last two exchange sites of a step: the logits shards are gathered when the
+    // caller wants logits; the greedy token is the largest of the ranks' shard maxima
+    // (first index on ties, as one scan of the whole row would find).
     const uint32_t site = e->tp_sites - 2;
-    const uint32_t grows = (rows > 0 && !greedy) ? rows : 0;
-    SNL_TRY(timed(e, "TpGather", 4.0 * grows * e->cfg.vocab,
-                  [&] { return launch_tp_gather_logits(e->tp.comm, site, grows, vl, e->logits_full, e->stream); }));
-    const uint32_t krows = (rows > 0 && greedy) ? rows : 0;
-    SNL_TRY(timed(e, "Argmax", 4.0 * krows * vl, [&] {
-      return launch_argmax_tp(e->head_out, krows, vl, e->amax, e->amax_part, e->tp.comm, site + 1, e->stream);
-    }));
+    if (!greedy)
+      SNL_TRY(timed(e, "TpGather", 4.0 * rows * e->cfg.vocab,
+                    [&] { return launch_tp_gather_logits(e->tp.comm, site, rows, vl, e->logits_full, e->stream); }));
+    else
+      SNL_TRY(timed(e, "Argmax", 4.0 * rows * vl, [&] {
+        return launch_argmax_tp(e->head_out, rows, vl, e->amax, e->amax_part, e->tp.comm, site + 1, e->stream);
+      }));
   } else if (rows > 0 && greedy) {
     SNL_TRY(timed(e, "Argmax", 4.0 * rows * vl,
                   [&] { return launch_argmax_with(e->head_out, rows, vl, e->amax, e->amax_part, e->stream); }));
@@ -873,10 +873,10 @@ extern "C" int snl_engine_create_tp(const snl_model_config* cfg, size_t ctx, int
   auto al = [](size_t v) { return (v + 255) / 256 * 256; };
   TpHost& t = e->tp;
   t.off_flags = 0;
-  t.off_gparts = al(t.off_flags + (size_t)snl::kTpSlots * snl::kTpMax * 8);
-  t.off_bparts = al(t.off_gparts + 2 * 4 * h * sizeof(float));
-  t.off_keys = al(t.off_bparts + 2 * MAX_M * h * sizeof(float));
-  t.off_logits = al(t.off_keys + LOGIT_ROWS * snl::kTpMax * 8);
+  t.off_bparts = al(t.off_flags + (size_t)snl::kTpSlots * snl::kTpMax * 8);
+  t.off_ll = al(t.off_bparts + 2 * MAX_M * h * sizeof(float));
+  t.off_llkeys = al(t.off_ll + (size_t)2 * snl::kTpMax * 4 * h * 8);
+  t.off_logits = al(t.off_llkeys + LOGIT_ROWS * snl::kTpMax * 2 * 8);
   t.region_bytes = al(t.off_logits + LOGIT_ROWS * (size_t)e->vocab_l * sizeof(float));
   cudaError_t ce = cudaMalloc(&t.region, t.region_bytes);
   if (ce == cudaSuccess) ce = cudaMemset(t.region, 0, t.region_bytes);
@@ -1143,9 +1143,9 @@ extern "C" int snl_engine_finalize(snl_engine* e) {
     for (int q = 0; q < e->tp.size; q++) {
       uint8_t* b = static_cast<uint8_t*>(e->tp.peer_base[q]);
       cm.flags[q] = reinterpret_cast<uint64_t*>(b + e->tp.off_flags);
-      cm.gparts[q] = reinterpret_cast<float*>(b + e->tp.off_gparts);
       cm.bparts[q] = reinterpret_cast<float*>(b + e->tp.off_bparts);
-      cm.keys[q] = reinterpret_cast<unsigned long long*>(b + e->tp.off_keys);
+      cm.ll[q] = reinterpret_cast<unsigned long long*>(b + e->tp.off_ll);
+      cm.llkeys[q] = reinterpret_cast<unsigned long long*>(b + e->tp.off_llkeys);
       cm.logits[q] = reinterpret_cast<float*>(b + e->tp.off_logits);
     }
     cm.gp_rows = (uint32_t)h;

@@ -657,32 +657,37 @@ __device__ __forceinline__ void group_finish(const GemvArgs& a, uint32_t grp, ui
     return;
   }
   if (a.tp.size > 1) {
-    // Row-parallel projection: publish this rank's partials of the group, signal the
-    // group's flag slot to every rank, wait for the peers' signals, then merge the sum
-    // of all ranks' partials in rank order (identical on every rank).
+    // Row-parallel projection: push this rank's partials of the group into every peer's
+    // memory as tagged words, collect the peers' from this rank's memory, and merge the
+    // sum of all ranks' partials in rank order (identical on every rank).
     const uint64_t epoch = tp_epoch(a.tp, a.tp_site);
-    const uint64_t par = (epoch & 1) * 4ull * a.tp.gp_rows;
+    const uint32_t tag = (uint32_t)epoch;
+    const uint64_t par = epoch & 1;
+    const int N = a.tp.size, me = a.tp.rank;
+    float own[(M + 1) / 2];
 #pragma unroll
     for (int pass = 0; pass < (M + 1) / 2; pass++) {
       const int tt = pass * 2 + lane / 16, r = lane % 16;
       const uint32_t row = grp * 16 + r;
-      if (tt < M && row < a.n) a.tp.gparts[a.tp.rank][par + (uint64_t)tt * a.tp.gp_rows + row] = val(tt, r);
+      own[pass] = 0.f;
+      if (tt < M && row < a.n) {
+        own[pass] = val(tt, r);
+        const unsigned long long w = ll_word(tag, __float_as_uint(own[pass]));
+        for (int q = 0; q < N; q++)
+          if (q != me) st_relaxed_sys_u64(a.tp.ll[q] + ((par * kTpMax + me) * 4 + tt) * a.tp.gp_rows + row, w);
+      }
     }
-    __threadfence_system();
-    __syncwarp();
-    if (lane == 0) tp_signal(a.tp, grp, epoch);
-    bool ok = true;
-    if (lane < a.tp.size && lane != a.tp.rank) ok = tp_wait_one(a.tp, grp, lane, epoch);
-    ok = __all_sync(0xffffffffu, ok);
 #pragma unroll
     for (int pass = 0; pass < (M + 1) / 2; pass++) {
       const int tt = pass * 2 + lane / 16, r = lane % 16;
       const uint32_t row = grp * 16 + r;
       const bool live = tt < M && row < a.n;
       float2 nx = make_float2(0.f, 0.f);
-      if (live && ok) {
+      if (live) {
         float v = 0.f;
-        for (int q = 0; q < a.tp.size; q++) v += ld_cv(a.tp.gparts[q] + par + (uint64_t)tt * a.tp.gp_rows + row);
+        for (int q = 0; q < N; q++)
+          v += q == me ? own[pass]
+                       : __uint_as_float(ll_wait(a.tp, a.tp.ll[me] + ((par * kTpMax + q) * 4 + tt) * a.tp.gp_rows + row, tag));
         nx = gemv_epilogue(a, tt, row, v * kXPlaneScale);
       }
       if (a.rnext) {

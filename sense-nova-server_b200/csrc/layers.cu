@@ -408,46 +408,44 @@ __global__ void argmax_pass2(const unsigned long long* __restrict__ part, uint32
 }
 
 // Tensor-parallel pass 2: the row's best key over this rank's vocabulary shard, rebased
-// to the global index, is written into every rank's key slot; after the exchange each
-// rank takes the largest key, so all ranks agree on the token (first index on ties).
-// With rows == 0 the CTA only takes part in the exchange.
-__global__ void argmax_tp_pass2(const unsigned long long* __restrict__ part, uint32_t nparts, uint32_t rows,
-                                uint32_t vl, TpComm c, uint32_t site, uint32_t* __restrict__ out) {
+// to the global index, is pushed into every rank's memory as two tagged words; each rank
+// then takes the largest of all ranks' keys, so all agree on the token (first index on
+// ties).
+__global__ void argmax_tp_pass2(const unsigned long long* __restrict__ part, uint32_t nparts, uint32_t vl, TpComm c,
+                                uint32_t site, uint32_t* __restrict__ out) {
   pdl_trigger();
   pdl_wait();
   const uint32_t row = blockIdx.x;
-  const uint64_t epoch = tp_epoch(c, site);
-  const uint32_t slot = kSlotKeys - row;
+  const uint32_t tag = (uint32_t)tp_epoch(c, site);
   unsigned long long best = 0;
-  if (row < rows) {
-    for (uint32_t i = threadIdx.x; i < nparts; i += 32) {
-      const unsigned long long k = part[(uint64_t)row * nparts + i];
-      best = k > best ? k : best;
-    }
+  for (uint32_t i = threadIdx.x; i < nparts; i += 32) {
+    const unsigned long long k = part[(uint64_t)row * nparts + i];
+    best = k > best ? k : best;
+  }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
-      best = t > best ? t : best;
-    }
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
+    best = t > best ? t : best;
   }
   if (threadIdx.x == 0) {
-    if (row < rows) {
-      const uint32_t gidx = (uint32_t)c.rank * vl + ~(uint32_t)(best & 0xFFFFFFFFull);
-      const unsigned long long key = (best & 0xFFFFFFFF00000000ull) | (unsigned long long)(~gidx);
-      for (int q = 0; q < c.size; q++) c.keys[q][(uint64_t)row * kTpMax + c.rank] = key;
+    const uint32_t gidx = (uint32_t)c.rank * vl + ~(uint32_t)(best & 0xFFFFFFFFull);
+    const uint32_t ord = (uint32_t)(best >> 32);
+    const unsigned long long key = ((unsigned long long)ord << 32) | (unsigned long long)(~gidx);
+    for (int q = 0; q < c.size; q++) {
+      if (q == c.rank) continue;
+      unsigned long long* slot = c.llkeys[q] + ((uint64_t)row * kTpMax + c.rank) * 2;
+      st_relaxed_sys_u64(slot, ll_word(tag, ord));
+      st_relaxed_sys_u64(slot + 1, ll_word(tag, ~gidx));
     }
-    tp_signal(c, slot, epoch);
-    bool ok = true;
-    for (int q = 0; q < c.size; q++)
-      if (q != c.rank) ok &= tp_wait_one(c, slot, q, epoch);
-    if (row < rows && ok) {
-      unsigned long long g = 0;
-      for (int q = 0; q < c.size; q++) {
-        const unsigned long long k = ld_cv_u64(c.keys[c.rank] + (uint64_t)row * kTpMax + q);
-        g = k > g ? k : g;
-      }
-      out[row] = ~(uint32_t)(g & 0xFFFFFFFFull);
+    unsigned long long g = key;
+    for (int q = 0; q < c.size; q++) {
+      if (q == c.rank) continue;
+      const unsigned long long* slot = c.llkeys[c.rank] + ((uint64_t)row * kTpMax + q) * 2;
+      const uint32_t o = ll_wait(c, slot, tag), ni = ll_wait(c, slot + 1, tag);
+      const unsigned long long k = ((unsigned long long)o << 32) | ni;
+      g = k > g ? k : g;
     }
+    out[row] = ~(uint32_t)(g & 0xFFFFFFFFull);
   }
 }
 
@@ -603,10 +601,10 @@ int launch_argmax_with(const float* logits, uint32_t rows, uint32_t n, uint32_t*
 
 int launch_argmax_tp(const float* logits, uint32_t rows, uint32_t vl, uint32_t* out_idx, unsigned long long* part,
                      const TpComm& c, uint32_t site, cudaStream_t s) {
-  if (rows > 0)
-    SNL_PDL_LAUNCH("argmax_pass1", argmax_pass1, dim3(dim3(kArgBlocks, rows)), dim3(512), (size_t)(0), s, logits, vl, part);
-  SNL_PDL_LAUNCH("argmax_tp_pass2", argmax_tp_pass2, dim3(std::max(rows, 1u)), dim3(32), (size_t)(0), s, part, kArgBlocks,
-                 rows, vl, c, site, out_idx);
+  if (rows == 0) return SNL_OK;
+  SNL_PDL_LAUNCH("argmax_pass1", argmax_pass1, dim3(dim3(kArgBlocks, rows)), dim3(512), (size_t)(0), s, logits, vl, part);
+  SNL_PDL_LAUNCH("argmax_tp_pass2", argmax_tp_pass2, dim3(rows), dim3(32), (size_t)(0), s, part, kArgBlocks, vl, c, site,
+                 out_idx);
   return SNL_OK;
 }
 

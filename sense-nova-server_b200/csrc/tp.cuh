@@ -4,11 +4,16 @@
 // every rank maps every peer's region. The region holds:
 //   flags[slot][src]  u64, the epoch at which rank `src` last signalled `slot`
 //                     (written by the peer with a system-scope release store);
-//   gemv parts        [2 parities][4 tokens][rows] f32: a row-parallel GEMV's partial
-//                     sums, read by the peers' same GEMV;
 //   bulk parts        [2 parities][MAX_M * hidden] f32: the prefill allreduce's input;
-//   keys              [src] u64: the greedy argmax candidates;
+//   ll                [2 parities][src][4 tokens][rows] u64: row-parallel GEMV partials
+//                     pushed by each peer, each value tagged with its exchange's epoch;
+//   llkeys            [2 rows][src][2] u64: the greedy argmax candidates, tagged alike;
 //   logits            [2 rows][vocab / N] f32: this rank's LM-head shard.
+// The decode exchanges (GEMV partials, argmax keys) use tagged words: the writer stores
+// (epoch << 32 | value) into the peer's memory with one 64-bit system-scope store, and
+// the reader polls its own memory until the tag matches, so no fence and no remote load
+// is on the path. The bulk exchanges (prefill partials, gathered logits) publish data and
+// then a flag.
 // An exchange at site s of step t uses epoch t * sites + s + 1, so flags only grow and
 // never need resetting. Data buffers alternate by epoch parity: a rank rewrites a buffer
 // two exchanges later, and by then every peer has signalled the exchange in between,
@@ -22,16 +27,16 @@
 namespace snl {
 
 constexpr int kTpMax = 8;
-constexpr uint32_t kTpSlots = 1024;  // flag slots per rank (>= row groups of a 4096-row GEMV)
+constexpr uint32_t kTpSlots = 1024;  // flag slots per rank
 constexpr long long kTpWaitCycles = 4000000000LL;
 
 // Device view of the communicator (passed by value to kernels).
 struct TpComm {
   int rank = 0, size = 1;
   uint64_t* flags[kTpMax] = {};     // each rank's flag array, [kTpSlots][kTpMax]
-  float* gparts[kTpMax] = {};       // each rank's GEMV partials, [2][4][gp_rows]
   float* bparts[kTpMax] = {};       // each rank's bulk partials, [2][bp_elems]
-  unsigned long long* keys[kTpMax] = {};  // each rank's argmax key slots, [2 rows][kTpMax]
+  unsigned long long* ll[kTpMax] = {};      // each rank's tagged GEMV partials, [2][kTpMax][4][gp_rows]
+  unsigned long long* llkeys[kTpMax] = {};  // each rank's tagged argmax keys, [2 rows][kTpMax][2]
   float* logits[kTpMax] = {};       // each rank's LM-head shard, [2][vocab_local]
   uint32_t gp_rows = 0;
   uint64_t bp_elems = 0;
@@ -84,6 +89,33 @@ __device__ __forceinline__ bool tp_wait_one(const TpComm& c, uint32_t slot, int 
   return true;
 }
 
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long ll_word(uint32_t tag, uint32_t bits) {
+  return ((unsigned long long)tag << 32) | bits;
+}
+// Polls a tagged word of this rank's memory until its tag is `tag`; returns the value
+// bits, or sets bit 1 of the error word and returns 0 when the bound runs out.
+__device__ __forceinline__ uint32_t ll_wait(const TpComm& c, const unsigned long long* p, uint32_t tag) {
+  unsigned long long w = ld_relaxed_sys_u64(p);
+  if ((uint32_t)(w >> 32) == tag) return (uint32_t)w;
+  const long long t0 = clock64();
+  for (;;) {
+    w = ld_relaxed_sys_u64(p);
+    if ((uint32_t)(w >> 32) == tag) return (uint32_t)w;
+    if (clock64() - t0 > kTpWaitCycles) {
+      atomicOr(c.err, 2);
+      return 0u;
+    }
+  }
+}
+
 // Host side.
 struct TpHost {
   int rank = 0, size = 1;
@@ -92,14 +124,13 @@ struct TpHost {
   void* peer_base[kTpMax] = {};  // mapped regions (own at [rank])
   bool connected = false;
   // offsets inside a region
-  size_t off_flags = 0, off_gparts = 0, off_bparts = 0, off_keys = 0, off_logits = 0;
+  size_t off_flags = 0, off_bparts = 0, off_ll = 0, off_llkeys = 0, off_logits = 0;
   TpComm comm;
 };
 
-// Flag slots: [0, row groups) for the row-parallel GEMVs, then these (from the top).
+// Flag slots of the bulk exchanges.
 constexpr uint32_t kSlotBulk = kTpSlots - 1;
 constexpr uint32_t kSlotLogits = kTpSlots - 2;
-constexpr uint32_t kSlotKeys = kTpSlots - 3;  // minus the logits row
 
 // Exchange kernels (tp.cu).
 // Sums every rank's bulk partial [n] (parity of the site's epoch) in rank order into out.
