@@ -130,6 +130,10 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
 // Launch helpers implemented per kernel family (internal, not part of the C ABI).
 int launch_mat(int dtype, StepRef st, const snl_mat_p& p, const float* x, const void* wq, const void* ws,
                int scale_f16, float* y, cudaStream_t s, uint32_t rows_m_host);
+// Prefill GEMM on the tcgen05 tensor cores (gemm_tc.cu), f32 scales, m token rows.
+bool gemm_tc_enabled();
+int launch_gemm_tc(int dtype, const snl_mat_p& p, uint32_t m, const float* x, const void* wq, const float* ws, float* y,
+                   cudaStream_t s);
 int launch_branch_norm(StepRef st, const snl_layer_p& p, const float* x, const float* coef, const float* w,
                        float* out, uint32_t n_groups, cudaStream_t s, XOut xo = XOut());
 // branch_norm mode 1 that first finishes the mHC router from nparts partial sums per

@@ -1,0 +1,352 @@
+// Block-quantized GEMM for prefill on the 5th-generation tensor cores (tcgen05).
+//
+// Y[t, n] = sum_k X[t, k] * q[n, k] * s[n, k/32], t < m tokens (matmul.wgsl:204-318,
+// `matmul` with load_slice/dequant8, for prefill chunks of up to 512 rows).
+//
+// CTA tile: 128 weight rows x 256 tokens, K in blocks of 64. The fp32 accumulator lives
+// in tensor memory (128 lanes x 256 columns). Precision: both operands are split into
+// fp16 hi + lo parts and three products are accumulated (hi*hi + hi*lo + lo*hi), which
+// keeps ~21 significant bits, well inside the 1e-3 bar; the dropped lo*lo term is
+// below 2^-22 of the result.
+//   * A (weights) is dequantized by the CTA's 256 threads from the file layout
+//     (weights.rs:48-55) into two fp16 tiles in the 128-byte-swizzled K-major layout of
+//     the MMA: v = code * scale * 256, hi = fp16(v), lo = fp16(v - hi).
+//   * B (tokens) comes from "x planes" [2][m][k] fp16 (x/16 split into hi and lo),
+//     written once per GEMM by tc_xpack_kernel and loaded by TMA with the same swizzle.
+//   * One thread issues the 12 MMAs of a K block (4 k-steps x 3 products, M=128 N=256
+//     K=16, kind::f16) and commits them to the stage's "empty" mbarrier, so the
+//     dequantization of block kb+1 overlaps the MMAs of block kb (2 stages).
+//   * Epilogue: 8 warps read the accumulator with tcgen05.ld (warp w: TMEM lanes
+//     32*(w%4).., columns 128*(w/4)..) and store y = acc / 16 (16 from the x prescale,
+//     1/256 from the weight prescale).
+// Every mbarrier wait is bounded; a wait that gives up sets the device error word, the
+// CTA stops issuing work, waits (bounded) for its MMAs, frees its tensor memory and
+// returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdlib>
+#include <mutex>
+
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace snl {
+namespace {
+
+constexpr uint32_t kTcM = 128, kTcN = 256, kTcK = 64;
+constexpr int kTcStages = 2;
+constexpr uint32_t kATile = kTcM * kTcK * 2;  // 16 KB of fp16
+constexpr uint32_t kBTile = kTcN * kTcK * 2;  // 32 KB of fp16
+constexpr uint32_t kStageBytes = 2 * kATile + 2 * kBTile;
+constexpr uint32_t kTcSmem = kTcStages * kStageBytes + 1024;  // + alignment slack
+constexpr uint32_t kTmemCols = kTcN;
+constexpr float kAScale = 256.0f;
+constexpr float kXPlaneScaleTc = 16.0f;  // x planes hold x / 16 (fp16 range for |x| up to ~1e6)
+
+struct TcArgs {
+  uint32_t n, k, m;
+  const uint8_t* wq;
+  const float* ws;
+  float* y;
+  uint32_t y_off, y_stride, n_off;
+  int* err;
+};
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row core-matrix
+// groups 1024 bytes apart (SBO), descriptor version 1 (sm_100).
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;             // leading byte offset (unused with this swizzle)
+  d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset
+  d |= (uint64_t)1 << 46;             // version
+  d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+  return d;
+}
+// Instruction descriptor, kind::f16: D f32, A and B f16, both K-major, N = 256, M = 128.
+constexpr uint32_t kIdesc = (1u << 4) | ((kTcN >> 3) << 17) | ((kTcM >> 4) << 24);
+
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(kIdesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+          "r"(smem_u32(dst)),
+      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_hl(float a, float b, bool lo) {
+  const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+  if (!lo) return (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
+  const __half la = __float2half_rn(a - __half2float(ha)), lb = __float2half_rn(b - __half2float(hb));
+  return (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
+}
+
+// Dequantizes the 128 x 64 weight tile of K block kb into the hi and lo A tiles. Thread
+// t takes row t/2 and the 32-element quant block (t%2) of the K block.
+template <int DT>
+__device__ __forceinline__ void produce_a(const TcArgs& a, uint32_t n0, uint32_t kb, uint8_t* ahi, uint8_t* alo,
+                                          uint32_t tid) {
+  const uint32_t r = tid >> 1, h = tid & 1;
+  const uint32_t row = n0 + r, kblk = kb * 2 + h;  // quant block index
+  float v[32];
+  if (row < a.n && kblk * 32 < a.k) {
+    const float sc = __ldg(a.ws + (uint64_t)row * (a.k / 32) + kblk) * kAScale;
+    if constexpr (DT == SNL_Q8_0) {
+      const uint4* src = reinterpret_cast<const uint4*>(a.wq + (uint64_t)row * a.k + kblk * 32);
+      const uint4 w0 = ld_stream16(src), w1 = ld_stream16(src + 1);
+      const uint32_t wd[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int i = 0; i < 32; i++) v[i] = (float)(int8_t)((wd[i / 4] >> (8 * (i % 4))) & 0xFFu) * sc;
+    } else {
+      const uint4 w = ld_stream16(a.wq + (uint64_t)row * (a.k / 2) + kblk * 16);
+      const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int i = 0; i < 32; i++) v[i] = (float)((int)((wd[i / 8] >> (4 * (i % 8))) & 0xFu) - 8) * sc;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = 0.f;
+  }
+#pragma unroll
+  for (int c = 0; c < 4; c++) {
+    const uint32_t chunk = h * 4 + c;
+    const uint32_t off = r * 128 + ((chunk ^ (r & 7)) << 4);
+    uint4 hi, lo;
+    hi.x = pack_hl(v[8 * c + 0], v[8 * c + 1], false);
+    hi.y = pack_hl(v[8 * c + 2], v[8 * c + 3], false);
+    hi.z = pack_hl(v[8 * c + 4], v[8 * c + 5], false);
+    hi.w = pack_hl(v[8 * c + 6], v[8 * c + 7], false);
+    lo.x = pack_hl(v[8 * c + 0], v[8 * c + 1], true);
+    lo.y = pack_hl(v[8 * c + 2], v[8 * c + 3], true);
+    lo.z = pack_hl(v[8 * c + 4], v[8 * c + 5], true);
+    lo.w = pack_hl(v[8 * c + 6], v[8 * c + 7], true);
+    *reinterpret_cast<uint4*>(ahi + off) = hi;
+    *reinterpret_cast<uint4*>(alo + off) = lo;
+  }
+}
+
+template <int DT>
+__global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap, TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  __shared__ uint64_t full_bar[kTcStages], empty_bar[kTcStages], done_bar;
+  __shared__ uint32_t tmem_sh;
+  __shared__ int fail_sh;
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t n0 = blockIdx.x * kTcM, t0 = blockIdx.y * kTcN;
+  const uint32_t nkb = (a.k + kTcK - 1) / kTcK;
+
+  if (tid == 0) {
+    for (int s = 0; s < kTcStages; s++) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&done_bar, 1);
+    fail_sh = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_sh)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_sh;
+
+  for (uint32_t kb = 0; kb < nkb; kb++) {
+    const int s = kb % kTcStages;
+    const uint32_t use = kb / kTcStages;
+    uint8_t* st = smem + s * kStageBytes;
+    uint8_t* ahi = st;
+    uint8_t* alo = st + kATile;
+    uint8_t* bhi = st + 2 * kATile;
+    uint8_t* blo = bhi + kBTile;
+    // The stage is free once the MMAs of block kb - kTcStages have completed.
+    if (kb >= (uint32_t)kTcStages && !mbar_wait_bounded(&empty_bar[s], (use - 1) & 1)) fail_sh = 1;
+    __syncthreads();
+    if (fail_sh) break;
+    if (tid == 0) {
+      mbar_arrive_expect_tx(&full_bar[s], 2 * kBTile);
+      tma_load_3d(bhi, &xmap, (int)(kb * kTcK), (int)t0, 0, &full_bar[s]);
+      tma_load_3d(blo, &xmap, (int)(kb * kTcK), (int)t0, 1, &full_bar[s]);
+    }
+    produce_a<DT>(a, n0, kb, ahi, alo, tid);
+    fence_proxy_async_smem();  // the dequantized tiles are read by the tensor cores (async proxy)
+    __syncthreads();
+    if (tid == 0) {
+      if (!mbar_wait_bounded(&full_bar[s], use & 1)) {
+        fail_sh = 1;
+      } else {
+        tc_fence_after();
+        const uint32_t sa_hi = smem_u32(ahi), sa_lo = smem_u32(alo), sb_hi = smem_u32(bhi), sb_lo = smem_u32(blo);
+#pragma unroll
+        for (uint32_t kk = 0; kk < kTcK / 16; kk++) {
+          const uint32_t o = kk * 32;  // 16 fp16 along K inside the 128-byte swizzled row
+          tc_mma(tmem, sdesc_sw128(sa_hi + o), sdesc_sw128(sb_hi + o), (kb | kk) != 0);
+          tc_mma(tmem, sdesc_sw128(sa_hi + o), sdesc_sw128(sb_lo + o), 1);
+          tc_mma(tmem, sdesc_sw128(sa_lo + o), sdesc_sw128(sb_hi + o), 1);
+        }
+        tc_commit(&empty_bar[s]);
+      }
+    }
+  }
+  if (tid == 0) {
+    tc_commit(&done_bar);  // arrives when every MMA issued above has completed
+    if (fail_sh) report_timeout(a.err);
+  }
+  const bool done = mbar_wait_bounded(&done_bar, 0);
+  __syncthreads();
+  tc_fence_after();
+  if (done && !fail_sh) {
+    const uint32_t quarter = warp & 3, half = warp >> 2;
+    const uint32_t row = n0 + quarter * 32 + lane;
+    const float out_scale = kXPlaneScaleTc / kAScale;
+#pragma unroll 1
+    for (uint32_t c0 = half * 128; c0 < half * 128 + 128; c0 += 32) {
+      uint32_t r[32];
+      const uint32_t taddr = tmem + ((quarter * 32) << 16) + c0;
+      asm volatile(
+          "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+          "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+          : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+            "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+            "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+            "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+          : "r"(taddr));
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      if (row < a.n) {
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+          const uint32_t t = t0 + c0 + j;
+          if (t < a.m) a.y[a.y_off + (uint64_t)t * a.y_stride + a.n_off + row] = __uint_as_float(r[j]) * out_scale;
+        }
+      }
+    }
+  } else if (tid == 0 && !done) {
+    report_timeout(a.err);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+}
+
+// x [m][x_stride] fp32 (from x_off) -> planes [2][m][k] fp16: hi and lo of x / 16.
+__global__ void tc_xpack_kernel(const float* __restrict__ x, uint32_t x_stride, uint32_t m, uint32_t k,
+                                __half* __restrict__ planes) {
+  const uint64_t total = (uint64_t)m * k;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t t = i / k, j = i % k;
+    const float vs = x[t * x_stride + j] * (1.0f / kXPlaneScaleTc);
+    const __half hi = __float2half_rn(vs);
+    planes[i] = hi;
+    planes[total + i] = __float2half_rn(vs - __half2float(hi));
+  }
+}
+
+PFN_cuTensorMapEncodeTiled encode_fn() {
+  static PFN_cuTensorMapEncodeTiled fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return (PFN_cuTensorMapEncodeTiled) nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled>(p);
+  }();
+  return fn;
+}
+
+// Per-device scratch for the x planes of one GEMM, grown on demand.
+__half* planes_scratch(size_t halves) {
+  static std::mutex mu;
+  static __half* buf[64] = {nullptr};
+  static size_t cap[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  if (cap[dev] < halves) {
+    if (buf[dev]) cudaFree(buf[dev]);
+    buf[dev] = nullptr;
+    cap[dev] = 0;
+    void* p = nullptr;
+    if (cudaMalloc(&p, halves * sizeof(__half)) != cudaSuccess) return nullptr;
+    buf[dev] = static_cast<__half*>(p);
+    cap[dev] = halves;
+  }
+  return buf[dev];
+}
+
+}  // namespace
+
+bool gemm_tc_enabled() {
+  static const bool on = getenv("SNL_NO_TC_GEMM") == nullptr;
+  return on;
+}
+
+int launch_gemm_tc(int dtype, const snl_mat_p& p, uint32_t m, const float* x, const void* wq, const float* ws, float* y,
+                   cudaStream_t s) {
+  if (dtype != SNL_Q8_0 && dtype != SNL_Q4_0) return fail(SNL_E_INVALID, "gemm_tc: dtype");
+  if (p.k % 32 || p.k == 0 || m == 0) return fail(SNL_E_INVALID, "gemm_tc: k must be a positive multiple of 32");
+  PFN_cuTensorMapEncodeTiled enc = encode_fn();
+  if (!enc) return fail(SNL_E_CUDA, "gemm_tc: cuTensorMapEncodeTiled is unavailable");
+  int* err = nullptr;
+  if (int rc = device_error_word(&err)) return rc;
+  __half* planes = planes_scratch((size_t)2 * m * p.k);
+  if (!planes) return fail(SNL_E_OOM, "gemm_tc: x planes scratch");
+  const uint64_t total = (uint64_t)m * p.k;
+  tc_xpack_kernel<<<(unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sm_count() * 8), 256, 0, s>>>(
+      x + p.x_off, p.x_stride, m, p.k, planes);
+  SNL_LAUNCH_CHECK("gemm_tc xpack");
+
+  CUtensorMap map;
+  const cuuint64_t dims[3] = {p.k, m, 2};
+  const cuuint64_t strides[2] = {(cuuint64_t)p.k * 2, (cuuint64_t)m * p.k * 2};
+  const cuuint32_t box[3] = {kTcK, kTcN, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult cr = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, planes, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return fail(SNL_E_CUDA, "gemm_tc: cuTensorMapEncodeTiled failed");
+
+  TcArgs ta{p.n, p.k, m, static_cast<const uint8_t*>(wq), ws, y, p.y_off, p.y_stride, p.n_off, err};
+  const dim3 grid((p.n + kTcM - 1) / kTcM, (m + kTcN - 1) / kTcN);
+  static bool attr[2][64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int di = dtype == SNL_Q8_0 ? 0 : 1;
+  if (dtype == SNL_Q8_0) {
+    if (dev >= 0 && dev < 64 && !attr[di][dev]) {
+      SNL_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<SNL_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem));
+      attr[di][dev] = true;
+    }
+    gemm_tc_kernel<SNL_Q8_0><<<grid, 256, kTcSmem, s>>>(map, ta);
+  } else {
+    if (dev >= 0 && dev < 64 && !attr[di][dev]) {
+      SNL_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<SNL_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem));
+      attr[di][dev] = true;
+    }
+    gemm_tc_kernel<SNL_Q4_0><<<grid, 256, kTcSmem, s>>>(map, ta);
+  }
+  SNL_LAUNCH_CHECK("gemm_tc");
+  return SNL_OK;
+}
+
+}  // namespace snl

@@ -550,6 +550,9 @@ int launch_mat(int dtype, StepRef st, const snl_mat_p& p, const float* x, const 
   if ((p.x_off % 4) || (p.x_stride % 4)) return fail(SNL_E_INVALID, "mat: x_off and x_stride must be multiples of 4");
   if (((uintptr_t)x % 16) || ((uintptr_t)wq % 16)) return fail(SNL_E_INVALID, "mat: x and wq must be 16-byte aligned");
   if (rows_m == 0 || p.n == 0) return SNL_OK;
+  // Prefill-sized steps run on the tcgen05 tensor cores.
+  if (rows_m >= 8 && !scale_f16 && gemm_tc_enabled())
+    return launch_gemm_tc(dtype, p, rows_m, x, wq, static_cast<const float*>(ws), y, s);
   if (dtype == SNL_Q8_0) {
     return scale_f16 ? launch_mat_t<SNL_Q8_0, __half>(p, rows_m, x, wq, (const __half*)ws, y, s)
                      : launch_mat_t<SNL_Q8_0, float>(p, rows_m, x, wq, (const float*)ws, y, s);

@@ -110,6 +110,18 @@ def test_mat_rows(T, lib, orc, dtype, m):
 
 
 @pytest.mark.parametrize("dtype", [SNL_Q8_0, SNL_Q4_0])
+@pytest.mark.parametrize("n,k,m", [(1000, 2048, 256), (1000, 2048, 300), (4096, 4096, 512), (333, 160, 40)])
+def test_mat_prefill_tensor_cores(T, lib, orc, dtype, n, k, m):
+    """Prefill rows (m >= 8) run on the tcgen05 GEMM: several token and row tiles, a
+    partial last K block (k = 160), against the oracle's f32 GEMM."""
+    y, ref = run_mat(T, lib, orc, dtype, n, k, m, seed=n + m)
+    assert rel(y, ref) < TOL
+    # Three fp16 hi/lo products; the tensor cores' fp32 accumulation over K leaves
+    # ~2e-5 at k = 4096, fifty times inside the bar.
+    assert rel(y, ref) < 1e-4
+
+
+@pytest.mark.parametrize("dtype", [SNL_Q8_0, SNL_Q4_0])
 def test_mat_config1_shape(T, lib, orc, dtype):
     # The benchmark GEMV: W [12288 x 4096], one token.
     y, ref = run_mat(T, lib, orc, dtype, 12288, 4096, 1, seed=5)
