@@ -3,8 +3,9 @@
 // Y[t, n] = sum_k X[t, k] * q[n, k] * s[n, k/32], t < m tokens (matmul.wgsl:204-318,
 // `matmul` with load_slice/dequant8, for prefill chunks of up to 512 rows).
 //
-// CTA tile: 128 weight rows x 256 tokens, K in blocks of 64. The fp32 accumulator lives
-// in tensor memory (128 lanes x 256 columns). Precision: both operands are split into
+// CTA tile: 128 weight rows x 256 tokens (128 when 256-token tiles would leave SMs
+// idle), K in blocks of 64. The fp32 accumulator lives in tensor memory (128 lanes x
+// one column per token). Precision: both operands are split into
 // fp16 hi + lo parts and three products are accumulated (hi*hi + hi*lo + lo*hi), which
 // keeps ~21 significant bits, well inside the 1e-3 bar; the dropped lo*lo term is
 // below 2^-22 of the result.
@@ -14,10 +15,10 @@
 //   * B (tokens) comes from "x planes" [2][m][k] fp16 (x/16 split into hi and lo),
 //     written once per GEMM by tc_xpack_kernel and loaded by TMA with the same swizzle.
 //   * One thread issues the 12 MMAs of a K block (4 k-steps x 3 products, M=128 N=256
-//     K=16, kind::f16) and commits them to the stage's "empty" mbarrier, so the
+//     or 128, K=16, kind::f16) and commits them to the stage's "empty" mbarrier, so the
 //     dequantization of block kb+1 overlaps the MMAs of block kb (2 stages).
 //   * Epilogue: 8 warps read the accumulator with tcgen05.ld (warp w: TMEM lanes
-//     32*(w%4).., columns 128*(w/4)..) and store y = acc / 16 (16 from the x prescale,
+//     32*(w%4).., the (w/4)-th half of the columns) and store y = acc / 16 (16 from the x prescale,
 //     1/256 from the weight prescale).
 // Every mbarrier wait is bounded; a wait that gives up sets the device error word, the
 // CTA stops issuing work, waits (bounded) for its MMAs, frees its tensor memory and
@@ -35,13 +36,18 @@
 namespace snl {
 namespace {
 
-constexpr uint32_t kTcM = 128, kTcN = 256, kTcK = 64;
+constexpr uint32_t kTcM = 128, kTcK = 64;
 constexpr int kTcStages = 2;
 constexpr uint32_t kATile = kTcM * kTcK * 2;  // 16 KB of fp16
-constexpr uint32_t kBTile = kTcN * kTcK * 2;  // 32 KB of fp16
-constexpr uint32_t kStageBytes = 2 * kATile + 2 * kBTile;
-constexpr uint32_t kTcSmem = kTcStages * kStageBytes + 1024;  // + alignment slack
-constexpr uint32_t kTmemCols = kTcN;
+// Token tile NT = 256 (or 128 when 256-token tiles would leave SMs idle).
+template <uint32_t NT>
+struct TcGeom {
+  static constexpr uint32_t kBTile = NT * kTcK * 2;
+  static constexpr uint32_t kStageBytes = 2 * kATile + 2 * kBTile;
+  static constexpr uint32_t kSmem = kTcStages * kStageBytes + 1024;  // + alignment slack
+  // Instruction descriptor, kind::f16: D f32, A and B f16, both K-major, N = NT, M = 128.
+  static constexpr uint32_t kIdesc = (1u << 4) | ((NT >> 3) << 17) | ((kTcM >> 4) << 24);
+};
 constexpr float kAScale = 256.0f;
 constexpr float kXPlaneScaleTc = 16.0f;  // x planes hold x / 16 (fp16 range for |x| up to ~1e6)
 
@@ -64,14 +70,11 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
   d |= (uint64_t)2 << 61;             // SWIZZLE_128B
   return d;
 }
-// Instruction descriptor, kind::f16: D f32, A and B f16, both K-major, N = 256, M = 128.
-constexpr uint32_t kIdesc = (1u << 4) | ((kTcN >> 3) << 17) | ((kTcM >> 4) << 24);
-
-__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t acc) {
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(kIdesc), "r"(acc)
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
@@ -96,31 +99,45 @@ __device__ __forceinline__ uint32_t pack_hl(float a, float b, bool lo) {
   return (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
 }
 
-// Dequantizes the 128 x 64 weight tile of K block kb into the hi and lo A tiles. Thread
-// t takes row t/2 and the 32-element quant block (t%2) of the K block.
+// The raw quants and scale one thread dequantizes per K block: row t/2 of the tile and
+// the 32-element quant block (t%2) of the K block. Loaded one K block ahead.
+struct RawA {
+  uint4 w0, w1;  // Q8: 32 codes; Q4: w0 = 32 nibbles
+  float sc;
+};
+
 template <int DT>
-__device__ __forceinline__ void produce_a(const TcArgs& a, uint32_t n0, uint32_t kb, uint8_t* ahi, uint8_t* alo,
-                                          uint32_t tid) {
+__device__ __forceinline__ RawA load_a(const TcArgs& a, uint32_t n0, uint32_t kb, uint32_t tid) {
   const uint32_t r = tid >> 1, h = tid & 1;
-  const uint32_t row = n0 + r, kblk = kb * 2 + h;  // quant block index
-  float v[32];
+  const uint32_t row = n0 + r, kblk = kb * 2 + h;
+  RawA raw{make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), 0.f};
   if (row < a.n && kblk * 32 < a.k) {
-    const float sc = __ldg(a.ws + (uint64_t)row * (a.k / 32) + kblk) * kAScale;
+    raw.sc = __ldg(a.ws + (uint64_t)row * (a.k / 32) + kblk) * kAScale;
     if constexpr (DT == SNL_Q8_0) {
       const uint4* src = reinterpret_cast<const uint4*>(a.wq + (uint64_t)row * a.k + kblk * 32);
-      const uint4 w0 = ld_stream16(src), w1 = ld_stream16(src + 1);
-      const uint32_t wd[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-      for (int i = 0; i < 32; i++) v[i] = (float)(int8_t)((wd[i / 4] >> (8 * (i % 4))) & 0xFFu) * sc;
+      raw.w0 = ld_stream16(src);
+      raw.w1 = ld_stream16(src + 1);
     } else {
-      const uint4 w = ld_stream16(a.wq + (uint64_t)row * (a.k / 2) + kblk * 16);
-      const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-      for (int i = 0; i < 32; i++) v[i] = (float)((int)((wd[i / 8] >> (4 * (i % 8))) & 0xFu) - 8) * sc;
+      raw.w0 = ld_stream16(a.wq + (uint64_t)row * (a.k / 2) + kblk * 16);
     }
-  } else {
+  }
+  return raw;
+}
+
+// Writes one thread's 32 dequantized values as hi and lo fp16 into the A tiles
+// (128-byte swizzled rows: 16-byte chunk c of row r at chunk c ^ (r % 8)).
+template <int DT>
+__device__ __forceinline__ void store_a(const RawA& raw, uint8_t* ahi, uint8_t* alo, uint32_t tid) {
+  const uint32_t r = tid >> 1, h = tid & 1;
+  float v[32];
+  if constexpr (DT == SNL_Q8_0) {
+    const uint32_t wd[8] = {raw.w0.x, raw.w0.y, raw.w0.z, raw.w0.w, raw.w1.x, raw.w1.y, raw.w1.z, raw.w1.w};
 #pragma unroll
-    for (int i = 0; i < 32; i++) v[i] = 0.f;
+    for (int i = 0; i < 32; i++) v[i] = (float)(int8_t)((wd[i / 4] >> (8 * (i % 4))) & 0xFFu) * raw.sc;
+  } else {
+    const uint32_t wd[4] = {raw.w0.x, raw.w0.y, raw.w0.z, raw.w0.w};
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = (float)((int)((wd[i / 8] >> (4 * (i % 8))) & 0xFu) - 8) * raw.sc;
   }
 #pragma unroll
   for (int c = 0; c < 4; c++) {
@@ -140,15 +157,17 @@ __device__ __forceinline__ void produce_a(const TcArgs& a, uint32_t n0, uint32_t
   }
 }
 
-template <int DT>
+template <int DT, uint32_t NT>
 __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap, TcArgs a) {
+  using G = TcGeom<NT>;
+  constexpr uint32_t kTmemCols = NT;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   __shared__ uint64_t full_bar[kTcStages], empty_bar[kTcStages], done_bar;
   __shared__ uint32_t tmem_sh;
   __shared__ int fail_sh;
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t n0 = blockIdx.x * kTcM, t0 = blockIdx.y * kTcN;
+  const uint32_t n0 = blockIdx.x * kTcM, t0 = blockIdx.y * NT;
   const uint32_t nkb = (a.k + kTcK - 1) / kTcK;
 
   if (tid == 0) {
@@ -171,24 +190,27 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
   tc_fence_after();
   const uint32_t tmem = tmem_sh;
 
+  RawA raw = load_a<DT>(a, n0, 0, tid);
   for (uint32_t kb = 0; kb < nkb; kb++) {
+    const RawA next = kb + 1 < nkb ? load_a<DT>(a, n0, kb + 1, tid) : RawA{};
     const int s = kb % kTcStages;
     const uint32_t use = kb / kTcStages;
-    uint8_t* st = smem + s * kStageBytes;
+    uint8_t* st = smem + s * G::kStageBytes;
     uint8_t* ahi = st;
     uint8_t* alo = st + kATile;
     uint8_t* bhi = st + 2 * kATile;
-    uint8_t* blo = bhi + kBTile;
+    uint8_t* blo = bhi + G::kBTile;
     // The stage is free once the MMAs of block kb - kTcStages have completed.
     if (kb >= (uint32_t)kTcStages && !mbar_wait_bounded(&empty_bar[s], (use - 1) & 1)) fail_sh = 1;
     __syncthreads();
     if (fail_sh) break;
     if (tid == 0) {
-      mbar_arrive_expect_tx(&full_bar[s], 2 * kBTile);
+      mbar_arrive_expect_tx(&full_bar[s], 2 * G::kBTile);
       tma_load_3d(bhi, &xmap, (int)(kb * kTcK), (int)t0, 0, &full_bar[s]);
       tma_load_3d(blo, &xmap, (int)(kb * kTcK), (int)t0, 1, &full_bar[s]);
     }
-    produce_a<DT>(a, n0, kb, ahi, alo, tid);
+    store_a<DT>(raw, ahi, alo, tid);
+    raw = next;
     fence_proxy_async_smem();  // the dequantized tiles are read by the tensor cores (async proxy)
     __syncthreads();
     if (tid == 0) {
@@ -200,9 +222,9 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
 #pragma unroll
         for (uint32_t kk = 0; kk < kTcK / 16; kk++) {
           const uint32_t o = kk * 32;  // 16 fp16 along K inside the 128-byte swizzled row
-          tc_mma(tmem, sdesc_sw128(sa_hi + o), sdesc_sw128(sb_hi + o), (kb | kk) != 0);
-          tc_mma(tmem, sdesc_sw128(sa_hi + o), sdesc_sw128(sb_lo + o), 1);
-          tc_mma(tmem, sdesc_sw128(sa_lo + o), sdesc_sw128(sb_hi + o), 1);
+          tc_mma(tmem, sdesc_sw128(sa_hi + o), sdesc_sw128(sb_hi + o), G::kIdesc, (kb | kk) != 0);
+          tc_mma(tmem, sdesc_sw128(sa_hi + o), sdesc_sw128(sb_lo + o), G::kIdesc, 1);
+          tc_mma(tmem, sdesc_sw128(sa_lo + o), sdesc_sw128(sb_hi + o), G::kIdesc, 1);
         }
         tc_commit(&empty_bar[s]);
       }
@@ -220,7 +242,7 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
     const uint32_t row = n0 + quarter * 32 + lane;
     const float out_scale = kXPlaneScaleTc / kAScale;
 #pragma unroll 1
-    for (uint32_t c0 = half * 128; c0 < half * 128 + 128; c0 += 32) {
+    for (uint32_t c0 = half * (NT / 2); c0 < half * (NT / 2) + NT / 2; c0 += 32) {
       uint32_t r[32];
       const uint32_t taddr = tmem + ((quarter * 32) << 16) + c0;
       asm volatile(
@@ -316,10 +338,15 @@ int launch_gemm_tc(int dtype, const snl_mat_p& p, uint32_t m, const float* x, co
       x + p.x_off, p.x_stride, m, p.k, planes);
   SNL_LAUNCH_CHECK("gemm_tc xpack");
 
+  // 256-token tiles unless the step has at most 128 tokens or 256-token tiles would leave
+  // SMs idle.
+  const uint32_t row_tiles = (p.n + kTcM - 1) / kTcM;
+  const bool narrow = m <= 128 || (uint64_t)row_tiles * ((m + 255) / 256) < (uint64_t)sm_count();
+  const uint32_t nt = narrow ? 128 : 256;
   CUtensorMap map;
   const cuuint64_t dims[3] = {p.k, m, 2};
   const cuuint64_t strides[2] = {(cuuint64_t)p.k * 2, (cuuint64_t)m * p.k * 2};
-  const cuuint32_t box[3] = {kTcK, kTcN, 1};
+  const cuuint32_t box[3] = {kTcK, nt, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   CUresult cr = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, planes, dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -327,24 +354,26 @@ int launch_gemm_tc(int dtype, const snl_mat_p& p, uint32_t m, const float* x, co
   if (cr != CUDA_SUCCESS) return fail(SNL_E_CUDA, "gemm_tc: cuTensorMapEncodeTiled failed");
 
   TcArgs ta{p.n, p.k, m, static_cast<const uint8_t*>(wq), ws, y, p.y_off, p.y_stride, p.n_off, err};
-  const dim3 grid((p.n + kTcM - 1) / kTcM, (m + kTcN - 1) / kTcN);
-  static bool attr[2][64] = {};
+  const dim3 grid(row_tiles, (m + nt - 1) / nt);
   int dev = 0;
   cudaGetDevice(&dev);
-  const int di = dtype == SNL_Q8_0 ? 0 : 1;
-  if (dtype == SNL_Q8_0) {
-    if (dev >= 0 && dev < 64 && !attr[di][dev]) {
-      SNL_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<SNL_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem));
-      attr[di][dev] = true;
+  auto go = [&](auto kern, uint32_t smem, bool* attr) -> int {
+    if (dev >= 0 && dev < 64 && !attr[dev]) {
+      SNL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      attr[dev] = true;
     }
-    gemm_tc_kernel<SNL_Q8_0><<<grid, 256, kTcSmem, s>>>(map, ta);
-  } else {
-    if (dev >= 0 && dev < 64 && !attr[di][dev]) {
-      SNL_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<SNL_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem));
-      attr[di][dev] = true;
-    }
-    gemm_tc_kernel<SNL_Q4_0><<<grid, 256, kTcSmem, s>>>(map, ta);
-  }
+    kern<<<grid, 256, smem, s>>>(map, ta);
+    return SNL_OK;
+  };
+  static bool attr[4][64] = {};
+  int rc;
+  if (dtype == SNL_Q8_0)
+    rc = narrow ? go(gemm_tc_kernel<SNL_Q8_0, 128>, TcGeom<128>::kSmem, attr[0])
+                : go(gemm_tc_kernel<SNL_Q8_0, 256>, TcGeom<256>::kSmem, attr[1]);
+  else
+    rc = narrow ? go(gemm_tc_kernel<SNL_Q4_0, 128>, TcGeom<128>::kSmem, attr[2])
+                : go(gemm_tc_kernel<SNL_Q4_0, 256>, TcGeom<256>::kSmem, attr[3]);
+  if (rc) return rc;
   SNL_LAUNCH_CHECK("gemm_tc");
   return SNL_OK;
 }
