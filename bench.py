@@ -52,7 +52,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=25.0)
     ap.add_argument("--profile", action="store_true", help="print the per-op table of one decode step")
-    ap.add_argument("--workload", choices=["decode", "gemv"], default="decode",
+    ap.add_argument("--turns", type=int, default=4, help="mtp workload: turns (BASELINE config 4 names 1000)")
+    ap.add_argument("--workload", choices=["decode", "gemv", "deltanet", "mtp"], default="decode",
                     help="gemv: only BASELINE configs[0], the one-token Q8_0 GEMV 12288x4096")
     ap.add_argument("--iters", type=int, default=40)
     ap.add_argument("--gemv-kernel", choices=["tile", "tc", "simt"], default="tile")
@@ -449,12 +450,174 @@ def run_gemv_only(args):
     return 0
 
 
+def run_deltanet(args):
+    """one Gated DeltaNet layer (16 QK / 32 V heads of 128,
+    fp32 state [32,128,128]). Inputs as the config states: q, k, v, b, a, z ~ N(0,1)
+    (q, k L2-normalised and beta = sigmoid(b) inside the kernel), A_log = 0 and
+    dt_bias = 0 (g = -softplus(a)), conv weights N(0, 0.5), norm weight 1. A prefill of
+    4096 tokens in the engine's 512-row steps, then 256 recurrent single-token steps,
+    through the engine's fused conv + delta kernel (snl_conv_delta)."""
+    import ctypes as C
+
+    import torch
+
+    from sensenova_b200 import ffi
+
+    torch.cuda.set_device(0)
+    lib = ffi.load()
+    n_k, n_v, D = 16, 32, 128
+    cd = 2 * n_k * D + n_v * D
+    stride = cd + n_v * D + 2 * n_v
+    lp = ffi.LinP(cd, stride, n_k, n_v, 1e-6, (0, 0, 0))
+    T, R, chunk = 4096, 256, 512
+    rng = np.random.default_rng(args.seed)
+    proj = rng.standard_normal((T + R, stride)).astype(np.float32)
+    lw = np.concatenate([np.sqrt(0.5) * rng.standard_normal(cd * 4), np.zeros(2 * n_v), np.ones(D)]).astype(np.float32)
+    dp, dlw = torch.from_numpy(proj).cuda(), torch.from_numpy(lw).cuda()
+    cs, S = torch.zeros(3 * cd, device="cuda"), torch.zeros(n_v * D * D, device="cuda")
+    out = torch.zeros((T + R) * n_v * D, device="cuda")
+    ptr = lambda t: C.c_void_p(t.data_ptr())
+
+    def step(r0, m):
+        st = ffi.StepU(m, r0, 1, 0)
+        ffi.check(lib.snl_conv_delta(C.byref(st), C.byref(lp), C.c_void_p(dp.data_ptr() + 4 * r0 * stride), ptr(cs),
+                                     ptr(S), ptr(dlw), C.c_void_p(out.data_ptr() + 4 * r0 * n_v * D), None, None, None))
+
+    def timed(fn):
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b)
+
+    for _ in range(max(args.warmup, 3)):  # warm-up on a scratch copy of the state
+        step(0, chunk)
+    cs.zero_()
+    S.zero_()
+    pf_ms = timed(lambda: [step(c, chunk) for c in range(0, T, chunk)])
+    dec_ms = timed(lambda: [step(T + i, 1) for i in range(R)])
+    # CPU reference on a bounded sample: the oracle's conv + delta over 64 tokens
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as orc
+
+    nS = 64
+    conv_out = np.zeros((nS, cd), np.float32)
+    cs_h, S_h, o_h = np.zeros((3, cd), np.float32), np.zeros((n_v, D, D), np.float32), np.zeros((nS, n_v * D), np.float32)
+    stc = ffi.StepU(nS, 0, 1, 0)
+    t0 = time.perf_counter()
+    orc.conv(stc, lp, proj[:nS], conv_out, cs_h, lw, np.zeros((3, cd), np.float32))
+    orc.delta(stc, lp, proj[:nS], conv_out, S_h, lw, o_h, np.zeros_like(S_h))
+    cpu_s = time.perf_counter() - t0
+    line = {
+        "metric": "Gated DeltaNet layer: prefill tok/s (4096 tokens) and recurrent us/token",
+        "value": T / (pf_ms / 1000.0), "unit": "tok/s", "n_gpus": 1, "higher_is_better": True,
+        "prefill_ms": pf_ms, "decode_us_per_token": dec_ms * 1000.0 / R, "decode_tok_s": R / (dec_ms / 1000.0),
+        "dtype": "f32", "data": "synthetic (BASELINE config 2 distributions)",
+        "config": {"workload": "BASELINE configs[1]: DeltaNet 16/32 heads x 128, 4096-token prefill in 512-row steps "
+                               "then 256 single-token steps", "kernel": "conv_delta_kernel (token-sequential)"},
+        "roofline": {"bound": "latency (token-sequential recurrence)", "state_bytes_per_token": 2 * n_v * D * D * 4},
+        "cpu_baseline": {"value": nS / cpu_s, "unit": "tok/s", "cores": 1, "kind": "port",
+                         "sample": f"oracle conv + delta over {nS} tokens"},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_mtp(args):
+    """the 9B-shape model with its MTP head. A 12K-token prefix
+    is prefilled once (with the MTP layer fed, as worker.rs:330-336) and snapshotted;
+    every turn restores it, feeds fresh random ids up to 16K, then decodes greedily with
+    draft-1 / verify-2 speculation exactly as worker.rs:197-255 (accept iff the verify
+    row's argmax is the draft, else roll back). Reports the acceptance rate and tok/s."""
+    import torch
+
+    from sensenova_b200.config import nine_b
+    from sensenova_b200.engine import Engine
+
+    torch.cuda.set_device(0)
+    cfg = nine_b()
+    prefix, full, dec = 12288, 16384, 32
+    eng = Engine.synthetic(cfg, full + dec + 64, args.seed, args.quant, mtp=True)
+    rng = np.random.default_rng(args.seed)
+    chunk = 512
+
+    def feed(toks, start):
+        lg = None
+        for c0 in range(0, len(toks), chunk):
+            c1 = min(c0 + chunk, len(toks))
+            pos = [[start + i] * 3 for i in range(c0, c1)]
+            lg = eng.forward_mm(toks[c0:c1], pos, (), 1 if c1 == len(toks) else 0, False)
+            a, r0 = start + c0, 1 if start + c0 == 0 else 0
+            if r0 < c1 - c0:
+                eng.mtp(r0, toks[c0 + r0:c1], [[a + i - 1] * 3 for i in range(r0, c1 - c0)], a + r0 - 1, False)
+        return lg
+
+    t0 = time.perf_counter()
+    feed(rng.integers(0, cfg.vocab, prefix).tolist(), 0)
+    eng.snapshot(0)
+    torch.cuda.synchronize()
+    prefix_s = time.perf_counter() - t0
+    drafted = accepted = produced = 0
+    dec_s = feed_s = 0.0
+    for turn in range(args.turns):
+        eng.restore(0, prefix)
+        t1 = time.perf_counter()
+        lg = feed(rng.integers(0, cfg.vocab, full - prefix).tolist(), prefix)
+        torch.cuda.synchronize()
+        feed_s += time.perf_counter() - t1
+        t2 = time.perf_counter()
+        tok = int(np.argmax(lg[0]))
+        rope = full
+        mtp_in = (eng.hid_rows(), [tok], [[full - 1] * 3], full - 1)
+        n_out = 0
+        while n_out < dec:
+            r0, toks, pos, slot0 = mtp_in
+            d = eng.mtp(r0, toks, pos, slot0, True)
+            slot = eng.pos
+            a0, a1 = eng.forward_greedy([tok, d], [[rope] * 3, [rope + 1] * 3], 2, True)
+            drafted += 1
+            if a0 == d:
+                accepted += 1
+                n_out += 2
+                tok = a1
+                mtp_in = (1, [d, tok], [[rope] * 3, [rope + 1] * 3], slot)
+                rope += 2
+            else:
+                eng.rollback()
+                n_out += 1
+                tok = a0
+                mtp_in = (1, [tok], [[rope] * 3], slot)
+                rope += 1
+        torch.cuda.synchronize()
+        dec_s += time.perf_counter() - t2
+        produced += n_out
+    line = {
+        "metric": "MTP speculative decode at 16K context: acceptance rate and tok/s",
+        "value": produced / dec_s, "unit": "tok/s", "n_gpus": 1, "higher_is_better": True,
+        "acceptance": accepted / max(drafted, 1), "drafted": drafted, "accepted": accepted,
+        "e2e_tok_s_with_feed": produced / (dec_s + feed_s), "feed_tok_s": args.turns * (full - prefix) / feed_s,
+        "prefix_prefill_s": prefix_s, "turns": args.turns, "dtype": "f32 (int8 weights)", "data": "synthetic",
+        "config": {"workload": f"BASELINE configs[3]: 12K-token prefix snapshot, feed to 16K, {dec} tokens per turn "
+                               f"with draft-1/verify-2, {args.turns} turns (1000 named; bounded sample)",
+                   "quant": args.quant},
+    }
+    print(json.dumps(line), flush=True)
+    eng.close()
+    return 0
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference(args)
     if args.workload == "gemv":
         return run_gemv_only(args)
+    if args.workload == "deltanet":
+        return run_deltanet(args)
+    if args.workload == "mtp":
+        return run_mtp(args)
     return run_ours(args)
 
 

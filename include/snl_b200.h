@@ -201,6 +201,11 @@ int snl_conv(const snl_step_u* step, const snl_lin_p* p, const float* proj, floa
  * gated RMSNorm; state [n_v, 128, 128] f32 (row i = key dim, column j = value dim). */
 int snl_delta(const snl_step_u* step, const snl_lin_p* p, const float* proj, const float* conv_out,
               float* state, const float* lw, float* out, float* state_ckpt, void* stream);
+/* conv followed by delta in one kernel, the engine's form: no conv_out buffer; the
+ * first value head of each key-head group owns that group's q/k conv state. Same
+ * arguments and results as snl_conv then snl_delta. */
+int snl_conv_delta(const snl_step_u* step, const snl_lin_p* p, const float* proj, float* conv_state, float* state,
+                   const float* lw, float* out, float* conv_ckpt, float* state_ckpt, void* stream);
 
 /* ---- kernel level: sampling ----------------------------------------------------- */
 

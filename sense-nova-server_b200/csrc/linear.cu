@@ -281,3 +281,12 @@ extern "C" int snl_delta(const snl_step_u* step, const snl_lin_p* p, const float
   if (step->ckpt > 0 && !state_ckpt) return snl::fail(SNL_E_INVALID, "snl_delta: ckpt needs state_ckpt");
   return snl::launch_delta(snl::step_val(*step), *p, proj, conv_out, state, lw, out, state_ckpt, (cudaStream_t)stream);
 }
+extern "C" int snl_conv_delta(const snl_step_u* step, const snl_lin_p* p, const float* proj, float* conv_state,
+                              float* state, const float* lw, float* out, float* conv_ckpt, float* state_ckpt,
+                              void* stream) {
+  if (!step || !p || !proj || !conv_state || !state || !lw || !out)
+    return snl::fail(SNL_E_INVALID, "snl_conv_delta: null argument");
+  if (step->ckpt > 0 && (!conv_ckpt || !state_ckpt)) return snl::fail(SNL_E_INVALID, "snl_conv_delta: ckpt needs buffers");
+  return snl::launch_conv_delta(snl::step_val(*step), *p, proj, conv_state, state, lw, out, conv_ckpt, state_ckpt,
+                                (cudaStream_t)stream);
+}

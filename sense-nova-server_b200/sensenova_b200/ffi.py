@@ -110,6 +110,7 @@ SIGNATURES = {
     "snl_attn_combine": (i32, [P(StepU), P(AttnP), vp, vp, vp, vp]),
     "snl_conv": (i32, [P(StepU), P(LinP), vp, vp, vp, vp, vp, vp]),
     "snl_delta": (i32, [P(StepU), P(LinP), vp, vp, vp, vp, vp, vp, vp]),
+    "snl_conv_delta": (i32, [P(StepU), P(LinP), vp, vp, vp, vp, vp, vp, vp, vp]),
     "snl_argmax": (i32, [vp, u32, u32, vp, vp]),
     "snl_argmax_noalloc": (i32, [vp, u32, u32, vp, vp]),
     "snl_synth_quant": (i32, [u64, C.c_char_p, i32, sz, sz, vp, vp, vp]),

@@ -396,6 +396,32 @@ def test_conv(T, lib, orc, m, ckpt):
         assert np.array_equal(host(ckd), ck_ref)
 
 
+@pytest.mark.parametrize("m,ckpt", [(1, 0), (2, 1), (40, 0), (512, 0)])
+def test_conv_delta_fused(T, lib, orc, m, ckpt):
+    """The engine's fused conv + delta kernel (snl_conv_delta) against the oracle's
+    conv then delta, states and checkpoints included."""
+    rng = np.random.default_rng(30 + m)
+    lpp, proj, lw, cd = lin_case(rng, m)
+    cs = rng.standard_normal((3, cd)).astype(np.float32)
+    S = (0.05 * rng.standard_normal((32, 128, 128))).astype(np.float32)
+    st = StepU(m, 0, 1, ckpt)
+    conv_out = np.zeros((m, cd), np.float32)
+    cs_ref, cck_ref = cs.copy(), np.zeros((3, cd), np.float32)
+    orc.conv(st, lpp, proj, conv_out, cs_ref, lw, cck_ref)
+    out_ref, S_ref, sck_ref = np.zeros((m, 4096), np.float32), S.copy(), np.zeros_like(S)
+    orc.delta(st, lpp, proj, conv_out, S_ref, lw, out_ref, sck_ref)
+    out, csd, Sd = T.zeros((m, 4096), device="cuda"), dev(T, cs), dev(T, S)
+    cck, sck = T.zeros((3, cd), device="cuda"), T.zeros(S.shape, device="cuda")
+    call(lib.snl_conv_delta(C.byref(st), C.byref(lpp), ptr(dev(T, proj)), ptr(csd), ptr(Sd), ptr(dev(T, lw)), ptr(out),
+                            ptr(cck), ptr(sck), None))
+    assert rel(host(out), out_ref) < TOL
+    assert rel(host(Sd), S_ref) < TOL
+    assert np.array_equal(host(csd), cs_ref)
+    if ckpt:
+        assert np.array_equal(host(cck), cck_ref)
+        assert rel(host(sck), sck_ref) < TOL
+
+
 @pytest.mark.parametrize("m,ckpt", [(1, 0), (2, 1), (24, 0)])
 def test_delta(T, lib, orc, m, ckpt):
     rng = np.random.default_rng(10 + m)
