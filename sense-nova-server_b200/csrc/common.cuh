@@ -167,6 +167,11 @@ int launch_delta(StepRef st, const snl_lin_p& p, const float* proj, const float*
 int launch_conv_delta(StepRef st, const snl_lin_p& p, const float* proj, float* conv_state, float* state,
                       const float* lw, float* out, float* conv_ckpt, float* state_ckpt, cudaStream_t s,
                       XOut xo = XOut());
+// Chunked conv + delta for prefill steps (linear.cu): host row count m, no checkpoint.
+constexpr uint32_t kChunkedMinRows = 16;  // steps of at least this many rows use it
+int launch_conv_delta_chunked(uint32_t m, const snl_lin_p& p, const float* proj, float* conv_state, float* state,
+                              const float* lw, float* out, float* conv_out, float* scratch, cudaStream_t s);
+size_t conv_delta_chunked_scratch(const snl_lin_p& p, uint32_t m);
 int launch_argmax(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_idx, cudaStream_t s);
 int launch_embed(const uint32_t* tokens, uint32_t m, const int8_t* q, const float* s_, uint32_t h, uint32_t vocab,
                  float* x, int* err_flag, cudaStream_t s, unsigned long long* step_ctr = nullptr);

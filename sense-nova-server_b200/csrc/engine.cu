@@ -137,6 +137,7 @@ struct snl_engine {
   uint32_t pstride = 0;
   // Router partial sums written by the residual-merging GEMV for the next mHC norm.
   float* rpart = nullptr;
+  float* dn_scratch = nullptr;  // chunk records of the chunked delta rule (prefill)
   bool rpart_ready = false;
 
   // Per-op timing of one eager step (snl_engine_profile).
@@ -414,9 +415,16 @@ int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
       float* sc = e->lin_ckpt + lin_slot * e->state_elems;
       const float* lw = find_f(e, L + "lin");
       const double cdim = (double)lp.conv_dim;
-      SNL_TRY(timed(e, "ConvDelta", 4.0 * (2.0 * e->state_elems + 10.0 * cdim + m * (cdim + 2 * 4096.0)), [&] {
-        return launch_conv_delta(st, lp, e->proj, cs, ss, lw, e->attn_out, cc, sc, e->stream, xo);
-      }));
+      if (!tc && m >= kChunkedMinRows && st.val.ckpt == 0) {
+        // Prefill step: the chunked delta rule (conv_out in act, chunk records in dn_scratch).
+        SNL_TRY(timed(e, "ConvDeltaChunked", 4.0 * (2.0 * e->state_elems + m * (3.0 * cdim + 2 * 4096.0)), [&] {
+          return launch_conv_delta_chunked(m, lp, e->proj, cs, ss, lw, e->attn_out, e->act, e->dn_scratch, e->stream);
+        }));
+      } else {
+        SNL_TRY(timed(e, "ConvDelta", 4.0 * (2.0 * e->state_elems + 10.0 * cdim + m * (cdim + 2 * 4096.0)), [&] {
+          return launch_conv_delta(st, lp, e->proj, cs, ss, lw, e->attn_out, cc, sc, e->stream, xo);
+        }));
+      }
       SNL_TRY(proj_out(*find_q(e, L + "out_proj"), e->attn_out, snl_synth::lin_value_dim(c), mhc ? 1 : 0, false,
                        mhc ? find_f(e, L + "mhc_ffn") : nullptr, nullptr, (uint32_t)(2 * vi)));
       lin_slot++;
@@ -1093,6 +1101,7 @@ extern "C" int snl_engine_finalize(snl_engine* e) {
   SNL_TRY(dalloc(e, &e->xpl, (size_t)8 * e->pstride));
   SNL_TRY(dalloc(e, &e->xpl_act, (size_t)8 * e->pstride));
   SNL_TRY(dalloc(e, &e->rpart, (size_t)4 * ((h + 15) / 16) * 9));
+  SNL_TRY(dalloc(e, &e->dn_scratch, conv_delta_chunked_scratch(lin_p(e), (uint32_t)MAX_M)));
   if (getenv("SNL_NO_TC")) e->use_tc = false;
   SNL_TRY(dalloc(e, &e->step_d, 1));
   SNL_TRY(dalloc(e, &e->mstep_d, 1));

@@ -5,6 +5,8 @@
 // A_log[n_v] | dt_bias[n_v] | norm w[128]. The recurrent state of value head h is a
 // [128 (key dim i), 128 (value dim j)] f32 matrix; column j evolves independently of
 // the other columns given the head's q, k, beta and decay.
+#include <mutex>
+
 #include "common.cuh"
 #include "ptx.cuh"
 
@@ -235,6 +237,238 @@ __global__ void __launch_bounds__(DV * kCdParts) conv_delta_kernel(StepRef sr, s
   for (uint32_t i = 0; i < kCdRows; i++) state[sbase + i * DV] = S[i];
 }
 
+// ---------------------------------------------------------------------------
+// Chunked form of the gated delta rule (prefill steps): the same recurrence as
+// delta_kernel, regrouped over chunks of kDnC tokens so that most of the work is
+// matrix products that run in parallel over (head, chunk). Within a chunk starting from
+// state S0 (token t: normalised q_t, k_t, v_t, beta_t, log decay l_t, Lambda_t = sum of
+// l_s for s <= t in the chunk, gamma_t = exp(Lambda_t)):
+//   S_t   = gamma_t S0 + sum_{s<=t} (gamma_t/gamma_s) k_s d_s^T
+//   d_t   = beta_t (v_t - S~_t^T k_t),  S~_t = (decayed S_{t-1})
+//   => (I + L) D = diag(beta) (V - Gamma K S0),  L[t][s] = beta_t (gamma_t/gamma_s) k_t.k_s (s < t)
+//   => D = U - W S0 with T = (I + L)^-1 diag(beta), W = T Gamma K, U = T V
+//   o_t  = S_t^T q_t  =>  O = P S0 + R, P = Gamma Q - M W, R = M U,
+//          M[t][s] = (gamma_t/gamma_s) q_t.k_s (s <= t)
+//   S_C  = gamma_C S0 + Kd^T D,  Kd[s] = (gamma_C/gamma_s) k_s.
+// dn_prep_kernel builds P, R, W, U, Kd and gamma_C for every (head, chunk) in parallel;
+// dn_scan_kernel carries the state through the chunks (each 32-column slice of a head's
+// state is independent, so a head spans 4 CTAs); dn_norm_kernel applies the gated
+// RMSNorm of the outputs. All of it is fp32.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kDnC = 64;                 // tokens per chunk
+constexpr uint32_t kDnCols = 32;              // state columns per scan CTA
+constexpr uint32_t kDnChunkFloats = 5 * kDnC * DK + 4;  // P, R, W, U, Kd, gamma_C (+pad)
+
+struct DnScratch {
+  float* chunks;  // [n_v][n_chunks][kDnChunkFloats]
+};
+
+__global__ void __launch_bounds__(256) dn_prep_kernel(uint32_t m, snl_lin_p p, const float* __restrict__ proj,
+                                                      const float* __restrict__ conv_out, const float* __restrict__ lw,
+                                                      float* __restrict__ chunks) {
+  extern __shared__ __align__(16) float dsm[];
+  float* kn = dsm;                    // [C][128]
+  float* qn = kn + kDnC * DK;         // [C][128]
+  float* vv = qn + kDnC * DK;         // [C][128]
+  float* X = vv + kDnC * DV;          // [C][C]: L, then (I+L)^-1
+  float* Mq = X + kDnC * kDnC;        // [C][C]
+  float* W = Mq + kDnC * kDnC;        // [C][128]
+  float* U = W + kDnC * DK;           // [C][128]
+  __shared__ float lam[kDnC], beta[kDnC];
+  const uint32_t c = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t t0 = c * kDnC, ce = min(kDnC, m - t0);
+  const uint32_t kh = h / (p.n_v / p.n_k), cd = p.conv_dim, key_dim = p.n_k * DK;
+  const uint32_t b_off = cd + p.n_v * DV, a_off = b_off + p.n_v;
+  // 1. q, k, v rows of the chunk (zero past the step's end), then per-token norms.
+  for (uint32_t e = tid; e < kDnC * DK; e += blockDim.x) {
+    const uint32_t t = e / DK, i = e % DK;
+    const bool in = t < ce;
+    const uint64_t row = (uint64_t)(t0 + t) * cd;
+    qn[e] = in ? conv_out[row + kh * DK + i] : 0.f;
+    kn[e] = in ? conv_out[row + key_dim + kh * DK + i] : 0.f;
+    vv[e] = in ? conv_out[row + 2 * key_dim + h * DV + i] : 0.f;
+  }
+  __syncthreads();
+  for (uint32_t t = warp; t < kDnC; t += blockDim.x / 32) {
+    float sq = 0.f, sk = 0.f;
+    for (uint32_t i = lane; i < DK; i += 32) {
+      sq = fmaf(qn[t * DK + i], qn[t * DK + i], sq);
+      sk = fmaf(kn[t * DK + i], kn[t * DK + i], sk);
+    }
+    sq = warp_sum(sq);
+    sk = warp_sum(sk);
+    const float rq = rsqrtf(sq + 1e-6f) * rsqrtf((float)DK), rk = rsqrtf(sk + 1e-6f);
+    for (uint32_t i = lane; i < DK; i += 32) {
+      qn[t * DK + i] *= rq;
+      kn[t * DK + i] *= rk;
+    }
+  }
+  if (tid == 0) {
+    const float neg_a = -__expf(lw[(uint64_t)cd * 4 + h]);
+    const float dt_bias = lw[(uint64_t)cd * 4 + p.n_v + h];
+    float acc = 0.f;
+    for (uint32_t t = 0; t < kDnC; t++) {
+      float bt = 0.f, lt = 0.f;
+      if (t < ce) {
+        const uint64_t prow = (uint64_t)(t0 + t) * p.proj_stride;
+        bt = 1.0f / (1.0f + __expf(-proj[prow + b_off + h]));
+        const float araw = proj[prow + a_off + h] + dt_bias;
+        const float sp = araw <= 20.0f ? log1pf(__expf(araw)) : araw;
+        lt = neg_a * sp;
+      }
+      acc += lt;
+      lam[t] = acc;
+      beta[t] = bt;
+    }
+  }
+  __syncthreads();
+  // 2. L (strictly lower) and M (lower with diagonal) from the Gram matrices.
+  for (uint32_t e = tid; e < kDnC * kDnC; e += blockDim.x) {
+    const uint32_t t = e / kDnC, s2 = e % kDnC;
+    float gk = 0.f, gq = 0.f;
+    if (s2 <= t) {
+      const float4* a4 = reinterpret_cast<const float4*>(kn + t * DK);
+      const float4* q4 = reinterpret_cast<const float4*>(qn + t * DK);
+      const float4* b4 = reinterpret_cast<const float4*>(kn + s2 * DK);
+#pragma unroll 8
+      for (uint32_t i = 0; i < DK / 4; i++) {
+        const float4 x = a4[i], y = b4[i], z = q4[i];
+        gk = fmaf(x.x, y.x, fmaf(x.y, y.y, fmaf(x.z, y.z, fmaf(x.w, y.w, gk))));
+        gq = fmaf(z.x, y.x, fmaf(z.y, y.y, fmaf(z.z, y.z, fmaf(z.w, y.w, gq))));
+      }
+    }
+    const float r = s2 <= t ? __expf(lam[t] - lam[s2]) : 0.f;
+    X[e] = s2 < t ? beta[t] * r * gk : 0.f;
+    Mq[e] = s2 <= t ? r * gq : 0.f;
+  }
+  __syncthreads();
+  // 3. (I + L)^-1 by forward substitution, row by row (unit lower triangular), in place:
+  //    X[t][s] = -sum_{r=s}^{t-1} L[t][r] X[r][s]. Row t's L entries are read before
+  //    the row is overwritten (registers), earlier rows already hold X.
+  for (uint32_t t = 1; t < kDnC; t++) {
+    float xv = 0.f;
+    if (tid < t) {
+      for (uint32_t r = tid; r < t; r++) {
+        const float lr = X[t * kDnC + r];
+        const float xr = r == tid ? 1.f : X[r * kDnC + tid];
+        xv = fmaf(lr, xr, xv);
+      }
+    }
+    __syncthreads();
+    if (tid < t) X[t * kDnC + tid] = -xv;
+    __syncthreads();
+  }
+  // T = X diag(beta) (X has an implicit unit diagonal).
+  // 4. W = T Gamma K, U = T V (row t: sum over s <= t).
+  for (uint32_t e = tid; e < kDnC * DK; e += blockDim.x) {
+    const uint32_t t = e / DK, i = e % DK;
+    float w = 0.f, u = 0.f;
+    for (uint32_t s2 = 0; s2 <= t; s2++) {
+      const float tt = (s2 == t ? 1.f : X[t * kDnC + s2]) * beta[s2];
+      w = fmaf(tt * __expf(lam[s2]), kn[s2 * DK + i], w);
+      u = fmaf(tt, vv[s2 * DV + i], u);
+    }
+    W[e] = w;
+    U[e] = u;
+  }
+  __syncthreads();
+  // 5. P = Gamma Q - M W, R = M U, Kd = (gamma_C / gamma_s) k_s; write the chunk record.
+  float* rec = chunks + ((uint64_t)h * gridDim.x + c) * kDnChunkFloats;
+  float* P = rec;
+  float* R = P + kDnC * DK;
+  float* Wg = R + kDnC * DV;
+  float* Ug = Wg + kDnC * DK;
+  float* Kd = Ug + kDnC * DV;
+  const float lam_c = lam[kDnC - 1];
+  for (uint32_t e = tid; e < kDnC * DK; e += blockDim.x) {
+    const uint32_t t = e / DK, i = e % DK;
+    float pw = 0.f, ru = 0.f;
+    for (uint32_t s2 = 0; s2 <= t; s2++) {
+      const float mm = Mq[t * kDnC + s2];
+      pw = fmaf(mm, W[s2 * DK + i], pw);
+      ru = fmaf(mm, U[s2 * DV + i], ru);
+    }
+    P[e] = fmaf(__expf(lam[t]), qn[e], -pw);
+    R[e] = ru;
+    Wg[e] = W[e];
+    Ug[e] = U[e];
+    Kd[e] = __expf(lam_c - lam[t]) * kn[e];
+  }
+  if (tid == 0) rec[5 * kDnC * DK] = __expf(lam_c);
+}
+
+// Carries one head's state slice (all 128 rows, kDnCols columns) through the chunks of
+// the step, writing the pre-norm outputs O = P S0 + R of its columns.
+__global__ void __launch_bounds__(256) dn_scan_kernel(uint32_t m, uint32_t n_chunks, snl_lin_p p,
+                                                      const float* __restrict__ chunks, float* __restrict__ state,
+                                                      float* __restrict__ out) {
+  extern __shared__ __align__(16) float ssm[];
+  float* S = ssm;                      // [128][kDnCols]
+  float* A = S + DK * kDnCols;         // [C][128]: P, then Kd
+  float* B = A + kDnC * DK;            // [C][128]: W
+  float* D = B + kDnC * DK;            // [C][kDnCols]
+  const uint32_t slice = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  const uint32_t j0 = slice * kDnCols;
+  float* Sg = state + (uint64_t)h * DK * DV;
+  for (uint32_t e = tid; e < DK * kDnCols; e += blockDim.x) S[e] = Sg[(e / kDnCols) * DV + j0 + e % kDnCols];
+  for (uint32_t c = 0; c < n_chunks; c++) {
+    const float* rec = chunks + ((uint64_t)h * n_chunks + c) * kDnChunkFloats;
+    const float* P = rec;
+    const float* R = P + kDnC * DK;
+    const float* Wg = R + kDnC * DV;
+    const float* Ug = Wg + kDnC * DK;
+    const float* Kd = Ug + kDnC * DV;
+    const float gC = rec[5 * kDnC * DK];
+    const uint32_t t0 = c * kDnC, ce = min(kDnC, m - t0);
+    __syncthreads();
+    for (uint32_t e = tid; e < kDnC * DK / 4; e += blockDim.x) {
+      reinterpret_cast<float4*>(A)[e] = reinterpret_cast<const float4*>(P)[e];
+      reinterpret_cast<float4*>(B)[e] = reinterpret_cast<const float4*>(Wg)[e];
+    }
+    __syncthreads();
+    // O = P S + R and D = U - W S for the slice: thread -> (token t, column j), 8 each.
+    for (uint32_t e = tid; e < kDnC * kDnCols; e += blockDim.x) {
+      const uint32_t t = e / kDnCols, j = e % kDnCols;
+      float o = 0.f, w = 0.f;
+#pragma unroll 8
+      for (uint32_t i = 0; i < DK; i++) {
+        const float sv = S[i * kDnCols + j];
+        o = fmaf(A[t * DK + i], sv, o);
+        w = fmaf(B[t * DK + i], sv, w);
+      }
+      D[e] = Ug[t * DV + j0 + j] - w;
+      if (t < ce) out[(uint64_t)(t0 + t) * p.n_v * DV + h * DV + j0 + j] = o + R[t * DV + j0 + j];
+    }
+    __syncthreads();
+    for (uint32_t e = tid; e < kDnC * DK / 4; e += blockDim.x)
+      reinterpret_cast<float4*>(A)[e] = reinterpret_cast<const float4*>(Kd)[e];
+    __syncthreads();
+    // S = gamma_C S + Kd^T D.
+    for (uint32_t e = tid; e < DK * kDnCols; e += blockDim.x) {
+      const uint32_t i = e / kDnCols, j = e % kDnCols;
+      float acc = 0.f;
+#pragma unroll 8
+      for (uint32_t t = 0; t < kDnC; t++) acc = fmaf(A[t * DK + i], D[t * kDnCols + j], acc);
+      S[e] = fmaf(gC, S[e], acc);
+    }
+  }
+  __syncthreads();
+  for (uint32_t e = tid; e < DK * kDnCols; e += blockDim.x) Sg[(e / kDnCols) * DV + j0 + e % kDnCols] = S[e];
+}
+
+// Gated RMSNorm of the delta outputs (linear.wgsl's tail of `delta`), in place.
+__global__ void __launch_bounds__(DV) dn_norm_kernel(snl_lin_p p, const float* __restrict__ proj,
+                                                     const float* __restrict__ lw, float* __restrict__ out) {
+  __shared__ float red[32];
+  const uint32_t t = blockIdx.x, h = blockIdx.y, j = threadIdx.x;
+  const uint64_t o_i = (uint64_t)t * p.n_v * DV + h * DV + j;
+  const float o = out[o_i];
+  const float var_o = block_sum(o * o, red) / (float)DV;
+  const float z = proj[(uint64_t)t * p.proj_stride + p.conv_dim + h * DV + j];
+  const float norm_w = lw[(uint64_t)p.conv_dim * 4 + 2 * p.n_v + j];
+  out[o_i] = o * rsqrtf(var_o + p.eps) * norm_w * (z / (1.0f + __expf(-z)));
+}
+
 }  // namespace
 
 static int check_lin(const snl_lin_p& p) {
@@ -259,6 +493,40 @@ int launch_delta(StepRef st, const snl_lin_p& p, const float* proj, const float*
   return SNL_OK;
 }
 
+// Chunked prefill form: conv (channel-parallel) into conv_out, then the three chunked
+// delta kernels. m is the host's row count; no checkpoint. scratch: the chunk records,
+// n_v * ceil(m / 64) * (5 * 64 * 128 + 4) floats.
+int launch_conv_delta_chunked(uint32_t m, const snl_lin_p& p, const float* proj, float* conv_state, float* state,
+                              const float* lw, float* out, float* conv_out, float* scratch, cudaStream_t s) {
+  if (int rc = check_lin(p)) return rc;
+  if (m == 0) return SNL_OK;
+  const snl_step_u sv{m, 0, 1, 0};
+  conv_kernel<<<(p.conv_dim + 255) / 256, 256, 0, s>>>(step_val(sv), p, proj, conv_out, conv_state, lw, nullptr);
+  SNL_LAUNCH_CHECK("conv");
+  const uint32_t nch = (m + kDnC - 1) / kDnC;
+  const size_t prep_smem = (3 * kDnC * DK + 2 * kDnC * kDnC + 2 * kDnC * DK) * sizeof(float);
+  const size_t scan_smem = (DK * kDnCols + 2 * kDnC * DK + kDnC * kDnCols) * sizeof(float);
+  static bool attr[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr[dev]) {
+    SNL_CUDA_TRY(cudaFuncSetAttribute(dn_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem));
+    SNL_CUDA_TRY(cudaFuncSetAttribute(dn_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)scan_smem));
+    attr[dev] = true;
+  }
+  dn_prep_kernel<<<dim3(nch, p.n_v), 256, prep_smem, s>>>(m, p, proj, conv_out, lw, scratch);
+  SNL_LAUNCH_CHECK("dn_prep");
+  dn_scan_kernel<<<dim3(DV / kDnCols, p.n_v), 256, scan_smem, s>>>(m, nch, p, scratch, state, out);
+  SNL_LAUNCH_CHECK("dn_scan");
+  dn_norm_kernel<<<dim3(m, p.n_v), DV, 0, s>>>(p, proj, lw, out);
+  SNL_LAUNCH_CHECK("dn_norm");
+  return SNL_OK;
+}
+
+size_t conv_delta_chunked_scratch(const snl_lin_p& p, uint32_t m) {
+  return (size_t)p.n_v * ((m + kDnC - 1) / kDnC) * kDnChunkFloats;
+}
+
 int launch_conv_delta(StepRef st, const snl_lin_p& p, const float* proj, float* conv_state, float* state,
                       const float* lw, float* out, float* conv_ckpt, float* state_ckpt, cudaStream_t s, XOut xo) {
   if (int rc = check_lin(p)) return rc;
@@ -281,12 +549,44 @@ extern "C" int snl_delta(const snl_step_u* step, const snl_lin_p* p, const float
   if (step->ckpt > 0 && !state_ckpt) return snl::fail(SNL_E_INVALID, "snl_delta: ckpt needs state_ckpt");
   return snl::launch_delta(snl::step_val(*step), *p, proj, conv_out, state, lw, out, state_ckpt, (cudaStream_t)stream);
 }
+namespace snl {
+namespace {
+// Per-device scratch of the chunked path for kernel-level callers, grown on demand.
+float* chunk_scratch(size_t floats) {
+  static std::mutex mu;
+  static float* buf[64] = {nullptr};
+  static size_t cap[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  if (cap[dev] < floats) {
+    if (buf[dev]) cudaFree(buf[dev]);
+    buf[dev] = nullptr;
+    cap[dev] = 0;
+    void* ptr = nullptr;
+    if (cudaMalloc(&ptr, floats * sizeof(float)) != cudaSuccess) return nullptr;
+    buf[dev] = static_cast<float*>(ptr);
+    cap[dev] = floats;
+  }
+  return buf[dev];
+}
+}  // namespace
+}  // namespace snl
+
 extern "C" int snl_conv_delta(const snl_step_u* step, const snl_lin_p* p, const float* proj, float* conv_state,
                               float* state, const float* lw, float* out, float* conv_ckpt, float* state_ckpt,
                               void* stream) {
   if (!step || !p || !proj || !conv_state || !state || !lw || !out)
     return snl::fail(SNL_E_INVALID, "snl_conv_delta: null argument");
   if (step->ckpt > 0 && (!conv_ckpt || !state_ckpt)) return snl::fail(SNL_E_INVALID, "snl_conv_delta: ckpt needs buffers");
+  if (step->m >= snl::kChunkedMinRows && step->ckpt == 0) {
+    // Prefill-sized steps: the chunked form (conv_out and chunk records in scratch).
+    const size_t conv_floats = (size_t)step->m * p->conv_dim;
+    float* buf = snl::chunk_scratch(conv_floats + snl::conv_delta_chunked_scratch(*p, step->m));
+    if (!buf) return snl::fail(SNL_E_OOM, "snl_conv_delta: scratch");
+    return snl::launch_conv_delta_chunked(step->m, *p, proj, conv_state, state, lw, out, buf, buf + conv_floats,
+                                          (cudaStream_t)stream);
+  }
   return snl::launch_conv_delta(snl::step_val(*step), *p, proj, conv_state, state, lw, out, conv_ckpt, state_ckpt,
                                 (cudaStream_t)stream);
 }
