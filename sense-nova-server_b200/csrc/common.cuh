@@ -98,6 +98,9 @@ __device__ __forceinline__ void xout_store(const XOut& xo, uint32_t t, uint32_t 
   xo.planes[(uint64_t)(2 * t + 1) * xo.stride + i] = lo;
 }
 
+// Stride of the per-group norm partials a residual-merging GEMV writes (gemv_mma.cuh).
+constexpr int kRpStride = 12;
+
 // Device address of the library's device error word (bit 0: a bounded wait gave up).
 int device_error_word(int** out);
 

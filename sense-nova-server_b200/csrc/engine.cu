@@ -67,9 +67,11 @@ struct FT {
 };
 
 uint32_t parts_for(size_t m, size_t total) {
-  // engine.rs:827: split-K attention only for short steps.
+  // engine.rs:827: split-K attention only for short steps. The reference splits every
+  // 256 keys; here a part is 64 keys (one 8-key group per warp of attend_kernel), so short
+  // contexts spread over more CTAs. The split changes only the summation order.
   if (m > 4) return 1;
-  size_t p = (total + 255) / 256;
+  size_t p = (total + 63) / 64;
   return (uint32_t)std::min<size_t>(std::max<size_t>(p, 1), MAX_PARTS);
 }
 
@@ -132,8 +134,10 @@ struct snl_engine {
   // Steps of <= 4 rows run their projections on the tensor-core GEMV, whose x operand is
   // these planes ([8][pstride] halves), written by the kernel that produces each input.
   bool use_tc = true;
+  bool use_fused_norm = true;
   __half* xpl = nullptr;
   __half* xpl_act = nullptr;  // planes of the SwiGLU output, written by the gate_up GEMV
+  __half* xpl_norm = nullptr;  // both residual streams x the next norm weight (fused norms)
   uint32_t pstride = 0;
   // Router partial sums written by the residual-merging GEMV for the next mHC norm.
   float* rpart = nullptr;
@@ -295,14 +299,40 @@ int push_norm(snl_engine* e, StepRef st, uint32_t m, const float* router, const 
 // One projection on the tensor-core GEMV (x = the planes). mode 0 writes y; mode 1
 // merges into the residual x like `merge` (engine.rs:471-480) and can expand stream 0
 // into stream 1 (the merge mode 3 that opens an mHC range).
+// A norm folded into the GEMV that consumes it (see GemvArgs::fused_norm): `on` when the
+// producing GEMV left the weighted streams in xpl_norm and the partials in rpart.
+struct NormFuse {
+  bool on = false;
+  const float* router = nullptr;
+};
+
 int matx(snl_engine* e, const QT& w, uint32_t rows, int mode, float* y, size_t y_stride, uint32_t merge_mode = 0,
-         int expand = 0, const float* rnext = nullptr, const __half* planes = nullptr, int tp_site = -1) {
+         int expand = 0, const float* rnext = nullptr, const __half* planes = nullptr, int tp_site = -1,
+         const NormFuse& nf_in = NormFuse(), const float* nw_out = nullptr) {
   GemvArgs a{};
   a.n = (uint32_t)w.rows;
   a.k = (uint32_t)w.cols;
   a.xplanes = planes ? planes : e->xpl;
   a.act_planes = e->xpl_act;
   a.act_stride = e->pstride;
+  uint32_t launch_rows = rows;
+  if (nf_in.on) {  // the x operand is the two weighted streams of each token
+    a.xplanes = e->xpl_norm;
+    a.fused_norm = 1;
+    a.nrpart = e->rpart;
+    a.nparts = (uint32_t)((e->cfg.hidden + 15) / 16);
+    a.nrouter = nf_in.router;
+    a.neps = e->cfg.eps;
+    a.niter = e->cfg.mhc_start >= 0 ? e->cfg.mhc_iterations : 0;
+    a.ncoef = e->coef;
+    launch_rows = 2 * rows;
+  }
+  if (nw_out) {  // leave the next norm's input for a fused consumer
+    a.nplanes = e->xpl_norm;
+    a.nstride = e->pstride;
+    a.nw = nw_out;
+    a.weight_one = 1.0f;
+  }
   if (tp_site >= 0 && e->tp.size > 1) {
     a.tp = e->tp.comm;
     a.tp_site = (uint32_t)tp_site;
@@ -318,11 +348,12 @@ int matx(snl_engine* e, const QT& w, uint32_t rows, int mode, float* y, size_t y
   a.merge_mode = (int)merge_mode;
   a.expand = expand;
   a.rnext = rnext;
-  a.rpart = e->rpart;
+  a.rpart = mode == 1 && (rnext || nw_out) ? e->rpart : nullptr;
   const double bytes = qbytes(w) + 4.0 * rows * (w.cols + w.rows);
   const std::string label = "mat n=" + std::to_string(w.rows) + (y == e->head_out ? " (head)" : "");
   SNL_TRY(timed(e, label, bytes, [&] {
-    if (w.tiles) return launch_gemv_tile(w.dtype, a, rows, w.tiles, w.tscales, e->stream);
+    if (w.tiles) return launch_gemv_tile(w.dtype, a, launch_rows, w.tiles, w.tscales, e->stream);
+    if (nf_in.on) return fail(SNL_E_STATE, "fused norm needs the tile layout");
     return launch_gemv_mma(w.dtype, a, rows, w.s, w.s_f16, e->stream);
   }));
   e->rpart_ready = rnext != nullptr;
@@ -350,8 +381,28 @@ int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
   const XOut xo = tc ? XOut{e->xpl, e->pstride} : XOut{};
   const double hb = 4.0 * m * h;
   // in-projection (x = normed residual) into y
+  // Fused norms (1-2 token rows on the tile path): a residual-merging GEMV leaves the next
+  // norm's weighted streams and partials, and the next projection finishes the norm.
+  const bool fuse = tc && m <= 2 && e->use_fused_norm;
+  bool fused_ready = false;  // xpl_norm and rpart hold the inputs of the upcoming norm
+  NormFuse pending;          // a norm deferred into the next projection
+  auto norm_step = [&](const float* router, const float* norm_w) -> int {
+    if (fuse && fused_ready) {
+      pending.on = true;
+      pending.router = router;
+      fused_ready = false;
+      return SNL_OK;
+    }
+    pending.on = false;
+    return push_norm(e, st, m, router, norm_w, xo);
+  };
+  auto take_pending = [&]() {
+    NormFuse f = pending;
+    pending.on = false;
+    return f;
+  };
   auto proj_in = [&](const QT& w, float* y, size_t y_stride) -> int {
-    if (tc) return matx(e, w, m, 0, y, y_stride);
+    if (tc) return matx(e, w, m, 0, y, y_stride, 0, 0, nullptr, nullptr, -1, take_pending());
     return mat(e, st, w, e->xn, h, y, y_stride, m);
   };
   // out-projection of `src` (K = src_dim) merged into the residual
@@ -359,8 +410,13 @@ int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
   // trades partials with the peers in its epilogue; the prefill GEMM writes this rank's
   // partial into the exchange region and an allreduce kernel sums the ranks' partials.
   auto proj_out = [&](const QT& w, const float* src, size_t src_dim, uint32_t merge_mode, bool expand,
-                      const float* rnext, const __half* planes, uint32_t site) -> int {
-    if (tc) return matx(e, w, m, 1, nullptr, 0, merge_mode, expand ? 1 : 0, rnext, planes, (int)site);
+                      const float* rnext, const __half* planes, uint32_t site, const float* next_norm_w) -> int {
+    if (tc) {
+      const float* nw = fuse ? next_norm_w : nullptr;
+      SNL_TRY(matx(e, w, m, 1, nullptr, 0, merge_mode, expand ? 1 : 0, rnext, planes, (int)site, NormFuse(), nw));
+      fused_ready = nw != nullptr;
+      return SNL_OK;
+    }
     if (e->tp.size > 1) {
       const uint64_t par = (((uint64_t)site + 1) & 1) * e->tp.comm.bp_elems;  // tp_sites is even
       float* part = e->tp.comm.bparts[e->tp.rank] + par;
@@ -383,9 +439,11 @@ int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
     const size_t li = e->plan[vi];
     const std::string L = "l" + std::to_string(li) + ".";
     const bool mhc = snl_synth::is_mhc(c, li);
-    if (mhc && (int32_t)li == c.mhc_start && !expanded)
+    if (mhc && (int32_t)li == c.mhc_start && !expanded) {
       SNL_TRY(timed(e, "Merge", 2 * hb, [&] { return launch_merge(st, layer_p(e, 3, false), e->x, e->coef, e->branch, m, e->stream); }));
-    SNL_TRY(push_norm(e, st, m, mhc ? find_f(e, L + "mhc_attn") : nullptr, find_f(e, L + "in_ln"), xo));
+      fused_ready = false;  // the streams changed after the fused inputs were written
+    }
+    SNL_TRY(norm_step(mhc ? find_f(e, L + "mhc_attn") : nullptr, find_f(e, L + "in_ln")));
     if (c.full_attention[li]) {
       SNL_TRY(proj_in(*find_q(e, L + "qkv"), e->proj, ap.proj_stride));
       const double kvd = (double)snl_synth::kv_dim(c), qd = (double)snl_synth::q_dim(c);
@@ -405,7 +463,8 @@ int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
       // o_proj's K shard: this rank's query heads within the attention it computed.
       const size_t xo_off = o_proj_offset(e);
       SNL_TRY(proj_out(*find_q(e, L + "o_proj"), e->attn_out + xo_off, snl_synth::q_dim(c), mhc ? 1 : 0, false,
-                       mhc ? find_f(e, L + "mhc_ffn") : nullptr, tc ? e->xpl + xo_off : nullptr, (uint32_t)(2 * vi)));
+                       mhc ? find_f(e, L + "mhc_ffn") : nullptr, tc ? e->xpl + xo_off : nullptr, (uint32_t)(2 * vi),
+                       find_f(e, L + "post_ln")));
       full_slot++;
     } else {
       SNL_TRY(proj_in(*find_q(e, L + "in_proj"), e->proj, lp.proj_stride));
@@ -426,15 +485,15 @@ int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
         }));
       }
       SNL_TRY(proj_out(*find_q(e, L + "out_proj"), e->attn_out, snl_synth::lin_value_dim(c), mhc ? 1 : 0, false,
-                       mhc ? find_f(e, L + "mhc_ffn") : nullptr, nullptr, (uint32_t)(2 * vi)));
+                       mhc ? find_f(e, L + "mhc_ffn") : nullptr, nullptr, (uint32_t)(2 * vi), find_f(e, L + "post_ln")));
       lin_slot++;
     }
-    SNL_TRY(push_norm(e, st, m, mhc ? find_f(e, L + "mhc_ffn") : nullptr, find_f(e, L + "post_ln"), xo));
+    SNL_TRY(norm_step(mhc ? find_f(e, L + "mhc_ffn") : nullptr, find_f(e, L + "post_ln")));
     const QT& gu = *find_q(e, L + "gate_up");
     const bool fused_swiglu = tc && gu.tiles && gu.pair_half;
     if (fused_swiglu) {
       // The gate_up GEMV finishes SwiGLU in its epilogue and writes the planes of act.
-      SNL_TRY(matx(e, gu, m, 2, nullptr, c.intermediate));
+      SNL_TRY(matx(e, gu, m, 2, nullptr, c.intermediate, 0, 0, nullptr, nullptr, -1, take_pending()));
     } else {
       SNL_TRY(proj_in(gu, e->proj, 2 * (size_t)c.intermediate));
       SNL_TRY(timed(e, "Swiglu", 12.0 * m * c.intermediate,
@@ -445,8 +504,9 @@ int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
                              (int32_t)e->plan[vi + 1] == c.mhc_start;
     const bool next_mhc = vi + 1 < e->plan.size() && snl_synth::is_mhc(c, e->plan[vi + 1]);
     const float* rnext = next_mhc ? find_f(e, "l" + std::to_string(e->plan[vi + 1]) + ".mhc_attn") : nullptr;
+    const float* next_ln = vi + 1 < e->plan.size() ? find_f(e, "l" + std::to_string(e->plan[vi + 1]) + ".in_ln") : nullptr;
     SNL_TRY(proj_out(*find_q(e, L + "down"), e->act, c.intermediate, mode, expand_next, rnext,
-                     fused_swiglu ? e->xpl_act : nullptr, (uint32_t)(2 * vi + 1)));
+                     fused_swiglu ? e->xpl_act : nullptr, (uint32_t)(2 * vi + 1), next_ln));
     expanded = expand_next;
   }
   return SNL_OK;
@@ -1100,7 +1160,9 @@ extern "C" int snl_engine_finalize(snl_engine* e) {
   e->pstride = (uint32_t)((std::max({h, I, snl_synth::q_dim(c), snl_synth::lin_value_dim(c)}) + 7) / 8 * 8);
   SNL_TRY(dalloc(e, &e->xpl, (size_t)8 * e->pstride));
   SNL_TRY(dalloc(e, &e->xpl_act, (size_t)8 * e->pstride));
-  SNL_TRY(dalloc(e, &e->rpart, (size_t)4 * ((h + 15) / 16) * 9));
+  SNL_TRY(dalloc(e, &e->xpl_norm, (size_t)8 * e->pstride));
+  if (getenv("SNL_NO_FUSED_NORM")) e->use_fused_norm = false;
+  SNL_TRY(dalloc(e, &e->rpart, (size_t)4 * ((h + 15) / 16) * kRpStride));
   SNL_TRY(dalloc(e, &e->dn_scratch, conv_delta_chunked_scratch(lin_p(e), (uint32_t)MAX_M)));
   if (getenv("SNL_NO_TC")) e->use_tc = false;
   SNL_TRY(dalloc(e, &e->step_d, 1));

@@ -25,6 +25,7 @@
 
 #include "common.cuh"
 #include "gemv_mma.cuh"
+#include "mhc.cuh"
 #include "ptx.cuh"
 
 namespace snl {
@@ -167,24 +168,7 @@ __global__ void __launch_bounds__(kWarpsK * 32) gemv_mma_kernel(GemvArgs a, cons
         for (int w = 0; w < kWarpsK; w++) v += red[w][tt][r];
         nx = gemv_epilogue(a, tt, row, v * kXPlaneScale);
       }
-      if (a.rnext) {  // warp-uniform
-        float rs[9];
-        const uint32_t d = 2 * a.h;
-#pragma unroll
-        for (int o = 0; o < 8; o++)
-          rs[o] = live ? fmaf(__ldg(a.rnext + (uint64_t)o * d + row), nx.x, __ldg(a.rnext + (uint64_t)o * d + a.h + row) * nx.y)
-                       : 0.f;
-        rs[8] = live ? fmaf(nx.x, nx.x, nx.y * nx.y) : 0.f;
-#pragma unroll
-        for (int o = 0; o < 9; o++) {
-#pragma unroll
-          for (int off = 8; off > 0; off >>= 1) rs[o] += __shfl_xor_sync(0xffffffffu, rs[o], off);
-        }
-        if (r == 0 && tt < M) {
-#pragma unroll
-          for (int o = 0; o < 9; o++) a.rpart[((uint64_t)tt * gridDim.x + blockIdx.x) * 9 + o] = rs[o];
-        }
-      }
+      merge_partials(a, tt, row, live, nx, (uint64_t)tt * gridDim.x + blockIdx.x, r == 0 && tt < M);
     }
   }
 }
@@ -435,24 +419,7 @@ __global__ void __launch_bounds__(kTileWarps * 32) gemv_tile_kernel(GemvArgs a, 
         for (int w = 0; w < kTileWarps; w++) v += red[w][tt][r];
         nx = gemv_epilogue(a, tt, row, v * kXPlaneScale);
       }
-      if (a.rnext) {
-        float rs[9];
-        const uint32_t d = 2 * a.h;
-#pragma unroll
-        for (int o = 0; o < 8; o++)
-          rs[o] = live ? fmaf(__ldg(a.rnext + (uint64_t)o * d + row), nx.x, __ldg(a.rnext + (uint64_t)o * d + a.h + row) * nx.y)
-                       : 0.f;
-        rs[8] = live ? fmaf(nx.x, nx.x, nx.y * nx.y) : 0.f;
-#pragma unroll
-        for (int o = 0; o < 9; o++) {
-#pragma unroll
-          for (int off = 8; off > 0; off >>= 1) rs[o] += __shfl_xor_sync(0xffffffffu, rs[o], off);
-        }
-        if (r == 0 && tt < M) {
-#pragma unroll
-          for (int o = 0; o < 9; o++) a.rpart[((uint64_t)tt * gridDim.x + blockIdx.x) * 9 + o] = rs[o];
-        }
-      }
+      merge_partials(a, tt, row, live, nx, (uint64_t)tt * gridDim.x + blockIdx.x, r == 0 && tt < M);
     }
   }
 }
@@ -583,24 +550,7 @@ __global__ void __launch_bounds__(kTileWarps * 32) gemv_tile_bulk_kernel(GemvArg
         for (int w = 0; w < kTileWarps; w++) v += red[w][tt][r];
         nx = gemv_epilogue(a, tt, row, v * kXPlaneScale);
       }
-      if (a.rnext) {
-        float rs[9];
-        const uint32_t d = 2 * a.h;
-#pragma unroll
-        for (int o = 0; o < 8; o++)
-          rs[o] = live ? fmaf(__ldg(a.rnext + (uint64_t)o * d + row), nx.x, __ldg(a.rnext + (uint64_t)o * d + a.h + row) * nx.y)
-                       : 0.f;
-        rs[8] = live ? fmaf(nx.x, nx.x, nx.y * nx.y) : 0.f;
-#pragma unroll
-        for (int o = 0; o < 9; o++) {
-#pragma unroll
-          for (int off = 8; off > 0; off >>= 1) rs[o] += __shfl_xor_sync(0xffffffffu, rs[o], off);
-        }
-        if (r == 0 && tt < M) {
-#pragma unroll
-          for (int o = 0; o < 9; o++) a.rpart[((uint64_t)tt * gridDim.x + blockIdx.x) * 9 + o] = rs[o];
-        }
-      }
+      merge_partials(a, tt, row, live, nx, (uint64_t)tt * gridDim.x + blockIdx.x, r == 0 && tt < M);
     }
   }
 }
@@ -635,10 +585,10 @@ struct PgGeom {
 };
 
 // The epilogue of one finished row group, run by one warp: val(tt, r) is the dot of
-// token tt, row 16*grp + r (lanes 16*j + r handle token 2*pass + j). Router partials
-// go to rpart[(tt * groups + grp) * 9 + o].
+// token tt, row 16*grp + r (lanes 16*j + r handle token 2*pass + j). Norm partials
+// go to rpart slot tt * groups + grp (merge_partials).
 template <int M, class V>
-__device__ __forceinline__ void group_finish(const GemvArgs& a, uint32_t grp, uint32_t groups, int lane, V&& val) {
+__device__ __forceinline__ void finish_body(const GemvArgs& a, uint32_t grp, uint32_t groups, int lane, V&& val) {
   if (a.mode == 2) {
     // SwiGLU (layers.wgsl `swiglu`): rows 0-7 of the group are gate rows 8*grp + r,
     // rows 8-15 the matching up rows (tiles repacked with pair_half).
@@ -690,24 +640,7 @@ __device__ __forceinline__ void group_finish(const GemvArgs& a, uint32_t grp, ui
                        : __uint_as_float(ll_wait(a.tp, a.tp.ll[me] + ((par * kTpMax + q) * 4 + tt) * a.tp.gp_rows + row, tag));
         nx = gemv_epilogue(a, tt, row, v * kXPlaneScale);
       }
-      if (a.rnext) {
-        float rs[9];
-        const uint32_t d = 2 * a.h;
-#pragma unroll
-        for (int o = 0; o < 8; o++)
-          rs[o] = live ? fmaf(__ldg(a.rnext + (uint64_t)o * d + row), nx.x, __ldg(a.rnext + (uint64_t)o * d + a.h + row) * nx.y)
-                       : 0.f;
-        rs[8] = live ? fmaf(nx.x, nx.x, nx.y * nx.y) : 0.f;
-#pragma unroll
-        for (int o = 0; o < 9; o++) {
-#pragma unroll
-          for (int off = 8; off > 0; off >>= 1) rs[o] += __shfl_xor_sync(0xffffffffu, rs[o], off);
-        }
-        if (r == 0 && tt < M) {
-#pragma unroll
-          for (int o = 0; o < 9; o++) a.rpart[((uint64_t)tt * groups + grp) * 9 + o] = rs[o];
-        }
-      }
+      merge_partials(a, tt, row, live, nx, (uint64_t)tt * groups + grp, r == 0 && tt < M);
     }
     return;
   }
@@ -718,23 +651,67 @@ __device__ __forceinline__ void group_finish(const GemvArgs& a, uint32_t grp, ui
     const bool live = tt < M && row < a.n;
     float2 nx = make_float2(0.f, 0.f);
     if (live) nx = gemv_epilogue(a, tt, row, val(tt, r) * kXPlaneScale);
-    if (a.rnext) {
-      float rs[9];
-      const uint32_t d = 2 * a.h;
+    merge_partials(a, tt, row, live, nx, (uint64_t)tt * groups + grp, r == 0 && tt < M);
+  }
+}
+
+// A finished row group. With a fused norm the M dot products are the two weighted
+// streams of M/2 tokens, combined as c0 * stream 0 + c1 * stream 1 with the token's
+// coefficients nrm[2 tt], nrm[2 tt + 1] (pre0 * rinv, pre1 * rinv) before the epilogue.
+template <int M, class V>
+__device__ __forceinline__ void group_finish(const GemvArgs& a, uint32_t grp, uint32_t groups, int lane, V&& val,
+                                             const float* nrm) {
+  if constexpr (M % 2 == 0) {
+    if (a.fused_norm) {
+      finish_body<M / 2>(a, grp, groups, lane, [&](int tt, int r) {
+        return nrm[2 * tt] * val(2 * tt, r) + nrm[2 * tt + 1] * val(2 * tt + 1, r);
+      });
+      return;
+    }
+  }
+  finish_body<M>(a, grp, groups, lane, val);
+}
+
+// Fused-norm prologue (one warp): the norm's router coefficients and 1 / rms of each of
+// the T tokens from the producing GEMV's per-group partials, into nrm (see group_finish);
+// block 0 also writes the coefficients for the later residual merge (layers.wgsl
+// branch_norm + mhc_finish, the separate kernels' math).
+template <int T>
+__device__ __forceinline__ void fused_norm_prologue(const GemvArgs& a, int lane, float* nrm) {
+#pragma unroll 1
+  for (int tt = 0; tt < T; tt++) {
+    float acc[11];
 #pragma unroll
-      for (int o = 0; o < 8; o++)
-        rs[o] = live ? fmaf(__ldg(a.rnext + (uint64_t)o * d + row), nx.x, __ldg(a.rnext + (uint64_t)o * d + a.h + row) * nx.y)
-                     : 0.f;
-      rs[8] = live ? fmaf(nx.x, nx.x, nx.y * nx.y) : 0.f;
+    for (int o = 0; o < 11; o++) acc[o] = 0.f;
+    for (uint32_t i = lane; i < a.nparts; i += 32) {
+      const float* rp = a.nrpart + ((uint64_t)tt * a.nparts + i) * kRpStride;
 #pragma unroll
-      for (int o = 0; o < 9; o++) {
+      for (int o = 0; o < 11; o++) acc[o] += rp[o];
+    }
 #pragma unroll
-        for (int off = 8; off > 0; off >>= 1) rs[o] += __shfl_xor_sync(0xffffffffu, rs[o], off);
+    for (int o = 0; o < 11; o++) acc[o] = warp_sum(acc[o]);
+    if (lane == 0) {
+      float pre0 = 1.f, pre1 = 0.f;
+      if (a.nrouter) {
+        float raw[9], bias[8], cb[8];
+#pragma unroll
+        for (int o = 0; o < 8; o++) {
+          raw[o] = acc[o];
+          bias[o] = a.nrouter[(uint64_t)16 * a.h + o];
+        }
+        raw[8] = acc[8] + acc[9];
+        mhc_coef_b(raw, bias, 2 * a.h, a.niter, cb);
+        pre0 = cb[0];
+        pre1 = cb[1];
+        if (blockIdx.x == 0) {
+#pragma unroll
+          for (int o = 0; o < 8; o++) a.ncoef[tt * 8 + o] = cb[o];
+        }
       }
-      if (r == 0 && tt < M) {
-#pragma unroll
-        for (int o = 0; o < 9; o++) a.rpart[((uint64_t)tt * groups + grp) * 9 + o] = rs[o];
-      }
+      const float ss = fmaf(pre0 * pre0, acc[8], fmaf(2.f * pre0 * pre1, acc[10], pre1 * pre1 * acc[9]));
+      const float rinv = rsqrtf(ss / (float)a.h + a.neps);
+      nrm[2 * tt] = pre0 * rinv;
+      nrm[2 * tt + 1] = pre1 * rinv;
     }
   }
 }
@@ -745,6 +722,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS >= 16 ? 2 : 3) gemv_pg_kerne
   using G = PgGeom<DT, WARPS, S>;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float red[2][WARPS][M][16];
+  __shared__ float nrm[M];
   pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -775,6 +753,10 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS >= 16 ? 2 : 3) gemv_pg_kerne
   };
   for (uint32_t j = 0; j < min((uint32_t)S, njobs); j++) issue(j);
   pdl_wait();
+  if constexpr (M % 2 == 0) {
+    // Visible to the epilogue through the first group's __syncthreads.
+    if (a.fused_norm && warp == 0) fused_norm_prologue<M / 2>(a, lane, nrm);
+  }
 
   const bool has_x = g < 2 * M;
   const __half* xbase = a.xplanes + (uint64_t)(has_x ? g : 0) * a.plane_stride + 8 * t;
@@ -839,7 +821,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS >= 16 ? 2 : 3) gemv_pg_kerne
 #pragma unroll
         for (int w = 0; w < WARPS; w++) v += red[buf][w][tt][r];
         return v;
-      });
+      }, nrm);
   }
   if (!ok) {
     // A bounded wait gave up: flag it and let the copies still in flight land before
@@ -931,7 +913,8 @@ int launch_gemv_tile(int dtype, const GemvArgs& a, uint32_t m, const void* tiles
   static const bool direct = getenv("SNL_GEMV_TILE_DIRECT") != nullptr;
   static const bool bulk = getenv("SNL_GEMV_BULK") != nullptr;
   if (a.mode == 2 && (!a.act_planes || a.n % 16)) return fail(SNL_E_INVALID, "gemv_tile: swiglu epilogue arguments");
-  if ((!direct && !bulk) || a.mode == 2) {
+  if (a.fused_norm && (m % 2 || a.mode == 1 || !a.nrpart)) return fail(SNL_E_INVALID, "gemv_tile: fused norm arguments");
+  if ((!direct && !bulk) || a.mode == 2 || a.fused_norm) {
     int* err = nullptr;
     if (int rc = device_error_word(&err)) return rc;
     if (dtype == SNL_Q8_0) {

@@ -39,8 +39,8 @@ struct GemvArgs {
   int merge_mode;       // 0, 1, 2
   int expand;           // also x1 = x0 afterwards
   // mode 1, optional: the mHC router of the next norm ([8, 2H] weights, then 8 biases).
-  // Each CTA writes the 9 router sums over its rows of the merged (x0 | x1) to
-  // rpart[(t * gridDim.x + blockIdx.x) * 9 + o] (8 dots, then the sum of squares).
+  // Each 16-row group writes its partial sums over the merged (x0 | x1) to rpart (layout
+  // at merge_partials).
   const float* rnext;
   float* rpart;
   // mode 2 (SwiGLU of a pair-repacked [gate; up] matrix): the x planes of act
@@ -52,7 +52,72 @@ struct GemvArgs {
   // tp_site, flag slot = group) and merges the rank-ordered sum.
   TpComm tp;
   uint32_t tp_site;
+  // mode 1, optional: the next norm's input as x planes of both residual streams, each
+  // pre-multiplied by the next norm's weight (weight_one + nw[row]): plane 4t / 4t+1 =
+  // hi / lo of stream 0 of token t, 4t+2 / 4t+3 of stream 1 (nstride halves apart).
+  __half* nplanes;
+  uint32_t nstride;
+  const float* nw;
+  float weight_one;
+  // Fused norm (modes 0 and 2, M = 2 x tokens): the x planes are the two weighted streams
+  // of each token (as written above); the GEMV finishes the norm from the producer's
+  // partials: y = rinv * (pre0 * dot(stream 0) + pre1 * dot(stream 1)), where pre0/pre1
+  // come from the mHC router (nrouter, or 1 and 0 without one) and rinv from the sums of
+  // squares. Block 0 also writes the router coefficients to ncoef for the later merge.
+  int fused_norm;
+  const float* nrpart;   // [t][groups][kRpStride] partials of the producing GEMV
+  uint32_t nparts;
+  const float* nrouter;  // [8, 2H] weights then 8 biases, or nullptr
+  float neps;
+  uint32_t niter;
+  float* ncoef;
 };
+
+// Partials of a residual-merging GEMV for the next norm, summed over a group's 16 rows:
+// rpart[(t * groups + group) * kRpStride + o], o = 0..7 the next mHC router's dots (when
+// rnext), 8 = sum x0^2, 9 = sum x1^2, 10 = sum x0 x1 of the merged streams.
+
+__device__ __forceinline__ void xplane4_store(__half* planes, uint32_t stride, uint32_t t, uint32_t i, float v0,
+                                              float v1) {
+  const float a = v0 * (1.0f / kXPlaneScale), b = v1 * (1.0f / kXPlaneScale);
+  const __half ah = __float2half_rn(a), bh = __float2half_rn(b);
+  planes[(uint64_t)(4 * t) * stride + i] = ah;
+  planes[(uint64_t)(4 * t + 1) * stride + i] = __float2half_rn(a - __half2float(ah));
+  planes[(uint64_t)(4 * t + 2) * stride + i] = bh;
+  planes[(uint64_t)(4 * t + 3) * stride + i] = __float2half_rn(b - __half2float(bh));
+}
+
+// Called by all 32 lanes of a warp; lanes 16*j + r hold row r of token tt (live or not).
+__device__ __forceinline__ void merge_partials(const GemvArgs& a, int tt, uint32_t row, bool live, float2 nx,
+                                               uint64_t slot, bool writer) {
+  if (a.mode != 1) return;
+  if (a.nplanes && live) {
+    const float w1 = a.weight_one + __ldg(a.nw + row);
+    xplane4_store(a.nplanes, a.nstride, tt, row, nx.x * w1, nx.y * w1);
+  }
+  // rpart holds one slot per 16-row group of the hidden dimension: only a residual merge
+  // (n = hidden) whose partials a norm consumes writes it.
+  if (!a.rpart || !(a.rnext || a.nplanes)) return;
+  float rs[11];
+  const uint32_t d = 2 * a.h;
+#pragma unroll
+  for (int o = 0; o < 8; o++)
+    rs[o] = live && a.rnext
+                ? fmaf(__ldg(a.rnext + (uint64_t)o * d + row), nx.x, __ldg(a.rnext + (uint64_t)o * d + a.h + row) * nx.y)
+                : 0.f;
+  rs[8] = live ? nx.x * nx.x : 0.f;
+  rs[9] = live ? nx.y * nx.y : 0.f;
+  rs[10] = live ? nx.x * nx.y : 0.f;
+#pragma unroll
+  for (int o = 0; o < 11; o++) {
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) rs[o] += __shfl_xor_sync(0xffffffffu, rs[o], off);
+  }
+  if (writer) {
+#pragma unroll
+    for (int o = 0; o < 11; o++) a.rpart[slot * kRpStride + o] = rs[o];
+  }
+}
 
 // Returns the merged (x0, x1) of element n (mode 1), for the router partials.
 __device__ __forceinline__ float2 gemv_epilogue(const GemvArgs& a, uint32_t t, uint32_t n, float v) {
