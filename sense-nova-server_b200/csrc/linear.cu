@@ -5,6 +5,8 @@
 // A_log[n_v] | dt_bias[n_v] | norm w[128]. The recurrent state of value head h is a
 // [128 (key dim i), 128 (value dim j)] f32 matrix; column j evolves independently of
 // the other columns given the head's q, k, beta and decay.
+#include <cooperative_groups.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -235,6 +237,176 @@ __global__ void __launch_bounds__(DV * kCdParts) conv_delta_kernel(StepRef sr, s
   }
 #pragma unroll
   for (uint32_t i = 0; i < kCdRows; i++) state[sbase + i * DV] = S[i];
+}
+
+// conv + delta for decode steps, kCsSplit CTAs per value head: CTA c of head h owns
+// state columns [32c, 32c + 32) (the columns evolve independently given q, k, beta and
+// decay). One thread-block cluster holds the CTAs of all value heads of a key head
+// (group = n_v / n_k heads x kCsSplit, at most 8). Each CTA runs the causal conv + SiLU
+// of the 128 q and 128 k channels of its key head (threads 0-127: q, 128-255: k) and of
+// its own 32 v channels; thread (part p, column j) keeps rows [16p, 16p + 16) of state
+// column j in registers and the 8 parts of a column add their partial dot products in
+// shared memory in part order. The gated RMSNorm over a head's 128 outputs needs the
+// sums of squares of its four CTAs: each CTA publishes its partial in shared memory and,
+// after a cluster barrier, adds the head's four in rank order. The q/k conv state is
+// read by every CTA of the cluster and written by rank 0 after a cluster barrier; the v
+// conv state by the CTA that owns the column.
+constexpr uint32_t kCsCols = 32;
+constexpr uint32_t kCsSplit = DV / kCsCols;
+constexpr uint32_t kCsParts = 8;
+constexpr uint32_t kCsRows = DK / kCsParts;
+constexpr uint32_t kCsThreads = kCsCols * kCsParts;  // 256 = q and k channels of the head
+static_assert(kCsThreads == 2 * DK, "one conv thread per q and k channel");
+
+__global__ void __launch_bounds__(kCsThreads)
+    conv_delta_split_kernel(StepRef sr, snl_lin_p p, const float* __restrict__ proj, float* __restrict__ conv_state,
+                            float* __restrict__ state, const float* __restrict__ lw, float* __restrict__ out,
+                            float* __restrict__ conv_ckpt, float* __restrict__ state_ckpt, XOut xo) {
+  namespace cg = cooperative_groups;
+  pdl_trigger();
+  __shared__ float qk[2][DK];                 // normalised-later conv outputs of q and k
+  __shared__ float vz[2][kCsCols];            // conv output of v, SiLU(z) of this CTA's columns
+  __shared__ float part[2][kCsParts][kCsCols];  // partial kv_mem, partial output
+  __shared__ float red[8];                    // warp sums of squares: q (0-3), k (4-7)
+  __shared__ float scal[2];                   // beta, decay
+  __shared__ float sq_out;                    // this CTA's sum of squared outputs (read by the cluster)
+  cg::cluster_group cluster = cg::this_cluster();
+  const uint32_t rank = cluster.block_rank();
+  const uint32_t h = blockIdx.x / kCsSplit, c0 = (blockIdx.x % kCsSplit) * kCsCols;
+  const uint32_t head_rank0 = rank - rank % kCsSplit;  // rank of this head's first CTA
+  const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t pp = tid / kCsCols, j = tid % kCsCols;  // state part, column within the CTA
+  const uint32_t group = p.n_v / p.n_k, kh = h / group;
+  const uint32_t cd = p.conv_dim, key_dim = p.n_k * DK;
+  const uint32_t z_off = cd, b_off = cd + p.n_v * DV, a_off = b_off + p.n_v;
+  // Constants (weights) before the wait: this thread's q/k conv channel, and for threads
+  // 0-31 the v conv channel of column c0 + tid.
+  const uint32_t ch = tid < DK ? kh * DK + tid : key_dim + kh * DK + (tid - DK);
+  const bool qk_owner = rank == 0;
+  const bool has_v = tid < kCsCols;
+  const uint32_t vch = 2 * key_dim + h * DV + c0 + (has_v ? tid : 0);
+  const float4 cw = *reinterpret_cast<const float4*>(lw + (uint64_t)ch * 4);
+  const float4 cwv = *reinterpret_cast<const float4*>(lw + (uint64_t)vch * 4);
+  const float norm_w = lw[(uint64_t)cd * 4 + 2 * p.n_v + c0 + j];
+  const float dt_bias = lw[(uint64_t)cd * 4 + p.n_v + h];
+  const float neg_a = -__expf(lw[(uint64_t)cd * 4 + h]);
+  const float inv_sqrt_dk = rsqrtf((float)DK);
+  pdl_wait();
+  const snl_step_u st = load_step(sr);
+  float r0 = conv_state[ch], r1 = conv_state[(uint64_t)cd + ch], r2 = conv_state[(uint64_t)2 * cd + ch];
+  float v0 = 0.f, v1 = 0.f, v2 = 0.f;
+  if (has_v) {
+    v0 = conv_state[vch];
+    v1 = conv_state[(uint64_t)cd + vch];
+    v2 = conv_state[(uint64_t)2 * cd + vch];
+  }
+  const uint64_t sbase = (uint64_t)h * DK * DV + (uint64_t)pp * kCsRows * DV + c0 + j;
+  float S[kCsRows];
+#pragma unroll
+  for (uint32_t i = 0; i < kCsRows; i++) S[i] = state[sbase + i * DV];
+
+  for (uint32_t m = 0; m < st.m; m++) {
+    const uint64_t prow = (uint64_t)m * p.proj_stride;
+    {
+      const float cur = proj[prow + ch];
+      const float o = fmaf(cw.w, cur, fmaf(cw.z, r2, fmaf(cw.y, r1, cw.x * r0)));
+      const float so = o / (1.0f + __expf(-o));
+      qk[tid / DK][tid % DK] = so;
+      r0 = r1;
+      r1 = r2;
+      r2 = cur;
+      const float ss = warp_sum(so * so);
+      if (lane == 0) red[warp] = ss;
+    }
+    if (has_v) {
+      const float cur = proj[prow + vch];
+      const float o = fmaf(cwv.w, cur, fmaf(cwv.z, v2, fmaf(cwv.y, v1, cwv.x * v0)));
+      vz[0][tid] = o / (1.0f + __expf(-o));
+      v0 = v1;
+      v1 = v2;
+      v2 = cur;
+    } else if (tid < 2 * kCsCols) {
+      const float z = proj[prow + z_off + h * DV + c0 + (tid - kCsCols)];
+      vz[1][tid - kCsCols] = z / (1.0f + __expf(-z));
+    } else if (tid == 2 * kCsCols) {
+      scal[0] = 1.0f / (1.0f + __expf(-proj[prow + b_off + h]));
+      const float araw = proj[prow + a_off + h] + dt_bias;
+      const float sp = araw <= 20.0f ? log1pf(__expf(araw)) : araw;
+      scal[1] = __expf(neg_a * sp);
+    }
+    if (m + 1 == st.ckpt) {
+      if (qk_owner) {
+        conv_ckpt[ch] = r0;
+        conv_ckpt[(uint64_t)cd + ch] = r1;
+        conv_ckpt[(uint64_t)2 * cd + ch] = r2;
+      }
+      if (has_v) {
+        conv_ckpt[vch] = v0;
+        conv_ckpt[(uint64_t)cd + vch] = v1;
+        conv_ckpt[(uint64_t)2 * cd + vch] = v2;
+      }
+    }
+    __syncthreads();
+    const float rq = rsqrtf(((red[0] + red[1]) + (red[2] + red[3])) + 1e-6f) * inv_sqrt_dk;
+    const float rk = rsqrtf(((red[4] + red[5]) + (red[6] + red[7])) + 1e-6f);
+    const float beta = scal[0], decay = scal[1];
+    const float* kr = &qk[1][pp * kCsRows];
+    const float* qr = &qk[0][pp * kCsRows];
+    float kvp = 0.f;
+#pragma unroll
+    for (uint32_t i = 0; i < kCsRows; i++) {
+      S[i] *= decay;
+      kvp = fmaf(S[i], kr[i] * rk, kvp);
+    }
+    part[0][pp][j] = kvp;
+    __syncthreads();
+    float kv_mem = 0.f;
+#pragma unroll
+    for (uint32_t q = 0; q < kCsParts; q++) kv_mem += part[0][q][j];
+    const float dlt = (vz[0][j] - kv_mem) * beta;
+    float op = 0.f;
+#pragma unroll
+    for (uint32_t i = 0; i < kCsRows; i++) {
+      S[i] = fmaf(kr[i] * rk, dlt, S[i]);
+      op = fmaf(S[i], qr[i] * rq, op);
+    }
+    part[1][pp][j] = op;
+    if (m + 1 == st.ckpt) {
+#pragma unroll
+      for (uint32_t i = 0; i < kCsRows; i++) state_ckpt[sbase + i * DV] = S[i];
+    }
+    __syncthreads();
+    float o = 0.f;
+    if (warp == 0) {
+#pragma unroll
+      for (uint32_t q = 0; q < kCsParts; q++) o += part[1][q][j];
+      const float w2 = warp_sum(o * o);
+      if (lane == 0) sq_out = w2;
+    }
+    cluster.sync();
+    if (warp == 0) {
+      float tot = 0.f;
+#pragma unroll
+      for (uint32_t r = 0; r < kCsSplit; r++) tot += *cluster.map_shared_rank(&sq_out, head_rank0 + r);
+      const float ov = o * rsqrtf(tot / (float)DV + p.eps) * norm_w * vz[1][j];
+      const uint32_t col = h * DV + c0 + j;
+      out[(uint64_t)m * p.n_v * DV + col] = ov;
+      if (xo.planes) xout_store(xo, m, col, ov);
+    }
+    cluster.sync();  // sq_out and the shared arrays are reused by the next token
+  }
+  if (qk_owner) {
+    conv_state[ch] = r0;
+    conv_state[(uint64_t)cd + ch] = r1;
+    conv_state[(uint64_t)2 * cd + ch] = r2;
+  }
+  if (has_v) {
+    conv_state[vch] = v0;
+    conv_state[(uint64_t)cd + vch] = v1;
+    conv_state[(uint64_t)2 * cd + vch] = v2;
+  }
+#pragma unroll
+  for (uint32_t i = 0; i < kCsRows; i++) state[sbase + i * DV] = S[i];
 }
 
 // ---------------------------------------------------------------------------
@@ -530,6 +702,28 @@ size_t conv_delta_chunked_scratch(const snl_lin_p& p, uint32_t m) {
 int launch_conv_delta(StepRef st, const snl_lin_p& p, const float* proj, float* conv_state, float* state,
                       const float* lw, float* out, float* conv_ckpt, float* state_ckpt, cudaStream_t s, XOut xo) {
   if (int rc = check_lin(p)) return rc;
+  static const bool split = getenv("SNL_CD_NOSPLIT") == nullptr;
+  const uint32_t cluster = p.n_v / p.n_k * kCsSplit;
+  if (split && cluster <= 8) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.n_v * kCsSplit);
+    cfg.blockDim = dim3(kCsThreads);
+    cfg.stream = s;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = cluster;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl_on() ? 2 : 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, conv_delta_split_kernel, st, p, proj, conv_state, state, lw, out,
+                                             conv_ckpt, state_ckpt, xo);
+    if (e != cudaSuccess) return cuda_fail(e, "conv_delta_split_kernel");
+    count_launch();
+    return SNL_OK;
+  }
   SNL_PDL_LAUNCH("conv_delta_kernel", conv_delta_kernel, dim3(p.n_v), dim3(DV * kCdParts), (size_t)(0), s, st, p, proj, conv_state, state, lw, out, conv_ckpt, state_ckpt, xo);
   return SNL_OK;
 }

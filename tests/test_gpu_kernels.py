@@ -396,7 +396,7 @@ def test_conv(T, lib, orc, m, ckpt):
         assert np.array_equal(host(ckd), ck_ref)
 
 
-@pytest.mark.parametrize("m,ckpt", [(1, 0), (2, 1), (40, 0), (512, 0)])
+@pytest.mark.parametrize("m,ckpt", [(1, 0), (2, 1), (7, 3), (40, 0), (512, 0)])
 def test_conv_delta_fused(T, lib, orc, m, ckpt):
     """The engine's fused conv + delta kernel (snl_conv_delta) against the oracle's
     conv then delta, states and checkpoints included."""
