@@ -53,8 +53,9 @@ def parse_args():
     ap.add_argument("--cpu-budget-s", type=float, default=25.0)
     ap.add_argument("--profile", action="store_true", help="print the per-op table of one decode step")
     ap.add_argument("--turns", type=int, default=4, help="mtp workload: turns (BASELINE config 4 names 1000)")
-    ap.add_argument("--workload", choices=["decode", "gemv", "deltanet", "mtp"], default="decode",
-                    help="gemv: only BASELINE configs[0], the one-token Q8_0 GEMV 12288x4096")
+    ap.add_argument("--workload", choices=["decode", "gemv", "gemm", "deltanet", "mtp"], default="decode",
+                    help="gemv: only BASELINE configs[0], the one-token Q8_0 GEMV 12288x4096; "
+                         "gemm: one prefill-chunk GEMM (512 tokens x 12288 x 4096) on the tcgen05 kernel")
     ap.add_argument("--iters", type=int, default=40)
     ap.add_argument("--gemv-kernel", choices=["tile", "tc", "simt"], default="tile")
     return ap.parse_args()
@@ -406,11 +407,11 @@ def run_ours(args):
             "config": {"workload": f"9B-shape {args.quant} greedy decode bs1 after a {args.prompt}-token prefill",
                        "prompt_tokens": args.prompt, "decode_tokens": K, "quant": args.quant, "scales": "f32",
                        "weight_bytes_per_token": weight_bytes_per_token(cfg, args.quant),
-                       "l2": "inputs larger than L2 (14.8 GB of weights streamed per token)",
+                       "l2": f"inputs larger than L2 ({weight_bytes_per_token(cfg, args.quant) / 1e9:.1f} GB of weights streamed per token)",
                        "parallelism": f"tp{world}" if world > 1 else "single"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "kernel": f"Q8_0 GEMV (all {n_mat} matrix launches of one decode step, "
+                         "kernel": f"{args.quant.upper()} GEMV (all {n_mat} matrix launches of one decode step, "
                                    f"{gb / 1e9:.2f} GB algorithmic)", "peak_kind": f"{peak_kind} hbm_gbs (burst)"},
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4 + 16 + 16, "d2h_bytes_per_step": 4,
                     "api": "snl_engine_forward_greedy"},
@@ -608,12 +609,69 @@ def run_mtp(args):
     return 0
 
 
+def run_gemm_only(args):
+    """One prefill chunk's largest matrix product: 512 token rows x W [12288 x 4096] in
+    Q8_0 (or Q4_0), the shape of BASELINE configs[2]'s 2048-token prefill in 512-row
+    steps, through snl_mat (which routes >= 8 rows to the tcgen05 GEMM). Weight copies
+    rotate so each launch reads its weights from HBM; CUDA events on the launching stream.
+    Achieved TFLOP/s counts the op's 2*m*n*k (the kernel's three fp16 hi/lo products are
+    3x that on the tensor pipe)."""
+    import ctypes as C
+
+    import torch
+
+    from sensenova_b200 import ffi
+
+    torch.cuda.set_device(0)
+    lib = ffi.load()
+    m, n, k, copies = 512, 12288, 4096, 4
+    dt = ffi.SNL_Q8_0 if args.quant == "q8_0" else ffi.SNL_Q4_0
+    qb = n * k if dt == ffi.SNL_Q8_0 else n * k // 2
+    ws = [torch.empty(qb, dtype=torch.uint8, device="cuda") for _ in range(copies)]
+    ss = [torch.empty(n * k // 32, dtype=torch.float32, device="cuda") for _ in range(copies)]
+    for i in range(copies):
+        ffi.check(lib.snl_synth_quant(200 + i, b"gemm", dt, n, k, C.c_void_p(ws[i].data_ptr()),
+                                      C.c_void_p(ss[i].data_ptr()), None))
+    x = torch.randn(m, k, device="cuda")
+    y = torch.empty(m, n, device="cuda")
+    st, p = ffi.StepU(m, 0, 1, 0), ffi.MatP(n, k, 0, k, 0, n, 0, 0)
+
+    def run(i):
+        ffi.check(lib.snl_mat(dt, C.byref(st), C.byref(p), C.c_void_p(x.data_ptr()), C.c_void_p(ws[i].data_ptr()),
+                              C.c_void_p(ss[i].data_ptr()), C.c_void_p(y.data_ptr()), None))
+
+    for i in range(2 * copies):
+        run(i % copies)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(args.iters):
+        run(i % copies)
+    b.record()
+    torch.cuda.synchronize()
+    us = a.elapsed_time(b) * 1000.0 / args.iters
+    flops = 2.0 * m * n * k
+    try:
+        pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        peak, kind = float(pk["bf16_tflops"]), "measured bf16_tflops (burst)"
+    except Exception:
+        peak, kind = 1590.0, "fallback"
+    wbytes = qb + n * k // 32 * 4
+    print(json.dumps({"workload": "prefill GEMM", "shape": [m, n, k], "quant": args.quant, "us_per_launch": us,
+                      "tflops": flops / us / 1e6, "peak_tflops": peak, "peak_kind": kind,
+                      "frac": flops / us / 1e6 / peak, "tensor_pipe_flops_per_launch": 3 * flops,
+                      "weight_bytes": wbytes, "weight_gbs": wbytes / us / 1e3, "copies_rotated": copies}), flush=True)
+    return 0
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference(args)
     if args.workload == "gemv":
         return run_gemv_only(args)
+    if args.workload == "gemm":
+        return run_gemm_only(args)
     if args.workload == "deltanet":
         return run_deltanet(args)
     if args.workload == "mtp":

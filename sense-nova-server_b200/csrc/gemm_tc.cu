@@ -3,23 +3,26 @@
 // Y[t, n] = sum_k X[t, k] * q[n, k] * s[n, k/32], t < m tokens (matmul.wgsl:204-318,
 // `matmul` with load_slice/dequant8, for prefill chunks of up to 512 rows).
 //
-// CTA tile: 128 weight rows x 256 tokens (128 when 256-token tiles would leave SMs
-// idle), K in blocks of 64. The fp32 accumulator lives in tensor memory (128 lanes x
-// one column per token). Precision: both operands are split into
+// CTA tile: 128 weight rows x 256 tokens (128 when 256-token tiles would not fill one
+// wave), K in blocks of 64 (two quant blocks). The fp32 accumulator lives in tensor
+// memory (128 lanes x one column per token). Precision: both operands are split into
 // fp16 hi + lo parts and three products are accumulated (hi*hi + hi*lo + lo*hi), which
 // keeps ~21 significant bits, well inside the 1e-3 bar; the dropped lo*lo term is
 // below 2^-22 of the result.
-//   * A (weights) is dequantized by the CTA's 256 threads from the file layout
-//     (weights.rs:48-55) into two fp16 tiles in the 128-byte-swizzled K-major layout of
-//     the MMA: v = code * scale * 256, hi = fp16(v), lo = fp16(v - hi).
+//   * A (weights): 8 warps dequantize the file layout (weights.rs:48-55) into two fp16
+//     tiles in the swizzled K-major layout of the MMA: v = code * scale * 256,
+//     hi = fp16(v), lo = fp16(v - hi). Each thread keeps the raw codes of its half of a
+//     K block three blocks ahead in registers.
 //   * B (tokens) comes from "x planes" [2][m][k] fp16 (x/16 split into hi and lo),
-//     written once per GEMM by tc_xpack_kernel and loaded by TMA with the same swizzle.
-//   * One thread issues the 12 MMAs of a K block (4 k-steps x 3 products, M=128 N=256
-//     or 128, K=16, kind::f16) and commits them to the stage's "empty" mbarrier, so the
-//     dequantization of block kb+1 overlaps the MMAs of block kb (2 stages).
-//   * Epilogue: 8 warps read the accumulator with tcgen05.ld (warp w: TMEM lanes
-//     32*(w%4).., the (w/4)-th half of the columns) and store y = acc / 16 (16 from the x prescale,
-//     1/256 from the weight prescale).
+//     written once per GEMM by tc_xpack_kernel and loaded by TMA with the same swizzle,
+//     one K block ahead of its MMAs.
+//   * A 9th warp issues the TMA loads and, on one thread, the 12 MMAs of a K block
+//     (4 k-steps x 3 products, M=128 N=256 or 128, K=16, kind::f16), committed to the
+//     stage's "empty" mbarrier. Dequantization and MMA issue meet only at per-stage
+//     mbarriers, never at a CTA-wide barrier.
+//   * Epilogue: the 8 dequant warps read the accumulator with tcgen05.ld (warp w: TMEM
+//     lanes 32*(w%4).., the (w/4)-th half of the columns) and store y = acc / 16 (16 from
+//     the x prescale, 1/256 from the weight prescale).
 // Every mbarrier wait is bounded; a wait that gives up sets the device error word, the
 // CTA stops issuing work, waits (bounded) for its MMAs, frees its tensor memory and
 // returns.
@@ -36,15 +39,19 @@
 namespace snl {
 namespace {
 
-constexpr uint32_t kTcM = 128, kTcK = 64;
-constexpr int kTcStages = 2;
-constexpr uint32_t kATile = kTcM * kTcK * 2;  // 16 KB of fp16
-// Token tile NT = 256 (or 128 when 256-token tiles would leave SMs idle).
-template <uint32_t NT>
+constexpr uint32_t kTcM = 128;
+// Tile geometry: NT tokens (256 or 128), K blocks of KB (32: one quant block, rows of 64
+// bytes, 64-byte swizzle; 64: two quant blocks, 128-byte rows and swizzle), S stages,
+// x tiles loaded AH blocks ahead of their MMAs (AH <= S - 1).
+template <uint32_t NT, uint32_t KB, int S, uint32_t AH>
 struct TcGeom {
-  static constexpr uint32_t kBTile = NT * kTcK * 2;
+  static_assert(KB == 32 || KB == 64, "K block");
+  static_assert(AH + 1 <= (uint32_t)S, "lookahead");
+  static constexpr uint32_t kRowBytes = KB * 2;
+  static constexpr uint32_t kATile = kTcM * KB * 2;
+  static constexpr uint32_t kBTile = NT * KB * 2;
   static constexpr uint32_t kStageBytes = 2 * kATile + 2 * kBTile;
-  static constexpr uint32_t kSmem = kTcStages * kStageBytes + 1024;  // + alignment slack
+  static constexpr uint32_t kSmem = S * kStageBytes + 1024;  // + alignment slack
   // Instruction descriptor, kind::f16: D f32, A and B f16, both K-major, N = NT, M = 128.
   static constexpr uint32_t kIdesc = (1u << 4) | ((NT >> 3) << 17) | ((kTcM >> 4) << 24);
 };
@@ -60,14 +67,16 @@ struct TcArgs {
   int* err;
 };
 
-// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row core-matrix
-// groups 1024 bytes apart (SBO), descriptor version 1 (sm_100).
-__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
+// Shared-memory matrix descriptor: K-major operand with rows of RB bytes (128: 128-byte
+// swizzle; 64: 64-byte swizzle), 8-row core-matrix groups 8 * RB bytes apart (SBO),
+// descriptor version 1 (sm_100).
+template <uint32_t RB>
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
   uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)1 << 16;             // leading byte offset (unused with this swizzle)
-  d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset
-  d |= (uint64_t)1 << 46;             // version
-  d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+  d |= (uint64_t)1 << 16;                 // leading byte offset (unused with a swizzle)
+  d |= (uint64_t)((8 * RB) >> 4) << 32;   // stride byte offset
+  d |= (uint64_t)1 << 46;                 // version
+  d |= (uint64_t)(RB == 128 ? 2 : 4) << 61;  // SWIZZLE_128B / SWIZZLE_64B
   return d;
 }
 __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
@@ -100,49 +109,66 @@ __device__ __forceinline__ uint32_t pack_hl(float a, float b, bool lo) {
 }
 
 // The raw quants and scale one thread dequantizes per K block: row t/2 of the tile and
-// the 32-element quant block (t%2) of the K block. Loaded one K block ahead.
+// half t%2 of the K block (KB/2 elements, inside one quant block).
 struct RawA {
-  uint4 w0, w1;  // Q8: 32 codes; Q4: w0 = 32 nibbles
+  uint4 w[2];  // Q8: KB/2 codes; Q4: KB/2 nibbles
   float sc;
 };
 
-template <int DT>
-__device__ __forceinline__ RawA load_a(const TcArgs& a, uint32_t n0, uint32_t kb, uint32_t tid) {
+__device__ __forceinline__ uint2 ld_stream8(const void* p) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+  return r;
+}
+
+template <int DT, uint32_t KB>
+__device__ __forceinline__ RawA load_a(const TcArgs& a, uint32_t n0, uint32_t kb, uint32_t nkb, uint32_t tid) {
   const uint32_t r = tid >> 1, h = tid & 1;
-  const uint32_t row = n0 + r, kblk = kb * 2 + h;
-  RawA raw{make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), 0.f};
-  if (row < a.n && kblk * 32 < a.k) {
-    raw.sc = __ldg(a.ws + (uint64_t)row * (a.k / 32) + kblk) * kAScale;
+  const uint32_t row = n0 + r;
+  const uint32_t e0 = kb * KB + h * (KB / 2);  // first element of this thread's half
+  RawA raw{{make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)}, 0.f};
+  if (row < a.n && kb < nkb && e0 < a.k) {
+    raw.sc = __ldg(a.ws + (uint64_t)row * (a.k / 32) + e0 / 32) * kAScale;
     if constexpr (DT == SNL_Q8_0) {
-      const uint4* src = reinterpret_cast<const uint4*>(a.wq + (uint64_t)row * a.k + kblk * 32);
-      raw.w0 = ld_stream16(src);
-      raw.w1 = ld_stream16(src + 1);
+      const uint8_t* src = a.wq + (uint64_t)row * a.k + e0;
+      raw.w[0] = ld_stream16(src);
+      if constexpr (KB == 64) raw.w[1] = ld_stream16(src + 16);
     } else {
-      raw.w0 = ld_stream16(a.wq + (uint64_t)row * (a.k / 2) + kblk * 16);
+      const uint8_t* src = a.wq + (uint64_t)row * (a.k / 2) + e0 / 2;
+      if constexpr (KB == 64) {
+        raw.w[0] = ld_stream16(src);
+      } else {
+        const uint2 w = ld_stream8(src);
+        raw.w[0].x = w.x;
+        raw.w[0].y = w.y;
+      }
     }
   }
   return raw;
 }
 
-// Writes one thread's 32 dequantized values as hi and lo fp16 into the A tiles
-// (128-byte swizzled rows: 16-byte chunk c of row r at chunk c ^ (r % 8)).
-template <int DT>
+// Writes one thread's KB/2 dequantized values as hi and lo fp16 into the A tiles
+// (swizzled rows: 16-byte chunk c of row r at chunk c ^ (r % 8) for 128-byte rows,
+// c ^ ((r / 2) % 4) for 64-byte rows).
+template <int DT, uint32_t KB>
 __device__ __forceinline__ void store_a(const RawA& raw, uint8_t* ahi, uint8_t* alo, uint32_t tid) {
+  constexpr uint32_t E = KB / 2, RB = KB * 2;
   const uint32_t r = tid >> 1, h = tid & 1;
-  float v[32];
+  float v[E];
+  const uint32_t wd[8] = {raw.w[0].x, raw.w[0].y, raw.w[0].z, raw.w[0].w,
+                          raw.w[1].x, raw.w[1].y, raw.w[1].z, raw.w[1].w};
   if constexpr (DT == SNL_Q8_0) {
-    const uint32_t wd[8] = {raw.w0.x, raw.w0.y, raw.w0.z, raw.w0.w, raw.w1.x, raw.w1.y, raw.w1.z, raw.w1.w};
 #pragma unroll
-    for (int i = 0; i < 32; i++) v[i] = (float)(int8_t)((wd[i / 4] >> (8 * (i % 4))) & 0xFFu) * raw.sc;
+    for (uint32_t i = 0; i < E; i++) v[i] = (float)(int8_t)((wd[i / 4] >> (8 * (i % 4))) & 0xFFu) * raw.sc;
   } else {
-    const uint32_t wd[4] = {raw.w0.x, raw.w0.y, raw.w0.z, raw.w0.w};
 #pragma unroll
-    for (int i = 0; i < 32; i++) v[i] = (float)((int)((wd[i / 8] >> (4 * (i % 8))) & 0xFu) - 8) * raw.sc;
+    for (uint32_t i = 0; i < E; i++) v[i] = (float)((int)((wd[i / 8] >> (4 * (i % 8))) & 0xFu) - 8) * raw.sc;
   }
 #pragma unroll
-  for (int c = 0; c < 4; c++) {
-    const uint32_t chunk = h * 4 + c;
-    const uint32_t off = r * 128 + ((chunk ^ (r & 7)) << 4);
+  for (uint32_t c = 0; c < E / 8; c++) {
+    const uint32_t chunk = h * (E / 8) + c;
+    const uint32_t sw = RB == 128 ? (r & 7) : ((r >> 1) & 3);
+    const uint32_t off = r * RB + ((chunk ^ sw) << 4);
     uint4 hi, lo;
     hi.x = pack_hl(v[8 * c + 0], v[8 * c + 1], false);
     hi.y = pack_hl(v[8 * c + 2], v[8 * c + 3], false);
@@ -157,22 +183,35 @@ __device__ __forceinline__ void store_a(const RawA& raw, uint8_t* ahi, uint8_t* 
   }
 }
 
-template <int DT, uint32_t NT>
-__global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap, TcArgs a) {
-  using G = TcGeom<NT>;
+__device__ __forceinline__ void mbar_arrive_cta(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Warp roles: warps 0-7 dequantize A (thread t: row t/2, half t%2 of the K block) and
+// run the epilogue; warp 8 (lane 0) issues the x-tile TMA loads and the MMAs. Per stage,
+// a_full (8 arrivals, one per dequant warp) and b_full (TMA bytes) hand the stage to
+// the MMA thread, and empty (tcgen05.commit) hands it back once its MMAs completed. No
+// CTA-wide barrier runs inside the K loop.
+constexpr uint32_t kTcDqWarps = 8;
+constexpr uint32_t kTcThreads = (kTcDqWarps + 1) * 32;
+
+template <int DT, uint32_t NT, uint32_t KB, int S, uint32_t AH>
+__global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap, TcArgs a) {
+  using G = TcGeom<NT, KB, S, AH>;
   constexpr uint32_t kTmemCols = NT;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  __shared__ uint64_t full_bar[kTcStages], empty_bar[kTcStages], done_bar;
+  __shared__ uint64_t a_full[S], b_full[S], empty_bar[S], done_bar;
   __shared__ uint32_t tmem_sh;
-  __shared__ int fail_sh;
+  __shared__ volatile int fail_sh;
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t n0 = blockIdx.x * kTcM, t0 = blockIdx.y * NT;
-  const uint32_t nkb = (a.k + kTcK - 1) / kTcK;
+  const uint32_t nkb = (a.k + KB - 1) / KB;
 
   if (tid == 0) {
-    for (int s = 0; s < kTcStages; s++) {
-      mbar_init(&full_bar[s], 1);
+    for (int s = 0; s < S; s++) {
+      mbar_init(&a_full[s], kTcDqWarps);
+      mbar_init(&b_full[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
     mbar_init(&done_bar, 1);
@@ -190,80 +229,109 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
   tc_fence_after();
   const uint32_t tmem = tmem_sh;
 
-  RawA raw = load_a<DT>(a, n0, 0, tid);
-  for (uint32_t kb = 0; kb < nkb; kb++) {
-    const RawA next = kb + 1 < nkb ? load_a<DT>(a, n0, kb + 1, tid) : RawA{};
-    const int s = kb % kTcStages;
-    const uint32_t use = kb / kTcStages;
-    uint8_t* st = smem + s * G::kStageBytes;
-    uint8_t* ahi = st;
-    uint8_t* alo = st + kATile;
-    uint8_t* bhi = st + 2 * kATile;
-    uint8_t* blo = bhi + G::kBTile;
-    // The stage is free once the MMAs of block kb - kTcStages have completed.
-    if (kb >= (uint32_t)kTcStages && !mbar_wait_bounded(&empty_bar[s], (use - 1) & 1)) fail_sh = 1;
-    __syncthreads();
-    if (fail_sh) break;
-    if (tid == 0) {
-      mbar_arrive_expect_tx(&full_bar[s], 2 * G::kBTile);
-      tma_load_3d(bhi, &xmap, (int)(kb * kTcK), (int)t0, 0, &full_bar[s]);
-      tma_load_3d(blo, &xmap, (int)(kb * kTcK), (int)t0, 1, &full_bar[s]);
+  if (warp < kTcDqWarps) {
+    // Dequantization: block kb into stage kb % S once the MMAs of block kb - S are done.
+    RawA r0 = load_a<DT, KB>(a, n0, 0, nkb, tid), r1 = load_a<DT, KB>(a, n0, 1, nkb, tid),
+         r2 = load_a<DT, KB>(a, n0, 2, nkb, tid);
+    for (uint32_t kb = 0; kb < nkb; kb++) {
+      const RawA r3 = load_a<DT, KB>(a, n0, kb + 3, nkb, tid);
+      const int s = kb % S;
+      const uint32_t use = kb / S;
+      // Warp-uniform: a lane that gave up stops the whole warp (the __syncwarp below).
+      const bool ok = __all_sync(0xffffffffu, kb < (uint32_t)S || mbar_wait_bounded(&empty_bar[s], (use - 1) & 1));
+      if (!ok) fail_sh = 1;
+      if (__shfl_sync(0xffffffffu, fail_sh, 0)) break;
+      uint8_t* st = smem + s * G::kStageBytes;
+      store_a<DT, KB>(r0, st, st + G::kATile, tid);
+      r0 = r1;
+      r1 = r2;
+      r2 = r3;
+      fence_proxy_async_smem();  // the dequantized tiles are read by the tensor cores (async proxy)
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cta(&a_full[s]);
     }
-    store_a<DT>(raw, ahi, alo, tid);
-    raw = next;
-    fence_proxy_async_smem();  // the dequantized tiles are read by the tensor cores (async proxy)
-    __syncthreads();
-    if (tid == 0) {
-      if (!mbar_wait_bounded(&full_bar[s], use & 1)) {
+  } else if (lane == 0) {
+    // TMA and MMA issue.
+    auto load_b = [&](uint32_t j) {
+      uint8_t* sp = smem + (j % S) * G::kStageBytes + 2 * G::kATile;
+      mbar_arrive_expect_tx(&b_full[j % S], 2 * G::kBTile);
+      tma_load_3d(sp, &xmap, (int)(j * KB), (int)t0, 0, &b_full[j % S]);
+      tma_load_3d(sp + G::kBTile, &xmap, (int)(j * KB), (int)t0, 1, &b_full[j % S]);
+    };
+    uint32_t issued = 0, consumed = 0;
+    for (; issued < nkb && issued <= AH && issued < (uint32_t)S; issued++) load_b(issued);
+    for (uint32_t kb = 0; kb < nkb && !fail_sh; kb++) {
+      // x tile of block kb + AH once its stage's previous block's MMAs are done.
+      const uint32_t j = kb + AH;
+      if (j < nkb && j == issued) {
+        if (j >= (uint32_t)S && !mbar_wait_bounded(&empty_bar[j % S], (j / S - 1) & 1)) {
+          fail_sh = 1;
+          break;
+        }
+        load_b(j);
+        issued++;
+      }
+      const int s = kb % S;
+      const uint32_t use = kb / S;
+      if (!mbar_wait_bounded(&b_full[s], use & 1) || !mbar_wait_bounded(&a_full[s], use & 1)) {
         fail_sh = 1;
-      } else {
-        tc_fence_after();
-        const uint32_t sa_hi = smem_u32(ahi), sa_lo = smem_u32(alo), sb_hi = smem_u32(bhi), sb_lo = smem_u32(blo);
-#pragma unroll
-        for (uint32_t kk = 0; kk < kTcK / 16; kk++) {
-          const uint32_t o = kk * 32;  // 16 fp16 along K inside the 128-byte swizzled row
-          tc_mma(tmem, sdesc_sw128(sa_hi + o), sdesc_sw128(sb_hi + o), G::kIdesc, (kb | kk) != 0);
-          tc_mma(tmem, sdesc_sw128(sa_hi + o), sdesc_sw128(sb_lo + o), G::kIdesc, 1);
-          tc_mma(tmem, sdesc_sw128(sa_lo + o), sdesc_sw128(sb_hi + o), G::kIdesc, 1);
-        }
-        tc_commit(&empty_bar[s]);
+        break;
       }
+      consumed = kb + 1;
+      tc_fence_after();
+      uint8_t* st = smem + s * G::kStageBytes;
+      const uint32_t sa_hi = smem_u32(st), sa_lo = sa_hi + G::kATile;
+      const uint32_t sb_hi = sa_hi + 2 * G::kATile, sb_lo = sb_hi + G::kBTile;
+#pragma unroll
+      for (uint32_t kk = 0; kk < KB / 16; kk++) {
+        const uint32_t o = kk * 32;  // 16 fp16 along K inside the swizzled row
+        tc_mma(tmem, sdesc<G::kRowBytes>(sa_hi + o), sdesc<G::kRowBytes>(sb_hi + o), G::kIdesc, (kb | kk) != 0);
+        tc_mma(tmem, sdesc<G::kRowBytes>(sa_hi + o), sdesc<G::kRowBytes>(sb_lo + o), G::kIdesc, 1);
+        tc_mma(tmem, sdesc<G::kRowBytes>(sa_lo + o), sdesc<G::kRowBytes>(sb_hi + o), G::kIdesc, 1);
+      }
+      tc_commit(&empty_bar[s]);
     }
-  }
-  if (tid == 0) {
     tc_commit(&done_bar);  // arrives when every MMA issued above has completed
-    if (fail_sh) report_timeout(a.err);
+    if (fail_sh) {
+      report_timeout(a.err);
+      // Let the x tiles still in flight land before the CTA exits.
+      for (uint32_t j = consumed; j < issued; j++) (void)mbar_wait_bounded(&b_full[j % S], (j / S) & 1);
+    }
   }
-  const bool done = mbar_wait_bounded(&done_bar, 0);
-  __syncthreads();
-  tc_fence_after();
-  if (done && !fail_sh) {
-    const uint32_t quarter = warp & 3, half = warp >> 2;
-    const uint32_t row = n0 + quarter * 32 + lane;
-    const float out_scale = kXPlaneScaleTc / kAScale;
+  if (warp == kTcDqWarps) __syncwarp();  // lane 0 rejoins before the CTA barrier below
+  // Epilogue (dequant warps): TMEM -> y once every MMA has completed. The condition is
+  // warp-uniform (tcgen05.ld is a warp-collective instruction).
+  if (warp < kTcDqWarps) {
+    const bool done = __all_sync(0xffffffffu, mbar_wait_bounded(&done_bar, 0));
+    tc_fence_after();
+    if (done && !__shfl_sync(0xffffffffu, fail_sh, 0)) {
+      const uint32_t quarter = warp & 3, half = warp >> 2;
+      const uint32_t row = n0 + quarter * 32 + lane;
+      const float out_scale = kXPlaneScaleTc / kAScale;
 #pragma unroll 1
-    for (uint32_t c0 = half * (NT / 2); c0 < half * (NT / 2) + NT / 2; c0 += 32) {
-      uint32_t r[32];
-      const uint32_t taddr = tmem + ((quarter * 32) << 16) + c0;
-      asm volatile(
-          "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
-          "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-          : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-            "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-            "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-            "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-          : "r"(taddr));
-      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-      if (row < a.n) {
+      for (uint32_t c0 = half * (NT / 2); c0 < half * (NT / 2) + NT / 2; c0 += 32) {
+        uint32_t r[32];
+        const uint32_t taddr = tmem + ((quarter * 32) << 16) + c0;
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+            "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+              "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+              "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+            : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (row < a.n) {
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
-          const uint32_t t = t0 + c0 + j;
-          if (t < a.m) a.y[a.y_off + (uint64_t)t * a.y_stride + a.n_off + row] = __uint_as_float(r[j]) * out_scale;
+          for (int j = 0; j < 32; j++) {
+            const uint32_t t = t0 + c0 + j;
+            if (t < a.m) a.y[a.y_off + (uint64_t)t * a.y_stride + a.n_off + row] = __uint_as_float(r[j]) * out_scale;
+          }
         }
       }
+    } else if (tid == 0 && !done) {
+      report_timeout(a.err);
     }
-  } else if (tid == 0 && !done) {
-    report_timeout(a.err);
   }
   tc_fence_before();
   __syncthreads();
@@ -338,41 +406,45 @@ int launch_gemm_tc(int dtype, const snl_mat_p& p, uint32_t m, const float* x, co
       x + p.x_off, p.x_stride, m, p.k, planes);
   SNL_LAUNCH_CHECK("gemm_tc xpack");
 
-  // 256-token tiles unless the step has at most 128 tokens or 256-token tiles would leave
-  // SMs idle.
+  // 256-token tiles (K blocks of 64, 2 stages, x one block ahead) unless the step has at
+  // most 128 tokens or 256-token tiles would not fill one wave; then 128-token tiles
+  // (3 stages). Measured on 512 x 12288 x 4096 (Q8_0): 189 us with 256-token tiles
+  // against 277 us with 128-token tiles, whose dequantization per MMA doubles.
   const uint32_t row_tiles = (p.n + kTcM - 1) / kTcM;
   const bool narrow = m <= 128 || (uint64_t)row_tiles * ((m + 255) / 256) < (uint64_t)sm_count();
   const uint32_t nt = narrow ? 128 : 256;
+  const uint32_t kbk = 64;
   CUtensorMap map;
   const cuuint64_t dims[3] = {p.k, m, 2};
   const cuuint64_t strides[2] = {(cuuint64_t)p.k * 2, (cuuint64_t)m * p.k * 2};
-  const cuuint32_t box[3] = {kTcK, nt, 1};
+  const cuuint32_t box[3] = {kbk, nt, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   CUresult cr = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, planes, dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, kbk == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) return fail(SNL_E_CUDA, "gemm_tc: cuTensorMapEncodeTiled failed");
 
   TcArgs ta{p.n, p.k, m, static_cast<const uint8_t*>(wq), ws, y, p.y_off, p.y_stride, p.n_off, err};
   const dim3 grid(row_tiles, (m + nt - 1) / nt);
   int dev = 0;
   cudaGetDevice(&dev);
-  auto go = [&](auto kern, uint32_t smem, bool* attr) -> int {
-    if (dev >= 0 && dev < 64 && !attr[dev]) {
+  static bool attr[2][2][64] = {};
+  auto go = [&](auto kern, uint32_t smem) -> int {
+    bool& done = attr[dtype == SNL_Q8_0 ? 0 : 1][narrow ? 1 : 0][dev >= 0 && dev < 64 ? dev : 0];
+    if (!done) {
       SNL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      attr[dev] = true;
+      done = true;
     }
-    kern<<<grid, 256, smem, s>>>(map, ta);
+    kern<<<grid, kTcThreads, smem, s>>>(map, ta);
     return SNL_OK;
   };
-  static bool attr[4][64] = {};
   int rc;
   if (dtype == SNL_Q8_0)
-    rc = narrow ? go(gemm_tc_kernel<SNL_Q8_0, 128>, TcGeom<128>::kSmem, attr[0])
-                : go(gemm_tc_kernel<SNL_Q8_0, 256>, TcGeom<256>::kSmem, attr[1]);
+    rc = narrow ? go(gemm_tc_kernel<SNL_Q8_0, 128, 64, 3, 1>, TcGeom<128, 64, 3, 1>::kSmem)
+                : go(gemm_tc_kernel<SNL_Q8_0, 256, 64, 2, 1>, TcGeom<256, 64, 2, 1>::kSmem);
   else
-    rc = narrow ? go(gemm_tc_kernel<SNL_Q4_0, 128>, TcGeom<128>::kSmem, attr[2])
-                : go(gemm_tc_kernel<SNL_Q4_0, 256>, TcGeom<256>::kSmem, attr[3]);
+    rc = narrow ? go(gemm_tc_kernel<SNL_Q4_0, 128, 64, 3, 1>, TcGeom<128, 64, 3, 1>::kSmem)
+                : go(gemm_tc_kernel<SNL_Q4_0, 256, 64, 2, 1>, TcGeom<256, 64, 2, 1>::kSmem);
   if (rc) return rc;
   SNL_LAUNCH_CHECK("gemm_tc");
   return SNL_OK;

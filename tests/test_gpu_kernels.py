@@ -110,7 +110,7 @@ def test_mat_rows(T, lib, orc, dtype, m):
 
 
 @pytest.mark.parametrize("dtype", [SNL_Q8_0, SNL_Q4_0])
-@pytest.mark.parametrize("n,k,m", [(1000, 2048, 256), (1000, 2048, 300), (4096, 4096, 512), (333, 160, 40)])
+@pytest.mark.parametrize("n,k,m", [(1000, 2048, 256), (1000, 2048, 300), (4096, 4096, 512), (333, 160, 40), (18944, 256, 300)])
 def test_mat_prefill_tensor_cores(T, lib, orc, dtype, n, k, m):
     """Prefill rows (m >= 8) run on the tcgen05 GEMM: several token and row tiles, a
     partial last K block (k = 160), against the oracle's f32 GEMM."""
