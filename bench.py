@@ -7,7 +7,7 @@ One step = one greedy decode token of the 9B-shape model (56 layer visits + the
 configs[2]). `value` is device-timed (CUDA events on the engine stream) with every
 step's inputs resident in HBM and the argmax fed back on the device; `e2e` is the same
 metric through the public API with the token crossing host->device and the next token
-device->host every step. The weights (14.8 GB streamed per token) are far larger than
+device->host every step. The weights (13.9 GB streamed per token) are far larger than
 L2, so no L2 flush is needed between steps.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
@@ -137,7 +137,7 @@ def phys_gpu_index(local_rank: int) -> int:
     return local_rank
 
 
-CONFIG1_BYTES = 12288 * 4096 + 12288 * 4096 // 32 * 4 + 4 * 4096 + 4 * 12288
+CONFIG1_BYTES = 12288 * 4096 + 12288 * 4096 // 32 * 2 + 4 * 4096 + 4 * 12288  # codes, fp16 block scales, x, y
 
 
 def traffic_from_profiles() -> float | None:
@@ -183,11 +183,13 @@ def cpu_decode(cfg, quant: int, budget_s: float, max_steps: int, warmup: int = 1
 
 
 def weight_bytes_per_token(cfg, quant: str) -> int:
-    """Quant + f32-scale bytes of every matrix one decode token streams (56 layer
-    visits + LM head); in_proj and lm_head stay Q8_0 (convert.rs:232-234, :286-298)."""
+    """Q8_0/Q4_0 block bytes (codes + an fp16 scale per 32 weights: 34 and 18 bytes) of
+    every matrix one decode token streams (56 layer visits + LM head); in_proj and
+    lm_head stay Q8_0 (convert.rs:232-234, :286-298). The tile layout the decode GEMV
+    reads holds exactly these bytes."""
     h, inter = cfg.hidden, cfg.intermediate
-    q8 = lambda r, k: r * k * 1.125
-    qq = (lambda r, k: r * k * 1.125) if quant == "q8_0" else (lambda r, k: r * k * 0.625)
+    q8 = lambda r, k: r * k * 34 / 32
+    qq = (lambda r, k: r * k * 34 / 32) if quant == "q8_0" else (lambda r, k: r * k * 18 / 32)
     tot = q8(cfg.vocab, h)
     for l in cfg.execution_plan():
         if cfg.full_attention[l]:
@@ -227,7 +229,7 @@ def gemv_config1(lib, quant: str, copies: int = 8, iters: int = 40, kernel: str 
         ffi.check(lib.snl_tile_sizes(dt, n, k, C.byref(tb), C.byref(sf)))
         for i in range(copies):
             tiles.append(torch.empty(tb.value, dtype=torch.uint8, device="cuda"))
-            tsc.append(torch.empty(sf.value, dtype=torch.float32, device="cuda"))
+            tsc.append(torch.empty(sf.value, dtype=torch.uint8, device="cuda"))
             ffi.check(lib.snl_tile_repack(dt, n, k, C.c_void_p(ws[i].data_ptr()), C.c_void_p(ss[i].data_ptr()),
                                           C.c_void_p(tiles[i].data_ptr()), C.c_void_p(tsc[i].data_ptr()), None))
 
@@ -252,8 +254,8 @@ def gemv_config1(lib, quant: str, copies: int = 8, iters: int = 40, kernel: str 
     b.record()
     torch.cuda.synchronize()
     us = a.elapsed_time(b) * 1000.0 / iters
-    nbytes = qb + n * k // 32 * 4 + 4 * k + 4 * n
-    return {"shape": [n, k], "quant": quant, "scales": "f32", "kernel": kernel, "us_per_launch": us,
+    nbytes = qb + n * k // 32 * 2 + 4 * k + 4 * n  # codes, fp16 block scales, x, y
+    return {"shape": [n, k], "quant": quant, "scales": "fp16 (tile layout; the file carries them as f32)", "kernel": kernel, "us_per_launch": us,
             "bytes_per_launch": nbytes,
             "achieved_gbs": nbytes / (us * 1e3), "copies_rotated": copies}
 
@@ -396,7 +398,7 @@ def run_ours(args):
         cpu = {"value": v, "unit": "tok/s", "cores": cores(), "kind": "port",
                "sample": f"oracle/ (C++ restatement of the WGSL kernels, OpenMP) greedy decode of the same "
                          f"9B-shape {args.quant} model after a 4-token prompt, {n} tokens timed; KV reads at "
-                         f"2K context are <1% of the 14.8 GB weight stream, so a short context stands in"}
+                         f"2K context are <1% of the 13.9 GB weight stream, so a short context stands in"}
 
     if rank == 0:
         line = {
@@ -405,7 +407,7 @@ def run_ours(args):
             "vs_baseline": value / PUBLISHED_DECODE_TOK_S, "dtype": "f32 (int8 weights, fp32 accumulate)",
             "data": "synthetic (seeded random-init weights, uniform random prompt ids)",
             "config": {"workload": f"9B-shape {args.quant} greedy decode bs1 after a {args.prompt}-token prefill",
-                       "prompt_tokens": args.prompt, "decode_tokens": K, "quant": args.quant, "scales": "f32",
+                       "prompt_tokens": args.prompt, "decode_tokens": K, "quant": args.quant, "scales": "fp16 block scales (tile layout)",
                        "weight_bytes_per_token": weight_bytes_per_token(cfg, args.quant),
                        "l2": f"inputs larger than L2 ({weight_bytes_per_token(cfg, args.quant) / 1e9:.1f} GB of weights streamed per token)",
                        "parallelism": f"tp{world}" if world > 1 else "single"},

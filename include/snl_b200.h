@@ -144,14 +144,16 @@ int snl_mat_xpack(int dtype, const snl_mat_p* p, uint32_t rows_m, const void* pl
 
 /* Tile layout of a Q8_0/Q4_0 matrix for the decode GEMV: 16-row groups, one 512-byte
  * (Q8) or 256-byte (Q4) tile per 32-element block holding each MMA lane's fragment
- * bytes contiguously, plus grouped f32 scales. The same values as the file layout in
- * another order (weights.rs:48-55 is the source). snl_tile_sizes gives the buffer
- * sizes; snl_tile_repack converts on the device; snl_mat_tiles is snl_mat_xpack on it. */
-int snl_tile_sizes(int dtype, uint32_t n, uint32_t k, size_t* tile_bytes, size_t* scale_floats);
+ * bytes contiguously, plus grouped fp16 block scales. The same values as the file layout
+ * in another order (weights.rs:48-55 is the source). snl_tile_sizes gives the buffer
+ * sizes in bytes; snl_tile_repack converts on the device and waits for it, failing with
+ * SNL_E_INVALID if a block scale is not an fp16 number (Q8_0/Q4_0 scales are);
+ * snl_mat_tiles is snl_mat_xpack on the tile layout. */
+int snl_tile_sizes(int dtype, uint32_t n, uint32_t k, size_t* tile_bytes, size_t* scale_bytes);
 int snl_tile_repack(int dtype, uint32_t n, uint32_t k, const void* q, const float* s, void* tiles,
-                    float* tile_scales, void* stream);
+                    void* tile_scales, void* stream);
 int snl_mat_tiles(int dtype, const snl_mat_p* p, uint32_t rows_m, const void* planes, const void* tiles,
-                  const float* tile_scales, float* y, void* stream);
+                  const void* tile_scales, float* y, void* stream);
 
 /* ---- kernel level: layers.wgsl ------------------------------------------------- */
 

@@ -58,7 +58,7 @@ struct QT {
   int s_f16 = 0;
   // the same matrix in the tile layout of the decode GEMV (gemv_mma.cu)
   void* tiles = nullptr;
-  float* tscales = nullptr;
+  __half* tscales = nullptr;
   uint32_t pair_half = 0;  // tiles pair gate row i with up row i (a layer's gate_up)
 };
 struct FT {
@@ -135,6 +135,8 @@ struct snl_engine {
   // these planes ([8][pstride] halves), written by the kernel that produces each input.
   bool use_tc = true;
   bool use_fused_norm = true;
+  bool tiles_on = false;      // every quantized matrix has its tile-layout copy
+  int* tile_flag = nullptr;   // repack scratch: set when a block scale is not an fp16 number
   __half* xpl = nullptr;
   __half* xpl_act = nullptr;  // planes of the SwiGLU output, written by the gate_up GEMV
   __half* xpl_norm = nullptr;  // both residual streams x the next norm weight (fused norms)
@@ -246,9 +248,11 @@ int timed(snl_engine* e, const std::string& label, double bytes, F&& fn) {
   return rc;
 }
 
+// Bytes the GEMV streams for w: codes plus a block scale per 32 weights, fp16 in the
+// tile layout and for f16-scale matrices, f32 otherwise.
 double qbytes(const QT& w) {
   const double n = (double)w.rows * w.cols;
-  return (w.dtype == SNL_Q8_0 ? n : n / 2) + n / 32 * (w.s_f16 ? 2 : 4);
+  return (w.dtype == SNL_Q8_0 ? n : n / 2) + n / 32 * (w.s_f16 || w.tiles ? 2 : 4);
 }
 
 // One matrix op (engine.rs:336-363): y[r, y_stride] for rows_m token rows.
@@ -383,7 +387,7 @@ int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
   // in-projection (x = normed residual) into y
   // Fused norms (1-2 token rows on the tile path): a residual-merging GEMV leaves the next
   // norm's weighted streams and partials, and the next projection finishes the norm.
-  const bool fuse = tc && m <= 2 && e->use_fused_norm;
+  const bool fuse = tc && m <= 2 && e->use_fused_norm && e->tiles_on;
   bool fused_ready = false;  // xpl_norm and rpart hold the inputs of the upcoming norm
   NormFuse pending;          // a norm deferred into the next projection
   auto norm_step = [&](const float* router, const float* norm_w) -> int {
@@ -1114,27 +1118,41 @@ extern "C" int snl_engine_finalize(snl_engine* e) {
     if (e->has_mtp) return fail(SNL_E_UNSUPPORTED, "tensor parallel engine: MTP is not supported");
     SNL_TRY(shard_weights(e));
   }
-  // Tile-layout copies for the decode GEMV (embed is only gathered, not multiplied).
+  // Tile-layout copies for the decode GEMV (embed is only gathered, not multiplied). If
+  // any matrix's block scales are not fp16 numbers, no matrix keeps its copy: the norm
+  // and SwiGLU fusions need the tile layout of every projection.
   if (!getenv("SNL_NO_TILES")) {
+    SNL_TRY(dalloc(e, &e->tile_flag, 1));
+    bool all_exact = true;
     for (auto& kv : e->qw) {
       if (kv.first == "embed") continue;
       snl::QT& t = kv.second;
-      size_t tb = 0, sf = 0;
-      tile_sizes(t.dtype, (uint32_t)t.rows, (uint32_t)t.cols, &tb, &sf);
+      size_t tb = 0, sb = 0;
+      tile_sizes(t.dtype, (uint32_t)t.rows, (uint32_t)t.cols, &tb, &sb);
       uint8_t* tiles = nullptr;
-      float* ts = nullptr;
+      __half* ts = nullptr;
       SNL_TRY(dalloc(e, &tiles, tb));
-      SNL_TRY(dalloc(e, &ts, sf));
+      SNL_TRY(dalloc(e, &ts, sb / sizeof(__half)));
       // A layer's [gate; up] matrix pairs gate row i with up row i for the SwiGLU epilogue.
       const std::string& nm = kv.first;
       const bool pair = nm.size() > 8 && nm[0] == 'l' && nm.compare(nm.size() - 8, 8, ".gate_up") == 0 &&
                         t.rows % 16 == 0;
       t.pair_half = pair ? (uint32_t)(t.rows / 2) : 0;
+      bool exact = false;
       SNL_TRY(launch_repack_tiles(t.dtype, (uint32_t)t.rows, (uint32_t)t.cols, t.q, (const float*)t.s, tiles, ts,
-                                  e->stream, t.pair_half));
+                                  e->tile_flag, &exact, e->stream, t.pair_half));
+      all_exact = all_exact && exact;
+      if (!all_exact) break;  // no further copies (those made so far stay allocated, unused)
       t.tiles = tiles;
       t.tscales = ts;
     }
+    e->tiles_on = all_exact;
+    if (!all_exact)
+      for (auto& kv : e->qw) {
+        kv.second.tiles = nullptr;
+        kv.second.tscales = nullptr;
+        kv.second.pair_half = 0;
+      }
   }
   const size_t proj_w = std::max({2 * I, snl_synth::lin_proj_rows(c), snl_synth::attn_proj_rows(c)});
   const size_t act_w = std::max(I, snl_synth::conv_dim(c));

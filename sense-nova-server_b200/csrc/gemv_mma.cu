@@ -255,15 +255,15 @@ extern "C" int snl_mat_xpack(int dtype, const snl_mat_p* p, uint32_t rows_m, con
 //   * in a Q4_0 tile, lane L owns 8 bytes: word t of row g, then word t of row g + 8,
 //     with nibble i of word t holding element 8t + 2(i % 4) + (i / 4) (nibbles i and
 //     i + 4 form the pair (8t + 2j, 8t + 2j + 1) that matches the natural-order x halves);
-//   * scales: per row group, blocks in fours: [group][b / 4][16 rows][4 blocks] f32.
+//   * scales: per row group, blocks in fours: [group][b / 4][16 rows][4 blocks] fp16.
+//     Q8_0/Q4_0 block scales are fp16 numbers (the file carries them as f32); the repack
+//     checks that each converts exactly and reports a matrix whose scales do not, which
+//     then stays on the reference-layout GEMV.
 // The values are the file's, bit for bit; only their order changes.
 // =====================================================================================
 
 namespace snl {
 namespace {
-
-constexpr int kTileWarps = 4;
-constexpr int kTileUnroll = 8;
 
 // pair_half != 0 (n = 2 * pair_half, pair_half % 8 == 0): group grp holds rows
 // 8*grp .. 8*grp+7 in its first 8 rows and pair_half + 8*grp .. +7 in the last 8, so a
@@ -273,8 +273,8 @@ __device__ __forceinline__ uint32_t tile_row(uint32_t grp, uint32_t r, uint32_t 
 }
 
 __global__ void repack_tiles_kernel(int dtype, uint32_t n, uint32_t k, const uint8_t* __restrict__ q,
-                                    const float* __restrict__ s, uint8_t* __restrict__ tiles, float* __restrict__ ts,
-                                    uint32_t pair_half) {
+                                    const float* __restrict__ s, uint8_t* __restrict__ tiles, __half* __restrict__ ts,
+                                    uint32_t pair_half, int* __restrict__ inexact) {
   // one thread per (group, block, lane)
   const uint32_t nb = k / 32, groups = (n + 15) / 16;
   const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -310,16 +310,11 @@ __global__ void repack_tiles_kernel(int dtype, uint32_t n, uint32_t k, const uin
   if (lane < 16) {
     const uint32_t row = tile_row(grp, lane, pair_half);
     const uint32_t nb4 = (nb + 3) / 4;
-    ts[(((uint64_t)grp * nb4 + b / 4) * 16 + lane) * 4 + b % 4] = row < n ? s[(uint64_t)row * nb + b] : 0.f;
+    const float v = row < n ? s[(uint64_t)row * nb + b] : 0.f;
+    const __half hv = __float2half_rn(v);
+    ts[(((uint64_t)grp * nb4 + b / 4) * 16 + lane) * 4 + b % 4] = hv;
+    if (!(__half2float(hv) == v)) atomicOr(inexact, 1);
   }
-}
-
-__device__ __forceinline__ uint4 ld_tile16(const uint8_t* p) {
-  uint4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p));
-  return r;
 }
 
 // Q8 codes stored as code + 128: half2(code_a, code_b) with one permute and one subtract.
@@ -329,230 +324,6 @@ __device__ __forceinline__ uint32_t u8pair(uint32_t w, uint32_t sel) {
 // Q4 (tile nibble order): half2 of nibbles (j, j + 4) of w, j = 0..3.
 __device__ __forceinline__ uint32_t u4pair(uint32_t w, int j) {
   return hsub2_u32(((w >> (4 * j)) & 0x000F000Fu) | 0x64006400u, 0x64086408u);
-}
-
-template <int DT, int M>
-__global__ void __launch_bounds__(kTileWarps * 32) gemv_tile_kernel(GemvArgs a, const uint8_t* __restrict__ tiles,
-                                                                    const float* __restrict__ ts) {
-  __shared__ float red[kTileWarps][M][16];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
-  const uint32_t nb = a.k / 32, nb4 = (nb + 3) / 4;
-  const uint32_t grp = blockIdx.x;
-  constexpr uint32_t TB = DT == SNL_Q8_0 ? 512 : 256;  // tile bytes
-  // This warp's blocks: a multiple-of-4 aligned range so scale loads stay whole.
-  const uint32_t per = ((nb4 + kTileWarps - 1) / kTileWarps) * 4;
-  const uint32_t b_begin = min(nb, warp * per), b_end = min(nb, b_begin + per);
-  const uint8_t* tp = tiles + ((uint64_t)grp * nb + b_begin) * TB + lane * (TB / 32);
-  const float* sp = ts + ((uint64_t)grp * nb4 + b_begin / 4) * 64;
-  const bool has_x = g < 2 * M;
-  const __half* xp = a.xplanes + (uint64_t)(has_x ? g : 0) * a.plane_stride + 8 * t + (uint64_t)b_begin * 32;
-
-  float accA = 0.f, accB = 0.f;
-  for (uint32_t b0 = b_begin; b0 < b_end; b0 += kTileUnroll) {
-    const uint32_t nu = min((uint32_t)kTileUnroll, b_end - b0);
-    uint4 w[kTileUnroll];
-    uint4 xv[kTileUnroll];
-    float4 sa[kTileUnroll / 4], sb[kTileUnroll / 4];
-#pragma unroll
-    for (int u = 0; u < kTileUnroll; u++) {
-      const uint32_t uu = min((uint32_t)u, nu - 1);
-      if constexpr (DT == SNL_Q8_0) {
-        w[u] = ld_tile16(tp + (uint64_t)uu * TB);
-      } else {
-        const uint2 v = *reinterpret_cast<const uint2*>(tp + (uint64_t)uu * TB);
-        w[u] = make_uint4(v.x, v.y, 0, 0);
-      }
-      xv[u] = has_x ? __ldg(reinterpret_cast<const uint4*>(xp + (uint64_t)uu * 32)) : make_uint4(0, 0, 0, 0);
-    }
-#pragma unroll
-    for (int q = 0; q < kTileUnroll / 4; q++) {
-      const uint32_t qq = min((uint32_t)q, (nu - 1) / 4);
-      sa[q] = __ldg(reinterpret_cast<const float4*>(sp + (uint64_t)qq * 64 + g * 4));
-      sb[q] = __ldg(reinterpret_cast<const float4*>(sp + (uint64_t)qq * 64 + (g + 8) * 4));
-    }
-#pragma unroll
-    for (int u = 0; u < kTileUnroll; u++) {
-      if ((uint32_t)u >= nu) break;
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
-      if constexpr (DT == SNL_Q8_0) {
-        // w.x/w.y: row g bytes 8t..8t+7; w.z/w.w: row g+8.
-        const uint32_t A0[4] = {u8pair(w[u].x, 0x4140), u8pair(w[u].z, 0x4140), u8pair(w[u].x, 0x4342),
-                                u8pair(w[u].z, 0x4342)};
-        const uint32_t A1[4] = {u8pair(w[u].y, 0x4140), u8pair(w[u].w, 0x4140), u8pair(w[u].y, 0x4342),
-                                u8pair(w[u].w, 0x4342)};
-        mma16816(d, A0, xv[u].x, xv[u].y);
-        mma16816(d, A1, xv[u].z, xv[u].w);
-      } else {
-        // w.x: row g word t, w.y: row g+8 word t; pair j = elements (8t+2j, 8t+2j+1).
-        const uint32_t A0[4] = {u4pair(w[u].x, 0), u4pair(w[u].y, 0), u4pair(w[u].x, 1), u4pair(w[u].y, 1)};
-        const uint32_t A1[4] = {u4pair(w[u].x, 2), u4pair(w[u].y, 2), u4pair(w[u].x, 3), u4pair(w[u].y, 3)};
-        mma16816(d, A0, xv[u].x, xv[u].y);
-        mma16816(d, A1, xv[u].z, xv[u].w);
-      }
-      const float4 s4a = sa[u / 4], s4b = sb[u / 4];
-      const int r = u % 4;
-      const float scA = r == 0 ? s4a.x : r == 1 ? s4a.y : r == 2 ? s4a.z : s4a.w;
-      const float scB = r == 0 ? s4b.x : r == 1 ? s4b.y : r == 2 ? s4b.z : s4b.w;
-      accA = fmaf(scA, d[0] + d[1], accA);
-      accB = fmaf(scB, d[2] + d[3], accB);
-    }
-    tp += (uint64_t)kTileUnroll * TB;
-    sp += (uint64_t)(kTileUnroll / 4) * 64;
-    xp += (uint64_t)kTileUnroll * 32;
-  }
-  if (t < M) {
-    red[warp][t][g] = accA;
-    red[warp][t][g + 8] = accB;
-  }
-  __syncthreads();
-  if (warp == 0) {
-#pragma unroll
-    for (int pass = 0; pass < (M + 1) / 2; pass++) {
-      const int tt = pass * 2 + lane / 16, r = lane % 16;
-      const uint32_t row = grp * 16 + r;
-      const bool live = tt < M && row < a.n;
-      float2 nx = make_float2(0.f, 0.f);
-      if (live) {
-        float v = 0.f;
-#pragma unroll
-        for (int w = 0; w < kTileWarps; w++) v += red[w][tt][r];
-        nx = gemv_epilogue(a, tt, row, v * kXPlaneScale);
-      }
-      merge_partials(a, tt, row, live, nx, (uint64_t)tt * gridDim.x + blockIdx.x, r == 0 && tt < M);
-    }
-  }
-}
-
-
-// Tile GEMV fed by bulk async copies: each warp streams its K range of a row group
-// through a ring of kBulkStages stages of 8 tiles (one contiguous copy of 4 KB (Q8) or
-// 2 KB (Q4) of tiles plus one of their grouped scales), so up to 4 stages are in flight
-// per warp whatever the consumer is doing. The consumer reads each lane's 16 (8) bytes
-// of a tile back from shared memory (contiguous, conflict-free) and runs the MMAs.
-constexpr int kBulkStages = 4;
-constexpr int kStageTiles = 8;
-
-template <int DT>
-struct BulkGeom {
-  static constexpr uint32_t TB = DT == SNL_Q8_0 ? 512 : 256;
-  static constexpr uint32_t kStageW = kStageTiles * TB;         // tile bytes per stage
-  static constexpr uint32_t kStageS = kStageTiles / 4 * 256;    // scale bytes per stage (2 groups of 4 blocks)
-  static constexpr uint32_t kStage = kStageW + kStageS;
-  static constexpr uint32_t kWarpBytes = kBulkStages * kStage;
-  static constexpr uint32_t kSmem = kTileWarps * kWarpBytes + kTileWarps * kBulkStages * 8;
-};
-
-template <int DT, int M>
-__global__ void __launch_bounds__(kTileWarps * 32) gemv_tile_bulk_kernel(GemvArgs a, const uint8_t* __restrict__ tiles,
-                                                                         const float* __restrict__ ts, int* err) {
-  using G = BulkGeom<DT>;
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ float red[kTileWarps][M][16];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
-  const uint32_t nb = a.k / 32, nb4 = (nb + 3) / 4;
-  const uint32_t grp = blockIdx.x;
-  // Warp ranges are multiples of a stage (8 blocks) so every stage's scales are whole groups.
-  const uint32_t per = ((nb + kTileWarps * kStageTiles - 1) / (kTileWarps * kStageTiles)) * kStageTiles;
-  const uint32_t b_begin = min(nb, warp * per), b_end = min(nb, b_begin + per);
-  const uint32_t njobs = (b_end - b_begin + kStageTiles - 1) / kStageTiles;
-  uint8_t* ring = smem + warp * G::kWarpBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTileWarps * G::kWarpBytes) + warp * kBulkStages;
-  const uint8_t* tsrc = tiles + ((uint64_t)grp * nb + b_begin) * G::TB;
-  const uint8_t* ssrc = reinterpret_cast<const uint8_t*>(ts + ((uint64_t)grp * nb4 + b_begin / 4) * 64);
-
-  if (lane == 0)
-    for (int s = 0; s < kBulkStages; s++) mbar_init(&bars[s], 1);
-  fence_mbar_init();
-  __syncwarp();
-  const uint64_t pol = l2_policy_evict_first();
-  auto issue = [&](uint32_t j) {
-    if (lane != 0) return;
-    const uint32_t s = j % kBulkStages;
-    const uint32_t nt = min((uint32_t)kStageTiles, b_end - b_begin - j * kStageTiles);
-    const uint32_t wbytes = nt * G::TB, sbytes = (nt + 3) / 4 * 256;
-    uint8_t* st = ring + s * G::kStage;
-    mbar_arrive_expect_tx(&bars[s], wbytes + sbytes);
-    bulk_g2s(st, tsrc + (uint64_t)j * G::kStageW, wbytes, &bars[s], pol);
-    bulk_g2s(st + G::kStageW, ssrc + (uint64_t)j * G::kStageS, sbytes, &bars[s], pol);
-  };
-  for (uint32_t j = 0; j < min((uint32_t)kBulkStages, njobs); j++) issue(j);
-
-  const bool has_x = g < 2 * M;
-  const __half* xp = a.xplanes + (uint64_t)(has_x ? g : 0) * a.plane_stride + 8 * t + (uint64_t)b_begin * 32;
-  float accA = 0.f, accB = 0.f;
-  uint32_t j = 0;
-  bool ok = true;
-  for (; j < njobs; j++) {
-    const uint32_t s = j % kBulkStages;
-    const uint32_t nt = min((uint32_t)kStageTiles, b_end - b_begin - j * kStageTiles);
-    uint4 xv[kStageTiles];
-#pragma unroll
-    for (int u = 0; u < kStageTiles; u++) {
-      const uint32_t uu = min((uint32_t)u, nt - 1);
-      xv[u] = has_x ? __ldg(reinterpret_cast<const uint4*>(xp + ((uint64_t)j * kStageTiles + uu) * 32))
-                    : make_uint4(0, 0, 0, 0);
-    }
-    if (!mbar_wait_bounded(&bars[s], (j / kBulkStages) & 1)) {
-      ok = false;
-      break;
-    }
-    const uint8_t* st = ring + s * G::kStage;
-    const float* sc = reinterpret_cast<const float*>(st + G::kStageW);
-#pragma unroll
-    for (int u = 0; u < kStageTiles; u++) {
-      if ((uint32_t)u >= nt) break;
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
-      if constexpr (DT == SNL_Q8_0) {
-        const uint4 w = *reinterpret_cast<const uint4*>(st + u * G::TB + lane * 16);
-        const uint32_t A0[4] = {u8pair(w.x, 0x4140), u8pair(w.z, 0x4140), u8pair(w.x, 0x4342), u8pair(w.z, 0x4342)};
-        const uint32_t A1[4] = {u8pair(w.y, 0x4140), u8pair(w.w, 0x4140), u8pair(w.y, 0x4342), u8pair(w.w, 0x4342)};
-        mma16816(d, A0, xv[u].x, xv[u].y);
-        mma16816(d, A1, xv[u].z, xv[u].w);
-      } else {
-        const uint2 w = *reinterpret_cast<const uint2*>(st + u * G::TB + lane * 8);
-        const uint32_t A0[4] = {u4pair(w.x, 0), u4pair(w.y, 0), u4pair(w.x, 1), u4pair(w.y, 1)};
-        const uint32_t A1[4] = {u4pair(w.x, 2), u4pair(w.y, 2), u4pair(w.x, 3), u4pair(w.y, 3)};
-        mma16816(d, A0, xv[u].x, xv[u].y);
-        mma16816(d, A1, xv[u].z, xv[u].w);
-      }
-      // scales: [group of 4 blocks][16 rows][4]
-      const float scA = sc[(u / 4) * 64 + g * 4 + (u % 4)];
-      const float scB = sc[(u / 4) * 64 + (g + 8) * 4 + (u % 4)];
-      accA = fmaf(scA, d[0] + d[1], accA);
-      accB = fmaf(scB, d[2] + d[3], accB);
-    }
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (j + kBulkStages < njobs) issue(j + kBulkStages);
-  }
-  if (!ok) {
-    if (lane == 0) report_timeout(err);
-    const uint32_t last = min(njobs, j + kBulkStages);
-    for (uint32_t k2 = j; k2 < last; k2++) (void)mbar_wait_bounded(&bars[k2 % kBulkStages], (k2 / kBulkStages) & 1);
-  }
-  if (t < M) {
-    red[warp][t][g] = accA;
-    red[warp][t][g + 8] = accB;
-  }
-  __syncthreads();
-  if (warp == 0) {
-#pragma unroll
-    for (int pass = 0; pass < (M + 1) / 2; pass++) {
-      const int tt = pass * 2 + lane / 16, r = lane % 16;
-      const uint32_t row = grp * 16 + r;
-      const bool live = tt < M && row < a.n;
-      float2 nx = make_float2(0.f, 0.f);
-      if (live) {
-        float v = 0.f;
-#pragma unroll
-        for (int w = 0; w < kTileWarps; w++) v += red[w][tt][r];
-        nx = gemv_epilogue(a, tt, row, v * kXPlaneScale);
-      }
-      merge_partials(a, tt, row, live, nx, (uint64_t)tt * gridDim.x + blockIdx.x, r == 0 && tt < M);
-    }
-  }
 }
 
 // ---------------------------------------------------------------------------
@@ -578,7 +349,7 @@ template <int DT, int WARPS, int S>
 struct PgGeom {
   static constexpr uint32_t TB = DT == SNL_Q8_0 ? 512 : 256;
   static constexpr uint32_t kStageW = kPgTiles * TB;
-  static constexpr uint32_t kStageS = kPgTiles / 4 * 256;
+  static constexpr uint32_t kStageS = kPgTiles / 4 * 128;  // fp16 scales: 16 rows x 4 blocks per four tiles
   static constexpr uint32_t kStage = kStageW + kStageS;
   static constexpr uint32_t kWarpBytes = S * kStage;
   static constexpr uint32_t kSmem = WARPS * kWarpBytes + WARPS * S * 8;
@@ -718,7 +489,7 @@ __device__ __forceinline__ void fused_norm_prologue(const GemvArgs& a, int lane,
 
 template <int DT, int M, int WARPS, int S>
 __global__ void __launch_bounds__(WARPS * 32, WARPS >= 16 ? 2 : 3) gemv_pg_kernel(GemvArgs a, const uint8_t* __restrict__ tiles,
-                                                             const float* __restrict__ ts, uint32_t groups, int* err) {
+                                                             const __half* __restrict__ ts, uint32_t groups, int* err) {
   using G = PgGeom<DT, WARPS, S>;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float red[2][WARPS][M][16];
@@ -745,7 +516,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS >= 16 ? 2 : 3) gemv_pg_kerne
     if (lane != 0) return;
     const uint32_t grp = g0 + j / nst, sg = st0 + j % nst;
     const uint32_t nt = min((uint32_t)kPgTiles, nb - sg * kPgTiles);
-    const uint32_t wbytes = nt * G::TB, sbytes = (nt + 3) / 4 * 256;
+    const uint32_t wbytes = nt * G::TB, sbytes = (nt + 3) / 4 * 128;
     uint8_t* st = ring + (j % S) * G::kStage;
     mbar_arrive_expect_tx(&bars[j % S], wbytes + sbytes);
     bulk_g2s(st, tiles + ((uint64_t)grp * nb + sg * kPgTiles) * G::TB, wbytes, &bars[j % S], pol);
@@ -781,7 +552,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS >= 16 ? 2 : 3) gemv_pg_kerne
         continue;
       }
       const uint8_t* st = ring + (j % S) * G::kStage;
-      const float* sc = reinterpret_cast<const float*>(st + G::kStageW);
+      const __half* sc = reinterpret_cast<const __half*>(st + G::kStageW);
 #pragma unroll
       for (int u = 0; u < kPgTiles; u++) {
         if ((uint32_t)u >= nt) break;
@@ -799,8 +570,8 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS >= 16 ? 2 : 3) gemv_pg_kerne
           mma16816(d, A0, xv[u].x, xv[u].y);
           mma16816(d, A1, xv[u].z, xv[u].w);
         }
-        const float scA = sc[(u / 4) * 64 + g * 4 + (u % 4)];
-        const float scB = sc[(u / 4) * 64 + (g + 8) * 4 + (u % 4)];
+        const float scA = __half2float(sc[(u / 4) * 64 + g * 4 + (u % 4)]);
+        const float scB = __half2float(sc[(u / 4) * 64 + (g + 8) * 4 + (u % 4)]);
         accA = fmaf(scA, d[0] + d[1], accA);
         accB = fmaf(scB, d[2] + d[3], accB);
       }
@@ -833,7 +604,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS >= 16 ? 2 : 3) gemv_pg_kerne
 }
 
 template <int DT, int M, int WARPS, int S>
-int launch_pg_cfg(const GemvArgs& a, const void* tiles, const float* ts, uint32_t groups, int* err, cudaStream_t s) {
+int launch_pg_cfg(const GemvArgs& a, const void* tiles, const __half* ts, uint32_t groups, int* err, cudaStream_t s) {
   using G = PgGeom<DT, WARPS, S>;
   static bool attr[64] = {false};
   int dev = 0;
@@ -851,7 +622,7 @@ int launch_pg_cfg(const GemvArgs& a, const void* tiles, const float* ts, uint32_
 }
 
 template <int DT, int M>
-int launch_pg_t(const GemvArgs& a, const void* tiles, const float* ts, int* err, cudaStream_t s) {
+int launch_pg_t(const GemvArgs& a, const void* tiles, const __half* ts, int* err, cudaStream_t s) {
   const uint32_t groups = (a.n + 15) / 16;
   const bool few = groups <= 2u * (uint32_t)sm_count();
   constexpr int kSA = DT == SNL_Q8_0 ? 2 : 3;  // stages per warp, 8-warp CTA
@@ -859,114 +630,57 @@ int launch_pg_t(const GemvArgs& a, const void* tiles, const float* ts, int* err,
   return launch_pg_cfg<DT, M, 8, kSA>(a, tiles, ts, groups, err, s);
 }
 
-template <int DT, int M>
-int launch_tile_bulk_t(const GemvArgs& a, const void* tiles, const float* ts, int* err, cudaStream_t s) {
-  using G = BulkGeom<DT>;
-  static bool attr[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  auto kern = gemv_tile_bulk_kernel<DT, M>;
-  if (dev >= 0 && dev < 64 && !attr[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
-    if (e != cudaSuccess) return cuda_fail(e, "gemv_tile_bulk: smem attribute");
-    attr[dev] = true;
-  }
-  kern<<<(a.n + 15) / 16, kTileWarps * 32, G::kSmem, s>>>(a, static_cast<const uint8_t*>(tiles), ts, err);
-  SNL_LAUNCH_CHECK("gemv_tile_bulk");
-  return SNL_OK;
-}
-
-template <int DT, int M>
-int launch_tile_t(const GemvArgs& a, const void* tiles, const float* ts, cudaStream_t s) {
-  gemv_tile_kernel<DT, M><<<(a.n + 15) / 16, kTileWarps * 32, 0, s>>>(a, static_cast<const uint8_t*>(tiles), ts);
-  SNL_LAUNCH_CHECK("gemv_tile");
-  return SNL_OK;
-}
-
 }  // namespace
 
-void tile_sizes(int dtype, uint32_t n, uint32_t k, size_t* tile_bytes, size_t* scale_floats) {
+void tile_sizes(int dtype, uint32_t n, uint32_t k, size_t* tile_bytes, size_t* scale_bytes) {
   const size_t groups = (n + 15) / 16, nb = k / 32, nb4 = (nb + 3) / 4;
   *tile_bytes = groups * nb * (dtype == SNL_Q8_0 ? 512 : 256);
-  *scale_floats = groups * nb4 * 64;
+  *scale_bytes = groups * nb4 * 64 * sizeof(__half);
 }
 
-int launch_repack_tiles(int dtype, uint32_t n, uint32_t k, const void* q, const float* s, void* tiles, float* ts,
-                        cudaStream_t st, uint32_t pair_half) {
+int launch_repack_tiles(int dtype, uint32_t n, uint32_t k, const void* q, const float* s, void* tiles, __half* ts,
+                        int* dflag, bool* exact, cudaStream_t st, uint32_t pair_half) {
   if (k % 32 || n == 0) return fail(SNL_E_INVALID, "repack: k must be a multiple of 32");
   if (pair_half && (n != 2 * pair_half || pair_half % 8)) return fail(SNL_E_INVALID, "repack: bad row pairing");
-  size_t tb, sf;
-  tile_sizes(dtype, n, k, &tb, &sf);
-  cudaError_t e = cudaMemsetAsync(ts, 0, sf * sizeof(float), st);  // scales of blocks past k in the last four
+  if (!dflag || !exact) return fail(SNL_E_INVALID, "repack: no flag");
+  size_t tb, sb;
+  tile_sizes(dtype, n, k, &tb, &sb);
+  cudaError_t e = cudaMemsetAsync(ts, 0, sb, st);  // scales of blocks past k in the last four
+  if (e == cudaSuccess) e = cudaMemsetAsync(dflag, 0, sizeof(int), st);
   if (e != cudaSuccess) return cuda_fail(e, "repack: memset");
   const uint64_t threads = (uint64_t)((n + 15) / 16) * (k / 32) * 32;
-  repack_tiles_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(dtype, n, k, static_cast<const uint8_t*>(q), s,
-                                                                         static_cast<uint8_t*>(tiles), ts, pair_half);
+  repack_tiles_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
+      dtype, n, k, static_cast<const uint8_t*>(q), s, static_cast<uint8_t*>(tiles), ts, pair_half, dflag);
   SNL_LAUNCH_CHECK("repack_tiles");
+  int h = 0;
+  e = cudaMemcpyAsync(&h, dflag, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(e, "repack: flag");
+  *exact = h == 0;
   return SNL_OK;
 }
 
-int launch_gemv_tile(int dtype, const GemvArgs& a, uint32_t m, const void* tiles, const float* ts, cudaStream_t s) {
+int launch_gemv_tile(int dtype, const GemvArgs& a, uint32_t m, const void* tiles, const __half* ts, cudaStream_t s) {
   if (a.k == 0 || a.k % 32) return fail(SNL_E_INVALID, "gemv_tile: k must be a multiple of 32");
   if (a.plane_stride % 8 || ((uintptr_t)a.xplanes % 16)) return fail(SNL_E_INVALID, "gemv_tile: planes alignment");
   if (a.n == 0) return SNL_OK;
-  static const bool direct = getenv("SNL_GEMV_TILE_DIRECT") != nullptr;
-  static const bool bulk = getenv("SNL_GEMV_BULK") != nullptr;
   if (a.mode == 2 && (!a.act_planes || a.n % 16)) return fail(SNL_E_INVALID, "gemv_tile: swiglu epilogue arguments");
   if (a.fused_norm && (m % 2 || a.mode == 1 || !a.nrpart)) return fail(SNL_E_INVALID, "gemv_tile: fused norm arguments");
-  if ((!direct && !bulk) || a.mode == 2 || a.fused_norm) {
-    int* err = nullptr;
-    if (int rc = device_error_word(&err)) return rc;
-    if (dtype == SNL_Q8_0) {
-      switch (m) {
-        case 1: return launch_pg_t<SNL_Q8_0, 1>(a, tiles, ts, err, s);
-        case 2: return launch_pg_t<SNL_Q8_0, 2>(a, tiles, ts, err, s);
-        case 3: return launch_pg_t<SNL_Q8_0, 3>(a, tiles, ts, err, s);
-        case 4: return launch_pg_t<SNL_Q8_0, 4>(a, tiles, ts, err, s);
-      }
-    } else if (dtype == SNL_Q4_0) {
-      switch (m) {
-        case 1: return launch_pg_t<SNL_Q4_0, 1>(a, tiles, ts, err, s);
-        case 2: return launch_pg_t<SNL_Q4_0, 2>(a, tiles, ts, err, s);
-        case 3: return launch_pg_t<SNL_Q4_0, 3>(a, tiles, ts, err, s);
-        case 4: return launch_pg_t<SNL_Q4_0, 4>(a, tiles, ts, err, s);
-      }
-    }
-    return fail(SNL_E_INVALID, "gemv_tile: dtype / rows");
-  }
-  if (!direct) {
-    int* err = nullptr;
-    if (int rc = device_error_word(&err)) return rc;
-    if (dtype == SNL_Q8_0) {
-      switch (m) {
-        case 1: return launch_tile_bulk_t<SNL_Q8_0, 1>(a, tiles, ts, err, s);
-        case 2: return launch_tile_bulk_t<SNL_Q8_0, 2>(a, tiles, ts, err, s);
-        case 3: return launch_tile_bulk_t<SNL_Q8_0, 3>(a, tiles, ts, err, s);
-        case 4: return launch_tile_bulk_t<SNL_Q8_0, 4>(a, tiles, ts, err, s);
-      }
-    } else if (dtype == SNL_Q4_0) {
-      switch (m) {
-        case 1: return launch_tile_bulk_t<SNL_Q4_0, 1>(a, tiles, ts, err, s);
-        case 2: return launch_tile_bulk_t<SNL_Q4_0, 2>(a, tiles, ts, err, s);
-        case 3: return launch_tile_bulk_t<SNL_Q4_0, 3>(a, tiles, ts, err, s);
-        case 4: return launch_tile_bulk_t<SNL_Q4_0, 4>(a, tiles, ts, err, s);
-      }
-    }
-    return fail(SNL_E_INVALID, "gemv_tile: dtype / rows");
-  }
+  int* err = nullptr;
+  if (int rc = device_error_word(&err)) return rc;
   if (dtype == SNL_Q8_0) {
     switch (m) {
-      case 1: return launch_tile_t<SNL_Q8_0, 1>(a, tiles, ts, s);
-      case 2: return launch_tile_t<SNL_Q8_0, 2>(a, tiles, ts, s);
-      case 3: return launch_tile_t<SNL_Q8_0, 3>(a, tiles, ts, s);
-      case 4: return launch_tile_t<SNL_Q8_0, 4>(a, tiles, ts, s);
+      case 1: return launch_pg_t<SNL_Q8_0, 1>(a, tiles, ts, err, s);
+      case 2: return launch_pg_t<SNL_Q8_0, 2>(a, tiles, ts, err, s);
+      case 3: return launch_pg_t<SNL_Q8_0, 3>(a, tiles, ts, err, s);
+      case 4: return launch_pg_t<SNL_Q8_0, 4>(a, tiles, ts, err, s);
     }
   } else if (dtype == SNL_Q4_0) {
     switch (m) {
-      case 1: return launch_tile_t<SNL_Q4_0, 1>(a, tiles, ts, s);
-      case 2: return launch_tile_t<SNL_Q4_0, 2>(a, tiles, ts, s);
-      case 3: return launch_tile_t<SNL_Q4_0, 3>(a, tiles, ts, s);
-      case 4: return launch_tile_t<SNL_Q4_0, 4>(a, tiles, ts, s);
+      case 1: return launch_pg_t<SNL_Q4_0, 1>(a, tiles, ts, err, s);
+      case 2: return launch_pg_t<SNL_Q4_0, 2>(a, tiles, ts, err, s);
+      case 3: return launch_pg_t<SNL_Q4_0, 3>(a, tiles, ts, err, s);
+      case 4: return launch_pg_t<SNL_Q4_0, 4>(a, tiles, ts, err, s);
     }
   }
   return fail(SNL_E_INVALID, "gemv_tile: dtype / rows");
@@ -974,21 +688,29 @@ int launch_gemv_tile(int dtype, const GemvArgs& a, uint32_t m, const void* tiles
 
 }  // namespace snl
 
-extern "C" int snl_tile_sizes(int dtype, uint32_t n, uint32_t k, size_t* tile_bytes, size_t* scale_floats) {
-  if (!tile_bytes || !scale_floats || (dtype != SNL_Q8_0 && dtype != SNL_Q4_0)) return snl::fail(SNL_E_INVALID, "snl_tile_sizes");
-  snl::tile_sizes(dtype, n, k, tile_bytes, scale_floats);
+extern "C" int snl_tile_sizes(int dtype, uint32_t n, uint32_t k, size_t* tile_bytes, size_t* scale_bytes) {
+  if (!tile_bytes || !scale_bytes || (dtype != SNL_Q8_0 && dtype != SNL_Q4_0)) return snl::fail(SNL_E_INVALID, "snl_tile_sizes");
+  snl::tile_sizes(dtype, n, k, tile_bytes, scale_bytes);
   return SNL_OK;
 }
 extern "C" int snl_tile_repack(int dtype, uint32_t n, uint32_t k, const void* q, const float* s, void* tiles,
-                               float* tile_scales, void* stream) {
+                               void* tile_scales, void* stream) {
   if (!q || !s || !tiles || !tile_scales || (dtype != SNL_Q8_0 && dtype != SNL_Q4_0))
     return snl::fail(SNL_E_INVALID, "snl_tile_repack: bad argument");
-  return snl::launch_repack_tiles(dtype, n, k, q, s, tiles, tile_scales, (cudaStream_t)stream);
+  int* dflag = nullptr;
+  if (cudaMalloc(&dflag, sizeof(int)) != cudaSuccess) return snl::fail(SNL_E_OOM, "snl_tile_repack: flag");
+  bool exact = false;
+  const int rc = snl::launch_repack_tiles(dtype, n, k, q, s, tiles, static_cast<__half*>(tile_scales), dflag, &exact,
+                                          (cudaStream_t)stream);
+  cudaFree(dflag);
+  if (rc) return rc;
+  if (!exact) return snl::fail(SNL_E_INVALID, "snl_tile_repack: block scales are not fp16 numbers");
+  return SNL_OK;
 }
 extern "C" int snl_mat_tiles(int dtype, const snl_mat_p* p, uint32_t rows_m, const void* planes, const void* tiles,
-                             const float* tile_scales, float* y, void* stream) {
+                             const void* tile_scales, float* y, void* stream) {
   if (!p || !planes || !tiles || !tile_scales || !y) return snl::fail(SNL_E_INVALID, "snl_mat_tiles: null argument");
   if (rows_m == 0 || rows_m > 4) return snl::fail(SNL_E_INVALID, "snl_mat_tiles: 1..4 token rows");
   snl::GemvArgs a = snl::gemv_args_plain(*p, static_cast<const __half*>(planes), p->k, tiles, y);
-  return snl::launch_gemv_tile(dtype, a, rows_m, tiles, tile_scales, (cudaStream_t)stream);
+  return snl::launch_gemv_tile(dtype, a, rows_m, tiles, static_cast<const __half*>(tile_scales), (cudaStream_t)stream);
 }

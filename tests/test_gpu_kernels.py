@@ -174,7 +174,7 @@ def test_mat_tiles(T, lib, orc, dtype, m, n, k):
     tb, sf = C.c_size_t(), C.c_size_t()
     call(lib.snl_tile_sizes(dtype, n, k, C.byref(tb), C.byref(sf)))
     tiles = T.empty(tb.value, dtype=T.uint8, device="cuda")
-    ts = T.empty(sf.value, dtype=T.float32, device="cuda")
+    ts = T.empty(sf.value, dtype=T.uint8, device="cuda")
     call(lib.snl_tile_repack(dtype, n, k, ptr(dev(T, q)), ptr(dev(T, s)), ptr(tiles), ptr(ts), None))
     planes = T.empty(2 * m * k, dtype=T.float16, device="cuda")
     call(lib.snl_xpack(ptr(dev(T, x)), m, k, k, ptr(planes), None))
@@ -183,6 +183,23 @@ def test_mat_tiles(T, lib, orc, dtype, m, n, k):
     call(lib.snl_mat_tiles(dtype, C.byref(p), m, ptr(planes), ptr(tiles), ptr(ts), ptr(y), None))
     err = rel(host(y), ref)
     assert err < TOL and err < 2e-5, err
+
+
+def test_tile_repack_rejects_non_fp16_scales(T, lib, orc):
+    """The tile layout keeps fp16 block scales (Q8_0/Q4_0 scales are fp16 numbers); a
+    scale that is not one is refused, not rounded."""
+    n, k = 32, 64
+    q, s = orc.gen_quant(5, "wtile", SNL_Q8_0, n, k)
+    tb, sb = C.c_size_t(), C.c_size_t()
+    call(lib.snl_tile_sizes(SNL_Q8_0, n, k, C.byref(tb), C.byref(sb)))
+    assert sb.value == (n // 16) * ((k // 32 + 3) // 4) * 64 * 2
+    tiles = T.empty(tb.value, dtype=T.uint8, device="cuda")
+    ts = T.empty(sb.value, dtype=T.uint8, device="cuda")
+    call(lib.snl_tile_repack(SNL_Q8_0, n, k, ptr(dev(T, q)), ptr(dev(T, s)), ptr(tiles), ptr(ts), None))
+    bad = s.copy()
+    bad.flat[7] = np.float32(0.1)  # not an fp16 number
+    rc = lib.snl_tile_repack(SNL_Q8_0, n, k, ptr(dev(T, q)), ptr(dev(T, bad)), ptr(tiles), ptr(ts), None)
+    assert rc == -1  # SNL_E_INVALID
 
 
 def test_mat_tensor_core_wide_range(T, lib, orc):
