@@ -224,19 +224,24 @@ def gemv_config1(lib, quant: str, copies: int = 8, iters: int = 40, kernel: str 
     planes = torch.empty(2 * k, dtype=torch.float16, device="cuda")
     ffi.check(lib.snl_xpack(C.c_void_p(x.data_ptr()), 1, k, k, C.c_void_p(planes.data_ptr()), None))
     tiles, tsc = [], []
+    scale_mode = "f32"  # the file layout's scales (snl_mat, snl_mat_xpack)
     if kernel == "tile":
         tb, sf = C.c_size_t(), C.c_size_t()
         ffi.check(lib.snl_tile_sizes(dt, n, k, C.byref(tb), C.byref(sf)))
         for i in range(copies):
             tiles.append(torch.empty(tb.value, dtype=torch.uint8, device="cuda"))
             tsc.append(torch.empty(sf.value, dtype=torch.uint8, device="cuda"))
+            f16 = C.c_int(-1)
             ffi.check(lib.snl_tile_repack(dt, n, k, C.c_void_p(ws[i].data_ptr()), C.c_void_p(ss[i].data_ptr()),
-                                          C.c_void_p(tiles[i].data_ptr()), C.c_void_p(tsc[i].data_ptr()), None))
+                                          C.c_void_p(tiles[i].data_ptr()), C.c_void_p(tsc[i].data_ptr()),
+                                          C.byref(f16), None))
+            scale_mode = "fp16" if f16.value else "f32"
 
     def run(i):
         if kernel == "tile":  # the decode path: tile layout, tensor-core GEMV over packed x
             ffi.check(lib.snl_mat_tiles(dt, C.byref(p), 1, C.c_void_p(planes.data_ptr()), C.c_void_p(tiles[i].data_ptr()),
-                                        C.c_void_p(tsc[i].data_ptr()), C.c_void_p(y.data_ptr()), None))
+                                        C.c_void_p(tsc[i].data_ptr()), 1 if scale_mode == "fp16" else 0,
+                                        C.c_void_p(y.data_ptr()), None))
         elif kernel == "tc":  # tensor-core GEMV on the file layout
             ffi.check(lib.snl_mat_xpack(dt, C.byref(p), 1, C.c_void_p(planes.data_ptr()), C.c_void_p(ws[i].data_ptr()),
                                         C.c_void_p(ss[i].data_ptr()), C.c_void_p(y.data_ptr()), None))
@@ -254,8 +259,9 @@ def gemv_config1(lib, quant: str, copies: int = 8, iters: int = 40, kernel: str 
     b.record()
     torch.cuda.synchronize()
     us = a.elapsed_time(b) * 1000.0 / iters
-    nbytes = qb + n * k // 32 * 2 + 4 * k + 4 * n  # codes, fp16 block scales, x, y
-    return {"shape": [n, k], "quant": quant, "scales": "fp16 (tile layout; the file carries them as f32)", "kernel": kernel, "us_per_launch": us,
+    # Algorithmic bytes: Q8_0/Q4_0 blocks (codes + an fp16 scale per 32), x, y.
+    nbytes = qb + n * k // 32 * 2 + 4 * k + 4 * n
+    return {"shape": [n, k], "quant": quant, "scales": scale_mode, "kernel": kernel, "us_per_launch": us,
             "bytes_per_launch": nbytes,
             "achieved_gbs": nbytes / (us * 1e3), "copies_rotated": copies}
 
@@ -319,6 +325,8 @@ def run_ours(args):
     # N > 1: one decode stream sharded over the N GPUs (tensor parallel, one process per GPU).
     tp = (rank, world) if world > 1 else None
     eng = Engine.synthetic(cfg, ctx, args.seed, args.quant, device=local_rank, tp=tp)
+    n16, n32 = eng.tile_scales()
+    scale_mode = f"tile layout: {n16} matrices with fp16 block scales, {n32} with f32"
     build_s = time.perf_counter() - t0
     rng = np.random.default_rng(args.seed)  # every rank feeds the same stream
     prompt = rng.integers(0, cfg.vocab, args.prompt).tolist()
@@ -407,7 +415,7 @@ def run_ours(args):
             "vs_baseline": value / PUBLISHED_DECODE_TOK_S, "dtype": "f32 (int8 weights, fp32 accumulate)",
             "data": "synthetic (seeded random-init weights, uniform random prompt ids)",
             "config": {"workload": f"9B-shape {args.quant} greedy decode bs1 after a {args.prompt}-token prefill",
-                       "prompt_tokens": args.prompt, "decode_tokens": K, "quant": args.quant, "scales": "fp16 block scales (tile layout)",
+                       "prompt_tokens": args.prompt, "decode_tokens": K, "quant": args.quant, "scales": scale_mode,
                        "weight_bytes_per_token": weight_bytes_per_token(cfg, args.quant),
                        "l2": f"inputs larger than L2 ({weight_bytes_per_token(cfg, args.quant) / 1e9:.1f} GB of weights streamed per token)",
                        "parallelism": f"tp{world}" if world > 1 else "single"},

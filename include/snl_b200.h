@@ -144,16 +144,17 @@ int snl_mat_xpack(int dtype, const snl_mat_p* p, uint32_t rows_m, const void* pl
 
 /* Tile layout of a Q8_0/Q4_0 matrix for the decode GEMV: 16-row groups, one 512-byte
  * (Q8) or 256-byte (Q4) tile per 32-element block holding each MMA lane's fragment
- * bytes contiguously, plus grouped fp16 block scales. The same values as the file layout
- * in another order (weights.rs:48-55 is the source). snl_tile_sizes gives the buffer
- * sizes in bytes; snl_tile_repack converts on the device and waits for it, failing with
- * SNL_E_INVALID if a block scale is not an fp16 number (Q8_0/Q4_0 scales are);
- * snl_mat_tiles is snl_mat_xpack on the tile layout. */
+ * bytes contiguously, plus grouped block scales. The same values as the file layout in
+ * another order (weights.rs:48-55 is the source). snl_tile_sizes gives the buffer sizes
+ * in bytes (scales sized for f32). snl_tile_repack converts on the device and waits for
+ * it; it keeps the scales as fp16 when every block scale is an fp16 number
+ * (*scales_f16 = 1), else as f32 (*scales_f16 = 0). snl_mat_tiles is snl_mat_xpack on
+ * the tile layout, given that mode. */
 int snl_tile_sizes(int dtype, uint32_t n, uint32_t k, size_t* tile_bytes, size_t* scale_bytes);
 int snl_tile_repack(int dtype, uint32_t n, uint32_t k, const void* q, const float* s, void* tiles,
-                    void* tile_scales, void* stream);
+                    void* tile_scales, int* scales_f16, void* stream);
 int snl_mat_tiles(int dtype, const snl_mat_p* p, uint32_t rows_m, const void* planes, const void* tiles,
-                  const void* tile_scales, float* y, void* stream);
+                  const void* tile_scales, int scales_f16, float* y, void* stream);
 
 /* ---- kernel level: layers.wgsl ------------------------------------------------- */
 
@@ -341,6 +342,9 @@ int snl_engine_restore(snl_engine* e, size_t slot, size_t pos);  /* engine.rs:67
 int snl_engine_rollback(snl_engine* e);                          /* engine.rs:685-697 */
 size_t snl_engine_hid_rows(const snl_engine* e);                 /* engine.rs:699-702 */
 int snl_engine_has_mtp(const snl_engine* e);                     /* engine.rs:704-706 */
+/* Matrices whose decode tile layout keeps fp16 block scales (every scale an fp16
+ * number) and those that keep f32 scales. */
+int snl_engine_tile_scales(const snl_engine* e, uint32_t* fp16_matrices, uint32_t* f32_matrices);
 size_t snl_engine_pos(const snl_engine* e);                      /* pub pos, engine.rs:185 */
 size_t snl_engine_ctx(const snl_engine* e);                      /* pub ctx, engine.rs:154 */
 /* Bytes of device memory the engine holds (Gpu::allocated, gpu.rs:17-18). */

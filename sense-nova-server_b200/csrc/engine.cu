@@ -58,7 +58,8 @@ struct QT {
   int s_f16 = 0;
   // the same matrix in the tile layout of the decode GEMV (gemv_mma.cu)
   void* tiles = nullptr;
-  __half* tscales = nullptr;
+  void* tscales = nullptr;
+  int tscale_f16 = 0;  // the tile scales are fp16 (every block scale is an fp16 number), else f32
   uint32_t pair_half = 0;  // tiles pair gate row i with up row i (a layer's gate_up)
 };
 struct FT {
@@ -136,7 +137,8 @@ struct snl_engine {
   bool use_tc = true;
   bool use_fused_norm = true;
   bool tiles_on = false;      // every quantized matrix has its tile-layout copy
-  int* tile_flag = nullptr;   // repack scratch: set when a block scale is not an fp16 number
+  int* tile_flag = nullptr;   // scale check scratch: set when a block scale is not an fp16 number
+  uint32_t tiles_f16 = 0, tiles_f32 = 0;  // matrices whose tile scales are fp16 / f32
   __half* xpl = nullptr;
   __half* xpl_act = nullptr;  // planes of the SwiGLU output, written by the gate_up GEMV
   __half* xpl_norm = nullptr;  // both residual streams x the next norm weight (fused norms)
@@ -248,11 +250,10 @@ int timed(snl_engine* e, const std::string& label, double bytes, F&& fn) {
   return rc;
 }
 
-// Bytes the GEMV streams for w: codes plus a block scale per 32 weights, fp16 in the
-// tile layout and for f16-scale matrices, f32 otherwise.
+// Bytes the GEMV streams for w: codes plus a block scale per 32 weights (fp16 or f32).
 double qbytes(const QT& w) {
   const double n = (double)w.rows * w.cols;
-  return (w.dtype == SNL_Q8_0 ? n : n / 2) + n / 32 * (w.s_f16 || w.tiles ? 2 : 4);
+  return (w.dtype == SNL_Q8_0 ? n : n / 2) + n / 32 * (w.tiles ? (w.tscale_f16 ? 2 : 4) : (w.s_f16 ? 2 : 4));
 }
 
 // One matrix op (engine.rs:336-363): y[r, y_stride] for rows_m token rows.
@@ -356,7 +357,7 @@ int matx(snl_engine* e, const QT& w, uint32_t rows, int mode, float* y, size_t y
   const double bytes = qbytes(w) + 4.0 * rows * (w.cols + w.rows);
   const std::string label = "mat n=" + std::to_string(w.rows) + (y == e->head_out ? " (head)" : "");
   SNL_TRY(timed(e, label, bytes, [&] {
-    if (w.tiles) return launch_gemv_tile(w.dtype, a, launch_rows, w.tiles, w.tscales, e->stream);
+    if (w.tiles) return launch_gemv_tile(w.dtype, a, launch_rows, w.tiles, w.tscales, w.tscale_f16, e->stream);
     if (nf_in.on) return fail(SNL_E_STATE, "fused norm needs the tile layout");
     return launch_gemv_mma(w.dtype, a, rows, w.s, w.s_f16, e->stream);
   }));
@@ -1118,41 +1119,42 @@ extern "C" int snl_engine_finalize(snl_engine* e) {
     if (e->has_mtp) return fail(SNL_E_UNSUPPORTED, "tensor parallel engine: MTP is not supported");
     SNL_TRY(shard_weights(e));
   }
-  // Tile-layout copies for the decode GEMV (embed is only gathered, not multiplied). If
-  // any matrix's block scales are not fp16 numbers, no matrix keeps its copy: the norm
-  // and SwiGLU fusions need the tile layout of every projection.
+  // Tile-layout copies for the decode GEMV (embed is only gathered, not multiplied). A
+  // matrix's block scales are kept as fp16 when every one is an fp16 number, else as f32.
   if (!getenv("SNL_NO_TILES")) {
     SNL_TRY(dalloc(e, &e->tile_flag, 1));
-    bool all_exact = true;
     for (auto& kv : e->qw) {
       if (kv.first == "embed") continue;
       snl::QT& t = kv.second;
-      size_t tb = 0, sb = 0;
-      tile_sizes(t.dtype, (uint32_t)t.rows, (uint32_t)t.cols, &tb, &sb);
+      size_t tb = 0, sf = 0;
+      tile_sizes(t.dtype, (uint32_t)t.rows, (uint32_t)t.cols, &tb, &sf);
+      bool f16 = false;
+      SNL_TRY(scales_fp16_exact((const float*)t.s, (uint64_t)t.rows * (t.cols / 32), e->tile_flag, &f16, e->stream));
       uint8_t* tiles = nullptr;
-      __half* ts = nullptr;
+      void* ts = nullptr;
       SNL_TRY(dalloc(e, &tiles, tb));
-      SNL_TRY(dalloc(e, &ts, sb / sizeof(__half)));
+      if (f16) {
+        __half* p = nullptr;
+        SNL_TRY(dalloc(e, &p, sf));
+        ts = p;
+      } else {
+        float* p = nullptr;
+        SNL_TRY(dalloc(e, &p, sf));
+        ts = p;
+      }
       // A layer's [gate; up] matrix pairs gate row i with up row i for the SwiGLU epilogue.
       const std::string& nm = kv.first;
       const bool pair = nm.size() > 8 && nm[0] == 'l' && nm.compare(nm.size() - 8, 8, ".gate_up") == 0 &&
                         t.rows % 16 == 0;
       t.pair_half = pair ? (uint32_t)(t.rows / 2) : 0;
-      bool exact = false;
       SNL_TRY(launch_repack_tiles(t.dtype, (uint32_t)t.rows, (uint32_t)t.cols, t.q, (const float*)t.s, tiles, ts,
-                                  e->tile_flag, &exact, e->stream, t.pair_half));
-      all_exact = all_exact && exact;
-      if (!all_exact) break;  // no further copies (those made so far stay allocated, unused)
+                                  f16 ? 1 : 0, e->stream, t.pair_half));
       t.tiles = tiles;
       t.tscales = ts;
+      t.tscale_f16 = f16 ? 1 : 0;
+      (f16 ? e->tiles_f16 : e->tiles_f32)++;
     }
-    e->tiles_on = all_exact;
-    if (!all_exact)
-      for (auto& kv : e->qw) {
-        kv.second.tiles = nullptr;
-        kv.second.tscales = nullptr;
-        kv.second.pair_half = 0;
-      }
+    e->tiles_on = true;
   }
   const size_t proj_w = std::max({2 * I, snl_synth::lin_proj_rows(c), snl_synth::attn_proj_rows(c)});
   const size_t act_w = std::max(I, snl_synth::conv_dim(c));
@@ -1539,6 +1541,12 @@ extern "C" int snl_engine_rollback(snl_engine* e) {
 
 extern "C" size_t snl_engine_hid_rows(const snl_engine* e) { return e ? e->hid_rows : 0; }
 extern "C" int snl_engine_has_mtp(const snl_engine* e) { return e && e->has_mtp ? 1 : 0; }
+extern "C" int snl_engine_tile_scales(const snl_engine* e, uint32_t* fp16_matrices, uint32_t* f32_matrices) {
+  if (!e || !fp16_matrices || !f32_matrices) return snl::fail(SNL_E_INVALID, "snl_engine_tile_scales: null argument");
+  *fp16_matrices = e->tiles_f16;
+  *f32_matrices = e->tiles_f32;
+  return SNL_OK;
+}
 extern "C" size_t snl_engine_pos(const snl_engine* e) { return e ? e->pos : 0; }
 extern "C" size_t snl_engine_ctx(const snl_engine* e) { return e ? e->ctx : 0; }
 extern "C" size_t snl_engine_device_bytes(const snl_engine* e) { return e ? e->bytes : 0; }

@@ -255,10 +255,10 @@ extern "C" int snl_mat_xpack(int dtype, const snl_mat_p* p, uint32_t rows_m, con
 //   * in a Q4_0 tile, lane L owns 8 bytes: word t of row g, then word t of row g + 8,
 //     with nibble i of word t holding element 8t + 2(i % 4) + (i / 4) (nibbles i and
 //     i + 4 form the pair (8t + 2j, 8t + 2j + 1) that matches the natural-order x halves);
-//   * scales: per row group, blocks in fours: [group][b / 4][16 rows][4 blocks] fp16.
-//     Q8_0/Q4_0 block scales are fp16 numbers (the file carries them as f32); the repack
-//     checks that each converts exactly and reports a matrix whose scales do not, which
-//     then stays on the reference-layout GEMV.
+//   * scales: per row group, blocks in fours: [group][b / 4][16 rows][4 blocks], as fp16
+//     when every block scale of the matrix is an fp16 number (checked before the repack;
+//     true of Q8_0/Q4_0 files whose scales came from fp16 blocks), else as f32, the file's
+//     own values.
 // The values are the file's, bit for bit; only their order changes.
 // =====================================================================================
 
@@ -273,8 +273,8 @@ __device__ __forceinline__ uint32_t tile_row(uint32_t grp, uint32_t r, uint32_t 
 }
 
 __global__ void repack_tiles_kernel(int dtype, uint32_t n, uint32_t k, const uint8_t* __restrict__ q,
-                                    const float* __restrict__ s, uint8_t* __restrict__ tiles, __half* __restrict__ ts,
-                                    uint32_t pair_half, int* __restrict__ inexact) {
+                                    const float* __restrict__ s, uint8_t* __restrict__ tiles, void* __restrict__ ts,
+                                    int ts_f16, uint32_t pair_half) {
   // one thread per (group, block, lane)
   const uint32_t nb = k / 32, groups = (n + 15) / 16;
   const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -311,13 +311,26 @@ __global__ void repack_tiles_kernel(int dtype, uint32_t n, uint32_t k, const uin
     const uint32_t row = tile_row(grp, lane, pair_half);
     const uint32_t nb4 = (nb + 3) / 4;
     const float v = row < n ? s[(uint64_t)row * nb + b] : 0.f;
-    const __half hv = __float2half_rn(v);
-    ts[(((uint64_t)grp * nb4 + b / 4) * 16 + lane) * 4 + b % 4] = hv;
-    if (!(__half2float(hv) == v)) atomicOr(inexact, 1);
+    const uint64_t i = (((uint64_t)grp * nb4 + b / 4) * 16 + lane) * 4 + b % 4;
+    if (ts_f16) static_cast<__half*>(ts)[i] = __float2half_rn(v);
+    else static_cast<float*>(ts)[i] = v;
   }
 }
 
 // Q8 codes stored as code + 128: half2(code_a, code_b) with one permute and one subtract.
+// Sets *inexact if any of the count scales is not an fp16 number.
+__global__ void fp16_exact_kernel(const float* __restrict__ s, uint64_t count, int* __restrict__ inexact) {
+  bool bad = false;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (uint64_t)gridDim.x * blockDim.x) {
+    const float v = s[i];
+    bad |= !(__half2float(__float2half_rn(v)) == v);
+  }
+  if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(inexact, 1);
+}
+
+__device__ __forceinline__ float scale_f(float v) { return v; }
+__device__ __forceinline__ float scale_f(__half v) { return __half2float(v); }
+
 __device__ __forceinline__ uint32_t u8pair(uint32_t w, uint32_t sel) {
   return hsub2_u32(__byte_perm(w, 0x64646464u, sel), 0x64806480u);
 }
@@ -345,11 +358,11 @@ __device__ __forceinline__ uint32_t u4pair(uint32_t w, int j) {
 constexpr int kPgTiles = 8;
 constexpr int kPgCtasPerSm = 3;
 
-template <int DT, int WARPS, int S>
+template <int DT, int WARPS, int S, typename ST>
 struct PgGeom {
   static constexpr uint32_t TB = DT == SNL_Q8_0 ? 512 : 256;
   static constexpr uint32_t kStageW = kPgTiles * TB;
-  static constexpr uint32_t kStageS = kPgTiles / 4 * 128;  // fp16 scales: 16 rows x 4 blocks per four tiles
+  static constexpr uint32_t kStageS = kPgTiles / 4 * 64 * sizeof(ST);  // scales: 16 rows x 4 blocks per four tiles
   static constexpr uint32_t kStage = kStageW + kStageS;
   static constexpr uint32_t kWarpBytes = S * kStage;
   static constexpr uint32_t kSmem = WARPS * kWarpBytes + WARPS * S * 8;
@@ -487,10 +500,10 @@ __device__ __forceinline__ void fused_norm_prologue(const GemvArgs& a, int lane,
   }
 }
 
-template <int DT, int M, int WARPS, int S>
+template <int DT, int M, int WARPS, int S, typename ST>
 __global__ void __launch_bounds__(WARPS * 32, WARPS >= 16 ? 2 : 3) gemv_pg_kernel(GemvArgs a, const uint8_t* __restrict__ tiles,
-                                                             const __half* __restrict__ ts, uint32_t groups, int* err) {
-  using G = PgGeom<DT, WARPS, S>;
+                                                             const ST* __restrict__ ts, uint32_t groups, int* err) {
+  using G = PgGeom<DT, WARPS, S, ST>;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float red[2][WARPS][M][16];
   __shared__ float nrm[M];
@@ -516,7 +529,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS >= 16 ? 2 : 3) gemv_pg_kerne
     if (lane != 0) return;
     const uint32_t grp = g0 + j / nst, sg = st0 + j % nst;
     const uint32_t nt = min((uint32_t)kPgTiles, nb - sg * kPgTiles);
-    const uint32_t wbytes = nt * G::TB, sbytes = (nt + 3) / 4 * 128;
+    const uint32_t wbytes = nt * G::TB, sbytes = (nt + 3) / 4 * 64 * (uint32_t)sizeof(ST);
     uint8_t* st = ring + (j % S) * G::kStage;
     mbar_arrive_expect_tx(&bars[j % S], wbytes + sbytes);
     bulk_g2s(st, tiles + ((uint64_t)grp * nb + sg * kPgTiles) * G::TB, wbytes, &bars[j % S], pol);
@@ -552,7 +565,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS >= 16 ? 2 : 3) gemv_pg_kerne
         continue;
       }
       const uint8_t* st = ring + (j % S) * G::kStage;
-      const __half* sc = reinterpret_cast<const __half*>(st + G::kStageW);
+      const ST* sc = reinterpret_cast<const ST*>(st + G::kStageW);
 #pragma unroll
       for (int u = 0; u < kPgTiles; u++) {
         if ((uint32_t)u >= nt) break;
@@ -570,8 +583,8 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS >= 16 ? 2 : 3) gemv_pg_kerne
           mma16816(d, A0, xv[u].x, xv[u].y);
           mma16816(d, A1, xv[u].z, xv[u].w);
         }
-        const float scA = __half2float(sc[(u / 4) * 64 + g * 4 + (u % 4)]);
-        const float scB = __half2float(sc[(u / 4) * 64 + (g + 8) * 4 + (u % 4)]);
+        const float scA = scale_f(sc[(u / 4) * 64 + g * 4 + (u % 4)]);
+        const float scB = scale_f(sc[(u / 4) * 64 + (g + 8) * 4 + (u % 4)]);
         accA = fmaf(scA, d[0] + d[1], accA);
         accB = fmaf(scB, d[2] + d[3], accB);
       }
@@ -603,13 +616,13 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS >= 16 ? 2 : 3) gemv_pg_kerne
   }
 }
 
-template <int DT, int M, int WARPS, int S>
-int launch_pg_cfg(const GemvArgs& a, const void* tiles, const __half* ts, uint32_t groups, int* err, cudaStream_t s) {
-  using G = PgGeom<DT, WARPS, S>;
+template <int DT, int M, int WARPS, int S, typename ST>
+int launch_pg_cfg(const GemvArgs& a, const void* tiles, const ST* ts, uint32_t groups, int* err, cudaStream_t s) {
+  using G = PgGeom<DT, WARPS, S, ST>;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
-  auto kern = gemv_pg_kernel<DT, M, WARPS, S>;
+  auto kern = gemv_pg_kernel<DT, M, WARPS, S, ST>;
   if (dev >= 0 && dev < 64 && !attr[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
     if (e != cudaSuccess) return cuda_fail(e, "gemv_pg: smem attribute");
@@ -621,96 +634,116 @@ int launch_pg_cfg(const GemvArgs& a, const void* tiles, const __half* ts, uint32
   return SNL_OK;
 }
 
-template <int DT, int M>
-int launch_pg_t(const GemvArgs& a, const void* tiles, const __half* ts, int* err, cudaStream_t s) {
+template <int DT, int M, typename ST>
+int launch_pg_t(const GemvArgs& a, const void* tiles, const ST* ts, int* err, cudaStream_t s) {
   const uint32_t groups = (a.n + 15) / 16;
   const bool few = groups <= 2u * (uint32_t)sm_count();
   constexpr int kSA = DT == SNL_Q8_0 ? 2 : 3;  // stages per warp, 8-warp CTA
-  if (few) return launch_pg_cfg<DT, M, 16, 1>(a, tiles, ts, groups, err, s);
-  return launch_pg_cfg<DT, M, 8, kSA>(a, tiles, ts, groups, err, s);
+  if (few) return launch_pg_cfg<DT, M, 16, 1, ST>(a, tiles, ts, groups, err, s);
+  return launch_pg_cfg<DT, M, 8, kSA, ST>(a, tiles, ts, groups, err, s);
 }
 
 }  // namespace
 
-void tile_sizes(int dtype, uint32_t n, uint32_t k, size_t* tile_bytes, size_t* scale_bytes) {
+void tile_sizes(int dtype, uint32_t n, uint32_t k, size_t* tile_bytes, size_t* scale_floats) {
   const size_t groups = (n + 15) / 16, nb = k / 32, nb4 = (nb + 3) / 4;
   *tile_bytes = groups * nb * (dtype == SNL_Q8_0 ? 512 : 256);
-  *scale_bytes = groups * nb4 * 64 * sizeof(__half);
+  *scale_floats = groups * nb4 * 64;
 }
 
-int launch_repack_tiles(int dtype, uint32_t n, uint32_t k, const void* q, const float* s, void* tiles, __half* ts,
-                        int* dflag, bool* exact, cudaStream_t st, uint32_t pair_half) {
-  if (k % 32 || n == 0) return fail(SNL_E_INVALID, "repack: k must be a multiple of 32");
-  if (pair_half && (n != 2 * pair_half || pair_half % 8)) return fail(SNL_E_INVALID, "repack: bad row pairing");
-  if (!dflag || !exact) return fail(SNL_E_INVALID, "repack: no flag");
-  size_t tb, sb;
-  tile_sizes(dtype, n, k, &tb, &sb);
-  cudaError_t e = cudaMemsetAsync(ts, 0, sb, st);  // scales of blocks past k in the last four
-  if (e == cudaSuccess) e = cudaMemsetAsync(dflag, 0, sizeof(int), st);
-  if (e != cudaSuccess) return cuda_fail(e, "repack: memset");
-  const uint64_t threads = (uint64_t)((n + 15) / 16) * (k / 32) * 32;
-  repack_tiles_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
-      dtype, n, k, static_cast<const uint8_t*>(q), s, static_cast<uint8_t*>(tiles), ts, pair_half, dflag);
-  SNL_LAUNCH_CHECK("repack_tiles");
+int scales_fp16_exact(const float* s, uint64_t count, int* dflag, bool* exact, cudaStream_t st) {
+  if (!dflag || !exact) return fail(SNL_E_INVALID, "scale check: no flag");
+  cudaError_t e = cudaMemsetAsync(dflag, 0, sizeof(int), st);
+  if (e != cudaSuccess) return cuda_fail(e, "scale check: memset");
+  if (count) {
+    const uint64_t blocks = std::min<uint64_t>((count + 255) / 256, (uint64_t)sm_count() * 8);
+    fp16_exact_kernel<<<(unsigned)blocks, 256, 0, st>>>(s, count, dflag);
+    SNL_LAUNCH_CHECK("fp16_exact");
+  }
   int h = 0;
   e = cudaMemcpyAsync(&h, dflag, sizeof(int), cudaMemcpyDeviceToHost, st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-  if (e != cudaSuccess) return cuda_fail(e, "repack: flag");
+  if (e != cudaSuccess) return cuda_fail(e, "scale check: flag");
   *exact = h == 0;
   return SNL_OK;
 }
 
-int launch_gemv_tile(int dtype, const GemvArgs& a, uint32_t m, const void* tiles, const __half* ts, cudaStream_t s) {
+int launch_repack_tiles(int dtype, uint32_t n, uint32_t k, const void* q, const float* s, void* tiles, void* ts,
+                        int ts_f16, cudaStream_t st, uint32_t pair_half) {
+  if (k % 32 || n == 0) return fail(SNL_E_INVALID, "repack: k must be a multiple of 32");
+  if (pair_half && (n != 2 * pair_half || pair_half % 8)) return fail(SNL_E_INVALID, "repack: bad row pairing");
+  size_t tb, sf;
+  tile_sizes(dtype, n, k, &tb, &sf);
+  // Scales of blocks past k in the last four stay zero.
+  cudaError_t e = cudaMemsetAsync(ts, 0, sf * (ts_f16 ? sizeof(__half) : sizeof(float)), st);
+  if (e != cudaSuccess) return cuda_fail(e, "repack: memset");
+  const uint64_t threads = (uint64_t)((n + 15) / 16) * (k / 32) * 32;
+  repack_tiles_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
+      dtype, n, k, static_cast<const uint8_t*>(q), s, static_cast<uint8_t*>(tiles), ts, ts_f16, pair_half);
+  SNL_LAUNCH_CHECK("repack_tiles");
+  return SNL_OK;
+}
+
+template <typename ST>
+int launch_gemv_tile_t(int dtype, const GemvArgs& a, uint32_t m, const void* tiles, const ST* ts, cudaStream_t s) {
+  int* err = nullptr;
+  if (int rc = device_error_word(&err)) return rc;
+  if (dtype == SNL_Q8_0) {
+    switch (m) {
+      case 1: return launch_pg_t<SNL_Q8_0, 1, ST>(a, tiles, ts, err, s);
+      case 2: return launch_pg_t<SNL_Q8_0, 2, ST>(a, tiles, ts, err, s);
+      case 3: return launch_pg_t<SNL_Q8_0, 3, ST>(a, tiles, ts, err, s);
+      case 4: return launch_pg_t<SNL_Q8_0, 4, ST>(a, tiles, ts, err, s);
+    }
+  } else if (dtype == SNL_Q4_0) {
+    switch (m) {
+      case 1: return launch_pg_t<SNL_Q4_0, 1, ST>(a, tiles, ts, err, s);
+      case 2: return launch_pg_t<SNL_Q4_0, 2, ST>(a, tiles, ts, err, s);
+      case 3: return launch_pg_t<SNL_Q4_0, 3, ST>(a, tiles, ts, err, s);
+      case 4: return launch_pg_t<SNL_Q4_0, 4, ST>(a, tiles, ts, err, s);
+    }
+  }
+  return fail(SNL_E_INVALID, "gemv_tile: dtype / rows");
+}
+
+int launch_gemv_tile(int dtype, const GemvArgs& a, uint32_t m, const void* tiles, const void* ts, int ts_f16,
+                     cudaStream_t s) {
   if (a.k == 0 || a.k % 32) return fail(SNL_E_INVALID, "gemv_tile: k must be a multiple of 32");
   if (a.plane_stride % 8 || ((uintptr_t)a.xplanes % 16)) return fail(SNL_E_INVALID, "gemv_tile: planes alignment");
   if (a.n == 0) return SNL_OK;
   if (a.mode == 2 && (!a.act_planes || a.n % 16)) return fail(SNL_E_INVALID, "gemv_tile: swiglu epilogue arguments");
   if (a.fused_norm && (m % 2 || a.mode == 1 || !a.nrpart)) return fail(SNL_E_INVALID, "gemv_tile: fused norm arguments");
-  int* err = nullptr;
-  if (int rc = device_error_word(&err)) return rc;
-  if (dtype == SNL_Q8_0) {
-    switch (m) {
-      case 1: return launch_pg_t<SNL_Q8_0, 1>(a, tiles, ts, err, s);
-      case 2: return launch_pg_t<SNL_Q8_0, 2>(a, tiles, ts, err, s);
-      case 3: return launch_pg_t<SNL_Q8_0, 3>(a, tiles, ts, err, s);
-      case 4: return launch_pg_t<SNL_Q8_0, 4>(a, tiles, ts, err, s);
-    }
-  } else if (dtype == SNL_Q4_0) {
-    switch (m) {
-      case 1: return launch_pg_t<SNL_Q4_0, 1>(a, tiles, ts, err, s);
-      case 2: return launch_pg_t<SNL_Q4_0, 2>(a, tiles, ts, err, s);
-      case 3: return launch_pg_t<SNL_Q4_0, 3>(a, tiles, ts, err, s);
-      case 4: return launch_pg_t<SNL_Q4_0, 4>(a, tiles, ts, err, s);
-    }
-  }
-  return fail(SNL_E_INVALID, "gemv_tile: dtype / rows");
+  if (ts_f16) return launch_gemv_tile_t(dtype, a, m, tiles, static_cast<const __half*>(ts), s);
+  return launch_gemv_tile_t(dtype, a, m, tiles, static_cast<const float*>(ts), s);
 }
 
 }  // namespace snl
 
 extern "C" int snl_tile_sizes(int dtype, uint32_t n, uint32_t k, size_t* tile_bytes, size_t* scale_bytes) {
   if (!tile_bytes || !scale_bytes || (dtype != SNL_Q8_0 && dtype != SNL_Q4_0)) return snl::fail(SNL_E_INVALID, "snl_tile_sizes");
-  snl::tile_sizes(dtype, n, k, tile_bytes, scale_bytes);
+  size_t sf = 0;
+  snl::tile_sizes(dtype, n, k, tile_bytes, &sf);
+  *scale_bytes = sf * sizeof(float);
   return SNL_OK;
 }
 extern "C" int snl_tile_repack(int dtype, uint32_t n, uint32_t k, const void* q, const float* s, void* tiles,
-                               void* tile_scales, void* stream) {
-  if (!q || !s || !tiles || !tile_scales || (dtype != SNL_Q8_0 && dtype != SNL_Q4_0))
+                               void* tile_scales, int* scales_f16, void* stream) {
+  if (!q || !s || !tiles || !tile_scales || !scales_f16 || (dtype != SNL_Q8_0 && dtype != SNL_Q4_0))
     return snl::fail(SNL_E_INVALID, "snl_tile_repack: bad argument");
+  if (k % 32) return snl::fail(SNL_E_INVALID, "snl_tile_repack: k must be a multiple of 32");
   int* dflag = nullptr;
   if (cudaMalloc(&dflag, sizeof(int)) != cudaSuccess) return snl::fail(SNL_E_OOM, "snl_tile_repack: flag");
   bool exact = false;
-  const int rc = snl::launch_repack_tiles(dtype, n, k, q, s, tiles, static_cast<__half*>(tile_scales), dflag, &exact,
-                                          (cudaStream_t)stream);
+  int rc = snl::scales_fp16_exact(s, (uint64_t)n * (k / 32), dflag, &exact, (cudaStream_t)stream);
   cudaFree(dflag);
   if (rc) return rc;
-  if (!exact) return snl::fail(SNL_E_INVALID, "snl_tile_repack: block scales are not fp16 numbers");
-  return SNL_OK;
+  *scales_f16 = exact ? 1 : 0;
+  return snl::launch_repack_tiles(dtype, n, k, q, s, tiles, tile_scales, *scales_f16, (cudaStream_t)stream);
 }
 extern "C" int snl_mat_tiles(int dtype, const snl_mat_p* p, uint32_t rows_m, const void* planes, const void* tiles,
-                             const void* tile_scales, float* y, void* stream) {
+                             const void* tile_scales, int scales_f16, float* y, void* stream) {
   if (!p || !planes || !tiles || !tile_scales || !y) return snl::fail(SNL_E_INVALID, "snl_mat_tiles: null argument");
   if (rows_m == 0 || rows_m > 4) return snl::fail(SNL_E_INVALID, "snl_mat_tiles: 1..4 token rows");
   snl::GemvArgs a = snl::gemv_args_plain(*p, static_cast<const __half*>(planes), p->k, tiles, y);
-  return snl::launch_gemv_tile(dtype, a, rows_m, tiles, static_cast<const __half*>(tile_scales), (cudaStream_t)stream);
+  return snl::launch_gemv_tile(dtype, a, rows_m, tiles, tile_scales, scales_f16, (cudaStream_t)stream);
 }

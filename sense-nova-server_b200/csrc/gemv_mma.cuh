@@ -169,12 +169,15 @@ inline GemvArgs gemv_args_plain(const snl_mat_p& p, const __half* planes, uint32
 
 int launch_gemv_mma(int dtype, const GemvArgs& a, uint32_t m, const void* ws, int scale_f16, cudaStream_t s);
 // Tile layout (see gemv_mma.cu): sizes, device repack from the reference layout, GEMV.
-void tile_sizes(int dtype, uint32_t n, uint32_t k, size_t* tile_bytes, size_t* scale_bytes);
-// Repacks and waits for it; *exact = every block scale converted to fp16 exactly (dflag:
-// one device int of scratch).
-int launch_repack_tiles(int dtype, uint32_t n, uint32_t k, const void* q, const float* s, void* tiles, __half* ts,
-                        int* dflag, bool* exact, cudaStream_t st, uint32_t pair_half = 0);
-int launch_gemv_tile(int dtype, const GemvArgs& a, uint32_t m, const void* tiles, const __half* ts, cudaStream_t s);
+void tile_sizes(int dtype, uint32_t n, uint32_t k, size_t* tile_bytes, size_t* scale_floats);
+// *exact = every one of the count f32 scales is an fp16 number (waits; dflag: one device
+// int of scratch).
+int scales_fp16_exact(const float* s, uint64_t count, int* dflag, bool* exact, cudaStream_t st);
+// ts: scale_floats fp16 (ts_f16) or f32 values.
+int launch_repack_tiles(int dtype, uint32_t n, uint32_t k, const void* q, const float* s, void* tiles, void* ts,
+                        int ts_f16, cudaStream_t st, uint32_t pair_half = 0);
+int launch_gemv_tile(int dtype, const GemvArgs& a, uint32_t m, const void* tiles, const void* ts, int ts_f16,
+                     cudaStream_t s);
 int launch_xpack(const float* x, uint32_t m, uint32_t k, uint32_t x_stride, __half* planes, uint32_t plane_stride,
                  cudaStream_t s);
 

@@ -138,6 +138,12 @@ class Engine:
     def has_mtp(self) -> bool:
         return bool(self.lib.snl_engine_has_mtp(self._h))
 
+    def tile_scales(self) -> tuple[int, int]:
+        """(matrices whose decode tile layout keeps fp16 block scales, those keeping f32)."""
+        a, b = C.c_uint32(), C.c_uint32()
+        ffi.check(self.lib.snl_engine_tile_scales(self._h, C.byref(a), C.byref(b)))
+        return a.value, b.value
+
     def reset(self) -> None:
         ffi.check(self.lib.snl_engine_reset(self._h))
 

@@ -98,8 +98,8 @@ SIGNATURES = {
     "snl_xpack": (i32, [vp, u32, u32, u32, vp, vp]),
     "snl_mat_xpack": (i32, [i32, P(MatP), u32, vp, vp, vp, vp, vp]),
     "snl_tile_sizes": (i32, [i32, u32, u32, P(sz), P(sz)]),
-    "snl_tile_repack": (i32, [i32, u32, u32, vp, vp, vp, vp, vp]),
-    "snl_mat_tiles": (i32, [i32, P(MatP), u32, vp, vp, vp, vp, vp]),
+    "snl_tile_repack": (i32, [i32, u32, u32, vp, vp, vp, vp, P(i32), vp]),
+    "snl_mat_tiles": (i32, [i32, P(MatP), u32, vp, vp, vp, i32, vp, vp]),
     "snl_branch_norm": (i32, [P(StepU), P(LayerP), vp, vp, vp, vp, u32, vp]),
     "snl_mhc_dots": (i32, [P(StepU), P(LayerP), vp, vp, vp, vp]),
     "snl_mhc_finish": (i32, [P(StepU), P(LayerP), vp, vp, vp, vp]),
@@ -135,6 +135,7 @@ SIGNATURES = {
     "snl_engine_rollback": (i32, [vp]),
     "snl_engine_hid_rows": (sz, [vp]),
     "snl_engine_has_mtp": (i32, [vp]),
+    "snl_engine_tile_scales": (i32, [vp, P(u32), P(u32)]),
     "snl_engine_pos": (sz, [vp]),
     "snl_engine_ctx": (sz, [vp]),
     "snl_engine_device_bytes": (sz, [vp]),

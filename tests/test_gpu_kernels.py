@@ -175,31 +175,45 @@ def test_mat_tiles(T, lib, orc, dtype, m, n, k):
     call(lib.snl_tile_sizes(dtype, n, k, C.byref(tb), C.byref(sf)))
     tiles = T.empty(tb.value, dtype=T.uint8, device="cuda")
     ts = T.empty(sf.value, dtype=T.uint8, device="cuda")
-    call(lib.snl_tile_repack(dtype, n, k, ptr(dev(T, q)), ptr(dev(T, s)), ptr(tiles), ptr(ts), None))
+    f16 = C.c_int(-1)
+    call(lib.snl_tile_repack(dtype, n, k, ptr(dev(T, q)), ptr(dev(T, s)), ptr(tiles), ptr(ts), C.byref(f16), None))
+    assert f16.value == 1  # the synthetic block scales are fp16 numbers
     planes = T.empty(2 * m * k, dtype=T.float16, device="cuda")
     call(lib.snl_xpack(ptr(dev(T, x)), m, k, k, ptr(planes), None))
     y = T.zeros((m, n), device="cuda")
     p = MatP(n, k, 0, k, 0, n, 0, 0)
-    call(lib.snl_mat_tiles(dtype, C.byref(p), m, ptr(planes), ptr(tiles), ptr(ts), ptr(y), None))
+    call(lib.snl_mat_tiles(dtype, C.byref(p), m, ptr(planes), ptr(tiles), ptr(ts), f16.value, ptr(y), None))
     err = rel(host(y), ref)
     assert err < TOL and err < 2e-5, err
 
 
-def test_tile_repack_rejects_non_fp16_scales(T, lib, orc):
-    """The tile layout keeps fp16 block scales (Q8_0/Q4_0 scales are fp16 numbers); a
-    scale that is not one is refused, not rounded."""
-    n, k = 32, 64
-    q, s = orc.gen_quant(5, "wtile", SNL_Q8_0, n, k)
+@pytest.mark.parametrize("dtype", [SNL_Q8_0, SNL_Q4_0])
+def test_tile_scales_f32_mode(T, lib, orc, dtype):
+    """Block scales that are not fp16 numbers (as a converter computing them in f32
+    writes) keep the tile layout's f32 scale mode: same results as the file layout."""
+    n, k, m = 300, 1024, 2
+    rng = np.random.default_rng(41)
+    q, s = orc.gen_quant(9, "wtile", dtype, n, k)
+    s = (s * np.float32(1.0 + 1e-3)).astype(np.float32)  # off the fp16 grid
+    s.flat[0] = np.float32(0.1)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    ref = np.zeros((m, n), np.float32)
+    orc.mat(dtype, StepU(m, 0, 1, 0), MatP(n, k, 0, k, 0, n, 0, 0), x, q, s, ref)
     tb, sb = C.c_size_t(), C.c_size_t()
-    call(lib.snl_tile_sizes(SNL_Q8_0, n, k, C.byref(tb), C.byref(sb)))
-    assert sb.value == (n // 16) * ((k // 32 + 3) // 4) * 64 * 2
+    call(lib.snl_tile_sizes(dtype, n, k, C.byref(tb), C.byref(sb)))
+    assert sb.value == ((n + 15) // 16) * ((k // 32 + 3) // 4) * 64 * 4
     tiles = T.empty(tb.value, dtype=T.uint8, device="cuda")
     ts = T.empty(sb.value, dtype=T.uint8, device="cuda")
-    call(lib.snl_tile_repack(SNL_Q8_0, n, k, ptr(dev(T, q)), ptr(dev(T, s)), ptr(tiles), ptr(ts), None))
-    bad = s.copy()
-    bad.flat[7] = np.float32(0.1)  # not an fp16 number
-    rc = lib.snl_tile_repack(SNL_Q8_0, n, k, ptr(dev(T, q)), ptr(dev(T, bad)), ptr(tiles), ptr(ts), None)
-    assert rc == -1  # SNL_E_INVALID
+    f16 = C.c_int(-1)
+    call(lib.snl_tile_repack(dtype, n, k, ptr(dev(T, q)), ptr(dev(T, s)), ptr(tiles), ptr(ts), C.byref(f16), None))
+    assert f16.value == 0
+    planes = T.empty(2 * m * k, dtype=T.float16, device="cuda")
+    call(lib.snl_xpack(ptr(dev(T, x)), m, k, k, ptr(planes), None))
+    y = T.zeros((m, n), device="cuda")
+    call(lib.snl_mat_tiles(dtype, C.byref(MatP(n, k, 0, k, 0, n, 0, 0)), m, ptr(planes), ptr(tiles), ptr(ts), 0,
+                           ptr(y), None))
+    err = rel(host(y), ref)
+    assert err < TOL and err < 2e-5, err
 
 
 def test_mat_tensor_core_wide_range(T, lib, orc):
