@@ -17,31 +17,56 @@ namespace {
 
 constexpr uint32_t DK = 128, DV = 128;
 
-// conv: one thread per channel walking the tokens of the step.
-__global__ void conv_kernel(StepRef sr, snl_lin_p p, const float* __restrict__ proj, float* __restrict__ conv_out,
-                            float* __restrict__ cs, const float* __restrict__ lw, float* __restrict__ ck) {
+// conv (linear.wgsl:38-66), token-parallel: thread (channel c, run of kConvTok tokens)
+// reads the run's inputs and the three before it (from the carried state for tokens
+// before the step) and writes SiLU(w . x) per token, the same expression as the
+// sequential form. The carried state and the checkpoint are written afterwards by
+// conv_state_kernel, once every thread has read the old state.
+constexpr uint32_t kConvTok = 8;
+
+__global__ void __launch_bounds__(256) conv_kernel(StepRef sr, snl_lin_p p, const float* __restrict__ proj,
+                                                   float* __restrict__ conv_out, const float* __restrict__ cs,
+                                                   const float* __restrict__ lw) {
   const snl_step_u st = load_step(sr);
-  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
-  const uint32_t cd = p.conv_dim;
-  if (c >= cd) return;
+  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x, cd = p.conv_dim;
+  const uint32_t m0 = blockIdx.y * kConvTok;
+  if (c >= cd || m0 >= st.m) return;
   const float4 w = *reinterpret_cast<const float4*>(lw + (uint64_t)c * 4);
-  float r0 = cs[c], r1 = cs[cd + c], r2 = cs[2 * cd + c];
-  for (uint32_t m = 0; m < st.m; m++) {
-    const float cur = proj[(uint64_t)m * p.proj_stride + c];
-    const float o = fmaf(w.w, cur, fmaf(w.z, r2, fmaf(w.y, r1, w.x * r0)));
-    conv_out[(uint64_t)m * cd + c] = o / (1.0f + __expf(-o));
-    r0 = r1;
-    r1 = r2;
-    r2 = cur;
-    if (m + 1 == st.ckpt) {
-      ck[c] = r0;
-      ck[cd + c] = r1;
-      ck[2 * cd + c] = r2;
-    }
+  float xv[kConvTok + 3];
+#pragma unroll
+  for (uint32_t j = 0; j < kConvTok + 3; j++) {
+    const int t = (int)(m0 + j) - 3;
+    xv[j] = t < 0 ? cs[(uint64_t)(t + 3) * cd + c] : ((uint32_t)t < st.m ? proj[(uint64_t)t * p.proj_stride + c] : 0.f);
   }
-  cs[c] = r0;
-  cs[cd + c] = r1;
-  cs[2 * cd + c] = r2;
+#pragma unroll
+  for (uint32_t j = 0; j < kConvTok; j++) {
+    const uint32_t m = m0 + j;
+    if (m >= st.m) break;
+    const float o = fmaf(w.w, xv[j + 3], fmaf(w.z, xv[j + 2], fmaf(w.y, xv[j + 1], w.x * xv[j])));
+    conv_out[(uint64_t)m * cd + c] = o / (1.0f + __expf(-o));
+  }
+}
+
+// The carried conv state after the step (the last three inputs, older ones from the
+// state before it) and, if ckpt > 0, the state after token ckpt - 1.
+__global__ void __launch_bounds__(256) conv_state_kernel(StepRef sr, snl_lin_p p, const float* __restrict__ proj,
+                                                         float* __restrict__ cs, float* __restrict__ ck) {
+  const snl_step_u st = load_step(sr);
+  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x, cd = p.conv_dim;
+  if (c >= cd || st.m == 0) return;
+  const float old[3] = {cs[c], cs[(uint64_t)cd + c], cs[(uint64_t)2 * cd + c]};
+  auto x = [&](int t) { return t < 0 ? old[t + 3] : proj[(uint64_t)t * p.proj_stride + c]; };
+  if (st.ckpt > 0 && ck) {
+    const int k = (int)st.ckpt;
+    ck[c] = x(k - 3);
+    ck[(uint64_t)cd + c] = x(k - 2);
+    ck[(uint64_t)2 * cd + c] = x(k - 1);
+  }
+  const int m = (int)st.m;
+  const float n0 = x(m - 3), n1 = x(m - 2), n2 = x(m - 1);
+  cs[c] = n0;
+  cs[(uint64_t)cd + c] = n1;
+  cs[(uint64_t)2 * cd + c] = n2;
 }
 
 // delta: CTA per value head, thread j owns state column j (128 floats in registers).
@@ -435,44 +460,103 @@ struct DnScratch {
   float* chunks;  // [n_v][n_chunks][kDnChunkFloats]
 };
 
+// 3xTF32 tensor-core products (mma.sync m16n8k8, f32 accumulate): each f32 operand is
+// split into tf32 hi + lo and hi*hi + hi*lo + lo*hi are accumulated, which keeps about
+// fp32 accuracy (the dropped lo*lo term is below 2^-22 of the product).
+__device__ __forceinline__ uint32_t tf32_of(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ void tf32_split(float x, uint32_t& hi, uint32_t& lo) {
+  hi = tf32_of(x);
+  lo = tf32_of(x - __uint_as_float(hi));
+}
+__device__ __forceinline__ void mma_tf32(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// d += A(16 x 8) B(8 x 8) in 3xTF32; a[4] / b[2] are the f32 fragment values (m16n8k8:
+// a0 (g, t), a1 (g + 8, t), a2 (g, t + 4), a3 (g + 8, t + 4); b0 (t, g), b1 (t + 4, g)).
+__device__ __forceinline__ void mma3_tf32(float d[4], const float a[4], const float b[2]) {
+  uint32_t ah[4], al[4], bh[2], bl[2];
+#pragma unroll
+  for (int i = 0; i < 4; i++) tf32_split(a[i], ah[i], al[i]);
+  tf32_split(b[0], bh[0], bl[0]);
+  tf32_split(b[1], bh[1], bl[1]);
+  mma_tf32(d, al, bh[0], bh[1]);
+  mma_tf32(d, ah, bl[0], bl[1]);
+  mma_tf32(d, ah, bh[0], bh[1]);
+}
+
+// Per (chunk, value head): P, R, W, U, Kd and gamma_C of the WY form, on the tensor
+// cores (3xTF32). Shared memory: the chunk's q, k, v rows (row stride 132), L / X / T
+// and M (64 x 68), W and U (64 x 132).
+constexpr uint32_t kPrS = 132, kPrT = 68;
+constexpr size_t kPrepSmemFloats = 5 * kDnC * kPrS + 2 * kDnC * kPrT;
+
+// 16 x 8 output tile (rows 16 mt, columns 8 nt) += A[rows][k] * B[k][cols] over k in
+// [k0, k1) (multiples of 8): A row-major with stride sa; B given by element (k, n) at
+// b[k * sbk + n * sbn].
+__device__ __forceinline__ void tile_mma3(float acc[4], const float* a, uint32_t sa, const float* b, uint32_t sbk,
+                                          uint32_t sbn, uint32_t mt, uint32_t nt, uint32_t k0, uint32_t k1, uint32_t g,
+                                          uint32_t t4) {
+  for (uint32_t k = k0; k < k1; k += 8) {
+    const float* ar = a + (16 * mt + g) * sa + k + t4;
+    const float av[4] = {ar[0], ar[8 * sa], ar[4], ar[8 * sa + 4]};
+    const float* br = b + (uint64_t)(k + t4) * sbk + (uint64_t)(8 * nt + g) * sbn;
+    const float bv[2] = {br[0], br[4 * sbk]};
+    mma3_tf32(acc, av, bv);
+  }
+}
+
 __global__ void __launch_bounds__(256) dn_prep_kernel(uint32_t m, snl_lin_p p, const float* __restrict__ proj,
                                                       const float* __restrict__ conv_out, const float* __restrict__ lw,
                                                       float* __restrict__ chunks) {
   extern __shared__ __align__(16) float dsm[];
-  float* kn = dsm;                    // [C][128]
-  float* qn = kn + kDnC * DK;         // [C][128]
-  float* vv = qn + kDnC * DK;         // [C][128]
-  float* X = vv + kDnC * DV;          // [C][C]: L, then (I+L)^-1
-  float* Mq = X + kDnC * kDnC;        // [C][C]
-  float* W = Mq + kDnC * kDnC;        // [C][128]
-  float* U = W + kDnC * DK;           // [C][128]
-  __shared__ float lam[kDnC], beta[kDnC];
+  float* kn = dsm;                 // [C][kPrS]: k, then Gamma K
+  float* qn = kn + kDnC * kPrS;    // [C][kPrS]
+  float* vv = qn + kDnC * kPrS;    // [C][kPrS]
+  float* W = vv + kDnC * kPrS;     // [C][kPrS]
+  float* U = W + kDnC * kPrS;      // [C][kPrS]
+  float* X = U + kDnC * kPrS;      // [C][kPrT]: L, then X = (I + L)^-1, then T = X diag(beta)
+  float* Mq = X + kDnC * kPrT;     // [C][kPrT]
+  __shared__ float lam[kDnC], beta[kDnC], elam[kDnC];
   const uint32_t c = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t g = lane >> 2, t4 = lane & 3;
   const uint32_t t0 = c * kDnC, ce = min(kDnC, m - t0);
   const uint32_t kh = h / (p.n_v / p.n_k), cd = p.conv_dim, key_dim = p.n_k * DK;
   const uint32_t b_off = cd + p.n_v * DV, a_off = b_off + p.n_v;
+  float* rec = chunks + ((uint64_t)h * gridDim.x + c) * kDnChunkFloats;
+  float* Pg = rec;
+  float* Rg = Pg + kDnC * DK;
+  float* Wg = Rg + kDnC * DV;
+  float* Ug = Wg + kDnC * DK;
+  float* Kd = Ug + kDnC * DV;
   // 1. q, k, v rows of the chunk (zero past the step's end), then per-token norms.
   for (uint32_t e = tid; e < kDnC * DK; e += blockDim.x) {
     const uint32_t t = e / DK, i = e % DK;
     const bool in = t < ce;
     const uint64_t row = (uint64_t)(t0 + t) * cd;
-    qn[e] = in ? conv_out[row + kh * DK + i] : 0.f;
-    kn[e] = in ? conv_out[row + key_dim + kh * DK + i] : 0.f;
-    vv[e] = in ? conv_out[row + 2 * key_dim + h * DV + i] : 0.f;
+    qn[t * kPrS + i] = in ? conv_out[row + kh * DK + i] : 0.f;
+    kn[t * kPrS + i] = in ? conv_out[row + key_dim + kh * DK + i] : 0.f;
+    vv[t * kPrS + i] = in ? conv_out[row + 2 * key_dim + h * DV + i] : 0.f;
   }
   __syncthreads();
   for (uint32_t t = warp; t < kDnC; t += blockDim.x / 32) {
     float sq = 0.f, sk = 0.f;
     for (uint32_t i = lane; i < DK; i += 32) {
-      sq = fmaf(qn[t * DK + i], qn[t * DK + i], sq);
-      sk = fmaf(kn[t * DK + i], kn[t * DK + i], sk);
+      sq = fmaf(qn[t * kPrS + i], qn[t * kPrS + i], sq);
+      sk = fmaf(kn[t * kPrS + i], kn[t * kPrS + i], sk);
     }
     sq = warp_sum(sq);
     sk = warp_sum(sk);
     const float rq = rsqrtf(sq + 1e-6f) * rsqrtf((float)DK), rk = rsqrtf(sk + 1e-6f);
     for (uint32_t i = lane; i < DK; i += 32) {
-      qn[t * DK + i] *= rq;
-      kn[t * DK + i] *= rk;
+      qn[t * kPrS + i] *= rq;
+      kn[t * kPrS + i] *= rk;
     }
   }
   if (tid == 0) {
@@ -491,98 +575,155 @@ __global__ void __launch_bounds__(256) dn_prep_kernel(uint32_t m, snl_lin_p p, c
       acc += lt;
       lam[t] = acc;
       beta[t] = bt;
+      elam[t] = __expf(acc);
     }
   }
   __syncthreads();
-  // 2. L (strictly lower) and M (lower with diagonal) from the Gram matrices.
-  for (uint32_t e = tid; e < kDnC * kDnC; e += blockDim.x) {
-    const uint32_t t = e / kDnC, s2 = e % kDnC;
-    float gk = 0.f, gq = 0.f;
-    if (s2 <= t) {
-      const float4* a4 = reinterpret_cast<const float4*>(kn + t * DK);
-      const float4* q4 = reinterpret_cast<const float4*>(qn + t * DK);
-      const float4* b4 = reinterpret_cast<const float4*>(kn + s2 * DK);
-#pragma unroll 8
-      for (uint32_t i = 0; i < DK / 4; i++) {
-        const float4 x = a4[i], y = b4[i], z = q4[i];
-        gk = fmaf(x.x, y.x, fmaf(x.y, y.y, fmaf(x.z, y.z, fmaf(x.w, y.w, gk))));
-        gq = fmaf(z.x, y.x, fmaf(z.y, y.y, fmaf(z.z, y.z, fmaf(z.w, y.w, gq))));
+  // 2. Gram matrices K K^T and Q K^T (64 x 64, K = 128): warp w takes row tile w / 2 and
+  //    column tiles 4 (w % 2) .. + 3; tiles wholly above the diagonal are zero. Then
+  //    L[t][s] = beta_t e^(lam_t - lam_s) k_t.k_s (s < t), M[t][s] = e^(lam_t - lam_s) q_t.k_s (s <= t).
+  {
+    const uint32_t mt = warp >> 1;
+#pragma unroll 1
+    for (uint32_t q = 0; q < 4; q++) {
+      const uint32_t nt = (warp & 1) * 4 + q;
+      float gk[4] = {0.f, 0.f, 0.f, 0.f}, gq[4] = {0.f, 0.f, 0.f, 0.f};
+      if (8 * nt <= 16 * mt + 15) {
+        tile_mma3(gk, kn, kPrS, kn, 1, kPrS, mt, nt, 0, DK, g, t4);
+        tile_mma3(gq, qn, kPrS, kn, 1, kPrS, mt, nt, 0, DK, g, t4);
+      }
+#pragma unroll
+      for (int r = 0; r < 4; r++) {
+        const uint32_t t = 16 * mt + g + (r >= 2 ? 8 : 0), s2 = 8 * nt + 2 * t4 + (r & 1);
+        const float e = s2 <= t ? __expf(lam[t] - lam[s2]) : 0.f;
+        X[t * kPrT + s2] = s2 < t ? beta[t] * e * gk[r] : 0.f;
+        Mq[t * kPrT + s2] = s2 <= t ? e * gq[r] : 0.f;
       }
     }
-    const float r = s2 <= t ? __expf(lam[t] - lam[s2]) : 0.f;
-    X[e] = s2 < t ? beta[t] * r * gk : 0.f;
-    Mq[e] = s2 <= t ? r * gq : 0.f;
   }
-  __syncthreads();
-  // 3. (I + L)^-1 by forward substitution, row by row (unit lower triangular), in place:
-  //    X[t][s] = -sum_{r=s}^{t-1} L[t][r] X[r][s]. Row t's L entries are read before
-  //    the row is overwritten (registers), earlier rows already hold X.
-  for (uint32_t t = 1; t < kDnC; t++) {
-    float xv = 0.f;
-    if (tid < t) {
-      for (uint32_t r = tid; r < t; r++) {
-        const float lr = X[t * kDnC + r];
-        const float xr = r == tid ? 1.f : X[r * kDnC + tid];
-        xv = fmaf(lr, xr, xv);
-      }
-    }
-    __syncthreads();
-    if (tid < t) X[t * kDnC + tid] = -xv;
-    __syncthreads();
-  }
-  // T = X diag(beta) (X has an implicit unit diagonal).
-  // 4. W = T Gamma K, U = T V (row t: sum over s <= t).
-  for (uint32_t e = tid; e < kDnC * DK; e += blockDim.x) {
-    const uint32_t t = e / DK, i = e % DK;
-    float w = 0.f, u = 0.f;
-    for (uint32_t s2 = 0; s2 <= t; s2++) {
-      const float tt = (s2 == t ? 1.f : X[t * kDnC + s2]) * beta[s2];
-      w = fmaf(tt * __expf(lam[s2]), kn[s2 * DK + i], w);
-      u = fmaf(tt, vv[s2 * DV + i], u);
-    }
-    W[e] = w;
-    U[e] = u;
-  }
-  __syncthreads();
-  // 5. P = Gamma Q - M W, R = M U, Kd = (gamma_C / gamma_s) k_s; write the chunk record.
-  float* rec = chunks + ((uint64_t)h * gridDim.x + c) * kDnChunkFloats;
-  float* P = rec;
-  float* R = P + kDnC * DK;
-  float* Wg = R + kDnC * DV;
-  float* Ug = Wg + kDnC * DK;
-  float* Kd = Ug + kDnC * DV;
+  // Kd = (gamma_C / gamma_t) k_t, then k becomes Gamma K in place.
   const float lam_c = lam[kDnC - 1];
   for (uint32_t e = tid; e < kDnC * DK; e += blockDim.x) {
     const uint32_t t = e / DK, i = e % DK;
-    float pw = 0.f, ru = 0.f;
-    for (uint32_t s2 = 0; s2 <= t; s2++) {
-      const float mm = Mq[t * kDnC + s2];
-      pw = fmaf(mm, W[s2 * DK + i], pw);
-      ru = fmaf(mm, U[s2 * DV + i], ru);
+    const float kv = kn[t * kPrS + i];
+    Kd[e] = __expf(lam_c - lam[t]) * kv;
+  }
+  __syncthreads();
+  for (uint32_t e = tid; e < kDnC * DK; e += blockDim.x) {
+    const uint32_t t = e / DK, i = e % DK;
+    kn[t * kPrS + i] *= elam[t];
+  }
+  // 3. X = (I + L)^-1, blocked by 16. Diagonal blocks: warps 0 and 1, half-warp per
+  //    block, lane c owns column c (forward substitution in registers).
+  if (warp < 2) {
+    const uint32_t bb = warp * 2 + (lane >> 4), cc = lane & 15, o = 16 * bb;
+    float x[16];
+#pragma unroll
+    for (uint32_t r = 0; r < 16; r++) {
+      float acc = 0.f;
+#pragma unroll
+      for (uint32_t k = 0; k < r; k++) acc = fmaf(X[(o + r) * kPrT + o + k], x[k], acc);
+      x[r] = r == cc ? 1.f : (r < cc ? 0.f : -acc);
     }
-    P[e] = fmaf(__expf(lam[t]), qn[e], -pw);
-    R[e] = ru;
-    Wg[e] = W[e];
-    Ug[e] = U[e];
-    Kd[e] = __expf(lam_c - lam[t]) * kn[e];
+    __syncwarp();
+#pragma unroll
+    for (uint32_t r = 0; r < 16; r++) X[(o + r) * kPrT + o + cc] = x[r];
+  }
+  __syncthreads();
+  //    Off-diagonal blocks, block row i = 1..3: X_ij = -X_ii sum_{k=j}^{i-1} L_ik X_kj
+  //    for all j < i at once (L_ij is read before X_ij replaces it). Thread (r, cc).
+  {
+    const uint32_t r = tid >> 4, cc = tid & 15;
+    float* tmp = W;  // scratch [3][16][16]
+    for (uint32_t i = 1; i < 4; i++) {
+      for (uint32_t j = 0; j < i; j++) {
+        float acc = 0.f;
+        for (uint32_t k = j; k < i; k++)
+#pragma unroll
+          for (uint32_t q = 0; q < 16; q++)
+            acc = fmaf(X[(16 * i + r) * kPrT + 16 * k + q], X[(16 * k + q) * kPrT + 16 * j + cc], acc);
+        tmp[(j * 16 + r) * 16 + cc] = acc;
+      }
+      __syncthreads();
+      for (uint32_t j = 0; j < i; j++) {
+        float acc = 0.f;
+#pragma unroll
+        for (uint32_t q = 0; q < 16; q++) acc = fmaf(X[(16 * i + r) * kPrT + 16 * i + q], tmp[(j * 16 + q) * 16 + cc], acc);
+        X[(16 * i + r) * kPrT + 16 * j + cc] = -acc;
+      }
+      __syncthreads();
+    }
+  }
+  //    T = X diag(beta) (X has a unit diagonal; the upper part is zero).
+  for (uint32_t e = tid; e < kDnC * kDnC; e += blockDim.x) {
+    const uint32_t t = e / kDnC, s2 = e % kDnC;
+    X[t * kPrT + s2] = s2 <= t ? X[t * kPrT + s2] * beta[s2] : 0.f;
+  }
+  __syncthreads();
+  // 4. W = T Gamma K, U = T V (64 x 128, K = 64, T lower triangular): warp w takes row
+  //    tile w / 2 and column tiles 8 (w % 2) .. + 7.
+  {
+    const uint32_t mt = warp >> 1, kend = 16 * (mt + 1);
+#pragma unroll 1
+    for (uint32_t q = 0; q < 8; q++) {
+      const uint32_t nt = (warp & 1) * 8 + q;
+      float w[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
+      tile_mma3(w, X, kPrT, kn, kPrS, 1, mt, nt, 0, kend, g, t4);
+      tile_mma3(u, X, kPrT, vv, kPrS, 1, mt, nt, 0, kend, g, t4);
+#pragma unroll
+      for (int r = 0; r < 4; r++) {
+        const uint32_t t = 16 * mt + g + (r >= 2 ? 8 : 0), i = 8 * nt + 2 * t4 + (r & 1);
+        W[t * kPrS + i] = w[r];
+        U[t * kPrS + i] = u[r];
+        Wg[t * DK + i] = w[r];
+        Ug[t * DV + i] = u[r];
+      }
+    }
+  }
+  __syncthreads();
+  // 5. P = Gamma Q - M W, R = M U (M lower triangular with diagonal).
+  {
+    const uint32_t mt = warp >> 1, kend = 16 * (mt + 1);
+#pragma unroll 1
+    for (uint32_t q = 0; q < 8; q++) {
+      const uint32_t nt = (warp & 1) * 8 + q;
+      float pw[4] = {0.f, 0.f, 0.f, 0.f}, ru[4] = {0.f, 0.f, 0.f, 0.f};
+      tile_mma3(pw, Mq, kPrT, W, kPrS, 1, mt, nt, 0, kend, g, t4);
+      tile_mma3(ru, Mq, kPrT, U, kPrS, 1, mt, nt, 0, kend, g, t4);
+#pragma unroll
+      for (int r = 0; r < 4; r++) {
+        const uint32_t t = 16 * mt + g + (r >= 2 ? 8 : 0), i = 8 * nt + 2 * t4 + (r & 1);
+        Pg[t * DK + i] = fmaf(elam[t], qn[t * kPrS + i], -pw[r]);
+        Rg[t * DV + i] = ru[r];
+      }
+    }
   }
   if (tid == 0) rec[5 * kDnC * DK] = __expf(lam_c);
 }
 
 // Carries one head's state slice (all 128 rows, kDnCols columns) through the chunks of
-// the step, writing the pre-norm outputs O = P S0 + R of its columns.
+// the step on the tensor cores, writing the pre-norm outputs O = P S0 + R of its
+// columns. 8 warps; per chunk: O and W S (64 x 32, K = 128: two 16 x 8 tiles per warp),
+// then S = gamma_C S + Kd^T D (128 x 32, K = 64: four tiles per warp). Shared-memory
+// row strides avoid bank conflicts of the fragment loads: 132 floats (= 4 mod 32) for
+// row-major A reads, 136 (= 8 mod 32) for the transposed Kd reads, 40 for S and D.
+constexpr uint32_t kScA = 132, kScKd = 136, kScS = 40;
+
 __global__ void __launch_bounds__(256) dn_scan_kernel(uint32_t m, uint32_t n_chunks, snl_lin_p p,
                                                       const float* __restrict__ chunks, float* __restrict__ state,
                                                       float* __restrict__ out) {
   extern __shared__ __align__(16) float ssm[];
-  float* S = ssm;                      // [128][kDnCols]
-  float* A = S + DK * kDnCols;         // [C][128]: P, then Kd
-  float* B = A + kDnC * DK;            // [C][128]: W
-  float* D = B + kDnC * DK;            // [C][kDnCols]
+  float* S = ssm;                       // [128][kScS]
+  float* A = S + DK * kScS;             // [C][kScA] P, then [C][kScKd] Kd
+  float* B = A + kDnC * kScKd;          // [C][kScA] W
+  float* D = B + kDnC * kScA;           // [C][kScS]
   const uint32_t slice = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  const uint32_t warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
   const uint32_t j0 = slice * kDnCols;
   float* Sg = state + (uint64_t)h * DK * DV;
-  for (uint32_t e = tid; e < DK * kDnCols; e += blockDim.x) S[e] = Sg[(e / kDnCols) * DV + j0 + e % kDnCols];
+  for (uint32_t e = tid; e < DK * kDnCols; e += blockDim.x) S[(e / kDnCols) * kScS + e % kDnCols] = Sg[(e / kDnCols) * DV + j0 + e % kDnCols];
+  // This warp's tiles: rows 16 * mt of the 64-token products, columns 8 * nt0 and 8 * nt0 + 8.
+  const uint32_t mt = warp >> 1, nt0 = (warp & 1) * 2;
   for (uint32_t c = 0; c < n_chunks; c++) {
     const float* rec = chunks + ((uint64_t)h * n_chunks + c) * kDnChunkFloats;
     const float* P = rec;
@@ -594,38 +735,80 @@ __global__ void __launch_bounds__(256) dn_scan_kernel(uint32_t m, uint32_t n_chu
     const uint32_t t0 = c * kDnC, ce = min(kDnC, m - t0);
     __syncthreads();
     for (uint32_t e = tid; e < kDnC * DK / 4; e += blockDim.x) {
-      reinterpret_cast<float4*>(A)[e] = reinterpret_cast<const float4*>(P)[e];
-      reinterpret_cast<float4*>(B)[e] = reinterpret_cast<const float4*>(Wg)[e];
+      const uint32_t r = e / (DK / 4), q = e % (DK / 4);
+      *reinterpret_cast<float4*>(A + r * kScA + 4 * q) = reinterpret_cast<const float4*>(P)[e];
+      *reinterpret_cast<float4*>(B + r * kScA + 4 * q) = reinterpret_cast<const float4*>(Wg)[e];
     }
     __syncthreads();
-    // O = P S + R and D = U - W S for the slice: thread -> (token t, column j), 8 each.
-    for (uint32_t e = tid; e < kDnC * kDnCols; e += blockDim.x) {
-      const uint32_t t = e / kDnCols, j = e % kDnCols;
-      float o = 0.f, w = 0.f;
-#pragma unroll 8
-      for (uint32_t i = 0; i < DK; i++) {
-        const float sv = S[i * kDnCols + j];
-        o = fmaf(A[t * DK + i], sv, o);
-        w = fmaf(B[t * DK + i], sv, w);
+    // O = P S, WS = W S for the warp's two tiles.
+    float o[2][4] = {}, ws[2][4] = {};
+#pragma unroll 4
+    for (uint32_t ks = 0; ks < DK / 8; ks++) {
+      const uint32_t kc = ks * 8 + t4;
+      const float* ar = A + (16 * mt + g) * kScA + kc;
+      const float* wr = B + (16 * mt + g) * kScA + kc;
+      const float pa[4] = {ar[0], ar[8 * kScA], ar[4], ar[8 * kScA + 4]};
+      const float wa[4] = {wr[0], wr[8 * kScA], wr[4], wr[8 * kScA + 4]};
+#pragma unroll
+      for (int q = 0; q < 2; q++) {
+        const uint32_t n = 8 * (nt0 + q) + g;
+        const float sb[2] = {S[kc * kScS + n], S[(kc + 4) * kScS + n]};
+        mma3_tf32(o[q], pa, sb);
+        mma3_tf32(ws[q], wa, sb);
       }
-      D[e] = Ug[t * DV + j0 + j] - w;
-      if (t < ce) out[(uint64_t)(t0 + t) * p.n_v * DV + h * DV + j0 + j] = o + R[t * DV + j0 + j];
+    }
+    // Outputs (+ R) and D = U - W S (c0/c1: row g, columns 2 t4, 2 t4 + 1; c2/c3: row g + 8).
+#pragma unroll
+    for (int q = 0; q < 2; q++) {
+#pragma unroll
+      for (int r = 0; r < 4; r++) {
+        const uint32_t t = 16 * mt + g + (r >= 2 ? 8 : 0), j = 8 * (nt0 + q) + 2 * t4 + (r & 1);
+        D[t * kScS + j] = Ug[t * DV + j0 + j] - ws[q][r];
+        if (t < ce) out[(uint64_t)(t0 + t) * p.n_v * DV + h * DV + j0 + j] = o[q][r] + R[t * DV + j0 + j];
+      }
     }
     __syncthreads();
-    for (uint32_t e = tid; e < kDnC * DK / 4; e += blockDim.x)
-      reinterpret_cast<float4*>(A)[e] = reinterpret_cast<const float4*>(Kd)[e];
+    for (uint32_t e = tid; e < kDnC * DK / 4; e += blockDim.x) {
+      const uint32_t r = e / (DK / 4), q = e % (DK / 4);
+      *reinterpret_cast<float4*>(A + r * kScKd + 4 * q) = reinterpret_cast<const float4*>(Kd)[e];
+    }
     __syncthreads();
-    // S = gamma_C S + Kd^T D.
-    for (uint32_t e = tid; e < DK * kDnCols; e += blockDim.x) {
-      const uint32_t i = e / kDnCols, j = e % kDnCols;
-      float acc = 0.f;
-#pragma unroll 8
-      for (uint32_t t = 0; t < kDnC; t++) acc = fmaf(A[t * DK + i], D[t * kDnCols + j], acc);
-      S[e] = fmaf(gC, S[e], acc);
+    // S = gamma_C S + Kd^T D: the warp's four tiles are state rows 16 * (warp % 8) and
+    // columns 8 * nt, nt = 0..3. A(i, t) = Kd[t][i].
+    {
+      const uint32_t it = warp;  // 8 row tiles of 16
+      float acc[4][4];
+#pragma unroll
+      for (int q = 0; q < 4; q++)
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+          const uint32_t i = 16 * it + g + (r >= 2 ? 8 : 0), j = 8 * q + 2 * t4 + (r & 1);
+          acc[q][r] = gC * S[i * kScS + j];
+        }
+#pragma unroll 2
+      for (uint32_t ks = 0; ks < kDnC / 8; ks++) {
+        const uint32_t kt = ks * 8 + t4;
+        const float* kr = A + kt * kScKd + 16 * it + g;
+        const float ka[4] = {kr[0], kr[8], kr[4 * kScKd], kr[4 * kScKd + 8]};
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          const uint32_t n = 8 * q + g;
+          const float db[2] = {D[kt * kScS + n], D[(kt + 4) * kScS + n]};
+          mma3_tf32(acc[q], ka, db);
+        }
+      }
+      __syncwarp();
+#pragma unroll
+      for (int q = 0; q < 4; q++)
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+          const uint32_t i = 16 * it + g + (r >= 2 ? 8 : 0), j = 8 * q + 2 * t4 + (r & 1);
+          S[i * kScS + j] = acc[q][r];
+        }
     }
   }
   __syncthreads();
-  for (uint32_t e = tid; e < DK * kDnCols; e += blockDim.x) Sg[(e / kDnCols) * DV + j0 + e % kDnCols] = S[e];
+  for (uint32_t e = tid; e < DK * kDnCols; e += blockDim.x) Sg[(e / kDnCols) * DV + j0 + e % kDnCols] = S[(e / kDnCols) * kScS + e % kDnCols];
 }
 
 // Gated RMSNorm of the delta outputs (linear.wgsl's tail of `delta`), in place.
@@ -652,8 +835,13 @@ static int check_lin(const snl_lin_p& p) {
 int launch_conv(StepRef st, const snl_lin_p& p, const float* proj, float* conv_out, float* conv_state, const float* lw,
                 float* conv_ckpt, cudaStream_t s) {
   if (int rc = check_lin(p)) return rc;
-  conv_kernel<<<(p.conv_dim + 255) / 256, 256, 0, s>>>(st, p, proj, conv_out, conv_state, lw, conv_ckpt);
+  const uint32_t m = st.val.m;  // the host copy sizes the grid
+  if (m == 0) return SNL_OK;
+  const dim3 grid((p.conv_dim + 255) / 256, (m + kConvTok - 1) / kConvTok);
+  conv_kernel<<<grid, 256, 0, s>>>(st, p, proj, conv_out, conv_state, lw);
   SNL_LAUNCH_CHECK("conv");
+  conv_state_kernel<<<(p.conv_dim + 255) / 256, 256, 0, s>>>(st, p, proj, conv_state, conv_ckpt);
+  SNL_LAUNCH_CHECK("conv_state");
   return SNL_OK;
 }
 
@@ -665,7 +853,7 @@ int launch_delta(StepRef st, const snl_lin_p& p, const float* proj, const float*
   return SNL_OK;
 }
 
-// Chunked prefill form: conv (channel-parallel) into conv_out, then the three chunked
+// Chunked prefill form: conv (token-parallel) into conv_out, then the three chunked
 // delta kernels. m is the host's row count; no checkpoint. scratch: the chunk records,
 // n_v * ceil(m / 64) * (5 * 64 * 128 + 4) floats.
 int launch_conv_delta_chunked(uint32_t m, const snl_lin_p& p, const float* proj, float* conv_state, float* state,
@@ -673,11 +861,10 @@ int launch_conv_delta_chunked(uint32_t m, const snl_lin_p& p, const float* proj,
   if (int rc = check_lin(p)) return rc;
   if (m == 0) return SNL_OK;
   const snl_step_u sv{m, 0, 1, 0};
-  conv_kernel<<<(p.conv_dim + 255) / 256, 256, 0, s>>>(step_val(sv), p, proj, conv_out, conv_state, lw, nullptr);
-  SNL_LAUNCH_CHECK("conv");
+  if (int rc = launch_conv(step_val(sv), p, proj, conv_out, conv_state, lw, nullptr, s)) return rc;
   const uint32_t nch = (m + kDnC - 1) / kDnC;
-  const size_t prep_smem = (3 * kDnC * DK + 2 * kDnC * kDnC + 2 * kDnC * DK) * sizeof(float);
-  const size_t scan_smem = (DK * kDnCols + 2 * kDnC * DK + kDnC * kDnCols) * sizeof(float);
+  const size_t prep_smem = kPrepSmemFloats * sizeof(float);
+  const size_t scan_smem = (DK * kScS + kDnC * kScKd + kDnC * kScA + kDnC * kScS) * sizeof(float);
   static bool attr[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);

@@ -411,7 +411,7 @@ def lin_case(rng, m, n_k=16, n_v=32):
     return lpp, proj, lw, cd
 
 
-@pytest.mark.parametrize("m,ckpt", [(1, 0), (2, 1), (37, 0)])
+@pytest.mark.parametrize("m,ckpt", [(1, 0), (2, 1), (11, 7), (37, 0), (37, 2)])
 def test_conv(T, lib, orc, m, ckpt):
     rng = np.random.default_rng(m)
     lpp, proj, lw, cd = lin_case(rng, m)
