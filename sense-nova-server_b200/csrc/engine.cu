@@ -279,6 +279,27 @@ int mat(snl_engine* e, StepRef st, const QT& w, const float* x, size_t x_stride,
     if (_rc) return _rc;       \
   } while (0)
 
+// One projection of an eager step (the MTP layer and head) with 1-4 token rows: x packed
+// into fp16 hi/lo planes and the tile GEMV, when the matrix has its tile copy; else mat().
+int mat_tile(snl_engine* e, StepRef st, const QT& w, const float* x, size_t x_stride, float* y, size_t y_stride,
+             uint32_t rows_m) {
+  if (!w.tiles || !e->use_tc || rows_m == 0 || rows_m > 4) return mat(e, st, w, x, x_stride, y, y_stride, rows_m);
+  SNL_TRY(timed(e, "XPack", 6.0 * rows_m * w.cols, [&] {
+    return launch_xpack(x, rows_m, (uint32_t)w.cols, (uint32_t)x_stride, e->xpl, e->pstride, e->stream);
+  }));
+  GemvArgs a{};
+  a.n = (uint32_t)w.rows;
+  a.k = (uint32_t)w.cols;
+  a.xplanes = e->xpl;
+  a.plane_stride = e->pstride;
+  a.mode = 0;
+  a.y = y;
+  a.y_stride = (uint32_t)y_stride;
+  const double bytes = qbytes(w) + 4.0 * rows_m * (w.cols + w.rows);
+  return timed(e, "mat n=" + std::to_string(w.rows), bytes,
+               [&] { return launch_gemv_tile(w.dtype, a, rows_m, w.tiles, w.tscales, w.tscale_f16, e->stream); });
+}
+
 int push_norm(snl_engine* e, StepRef st, uint32_t m, const float* router, const float* norm_w, XOut xo = XOut()) {
   const double h = e->cfg.hidden;
   if (router && e->rpart_ready) {
@@ -1344,25 +1365,25 @@ extern "C" int snl_engine_mtp(snl_engine* e, size_t r0, const uint32_t* tokens, 
     snl_layer_p ph = p0;
     ph.x_stride = (uint32_t)h;
     SNL_TRY(launch_branch_norm(st, ph, e->hid + (r0 + c0) * h, e->coef, find_f(e, "mtp.norm_h"), e->hn, m, e->stream));
-    SNL_TRY(mat(e, st, *find_q(e, "mtp.fc_e"), e->xn, h, e->mx, 2 * h, m));
-    SNL_TRY(mat(e, st, *find_q(e, "mtp.fc_h"), e->hn, h, e->branch, h, m));
+    SNL_TRY(mat_tile(e, st, *find_q(e, "mtp.fc_e"), e->xn, h, e->mx, 2 * h, m));
+    SNL_TRY(mat_tile(e, st, *find_q(e, "mtp.fc_h"), e->hn, h, e->branch, h, m));
     SNL_TRY(launch_merge(st, p0, e->mx, e->coef, e->branch, m, e->stream));
     SNL_TRY(launch_branch_norm(st, p0, e->mx, e->coef, find_f(e, "mtp.in_ln"), e->xn, m, e->stream));
-    SNL_TRY(mat(e, st, *find_q(e, "mtp.qkv"), e->xn, h, e->proj, ap.proj_stride, m));
+    SNL_TRY(mat_tile(e, st, *find_q(e, "mtp.qkv"), e->xn, h, e->proj, ap.proj_stride, m));
     SNL_TRY(launch_attn_prep(st, ap, e->proj, e->qbuf, e->m_kc, e->m_vc, find_f(e, "mtp.qk_norm"), e->rpos, m, e->stream));
     SNL_TRY(launch_attend(st, ap, e->proj, e->qbuf, e->m_kc, e->m_vc, e->attn_out, e->partial, m, sh.parts, e->stream));
     if (sh.parts > 1) SNL_TRY(launch_attn_combine(st, ap, e->proj, e->partial, e->attn_out, m, e->stream, 1));
-    SNL_TRY(mat(e, st, *find_q(e, "mtp.o_proj"), e->attn_out, snl_synth::q_dim(c), e->branch, h, m));
+    SNL_TRY(mat_tile(e, st, *find_q(e, "mtp.o_proj"), e->attn_out, snl_synth::q_dim(c), e->branch, h, m));
     SNL_TRY(launch_merge(st, p0, e->mx, e->coef, e->branch, m, e->stream));
     SNL_TRY(launch_branch_norm(st, p0, e->mx, e->coef, find_f(e, "mtp.post_ln"), e->xn, m, e->stream));
-    SNL_TRY(mat(e, st, *find_q(e, "mtp.gate_up"), e->xn, h, e->proj, 2 * (size_t)c.intermediate, m));
+    SNL_TRY(mat_tile(e, st, *find_q(e, "mtp.gate_up"), e->xn, h, e->proj, 2 * (size_t)c.intermediate, m));
     SNL_TRY(launch_swiglu(st, p0, e->proj, e->act, m, e->stream));
-    SNL_TRY(mat(e, st, *find_q(e, "mtp.down"), e->act, c.intermediate, e->branch, h, m));
+    SNL_TRY(mat_tile(e, st, *find_q(e, "mtp.down"), e->act, c.intermediate, e->branch, h, m));
     SNL_TRY(launch_merge(st, p0, e->mx, e->coef, e->branch, m, e->stream));
     if (last && draft) {
       snl_layer_p pl = layer_p(e, 0, true);
       SNL_TRY(launch_branch_norm(st, pl, e->mx, e->coef, find_f(e, "mtp.norm"), e->xn, 1, e->stream));
-      SNL_TRY(mat(e, st, *find_q(e, "lm_head"), e->xn, h, e->m_logits, c.vocab, 1, 1));
+      SNL_TRY(mat_tile(e, st, *find_q(e, "lm_head"), e->xn, h, e->m_logits, c.vocab, 1));
       SNL_TRY(launch_argmax_with(e->m_logits, 1, c.vocab, e->amax, e->amax_part, e->stream));
     }
     SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));
