@@ -58,6 +58,8 @@ def parse_args():
                          "gemm: one prefill-chunk GEMM (512 tokens x 12288 x 4096) on the tcgen05 kernel")
     ap.add_argument("--iters", type=int, default=40)
     ap.add_argument("--gemv-kernel", choices=["tile", "tc", "simt"], default="tile")
+    ap.add_argument("--gemm-dequant", action="store_true",
+                    help="gemm workload: dequantize in the kernel instead of the engine's weight planes")
     return ap.parse_args()
 
 
@@ -645,10 +647,23 @@ def run_gemm_only(args):
     x = torch.randn(m, k, device="cuda")
     y = torch.empty(m, n, device="cuda")
     st, p = ffi.StepU(m, 0, 1, 0), ffi.MatP(n, k, 0, k, 0, n, 0, 0)
+    # The engine's form: the weights' fp16 hi/lo planes made once, loaded by TMA
+    # (--gemm-dequant: the kernel dequantizes the file layout itself).
+    planes = []
+    if not args.gemm_dequant:
+        for i in range(copies):
+            planes.append(torch.empty(2 * n * k, dtype=torch.float16, device="cuda"))
+            ffi.check(lib.snl_weight_planes(dt, n, k, C.c_void_p(ws[i].data_ptr()), C.c_void_p(ss[i].data_ptr()),
+                                            C.c_void_p(planes[i].data_ptr()), None))
 
     def run(i):
-        ffi.check(lib.snl_mat(dt, C.byref(st), C.byref(p), C.c_void_p(x.data_ptr()), C.c_void_p(ws[i].data_ptr()),
-                              C.c_void_p(ss[i].data_ptr()), C.c_void_p(y.data_ptr()), None))
+        if planes:
+            ffi.check(lib.snl_mat_wplanes(dt, C.byref(st), C.byref(p), C.c_void_p(x.data_ptr()),
+                                          C.c_void_p(ws[i].data_ptr()), C.c_void_p(ss[i].data_ptr()),
+                                          C.c_void_p(planes[i].data_ptr()), C.c_void_p(y.data_ptr()), None))
+        else:
+            ffi.check(lib.snl_mat(dt, C.byref(st), C.byref(p), C.c_void_p(x.data_ptr()), C.c_void_p(ws[i].data_ptr()),
+                                  C.c_void_p(ss[i].data_ptr()), C.c_void_p(y.data_ptr()), None))
 
     for i in range(2 * copies):
         run(i % copies)
@@ -667,7 +682,9 @@ def run_gemm_only(args):
     except Exception:
         peak, kind = 1590.0, "fallback"
     wbytes = qb + n * k // 32 * 4
-    print(json.dumps({"workload": "prefill GEMM", "shape": [m, n, k], "quant": args.quant, "us_per_launch": us,
+    print(json.dumps({"workload": "prefill GEMM", "shape": [m, n, k], "quant": args.quant,
+                      "a_operand": "dequantized in the kernel" if args.gemm_dequant else "weight planes by TMA",
+                      "us_per_launch": us,
                       "tflops": flops / us / 1e6, "peak_tflops": peak, "peak_kind": kind,
                       "frac": flops / us / 1e6 / peak, "tensor_pipe_flops_per_launch": 3 * flops,
                       "weight_bytes": wbytes, "weight_gbs": wbytes / us / 1e3, "copies_rotated": copies}), flush=True)

@@ -133,6 +133,14 @@ int snl_config_validate(const snl_model_config* cfg);
  * [n, k/8] + f32 scales [n, k/32]. */
 int snl_mat(int dtype, const snl_step_u* step, const snl_mat_p* p, const float* x, const void* wq,
             const float* ws, float* y, void* stream);
+/* Weight planes of a Q8_0/Q4_0 matrix for the prefill GEMM: planes [2][n][k] fp16 (4 n k
+ * bytes), the hi and lo parts of each dequantized value (x 256). snl_mat_wplanes is
+ * snl_mat with them: steps of >= 8 rows then load the weights by TMA instead of
+ * dequantizing them; the results are the same. The engine keeps planes for every
+ * matrix when device memory allows. */
+int snl_weight_planes(int dtype, uint32_t n, uint32_t k, const void* wq, const float* ws, void* planes, void* stream);
+int snl_mat_wplanes(int dtype, const snl_step_u* step, const snl_mat_p* p, const float* x, const void* wq,
+                    const float* ws, const void* planes, float* y, void* stream);
 
 /* The same product on the tensor cores for 1..4 token rows, with x given as "x planes":
  * [2*rows_m][k] fp16, plane 2t = hi and 2t+1 = lo of x[t]/16 (written by snl_xpack or by

@@ -131,12 +131,18 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   } while (0)
 
 // Launch helpers implemented per kernel family (internal, not part of the C ABI).
+// wplanes (optional): the matrix's weight planes (launch_weight_planes) for the
+// prefill GEMM.
 int launch_mat(int dtype, StepRef st, const snl_mat_p& p, const float* x, const void* wq, const void* ws,
-               int scale_f16, float* y, cudaStream_t s, uint32_t rows_m_host);
+               int scale_f16, float* y, cudaStream_t s, uint32_t rows_m_host, const __half* wplanes = nullptr);
 // Prefill GEMM on the tcgen05 tensor cores (gemm_tc.cu), f32 scales, m token rows.
 bool gemm_tc_enabled();
 int launch_gemm_tc(int dtype, const snl_mat_p& p, uint32_t m, const float* x, const void* wq, const float* ws, float* y,
-                   cudaStream_t s);
+                   cudaStream_t s, const __half* wplanes = nullptr);
+// Weight planes [2][n][k] fp16 (hi, lo of code * scale * 256) of a Q8_0/Q4_0 matrix: the
+// prefill GEMM then loads its A operand by TMA instead of dequantizing it.
+int launch_weight_planes(int dtype, uint32_t n, uint32_t k, const void* q, const float* s, __half* planes,
+                         cudaStream_t st);
 int launch_branch_norm(StepRef st, const snl_layer_p& p, const float* x, const float* coef, const float* w,
                        float* out, uint32_t n_groups, cudaStream_t s, XOut xo = XOut());
 // branch_norm mode 1 that first finishes the mHC router from nparts partial sums per

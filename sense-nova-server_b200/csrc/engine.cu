@@ -61,6 +61,7 @@ struct QT {
   void* tscales = nullptr;
   int tscale_f16 = 0;  // the tile scales are fp16 (every block scale is an fp16 number), else f32
   uint32_t pair_half = 0;  // tiles pair gate row i with up row i (a layer's gate_up)
+  __half* wplanes = nullptr;  // fp16 hi/lo weight planes for the prefill GEMM (optional)
 };
 struct FT {
   float* p = nullptr;
@@ -270,7 +271,8 @@ int mat(snl_engine* e, StepRef st, const QT& w, const float* x, size_t x_stride,
   p.m_one = m_one;
   const double bytes = qbytes(w) + 4.0 * rows_m * (w.cols + w.rows);
   const std::string label = "mat n=" + std::to_string(w.rows) + (m_one ? " (head)" : "");
-  return timed(e, label, bytes, [&] { return launch_mat(w.dtype, st, p, x, w.q, w.s, w.s_f16, y, e->stream, rows_m); });
+  return timed(e, label, bytes,
+               [&] { return launch_mat(w.dtype, st, p, x, w.q, w.s, w.s_f16, y, e->stream, rows_m, w.wplanes); });
 }
 
 #define SNL_TRY(expr)          \
@@ -1266,6 +1268,28 @@ extern "C" int snl_engine_finalize(snl_engine* e) {
     cm.sites = e->tp_sites;
     cm.err = err;
     e->head_out = cm.logits[e->tp.rank];
+  }
+  // Weight planes for the prefill GEMM (4 bytes per weight: fp16 hi and lo of each value),
+  // made last and only when they fit with kPlanesHeadroom to spare; otherwise the GEMM
+  // dequantizes the file layout itself (the same values). SNL_NO_WPLANES skips them.
+  if (!getenv("SNL_NO_WPLANES") && gemm_tc_enabled()) {
+    constexpr size_t kPlanesHeadroom = (size_t)8 << 30;
+    size_t need = 0;
+    for (auto& kv : e->qw)
+      if (kv.first != "embed" && !kv.second.s_f16) need += kv.second.rows * kv.second.cols * 2 * sizeof(__half);
+    size_t fr = 0, tot = 0;
+    SNL_CUDA_TRY(cudaMemGetInfo(&fr, &tot));
+    if (fr > need + kPlanesHeadroom) {
+      for (auto& kv : e->qw) {
+        if (kv.first == "embed" || kv.second.s_f16) continue;
+        snl::QT& t = kv.second;
+        __half* pl = nullptr;
+        SNL_TRY(dalloc(e, &pl, 2 * t.rows * t.cols));
+        SNL_TRY(launch_weight_planes(t.dtype, (uint32_t)t.rows, (uint32_t)t.cols, t.q, (const float*)t.s, pl,
+                                     e->stream));
+        t.wplanes = pl;
+      }
+    }
   }
   SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));
   e->finalized = true;

@@ -543,7 +543,7 @@ int launch_mat_t(const snl_mat_p& p, uint32_t rows_m, const float* x, const void
 }  // namespace
 
 int launch_mat(int dtype, StepRef st, const snl_mat_p& p, const float* x, const void* wq, const void* ws,
-               int scale_f16, float* y, cudaStream_t s, uint32_t rows_m) {
+               int scale_f16, float* y, cudaStream_t s, uint32_t rows_m, const __half* wplanes) {
   (void)st;
   if (dtype != SNL_Q8_0 && dtype != SNL_Q4_0) return fail(SNL_E_INVALID, "mat: dtype must be Q8_0 or Q4_0");
   if (p.k == 0 || p.k % 32) return fail(SNL_E_INVALID, "mat: k must be a positive multiple of 32");
@@ -552,7 +552,7 @@ int launch_mat(int dtype, StepRef st, const snl_mat_p& p, const float* x, const 
   if (rows_m == 0 || p.n == 0) return SNL_OK;
   // Prefill-sized steps run on the tcgen05 tensor cores.
   if (rows_m >= 8 && !scale_f16 && gemm_tc_enabled())
-    return launch_gemm_tc(dtype, p, rows_m, x, wq, static_cast<const float*>(ws), y, s);
+    return launch_gemm_tc(dtype, p, rows_m, x, wq, static_cast<const float*>(ws), y, s, wplanes);
   if (dtype == SNL_Q8_0) {
     return scale_f16 ? launch_mat_t<SNL_Q8_0, __half>(p, rows_m, x, wq, (const __half*)ws, y, s)
                      : launch_mat_t<SNL_Q8_0, float>(p, rows_m, x, wq, (const float*)ws, y, s);
@@ -579,4 +579,16 @@ extern "C" int snl_mat(int dtype, const snl_step_u* step, const snl_mat_p* p, co
   if (!step || !p || !x || !wq || !ws || !y) return snl::fail(SNL_E_INVALID, "snl_mat: null argument");
   const uint32_t rows_m = p->m_one > 0 ? p->m_one : step->m;
   return snl::launch_mat(dtype, snl::step_val(*step), *p, x, wq, ws, 0, y, (cudaStream_t)stream, rows_m);
+}
+extern "C" int snl_weight_planes(int dtype, uint32_t n, uint32_t k, const void* wq, const float* ws, void* planes,
+                                 void* stream) {
+  if (!wq || !ws || !planes) return snl::fail(SNL_E_INVALID, "snl_weight_planes: null argument");
+  return snl::launch_weight_planes(dtype, n, k, wq, ws, static_cast<__half*>(planes), (cudaStream_t)stream);
+}
+extern "C" int snl_mat_wplanes(int dtype, const snl_step_u* step, const snl_mat_p* p, const float* x, const void* wq,
+                               const float* ws, const void* planes, float* y, void* stream) {
+  if (!step || !p || !x || !wq || !ws || !planes || !y) return snl::fail(SNL_E_INVALID, "snl_mat_wplanes: null argument");
+  const uint32_t rows_m = p->m_one > 0 ? p->m_one : step->m;
+  return snl::launch_mat(dtype, snl::step_val(*step), *p, x, wq, ws, 0, y, (cudaStream_t)stream, rows_m,
+                         static_cast<const __half*>(planes));
 }

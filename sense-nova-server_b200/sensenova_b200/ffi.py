@@ -97,6 +97,8 @@ SIGNATURES = {
     "snl_mat": (i32, [i32, P(StepU), P(MatP), vp, vp, vp, vp, vp]),
     "snl_xpack": (i32, [vp, u32, u32, u32, vp, vp]),
     "snl_mat_xpack": (i32, [i32, P(MatP), u32, vp, vp, vp, vp, vp]),
+    "snl_weight_planes": (i32, [i32, u32, u32, vp, vp, vp, vp]),
+    "snl_mat_wplanes": (i32, [i32, P(StepU), P(MatP), vp, vp, vp, vp, vp, vp]),
     "snl_tile_sizes": (i32, [i32, u32, u32, P(sz), P(sz)]),
     "snl_tile_repack": (i32, [i32, u32, u32, vp, vp, vp, vp, P(i32), vp]),
     "snl_mat_tiles": (i32, [i32, P(MatP), u32, vp, vp, vp, i32, vp, vp]),

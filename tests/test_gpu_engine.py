@@ -97,6 +97,23 @@ def test_forward_greedy_matches_logits(torch_cuda, orc, cfg):
     e2.close()
 
 
+def test_weight_planes_bitwise(torch_cuda, cfg, monkeypatch):
+    """Prefill rows with the engine's weight planes (default) give the same logits, bit
+    for bit, as the dequantizing GEMM (SNL_NO_WPLANES)."""
+    a = Engine.synthetic(cfg, 320, 33)
+    monkeypatch.setenv("SNL_NO_WPLANES", "1")
+    b = Engine.synthetic(cfg, 320, 33)
+    monkeypatch.delenv("SNL_NO_WPLANES")
+    prompt = [(5 + i * 53) % cfg.vocab for i in range(45)]
+    la, lb = a.forward(prompt, True), b.forward(prompt, True)
+    assert np.array_equal(la, lb)
+    t = int(np.argmax(la))
+    la, lb = a.forward([t], True), b.forward([t], True)
+    assert np.array_equal(la, lb)
+    a.close()
+    b.close()
+
+
 def test_verify_two_rows_and_rollback(torch_cuda, orc, cfg):
     e, o = pair(orc, cfg, seed=14)
     prompt = [5, 17, 99, 400, 1234, 7]

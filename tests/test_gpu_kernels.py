@@ -122,6 +122,25 @@ def test_mat_prefill_tensor_cores(T, lib, orc, dtype, n, k, m):
 
 
 @pytest.mark.parametrize("dtype", [SNL_Q8_0, SNL_Q4_0])
+@pytest.mark.parametrize("n,k,m", [(1000, 2048, 300), (4096, 4096, 512), (333, 160, 40), (18944, 256, 300)])
+def test_mat_weight_planes_bitwise(T, lib, dtype, n, k, m, orc):
+    """Prefill GEMM with precomputed weight planes (A by TMA) == the dequantizing GEMM,
+    bit for bit: the same operand values, tiles and MMA order."""
+    rng = np.random.default_rng(n + k + m)
+    q, s = orc.gen_quant(n + 3, "wp", dtype, n, k)
+    x = rng.standard_normal(m * k).astype(np.float32)
+    p, st = MatP(n, k, 0, k, 0, n, 0, 0), StepU(m, 0, 1, 0)
+    qd, sd, xd = dev(T, q), dev(T, s), dev(T, x)
+    planes = T.empty(2 * n * k, dtype=T.float16, device="cuda")
+    call(lib.snl_weight_planes(dtype, n, k, ptr(qd), ptr(sd), ptr(planes), None))
+    y0 = T.zeros(m * n, dtype=T.float32, device="cuda")
+    y1 = T.zeros(m * n, dtype=T.float32, device="cuda")
+    call(lib.snl_mat(dtype, C.byref(st), C.byref(p), ptr(xd), ptr(qd), ptr(sd), ptr(y0), None))
+    call(lib.snl_mat_wplanes(dtype, C.byref(st), C.byref(p), ptr(xd), ptr(qd), ptr(sd), ptr(planes), ptr(y1), None))
+    assert np.array_equal(host(y0), host(y1))
+
+
+@pytest.mark.parametrize("dtype", [SNL_Q8_0, SNL_Q4_0])
 def test_mat_config1_shape(T, lib, orc, dtype):
     # The benchmark GEMV: W [12288 x 4096], one token.
     y, ref = run_mat(T, lib, orc, dtype, 12288, 4096, 1, seed=5)
