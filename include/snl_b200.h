@@ -234,6 +234,29 @@ int snl_argmax(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_idx
  * any stream capture. All calls share the array: calls that overlap on the GPU (for
  * example on two streams at once) race and must be serialised by the caller. */
 int snl_argmax_noalloc(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_idx, void* stream);
+
+/* SamplingParams (sampler.rs:4-14) without the seed: the host keeps the random number
+ * generator and passes its uniform draws. */
+typedef struct snl_sample_p {
+  float temperature, top_p;
+  uint32_t top_k;
+  float min_p, presence_penalty, frequency_penalty, repetition_penalty;
+  uint32_t pad;
+} snl_sample_p;
+
+/* Sampler::sample (draft < 0) or Sampler::verify(draft) (sampler.rs:54-167) on the device,
+ * for one row of n logits (device, f32; the penalties modify it in place, as the
+ * reference modifies its slice). hist_tok / hist_cnt: device arrays of the n_hist tokens
+ * generated so far and their counts (Sampler::counts). u: two host uniform draws in
+ * [0, 1) from the caller's generator, used in the reference's order: sample uses u[0] for
+ * the draw; verify uses u[0] for the acceptance test when p(draft) > 0 and the next one
+ * for the redraw. out: device u32[3] = token, accepted (1/0), draws used (0-2).
+ * scratch: snl_sample_scratch_bytes() of device memory. Supported: temperature <= 1e-5
+ * (greedy), or top_k in 1..256 (the reference's top_k_small branch, which ranks equal
+ * logits by index); top_k 0 or > 256 returns SNL_E_UNSUPPORTED, and n <= 262144. */
+int snl_sample(const snl_sample_p* p, float* logits, uint32_t n, const uint32_t* hist_tok, const uint32_t* hist_cnt,
+               uint32_t n_hist, const float* u, int64_t draft, uint32_t* out, void* scratch, void* stream);
+size_t snl_sample_scratch_bytes(void);
 /* ---- seeded synthetic tensors ------------------------------------------------------- */
 
 /* Fill device buffers with tensor `name` of the seeded synthetic model (the benchmark
@@ -349,6 +372,13 @@ int snl_engine_snapshot(snl_engine* e, size_t slot);             /* engine.rs:66
 int snl_engine_restore(snl_engine* e, size_t slot, size_t pos);  /* engine.rs:672-683 */
 int snl_engine_rollback(snl_engine* e);                          /* engine.rs:685-697 */
 size_t snl_engine_hid_rows(const snl_engine* e);                 /* engine.rs:699-702 */
+/* Sampler::sample / Sampler::verify (sampler.rs:54-167) on row `row` of the logits of
+ * the last snl_engine_forward_mm, on the device (as snl_sample; out3 on the host:
+ * token, accepted, draws used). A forward_mm with logits_out == NULL and logit_rows > 0
+ * keeps its logits on the device for this, without the copy to the host. hist_tok /
+ * hist_cnt: host arrays of the tokens generated so far and their counts. */
+int snl_engine_sample(snl_engine* e, size_t row, const snl_sample_p* p, const uint32_t* hist_tok,
+                      const uint32_t* hist_cnt, size_t n_hist, const float* u, int64_t draft, uint32_t* out3);
 int snl_engine_has_mtp(const snl_engine* e);                     /* engine.rs:704-706 */
 /* Matrices whose decode tile layout keeps fp16 block scales (every scale an fp16
  * number) and those that keep f32 scales. */

@@ -610,6 +610,101 @@ ORC_API uint32_t orc_argmax(const float* v, size_t n) {
   return (uint32_t)best;
 }
 
+// Sampler::distribution + draw / verify (sampler.rs:54-167) with the caller's uniform
+// draws u[] in the reference's order; the top_k_small branch (top_k 1..256) and greedy.
+// out: token, accepted, draws used.
+ORC_API int orc_sample(const snl_sample_p* p, float* logits, uint32_t n, const uint32_t* hist_tok,
+                       const uint32_t* hist_cnt, uint32_t n_hist, const float* u, int64_t draft, uint32_t* out) {
+  for (uint32_t i = 0; i < n_hist; i++) {  // sampler.rs:81-88
+    if (hist_tok[i] >= n) continue;
+    float& l = logits[hist_tok[i]];
+    if (p->repetition_penalty != 1.0f) l = l > 0.0f ? l / p->repetition_penalty : l * p->repetition_penalty;
+    l -= p->presence_penalty + p->frequency_penalty * (float)hist_cnt[i];
+  }
+  if (p->temperature <= 1e-5f) {  // sampler.rs:89-91
+    const uint32_t t = orc_argmax(logits, n);
+    out[0] = t;
+    out[1] = draft >= 0 && (uint64_t)draft == t ? 1 : 0;
+    out[2] = 0;
+    return 0;
+  }
+  const size_t k = p->top_k == 0 ? n : std::min<size_t>(p->top_k, n);
+  if (k > 256) return fail(-7, "orc_sample: top_k > 256 is not restated");
+  // top_k_small (sampler.rs:146-164): insertion after every entry >= v.
+  std::vector<std::pair<float, uint32_t>> best;
+  float floor = -INFINITY;
+  for (uint32_t i = 0; i < n; i++) {
+    const float v = logits[i];
+    if (best.size() == k && v <= floor) continue;
+    size_t pos = 0;
+    while (pos < best.size() && best[pos].first >= v) pos++;
+    best.insert(best.begin() + pos, {v, i});
+    if (best.size() > k) best.pop_back();
+    if (best.size() == k) floor = best[k - 1].first;
+  }
+  const float mx = logits[best[0].second];  // sampler.rs:105-108
+  std::vector<float> probs(k);
+  float sum = 0.0f;
+  for (size_t i = 0; i < k; i++) {
+    probs[i] = expf((logits[best[i].second] - mx) / p->temperature);
+    sum += probs[i];
+  }
+  for (auto& x : probs) x /= sum;
+  size_t keep = k;  // sampler.rs:110-124
+  if (p->min_p > 0.0f) {
+    const float thresh = probs[0] * p->min_p;
+    keep = 0;
+    while (keep < k && probs[keep] >= thresh) keep++;
+    keep = std::max<size_t>(keep, 1);
+  }
+  if (p->top_p < 1.0f) {
+    float cum = 0.0f;
+    for (size_t i = 0; i < keep; i++) {
+      cum += probs[i];
+      if (cum >= p->top_p) {
+        keep = i + 1;
+        break;
+      }
+    }
+  }
+  float total = 0.0f;
+  for (size_t i = 0; i < keep; i++) total += probs[i];
+  for (size_t i = 0; i < keep; i++) probs[i] /= total;
+  auto draw = [&](float uu, int64_t exclude) -> uint32_t {  // sampler.rs:130-144
+    float tot = 0.0f;
+    for (size_t i = 0; i < keep; i++)
+      if ((int64_t)best[i].second != exclude) tot += probs[i];
+    float r = uu * tot;
+    uint32_t last = best[0].second;
+    for (size_t i = 0; i < keep; i++) {
+      if ((int64_t)best[i].second == exclude) continue;
+      r -= probs[i];
+      last = best[i].second;
+      if (r <= 0.0f) return best[i].second;
+    }
+    return last;
+  };
+  if (draft < 0) {  // sample (sampler.rs:54-59)
+    out[0] = draw(u[0], -1);
+    out[1] = 0;
+    out[2] = 1;
+    return 0;
+  }
+  float pd = 0.0f;  // verify (sampler.rs:62-76)
+  for (size_t i = 0; i < keep; i++)
+    if ((int64_t)best[i].second == draft) pd = probs[i];
+  if (pd > 0.0f && u[0] < pd) {
+    out[0] = (uint32_t)draft;
+    out[1] = 1;
+    out[2] = 1;
+  } else {
+    out[0] = draw(pd > 0.0f ? u[1] : u[0], draft);
+    out[1] = 0;
+    out[2] = pd > 0.0f ? 2 : 1;
+  }
+  return 0;
+}
+
 // dequant_q8_row (weights.rs:155-162).
 ORC_API void orc_dequant_q8_row(const int8_t* q, const float* scales, size_t n, float* out) {
   for (size_t i = 0; i < n; i++) out[i] = (float)q[i] * scales[i / 32];

@@ -14,7 +14,7 @@ import numpy as np
 
 ROOT = Path(__file__).resolve().parent.parent
 sys.path.insert(0, str(ROOT / "sense-nova-server_b200"))
-from sensenova_b200.ffi import AttnP, LayerP, LinP, MatP, ModelConfigC, StepU  # noqa: E402  (struct layouts only)
+from sensenova_b200.ffi import AttnP, LayerP, LinP, MatP, ModelConfigC, SampleP, StepU  # noqa: E402  (struct layouts only)
 from sensenova_b200.config import ModelConfig  # noqa: E402
 
 LIB_PATH = Path(os.environ.get("SNL_ORACLE_LIB", ROOT / "oracle" / "_build" / "liboracle.so"))
@@ -35,6 +35,7 @@ _SIG = {
     "orc_conv": (i32, [P(StepU), P(LinP), vp, vp, vp, vp, vp]),
     "orc_delta": (i32, [P(StepU), P(LinP), vp, vp, vp, vp, vp, vp]),
     "orc_argmax": (u32, [vp, sz]),
+    "orc_sample": (i32, [P(SampleP), vp, u32, vp, vp, u32, vp, C.c_int64, vp]),
     "orc_dequant_q8_row": (None, [vp, vp, sz, vp]),
     "orc_gen_quant": (None, [u64, C.c_char_p, i32, sz, sz, vp, vp]),
     "orc_gen_f32": (None, [u64, C.c_char_p, u32, sz, C.c_float, C.c_float, vp]),
@@ -137,6 +138,20 @@ def conv(step, p, proj, conv_out, conv_state, lw, conv_ckpt):
 def delta(step, p, proj, conv_out, state, lw, out, state_ckpt):
     _check(lib().orc_delta(C.byref(step), C.byref(p), _p(proj), _p(conv_out), _p(state), _p(lw), _p(out),
                            _p(state_ckpt)))
+
+
+def sample(params, logits: np.ndarray, hist_tok, hist_cnt, u, draft: int = -1) -> tuple[int, int, int]:
+    """Sampler::sample / verify (sampler.rs:54-167) given the uniform draws u; logits are
+    modified in place by the penalties. Returns (token, accepted, draws used)."""
+    ht = np.ascontiguousarray(hist_tok, np.uint32)
+    hc = np.ascontiguousarray(hist_cnt, np.uint32)
+    uu = np.ascontiguousarray(u, np.float32)
+    out = np.zeros(3, np.uint32)
+    rc = lib().orc_sample(C.byref(params), _p(logits), logits.size, _p(ht), _p(hc), ht.size, _p(uu), int(draft),
+                          _p(out))
+    if rc:
+        raise RuntimeError(lib().orc_last_error().decode())
+    return int(out[0]), int(out[1]), int(out[2])
 
 
 def argmax(v: np.ndarray) -> int:

@@ -131,6 +131,9 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   } while (0)
 
 // Launch helpers implemented per kernel family (internal, not part of the C ABI).
+size_t sample_scratch_bytes();
+int launch_sample(const snl_sample_p& p, float* logits, uint32_t n, const uint32_t* hist_tok, const uint32_t* hist_cnt,
+                  uint32_t n_hist, float u0, float u1, int64_t draft, uint32_t* out, void* scratch, cudaStream_t s);
 // wplanes (optional): the matrix's weight planes (launch_weight_planes) for the
 // prefill GEMM.
 int launch_mat(int dtype, StepRef st, const snl_mat_p& p, const float* x, const void* wq, const void* ws,

@@ -137,6 +137,14 @@ struct snl_engine {
   // these planes ([8][pstride] halves), written by the kernel that produces each input.
   bool use_tc = true;
   bool use_fused_norm = true;
+  // On-device sampling (snl_engine_sample): logit rows of the last forward, scratch, the
+  // history copied per call (grown on demand) and the result words.
+  size_t last_logit_rows = 0;
+  void* sample_scratch = nullptr;
+  uint32_t* sample_out = nullptr;
+  uint32_t* h_sample_out = nullptr;
+  uint32_t* hist_d = nullptr;
+  size_t hist_cap = 0;
   bool tiles_on = false;      // every quantized matrix has its tile-layout copy
   int* tile_flag = nullptr;   // scale check scratch: set when a block scale is not an fp16 number
   uint32_t tiles_f16 = 0, tiles_f32 = 0;  // matrices whose tile scales are fp16 / f32
@@ -1314,6 +1322,10 @@ extern "C" void snl_engine_destroy(snl_engine* e) {
     if (e->h_step) cudaFreeHost(e->h_step);
     if (e->h_logits) cudaFreeHost(e->h_logits);
     if (e->h_amax) cudaFreeHost(e->h_amax);
+    if (e->h_sample_out) cudaFreeHost(e->h_sample_out);
+    if (e->sample_scratch) cudaFree(e->sample_scratch);
+    if (e->sample_out) cudaFree(e->sample_out);
+    if (e->hist_d) cudaFree(e->hist_d);
     if (e->stream) cudaStreamDestroy(e->stream);
   }
   delete e;
@@ -1324,11 +1336,12 @@ extern "C" int snl_engine_forward_mm(snl_engine* e, const uint32_t* tokens, size
                                      int ckpt, float* logits_out) {
   if (!e) return fail(SNL_E_INVALID, "null engine");
   if (n_embeds && (!embed_idx || !embeds)) return fail(SNL_E_INVALID, "forward: embeds without rows");
-  if (logit_rows && !logits_out) return fail(SNL_E_INVALID, "forward: logits requested without an output buffer");
   DeviceGuard dg(e->device);
   size_t rows = 0;
+  e->last_logit_rows = 0;
   SNL_TRY(forward_impl(e, tokens, n, pos, embed_idx, embeds, n_embeds, logit_rows, ckpt, false, &rows));
-  if (rows) {
+  e->last_logit_rows = rows;
+  if (rows && logits_out) {
     const size_t nbytes = rows * e->cfg.vocab * sizeof(float);
     const float* src = e->tp.size > 1 ? e->logits_full : e->head_out;
     SNL_CUDA_TRY(cudaMemcpyAsync(e->h_logits, src, nbytes, cudaMemcpyDeviceToHost, e->stream));
@@ -1351,6 +1364,40 @@ extern "C" int snl_engine_forward_greedy(snl_engine* e, const uint32_t* tokens, 
   SNL_CUDA_TRY(cudaMemcpyAsync(e->h_amax, e->amax, rows * sizeof(uint32_t), cudaMemcpyDeviceToHost, e->stream));
   SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));
   memcpy(argmax_out, e->h_amax, rows * sizeof(uint32_t));
+  return SNL_OK;
+}
+
+// Sampler::sample / verify (sampler.rs:54-167) on row `row` of the last forward's logits,
+// on the device: only the token and two flags come back, not the 1 MB row.
+extern "C" int snl_engine_sample(snl_engine* e, size_t row, const snl_sample_p* p, const uint32_t* hist_tok,
+                                 const uint32_t* hist_cnt, size_t n_hist, const float* u, int64_t draft, uint32_t* out3) {
+  if (!e || !p || !u || !out3) return fail(SNL_E_INVALID, "sample: null argument");
+  if (n_hist && (!hist_tok || !hist_cnt)) return fail(SNL_E_INVALID, "sample: history arrays missing");
+  if (row >= e->last_logit_rows) return fail(SNL_E_STATE, "sample: the last forward kept no logits for that row");
+  DeviceGuard dg(e->device);
+  if (!e->sample_scratch) {
+    SNL_CUDA_TRY(cudaMalloc(&e->sample_scratch, sample_scratch_bytes()));
+    SNL_CUDA_TRY(cudaMalloc(&e->sample_out, 4 * sizeof(uint32_t)));
+    SNL_CUDA_TRY(cudaMallocHost(&e->h_sample_out, 4 * sizeof(uint32_t)));
+  }
+  if (n_hist > e->hist_cap) {
+    if (e->hist_d) cudaFree(e->hist_d);
+    e->hist_d = nullptr;
+    e->hist_cap = 0;
+    SNL_CUDA_TRY(cudaMalloc(&e->hist_d, 2 * n_hist * sizeof(uint32_t)));
+    e->hist_cap = n_hist;
+  }
+  if (n_hist) {
+    SNL_CUDA_TRY(cudaMemcpyAsync(e->hist_d, hist_tok, n_hist * sizeof(uint32_t), cudaMemcpyHostToDevice, e->stream));
+    SNL_CUDA_TRY(cudaMemcpyAsync(e->hist_d + e->hist_cap, hist_cnt, n_hist * sizeof(uint32_t), cudaMemcpyHostToDevice,
+                                 e->stream));
+  }
+  float* src = (e->tp.size > 1 ? e->logits_full : e->head_out) + row * (size_t)e->cfg.vocab;
+  SNL_TRY(launch_sample(*p, src, e->cfg.vocab, e->hist_d, e->hist_d + e->hist_cap, (uint32_t)n_hist, u[0], u[1], draft,
+                        e->sample_out, e->sample_scratch, e->stream));
+  SNL_CUDA_TRY(cudaMemcpyAsync(e->h_sample_out, e->sample_out, 3 * sizeof(uint32_t), cudaMemcpyDeviceToHost, e->stream));
+  SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));
+  memcpy(out3, e->h_sample_out, 3 * sizeof(uint32_t));
   return SNL_OK;
 }
 

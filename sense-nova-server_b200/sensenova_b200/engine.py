@@ -192,6 +192,27 @@ class Engine:
             logit_rows, int(bool(ckpt)), out.ctypes.data if out is not None else None))
         return out
 
+    def forward_keep(self, tokens: Sequence[int], logit_rows: int = 1, ckpt: bool = False) -> None:
+        """forward_mm whose logits stay on the device for sample() (no 1 MB copy per row)."""
+        toks = _u32(tokens)
+        ffi.check(self.lib.snl_engine_forward_mm(self._h, toks.ctypes.data if len(toks) else None, len(toks), None,
+                                                 None, None, 0, logit_rows, int(bool(ckpt)), None))
+
+    def sample(self, row: int, params, history: dict[int, int] | None = None, u=(0.5, 0.5),
+               draft: int = -1) -> tuple[int, bool, int]:
+        """Sampler::sample (draft < 0) or Sampler::verify(draft) (sampler.rs:54-167) on the
+        device, on logit row `row` of the last forward; u: the host generator's uniform
+        draws. Returns (token, accepted, draws used)."""
+        hist = history or {}
+        ht = np.ascontiguousarray(list(hist.keys()), dtype=np.uint32)
+        hc = np.ascontiguousarray(list(hist.values()), dtype=np.uint32)
+        uu = np.ascontiguousarray(u, dtype=np.float32)
+        out = np.zeros(3, dtype=np.uint32)
+        ffi.check(self.lib.snl_engine_sample(self._h, row, C.byref(params), ht.ctypes.data if ht.size else None,
+                                             hc.ctypes.data if hc.size else None, ht.size, uu.ctypes.data, int(draft),
+                                             out.ctypes.data))
+        return int(out[0]), bool(out[1]), int(out[2])
+
     def forward_greedy(self, tokens: Sequence[int], pos: Sequence[Sequence[int]] | None = None,
                        logit_rows: int = 1, ckpt: bool = False) -> list[int]:
         """forward_mm + argmax on the device; only the token ids come back."""

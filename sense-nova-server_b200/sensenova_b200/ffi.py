@@ -30,6 +30,14 @@ class StepU(C.Structure):
     _fields_ = [("m", C.c_uint32), ("pos0", C.c_uint32), ("parts", C.c_uint32), ("ckpt", C.c_uint32)]
 
 
+class SampleP(C.Structure):
+    """SamplingParams without the seed (sampler.rs:4-14)."""
+
+    _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("top_k", C.c_uint32), ("min_p", C.c_float),
+                ("presence_penalty", C.c_float), ("frequency_penalty", C.c_float),
+                ("repetition_penalty", C.c_float), ("pad", C.c_uint32)]
+
+
 class MatP(C.Structure):
     """MatP (engine.rs:34-45)."""
     _fields_ = [(n, C.c_uint32) for n in ("n", "k", "x_off", "x_stride", "y_off", "y_stride", "n_off", "m_one")]
@@ -98,6 +106,8 @@ SIGNATURES = {
     "snl_xpack": (i32, [vp, u32, u32, u32, vp, vp]),
     "snl_mat_xpack": (i32, [i32, P(MatP), u32, vp, vp, vp, vp, vp]),
     "snl_weight_planes": (i32, [i32, u32, u32, vp, vp, vp, vp]),
+    "snl_sample": (i32, [P(SampleP), vp, u32, vp, vp, u32, vp, C.c_int64, vp, vp, vp]),
+    "snl_sample_scratch_bytes": (C.c_size_t, []),
     "snl_mat_wplanes": (i32, [i32, P(StepU), P(MatP), vp, vp, vp, vp, vp, vp]),
     "snl_tile_sizes": (i32, [i32, u32, u32, P(sz), P(sz)]),
     "snl_tile_repack": (i32, [i32, u32, u32, vp, vp, vp, vp, P(i32), vp]),
@@ -137,6 +147,7 @@ SIGNATURES = {
     "snl_engine_rollback": (i32, [vp]),
     "snl_engine_hid_rows": (sz, [vp]),
     "snl_engine_has_mtp": (i32, [vp]),
+    "snl_engine_sample": (i32, [vp, C.c_size_t, P(SampleP), vp, vp, C.c_size_t, vp, C.c_int64, vp]),
     "snl_engine_tile_scales": (i32, [vp, P(u32), P(u32)]),
     "snl_engine_pos": (sz, [vp]),
     "snl_engine_ctx": (sz, [vp]),

@@ -114,6 +114,34 @@ def test_weight_planes_bitwise(torch_cuda, cfg, monkeypatch):
     b.close()
 
 
+def test_engine_sample_on_device_matches_oracle(torch_cuda, orc, cfg):
+    """snl_engine_sample on the logits a forward kept on the device gives the oracle
+    sampler's result on the same logits (copied out by a twin engine), for sampling and
+    for speculative verify, with a growing history of generated tokens."""
+    from sensenova_b200.ffi import SampleP
+
+    a = Engine.synthetic(cfg, 320, 41)
+    b = Engine.synthetic(cfg, 320, 41)
+    rng = np.random.default_rng(5)
+    params = [SampleP(1.0, 0.95, 20, 0.0, 0.0, 0.0, 1.0, 0), SampleP(0.7, 0.8, 64, 0.05, 0.2, 0.1, 1.1, 0),
+              SampleP(0.0, 1.0, 1, 0.0, 0.0, 0.0, 1.3, 0)]
+    hist: dict[int, int] = {}
+    tok = [3, 14, 15, 92, 65]
+    for step in range(12):
+        p = params[step % 3]
+        lg = b.forward(tok, True)
+        a.forward_keep(tok, 1)
+        u = rng.random(2).astype(np.float32)
+        draft = -1 if step % 2 == 0 else int(np.argmax(lg))
+        want = orc.sample(p, lg.copy().ravel(), list(hist.keys()), list(hist.values()), u, draft)
+        got = a.sample(0, p, hist, u, draft)
+        assert (got[0], int(got[1]), got[2]) == want, (step, got, want)
+        tok = [got[0]]
+        hist[got[0]] = hist.get(got[0], 0) + 1
+    a.close()
+    b.close()
+
+
 def test_verify_two_rows_and_rollback(torch_cuda, orc, cfg):
     e, o = pair(orc, cfg, seed=14)
     prompt = [5, 17, 99, 400, 1234, 7]

@@ -488,3 +488,51 @@ def test_delta(T, lib, orc, m, ckpt):
     assert rel(host(Sd), S_ref) < TOL
     if ckpt:
         assert rel(host(ckd), ck_ref) < TOL
+
+
+# ---- sampler.rs ------------------------------------------------------------------------
+
+
+def test_sample_matches_oracle(T, lib, orc):
+    """snl_sample (penalties, greedy, top-k order, temperature, min-p, top-p, draw and
+    verify with the caller's draws) against the oracle's restatement, at the 9B vocab
+    size and small ones."""
+    from sensenova_b200.ffi import SampleP
+
+    rng = np.random.default_rng(77)
+    scratch = T.empty(int(lib.snl_sample_scratch_bytes()), dtype=T.uint8, device="cuda")
+    out = T.zeros(3, dtype=T.int32, device="cuda")
+    for i in range(200):
+        n = int(rng.choice([37, 1000, 248320]))
+        p = SampleP(float(rng.choice([0.0, 0.6, 1.0, 1.4])), float(rng.choice([1.0, 0.95, 0.7])),
+                    int(rng.choice([1, 7, 20, 100, 256])), float(rng.choice([0.0, 0.05, 0.3])),
+                    float(rng.choice([0.0, 0.4])), float(rng.choice([0.0, 0.15])), float(rng.choice([1.0, 1.2, 0.8])), 0)
+        logits = (rng.standard_normal(n) * rng.choice([1.0, 4.0])).astype(np.float32)
+        if i % 7 == 0:
+            logits[rng.integers(0, n, 20)] = logits.max()  # exact ties: ranked by index
+        ht = rng.choice(n, size=min(n, int(rng.integers(0, 16))), replace=False).astype(np.uint32)
+        hc = rng.integers(1, 5, size=ht.size).astype(np.uint32)
+        u = rng.random(2).astype(np.float32)
+        draft = -1 if i % 3 == 0 else (int(np.argmax(logits)) if i % 3 == 1 else int(rng.integers(0, n)))
+        want = orc.sample(p, logits.copy(), ht, hc, u, draft)
+        ld = dev(T, logits)
+        htd = dev(T, ht.view(np.int32)) if ht.size else None
+        hcd = dev(T, hc.view(np.int32)) if hc.size else None
+        call(lib.snl_sample(C.byref(p), ptr(ld), n, ptr(htd), ptr(hcd), int(ht.size),
+                            u.ctypes.data_as(C.c_void_p), draft, ptr(out), ptr(scratch), None))
+        got = tuple(int(v) for v in host(out).view(np.uint32))
+        assert got == want, (i, n, p.temperature, p.top_k, p.top_p, p.min_p, got, want)
+
+
+def test_sample_refuses_unordered_top_k(T, lib):
+    from sensenova_b200.ffi import SampleP
+
+    scratch = T.empty(int(lib.snl_sample_scratch_bytes()), dtype=T.uint8, device="cuda")
+    out = T.zeros(3, dtype=T.int32, device="cuda")
+    logits = T.zeros(1000, dtype=T.float32, device="cuda")
+    u = np.array([0.5, 0.5], np.float32)
+    for k in (0, 257):
+        p = SampleP(1.0, 0.95, k, 0.0, 0.0, 0.0, 1.0, 0)
+        rc = lib.snl_sample(C.byref(p), ptr(logits), 1000, None, None, 0, u.ctypes.data_as(C.c_void_p), -1, ptr(out),
+                            ptr(scratch), None)
+        assert rc == -7  # SNL_E_UNSUPPORTED
