@@ -381,6 +381,18 @@ def run_ours(args):
         tok = int(np.argmax(lg))
     torch.cuda.synchronize()
     e2e_logits = El / (time.perf_counter() - t0)
+    # the reference's default sampler (sampler.rs:17-29: temperature 1, top-p 0.95, top-k 20)
+    # on the device: the logits stay there, the token comes back (snl_engine_sample)
+    Es = max(args.e2e_logits_steps, 1)
+    sp = ffi.SampleP(1.0, 0.95, 20, 0.0, 0.0, 0.0, 1.0, 0)
+    srng = np.random.default_rng(args.seed + 7)
+    hist: dict[int, int] = {}
+    t0 = time.perf_counter()
+    for _ in range(Es):
+        eng.forward_keep([tok], 1)
+        tok, _, _ = eng.sample(0, sp, hist, srng.random(2))
+        hist[tok] = hist.get(tok, 0) + 1
+    e2e_sampled = Es / (time.perf_counter() - t0)
 
     # Roofline of the dominant kernel: the Q8_0 GEMVs of one decode step, each bracketed by
     # CUDA events on the engine stream.
@@ -427,6 +439,9 @@ def run_ours(args):
                                    f"{gb / 1e9:.2f} GB algorithmic)", "peak_kind": f"{peak_kind} hbm_gbs (burst)"},
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4 + 16 + 16, "d2h_bytes_per_step": 4,
                     "api": "snl_engine_forward_greedy"},
+            "e2e_sampled": {"value": e2e_sampled, "unit": "tok/s", "d2h_bytes_per_step": 12,
+                            "api": "snl_engine_forward_mm (logits kept on the device) + snl_engine_sample "
+                                   "(temperature 1, top-p 0.95, top-k 20)"},
             "e2e_logits": {"value": e2e_logits, "unit": "tok/s", "d2h_bytes_per_step": 4 * cfg.vocab,
                            "api": "snl_engine_forward_mm (full logits row, as engine.rs:917-931)"},
             "gpu_launches": int(launches),
