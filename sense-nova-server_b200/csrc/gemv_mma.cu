@@ -535,8 +535,23 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS >= 16 ? 2 : 3) gemv_pg_kerne
     bulk_g2s(st, tiles + ((uint64_t)grp * nb + sg * kPgTiles) * G::TB, wbytes, &bars[j % S], pol);
     bulk_g2s(st + G::kStageW, ts + ((uint64_t)grp * nb4 + sg * (kPgTiles / 4)) * 64, sbytes, &bars[j % S], pol);
   };
+  // The epilogue operands of this CTA's first group go to L2 early (its dot products hide
+  // the fetch): a residual merge's router and norm weights (constant) before the wait, its
+  // residual rows and merge coefficients (written by earlier kernels) right after it.
+  const bool pf = a.mode == 1 && warp == WARPS - 1 && g0 < g1;
+  const uint32_t prow = g0 * 16;  // 16 rows = one 64-byte line per array
+  if (pf) {
+    if (a.rnext && lane < 16)
+      prefetch_l2(a.rnext + (uint64_t)(lane >> 1) * 2 * a.h + (lane & 1) * a.h + prow);
+    if (a.nw && lane == 16) prefetch_l2(a.nw + prow);
+  }
   for (uint32_t j = 0; j < min((uint32_t)S, njobs); j++) issue(j);
   pdl_wait();
+  if (pf && lane < 2 * M) {
+    const uint32_t tt = lane >> 1;
+    prefetch_l2(a.resid + (uint64_t)tt * 2 * a.h + (lane & 1) * a.h + prow);
+    if ((lane & 1) == 0 && a.coef) prefetch_l2(a.coef + tt * 8);
+  }
   if constexpr (M % 2 == 0) {
     // Visible to the epilogue through the first group's __syncthreads.
     if (a.fused_norm && warp == 0) fused_norm_prologue<M / 2>(a, lane, nrm);

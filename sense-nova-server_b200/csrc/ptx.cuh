@@ -60,6 +60,9 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Fetches the 128-byte line holding p into L2 (no register, no wait).
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
 // Bit 0 of a device error word: a bounded wait gave up (read back by the host).
 __device__ __forceinline__ void report_timeout(int* err) { atomicOr(err, 1); }
 
