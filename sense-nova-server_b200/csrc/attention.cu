@@ -108,6 +108,23 @@ __global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, c
                                                      const uint32_t* __restrict__ vc, float* __restrict__ out,
                                                      float* __restrict__ partial, XOut xo) {
   pdl_trigger();
+  {
+    // The part's K and V rows into L2 before the wait (the step descriptor is written by
+    // the host before the step's first kernel; L2 stays coherent with the new key that
+    // the prep kernel writes meanwhile).
+    const snl_step_u s0 = load_step(sr);
+    const uint32_t m0 = blockIdx.y, part0 = blockIdx.z;
+    if (m0 < s0.m && part0 < s0.parts) {
+      const uint32_t tot = s0.pos0 + m0 + 1, ch = (tot + s0.parts - 1) / s0.parts;
+      const uint32_t a0 = min(tot, part0 * ch), a1 = min(tot, a0 + ch);
+      const uint32_t kvd = p.n_kv * HD, lines = (a1 - a0) * 8;  // 4 lines of 128 B per row, K and V
+      for (uint32_t i = threadIdx.x; i < lines; i += blockDim.x) {
+        const uint32_t t = a0 + (i >> 3), l = i & 3;
+        const uint32_t* base = (i & 4) ? vc : kc;
+        prefetch_l2(base + ((uint64_t)t * kvd + blockIdx.x * HD) / 2 + l * 32);
+      }
+    }
+  }
   pdl_wait();
   __shared__ float s_acc[kAttWarps][G][HD];  // 32 KB
   __shared__ float s_ml[kAttWarps][G][2];

@@ -316,6 +316,9 @@ __global__ void __launch_bounds__(kCsThreads)
   const float dt_bias = lw[(uint64_t)cd * 4 + p.n_v + h];
   const float neg_a = -__expf(lw[(uint64_t)cd * 4 + h]);
   const float inv_sqrt_dk = rsqrtf((float)DK);
+  // This CTA's state slice (one 128-byte line per row) into L2 before the wait; the
+  // previous step wrote it, and L2 is coherent.
+  if (tid < DK) prefetch_l2(state + (uint64_t)h * DK * DV + (uint64_t)tid * DV + c0);
   pdl_wait();
   const snl_step_u st = load_step(sr);
   float r0 = conv_state[ch], r1 = conv_state[(uint64_t)cd + ch], r2 = conv_state[(uint64_t)2 * cd + ch];
