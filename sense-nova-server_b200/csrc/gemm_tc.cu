@@ -494,14 +494,21 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_planes_kernel(const __grid_con
 // x [m][x_stride] fp32 (from x_off) -> planes [2][m][k] fp16: hi and lo of x / 16.
 __global__ void tc_xpack_kernel(const float* __restrict__ x, uint32_t x_stride, uint32_t m, uint32_t k,
                                 __half* __restrict__ planes) {
-  const uint64_t total = (uint64_t)m * k;
-  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
-    const uint64_t t = i / k, j = i % k;
-    const float vs = x[t * x_stride + j] * (1.0f / kXPlaneScaleTc);
-    const __half hi = __float2half_rn(vs);
-    planes[i] = hi;
-    planes[total + i] = __float2half_rn(vs - __half2float(hi));
+  // Row blockIdx.y, four consecutive elements per thread (x_stride and k multiples of 4).
+  const uint32_t t = blockIdx.y, j = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (t >= m || j >= k) return;
+  const float4 v = *reinterpret_cast<const float4*>(x + (uint64_t)t * x_stride + j);
+  const float vs[4] = {v.x * (1.0f / kXPlaneScaleTc), v.y * (1.0f / kXPlaneScaleTc), v.z * (1.0f / kXPlaneScaleTc),
+                       v.w * (1.0f / kXPlaneScaleTc)};
+  __half hi[4], lo[4];
+#pragma unroll
+  for (int e = 0; e < 4; e++) {
+    hi[e] = __float2half_rn(vs[e]);
+    lo[e] = __float2half_rn(vs[e] - __half2float(hi[e]));
   }
+  const uint64_t o = (uint64_t)t * k + j, total = (uint64_t)m * k;
+  *reinterpret_cast<uint2*>(planes + o) = *reinterpret_cast<const uint2*>(hi);
+  *reinterpret_cast<uint2*>(planes + total + o) = *reinterpret_cast<const uint2*>(lo);
 }
 
 PFN_cuTensorMapEncodeTiled encode_fn() {
@@ -564,8 +571,7 @@ int launch_gemm_tc(int dtype, const snl_mat_p& p, uint32_t m, const float* x, co
   __half* planes = planes_scratch((size_t)2 * m * p.k);
   if (!planes) return fail(SNL_E_OOM, "gemm_tc: x planes scratch");
   const uint64_t total = (uint64_t)m * p.k;
-  tc_xpack_kernel<<<(unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sm_count() * 8), 256, 0, s>>>(
-      x + p.x_off, p.x_stride, m, p.k, planes);
+  tc_xpack_kernel<<<dim3((p.k / 4 + 255) / 256, m), 256, 0, s>>>(x + p.x_off, p.x_stride, m, p.k, planes);
   SNL_LAUNCH_CHECK("gemm_tc xpack");
 
   // 256-token tiles (K blocks of 64, 2 stages, x one block ahead) unless the step has at

@@ -216,24 +216,47 @@ __global__ void mhc_finish_kernel(StepRef sr, snl_layer_p p, const float* __rest
 // of token m -> part[(m * slices + s) * 9 + o]; then one warp per token sums the
 // slices and finishes the Sinkhorn step (mhc_coef).
 constexpr int kMhcSlices = 16;
-__global__ void __launch_bounds__(256) mhc_part_kernel(snl_layer_p p, const float* __restrict__ x,
+// The 9 router sums (8 dots + sum of squares) of kMhcTok tokens over slice `blockIdx.x`
+// of the 2H inputs: each thread loads its router weights once per element and applies
+// them to the block's tokens; the 36 sums take one warp-shuffle and one shared-memory pass.
+constexpr uint32_t kMhcTok = 4;
+__global__ void __launch_bounds__(256) mhc_part_kernel(snl_layer_p p, uint32_t m_rows, const float* __restrict__ x,
                                                        const float* __restrict__ w, float* __restrict__ part) {
-  __shared__ float sh[32];
-  const uint32_t sl = blockIdx.x, m = blockIdx.y, d = 2 * p.h;
+  __shared__ float red[8][kMhcTok * 9];
+  const uint32_t sl = blockIdx.x, m0 = blockIdx.y * kMhcTok, d = 2 * p.h;
   const uint32_t len = d / kMhcSlices, i0 = sl * len;
-  float acc[9];
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float acc[kMhcTok][9];
 #pragma unroll
-  for (int o = 0; o < 9; o++) acc[o] = 0.f;
+  for (uint32_t t = 0; t < kMhcTok; t++)
+#pragma unroll
+    for (int o = 0; o < 9; o++) acc[t][o] = 0.f;
   for (uint32_t i = i0 + threadIdx.x; i < i0 + len; i += blockDim.x) {
-    const float v = x[(uint64_t)m * d + i];
+    float wv[8];
 #pragma unroll
-    for (int o = 0; o < 8; o++) acc[o] = fmaf(__ldg(w + (uint64_t)o * d + i), v, acc[o]);
-    acc[8] = fmaf(v, v, acc[8]);
+    for (int o = 0; o < 8; o++) wv[o] = __ldg(w + (uint64_t)o * d + i);
+#pragma unroll
+    for (uint32_t t = 0; t < kMhcTok; t++) {
+      const float v = m0 + t < m_rows ? x[(uint64_t)(m0 + t) * d + i] : 0.f;
+#pragma unroll
+      for (int o = 0; o < 8; o++) acc[t][o] = fmaf(wv[o], v, acc[t][o]);
+      acc[t][8] = fmaf(v, v, acc[t][8]);
+    }
   }
 #pragma unroll
-  for (int o = 0; o < 9; o++) {
-    const float t = block_sum(acc[o], sh);
-    if (threadIdx.x == 0) part[((uint64_t)m * kMhcSlices + sl) * 9 + o] = t;
+  for (uint32_t t = 0; t < kMhcTok; t++)
+#pragma unroll
+    for (int o = 0; o < 9; o++) {
+      const float v = warp_sum(acc[t][o]);
+      if (lane == 0) red[warp][t * 9 + o] = v;
+    }
+  __syncthreads();
+  if (threadIdx.x < kMhcTok * 9) {
+    const uint32_t t = threadIdx.x / 9, o = threadIdx.x % 9;
+    float v = 0.f;
+#pragma unroll
+    for (int wi = 0; wi < 8; wi++) v += red[wi][threadIdx.x];
+    if (m0 + t < m_rows) part[((uint64_t)(m0 + t) * kMhcSlices + sl) * 9 + o] = v;
   }
 }
 __global__ void mhc_coef_kernel(snl_layer_p p, uint32_t m_rows, const float* __restrict__ part,
@@ -250,46 +273,64 @@ __global__ void mhc_coef_kernel(snl_layer_p p, uint32_t m_rows, const float* __r
 }
 
 // merge (layers.wgsl:268-302).
+// Row blockIdx.y, four consecutive elements per thread (H is a multiple of 4).
 __global__ void merge_kernel(snl_layer_p p, uint32_t m_rows, float* __restrict__ x, const float* __restrict__ coef,
                              const float* __restrict__ br) {
   pdl_trigger();
   pdl_wait();
-  const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= (uint64_t)m_rows * p.h) return;
-  const uint64_t m = idx / p.h, i = idx % p.h;
-  const uint64_t b0 = m * 2 * p.h + i, b1 = b0 + p.h;
-  if (p.mode == 0) {
-    x[b0] += br[idx];
+  const uint32_t m = blockIdx.y, i = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (m >= m_rows || i >= p.h) return;
+  float4* p0 = reinterpret_cast<float4*>(x + (uint64_t)m * 2 * p.h + i);
+  float4* p1 = reinterpret_cast<float4*>(x + (uint64_t)m * 2 * p.h + p.h + i);
+  if (p.mode == 3) {
+    *p1 = *p0;
     return;
   }
-  if (p.mode == 3) {
-    x[b1] = x[b0];
+  const float4 bv = *reinterpret_cast<const float4*>(br + (uint64_t)m * p.h + i);
+  float4 a0 = *p0;
+  if (p.mode == 0) {
+    a0.x += bv.x;
+    a0.y += bv.y;
+    a0.z += bv.z;
+    a0.w += bv.w;
+    *p0 = a0;
     return;
   }
   const float* c = coef + m * 8;
-  const float x0 = x[b0], x1 = x[b1], b = br[idx];
-  const float n0 = fmaf(c[4], x0, fmaf(c[5], x1, c[2] * b));
-  const float n1 = fmaf(c[6], x0, fmaf(c[7], x1, c[3] * b));
+  const float4 a1 = *p1;
+  const float xs0[4] = {a0.x, a0.y, a0.z, a0.w}, xs1[4] = {a1.x, a1.y, a1.z, a1.w}, bs[4] = {bv.x, bv.y, bv.z, bv.w};
+  float n0[4], n1[4];
+#pragma unroll
+  for (int e = 0; e < 4; e++) {
+    n0[e] = fmaf(c[4], xs0[e], fmaf(c[5], xs1[e], c[2] * bs[e]));
+    n1[e] = fmaf(c[6], xs0[e], fmaf(c[7], xs1[e], c[3] * bs[e]));
+  }
   if (p.mode == 2) {
-    x[b0] = 0.5f * (n0 + n1);
+    *p0 = make_float4(0.5f * (n0[0] + n1[0]), 0.5f * (n0[1] + n1[1]), 0.5f * (n0[2] + n1[2]), 0.5f * (n0[3] + n1[3]));
   } else {
-    x[b0] = n0;
-    x[b1] = n1;
+    *p0 = make_float4(n0[0], n0[1], n0[2], n0[3]);
+    *p1 = make_float4(n1[0], n1[1], n1[2], n1[3]);
   }
 }
 
 // swiglu (layers.wgsl:304-315).
+// Row blockIdx.y, four consecutive outputs per thread (the FFN width is a multiple of 4).
 __global__ void swiglu_kernel(snl_layer_p p, uint32_t m_rows, const float* __restrict__ gu, float* __restrict__ act,
                               XOut xo) {
   pdl_trigger();
   pdl_wait();
-  const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= (uint64_t)m_rows * p.inter) return;
-  const uint64_t m = idx / p.inter, i = idx % p.inter;
-  const float g = gu[m * 2 * p.inter + i], u = gu[m * 2 * p.inter + p.inter + i];
-  const float a = g / (1.0f + __expf(-g)) * u;
-  act[idx] = a;
-  if (xo.planes) xout_store(xo, (uint32_t)m, (uint32_t)i, a);
+  const uint32_t m = blockIdx.y, i = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (m >= m_rows || i >= p.inter) return;
+  const float4 g = *reinterpret_cast<const float4*>(gu + (uint64_t)m * 2 * p.inter + i);
+  const float4 u = *reinterpret_cast<const float4*>(gu + (uint64_t)m * 2 * p.inter + p.inter + i);
+  const float gs[4] = {g.x, g.y, g.z, g.w}, us[4] = {u.x, u.y, u.z, u.w};
+  float a[4];
+#pragma unroll
+  for (int e = 0; e < 4; e++) a[e] = gs[e] / (1.0f + __expf(-gs[e])) * us[e];
+  *reinterpret_cast<float4*>(act + (uint64_t)m * p.inter + i) = make_float4(a[0], a[1], a[2], a[3]);
+  if (xo.planes)
+#pragma unroll
+    for (int e = 0; e < 4; e++) xout_store(xo, m, i + e, a[e]);
 }
 
 // Greedy argmax, two passes. Key = (ordered float bits << 32) | ~index so that the
@@ -486,7 +527,7 @@ int launch_mhc_router(const snl_layer_p& p, const float* x, const float* w, floa
                       cudaStream_t s) {
   if (m == 0) return SNL_OK;
   if ((2 * p.h) % kMhcSlices) return fail(SNL_E_INVALID, "mhc: 2H must divide into slices");
-  mhc_part_kernel<<<dim3(kMhcSlices, m), 256, 0, s>>>(p, x, w, part);
+  mhc_part_kernel<<<dim3(kMhcSlices, (m + kMhcTok - 1) / kMhcTok), 256, 0, s>>>(p, m, x, w, part);
   SNL_LAUNCH_CHECK("mhc_part");
   mhc_coef_kernel<<<(m + 3) / 4, 128, 0, s>>>(p, m, part, w, coef);
   SNL_LAUNCH_CHECK("mhc_coef");
@@ -498,14 +539,17 @@ int launch_merge(StepRef st, const snl_layer_p& p, float* x, const float* coef, 
   (void)st;
   const uint64_t n = (uint64_t)m * p.h;
   if (n == 0) return SNL_OK;
-  SNL_PDL_LAUNCH("merge_kernel", merge_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), (size_t)(0), s, p, m, x, coef, br);
+  if (p.h % 4 || ((uintptr_t)x | (uintptr_t)br) % 16) return fail(SNL_E_INVALID, "merge: H must be a multiple of 4 and x, branch 16-byte aligned");
+  SNL_PDL_LAUNCH("merge_kernel", merge_kernel, dim3((p.h / 4 + 255) / 256, m), dim3(256), (size_t)(0), s, p, m, x, coef, br);
   return SNL_OK;
 }
 int launch_swiglu(StepRef st, const snl_layer_p& p, const float* gu, float* act, uint32_t m, cudaStream_t s, XOut xo) {
   (void)st;
   const uint64_t n = (uint64_t)m * p.inter;
   if (n == 0) return SNL_OK;
-  SNL_PDL_LAUNCH("swiglu_kernel", swiglu_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), (size_t)(0), s, p, m, gu, act, xo);
+  if (p.inter % 4 || ((uintptr_t)gu | (uintptr_t)act) % 16)
+    return fail(SNL_E_INVALID, "swiglu: the FFN width must be a multiple of 4 and the buffers 16-byte aligned");
+  SNL_PDL_LAUNCH("swiglu_kernel", swiglu_kernel, dim3((p.inter / 4 + 255) / 256, m), dim3(256), (size_t)(0), s, p, m, gu, act, xo);
   return SNL_OK;
 }
 
