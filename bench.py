@@ -583,7 +583,8 @@ def run_mtp(args):
         return lg
 
     t0 = time.perf_counter()
-    feed(rng.integers(0, cfg.vocab, prefix).tolist(), 0)
+    prefix_ids = rng.integers(0, cfg.vocab, prefix).tolist()
+    feed(prefix_ids, 0)
     eng.snapshot(0)
     torch.cuda.synchronize()
     prefix_s = time.perf_counter() - t0
@@ -621,12 +622,47 @@ def run_mtp(args):
         torch.cuda.synchronize()
         dec_s += time.perf_counter() - t2
         produced += n_out
+    # The same turns through the generation loop (snl_worker, worker.rs:118-270): each turn
+    # is a request whose prompt is the 12K prefix plus fresh ids, with a snapshot at the
+    # prefix. Turn 0 runs cold and leaves the snapshot; later turns restore it. The loop
+    # drafts with the MTP head and pauses drafting when the drafts do not pay off.
+    from sensenova_b200.worker import GREEDY, Worker
+
+    w = Worker(eng)
+    wk = {"turns": 0, "tokens": 0, "decode_s": 0.0, "prefill_s": 0.0, "drafted": 0, "accepted": 0, "cached": 0}
+    cold_prefill_s = 0.0
+    for turn in range(args.turns + 1):
+        prompt = prefix_ids + rng.integers(0, cfg.vocab, full - prefix).tolist()
+        _, fin = w.run(prompt, GREEDY, dec, snapshot_at=prefix)
+        wk["drafted"] += fin.drafted
+        wk["accepted"] += fin.accepted
+        if turn == 0:
+            cold_prefill_s = fin.prefill_secs
+            continue
+        wk["turns"] += 1
+        wk["tokens"] += fin.completion_tokens
+        wk["decode_s"] += fin.decode_secs
+        wk["prefill_s"] += fin.prefill_secs
+        wk["cached"] += fin.cached_tokens
+    spec_on, pause = w.spec()
+    w.close()
     line = {
         "metric": "MTP speculative decode at 16K context: acceptance rate and tok/s",
         "value": produced / dec_s, "unit": "tok/s", "n_gpus": 1, "higher_is_better": True,
         "acceptance": accepted / max(drafted, 1), "drafted": drafted, "accepted": accepted,
         "e2e_tok_s_with_feed": produced / (dec_s + feed_s), "feed_tok_s": args.turns * (full - prefix) / feed_s,
         "prefix_prefill_s": prefix_s, "turns": args.turns, "dtype": "f32 (int8 weights)", "data": "synthetic",
+        "worker": {
+            "what": "the same turns as requests to snl_worker_run (prefix cache, drafting with self-pause)",
+            "decode_tok_s": wk["tokens"] / max(wk["decode_s"], 1e-9),
+            "e2e_tok_s_with_feed": wk["tokens"] / max(wk["decode_s"] + wk["prefill_s"], 1e-9),
+            "feed_tok_s": wk["turns"] * (full - prefix) / max(wk["prefill_s"], 1e-9),
+            "cached_tokens_per_turn": wk["cached"] / max(wk["turns"], 1),
+            "cold_turn_prefill_s": cold_prefill_s,
+            "drafted": wk["drafted"], "accepted": wk["accepted"],
+            "acceptance": wk["accepted"] / max(wk["drafted"], 1),
+            "drafting_after": {"on": spec_on, "pause_requests_left": pause},
+        },
         "config": {"workload": f"BASELINE configs[3]: 12K-token prefix snapshot, feed to 16K, {dec} tokens per turn "
                                f"with draft-1/verify-2, {args.turns} turns (1000 named; bounded sample)",
                    "quant": args.quant},

@@ -390,6 +390,105 @@ size_t snl_engine_device_bytes(const snl_engine* e);
 /* Copy `rows` rows of the last step's normed hidden states (row 0 = the token before
  * the step) to host memory; for tests of the hidden-row bookkeeping. */
 int snl_engine_read_hidden(const snl_engine* e, size_t row0, size_t rows, float* out);
+/* Engine::prefill_chunk (engine.rs:187, :599): token rows per forward step. */
+size_t snl_engine_prefill_chunk(const snl_engine* e);
+
+/* ---- generation loop (src/worker.rs) ----------------------------------------------
+ *
+ * snl_worker is the reference's Worker without its tokenizer, text streaming and media
+ * encoding: one request at a time over one engine, reusing cached prefixes across
+ * requests (the live cache, and SNL_WORKER_SNAPSHOTS snapshot slots evicted least
+ * recently used), with MTP draft-1 / verify-2 speculation, rollback of rejected drafts
+ * and the self-pause when drafting does not pay off (worker.rs:118-270, :298-338).
+ * Sampling runs on the device (snl_engine_sample); the uniform draws come from a
+ * seeded ChaCha12 generator on the host, one draw per use as the reference's Sampler
+ * takes them. Stop strings, detokenisation and the vision encoder are outside it: the
+ * caller passes the prompt as token ids, prefix keys and M-RoPE positions, with any
+ * media rows already encoded.
+ *
+ * snl_worker_ops is the engine as the worker sees it (the methods of engine.rs that
+ * worker.rs calls). snl_worker_create fills it from an snl_engine; snl_worker_create_ops
+ * accepts any implementation (a host model in tests). */
+#define SNL_WORKER_SNAPSHOTS 4 /* engine.rs:20 */
+typedef struct snl_worker snl_worker;
+typedef struct snl_worker_ops {
+  void* self;
+  size_t ctx;           /* Engine::ctx */
+  size_t prefill_chunk; /* Engine::prefill_chunk */
+  size_t hidden;        /* Config::hidden: floats per encoded media row */
+  int has_mtp;          /* Engine::has_mtp */
+  /* forward_mm with the logits of the last logit_rows rows kept for `sample` */
+  int (*forward)(void* self, const uint32_t* tokens, size_t n, const uint32_t* pos, const uint32_t* embed_idx,
+                 const float* embeds, size_t n_embeds, size_t logit_rows, int ckpt);
+  /* forward_mm plus the device argmax of each logit row; NULL = forward + sample */
+  int (*forward_greedy)(void* self, const uint32_t* tokens, size_t n, const uint32_t* pos, size_t logit_rows,
+                        int ckpt, uint32_t* argmax_out);
+  /* Sampler::sample (draft < 0) or Sampler::verify (draft >= 0) on a kept logit row;
+   * out3 = token, accepted, uniform draws used (as snl_engine_sample) */
+  int (*sample)(void* self, size_t row, const snl_sample_p* p, const uint32_t* hist_tok, const uint32_t* hist_cnt,
+                size_t n_hist, const float* u, int64_t draft, uint32_t* out3);
+  int (*mtp)(void* self, size_t r0, const uint32_t* tokens, size_t n, const uint32_t* pos, size_t slot0, int draft,
+             uint32_t* draft_out);
+  int (*reset)(void* self);
+  int (*snapshot)(void* self, size_t slot);
+  int (*restore)(void* self, size_t slot, size_t pos);
+  int (*rollback)(void* self);
+  size_t (*hid_rows)(void* self);
+  size_t (*pos)(void* self);
+  double (*now)(void* self); /* seconds; NULL = the host's steady clock */
+} snl_worker_ops;
+
+/* GenRequest (worker.rs:17-27) with Prompt (mm.rs:383-392) flattened. */
+typedef struct snl_gen_request {
+  const uint32_t* tokens; /* [n] */
+  const uint64_t* keys;   /* [n] prefix-cache keys; NULL = the token ids (Prompt::text) */
+  const uint32_t* pos;    /* [n][3] M-RoPE positions; NULL = [i, i, i] */
+  size_t n;
+  /* encoded media rows: embeds row i (hidden floats) replaces prompt token embed_idx[i] */
+  const uint32_t* embed_idx;
+  const float* embeds;
+  size_t n_embeds;
+  int64_t snapshot_at; /* snapshot the state after this many prompt tokens; < 0 = none */
+  snl_sample_p params;
+  uint64_t seed; /* SamplingParams::seed */
+  int has_seed;  /* 0 = seed from the host's entropy */
+  size_t max_tokens;
+  const uint32_t* eos; /* end-of-sequence ids (cfg.eos) */
+  size_t n_eos;
+  /* each generated token as it is produced (EOS excluded); return 0 when the client has
+   * gone away. NULL = no streaming. */
+  int (*on_token)(void* user, uint32_t token);
+  void* user;
+} snl_gen_request;
+
+#define SNL_FINISH_STOP 0
+#define SNL_FINISH_LENGTH 1
+/* Finish (worker.rs:41-55). */
+typedef struct snl_finish {
+  int reason; /* SNL_FINISH_STOP or SNL_FINISH_LENGTH */
+  int cancelled;
+  size_t prompt_tokens, completion_tokens, cached_tokens;
+  size_t drafted, accepted;
+  double prefill_secs, decode_secs;
+} snl_finish;
+
+int snl_worker_create(snl_engine* e, snl_worker** out);
+int snl_worker_create_ops(const snl_worker_ops* ops, snl_worker** out);
+void snl_worker_destroy(snl_worker* w);
+/* Worker::run (worker.rs:118-270). out_tokens (optional, out_cap entries) receives the
+ * generated ids in order, the EOS id last when reason is SNL_FINISH_STOP. On an error
+ * the engine is reset and every cached prefix dropped (worker.rs:93-100). */
+int snl_worker_run(snl_worker* w, const snl_gen_request* r, uint32_t* out_tokens, size_t out_cap, snl_finish* fin);
+/* The prefix keys of the live cache (slot < 0) or of snapshot slot `slot`, and that
+ * slot's last-used clock. *n = 0 and *used = 0 for an empty slot. */
+int snl_worker_prefix(const snl_worker* w, int slot, uint64_t* keys, size_t cap, size_t* n, uint64_t* used);
+/* Whether the current request drafts, and the requests left in a drafting pause. */
+int snl_worker_spec(const snl_worker* w, int* spec, size_t* pause);
+/* The first n uniform draws [0, 1) of the worker's generator for `seed`. */
+int snl_rng_uniforms(uint64_t seed, size_t n, float* out);
+/* The ChaCha block function (Bernstein 2008; RFC 8439 section 2.3) with `rounds`
+ * rounds (12 in the worker's generator) on the 16-word input state. */
+int snl_chacha_block(const uint32_t in[16], int rounds, uint32_t out[16]);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

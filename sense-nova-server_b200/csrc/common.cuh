@@ -22,6 +22,13 @@ void count_launch(uint64_t n = 1);
     if (_e != cudaSuccess) return ::snl::cuda_fail(_e, #expr);   \
   } while (0)
 
+// Returns a non-zero status code from the enclosing function.
+#define SNL_TRY(expr)          \
+  do {                         \
+    int _rc = (expr);          \
+    if (_rc) return _rc;       \
+  } while (0)
+
 // Checks the launch that was just issued and counts it.
 #define SNL_LAUNCH_CHECK(what)                                   \
   do {                                                           \

@@ -283,12 +283,6 @@ int mat(snl_engine* e, StepRef st, const QT& w, const float* x, size_t x_stride,
                [&] { return launch_mat(w.dtype, st, p, x, w.q, w.s, w.s_f16, y, e->stream, rows_m, w.wplanes); });
 }
 
-#define SNL_TRY(expr)          \
-  do {                         \
-    int _rc = (expr);          \
-    if (_rc) return _rc;       \
-  } while (0)
-
 // One projection of an eager step (the MTP layer and head) with 1-4 token rows: x packed
 // into fp16 hi/lo planes and the tile GEMV, when the matrix has its tile copy; else mat().
 int mat_tile(snl_engine* e, StepRef st, const QT& w, const float* x, size_t x_stride, float* y, size_t y_stride,
@@ -1651,3 +1645,9 @@ extern "C" int snl_engine_read_hidden(const snl_engine* e, size_t row0, size_t r
   SNL_CUDA_TRY(cudaMemcpy(out, e->hid + row0 * e->h(), rows * e->h() * sizeof(float), cudaMemcpyDeviceToHost));
   return SNL_OK;
 }
+
+extern "C" size_t snl_engine_prefill_chunk(const snl_engine* e) { return e ? MAX_M : 0; }
+
+namespace snl {
+size_t engine_hidden(const snl_engine* e) { return e ? e->cfg.hidden : 0; }
+}  // namespace snl

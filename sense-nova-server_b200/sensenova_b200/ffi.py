@@ -18,10 +18,14 @@ ERRORS = {
     -1: "SNL_E_INVALID", -2: "SNL_E_RANGE", -3: "SNL_E_CUDA", -4: "SNL_E_OOM",
     -5: "SNL_E_STATE", -6: "SNL_E_TIMEOUT", -7: "SNL_E_UNSUPPORTED", -8: "SNL_E_NCCL",
 }
+(SNL_E_INVALID, SNL_E_RANGE, SNL_E_CUDA, SNL_E_OOM, SNL_E_STATE, SNL_E_TIMEOUT, SNL_E_UNSUPPORTED,
+ SNL_E_NCCL) = -1, -2, -3, -4, -5, -6, -7, -8
 SNL_TP_HANDLE_BYTES = 64
 SNL_TP_FULL, SNL_TP_ROWS, SNL_TP_COLS, SNL_TP_ELEMS = 0, 1, 2, 3
 SNL_ENGINE_MTP = 1
 SNL_ENGINE_F16_SCALES = 2
+SNL_FINISH_STOP, SNL_FINISH_LENGTH = 0, 1
+SNL_WORKER_SNAPSHOTS = 4
 MAX_LAYERS = 256
 
 
@@ -79,6 +83,44 @@ class ModelConfigC(C.Structure):
 class OpStat(C.Structure):
     """snl_op_stat: one row of the per-op profile."""
     _fields_ = [("label", C.c_char * 32), ("calls", C.c_uint32), ("ms", C.c_double), ("bytes", C.c_double)]
+
+
+# Callback types of snl_worker_ops and snl_gen_request (include/snl_b200.h).
+sz_t = C.c_size_t
+FWD_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_void_p, sz_t, C.c_void_p, C.c_void_p, C.c_void_p, sz_t, sz_t, C.c_int)
+FWD_GREEDY_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_void_p, sz_t, C.c_void_p, sz_t, C.c_int, C.c_void_p)
+SAMPLE_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, sz_t, C.POINTER(SampleP), C.c_void_p, C.c_void_p, sz_t, C.c_void_p,
+                        C.c_int64, C.c_void_p)
+MTP_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, sz_t, C.c_void_p, sz_t, C.c_void_p, sz_t, C.c_int, C.c_void_p)
+SELF_FN = C.CFUNCTYPE(C.c_int, C.c_void_p)
+SLOT_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, sz_t)
+RESTORE_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, sz_t, sz_t)
+SIZE_FN = C.CFUNCTYPE(sz_t, C.c_void_p)
+NOW_FN = C.CFUNCTYPE(C.c_double, C.c_void_p)
+TOKEN_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_uint32)
+
+
+class WorkerOps(C.Structure):
+    """snl_worker_ops: the engine as the generation loop sees it."""
+    _fields_ = [("self", C.c_void_p), ("ctx", sz_t), ("prefill_chunk", sz_t), ("hidden", sz_t), ("has_mtp", C.c_int),
+                ("forward", FWD_FN), ("forward_greedy", FWD_GREEDY_FN), ("sample", SAMPLE_FN), ("mtp", MTP_FN),
+                ("reset", SELF_FN), ("snapshot", SLOT_FN), ("restore", RESTORE_FN), ("rollback", SELF_FN),
+                ("hid_rows", SIZE_FN), ("pos", SIZE_FN), ("now", NOW_FN)]
+
+
+class GenRequestC(C.Structure):
+    """snl_gen_request: GenRequest (worker.rs:17-27) with the Prompt flattened."""
+    _fields_ = [("tokens", C.c_void_p), ("keys", C.c_void_p), ("pos", C.c_void_p), ("n", sz_t),
+                ("embed_idx", C.c_void_p), ("embeds", C.c_void_p), ("n_embeds", sz_t), ("snapshot_at", C.c_int64),
+                ("params", SampleP), ("seed", C.c_uint64), ("has_seed", C.c_int), ("max_tokens", sz_t),
+                ("eos", C.c_void_p), ("n_eos", sz_t), ("on_token", TOKEN_FN), ("user", C.c_void_p)]
+
+
+class FinishC(C.Structure):
+    """snl_finish: Finish (worker.rs:41-55)."""
+    _fields_ = [("reason", C.c_int), ("cancelled", C.c_int), ("prompt_tokens", sz_t), ("completion_tokens", sz_t),
+                ("cached_tokens", sz_t), ("drafted", sz_t), ("accepted", sz_t), ("prefill_secs", C.c_double),
+                ("decode_secs", C.c_double)]
 
 
 class SnlError(RuntimeError):
@@ -153,6 +195,15 @@ SIGNATURES = {
     "snl_engine_ctx": (sz, [vp]),
     "snl_engine_device_bytes": (sz, [vp]),
     "snl_engine_read_hidden": (i32, [vp, sz, sz, vp]),
+    "snl_engine_prefill_chunk": (sz, [vp]),
+    "snl_worker_create": (i32, [vp, P(vp)]),
+    "snl_worker_create_ops": (i32, [P(WorkerOps), P(vp)]),
+    "snl_worker_destroy": (None, [vp]),
+    "snl_worker_run": (i32, [vp, P(GenRequestC), vp, sz, P(FinishC)]),
+    "snl_worker_prefix": (i32, [vp, i32, vp, sz, P(sz), P(u64)]),
+    "snl_worker_spec": (i32, [vp, P(i32), P(sz)]),
+    "snl_rng_uniforms": (i32, [u64, sz, vp]),
+    "snl_chacha_block": (i32, [vp, i32, vp]),
 }
 
 _lib: C.CDLL | None = None
