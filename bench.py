@@ -53,10 +53,11 @@ def parse_args():
     ap.add_argument("--cpu-budget-s", type=float, default=25.0)
     ap.add_argument("--profile", action="store_true", help="print the per-op table of one decode step")
     ap.add_argument("--turns", type=int, default=4, help="mtp workload: turns (BASELINE config 4 names 1000)")
-    ap.add_argument("--workload", choices=["decode", "gemv", "gemm", "deltanet", "mtp"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "gemv", "gemm", "deltanet", "mtp", "vision"], default="decode",
                     help="gemv: only BASELINE configs[0], the one-token Q8_0 GEMV 12288x4096; "
                          "gemm: one prefill-chunk GEMM (512 tokens x 12288 x 4096) on the tcgen05 kernel")
     ap.add_argument("--iters", type=int, default=40)
+    ap.add_argument("--grid", type=int, default=32, help="vision workload: patches per image side")
     ap.add_argument("--gemv-kernel", choices=["tile", "tc", "simt"], default="tile")
     ap.add_argument("--gemm-dequant", action="store_true",
                     help="gemm workload: dequantize in the kernel instead of the engine's weight planes")
@@ -742,6 +743,46 @@ def run_gemm_only(args):
     return 0
 
 
+def run_vision(args):
+    """The vision tower (vision.rs Vision::encode) on one image of grid x grid patches, at a
+    Qwen3-VL-sized configuration (hidden 1152, 27 blocks, 16 heads of 72, MLP 4304 padded
+    to 4320, 16-pixel patches over 2 frames, 2x2 merge to 4096). Seeded synthetic weights
+    and patches. Times snl_vision_encode end to end (patches from the host, features back)."""
+    import torch
+
+    from sensenova_b200.vision import Vision, VisionConfig
+
+    torch.cuda.set_device(0)
+    cfg = VisionConfig()
+    v = Vision.synthetic(cfg, seed=args.seed)
+    g = args.grid
+    n = g * g
+    patches = np.random.default_rng(args.seed).standard_normal((1, n, cfg.patch_dim())).astype(np.float32)
+    for _ in range(max(args.warmup, 3)):
+        v.encode(patches, 1, g, g)
+    torch.cuda.synchronize()
+    iters = max(1, min(args.iters, 20))
+    t0 = time.perf_counter()
+    for _ in range(iters):
+        out = v.encode(patches, 1, g, g)
+    dt = (time.perf_counter() - t0) / iters
+    h, ip, md = cfg.hidden, cfg.intermediate_padded, cfg.merged_dim()
+    gemm = 2.0 * n * (cfg.patch_dim() * h + cfg.depth * (3 * h * h + h * h + 2 * ip * h)) \
+        + 2.0 * (n // 4) * (md * md + md * cfg.out_hidden)
+    attn = cfg.depth * 4.0 * n * n * h
+    print(json.dumps({
+        "workload": "vision tower encode (vision.rs:176-311), one frame", "grid": [g, g], "patches": n,
+        "out_tokens": n // 4, "ms_per_frame": dt * 1e3, "frames_per_s": 1.0 / dt,
+        "out_tokens_per_s": (n // 4) / dt, "gemm_gflop": gemm / 1e9, "attention_gflop": attn / 1e9,
+        "tflops_total": (gemm + attn) / dt / 1e12, "dtype": "f32 (int8 weights)", "data": "synthetic",
+        "output_finite": bool(np.isfinite(out).all()),
+        "config": {k: getattr(cfg, k) for k in ("hidden", "intermediate", "depth", "n_heads", "patch",
+                                                "temporal_patch", "merge", "out_hidden", "pos_side")},
+    }), flush=True)
+    v.close()
+    return 0
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
@@ -754,6 +795,8 @@ def main():
         return run_deltanet(args)
     if args.workload == "mtp":
         return run_mtp(args)
+    if args.workload == "vision":
+        return run_vision(args)
     return run_ours(args)
 
 

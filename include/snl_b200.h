@@ -393,6 +393,51 @@ int snl_engine_read_hidden(const snl_engine* e, size_t row0, size_t rows, float*
 /* Engine::prefill_chunk (engine.rs:187, :599): token rows per forward step. */
 size_t snl_engine_prefill_chunk(const snl_engine* e);
 
+/* ---- vision tower (src/vision.rs, src/shaders/vision.wgsl) -------------------------- */
+
+/* VisP (vision.rs:39-50). Rows of one frame are in merge order: each run of 4 rows is
+ * a 2x2 block of patches, blocks row-major over a (grid_h/2) x (grid_w/2) grid. */
+typedef struct snl_vis_p {
+  uint32_t rows, cols, mode, act;
+  float eps;
+  uint32_t grid_w, heads, pad;
+} snl_vis_p;
+#define SNL_VIS_HEAD_DIM 72 /* vision.wgsl:22 */
+#define SNL_VIS_ACT_GELU_TANH 1
+#define SNL_VIS_ACT_GELU_ERF 2
+
+/* The four vision.wgsl entry points (device pointers, f32):
+ *   layer_norm (vision.wgsl:42-62): b[r] = LayerNorm(a[r]), w = weight[cols] | bias[cols];
+ *   epilogue (:82-98): v = act(a + bias); mode 0: a = v; mode 1: b += v; mode 2: b = v + e;
+ *   rope (:102-130): 2D rotary on q and k of qkv rows [rows, 3, heads, 72];
+ *   attend (:142-206): bidirectional attention over all rows, out [rows, heads * 72]. */
+int snl_vis_layer_norm(const snl_vis_p* p, const float* a, float* b, const float* w, void* stream);
+int snl_vis_epilogue(const snl_vis_p* p, float* a, float* b, const float* w, const float* e, void* stream);
+int snl_vis_rope(const snl_vis_p* p, float* qkv, void* stream);
+int snl_vis_attend(const snl_vis_p* p, const float* qkv, float* out, void* stream);
+
+/* VisionConfig (config.rs:40-70). The kernels need head_dim = hidden / n_heads = 72 and
+ * merge = 2, as vision.wgsl hard-codes them. */
+typedef struct snl_vision_config {
+  uint32_t hidden, intermediate, intermediate_padded, depth, n_heads;
+  uint32_t patch, temporal_patch, merge, out_hidden, pos_side;
+} snl_vision_config;
+typedef struct snl_vision snl_vision;
+/* Vision::load without the file part: tensors by name (convert.rs:165-199: v.patch,
+ * v.patch_b, v.pos, v{i}.n1/.n2/.qkv/.qkv_b/.proj/.proj_b/.fc1/.fc1_b/.fc2/.fc2_b,
+ * vm.norm, vm.fc1, vm.fc1_b, vm.fc2, vm.fc2_b) or the seeded synthetic set, then
+ * finalize. Matrices are Q8_0 (q int8 + f32 scales), vectors f32. */
+int snl_vision_create(const snl_vision_config* cfg, int device, snl_vision** out);
+int snl_vision_set_tensor(snl_vision* v, const char* name, int dtype, size_t rows, size_t cols, const void* q,
+                          const void* s);
+int snl_vision_fill_synthetic(snl_vision* v, uint64_t seed);
+int snl_vision_finalize(snl_vision* v);
+/* Vision::encode (vision.rs:176-311): patches (host) = frames * h * w patch vectors of
+ * patch_dim floats, in merge order, frame-major; out (host) = frames * h * w / 4 rows of
+ * out_hidden floats. Frames are encoded one at a time (attention never crosses frames). */
+int snl_vision_encode(snl_vision* v, const float* patches, size_t frames, size_t h, size_t w, float* out);
+void snl_vision_destroy(snl_vision* v);
+
 /* ---- generation loop (src/worker.rs) ----------------------------------------------
  *
  * snl_worker is the reference's Worker without its tokenizer, text streaming and media

@@ -1223,3 +1223,297 @@ ORC_API const float* orc_model_mtp_logits(void* hm) {
 // The shared f32 <-> f16 conversions (synth.h), exported for tests against numpy.
 ORC_API uint16_t orc_f32_to_f16(float f) { return snl_f32_to_f16(f); }
 ORC_API float orc_f16_to_f32(uint16_t h) { return snl_f16_to_f32(h); }
+
+// ---------------------------------------------------------------------------
+// The vision tower: src/shaders/vision.wgsl and Vision::encode (src/vision.rs).
+// ---------------------------------------------------------------------------
+
+// layer_norm (vision.wgsl:40-62): per row, 256 lane-strided partial sums then the tree
+// (reduce_sum, vision.wgsl:29-38) for the mean and for the centred variance.
+ORC_API int orc_vis_layer_norm(const snl_vis_p* p, const float* a, float* b, const float* w) {
+  const uint32_t cols = p->cols;
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < (int64_t)p->rows; r++) {
+    const float* ar = a + (uint64_t)r * cols;
+    float red[256];
+    for (uint32_t lid = 0; lid < 256; lid++) {
+      float s = 0.f;
+      for (uint32_t c = lid; c < cols; c += 256) s += ar[c];
+      red[lid] = s;
+    }
+    const float mean = tree256(red) / (float)cols;
+    for (uint32_t lid = 0; lid < 256; lid++) {
+      float v = 0.f;
+      for (uint32_t c = lid; c < cols; c += 256) {
+        const float d = ar[c] - mean;
+        v += d * d;
+      }
+      red[lid] = v;
+    }
+    const float inv = 1.0f / sqrtf(tree256(red) / (float)cols + p->eps);
+    for (uint32_t c = 0; c < cols; c++) b[(uint64_t)r * cols + c] = (ar[c] - mean) * inv * w[c] + w[cols + c];
+  }
+  return 0;
+}
+
+static float vis_gelu_tanh(float x) {  // vision.wgsl:64-67
+  float u = 0.7978845608f * (x + 0.044715f * x * x * x);
+  u = u < -15.f ? -15.f : (u > 15.f ? 15.f : u);
+  return 0.5f * x * (1.0f + tanhf(u));
+}
+static float vis_erf(float x) {  // vision.wgsl:69-75 (Abramowitz & Stegun 7.1.26)
+  const float t = 1.0f / (1.0f + 0.3275911f * fabsf(x));
+  const float y =
+      1.0f - (((((1.061405429f * t - 1.453152027f) * t) + 1.421413741f) * t - 0.284496736f) * t + 0.254829592f) * t *
+                 expf(-x * x);
+  return x >= 0.f ? y : -y;
+}
+static float vis_gelu_erf(float x) { return 0.5f * x * (1.0f + vis_erf(x * 0.7071067812f)); }
+
+// epilogue (vision.wgsl:77-98).
+ORC_API int orc_vis_epilogue(const snl_vis_p* p, float* a, float* b, const float* w, const float* e) {
+  const uint64_t total = (uint64_t)p->rows * p->cols;
+  for (uint64_t i = 0; i < total; i++) {
+    float v = a[i] + w[i % p->cols];
+    if (p->act == 1) v = vis_gelu_tanh(v);
+    else if (p->act == 2) v = vis_gelu_erf(v);
+    if (p->mode == 0) a[i] = v;
+    else if (p->mode == 1) b[i] = b[i] + v;
+    else b[i] = v + e[i];
+  }
+  return 0;
+}
+
+// rope (vision.wgsl:100-130) on [rows, 3, heads, 72].
+ORC_API int orc_vis_rope(const snl_vis_p* p, float* a) {
+  const uint32_t HD = 72, HALF = 36, per_token = p->heads * HALF, hidden = p->heads * HD;
+  for (uint64_t i = 0; i < (uint64_t)p->rows * per_token; i++) {
+    const uint32_t token = (uint32_t)(i / per_token), h = (uint32_t)(i % per_token) / HALF, j = (uint32_t)(i % HALF);
+    const uint32_t mw = p->grid_w / 2, blk = token / 4, intra = token % 4;
+    const uint32_t row = (blk / mw) * 2 + intra / 2, col = (blk % mw) * 2 + intra % 2;
+    const uint32_t fi = j % (HALF / 2);
+    const uint32_t pos = j >= HALF / 2 ? col : row;
+    const float ang = (float)pos * powf(10000.0f, -(float)(2 * fi) / (float)HALF);
+    const float cs = cosf(ang), sn = sinf(ang);
+    for (uint32_t part = 0; part < 2; part++) {
+      const uint64_t base = (uint64_t)token * 3 * hidden + part * hidden + h * HD;
+      const float x1 = a[base + j], x2 = a[base + j + HALF];
+      a[base + j] = x1 * cs - x2 * sn;
+      a[base + j + HALF] = x2 * cs + x1 * sn;
+    }
+  }
+  return 0;
+}
+
+// attend (vision.wgsl:137-206): per query, 16-key tiles, online softmax.
+ORC_API int orc_vis_attend(const snl_vis_p* p, const float* qkv, float* out) {
+  const uint32_t HD = 72, TK = 16, n = p->rows, hidden = p->heads * HD, stride = 3 * hidden;
+  const float scale = 1.0f / sqrtf((float)HD);
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int64_t h = 0; h < (int64_t)p->heads; h++) {
+    for (int64_t qi = 0; qi < (int64_t)n; qi++) {
+      float q[72], acc[72] = {0};
+      for (uint32_t d = 0; d < HD; d++) q[d] = qkv[(uint64_t)qi * stride + h * HD + d] * scale;
+      float mx = -1e30f, l = 0.f, sc[16];
+      for (uint32_t k0 = 0; k0 < n; k0 += TK) {
+        const uint32_t cnt = std::min(TK, n - k0);
+        float tmax = mx;
+        for (uint32_t j = 0; j < cnt; j++) {
+          const float* kr = qkv + (uint64_t)(k0 + j) * stride + hidden + h * HD;
+          float s = 0.f;
+          for (uint32_t d = 0; d < HD; d += 4) s += q[d] * kr[d] + q[d + 1] * kr[d + 1] + q[d + 2] * kr[d + 2] + q[d + 3] * kr[d + 3];
+          sc[j] = s;
+          tmax = std::max(tmax, s);
+        }
+        const float corr = expf(mx - tmax);
+        l *= corr;
+        for (uint32_t d = 0; d < HD; d++) acc[d] *= corr;
+        for (uint32_t j = 0; j < cnt; j++) {
+          const float* vr = qkv + (uint64_t)(k0 + j) * stride + 2 * hidden + h * HD;
+          const float pj = expf(sc[j] - tmax);
+          l += pj;
+          for (uint32_t d = 0; d < HD; d++) acc[d] += pj * vr[d];
+        }
+        mx = tmax;
+      }
+      for (uint32_t d = 0; d < HD; d++) out[(uint64_t)qi * hidden + h * HD + d] = acc[d] / l;
+    }
+  }
+  return 0;
+}
+
+namespace {
+
+struct OrcVision {
+  snl_vision_config c;
+  std::map<std::string, QW> qw;
+  std::map<std::string, std::vector<float>> fv;
+};
+
+// The synthetic tower of snl_vision_fill_synthetic: Q8_0 matrices by the shared rules,
+// LayerNorm weight 1 + 0.1 z | bias 0.05 z, other biases 0.02 z, position table 0.3 z.
+void vis_gen(OrcVision& V, uint64_t seed) {
+  const auto& c = V.c;
+  const size_t h = c.hidden, ip = c.intermediate_padded, md = (size_t)h * 4, pd = 3ull * c.temporal_patch * c.patch * c.patch;
+  auto q8 = [&](const std::string& n, size_t rows, size_t cols) {
+    QW w;
+    w.dtype = SNL_Q8_0;
+    w.rows = rows;
+    w.cols = cols;
+    w.q.resize(rows * cols / 4);
+    w.s.resize(rows * cols / 32);
+    orc_gen_quant(seed, n.c_str(), SNL_Q8_0, rows, cols, w.q.data(), w.s.data());
+    V.qw[n] = std::move(w);
+  };
+  auto vec = [&](const std::string& n, size_t len, float mult) {
+    std::vector<float> v(len);
+    orc_gen_f32(seed, n.c_str(), 0, len, mult, 0.f, v.data());
+    V.fv[n] = std::move(v);
+  };
+  auto norm = [&](const std::string& n) {
+    std::vector<float> v(2 * h);
+    orc_gen_f32(seed, n.c_str(), 0, h, 0.1f, 1.0f, v.data());
+    orc_gen_f32(seed, n.c_str(), 1, h, 0.05f, 0.0f, v.data() + h);
+    V.fv[n] = std::move(v);
+  };
+  q8("v.patch", h, pd);
+  vec("v.patch_b", h, 0.02f);
+  vec("v.pos", (size_t)c.pos_side * c.pos_side * h, 0.3f);
+  for (uint32_t i = 0; i < c.depth; i++) {
+    const std::string b = "v" + std::to_string(i) + ".";
+    norm(b + "n1");
+    norm(b + "n2");
+    q8(b + "qkv", 3 * h, h);
+    vec(b + "qkv_b", 3 * h, 0.02f);
+    q8(b + "proj", h, h);
+    vec(b + "proj_b", h, 0.02f);
+    q8(b + "fc1", ip, h);
+    vec(b + "fc1_b", ip, 0.02f);
+    q8(b + "fc2", h, ip);
+    vec(b + "fc2_b", h, 0.02f);
+  }
+  norm("vm.norm");
+  q8("vm.fc1", md, md);
+  vec("vm.fc1_b", md, 0.02f);
+  q8("vm.fc2", c.out_hidden, md);
+  vec("vm.fc2_b", c.out_hidden, 0.02f);
+}
+
+// Vision::pos_embed (vision.rs:141-175).
+std::vector<float> vis_pos_embed(const OrcVision& V, size_t h, size_t w) {
+  const size_t side = V.c.pos_side, hid = V.c.hidden, m = V.c.merge;
+  auto lin = [&](size_t n) {
+    std::vector<float> o(n);
+    for (size_t i = 0; i < n; i++) o[i] = n == 1 ? 0.0f : (float)(side - 1) * (float)i / (float)(n - 1);
+    return o;
+  };
+  const std::vector<float> hs = lin(h), ws = lin(w);
+  const std::vector<float>& pos = V.fv.at("v.pos");
+  std::vector<float> out(h * w * hid, 0.f);
+  for (size_t token = 0; token < h * w; token++) {
+    const size_t blk = token / (m * m), intra = token % (m * m);
+    const size_t r = (blk / (w / m)) * m + intra / m, c = (blk % (w / m)) * m + intra % m;
+    const size_t fh = (size_t)hs[r], fw = (size_t)ws[c];
+    const size_t ch = std::min(fh + 1, side - 1), cw = std::min(fw + 1, side - 1);
+    const float dh = hs[r] - (float)fh, dw = ws[c] - (float)fw;
+    const size_t idx[4] = {fh * side + fw, fh * side + cw, ch * side + fw, ch * side + cw};
+    const float wt[4] = {(1.0f - dh) * (1.0f - dw), (1.0f - dh) * dw, dh * (1.0f - dw), dh * dw};
+    for (int k = 0; k < 4; k++)
+      for (size_t j = 0; j < hid; j++) out[token * hid + j] += pos[idx[k] * hid + j] * wt[k];
+  }
+  return out;
+}
+
+// Kernels::matmul over `rows` token rows (vision.rs:314-343, one chunk).
+void vis_mat(const QW& w, const float* x, size_t rows, float* y, size_t y_stride) {
+  snl_mat_p p;
+  p.n = (uint32_t)w.rows;
+  p.k = (uint32_t)w.cols;
+  p.x_off = 0;
+  p.x_stride = (uint32_t)w.cols;
+  p.y_off = 0;
+  p.y_stride = (uint32_t)y_stride;
+  p.n_off = 0;
+  p.m_one = 0;
+  snl_step_u st{(uint32_t)rows, 0, 1, 0};
+  orc_mat(w.dtype, &st, &p, x, w.q.data(), w.s.data(), y);
+}
+
+}  // namespace
+
+ORC_API void* orc_vision_create(const snl_vision_config* cfg, uint64_t seed) {
+  OrcVision* V = new OrcVision();
+  V->c = *cfg;
+  vis_gen(*V, seed);
+  return V;
+}
+ORC_API void orc_vision_destroy(void* hv) { delete (OrcVision*)hv; }
+
+// Vision::encode (vision.rs:176-311), frame by frame, in the op order of :222-272.
+ORC_API int orc_vision_encode(void* hv, const float* patches, size_t frames, size_t h, size_t w, float* out) {
+  OrcVision& V = *(OrcVision*)hv;
+  const auto& c = V.c;
+  const size_t pd = 3ull * c.temporal_patch * c.patch * c.patch;
+  if (h % c.merge || w % c.merge) return fail(SNL_E_INVALID, "vision input has the wrong shape");
+  const size_t n = h * w, hid = c.hidden, nq = n / (c.merge * c.merge), ip = c.intermediate_padded,
+               md = hid * c.merge * c.merge;
+  const std::vector<float> pos = vis_pos_embed(V, h, w);
+  std::vector<float> x(n * hid), xn(n * hid), tmp(n * hid), att(n * hid), qkv(std::max(n * 3 * hid, nq * c.out_hidden)),
+      mlp(std::max(n * ip, nq * md)), dummy(16);
+  auto norm = [&](const std::vector<float>& nw) {
+    snl_vis_p p{(uint32_t)n, (uint32_t)hid, 0, 0, 1e-6f, 0, 0, 0};
+    orc_vis_layer_norm(&p, x.data(), xn.data(), nw.data());
+  };
+  auto epi = [&](float* a, float* b, const std::vector<float>& bias, const float* e, size_t rows, size_t cols,
+                 uint32_t mode, uint32_t act) {
+    snl_vis_p p{(uint32_t)rows, (uint32_t)cols, mode, act, 0.f, 0, 0, 0};
+    orc_vis_epilogue(&p, a, b, bias.data(), e);
+  };
+  for (size_t f = 0; f < frames; f++) {
+    vis_mat(V.qw.at("v.patch"), patches + f * n * pd, n, tmp.data(), hid);
+    epi(tmp.data(), x.data(), V.fv.at("v.patch_b"), pos.data(), n, hid, 2, 0);
+    for (uint32_t i = 0; i < c.depth; i++) {
+      const std::string b = "v" + std::to_string(i) + ".";
+      norm(V.fv.at(b + "n1"));
+      vis_mat(V.qw.at(b + "qkv"), xn.data(), n, qkv.data(), 3 * hid);
+      epi(qkv.data(), dummy.data(), V.fv.at(b + "qkv_b"), nullptr, n, 3 * hid, 0, 0);
+      snl_vis_p rp{(uint32_t)n, 0, 0, 0, 0.f, (uint32_t)w, c.n_heads, 0};
+      orc_vis_rope(&rp, qkv.data());
+      orc_vis_attend(&rp, qkv.data(), att.data());
+      vis_mat(V.qw.at(b + "proj"), att.data(), n, tmp.data(), hid);
+      epi(tmp.data(), x.data(), V.fv.at(b + "proj_b"), nullptr, n, hid, 1, 0);
+      norm(V.fv.at(b + "n2"));
+      vis_mat(V.qw.at(b + "fc1"), xn.data(), n, mlp.data(), ip);
+      epi(mlp.data(), dummy.data(), V.fv.at(b + "fc1_b"), nullptr, n, ip, 0, 1);
+      vis_mat(V.qw.at(b + "fc2"), mlp.data(), n, tmp.data(), hid);
+      epi(tmp.data(), x.data(), V.fv.at(b + "fc2_b"), nullptr, n, hid, 1, 0);
+    }
+    norm(V.fv.at("vm.norm"));
+    vis_mat(V.qw.at("vm.fc1"), xn.data(), nq, mlp.data(), md);
+    epi(mlp.data(), dummy.data(), V.fv.at("vm.fc1_b"), nullptr, nq, md, 0, 2);
+    vis_mat(V.qw.at("vm.fc2"), mlp.data(), nq, qkv.data(), c.out_hidden);
+    epi(qkv.data(), dummy.data(), V.fv.at("vm.fc2_b"), nullptr, nq, c.out_hidden, 0, 0);
+    memcpy(out + f * nq * c.out_hidden, qkv.data(), nq * c.out_hidden * sizeof(float));
+  }
+  return 0;
+}
+
+// The synthetic tower's tensors, for the GPU tests that load them through set_tensor.
+ORC_API int orc_vision_tensor(void* hv, const char* name, const void** q, const float** s, size_t* rows, size_t* cols) {
+  OrcVision& V = *(OrcVision*)hv;
+  auto it = V.qw.find(name);
+  if (it != V.qw.end()) {
+    *q = it->second.q.data();
+    *s = it->second.s.data();
+    *rows = it->second.rows;
+    *cols = it->second.cols;
+    return SNL_Q8_0;
+  }
+  auto jt = V.fv.find(name);
+  if (jt == V.fv.end()) return fail(SNL_E_INVALID, "orc_vision_tensor: unknown tensor");
+  *q = jt->second.data();
+  *s = nullptr;
+  *rows = 1;
+  *cols = jt->second.size();
+  return SNL_F32;
+}

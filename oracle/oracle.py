@@ -14,7 +14,8 @@ import numpy as np
 
 ROOT = Path(__file__).resolve().parent.parent
 sys.path.insert(0, str(ROOT / "sense-nova-server_b200"))
-from sensenova_b200.ffi import AttnP, LayerP, LinP, MatP, ModelConfigC, SampleP, StepU  # noqa: E402  (struct layouts only)
+from sensenova_b200.ffi import (AttnP, LayerP, LinP, MatP, ModelConfigC, SampleP, StepU, VisionConfigC,  # noqa: E402
+                                 VisP)  # (struct layouts only)
 from sensenova_b200.config import ModelConfig  # noqa: E402
 
 LIB_PATH = Path(os.environ.get("SNL_ORACLE_LIB", ROOT / "oracle" / "_build" / "liboracle.so"))
@@ -53,6 +54,14 @@ _SIG = {
     "orc_model_forward_mm": (i32, [vp, vp, sz, vp, vp, vp, sz, sz, i32, vp]),
     "orc_model_mtp": (i32, [vp, sz, vp, sz, vp, sz, i32, vp]),
     "orc_model_mtp_logits": (vp, [vp]),
+    "orc_vis_layer_norm": (i32, [P(VisP), vp, vp, vp]),
+    "orc_vis_epilogue": (i32, [P(VisP), vp, vp, vp, vp]),
+    "orc_vis_rope": (i32, [P(VisP), vp]),
+    "orc_vis_attend": (i32, [P(VisP), vp, vp]),
+    "orc_vision_create": (vp, [P(VisionConfigC), u64]),
+    "orc_vision_destroy": (None, [vp]),
+    "orc_vision_encode": (i32, [vp, vp, sz, sz, sz, vp]),
+    "orc_vision_tensor": (i32, [vp, C.c_char_p, P(vp), P(vp), P(sz), P(sz)]),
     "orc_f32_to_f16": (C.c_uint16, [C.c_float]),
     "orc_f16_to_f32": (C.c_float, [C.c_uint16]),
 }
@@ -264,3 +273,66 @@ class OracleModel:
     def mtp_logits(self) -> np.ndarray:
         ptr = lib().orc_model_mtp_logits(self._h)
         return np.ctypeslib.as_array((C.c_float * self.cfg.vocab).from_address(ptr)).copy()
+
+
+# ---- vision tower (vision.wgsl, vision.rs) ----------------------------------------------
+
+def vis_layer_norm(p: VisP, a: np.ndarray, w: np.ndarray) -> np.ndarray:
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.zeros_like(a)
+    _check(lib().orc_vis_layer_norm(C.byref(p), _p(a), _p(b), _p(np.ascontiguousarray(w, np.float32))))
+    return b
+
+
+def vis_epilogue(p: VisP, a: np.ndarray, b: np.ndarray | None, w: np.ndarray, e: np.ndarray | None = None):
+    """In place on a (mode 0) or b (modes 1, 2), as the kernel."""
+    _check(lib().orc_vis_epilogue(C.byref(p), _p(a), None if b is None else _p(b), _p(np.ascontiguousarray(w, np.float32)),
+                                  None if e is None else _p(e)))
+
+
+def vis_rope(p: VisP, qkv: np.ndarray) -> None:
+    _check(lib().orc_vis_rope(C.byref(p), _p(qkv)))
+
+
+def vis_attend(p: VisP, qkv: np.ndarray) -> np.ndarray:
+    out = np.zeros((p.rows, p.heads * 72), np.float32)
+    _check(lib().orc_vis_attend(C.byref(p), _p(np.ascontiguousarray(qkv, np.float32)), _p(out)))
+    return out
+
+
+class OracleVision:
+    """Vision (vision.rs) on the CPU with the seeded synthetic tower."""
+
+    def __init__(self, cfg, seed: int = 0):
+        self.cfg = cfg
+        self._c = cfg.to_c()
+        self._h = lib().orc_vision_create(C.byref(self._c), seed)
+
+    def close(self):
+        if self._h:
+            lib().orc_vision_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def encode(self, patches: np.ndarray, frames: int, h: int, w: int) -> np.ndarray:
+        patches = np.ascontiguousarray(patches, np.float32)
+        out = np.zeros((frames * h * w // 4, self.cfg.out_hidden), np.float32)
+        _check(lib().orc_vision_encode(self._h, _p(patches), frames, h, w, _p(out)))
+        return out
+
+    def tensor(self, name: str):
+        """(dtype, q bytes / f32 array, f32 scales or None, rows, cols) of one synthetic tensor."""
+        q, s, r, c = C.c_void_p(), C.c_void_p(), C.c_size_t(), C.c_size_t()
+        dt = lib().orc_vision_tensor(self._h, name.encode(), C.byref(q), C.byref(s), C.byref(r), C.byref(c))
+        _check(dt if dt < 0 else 0)
+        n = r.value * c.value
+        if dt == 1:
+            qa = np.ctypeslib.as_array((C.c_int8 * n).from_address(q.value)).copy()
+            sa = np.ctypeslib.as_array((C.c_float * (n // 32)).from_address(s.value)).copy()
+            return dt, qa, sa, r.value, c.value
+        return dt, np.ctypeslib.as_array((C.c_float * n).from_address(q.value)).copy(), None, r.value, c.value

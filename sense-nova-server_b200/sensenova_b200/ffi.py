@@ -26,6 +26,8 @@ SNL_ENGINE_MTP = 1
 SNL_ENGINE_F16_SCALES = 2
 SNL_FINISH_STOP, SNL_FINISH_LENGTH = 0, 1
 SNL_WORKER_SNAPSHOTS = 4
+SNL_VIS_HEAD_DIM = 72
+SNL_VIS_ACT_GELU_TANH, SNL_VIS_ACT_GELU_ERF = 1, 2
 MAX_LAYERS = 256
 
 
@@ -83,6 +85,18 @@ class ModelConfigC(C.Structure):
 class OpStat(C.Structure):
     """snl_op_stat: one row of the per-op profile."""
     _fields_ = [("label", C.c_char * 32), ("calls", C.c_uint32), ("ms", C.c_double), ("bytes", C.c_double)]
+
+
+class VisP(C.Structure):
+    """VisP (vision.rs:39-50)."""
+    _fields_ = [("rows", C.c_uint32), ("cols", C.c_uint32), ("mode", C.c_uint32), ("act", C.c_uint32),
+                ("eps", C.c_float), ("grid_w", C.c_uint32), ("heads", C.c_uint32), ("pad", C.c_uint32)]
+
+
+class VisionConfigC(C.Structure):
+    """snl_vision_config (VisionConfig, config.rs:40-70)."""
+    _fields_ = [(n, C.c_uint32) for n in ("hidden", "intermediate", "intermediate_padded", "depth", "n_heads", "patch",
+                                          "temporal_patch", "merge", "out_hidden", "pos_side")]
 
 
 # Callback types of snl_worker_ops and snl_gen_request (include/snl_b200.h).
@@ -196,6 +210,16 @@ SIGNATURES = {
     "snl_engine_device_bytes": (sz, [vp]),
     "snl_engine_read_hidden": (i32, [vp, sz, sz, vp]),
     "snl_engine_prefill_chunk": (sz, [vp]),
+    "snl_vis_layer_norm": (i32, [P(VisP), vp, vp, vp, vp]),
+    "snl_vis_epilogue": (i32, [P(VisP), vp, vp, vp, vp, vp]),
+    "snl_vis_rope": (i32, [P(VisP), vp, vp]),
+    "snl_vis_attend": (i32, [P(VisP), vp, vp, vp]),
+    "snl_vision_create": (i32, [P(VisionConfigC), i32, P(vp)]),
+    "snl_vision_set_tensor": (i32, [vp, C.c_char_p, i32, sz, sz, vp, vp]),
+    "snl_vision_fill_synthetic": (i32, [vp, u64]),
+    "snl_vision_finalize": (i32, [vp]),
+    "snl_vision_encode": (i32, [vp, vp, sz, sz, sz, vp]),
+    "snl_vision_destroy": (None, [vp]),
     "snl_worker_create": (i32, [vp, P(vp)]),
     "snl_worker_create_ops": (i32, [P(WorkerOps), P(vp)]),
     "snl_worker_destroy": (None, [vp]),
