@@ -12,8 +12,10 @@ L2, so no L2 flush is needed between steps.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Under torchrun (N > 1) every rank runs its own replica of the model on its GPU
-("replicas"; weak scaling); time is the max over ranks.
+Under torchrun (N > 1) the N ranks decode ONE stream together, tensor-parallel: every
+quantized matrix is split by rows or columns across the GPUs and the partial sums are
+exchanged over NVLink peer memory inside the GEMV epilogue ("scaling": "strong"); time is
+the max over ranks.
 """
 from __future__ import annotations
 
@@ -33,7 +35,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "sense-nova-server_b200"))
 
 METRIC = "decode tok/s @bs1 Q8_0 9B-shape; Q8 GEMV achieved HBM GB/s vs peak"
-PUBLISHED_DECODE_TOK_S = 38.0  # ~38 tok/s decode, batch 1, Q8_0 (RTX 5080, README.md:218)
+PUBLISHED_DECODE_TOK_S = 38.0  # the reference's published decode: ~38 tok/s, batch 1, Q8_0 (RTX 5080, README.md:218)
 FALLBACK_HBM_GBS = 6650.0
 
 

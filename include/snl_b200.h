@@ -284,8 +284,8 @@ int snl_engine_create(const snl_model_config* cfg, size_t ctx, int device, uint3
 
 /* Tensor parallelism over 2, 4 or 8 GPUs of one node: one process (and one engine) per
  * GPU, all driven through the same call sequence, as the reference's single Engine is.
- * (The reference has no tensor parallelism. SURVEY §8e proposes `snl_engine_create(...,
- * tp_rank, tp_size, nccl_id)`; the rendezvous here is CUDA IPC instead of an NCCL id.)
+ * (The reference has no tensor parallelism. A create call taking (tp_rank, tp_size,
+ * nccl_id) was the obvious shape; the rendezvous here is CUDA IPC instead of an NCCL id.)
  * The in-projections and the LM head are split by output rows (qkv by head, in_proj by
  * key/value head, gate_up by intermediate slice, lm_head by vocabulary). The
  * out-projections are split by K, and their partial sums are added across GPUs over

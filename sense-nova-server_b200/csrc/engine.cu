@@ -777,7 +777,7 @@ extern "C" int snl_engine_create(const snl_model_config* cfg, size_t ctx, int de
 }
 
 // ---------------------------------------------------------------------------
-// Tensor parallelism (Megatron split): column-parallel in-projections
+// Tensor parallelism (the Megatron split): column-parallel in-projections
 // (qkv by head, in_proj by key/value head, gate_up by intermediate slice) and LM head
 // (by vocabulary rows); row-parallel out-projections (o_proj, out_proj, down: K split)
 // whose partial sums are exchanged over NVLink peer memory (tp.cuh). Norms, mHC and the

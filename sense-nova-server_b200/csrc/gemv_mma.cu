@@ -54,11 +54,26 @@ __device__ __forceinline__ void q8_half2(uint32_t w, uint32_t& h01, uint32_t& h2
   h01 = hsub2_u32(__byte_perm(u, 0x64646464u, 0x4140), off);  // [b0, 0x64, b1, 0x64]
   h23 = hsub2_u32(__byte_perm(u, 0x64646464u, 0x4342), off);
 }
-// 8 nibbles of w (element i = nibble i, value nibble - 8) -> half2 pairs (i, i+4), i < 4.
+__device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
+  __half2 r = __hfma2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b), *reinterpret_cast<__half2*>(&c));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// 8 nibbles of w (element i = nibble i, value nibble - 8) -> half2 pairs (i, i+4), i < 4,
+// exact, in 9 instructions per word. A nibble at bits 0-3 of a half, or-ed into fp16 1024
+// (0x6400), is 1024 + n: subtract 1032. A nibble left at bits 4-7 gives 1024 + 16 n:
+// (1024 + 16 n) / 16 - 72 = n - 8 is one packed fma (both steps exact in fp16). Nibbles
+// 2, 3, 6, 7 take the same two forms after one shift of the word by 8.
 __device__ __forceinline__ void q4_half2(uint32_t w, uint32_t h[4]) {
-  const uint32_t off = 0x64086408u;  // half2(1032, 1032)
-#pragma unroll
-  for (int i = 0; i < 4; i++) h[i] = hsub2_u32(((w >> (4 * i)) & 0x000F000Fu) | 0x64006400u, off);
+  constexpr uint32_t kMagic = 0x64006400u;   // half2(1024, 1024)
+  constexpr uint32_t kOff = 0x64086408u;     // half2(1032, 1032)
+  constexpr uint32_t kSixteenth = 0x2C002C00u;  // half2(1/16, 1/16)
+  constexpr uint32_t kNeg72 = 0xD480D480u;   // half2(-72, -72)
+  const uint32_t w8 = w >> 8;
+  h[0] = hsub2_u32((w & 0x000F000Fu) | kMagic, kOff);
+  h[1] = hfma2_u32((w & 0x00F000F0u) | kMagic, kSixteenth, kNeg72);
+  h[2] = hsub2_u32((w8 & 0x000F000Fu) | kMagic, kOff);
+  h[3] = hfma2_u32((w8 & 0x00F000F0u) | kMagic, kSixteenth, kNeg72);
 }
 
 template <typename ST>
@@ -334,10 +349,6 @@ __device__ __forceinline__ float scale_f(__half v) { return __half2float(v); }
 __device__ __forceinline__ uint32_t u8pair(uint32_t w, uint32_t sel) {
   return hsub2_u32(__byte_perm(w, 0x64646464u, sel), 0x64806480u);
 }
-// Q4 (tile nibble order): half2 of nibbles (j, j + 4) of w, j = 0..3.
-__device__ __forceinline__ uint32_t u4pair(uint32_t w, int j) {
-  return hsub2_u32(((w >> (4 * j)) & 0x000F000Fu) | 0x64006400u, 0x64086408u);
-}
 
 // ---------------------------------------------------------------------------
 // Persistent row-group tile GEMV (the default decode GEMV).
@@ -593,8 +604,12 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS >= 16 ? 2 : 3) gemv_pg_kerne
           mma16816(d, A1, xv[u].z, xv[u].w);
         } else {
           const uint2 w = *reinterpret_cast<const uint2*>(st + u * G::TB + lane * 8);
-          const uint32_t A0[4] = {u4pair(w.x, 0), u4pair(w.y, 0), u4pair(w.x, 1), u4pair(w.y, 1)};
-          const uint32_t A1[4] = {u4pair(w.x, 2), u4pair(w.y, 2), u4pair(w.x, 3), u4pair(w.y, 3)};
+          // Tile nibble order: nibbles (j, j + 4) of a word are elements (8t + 2j, 8t + 2j + 1).
+          uint32_t hx[4], hy[4];
+          q4_half2(w.x, hx);
+          q4_half2(w.y, hy);
+          const uint32_t A0[4] = {hx[0], hy[0], hx[1], hy[1]};
+          const uint32_t A1[4] = {hx[2], hy[2], hx[3], hy[3]};
           mma16816(d, A0, xv[u].x, xv[u].y);
           mma16816(d, A1, xv[u].z, xv[u].w);
         }
