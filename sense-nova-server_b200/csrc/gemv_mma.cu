@@ -578,12 +578,21 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS >= 16 ? 2 : 3) gemv_pg_kerne
       if (!ok) continue;
       const uint32_t sg = st0 + si;
       const uint32_t nt = min((uint32_t)kPgTiles, nb - sg * kPgTiles);
+      const bool full = nt == (uint32_t)kPgTiles;
       uint4 xv[kPgTiles];
+      if (full) {
+        // A full stage (every stage when k is a multiple of 256): one base address,
+        // constant offsets, no per-tile bound checks.
+        const uint4* xs = reinterpret_cast<const uint4*>(xbase + (uint64_t)sg * (kPgTiles * 32));
 #pragma unroll
-      for (int u = 0; u < kPgTiles; u++) {
-        const uint32_t uu = min((uint32_t)u, nt - 1);
-        xv[u] = has_x ? __ldg(reinterpret_cast<const uint4*>(xbase + ((uint64_t)sg * kPgTiles + uu) * 32))
-                      : make_uint4(0, 0, 0, 0);
+        for (int u = 0; u < kPgTiles; u++) xv[u] = has_x ? __ldg(xs + 4 * u) : make_uint4(0, 0, 0, 0);
+      } else {
+#pragma unroll
+        for (int u = 0; u < kPgTiles; u++) {
+          const uint32_t uu = min((uint32_t)u, nt - 1);
+          xv[u] = has_x ? __ldg(reinterpret_cast<const uint4*>(xbase + ((uint64_t)sg * kPgTiles + uu) * 32))
+                        : make_uint4(0, 0, 0, 0);
+        }
       }
       if (!__all_sync(0xffffffffu, mbar_wait_bounded(&bars[j % S], (j / S) & 1))) {
         ok = false;
@@ -592,9 +601,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS >= 16 ? 2 : 3) gemv_pg_kerne
       }
       const uint8_t* st = ring + (j % S) * G::kStage;
       const ST* sc = reinterpret_cast<const ST*>(st + G::kStageW);
-#pragma unroll
-      for (int u = 0; u < kPgTiles; u++) {
-        if ((uint32_t)u >= nt) break;
+      auto tile = [&](int u) {
         float d[4] = {0.f, 0.f, 0.f, 0.f};
         if constexpr (DT == SNL_Q8_0) {
           const uint4 w = *reinterpret_cast<const uint4*>(st + u * G::TB + lane * 16);
@@ -617,6 +624,16 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS >= 16 ? 2 : 3) gemv_pg_kerne
         const float scB = scale_f(sc[(u / 4) * 64 + (g + 8) * 4 + (u % 4)]);
         accA = fmaf(scA, d[0] + d[1], accA);
         accB = fmaf(scB, d[2] + d[3], accB);
+      };
+      if (full) {
+#pragma unroll
+        for (int u = 0; u < kPgTiles; u++) tile(u);
+      } else {
+#pragma unroll
+        for (int u = 0; u < kPgTiles; u++) {
+          if ((uint32_t)u >= nt) break;
+          tile(u);
+        }
       }
       fence_proxy_async_smem();
       __syncwarp();
