@@ -473,15 +473,32 @@ __device__ __forceinline__ void group_finish(const GemvArgs& a, uint32_t grp, ui
 // branch_norm + mhc_finish, the separate kernels' math).
 template <int T>
 __device__ __forceinline__ void fused_norm_prologue(const GemvArgs& a, int lane, float* nrm) {
+  static_assert(kRpStride % 4 == 0 && kRpStride >= 11, "a part is whole float4s holding 11 sums");
 #pragma unroll 1
   for (int tt = 0; tt < T; tt++) {
     float acc[11];
 #pragma unroll
     for (int o = 0; o < 11; o++) acc[o] = 0.f;
-    for (uint32_t i = lane; i < a.nparts; i += 32) {
-      const float* rp = a.nrpart + ((uint64_t)tt * a.nparts + i) * kRpStride;
+    // Parts lane, lane + 32, ... in batches of 4 whose 12 vector loads are all in flight
+    // before the first add; the adds keep the part order, so the sums are unchanged.
+    const float4* rp4 = reinterpret_cast<const float4*>(a.nrpart + (uint64_t)tt * a.nparts * kRpStride);
+    for (uint32_t i0 = lane; i0 < a.nparts; i0 += 32 * 4) {
+      float4 v[4][3];
 #pragma unroll
-      for (int o = 0; o < 11; o++) acc[o] += rp[o];
+      for (int b = 0; b < 4; b++) {
+        const uint32_t i = i0 + 32 * b;
+#pragma unroll
+        for (int q = 0; q < 3; q++)
+          v[b][q] = i < a.nparts ? rp4[(uint64_t)i * (kRpStride / 4) + q] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int b = 0; b < 4; b++) {
+        if (i0 + 32 * b >= a.nparts) break;
+        const float f[11] = {v[b][0].x, v[b][0].y, v[b][0].z, v[b][0].w, v[b][1].x, v[b][1].y,
+                             v[b][1].z, v[b][1].w, v[b][2].x, v[b][2].y, v[b][2].z};
+#pragma unroll
+        for (int o = 0; o < 11; o++) acc[o] += f[o];
+      }
     }
 #pragma unroll
     for (int o = 0; o < 11; o++) acc[o] = warp_sum(acc[o]);
