@@ -415,6 +415,24 @@ def run_ours(args):
     if rank == 0 and args.profile:
         eng.print_profile(prof)
     g1 = None if args.no_gemv else gemv_config1(lib, args.quant)
+    # The metric's "GEMV achieved HBM GB/s vs peak" is the config-1 GEMV (BASELINE.json
+    # configs[0]): its launches timed back to back with CUDA events on the launching stream.
+    # The decode step's matrix launches, each bracketed by events in one eager step (no
+    # overlap with the previous kernel, so a lower bound), are reported beside it.
+    step_roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "kernel": f"{args.quant.upper()} GEMV (all {n_mat} matrix launches of one decode step, "
+                               f"{gb / 1e9:.2f} GB algorithmic, each timed alone)",
+                     "peak_kind": f"{peak_kind} hbm_gbs (burst)"}
+    roofline = step_roofline
+    if g1:
+        roofline = {"bound": "hbm", "achieved": g1["achieved_gbs"], "peak": peak, "unit": "GB/s",
+                    "frac": g1["achieved_gbs"] / peak,
+                    "traffic": (t1 if t1 is not None and args.quant == "q8_0" else None),
+                    "kernel": f"gemv_pg_kernel, BASELINE configs[0] ({args.quant.upper()} 12288x4096, one token): "
+                              f"{g1['bytes_per_launch']} algorithmic bytes per launch / {g1['us_per_launch']:.2f} us "
+                              f"average over 40 back-to-back launches (CUDA events, launching stream)",
+                    "peak_kind": f"{peak_kind} hbm_gbs (burst)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -436,10 +454,8 @@ def run_ours(args):
                        "weight_bytes_per_token": weight_bytes_per_token(cfg, args.quant),
                        "l2": f"inputs larger than L2 ({weight_bytes_per_token(cfg, args.quant) / 1e9:.1f} GB of weights streamed per token)",
                        "parallelism": f"tp{world}" if world > 1 else "single"},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic,
-                         "kernel": f"{args.quant.upper()} GEMV (all {n_mat} matrix launches of one decode step, "
-                                   f"{gb / 1e9:.2f} GB algorithmic)", "peak_kind": f"{peak_kind} hbm_gbs (burst)"},
+            "roofline": roofline,
+            "roofline_decode_step": step_roofline,
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4 + 16 + 16, "d2h_bytes_per_step": 4,
                     "api": "snl_engine_forward_greedy"},
             "e2e_sampled": {"value": e2e_sampled, "unit": "tok/s", "d2h_bytes_per_step": 12,
