@@ -99,6 +99,7 @@ __device__ __forceinline__ void h8_to_f(const uint4 w, float f[8]) {
 
 constexpr int kAttWarps = 8;
 constexpr int kKeysPerGroup = 8;
+constexpr uint32_t kPrefetchKeys = 64;
 
 // attend: CTA (KV head, token, part); 8 warps each take 8-key groups round-robin and
 // keep their own online softmax for the G = 4 query heads; lane l owns head dims
@@ -117,7 +118,9 @@ __global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, c
     if (m0 < s0.m && part0 < s0.parts) {
       const uint32_t tot = s0.pos0 + m0 + 1, ch = (tot + s0.parts - 1) / s0.parts;
       const uint32_t a0 = min(tot, part0 * ch), a1 = min(tot, a0 + ch);
-      const uint32_t kvd = p.n_kv * HD, lines = (a1 - a0) * 8;  // 4 lines of 128 B per row, K and V
+      // 4 lines of 128 B per row, K and V, for at most the part's first kPrefetchKeys rows:
+      // a long context's whole KV (134 MB per layer at 32K) would overflow L2.
+      const uint32_t kvd = p.n_kv * HD, lines = min(a1 - a0, kPrefetchKeys) * 8;
       for (uint32_t i = threadIdx.x; i < lines; i += blockDim.x) {
         const uint32_t t = a0 + (i >> 3), l = i & 3;
         const uint32_t* base = (i & 4) ? vc : kc;

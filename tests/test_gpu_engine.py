@@ -82,6 +82,23 @@ def test_simt_fallback_path_matches_oracle(torch_cuda, orc, cfg, monkeypatch):
     e.close()
 
 
+def test_long_context_decode_matches_oracle(torch_cuda, orc, cfg):
+    """Decode past 4096 keys of context, where the split-key attention needs more than 64
+    parts (a second captured decode graph): logits within 1e-3 and the same greedy
+    tokens as the oracle."""
+    e, o = pair(orc, cfg, ctx=4400, seed=21)
+    prompt = [(1000 + i * 7919) % cfg.vocab for i in range(4200)]
+    le, lo = e.forward(prompt, True), o.forward(prompt, True)
+    assert rel(le, lo) < TOL, rel(le, lo)
+    te, to = int(np.argmax(le)), int(np.argmax(lo))
+    for step in range(4):
+        assert te == to, (step, te, to)
+        le, lo = e.forward([te], True), o.forward([to], True)
+        assert rel(le, lo) < TOL, (step, rel(le, lo))
+        te, to = int(np.argmax(le)), int(np.argmax(lo))
+    e.close()
+
+
 def test_forward_greedy_matches_logits(torch_cuda, orc, cfg):
     e, _ = pair(orc, cfg, seed=13)
     e2 = Engine.synthetic(cfg, 320, 13)
