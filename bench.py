@@ -52,6 +52,8 @@ def parse_args():
     ap.add_argument("--e2e-logits-steps", type=int, default=16)
     ap.add_argument("--no-gemv", action="store_true", help="skip the standalone config-1 GEMV timing")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the oracle parity check (and with it the CPU baseline)")
     ap.add_argument("--cpu-budget-s", type=float, default=25.0)
     ap.add_argument("--profile", action="store_true", help="print the per-op table of one decode step")
     ap.add_argument("--turns", type=int, default=4, help="mtp workload: turns (BASELINE config 4 names 1000)")
@@ -145,46 +147,84 @@ def phys_gpu_index(local_rank: int) -> int:
 CONFIG1_BYTES = 12288 * 4096 + 12288 * 4096 // 32 * 2 + 4 * 4096 + 4 * 12288  # codes, fp16 block scales, x, y
 
 
-def traffic_from_profiles() -> float | None:
-    """DRAM bytes per launch of the config-1 GEMV from the committed ncu summary
-    (profiles/gemv_q8_decode.md, `dram_bytes_per_launch:`)."""
-    f = ROOT / "profiles" / "gemv_q8_decode.md"
-    if not f.exists():
-        return None
-    for line in f.read_text().splitlines():
-        if line.strip().startswith("dram_bytes_per_launch:"):
-            try:
-                return float(line.split(":", 1)[1].strip().split()[0])
-            except ValueError:
-                return None
-    return None
-
-
 # ---- CPU side (oracle): the reference's algorithm restated in C++ ------------------------------
 
 
-def cpu_decode(cfg, quant: int, budget_s: float, max_steps: int, warmup: int = 1, seed: int = 0):
-    """Greedy decode with the CPU restatement of the reference's kernels (oracle/),
-    all host threads. Returns (tok/s, steps timed, build seconds)."""
+def oracle_model(cfg, quant: str, seed: int, ctx: int = 64):
+    """The CPU restatement of the reference's kernels (oracle/) for the same seeded model,
+    on every host thread (torchrun sets OMP_NUM_THREADS=1 in its workers; the oracle's
+    thread count is set explicitly). Returns (oracle module, model, build seconds)."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle as orc  # test/baseline infrastructure only
 
+    orc.set_threads(cores())
     t0 = time.perf_counter()
-    m = orc.OracleModel(cfg, 64, seed=seed, quant=quant)
-    build_s = time.perf_counter() - t0
-    prompt = [int(v) for v in np.random.default_rng(seed).integers(0, cfg.vocab, 4)]
-    lg = m.forward(prompt, True)
-    tok = orc.argmax(lg)
+    m = orc.OracleModel(cfg, ctx, seed=seed, quant={"q8_0": 1, "q4_0": 2}[quant])
+    return orc, m, time.perf_counter() - t0
+
+
+def parity_prompt(cfg, seed: int, n: int = 4) -> list[int]:
+    return [int(v) for v in np.random.default_rng(seed).integers(0, cfg.vocab, n)]
+
+
+def first_max(v: np.ndarray) -> int:
+    """sampler.rs:169-177 on a host row: the first maximum."""
+    return int(np.argmax(v))
+
+
+PARITY_STEPS = 8
+
+
+def gpu_parity_run(eng, prompt: list[int], steps: int = PARITY_STEPS):
+    """The engine on the parity prompt, twice from a reset state: (a) forward_mm with the
+    logits row every step (host argmax), (b) the product greedy path: forward_greedy for
+    the prompt, then the device decode loop. Returns (tokens a, logits a, tokens b)."""
+    eng.reset()
+    lg = [eng.forward(prompt, True)]
+    toks = [first_max(lg[0])]
+    for _ in range(steps):
+        lg.append(eng.forward([toks[-1]], True))
+        toks.append(first_max(lg[-1]))
+    eng.reset()
+    t0 = eng.forward_greedy(prompt, None, 1)[0]
+    gen, _ = eng.generate(t0, steps)
+    eng.reset()
+    return toks, lg, [t0] + list(gen)
+
+
+def oracle_parity(orc, m, prompt: list[int], gpu_tokens: list[int], gpu_logits: list, greedy_tokens: list[int]):
+    """Greedy decode of the oracle on the same prompt (its own tokens fed back), compared
+    forward by forward with the GPU's logits: max |gpu - oracle| / max |oracle| per step,
+    identical tokens, and at the first differing token the oracle's top-2 gap."""
+    lo = m.forward(prompt, True)
+    rels, toks, flip = [], [], None
+    for i in range(len(gpu_logits)):
+        if i:
+            lo = m.forward([toks[-1]], True)
+        rels.append(float(np.abs(gpu_logits[i].astype(np.float64) - lo).max() / max(np.abs(lo).max(), 1e-30)))
+        toks.append(orc.argmax(lo))
+        if flip is None and toks[-1] != gpu_tokens[i]:
+            top = np.sort(lo)[-2:]
+            flip = {"step": i, "oracle": toks[-1], "gpu": gpu_tokens[i], "oracle_top2_gap": float(top[1] - top[0])}
+    return {"logits_rel_max": max(rels), "logits_rel_per_step": rels, "tokens_oracle": toks,
+            "tokens_gpu_logits_path": gpu_tokens, "tokens_gpu_greedy_path": greedy_tokens,
+            "tokens_identical": toks == gpu_tokens == greedy_tokens, "first_flip": flip,
+            "tolerance": 1e-3, "within_tolerance": max(rels) < 1e-3}
+
+
+def oracle_decode(m, orc, first: int, warmup: int, steps: int, budget_s: float):
+    """Greedy decode steps of the oracle model from token `first`: `warmup` untimed, then
+    up to `steps` timed (fewer when `budget_s` of CPU time runs out). Returns (tok/s, steps)."""
+    tok = first
     for _ in range(warmup):
         tok = orc.argmax(m.forward([tok], True))
-    steps, t = 0, 0.0
-    while steps < max_steps and (steps == 0 or t < budget_s):
+    n, t = 0, 0.0
+    while n < steps and (n == 0 or t < budget_s):
         t1 = time.perf_counter()
         tok = orc.argmax(m.forward([tok], True))
         t += time.perf_counter() - t1
-        steps += 1
-    m.close()
-    return steps / t, steps, build_s
+        n += 1
+    return n / t, n
 
 
 def weight_bytes_per_token(cfg, quant: str) -> int:
@@ -266,7 +306,7 @@ def gemv_config1(lib, quant: str, copies: int = 8, iters: int = 40, kernel: str 
     us = a.elapsed_time(b) * 1000.0 / iters
     # Algorithmic bytes: Q8_0/Q4_0 blocks (codes + an fp16 scale per 32), x, y.
     nbytes = qb + n * k // 32 * 2 + 4 * k + 4 * n
-    return {"shape": [n, k], "quant": quant, "scales": scale_mode, "kernel": kernel, "us_per_launch": us,
+    return {"shape": [n, k], "quant": quant, "scales": scale_mode, "kernel": kernel, "us_per_launch": us, "iters": iters,
             "bytes_per_launch": nbytes,
             "achieved_gbs": nbytes / (us * 1e3), "copies_rotated": copies}
 
@@ -279,23 +319,34 @@ def cores() -> int:
 
 
 def run_reference(args):
+    """The reference arm: the CPU restatement of the reference's kernels (the reference is
+    a Rust/wgpu crate that cannot be built or run here), greedy decode of the same 9B-shape
+    model on all host threads, W warm-up and K timed steps (fewer if ~150 s of CPU time
+    runs out). Under torchrun only rank 0 runs it."""
     rank, world, _ = env_rank()
     if rank != 0:
         return 0
     from sensenova_b200.config import nine_b
 
     cfg = nine_b()
-    quant = {"q8_0": 1, "q4_0": 2}[args.quant]
-    budget = max(30.0, min(150.0, 4.0 * args.steps))
-    v, n, build_s = cpu_decode(cfg, quant, budget, args.steps, warmup=min(args.warmup, 1), seed=args.seed)
-    sample = (f"9B-shape {args.quant} greedy decode, 4-token prompt, {n} timed tokens (of --steps {args.steps}; "
-              f"capped to ~{budget:.0f} s of CPU work), weights generated in {build_s:.0f} s")
+    budget = 150.0
+    orc, m, build_s = oracle_model(cfg, args.quant, args.seed)
+    prompt = parity_prompt(cfg, args.seed)
+    first = orc.argmax(m.forward(prompt, True))
+    v, n = oracle_decode(m, orc, first, args.warmup, args.steps, budget)
+    thr = orc.threads()
+    m.close()
+    sample = (f"9B-shape {args.quant} greedy decode after a {len(prompt)}-token prompt, {args.warmup} warm-up and "
+              f"{n} timed tokens (of --steps {args.steps}; capped at ~{budget:.0f} s of CPU work), {thr} OpenMP "
+              f"threads, weights generated in {build_s:.0f} s. The prompt is short because a 2048-token prefill "
+              f"costs ~54 TFLOP on the CPU; the KV reads at 2K context are <1% of a decode step's bytes")
     line = {
         "metric": METRIC, "value": v, "unit": "tok/s", "impl": "reference", "n_gpus": world, "steps": n,
-        "warmup": min(args.warmup, 1), "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": v / PUBLISHED_DECODE_TOK_S, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "9B-shape Q8_0 decode bs1", "quant": args.quant},
-        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores(), "kind": "port", "sample": sample},
+        "config": {"workload": f"9B-shape {args.quant} greedy decode bs1 after a {len(prompt)}-token prompt",
+                   "quant": args.quant, "prompt_tokens": len(prompt)},
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": thr, "kind": "port", "sample": sample},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference = CPU restatement of the reference's WGSL kernels (oracle/); the Rust/wgpu reference "
                 "cannot be built or run here (no Rust toolchain, no graphics stack)",
@@ -333,6 +384,27 @@ def run_ours(args):
     n16, n32 = eng.tile_scales()
     scale_mode = f"tile layout: {n16} matrices with fp16 block scales, {n32} with f32"
     build_s = time.perf_counter() - t0
+
+    # Parity on this configuration before anything is timed: the engine (every rank under
+    # tensor parallelism) against the oracle's unsharded model of the same seed, on a
+    # short prompt and PARITY_STEPS greedy steps; rank 0 runs the oracle.
+    pprompt = parity_prompt(cfg, args.seed)
+    ptoks, plogits, pgreedy = gpu_parity_run(eng, pprompt) if not args.no_parity else ([], [], [])
+    ranks_agree = True
+    if dist and ptoks:
+        mine = torch.tensor(ptoks + pgreedy, dtype=torch.int64, device="cuda")
+        allt = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allt, mine)
+        ranks_agree = all(bool((t == mine).all()) for t in allt)
+    parity = orc = om = None
+    if rank == 0 and not args.no_parity:
+        orc, om, obuild_s = oracle_model(cfg, args.quant, args.seed)
+        parity = oracle_parity(orc, om, pprompt, ptoks, plogits, pgreedy)
+        parity.update({"config": f"9B-shape {args.quant}", "prompt_tokens": len(pprompt), "steps": PARITY_STEPS,
+                       "ranks_agree": ranks_agree, "device_error": int(lib.snl_device_error(1)),
+                       "oracle_threads": orc.threads()})
+    if dist:
+        dist.barrier()
     rng = np.random.default_rng(args.seed)  # every rank feeds the same stream
     prompt = rng.integers(0, cfg.vocab, args.prompt).tolist()
 
@@ -397,57 +469,46 @@ def run_ours(args):
         hist[tok] = hist.get(tok, 0) + 1
     e2e_sampled = Es / (time.perf_counter() - t0)
 
-    # Roofline of the dominant kernel: the Q8_0 GEMVs of one decode step, each bracketed by
-    # CUDA events on the engine stream.
+    # One eager decode step op by op, each launch bracketed by CUDA events on the engine
+    # stream (so no launch overlaps its predecessor, unlike the captured step): a per-op
+    # table of time and algorithmic GB/s, reported beside the device-timed step.
     prof = eng.profile(tok)
-    mats = [r for r in prof if r["label"].startswith("mat")]
-    gb = sum(r["bytes"] for r in mats)
-    gms = sum(r["ms"] for r in mats)
     step_ms = sum(r["ms"] for r in prof)
+    ops = [{"op": r["label"], "calls": r["calls"], "ms": round(r["ms"], 4), "share": round(r["ms"] / step_ms, 4),
+            "gbs": round(r["bytes"] / (r["ms"] * 1e6), 1) if r["ms"] > 0 else 0.0}
+           for r in sorted(prof, key=lambda r: -r["ms"])]
     peak, peak_kind = peaks()
-    achieved = gb / (gms * 1e6)
-    n_mat = sum(r["calls"] for r in mats)
-    # ncu traffic of config 1 scaled to this step's average matrix launch (same kernel,
-    # every weight byte read once at every shape).
-    t1 = traffic_from_profiles()
-    traffic = None if t1 is None or n_mat == 0 else (gb / n_mat) * (t1 / CONFIG1_BYTES)
-
     if rank == 0 and args.profile:
         eng.print_profile(prof)
     g1 = None if args.no_gemv else gemv_config1(lib, args.quant)
     # The metric's "GEMV achieved HBM GB/s vs peak" is the config-1 GEMV (BASELINE.json
     # configs[0]): its launches timed back to back with CUDA events on the launching stream.
-    # The decode step's matrix launches, each bracketed by events in one eager step (no
-    # overlap with the previous kernel, so a lower bound), are reported beside it.
-    step_roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": traffic,
-                     "kernel": f"{args.quant.upper()} GEMV (all {n_mat} matrix launches of one decode step, "
-                               f"{gb / 1e9:.2f} GB algorithmic, each timed alone)",
-                     "peak_kind": f"{peak_kind} hbm_gbs (burst)"}
-    roofline = step_roofline
+    # DRAM traffic needs an ncu capture, which this run does not make: null here.
+    roofline = None
     if g1:
         roofline = {"bound": "hbm", "achieved": g1["achieved_gbs"], "peak": peak, "unit": "GB/s",
-                    "frac": g1["achieved_gbs"] / peak,
-                    "traffic": (t1 if t1 is not None and args.quant == "q8_0" else None),
+                    "frac": g1["achieved_gbs"] / peak, "traffic": None,
                     "kernel": f"gemv_pg_kernel, BASELINE configs[0] ({args.quant.upper()} 12288x4096, one token): "
                               f"{g1['bytes_per_launch']} algorithmic bytes per launch / {g1['us_per_launch']:.2f} us "
-                              f"average over 40 back-to-back launches (CUDA events, launching stream)",
+                              f"average over {g1['iters']} back-to-back launches (CUDA events, launching stream)",
                     "peak_kind": f"{peak_kind} hbm_gbs (burst)"}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        quant = {"q8_0": 1, "q4_0": 2}[args.quant]
-        v, n, bs = cpu_decode(cfg, quant, args.cpu_budget_s, 8, warmup=0, seed=args.seed)
-        cpu = {"value": v, "unit": "tok/s", "cores": cores(), "kind": "port",
-               "sample": f"oracle/ (C++ restatement of the WGSL kernels, OpenMP) greedy decode of the same "
-                         f"9B-shape {args.quant} model after a 4-token prompt, {n} tokens timed; KV reads at "
-                         f"2K context are <1% of the 13.9 GB weight stream, so a short context stands in"}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and om is not None:
+        # the oracle model of the parity check, decoding on from where it stopped
+        v, n = oracle_decode(om, orc, parity["tokens_oracle"][-1], 0, 32, args.cpu_budget_s)
+        cpu = {"value": v, "unit": "tok/s", "cores": orc.threads(), "kind": "port",
+               "sample": f"oracle/ (C++ restatement of the WGSL kernels, OpenMP, AVX2) greedy decode of the same "
+                         f"9B-shape {args.quant} model after a {len(pprompt)}-token prompt, {n} tokens timed; KV "
+                         f"reads at 2K context are <1% of the 13.9 GB weight stream, so a short context stands in"}
+    if om is not None:
+        om.close()
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": value / PUBLISHED_DECODE_TOK_S, "dtype": "f32 (int8 weights, fp32 accumulate)",
+            "vs_baseline": value / PUBLISHED_DECODE_TOK_S, "dtype": "int8 weights, x as fp16 hi+lo (~22 bits), fp32 accumulate",
             "data": "synthetic (seeded random-init weights, uniform random prompt ids)",
             "config": {"workload": f"9B-shape {args.quant} greedy decode bs1 after a {args.prompt}-token prefill",
                        "prompt_tokens": args.prompt, "decode_tokens": K, "quant": args.quant, "scales": scale_mode,
@@ -455,7 +516,7 @@ def run_ours(args):
                        "l2": f"inputs larger than L2 ({weight_bytes_per_token(cfg, args.quant) / 1e9:.1f} GB of weights streamed per token)",
                        "parallelism": f"tp{world}" if world > 1 else "single"},
             "roofline": roofline,
-            "roofline_decode_step": step_roofline,
+            "parity": parity,
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4 + 16 + 16, "d2h_bytes_per_step": 4,
                     "api": "snl_engine_forward_greedy"},
             "e2e_sampled": {"value": e2e_sampled, "unit": "tok/s", "d2h_bytes_per_step": 12,
@@ -466,7 +527,7 @@ def run_ours(args):
             "gpu_launches": int(launches),
             "clocks": clk,
             "prefill_tok_s": args.prompt / prefill_s,
-            "step_profile_ms": step_ms,
+            "step_ops_each_timed_alone": {"total_ms": step_ms, "ops": ops},
             "build_s": build_s,
         }
         if g1:

@@ -115,9 +115,12 @@ const char* snl_last_error(void);
 const char* snl_version(void);
 uint64_t snl_launch_count(void);
 
-/* Device error word of the current device: bit 0 = a bounded device-side wait gave up
- * (the kernel returned instead of hanging). Returns the word (>= 0), clearing it when
- * clear != 0, or a negative code. */
+/* Device error word of the current device: bit 0 = a bounded device-side wait on an
+ * asynchronous copy gave up, bit 1 = a tensor-parallel peer did not answer within the
+ * wait bound (the kernel returned instead of hanging). Returns the word (>= 0), clearing
+ * it when clear != 0, or a negative code. The engine calls (forward_mm, forward_greedy,
+ * mtp, generate) read it themselves: a set word makes them fail with SNL_E_TIMEOUT and
+ * clears it. */
 int snl_device_error(int clear);
 
 /* ModelConfig::validate (src/config.rs:194-240). */
@@ -221,7 +224,8 @@ int snl_conv_delta(const snl_step_u* step, const snl_lin_p* p, const float* proj
 /* ---- kernel level: sampling ----------------------------------------------------- */
 
 /* Greedy argmax of each of `rows` rows of `n` logits (sampler.rs:169-177: the first
- * maximum wins); out_idx is a device u32[rows]. */
+ * maximum wins, -0.0 ties with +0.0, NaN never wins except that a row whose element 0
+ * is NaN gives 0, as the reference's scan does); out_idx is a device u32[rows]. */
 int snl_argmax(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_idx, void* stream);
 
 /* snl_argmax for callers that must not allocate device memory when they call it (no
@@ -231,8 +235,10 @@ int snl_argmax(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_idx
  * allocating routine. Its scratch is a static 16 KB device array per GPU, so rows must
  * be <= 16 (SNL_E_RANGE otherwise). The first call on a device looks up that array's
  * address (cudaGetSymbolAddress) with the device current; make that first call before
- * any stream capture. All calls share the array: calls that overlap on the GPU (for
- * example on two streams at once) race and must be serialised by the caller. */
+ * any stream capture. The address is kept for the life of the process, which assumes
+ * one CUDA context per device: do not call it again after cudaDeviceReset. All calls
+ * share the array: calls that overlap on the GPU (for example on two streams at once)
+ * race and must be serialised by the caller. */
 int snl_argmax_noalloc(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_idx, void* stream);
 
 /* SamplingParams (sampler.rs:4-14) without the seed: the host keeps the random number
@@ -299,7 +305,11 @@ int snl_engine_create(const snl_model_config* cfg, size_t ctx, int device, uint3
  *      shard.
  * forward_mm returns the full logits row on every rank; forward_greedy returns the same
  * token on every rank. With tp_size == 1 this is snl_engine_create. MTP is not supported
- * under tensor parallelism (finalize fails with SNL_E_UNSUPPORTED). */
+ * under tensor parallelism (finalize fails with SNL_E_UNSUPPORTED).
+ * Every cross-GPU wait is bounded: 2 s, or SNL_TP_WAIT_MS milliseconds when that
+ * environment variable is set at finalize. When a peer stops taking part, the waiting
+ * rank's call returns SNL_E_TIMEOUT after about one bound (later waits of the device give
+ * up at once); the engines of every rank must then be destroyed and created again. */
 #define SNL_TP_HANDLE_BYTES 64
 /* The shard a rank keeps of one named tensor (what finalize applies): kind
  * SNL_TP_FULL (replicated), SNL_TP_ROWS (the listed row ranges of a matrix, in order),

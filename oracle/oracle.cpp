@@ -19,7 +19,9 @@
 // Transcendentals (exp, log, pow, sin, cos, inverseSqrt) come from the host libm;
 // WGSL leaves their precision to the implementation, so kernels using them are
 // compared within a tolerance.
+#include <immintrin.h>
 #include <math.h>
+#include <omp.h>
 #include <stdint.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -112,6 +114,162 @@ static void matvec_row(int dtype, const uint32_t* w, const float* ws, uint32_t r
   }
 }
 
+// ---- vectorized forms (AVX2), bit-identical to the scalar statements above ----------
+//
+// The scalar functions above are the restatement. The forms below compute the same
+// expression for every output element, with the same operations in the same order
+// (one rounding per multiply and per add; the build disables FMA contraction): the
+// decode form runs 8 of matvec's 32 lanes per AVX register, the prefill form 8 token
+// rows. They only make the checker fast enough for full-size models;
+// orc_set_vector(0) switches back to the scalar statements, and a CPU test checks that
+// both give identical bits.
+static bool g_vector = true;
+ORC_API void orc_set_vector(int on) { g_vector = on != 0; }
+// Threads of the oracle's parallel loops (all host cores by default; torchrun sets
+// OMP_NUM_THREADS=1 in its workers, which a caller timing the CPU baseline undoes here).
+ORC_API void orc_set_threads(int n) {
+  if (n > 0) omp_set_num_threads(n);
+}
+ORC_API int orc_get_threads(void) { return omp_get_max_threads(); }
+
+// Element e of word-vector w as f32: Q8 byte e (sign-extended), or Q4 nibble at `shift`+4e
+// minus 8 (i8x4 / u4x4).
+static inline __m256 q8_elem(__m256i w, int e) {
+  switch (e) {
+    case 0: return _mm256_cvtepi32_ps(_mm256_srai_epi32(_mm256_slli_epi32(w, 24), 24));
+    case 1: return _mm256_cvtepi32_ps(_mm256_srai_epi32(_mm256_slli_epi32(w, 16), 24));
+    case 2: return _mm256_cvtepi32_ps(_mm256_srai_epi32(_mm256_slli_epi32(w, 8), 24));
+    default: return _mm256_cvtepi32_ps(_mm256_srai_epi32(w, 24));
+  }
+}
+static inline __m256 q4_elem(__m256i w, int sh) {
+  const __m256i n = _mm256_and_si256(_mm256_srlv_epi32(w, _mm256_set1_epi32(sh)), _mm256_set1_epi32(15));
+  return _mm256_sub_ps(_mm256_cvtepi32_ps(n), _mm256_set1_ps(8.0f));
+}
+
+// matvec_row for one weight row, lanes 8G..8G+7 of a round at once. xt holds each token's
+// x regrouped by 8-block group: xt[((t * ngrp + g) * 32 + e) * 8 + j] = x_t[(8g + j) * 32 + e].
+static void matvec_row_vec(int dtype, const uint32_t* w, const float* ws, uint32_t row, uint32_t nb,
+                           const float* const* xs, const float* xt, uint32_t ngrp, int m_rows, float* out) {
+  const uint32_t bw = dtype == SNL_Q8_0 ? 8 : 4;
+  alignas(32) float acc[8][32];
+  for (int t = 0; t < m_rows; t++)
+    for (int l = 0; l < 32; l++) acc[t][l] = 0.f;
+  const uint32_t* wr = w + (uint64_t)row * nb * bw;
+  const float* sr = ws + (uint64_t)row * nb;
+  const __m256i lane_words = _mm256_mullo_epi32(_mm256_setr_epi32(0, 1, 2, 3, 4, 5, 6, 7), _mm256_set1_epi32((int)bw));
+  for (uint32_t r0 = 0; r0 < nb; r0 += 32) {
+    for (uint32_t G = 0; G < 4; G++) {
+      const uint32_t b0 = r0 + 8 * G;
+      if (b0 >= nb) break;
+      if (b0 + 8 > nb) {  // partial group: the valid lanes, scalar, in the same order
+        for (uint32_t j = 0; b0 + j < nb; j++) {
+          const uint32_t b = b0 + j;
+          for (int t = 0; t < m_rows; t++)
+            acc[t][8 * G + j] += sr[b] * block_dot(dtype, wr + (uint64_t)b * bw, xs[t] + (uint64_t)b * 32);
+        }
+        continue;
+      }
+      __m256i W[8];
+      for (uint32_t i = 0; i < bw; i++)
+        W[i] = _mm256_i32gather_epi32((const int*)(wr + (uint64_t)b0 * bw + i), lane_words, 4);
+      const __m256 sv = _mm256_loadu_ps(sr + b0);
+      const uint32_t g = b0 / 8;
+      for (int t = 0; t < m_rows; t++) {
+        const float* xg = xt + ((uint64_t)t * ngrp + g) * 32 * 8;
+        __m256 bd = _mm256_setzero_ps();
+        for (int i = 0; i < 8; i++) {
+          __m256 v[4];
+          for (int e = 0; e < 4; e++)
+            v[e] = dtype == SNL_Q8_0 ? q8_elem(W[i], e) : q4_elem(W[i / 2], ((i & 1) ? 16 : 0) + 4 * e);
+          const float* xe = xg + (uint64_t)(4 * i) * 8;
+          __m256 d = _mm256_add_ps(_mm256_mul_ps(v[0], _mm256_loadu_ps(xe)), _mm256_mul_ps(v[1], _mm256_loadu_ps(xe + 8)));
+          d = _mm256_add_ps(d, _mm256_mul_ps(v[2], _mm256_loadu_ps(xe + 16)));
+          d = _mm256_add_ps(d, _mm256_mul_ps(v[3], _mm256_loadu_ps(xe + 24)));
+          bd = i == 0 ? d : _mm256_add_ps(bd, d);
+        }
+        __m256 a = _mm256_load_ps(&acc[t][8 * G]);
+        _mm256_store_ps(&acc[t][8 * G], _mm256_add_ps(a, _mm256_mul_ps(sv, bd)));
+      }
+    }
+  }
+  for (int t = 0; t < m_rows; t++) out[t] = lane_tree(acc[t]);
+}
+
+// The tiled matmul's per-element statement (c = c + w[k] * x[k] for k = 0..K-1, w the
+// dequantized row) for 8 weight rows x 8 token rows per step of k. K is walked in tiles
+// so a tile of every token's x stays in cache; the partial sums carry over between tiles,
+// so each element still sees k in order.
+static void matmul_vec(int dtype, const snl_mat_p* p, uint32_t rows_m, const float* x, const uint32_t* w,
+                       const float* ws, float* y) {
+  const uint32_t K = p->k, N = p->n, nb = K / 32, bw = dtype == SNL_Q8_0 ? 8 : 4;
+  const uint32_t G = rows_m / 8, mv = G * 8;
+  constexpr uint32_t KT = 256, RT = 8;
+  std::vector<float> xT((size_t)G * K * 8);
+#pragma omp parallel for schedule(static)
+  for (int64_t gk = 0; gk < (int64_t)G * K; gk++) {
+    const uint64_t g = (uint64_t)gk / K, k = (uint64_t)gk % K;
+    for (uint32_t j = 0; j < 8; j++) xT[(uint64_t)gk * 8 + j] = x[p->x_off + (g * 8 + j) * p->x_stride + k];
+  }
+  std::vector<float> acc((size_t)N * mv, 0.f);
+  for (uint32_t k0 = 0; k0 < K; k0 += KT) {
+    const uint32_t kt = std::min(KT, K - k0);
+#pragma omp parallel for schedule(static)
+    for (int64_t n0 = 0; n0 < (int64_t)N; n0 += RT) {
+      const uint32_t rt = (uint32_t)std::min<int64_t>(RT, N - n0);
+      alignas(32) float wt[RT][KT];
+      for (uint32_t r = 0; r < RT; r++) {
+        for (uint32_t kk = 0; kk < kt; kk++) {
+          if (r >= rt) {
+            wt[r][kk] = 0.f;
+            continue;
+          }
+          const uint64_t n = n0 + r, k = k0 + kk, b = k / 32;
+          const uint32_t e = (uint32_t)(k % 32), i = e / 4, q = e % 4;
+          const uint32_t* wb = w + (n * nb + b) * bw;
+          float v[4];
+          if (dtype == SNL_Q8_0) i8x4(wb[i], v);
+          else u4x4(wb[i / 2], (i & 1) ? 16u : 0u, v);
+          wt[r][kk] = v[q] * ws[n * nb + b];
+        }
+      }
+      for (uint32_t g = 0; g < G; g++) {
+        __m256 c[RT];
+        for (uint32_t r = 0; r < RT; r++) c[r] = _mm256_loadu_ps(&acc[((uint64_t)n0 + (r < rt ? r : 0)) * mv + g * 8]);
+        const float* xg = &xT[((uint64_t)g * K + k0) * 8];
+        for (uint32_t kk = 0; kk < kt; kk++) {
+          const __m256 xv = _mm256_loadu_ps(xg + (uint64_t)kk * 8);
+          for (uint32_t r = 0; r < RT; r++) c[r] = _mm256_add_ps(c[r], _mm256_mul_ps(_mm256_broadcast_ss(&wt[r][kk]), xv));
+        }
+        for (uint32_t r = 0; r < rt; r++) _mm256_storeu_ps(&acc[((uint64_t)n0 + r) * mv + g * 8], c[r]);
+      }
+    }
+  }
+#pragma omp parallel for schedule(static)
+  for (int64_t n = 0; n < (int64_t)N; n++) {
+    for (uint32_t t = 0; t < mv; t++) y[p->y_off + (uint64_t)t * p->y_stride + p->n_off + n] = acc[(uint64_t)n * mv + t];
+    if (mv == rows_m) continue;
+    // token rows past the last full group of 8: the scalar statement
+    std::vector<float> wrow(K);
+    for (uint32_t b = 0; b < nb; b++) {
+      float s = ws[(uint64_t)n * nb + b];
+      const uint32_t* wb = w + ((uint64_t)n * nb + b) * bw;
+      float v[4];
+      for (int i = 0; i < 8; i++) {
+        if (dtype == SNL_Q8_0) i8x4(wb[i], v);
+        else u4x4(wb[i / 2], (i & 1) ? 16u : 0u, v);
+        for (int e = 0; e < 4; e++) wrow[b * 32 + i * 4 + e] = v[e] * s;
+      }
+    }
+    for (uint32_t m = mv; m < rows_m; m++) {
+      const float* xr = x + p->x_off + (uint64_t)m * p->x_stride;
+      float c = 0.f;
+      for (uint32_t k = 0; k < K; k++) c = c + wrow[k] * xr[k];
+      y[p->y_off + (uint64_t)m * p->y_stride + p->n_off + n] = c;
+    }
+  }
+}
+
 // Kernels::matmul dispatch (gpu.rs:211-218, engine.rs:967-984) and the four kernels.
 ORC_API int orc_mat(int dtype, const snl_step_u* st, const snl_mat_p* p, const float* x, const void* wq,
                     const float* ws, float* y) {
@@ -127,12 +285,31 @@ ORC_API int orc_mat(int dtype, const snl_step_u* st, const snl_mat_p* p, const f
     const int m_rows = (int)std::min<uint32_t>(rows_m, 8);
     const float* xs[8];
     for (int t = 0; t < m_rows; t++) xs[t] = x + p->x_off + (uint64_t)t * p->x_stride;
+    if (g_vector) {
+      const uint32_t ngrp = (nb + 7) / 8;
+      std::vector<float> xt((size_t)m_rows * ngrp * 32 * 8, 0.f);
+      for (int t = 0; t < m_rows; t++)
+        for (uint32_t b = 0; b < nb; b++)
+          for (uint32_t e = 0; e < 32; e++)
+            xt[(((uint64_t)t * ngrp + b / 8) * 32 + e) * 8 + b % 8] = xs[t][(uint64_t)b * 32 + e];
+#pragma omp parallel for schedule(static)
+      for (int64_t row = 0; row < (int64_t)p->n; row++) {
+        float out[8];
+        matvec_row_vec(dtype, w, ws, (uint32_t)row, nb, xs, xt.data(), ngrp, m_rows, out);
+        for (int t = 0; t < m_rows; t++) y[p->y_off + (uint64_t)t * p->y_stride + p->n_off + row] = out[t];
+      }
+      return 0;
+    }
 #pragma omp parallel for schedule(static)
     for (int64_t row = 0; row < (int64_t)p->n; row++) {
       float out[8];
       matvec_row(dtype, w, ws, (uint32_t)row, nb, xs, m_rows, out);
       for (int t = 0; t < m_rows; t++) y[p->y_off + (uint64_t)t * p->y_stride + p->n_off + row] = out[t];
     }
+    return 0;
+  }
+  if (g_vector) {
+    matmul_vec(dtype, p, rows_m, x, w, ws, y);
     return 0;
   }
   // matmul (matmul.wgsl:242-318): dequantize to f32 (dequant8, gpu.rs:265-273 /

@@ -63,6 +63,9 @@ _SIG = {
     "orc_vision_encode": (i32, [vp, vp, sz, sz, sz, vp]),
     "orc_vision_tensor": (i32, [vp, C.c_char_p, P(vp), P(vp), P(sz), P(sz)]),
     "orc_f32_to_f16": (C.c_uint16, [C.c_float]),
+    "orc_set_vector": (None, [i32]),
+    "orc_set_threads": (None, [i32]),
+    "orc_get_threads": (i32, []),
     "orc_f16_to_f32": (C.c_float, [C.c_uint16]),
 }
 
@@ -161,6 +164,21 @@ def sample(params, logits: np.ndarray, hist_tok, hist_cnt, u, draft: int = -1) -
     if rc:
         raise RuntimeError(lib().orc_last_error().decode())
     return int(out[0]), int(out[1]), int(out[2])
+
+
+def set_vector(on: bool) -> None:
+    """AVX2 forms of the matrix kernels (default) or the scalar statements; both give
+    identical bits (tests/test_oracle_kernels.py checks it)."""
+    lib().orc_set_vector(1 if on else 0)
+
+
+def set_threads(n: int) -> None:
+    """Threads of the oracle's OpenMP loops (n <= 0 leaves them as they are)."""
+    lib().orc_set_threads(int(n))
+
+
+def threads() -> int:
+    return int(lib().orc_get_threads())
 
 
 def argmax(v: np.ndarray) -> int:

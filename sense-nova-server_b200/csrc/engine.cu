@@ -124,6 +124,7 @@ struct snl_engine {
   snl_step_u* h_step = nullptr;
   float* h_logits = nullptr;
   uint32_t* h_amax = nullptr;
+  int* h_err = nullptr;  // the device error word, read back with each call's results
 
   size_t pos = 0, hid_rows = 0, head_rows = 1;
   // captured step graphs keyed by (m, head rows, ckpt, greedy)
@@ -627,6 +628,33 @@ int run_step(snl_engine* e, const snl_step_u& sh, uint32_t m, uint32_t rows, boo
   SNL_CUDA_TRY(cudaGraphLaunch(it->second.exec, e->stream));
   count_launch(it->second.launches);
   return SNL_OK;
+}
+
+// Queues the read-back of the device error word behind the call's work on the engine
+// stream; take_device_error() reads it after the stream synchronizes.
+int queue_error_read(snl_engine* e) {
+  if (!e->h_err) return SNL_OK;
+  int* w = nullptr;
+  SNL_TRY(device_error_word(&w));
+  SNL_CUDA_TRY(cudaMemcpyAsync(e->h_err, w, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+  return SNL_OK;
+}
+// After the stream synchronized: a bounded device-side wait that gave up during the call
+// (bit 1: a tensor-parallel peer never answered; bit 0: an asynchronous copy never
+// landed) left the call's results undefined, so the call fails with SNL_E_TIMEOUT. The
+// word is cleared, so the next call starts clean.
+int take_device_error(snl_engine* e) {
+  if (!e->h_err) return SNL_OK;
+  const int v = *e->h_err;
+  if (!v) return SNL_OK;
+  *e->h_err = 0;
+  int* w = nullptr;
+  SNL_TRY(device_error_word(&w));
+  SNL_CUDA_TRY(cudaMemsetAsync(w, 0, sizeof(int), e->stream));
+  SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));
+  return fail(SNL_E_TIMEOUT, (v & 2) ? "a tensor-parallel peer did not answer within the wait bound "
+                                       "(device error word " + std::to_string(v) + "); recreate the engines of every rank"
+                                     : "a device-side wait gave up (device error word " + std::to_string(v) + ")");
 }
 
 int check_tokens(const snl_engine* e, const uint32_t* toks, size_t n) {
@@ -1246,6 +1274,8 @@ extern "C" int snl_engine_finalize(snl_engine* e) {
   SNL_CUDA_TRY(cudaMallocHost(&e->h_step, sizeof(snl_step_u)));
   SNL_CUDA_TRY(cudaMallocHost(&e->h_logits, LOGIT_ROWS * (size_t)c.vocab * sizeof(float)));
   SNL_CUDA_TRY(cudaMallocHost(&e->h_amax, LOGIT_ROWS * sizeof(uint32_t)));
+  SNL_CUDA_TRY(cudaMallocHost(&e->h_err, sizeof(int)));
+  *e->h_err = 0;
   SNL_TRY(dalloc(e, &e->step_ctr, 1));
   e->tp_sites = (uint32_t)(2 * e->plan.size() + 2);
   e->head_out = e->logits;
@@ -1269,6 +1299,10 @@ extern "C" int snl_engine_finalize(snl_engine* e) {
     cm.step = e->step_ctr;
     cm.sites = e->tp_sites;
     cm.err = err;
+    if (const char* ms = getenv("SNL_TP_WAIT_MS")) {
+      const double v = atof(ms);
+      if (v > 0) cm.wait_ns = (unsigned long long)(v * 1e6);
+    }
     e->head_out = cm.logits[e->tp.rank];
   }
   // Weight planes for the prefill GEMM (4 bytes per weight: fp16 hi and lo of each value),
@@ -1316,6 +1350,7 @@ extern "C" void snl_engine_destroy(snl_engine* e) {
     if (e->h_step) cudaFreeHost(e->h_step);
     if (e->h_logits) cudaFreeHost(e->h_logits);
     if (e->h_amax) cudaFreeHost(e->h_amax);
+    if (e->h_err) cudaFreeHost(e->h_err);
     if (e->h_sample_out) cudaFreeHost(e->h_sample_out);
     if (e->sample_scratch) cudaFree(e->sample_scratch);
     if (e->sample_out) cudaFree(e->sample_out);
@@ -1339,11 +1374,15 @@ extern "C" int snl_engine_forward_mm(snl_engine* e, const uint32_t* tokens, size
     const size_t nbytes = rows * e->cfg.vocab * sizeof(float);
     const float* src = e->tp.size > 1 ? e->logits_full : e->head_out;
     SNL_CUDA_TRY(cudaMemcpyAsync(e->h_logits, src, nbytes, cudaMemcpyDeviceToHost, e->stream));
+    SNL_TRY(queue_error_read(e));
     SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    SNL_TRY(take_device_error(e));
     memcpy(logits_out, e->h_logits, nbytes);
   } else {
     // Keep the host from running far ahead of the device (engine.rs:933-934).
+    SNL_TRY(queue_error_read(e));
     SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    SNL_TRY(take_device_error(e));
   }
   return SNL_OK;
 }
@@ -1356,7 +1395,9 @@ extern "C" int snl_engine_forward_greedy(snl_engine* e, const uint32_t* tokens, 
   size_t rows = 0;
   SNL_TRY(forward_impl(e, tokens, n, pos, nullptr, nullptr, 0, logit_rows, ckpt, true, &rows));
   SNL_CUDA_TRY(cudaMemcpyAsync(e->h_amax, e->amax, rows * sizeof(uint32_t), cudaMemcpyDeviceToHost, e->stream));
+  SNL_TRY(queue_error_read(e));
   SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));
+  SNL_TRY(take_device_error(e));
   memcpy(argmax_out, e->h_amax, rows * sizeof(uint32_t));
   return SNL_OK;
 }
@@ -1451,7 +1492,9 @@ extern "C" int snl_engine_mtp(snl_engine* e, size_t r0, const uint32_t* tokens, 
       SNL_TRY(mat_tile(e, st, *find_q(e, "lm_head"), e->xn, h, e->m_logits, c.vocab, 1));
       SNL_TRY(launch_argmax_with(e->m_logits, 1, c.vocab, e->amax, e->amax_part, e->stream));
     }
+    SNL_TRY(queue_error_read(e));
     SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    SNL_TRY(take_device_error(e));
   }
   if (draft && draft_out) {
     SNL_CUDA_TRY(cudaMemcpy(draft_out, e->amax, sizeof(uint32_t), cudaMemcpyDeviceToHost));
@@ -1510,10 +1553,12 @@ extern "C" int snl_engine_generate(snl_engine* e, uint32_t first_token, size_t n
       e->hid_rows = 1;
     }
     cudaEventRecord(t1, e->stream);
+    if (!rc) rc = queue_error_read(e);
     if ((ce = cudaStreamSynchronize(e->stream)) != cudaSuccess) {
       rc = cuda_fail(ce, "generate");
       break;
     }
+    if (!rc) rc = take_device_error(e);
     if (!rc && device_ms) cudaEventElapsedTime(device_ms, t0, t1);
     if (!rc && (ce = cudaMemcpy(out_tokens, gen_d, n * sizeof(uint32_t), cudaMemcpyDeviceToHost)) != cudaSuccess)
       rc = cuda_fail(ce, "generate: read-back");

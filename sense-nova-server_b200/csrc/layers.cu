@@ -335,24 +335,33 @@ __global__ void swiglu_kernel(snl_layer_p p, uint32_t m_rows, const float* __res
 
 // Greedy argmax, two passes. Key = (ordered float bits << 32) | ~index so that the
 // largest key is the largest value with the smallest index (the first maximum, as
-// sampler.rs:169-177). NaN never wins (the reference's `x > v[best]` is false for it).
-__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t i) {
+// sampler.rs:169-177, which starts at best = 0 and moves only on `x > v[best]`). So:
+//   - -0.0 and +0.0 compare equal there and take the key of +0.0 (the first one wins);
+//   - NaN never wins, except at index 0 of the row: with v[0] NaN, `x > v[0]` is false
+//     for every x and the scan returns 0, so that element gets the largest key.
+// `row_start` says whether index 0 of this scan is index 0 of the whole row (false for
+// the vocabulary shards of tensor-parallel ranks other than 0).
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t i, bool row_start) {
   uint32_t b = __float_as_uint(v);
-  if (v != v) b = 0xFF800000u;  // NaN -> -inf
+  if (v != v) {
+    if (row_start && i == 0) return ~0ull;
+    b = 0xFF800000u;  // NaN -> -inf
+  }
+  if (v == 0.f) b = 0u;  // -0.0 -> +0.0
   const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
   return ((unsigned long long)ord << 32) | (unsigned long long)(~i);
 }
 
 constexpr int kArgBlocks = 128;
 __global__ void __launch_bounds__(512) argmax_pass1(const float* __restrict__ v, uint32_t n,
-                                                    unsigned long long* __restrict__ part) {
+                                                    unsigned long long* __restrict__ part, int row_start) {
   pdl_trigger();
   pdl_wait();
   const uint32_t row = blockIdx.y;
   const float* r = v + (uint64_t)row * n;
   unsigned long long best = 0;
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const unsigned long long k = argmax_key(__ldg(r + i), i);
+    const unsigned long long k = argmax_key(__ldg(r + i), i, row_start != 0);
     best = k > best ? k : best;
   }
 #pragma unroll
@@ -575,7 +584,8 @@ static unsigned long long* argmax_scratch(uint32_t rows) {
 int launch_argmax_with(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_idx, unsigned long long* part,
                        cudaStream_t s) {
   if (rows == 0) return SNL_OK;
-  SNL_PDL_LAUNCH("argmax_pass1", argmax_pass1, dim3(dim3(kArgBlocks, rows)), dim3(512), (size_t)(0), s, logits, n, part);
+  SNL_PDL_LAUNCH("argmax_pass1", argmax_pass1, dim3(dim3(kArgBlocks, rows)), dim3(512), (size_t)(0), s, logits, n, part,
+                 1);
   SNL_PDL_LAUNCH("argmax_pass2", argmax_pass2, dim3(rows), dim3(32), (size_t)(0), s, part, kArgBlocks, out_idx);
   return SNL_OK;
 }
@@ -583,7 +593,8 @@ int launch_argmax_with(const float* logits, uint32_t rows, uint32_t n, uint32_t*
 int launch_argmax_tp(const float* logits, uint32_t rows, uint32_t vl, uint32_t* out_idx, unsigned long long* part,
                      const TpComm& c, uint32_t site, cudaStream_t s) {
   if (rows == 0) return SNL_OK;
-  SNL_PDL_LAUNCH("argmax_pass1", argmax_pass1, dim3(dim3(kArgBlocks, rows)), dim3(512), (size_t)(0), s, logits, vl, part);
+  SNL_PDL_LAUNCH("argmax_pass1", argmax_pass1, dim3(dim3(kArgBlocks, rows)), dim3(512), (size_t)(0), s, logits, vl, part,
+                 c.rank == 0 ? 1 : 0);
   SNL_PDL_LAUNCH("argmax_tp_pass2", argmax_tp_pass2, dim3(rows), dim3(32), (size_t)(0), s, part, kArgBlocks, vl, c, site,
                  out_idx);
   return SNL_OK;
@@ -684,6 +695,9 @@ extern "C" int snl_synth_f32(uint64_t seed, const char* name, uint32_t sub, size
 // allocator, or a per-token serving loop that shares the GPU and cannot afford the
 // device-wide wait of a free. Its scratch is this file-scope array, sized for
 // kNoAllocRows rows (16 KB), held by every GPU that loads the library until exit.
+// The array's device address is looked up once per device and kept for the life of the
+// process: that assumes one CUDA context per device, so a caller that destroys and
+// re-creates its context (cudaDeviceReset) must not call this entry point afterwards.
 namespace snl {
 namespace {
 constexpr uint32_t kNoAllocRows = 16;

@@ -17,8 +17,10 @@
 // An exchange at site s of step t uses epoch t * sites + s + 1, so flags only grow and
 // never need resetting. Data buffers alternate by epoch parity: a rank rewrites a buffer
 // two exchanges later, and by then every peer has signalled the exchange in between,
-// which it does only after it has finished reading. Every wait is bounded by clock64;
-// one that runs out sets bit 1 of the device error word and the kernel carries on.
+// which it does only after it has finished reading. Every wait is bounded by the global
+// timer (TpComm::wait_ns, 2 s unless SNL_TP_WAIT_MS says otherwise); one that runs out
+// sets bit 1 of the device error word and the kernel carries on. A wait that finds bit 1
+// already set gives up at once, so a dead peer costs one bound per step, not one per wait.
 #pragma once
 #include <stdint.h>
 
@@ -28,7 +30,7 @@ namespace snl {
 
 constexpr int kTpMax = 8;
 constexpr uint32_t kTpSlots = 1024;  // flag slots per rank
-constexpr long long kTpWaitCycles = 4000000000LL;
+constexpr unsigned long long kTpWaitNs = 2000000000ull;  // default bound of one cross-GPU wait
 
 // Device view of the communicator (passed by value to kernels).
 struct TpComm {
@@ -43,7 +45,16 @@ struct TpComm {
   const unsigned long long* step = nullptr;  // device step counter (this rank)
   uint32_t sites = 1;                        // exchanges per step
   int* err = nullptr;
+  unsigned long long wait_ns = kTpWaitNs;    // bound of every wait, in global-timer ns
 };
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// True once some wait of this device has given up (bit 1 of the error word).
+__device__ __forceinline__ bool tp_gave_up(const TpComm& c) { return (*(volatile const int*)c.err & 2) != 0; }
 
 __device__ __forceinline__ uint64_t tp_epoch(const TpComm& c, uint32_t site) {
   return *(volatile const unsigned long long*)c.step * c.sites + site + 1;
@@ -79,9 +90,11 @@ __device__ __forceinline__ void tp_signal(const TpComm& c, uint32_t slot, uint64
 __device__ __forceinline__ bool tp_wait_one(const TpComm& c, uint32_t slot, int src, uint64_t epoch) {
   const uint64_t* f = c.flags[c.rank] + (uint64_t)slot * kTpMax + src;
   if (ld_acquire_sys(f) >= epoch) return true;
-  const long long t0 = clock64();
+  if (tp_gave_up(c)) return false;
+  const unsigned long long t0 = global_ns();
   while (ld_acquire_sys(f) < epoch) {
-    if (clock64() - t0 > kTpWaitCycles) {
+    if (tp_gave_up(c)) return false;
+    if (global_ns() - t0 > c.wait_ns) {
       atomicOr(c.err, 2);
       return false;
     }
@@ -101,15 +114,18 @@ __device__ __forceinline__ unsigned long long ll_word(uint32_t tag, uint32_t bit
   return ((unsigned long long)tag << 32) | bits;
 }
 // Polls a tagged word of this rank's memory until its tag is `tag`; returns the value
-// bits, or sets bit 1 of the error word and returns 0 when the bound runs out.
+// bits, or sets bit 1 of the error word and returns 0 when the bound runs out (at once
+// when another wait already gave up).
 __device__ __forceinline__ uint32_t ll_wait(const TpComm& c, const unsigned long long* p, uint32_t tag) {
   unsigned long long w = ld_relaxed_sys_u64(p);
   if ((uint32_t)(w >> 32) == tag) return (uint32_t)w;
-  const long long t0 = clock64();
+  if (tp_gave_up(c)) return 0u;
+  const unsigned long long t0 = global_ns();
   for (;;) {
     w = ld_relaxed_sys_u64(p);
     if ((uint32_t)(w >> 32) == tag) return (uint32_t)w;
-    if (clock64() - t0 > kTpWaitCycles) {
+    if (tp_gave_up(c)) return 0u;
+    if (global_ns() - t0 > c.wait_ns) {
       atomicOr(c.err, 2);
       return 0u;
     }

@@ -236,6 +236,73 @@ def test_mtp_draft_matches_oracle(torch_cuda, orc, cfg):
     e.close()
 
 
+def spec_loop(eng, prompt, steps, forced):
+    """The draft-1 / verify-2 loop of worker.rs:197-255 at temperature 0 (as bench.py's
+    MTP workload runs it) on an engine or the oracle. On steps where forced(i, committed)
+    returns a token, that token is verified instead of the MTP head's draft (the head is
+    still run, so its cache advances the same way): with the true greedy continuation
+    this takes the accept branch, which a random-weight head never reaches.
+    Returns [(mtp draft, verified token, accepted, verify logits)], committed tokens."""
+    n = len(prompt)
+    lg = eng.forward(prompt, True)
+    tok = int(np.argmax(lg))
+    eng.mtp(1, prompt[1:], [[i] * 3 for i in range(n - 1)], 0, False)
+    committed, log = [tok], []
+    rope, mtp_in = n, (n, [tok], [[n - 1] * 3], n - 1)
+    for i in range(steps):
+        r0, toks, pos, slot0 = mtp_in
+        d = eng.mtp(r0, toks, pos, slot0, True)
+        f = forced(i, committed)
+        v = d if f is None else f
+        slot = eng.pos
+        lv = eng.forward_mm([tok, v], [[rope] * 3, [rope + 1] * 3], logit_rows=2, ckpt=True)
+        a0, a1 = int(np.argmax(lv[0])), int(np.argmax(lv[1]))
+        ok = a0 == v
+        log.append((d, v, ok, lv))
+        if ok:
+            tok = a1
+            committed += [v, tok]
+            mtp_in = (1, [v, tok], [[rope] * 3, [rope + 1] * 3], slot)
+            rope += 2
+        else:
+            eng.rollback()
+            tok = a0
+            committed.append(tok)
+            mtp_in = (1, [tok], [[rope] * 3], slot)
+            rope += 1
+    return log, committed
+
+
+def test_mtp_accept_and_reject_decisions_match_oracle(torch_cuda, orc, cfg):
+    """Every draft, accept/reject decision, verify row and committed token of 12
+    speculative steps against the oracle. Odd steps verify the true greedy continuation
+    (accept branch: no rollback, both verify rows kept), even steps the MTP head's own
+    draft (reject branch with random weights). The committed text equals plain greedy
+    decoding (MTP on/off identity, README.md:42)."""
+    e, o = pair(orc, cfg, seed=19, mtp=True)
+    prompt = [2, 7, 1, 8, 2, 8, 1, 8, 2, 8]
+    g = orc.OracleModel(cfg, 320, seed=19, quant=1)
+    greedy = [int(np.argmax(g.forward(prompt, True)))]
+    for _ in range(40):
+        greedy.append(int(np.argmax(g.forward([greedy[-1]], True))))
+    g.close()
+
+    def forced(i, committed):
+        return greedy[len(committed)] if i % 2 == 1 else None
+
+    le, ce = spec_loop(e, prompt, 12, forced)
+    lo, co = spec_loop(o, prompt, 12, forced)
+    assert [x[0] for x in le] == [x[0] for x in lo]  # MTP drafts
+    assert [x[1] for x in le] == [x[1] for x in lo]  # verified tokens
+    assert [x[2] for x in le] == [x[2] for x in lo]  # accept / reject decisions
+    assert any(x[2] for x in le) and not all(x[2] for x in le)  # both branches taken
+    for (_, _, _, a), (_, _, _, b) in zip(le, lo):
+        assert rel(a, b) < TOL
+    assert ce == co == greedy[: len(ce)]
+    assert e.pos == o.pos
+    e.close()
+
+
 def test_snl_file_roundtrip(torch_cuda, orc, cfg, tmp_path):
     """Engine.load of a .snl file (weights.rs layout) == the same weights generated in place."""
     from sensenova_b200.weights import write_snl

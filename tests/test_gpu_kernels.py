@@ -352,6 +352,30 @@ def test_argmax_exact(T, lib, orc, n):
     assert list(got) == [orc.argmax(v[0]), orc.argmax(v[1])]
 
 
+def argmax_edge_rows(n=4096):
+    """Rows where the reference's scan (best = 0, move on x > v[best]) differs from a naive
+    ordering of floats: -0.0 tied with +0.0, NaN at index 0, NaN elsewhere, all -inf."""
+    rows = np.full((6, n), -1.0, np.float32)
+    rows[0, 5], rows[0, 9] = -0.0, 0.0      # -0.0 first, +0.0 later: index 5 wins
+    rows[1, 5], rows[1, 9] = 0.0, -0.0      # +0.0 first: index 5 wins
+    rows[2, 0], rows[2, 7] = np.nan, 3.0    # NaN at index 0: the scan never moves, 0
+    rows[3, 3], rows[3, 8] = np.nan, 2.0    # NaN elsewhere never wins: 8
+    rows[4, :] = -np.inf                    # all equal: 0
+    rows[5, :] = np.nan                     # all NaN: 0
+    return rows
+
+
+@pytest.mark.parametrize("entry", ["snl_argmax", "snl_argmax_noalloc"])
+def test_argmax_edge_cases(T, lib, orc, entry):
+    v = argmax_edge_rows()
+    want = [orc.argmax(r) for r in v]
+    assert want == [5, 5, 0, 8, 0, 0]
+    out = T.zeros(len(v), dtype=T.int32, device="cuda")
+    call(getattr(lib, entry)(ptr(dev(T, v)), len(v), v.shape[1], ptr(out), None))
+    T.cuda.synchronize()
+    assert list(host(out).view(np.uint32)) == want
+
+
 # ---- attention.wgsl -------------------------------------------------------------------
 
 
@@ -470,6 +494,47 @@ def test_conv_delta_fused(T, lib, orc, m, ckpt):
     if ckpt:
         assert np.array_equal(host(cck), cck_ref)
         assert rel(host(sck), sck_ref) < TOL
+
+
+@pytest.mark.slow
+def test_deltanet_config2_full_length(T, lib, orc):
+    """BASELINE.json configs[1] at its full length: one Gated DeltaNet layer (16 QK / 32 V
+    heads of 128) over a 4096-token prefill in 8 chained 512-row steps (the chunked form,
+    chunks of 64), then 256 single-token steps (the recurrent form), each carrying the
+    conv and delta states of the step before. Inputs as the config states: q, k, v, b, a,
+    z ~ N(0,1), A_log = dt_bias = 0 (so g = -softplus(a)), conv weights N(0, 0.5), norm
+    weight 1. The oracle runs the reference's token-sequential conv + delta over the same
+    steps: every step's output rows and the state after each step within 1e-3, the conv
+    state bit-exact."""
+    n_k, n_v, D = 16, 32, 128
+    cd = 2 * n_k * D + n_v * D
+    stride = cd + n_v * D + 2 * n_v
+    lpp = LinP(cd, stride, n_k, n_v, 1e-6, (0, 0, 0))
+    P, R, chunk = 4096, 256, 512
+    rng = np.random.default_rng(2024)
+    proj = rng.standard_normal((P + R, stride)).astype(np.float32)
+    lw = np.concatenate([np.sqrt(0.5) * rng.standard_normal(cd * 4), np.zeros(2 * n_v), np.ones(D)]).astype(np.float32)
+    cs_h, S_h = np.zeros((3, cd), np.float32), np.zeros((n_v, D, D), np.float32)
+    dproj, dlw = dev(T, proj), dev(T, lw)
+    cs_d, S_d = T.zeros((3, cd), device="cuda"), T.zeros((n_v, D, D), device="cuda")
+    out_d = T.zeros((P + R, n_v * D), device="cuda")
+    steps = [(r0, chunk) for r0 in range(0, P, chunk)] + [(P + i, 1) for i in range(R)]
+    worst_out, worst_state = 0.0, 0.0
+    out_ref = np.zeros((P + R, n_v * D), np.float32)
+    for i, (r0, m) in enumerate(steps):
+        st = StepU(m, r0, 1, 0)
+        conv_out = np.zeros((m, cd), np.float32)
+        orc.conv(st, lpp, proj[r0:r0 + m], conv_out, cs_h, lw, np.zeros((3, cd), np.float32))
+        orc.delta(st, lpp, proj[r0:r0 + m], conv_out, S_h, lw, out_ref[r0:r0 + m], np.zeros_like(S_h))
+        call(lib.snl_conv_delta(C.byref(st), C.byref(lpp), C.c_void_p(dproj.data_ptr() + 4 * r0 * stride), ptr(cs_d),
+                                ptr(S_d), ptr(dlw), C.c_void_p(out_d.data_ptr() + 4 * r0 * n_v * D), None, None, None))
+        if m > 1 or i == len(steps) - 1 or (r0 - P) % 32 == 31:
+            worst_out = max(worst_out, rel(host(out_d[r0:r0 + m]), out_ref[r0:r0 + m]))
+            worst_state = max(worst_state, rel(host(S_d), S_h))
+            assert np.array_equal(host(cs_d), cs_h), (r0, m)
+    assert worst_out < TOL, worst_out
+    assert worst_state < TOL, worst_state
+    assert rel(host(out_d), out_ref) < TOL
 
 
 @pytest.mark.parametrize("m,ckpt", [(1, 0), (2, 1), (24, 0)])

@@ -94,6 +94,30 @@ def test_mat_vs_float64(orc, dtype, m):
     assert err < 2e-6, err
 
 
+@pytest.mark.parametrize("dtype", [SNL_Q8_0, SNL_Q4_0])
+@pytest.mark.parametrize("m,n,k", [(1, 67, 4096), (2, 40, 96), (3, 33, 1056), (8, 24, 800), (9, 37, 288),
+                                   (17, 19, 512), (40, 21, 320)])
+def test_mat_vector_forms_bit_identical(orc, dtype, m, n, k):
+    """The AVX2 forms of the oracle's matvec/matmul give the scalar statements' bits:
+    block counts that are not multiples of 8 or 32 (partial lane groups), token counts
+    with a ragged last group of 8, strided x/y with offsets."""
+    rng = np.random.default_rng(m * 1000 + k + dtype)
+    q, s = orc.gen_quant(11, f"v{dtype}", dtype, n, k)
+    xs = k + 5
+    x = rng.standard_normal(3 + m * xs).astype(np.float32)
+    p = MatP(n, k, 3, xs, 2, n + 4, 1, 0)
+    ys = []
+    for vec in (False, True):
+        y = np.full(2 + m * (n + 4), np.nan, dtype=np.float32)
+        orc.set_vector(vec)
+        try:
+            orc.mat(dtype, StepU(m, 0, 1, 0), p, x, q, s, y)
+        finally:
+            orc.set_vector(True)
+        ys.append(y)
+    assert np.array_equal(ys[0].view(np.uint32), ys[1].view(np.uint32))
+
+
 def test_mat_offsets_and_m_one(orc):
     # The head's use of MatP (engine.rs:835-842): x_off picks the last rows, m_one fixes the count.
     rng = np.random.default_rng(3)
