@@ -169,20 +169,20 @@ int snl_mat_tiles(int dtype, const snl_mat_p* p, uint32_t rows_m, const void* pl
 
 /* ---- kernel level: layers.wgsl ------------------------------------------------- */
 
-/* branch_norm (layers.wgsl:186-213): n_groups workgroups (step->m, or 1 for the
+/* branch_norm (layers.wgsl:49-76): n_groups workgroups (step->m, or 1 for the
  * final-row norm). x, coef, w, out as the WGSL bindings. */
 int snl_branch_norm(const snl_step_u* step, const snl_layer_p* p, const float* x, const float* coef,
                     const float* w, float* out, uint32_t n_groups, void* stream);
-/* mhc_dots (layers.wgsl:215-232): grid (9, step->m); writes raw[m*9 + o]. */
+/* mhc_dots (layers.wgsl:78-95): grid (9, step->m); writes raw[m*9 + o]. */
 int snl_mhc_dots(const snl_step_u* step, const snl_layer_p* p, const float* x, const float* w,
                  float* raw, void* stream);
-/* mhc_finish (layers.wgsl:234-266): coef[m*8 + 0..8] from raw and the router bias. */
+/* mhc_finish (layers.wgsl:97-132): coef[m*8 + 0..8] from raw and the router bias. */
 int snl_mhc_finish(const snl_step_u* step, const snl_layer_p* p, const float* raw, const float* w,
                    float* coef, void* stream);
-/* merge (layers.wgsl:268-302): width = h; modes 0..3. */
+/* merge (layers.wgsl:134-164): width = h; modes 0..3. */
 int snl_merge(const snl_step_u* step, const snl_layer_p* p, float* x, const float* coef,
               const float* branch, void* stream);
-/* swiglu (layers.wgsl:304-315): act[m, i] = silu(gate_up[m, i]) * gate_up[m, I + i]. */
+/* swiglu (layers.wgsl:166-175): act[m, i] = silu(gate_up[m, i]) * gate_up[m, I + i]. */
 int snl_swiglu(const snl_step_u* step, const snl_layer_p* p, const float* gate_up, float* act,
                void* stream);
 

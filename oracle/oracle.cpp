@@ -341,14 +341,14 @@ ORC_API int orc_mat(int dtype, const snl_step_u* st, const snl_mat_p* p, const f
 // layers.wgsl
 // ---------------------------------------------------------------------------
 
-// reduce_sum (layers.wgsl:174-184): 256-lane tree.
+// reduce_sum (layers.wgsl:34-47): 256-lane tree.
 static inline float tree256(float* red) {
   for (int s = 128; s > 0; s >>= 1)
     for (int l = 0; l < s; l++) red[l] += red[l + s];
   return red[0];
 }
 
-// branch_norm (layers.wgsl:186-213).
+// branch_norm (layers.wgsl:49-76).
 ORC_API int orc_branch_norm(const snl_step_u* st, const snl_layer_p* p, const float* x, const float* coef,
                             const float* w, float* out, uint32_t n_groups) {
   for (uint32_t g = 0; g < n_groups; g++) {
@@ -381,7 +381,7 @@ ORC_API int orc_branch_norm(const snl_step_u* st, const snl_layer_p* p, const fl
   return 0;
 }
 
-// mhc_dots (layers.wgsl:215-232).
+// mhc_dots (layers.wgsl:78-95).
 ORC_API int orc_mhc_dots(const snl_step_u* st, const snl_layer_p* p, const float* x, const float* w, float* raw) {
   uint32_t d = 2 * p->h;
   for (uint32_t m = 0; m < st->m; m++) {
@@ -411,7 +411,7 @@ static inline float lse2(float a, float b) {
   return mx + logf(expf(a - mx) + expf(b - mx));
 }
 
-// mhc_finish (layers.wgsl:234-266).
+// mhc_finish (layers.wgsl:97-132).
 ORC_API int orc_mhc_finish(const snl_step_u* st, const snl_layer_p* p, const float* raw, const float* w,
                            float* coef) {
   uint32_t d = 2 * p->h;
@@ -445,7 +445,7 @@ ORC_API int orc_mhc_finish(const snl_step_u* st, const snl_layer_p* p, const flo
   return 0;
 }
 
-// merge (layers.wgsl:268-302).
+// merge (layers.wgsl:134-164).
 ORC_API int orc_merge(const snl_step_u* st, const snl_layer_p* p, float* x, const float* coef, const float* br) {
   uint64_t total = (uint64_t)st->m * p->h;
   for (uint64_t idx = 0; idx < total; idx++) {
@@ -473,7 +473,7 @@ ORC_API int orc_merge(const snl_step_u* st, const snl_layer_p* p, float* x, cons
   return 0;
 }
 
-// swiglu (layers.wgsl:304-315).
+// swiglu (layers.wgsl:166-175).
 ORC_API int orc_swiglu(const snl_step_u* st, const snl_layer_p* p, const float* gu, float* act) {
   uint64_t total = (uint64_t)st->m * p->inter;
   for (uint64_t idx = 0; idx < total; idx++) {

@@ -21,7 +21,7 @@ __device__ __forceinline__ void xplane_store(__half* planes, uint32_t plane_stri
 
 // Epilogue of one output element (token t, output row n):
 //   mode 0: y[y_off + t*y_stride + n_off + n] = v
-//   mode 1: residual merge into x [t, 2H] (layers.wgsl:268-302 `merge` mode `merge_mode`),
+//   mode 1: residual merge into x [t, 2H] (layers.wgsl:134-164 `merge` mode `merge_mode`),
 //           then optionally copy stream 0 into stream 1 (`expand`, merge mode 3).
 //   mode 2: SwiGLU of gate/up row pairs (tile GEMV only, see group_finish).
 struct GemvArgs {

@@ -13,7 +13,7 @@
 namespace snl {
 namespace {
 
-// branch_norm (layers.wgsl:186-213): one CTA per output row.
+// branch_norm (layers.wgsl:49-76): one CTA per output row.
 // Generic form (any h): strided loops.
 __global__ void __launch_bounds__(256) branch_norm_loop_kernel(StepRef sr, snl_layer_p p, const float* __restrict__ x,
                                                                const float* __restrict__ coef, const float* __restrict__ w,
@@ -167,7 +167,7 @@ __global__ void __launch_bounds__(256) branch_norm_kernel(StepRef sr, snl_layer_
   }
 }
 
-// The 9 router sums of mhc_dots (layers.wgsl:215-232) for one token, in one pass
+// The 9 router sums of mhc_dots (layers.wgsl:78-95) for one token, in one pass
 // over its two streams.
 __device__ __forceinline__ void mhc_sums(const float* __restrict__ x, const float* __restrict__ w, uint32_t d,
                                          float out9[9], float* sh) {
@@ -272,7 +272,7 @@ __global__ void mhc_coef_kernel(snl_layer_p p, uint32_t m_rows, const float* __r
   if (lane == 0) mhc_coef(r, w, 2 * p.h, p.iterations, coef + m * 8);
 }
 
-// merge (layers.wgsl:268-302).
+// merge (layers.wgsl:134-164).
 // Row blockIdx.y, four consecutive elements per thread (H is a multiple of 4).
 __global__ void merge_kernel(snl_layer_p p, uint32_t m_rows, float* __restrict__ x, const float* __restrict__ coef,
                              const float* __restrict__ br) {
@@ -313,7 +313,7 @@ __global__ void merge_kernel(snl_layer_p p, uint32_t m_rows, float* __restrict__
   }
 }
 
-// swiglu (layers.wgsl:304-315).
+// swiglu (layers.wgsl:166-175).
 // Row blockIdx.y, four consecutive outputs per thread (the FFN width is a multiple of 4).
 __global__ void swiglu_kernel(snl_layer_p p, uint32_t m_rows, const float* __restrict__ gu, float* __restrict__ act,
                               XOut xo) {

@@ -1,4 +1,4 @@
-// The mHC router's finish (layers.wgsl:234-266, `mhc_finish`) for one token: shared by
+// The mHC router's finish (layers.wgsl:97-132, `mhc_finish`) for one token: shared by
 // the norm kernel (layers.cu) and the tile GEMV's fused-norm prologue (gemv_mma.cu).
 #pragma once
 #include "common.cuh"
@@ -10,7 +10,7 @@ __device__ __forceinline__ float lse2(float a, float b) {
   return mx + __logf(__expf(a - mx) + __expf(b - mx));
 }
 
-// mhc_finish (layers.wgsl:234-266) for one token, with the 8 router biases given.
+// mhc_finish (layers.wgsl:97-132) for one token, with the 8 router biases given.
 // The Sinkhorn normalisation of the 2x2 mixing matrix runs on exp(logits - max), where
 // each half-step is a sum, one reciprocal and two products (the same iterates as the
 // log-domain form, without a log per step); if any row or column sum underflows, it is

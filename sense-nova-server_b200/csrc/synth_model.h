@@ -59,7 +59,7 @@ void for_each_tensor(const snl_model_config& c, bool mtp, int quant, Q&& qf, V&&
       qf(L + "out_proj", quant, h, lin_value_dim(c));
     }
     if (is_mhc(c, i)) {
-      // router weight [8, 2H] then bias [8] (convert.rs:260-272, layers.wgsl:215-217)
+      // router weight [8, 2H] then bias [8] (convert.rs:260-272, layers.wgsl:78-86)
       Seg mh[2] = {{0, 8 * 2 * h, 0.02f, 0.f}, {1, 8, 0.1f, 0.f}};
       vf(L + "mhc_attn", mh, 2);
       vf(L + "mhc_ffn", mh, 2);
