@@ -385,26 +385,6 @@ def run_ours(args):
     scale_mode = f"tile layout: {n16} matrices with fp16 block scales, {n32} with f32"
     build_s = time.perf_counter() - t0
 
-    # Parity on this configuration before anything is timed: the engine (every rank under
-    # tensor parallelism) against the oracle's unsharded model of the same seed, on a
-    # short prompt and PARITY_STEPS greedy steps; rank 0 runs the oracle.
-    pprompt = parity_prompt(cfg, args.seed)
-    ptoks, plogits, pgreedy = gpu_parity_run(eng, pprompt) if not args.no_parity else ([], [], [])
-    ranks_agree = True
-    if dist and ptoks:
-        mine = torch.tensor(ptoks + pgreedy, dtype=torch.int64, device="cuda")
-        allt = [torch.empty_like(mine) for _ in range(world)]
-        dist.all_gather(allt, mine)
-        ranks_agree = all(bool((t == mine).all()) for t in allt)
-    parity = orc = om = None
-    if rank == 0 and not args.no_parity:
-        orc, om, obuild_s = oracle_model(cfg, args.quant, args.seed)
-        parity = oracle_parity(orc, om, pprompt, ptoks, plogits, pgreedy)
-        parity.update({"config": f"9B-shape {args.quant}", "prompt_tokens": len(pprompt), "steps": PARITY_STEPS,
-                       "ranks_agree": ranks_agree, "device_error": int(lib.snl_device_error(1)),
-                       "oracle_threads": orc.threads()})
-    if dist:
-        dist.barrier()
     rng = np.random.default_rng(args.seed)  # every rank feeds the same stream
     prompt = rng.integers(0, cfg.vocab, args.prompt).tolist()
 
@@ -493,6 +473,27 @@ def run_ours(args):
                               f"average over {g1['iters']} back-to-back launches (CUDA events, launching stream)",
                     "peak_kind": f"{peak_kind} hbm_gbs (burst)"}
 
+    # Parity on this configuration, after the timed legs (the CPU oracle runs only now): the
+    # engine (every rank under tensor parallelism), reset, against the oracle's unsharded
+    # model of the same seed, on a short prompt and PARITY_STEPS greedy steps; rank 0 runs
+    # the oracle.
+    pprompt = parity_prompt(cfg, args.seed)
+    ptoks, plogits, pgreedy = gpu_parity_run(eng, pprompt) if not args.no_parity else ([], [], [])
+    ranks_agree = True
+    if dist and ptoks:
+        mine = torch.tensor(ptoks + pgreedy, dtype=torch.int64, device="cuda")
+        allt = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allt, mine)
+        ranks_agree = all(bool((t == mine).all()) for t in allt)
+    parity = orc = om = None
+    if rank == 0 and not args.no_parity:
+        orc, om, obuild_s = oracle_model(cfg, args.quant, args.seed)
+        parity = oracle_parity(orc, om, pprompt, ptoks, plogits, pgreedy)
+        parity.update({"config": f"9B-shape {args.quant}", "prompt_tokens": len(pprompt), "steps": PARITY_STEPS,
+                       "ranks_agree": ranks_agree, "device_error": int(lib.snl_device_error(1)),
+                       "oracle_threads": orc.threads()})
+    if dist:
+        dist.barrier()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and om is not None:
         # the oracle model of the parity check, decoding on from where it stopped

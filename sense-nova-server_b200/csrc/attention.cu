@@ -161,13 +161,21 @@ __global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, c
   const uint64_t kbase = (uint64_t)kh * HD;  // in halves
   for (uint32_t t0 = start + warp * kKeysPerGroup; t0 < end; t0 += kAttWarps * kKeysPerGroup) {
     const uint32_t nk = min((uint32_t)kKeysPerGroup, end - t0);
+    // The group's K and V rows are all loaded here, before the scores: the V loads do not
+    // wait for the softmax, so the group costs one memory latency instead of nine. Rows past
+    // the part's end repeat its last key and get weight 0.
+    uint4 kw[kKeysPerGroup], vw[kKeysPerGroup];
+#pragma unroll
+    for (int j = 0; j < kKeysPerGroup; j++) {
+      const uint64_t row = ((uint64_t)(t0 + min((uint32_t)j, nk - 1)) * kv_dim + kbase) / 2 + lane * 4;
+      kw[j] = *reinterpret_cast<const uint4*>(kc + row);
+      vw[j] = *reinterpret_cast<const uint4*>(vc + row);
+    }
     float part_s[32];
 #pragma unroll
     for (int j = 0; j < kKeysPerGroup; j++) {
-      const uint32_t t = t0 + min((uint32_t)j, nk - 1);
-      const uint4 w = *reinterpret_cast<const uint4*>(kc + ((uint64_t)t * kv_dim + kbase) / 2 + lane * 4);
       float k8[8];
-      h8_to_f(w, k8);
+      h8_to_f(kw[j], k8);
 #pragma unroll
       for (int g = 0; g < (int)G; g++) {
         float s = 0.f;
@@ -201,10 +209,10 @@ __global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, c
     for (int g = 0; g < (int)G; g++)
 #pragma unroll
       for (int e = 0; e < 8; e++) acc[g][e] *= cg[g];
-    for (uint32_t j = 0; j < nk; j++) {
-      const uint4 w = *reinterpret_cast<const uint4*>(vc + ((uint64_t)(t0 + j) * kv_dim + kbase) / 2 + lane * 4);
+#pragma unroll
+    for (int j = 0; j < kKeysPerGroup; j++) {
       float v8[8];
-      h8_to_f(w, v8);
+      h8_to_f(vw[j], v8);
       const float4 pj = *reinterpret_cast<const float4*>(&s_p[warp][j * 4]);
       const float pg[G] = {pj.x, pj.y, pj.z, pj.w};
 #pragma unroll
@@ -256,7 +264,11 @@ __global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, c
   }
 }
 
-// combine: CTA (head, token), thread = head dim.
+// combine: CTA (head, token), thread = head dim. The parts' maxima and weights are
+// loaded by all threads at once (one part per thread, 256 parts per round) instead of
+// one after another by every thread; each thread then adds its dim over the parts in
+// part order with 16 loads in flight, and the softmax denominator is added in part order
+// from shared memory, so the sums are the sequential ones of attention.wgsl:248-269.
 // skip_single: the step's attend already wrote `out` (parts == 1); used by captured
 // graphs, whose launch list is fixed while parts changes between replays.
 __global__ void __launch_bounds__(256) combine_kernel(StepRef sr, snl_attn_p p, const float* __restrict__ proj,
@@ -264,19 +276,41 @@ __global__ void __launch_bounds__(256) combine_kernel(StepRef sr, snl_attn_p p, 
                                                       int skip_single, XOut xo) {
   pdl_trigger();
   pdl_wait();
+  __shared__ float s_w[HD], s_l[HD], s_red[HD / 32];
   const snl_step_u st = load_step(sr);
   const uint32_t h = blockIdx.x, m = blockIdx.y, d = threadIdx.x;
   if (m >= st.m || (skip_single && st.parts <= 1)) return;
-  const uint32_t q_dim = p.n_heads * HD;
-  const uint64_t base = ((uint64_t)m * p.n_heads + h) * st.parts;
+  const uint32_t q_dim = p.n_heads * HD, parts = st.parts;
+  const uint64_t base = ((uint64_t)m * p.n_heads + h) * parts;
   float mx = -1e30f;
-  for (uint32_t i = 0; i < st.parts; i++) mx = fmaxf(mx, partial[(base + i) * (HD + 2) + HD]);
+  for (uint32_t i = d; i < parts; i += HD) mx = fmaxf(mx, partial[(base + i) * (HD + 2) + HD]);
+  mx = warp_max(mx);
+  if ((d & 31) == 0) s_red[d >> 5] = mx;
+  __syncthreads();
+#pragma unroll
+  for (uint32_t w = 0; w < HD / 32; w++) mx = fmaxf(mx, s_red[w]);
   float l = 0.f, acc = 0.f;
-  for (uint32_t i = 0; i < st.parts; i++) {
-    const uint64_t o = (base + i) * (HD + 2);
-    const float f = __expf(partial[o + HD] - mx);
-    l = fmaf(partial[o + HD + 1], f, l);
-    acc = fmaf(partial[o + d], f, acc);
+  for (uint32_t c0 = 0; c0 < parts; c0 += HD) {
+    const uint32_t n = min(HD, parts - c0);
+    __syncthreads();  // the previous round's weights are read
+    if (d < n) {
+      const uint64_t o = (base + c0 + d) * (HD + 2);
+      s_w[d] = __expf(partial[o + HD] - mx);
+      s_l[d] = partial[o + HD + 1];
+    } else {
+      s_w[d] = 0.f;  // parts past n add 0 (their loads below repeat the last part)
+    }
+    __syncthreads();
+    const float* col = partial + (base + c0) * (HD + 2) + d;
+    // 16 parts' loads in flight at a time (their L2 latency is paid once per 16 parts).
+    for (uint32_t j0 = 0; j0 < n; j0 += 16) {
+      float v[16];
+#pragma unroll
+      for (int u = 0; u < 16; u++) v[u] = col[(uint64_t)min(j0 + u, n - 1) * (HD + 2)];
+#pragma unroll
+      for (int u = 0; u < 16; u++) acc = fmaf(v[u], s_w[j0 + u], acc);
+    }
+    for (uint32_t i = 0; i < n; i++) l = fmaf(s_l[i], s_w[i], l);
   }
   const float gate = proj[(uint64_t)m * p.proj_stride + h * 2 * HD + HD + d];
   const float o = acc / l / (1.0f + __expf(-gate));

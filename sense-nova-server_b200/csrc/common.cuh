@@ -40,6 +40,10 @@ void count_launch(uint64_t n = 1);
 // A step descriptor passed to kernels: either by value (kernel-level C ABI) or
 // through a device pointer (engine graphs, where pos0/parts change between replays
 // while the captured launch stays the same, like the reference's `step` uniform).
+// A graph is captured per (rows, checkpoint) pair, so m and ckpt of the device copy
+// always equal those of the host copy passed by value: kernels take them from the
+// argument and read only pos0 and parts from device memory, so a kernel's loop over the
+// step's rows does not wait for that load.
 struct StepRef {
   const snl_step_u* dev;
   snl_step_u val;
@@ -47,10 +51,10 @@ struct StepRef {
 __device__ __forceinline__ snl_step_u load_step(const StepRef& s) {
   if (s.dev) {
     snl_step_u v;
-    v.m = s.dev->m;
+    v.m = s.val.m;
+    v.ckpt = s.val.ckpt;
     v.pos0 = s.dev->pos0;
     v.parts = s.dev->parts;
-    v.ckpt = s.dev->ckpt;
     return v;
   }
   return s.val;

@@ -443,17 +443,32 @@ __global__ void embed_kernel(const uint32_t* __restrict__ toks, uint32_t h, uint
                              int* __restrict__ err, unsigned long long* __restrict__ step_ctr) {
   pdl_trigger();
   pdl_wait();
-  const uint32_t m = blockIdx.x;
+  const uint32_t m = blockIdx.y;
   // The embedding is the first kernel of every step: it advances the step counter that
   // numbers the step's tensor-parallel exchanges.
-  if (step_ctr && m == 0 && threadIdx.x == 0) *step_ctr += 1;
+  if (step_ctr && m == 0 && blockIdx.x == 0 && threadIdx.x == 0) *step_ctr += 1;
   const uint32_t t = toks[m];
   const bool ok = t < vocab;
   if (!ok && threadIdx.x == 0 && err) *err = 1;
-  for (uint32_t i = threadIdx.x; i < h; i += blockDim.x) {
-    const float v = ok ? (float)q[(uint64_t)t * h + i] * s[((uint64_t)t * h + i) / 32] : 0.f;
-    x[(uint64_t)m * 2 * h + i] = v;
-    x[(uint64_t)m * 2 * h + h + i] = 0.f;
+  // CTA x covers elements [1024 x, 1024 x + 1024) of the row, four per thread.
+  const uint32_t i = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (i >= h) return;
+  float* x0 = x + (uint64_t)m * 2 * h;
+  if (h % 4 == 0) {
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (ok) {
+      const uint64_t e = (uint64_t)t * h + i;
+      const char4 c = *reinterpret_cast<const char4*>(q + e);
+      const float sc = s[e / 32];
+      v = make_float4((float)c.x * sc, (float)c.y * sc, (float)c.z * sc, (float)c.w * sc);
+    }
+    *reinterpret_cast<float4*>(x0 + i) = v;
+    *reinterpret_cast<float4*>(x0 + h + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+    return;
+  }
+  for (uint32_t j = i; j < min(h, i + 4); j++) {
+    x0[j] = ok ? (float)q[(uint64_t)t * h + j] * s[((uint64_t)t * h + j) / 32] : 0.f;
+    x0[h + j] = 0.f;
   }
 }
 
@@ -609,8 +624,8 @@ int launch_argmax(const float* logits, uint32_t rows, uint32_t n, uint32_t* out_
 int launch_embed(const uint32_t* tokens, uint32_t m, const int8_t* q, const float* s_, uint32_t h, uint32_t vocab,
                  float* x, int* err_flag, cudaStream_t s, unsigned long long* step_ctr) {
   if (m == 0) return SNL_OK;
-  SNL_PDL_LAUNCH("embed_kernel", embed_kernel, dim3(m), dim3(256), (size_t)(0), s, tokens, h, vocab, q, s_, x, err_flag,
-                 step_ctr);
+  SNL_PDL_LAUNCH("embed_kernel", embed_kernel, dim3((h + 1023) / 1024, m), dim3(256), (size_t)(0), s, tokens, h, vocab, q,
+                 s_, x, err_flag, step_ctr);
   return SNL_OK;
 }
 
