@@ -26,11 +26,26 @@ __global__ void __launch_bounds__(256) prep_kernel(StepRef sr, snl_attn_p p, con
                                                    uint32_t* __restrict__ vc, const float* __restrict__ norms,
                                                    const uint32_t* __restrict__ rpos) {
   pdl_trigger();
-  pdl_wait();
   __shared__ float sh[HD];
   __shared__ float red[32];
   const snl_step_u st = load_step(sr);
   const uint32_t slot = blockIdx.x, m = blockIdx.y, d = threadIdx.x;
+  // Before the wait: the norm weight and this dim's rotation, whose positions the host
+  // wrote before the step (the projection is the only input an earlier kernel writes).
+  const bool is_q = slot < p.n_heads;
+  const uint32_t half_rot = p.rot_dim / 2;
+  const float nw = slot < p.n_heads + p.n_kv ? 1.0f + norms[(is_q ? 0 : HD) + d] : 0.f;
+  float sn = 0.f, cs = 1.f;
+  if (d < p.rot_dim && m < st.m) {
+    const uint32_t fi = d % half_rot;
+    const float inv_freq = powf(p.rope_theta, -(float)(2 * fi) / (float)p.rot_dim);
+    const uint32_t* rp = rpos + 4 * m;
+    uint32_t rot_pos = rp[0];
+    if (fi % 3 == 1 && fi < (p.mrope >> 16)) rot_pos = rp[1];
+    else if (fi % 3 == 2 && fi < (p.mrope & 0xFFFFu)) rot_pos = rp[2];
+    sincosf((float)rot_pos * inv_freq, &sn, &cs);
+  }
+  pdl_wait();
   if (m >= st.m) return;
   const uint64_t pos = (uint64_t)st.pos0 + m;
   const uint32_t q_dim = p.n_heads * HD, kv_dim = p.n_kv * HD;
@@ -42,24 +57,12 @@ __global__ void __launch_bounds__(256) prep_kernel(StepRef sr, snl_attn_p p, con
     if ((d & 1) == 0) vc[(pos * kv_dim + kh * HD + d) / 2] = pack_h2(sh[d], sh[d + 1]);
     return;
   }
-  const bool is_q = slot < p.n_heads;
   float v = is_q ? proj[row + slot * 2 * HD + d] : proj[row + 2 * q_dim + (slot - p.n_heads) * HD + d];
   const float total = block_sum(v * v, red);
-  v = v * rsqrtf(total / (float)HD + p.eps) * (1.0f + norms[(is_q ? 0 : HD) + d]);
+  v = v * rsqrtf(total / (float)HD + p.eps) * nw;
   sh[d] = v;
   __syncthreads();
-  const uint32_t half_rot = p.rot_dim / 2;
-  if (d < p.rot_dim) {
-    const uint32_t fi = d % half_rot;
-    const float inv_freq = powf(p.rope_theta, -(float)(2 * fi) / (float)p.rot_dim);
-    const uint32_t* rp = rpos + 4 * m;
-    uint32_t rot_pos = rp[0];
-    if (fi % 3 == 1 && fi < (p.mrope >> 16)) rot_pos = rp[1];
-    else if (fi % 3 == 2 && fi < (p.mrope & 0xFFFFu)) rot_pos = rp[2];
-    float sn, cs;
-    sincosf((float)rot_pos * inv_freq, &sn, &cs);
-    v = d < half_rot ? v * cs - sh[d + half_rot] * sn : v * cs + sh[d - half_rot] * sn;
-  }
+  if (d < p.rot_dim) v = d < half_rot ? v * cs - sh[d + half_rot] * sn : v * cs + sh[d - half_rot] * sn;
   if (is_q) {
     qbuf[(uint64_t)m * q_dim + slot * HD + d] = v;
   } else {
@@ -109,38 +112,61 @@ __global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, c
                                                      const uint32_t* __restrict__ vc, float* __restrict__ out,
                                                      float* __restrict__ partial, XOut xo) {
   pdl_trigger();
-  {
-    // The part's K and V rows into L2 before the wait (the step descriptor is written by
-    // the host before the step's first kernel; L2 stays coherent with the new key that
-    // the prep kernel writes meanwhile).
-    const snl_step_u s0 = load_step(sr);
-    const uint32_t m0 = blockIdx.y, part0 = blockIdx.z;
-    if (m0 < s0.m && part0 < s0.parts) {
-      const uint32_t tot = s0.pos0 + m0 + 1, ch = (tot + s0.parts - 1) / s0.parts;
-      const uint32_t a0 = min(tot, part0 * ch), a1 = min(tot, a0 + ch);
-      // 4 lines of 128 B per row, K and V, for at most the part's first kPrefetchKeys rows:
-      // a long context's whole KV (134 MB per layer at 32K) would overflow L2.
-      const uint32_t kvd = p.n_kv * HD, lines = min(a1 - a0, kPrefetchKeys) * 8;
-      for (uint32_t i = threadIdx.x; i < lines; i += blockDim.x) {
-        const uint32_t t = a0 + (i >> 3), l = i & 3;
-        const uint32_t* base = (i & 4) ? vc : kc;
-        prefetch_l2(base + ((uint64_t)t * kvd + blockIdx.x * HD) / 2 + l * 32);
+  // The step descriptor is written before the step's first kernel, so the part's key
+  // range is known before the wait. Every cached key before the step's own (position
+  // pos0 on) was written by earlier steps: the warp's first 8-key group of K and V rows is
+  // loaded into registers here, and its rows of the step's own keys (which the prep
+  // kernel writes meanwhile) again after the wait. Later groups' rows go to L2 here.
+  const snl_step_u st = load_step(sr);
+  const uint32_t kh = blockIdx.x, m = blockIdx.y, part = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t q_dim = p.n_heads * HD, kv_dim = p.n_kv * HD;
+  const bool live = m < st.m && part < st.parts;
+  const uint32_t total = st.pos0 + m + 1;
+  const uint32_t chunk = (total + st.parts - 1) / st.parts;
+  const uint32_t start = min(total, part * chunk);
+  const uint32_t end = min(total, start + chunk);
+  const uint64_t kbase = (uint64_t)kh * HD;  // in halves
+  uint4 kw[kKeysPerGroup], vw[kKeysPerGroup];
+  uint32_t t0 = start + warp * kKeysPerGroup;
+  bool preloaded = false;
+  if (live) {
+    if (t0 < end) {
+      const uint32_t nk = min((uint32_t)kKeysPerGroup, end - t0);
+#pragma unroll
+      for (int j = 0; j < kKeysPerGroup; j++) {
+        const uint64_t row = ((uint64_t)(t0 + min((uint32_t)j, nk - 1)) * kv_dim + kbase) / 2 + lane * 4;
+        kw[j] = *reinterpret_cast<const uint4*>(kc + row);
+        vw[j] = *reinterpret_cast<const uint4*>(vc + row);
       }
+      preloaded = true;
+    }
+    // 4 lines of 128 B per row, K and V, of the part's rows after the first 64 (at most
+    // kPrefetchKeys more): a long context's whole KV (134 MB per layer at 32K) would
+    // overflow L2.
+    const uint32_t a0 = start + kAttWarps * kKeysPerGroup;
+    const uint32_t lines = a0 < end ? min(end - a0, kPrefetchKeys) * 8 : 0;
+    for (uint32_t i = threadIdx.x; i < lines; i += blockDim.x) {
+      const uint32_t t = a0 + (i >> 3), l = i & 3;
+      const uint32_t* base = (i & 4) ? vc : kc;
+      prefetch_l2(base + ((uint64_t)t * kv_dim + kbase) / 2 + l * 32);
     }
   }
   pdl_wait();
   __shared__ float s_acc[kAttWarps][G][HD];  // 32 KB
   __shared__ float s_ml[kAttWarps][G][2];
   __shared__ float s_p[kAttWarps][32];
-  const snl_step_u st = load_step(sr);
-  const uint32_t kh = blockIdx.x, m = blockIdx.y, part = blockIdx.z;
-  if (m >= st.m || part >= st.parts) return;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t q_dim = p.n_heads * HD, kv_dim = p.n_kv * HD;
-  const uint32_t total = st.pos0 + m + 1;
-  const uint32_t chunk = (total + st.parts - 1) / st.parts;
-  const uint32_t start = min(total, part * chunk);
-  const uint32_t end = min(total, start + chunk);
+  if (m >= st.m) return;
+  if (part >= st.parts) {
+    // An unused part slot of a captured step (the grid has the largest part count): a
+    // partial that the merge weighs by zero.
+    const uint64_t pi0 = ((uint64_t)m * p.n_heads + kh * G) * gridDim.z + part;
+    for (uint32_t i = threadIdx.x; i < G * (HD + 2); i += blockDim.x) {
+      const uint32_t g = i / (HD + 2), e = i % (HD + 2);
+      partial[(pi0 + (uint64_t)g * gridDim.z) * (HD + 2) + e] = e == HD ? -1e30f : 0.f;
+    }
+    return;
+  }
 
   float q[G][8];
 #pragma unroll
@@ -158,19 +184,21 @@ __global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, c
   const int my_g = lane & 3;       // score lane -> (key lane/4, head lane%4)
   float m_run = -1e30f, l_run = 0.f;  // for head my_g (replicated over lanes with that g)
 
-  const uint64_t kbase = (uint64_t)kh * HD;  // in halves
-  for (uint32_t t0 = start + warp * kKeysPerGroup; t0 < end; t0 += kAttWarps * kKeysPerGroup) {
+  for (; t0 < end; t0 += kAttWarps * kKeysPerGroup) {
     const uint32_t nk = min((uint32_t)kKeysPerGroup, end - t0);
-    // The group's K and V rows are all loaded here, before the scores: the V loads do not
-    // wait for the softmax, so the group costs one memory latency instead of nine. Rows past
-    // the part's end repeat its last key and get weight 0.
-    uint4 kw[kKeysPerGroup], vw[kKeysPerGroup];
+    // The group's K and V rows are all loaded before the scores: the V loads do not wait
+    // for the softmax, so the group costs one memory latency instead of nine. Rows past
+    // the part's end repeat its last key and get weight 0. The first group's rows came
+    // before the wait; only its rows of this step's keys are read again.
 #pragma unroll
     for (int j = 0; j < kKeysPerGroup; j++) {
-      const uint64_t row = ((uint64_t)(t0 + min((uint32_t)j, nk - 1)) * kv_dim + kbase) / 2 + lane * 4;
+      const uint32_t t = t0 + min((uint32_t)j, nk - 1);
+      if (preloaded && t < st.pos0) continue;
+      const uint64_t row = ((uint64_t)t * kv_dim + kbase) / 2 + lane * 4;
       kw[j] = *reinterpret_cast<const uint4*>(kc + row);
       vw[j] = *reinterpret_cast<const uint4*>(vc + row);
     }
+    preloaded = false;
     float part_s[32];
 #pragma unroll
     for (int j = 0; j < kKeysPerGroup; j++) {
@@ -248,13 +276,15 @@ __global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, c
       A = fmaf(s_acc[w][g][d], f, A);
     }
     const uint32_t h = kh * G + g;
-    if (st.parts == 1) {
+    if (gridDim.z == 1) {
       const float gate = proj[(uint64_t)m * p.proj_stride + h * 2 * HD + HD + d];
       const float o = A / L / (1.0f + __expf(-gate));
       out[(uint64_t)m * q_dim + h * HD + d] = o;
       if (xo.planes) xout_store(xo, m, h * HD + d, o);
     } else {
-      const uint64_t pi = ((uint64_t)m * p.n_heads + h) * st.parts + part;
+      // [(m * n_heads + h) * slots + part][258] with slots = the grid's part count (the
+      // step's part count except in captured steps, which have the largest one).
+      const uint64_t pi = ((uint64_t)m * p.n_heads + h) * gridDim.z + part;
       partial[pi * (HD + 2) + d] = A;
       if (d == 0) {
         partial[pi * (HD + 2) + HD] = M;
@@ -264,52 +294,66 @@ __global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, c
   }
 }
 
-// combine: CTA (head, token), thread = head dim. The parts' maxima and weights are
-// loaded by all threads at once (one part per thread, 256 parts per round) instead of
-// one after another by every thread; each thread then adds its dim over the parts in
-// part order with 16 loads in flight, and the softmax denominator is added in part order
-// from shared memory, so the sums are the sequential ones of attention.wgsl:248-269.
-// skip_single: the step's attend already wrote `out` (parts == 1); used by captured
-// graphs, whose launch list is fixed while parts changes between replays.
+// combine: CTA (head, token), thread = head dim. `slots` = the partial layout's part
+// count: the attend grid's, in which unused slots hold partials of weight zero; 0 = the
+// step's part count (the kernel-level call, the reference's layout). All the loads (the
+// first 64 parts' maxima, denominators and this thread's accumulator values) go out at
+// once; each thread then adds its dim over the parts in part order, and every thread adds
+// the denominator in part order from shared memory: the sequential sums of
+// attention.wgsl:248-269. In a captured step nothing here waits on the step descriptor.
 __global__ void __launch_bounds__(256) combine_kernel(StepRef sr, snl_attn_p p, const float* __restrict__ proj,
                                                       const float* __restrict__ partial, float* __restrict__ out,
-                                                      int skip_single, XOut xo) {
+                                                      uint32_t slots, XOut xo) {
   pdl_trigger();
   pdl_wait();
+  constexpr uint32_t kPre = 64;  // parts whose values are loaded in the first round
   __shared__ float s_w[HD], s_l[HD], s_red[HD / 32];
-  const snl_step_u st = load_step(sr);
   const uint32_t h = blockIdx.x, m = blockIdx.y, d = threadIdx.x;
-  if (m >= st.m || (skip_single && st.parts <= 1)) return;
-  const uint32_t q_dim = p.n_heads * HD, parts = st.parts;
+  uint32_t parts = slots;
+  if (slots == 0) {
+    const snl_step_u st = load_step(sr);
+    if (m >= st.m) return;
+    parts = st.parts;
+  } else if (m >= sr.val.m) {
+    return;
+  }
+  const uint32_t q_dim = p.n_heads * HD;
   const uint64_t base = ((uint64_t)m * p.n_heads + h) * parts;
-  float mx = -1e30f;
-  for (uint32_t i = d; i < parts; i += HD) mx = fmaxf(mx, partial[(base + i) * (HD + 2) + HD]);
+  const float* col = partial + base * (HD + 2) + d;
+  const uint32_t n0 = min(parts, kPre);
+  float v[kPre];
+#pragma unroll
+  for (uint32_t u = 0; u < kPre; u++) v[u] = col[(uint64_t)min(u, n0 - 1) * (HD + 2)];
+  float mi = -1e30f, li = 0.f;
+  if (d < n0) {
+    mi = partial[(base + d) * (HD + 2) + HD];
+    li = partial[(base + d) * (HD + 2) + HD + 1];
+  }
+  float mx = mi;
+  for (uint32_t i = kPre + d; i < parts; i += HD) mx = fmaxf(mx, partial[(base + i) * (HD + 2) + HD]);
   mx = warp_max(mx);
   if ((d & 31) == 0) s_red[d >> 5] = mx;
   __syncthreads();
 #pragma unroll
   for (uint32_t w = 0; w < HD / 32; w++) mx = fmaxf(mx, s_red[w]);
-  float l = 0.f, acc = 0.f;
-  for (uint32_t c0 = 0; c0 < parts; c0 += HD) {
+  s_w[d] = d < n0 ? __expf(mi - mx) : 0.f;  // parts past n0 add 0
+  s_l[d] = li;
+  __syncthreads();
+  float acc = 0.f, l = 0.f;
+#pragma unroll
+  for (uint32_t u = 0; u < kPre; u++) acc = fmaf(v[u], s_w[u], acc);
+  for (uint32_t i = 0; i < n0; i++) l = fmaf(s_l[i], s_w[i], l);
+  // Parts past the first 64 (kernel-level calls only): rounds of up to 256.
+  for (uint32_t c0 = kPre; c0 < parts; c0 += HD) {
     const uint32_t n = min(HD, parts - c0);
-    __syncthreads();  // the previous round's weights are read
+    __syncthreads();
     if (d < n) {
       const uint64_t o = (base + c0 + d) * (HD + 2);
       s_w[d] = __expf(partial[o + HD] - mx);
       s_l[d] = partial[o + HD + 1];
-    } else {
-      s_w[d] = 0.f;  // parts past n add 0 (their loads below repeat the last part)
     }
     __syncthreads();
-    const float* col = partial + (base + c0) * (HD + 2) + d;
-    // 16 parts' loads in flight at a time (their L2 latency is paid once per 16 parts).
-    for (uint32_t j0 = 0; j0 < n; j0 += 16) {
-      float v[16];
-#pragma unroll
-      for (int u = 0; u < 16; u++) v[u] = col[(uint64_t)min(j0 + u, n - 1) * (HD + 2)];
-#pragma unroll
-      for (int u = 0; u < 16; u++) acc = fmaf(v[u], s_w[j0 + u], acc);
-    }
+    for (uint32_t j = 0; j < n; j++) acc = fmaf(col[(uint64_t)(c0 + j) * (HD + 2)], s_w[j], acc);
     for (uint32_t i = 0; i < n; i++) l = fmaf(s_l[i], s_w[i], l);
   }
   const float gate = proj[(uint64_t)m * p.proj_stride + h * 2 * HD + HD + d];
@@ -344,10 +388,10 @@ int launch_attend(StepRef st, const snl_attn_p& p, const float* proj, const floa
 }
 
 int launch_attn_combine(StepRef st, const snl_attn_p& p, const float* proj, const float* partial, float* out,
-                        uint32_t m, cudaStream_t s, int skip_single, XOut xo) {
+                        uint32_t m, cudaStream_t s, uint32_t slots, XOut xo) {
   if (int rc = check_attn(p)) return rc;
   if (m == 0) return SNL_OK;
-  SNL_PDL_LAUNCH("combine_kernel", combine_kernel, dim3(dim3(p.n_heads, m)), dim3(HD), (size_t)(0), s, st, p, proj, partial, out, skip_single, xo);
+  SNL_PDL_LAUNCH("combine_kernel", combine_kernel, dim3(dim3(p.n_heads, m)), dim3(HD), (size_t)(0), s, st, p, proj, partial, out, slots, xo);
   return SNL_OK;
 }
 

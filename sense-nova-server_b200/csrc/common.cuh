@@ -180,8 +180,9 @@ int launch_attn_prep(StepRef st, const snl_attn_p& p, const float* proj, float* 
 int launch_attend(StepRef st, const snl_attn_p& p, const float* proj, const float* qbuf, const uint32_t* kc,
                   const uint32_t* vc, float* out, float* partial, uint32_t m, uint32_t parts_grid, cudaStream_t s,
                   XOut xo = XOut());
+// slots: the partial layout's part count (the attend grid's); 0 = the step's.
 int launch_attn_combine(StepRef st, const snl_attn_p& p, const float* proj, const float* partial, float* out,
-                        uint32_t m, cudaStream_t s, int skip_single, XOut xo = XOut());
+                        uint32_t m, cudaStream_t s, uint32_t slots, XOut xo = XOut());
 int launch_conv(StepRef st, const snl_lin_p& p, const float* proj, float* conv_out, float* conv_state,
                 const float* lw, float* conv_ckpt, cudaStream_t s);
 int launch_delta(StepRef st, const snl_lin_p& p, const float* proj, const float* conv_out, float* state,

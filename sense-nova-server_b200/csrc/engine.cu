@@ -489,7 +489,7 @@ int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
       }));
       if (parts_grid > 1)
         SNL_TRY(timed(e, "Combine", 4.0 * m * qd * 2, [&] {
-          return launch_attn_combine(st, ap, e->proj, e->partial, e->attn_out, m, e->stream, 1, xo);
+          return launch_attn_combine(st, ap, e->proj, e->partial, e->attn_out, m, e->stream, parts_grid, xo);
         }));
       // o_proj's K shard: this rank's query heads within the attention it computed.
       const size_t xo_off = o_proj_offset(e);
@@ -1478,7 +1478,7 @@ extern "C" int snl_engine_mtp(snl_engine* e, size_t r0, const uint32_t* tokens, 
     SNL_TRY(mat_tile(e, st, *find_q(e, "mtp.qkv"), e->xn, h, e->proj, ap.proj_stride, m));
     SNL_TRY(launch_attn_prep(st, ap, e->proj, e->qbuf, e->m_kc, e->m_vc, find_f(e, "mtp.qk_norm"), e->rpos, m, e->stream));
     SNL_TRY(launch_attend(st, ap, e->proj, e->qbuf, e->m_kc, e->m_vc, e->attn_out, e->partial, m, sh.parts, e->stream));
-    if (sh.parts > 1) SNL_TRY(launch_attn_combine(st, ap, e->proj, e->partial, e->attn_out, m, e->stream, 1));
+    if (sh.parts > 1) SNL_TRY(launch_attn_combine(st, ap, e->proj, e->partial, e->attn_out, m, e->stream, sh.parts));
     SNL_TRY(mat_tile(e, st, *find_q(e, "mtp.o_proj"), e->attn_out, snl_synth::q_dim(c), e->branch, h, m));
     SNL_TRY(launch_merge(st, p0, e->mx, e->coef, e->branch, m, e->stream));
     SNL_TRY(launch_branch_norm(st, p0, e->mx, e->coef, find_f(e, "mtp.post_ln"), e->xn, m, e->stream));

@@ -316,10 +316,10 @@ __global__ void __launch_bounds__(kCsThreads)
   const float dt_bias = lw[(uint64_t)cd * 4 + p.n_v + h];
   const float neg_a = -__expf(lw[(uint64_t)cd * 4 + h]);
   const float inv_sqrt_dk = rsqrtf((float)DK);
-  // This CTA's state slice (one 128-byte line per row) into L2 before the wait; the
-  // previous step wrote it, and L2 is coherent.
-  if (tid < DK) prefetch_l2(state + (uint64_t)h * DK * DV + (uint64_t)tid * DV + c0);
-  pdl_wait();
+  // The conv state and this thread's rows of the recurrent state are loaded before the
+  // wait: only this layer's kernel of an earlier step wrote them (each step starts after
+  // the previous one has finished), so they do not depend on the kernels this one waits
+  // for.
   const snl_step_u st = load_step(sr);
   float r0 = conv_state[ch], r1 = conv_state[(uint64_t)cd + ch], r2 = conv_state[(uint64_t)2 * cd + ch];
   float v0 = 0.f, v1 = 0.f, v2 = 0.f;
@@ -332,6 +332,7 @@ __global__ void __launch_bounds__(kCsThreads)
   float S[kCsRows];
 #pragma unroll
   for (uint32_t i = 0; i < kCsRows; i++) S[i] = state[sbase + i * DV];
+  pdl_wait();
 
   for (uint32_t m = 0; m < st.m; m++) {
     const uint64_t prow = (uint64_t)m * p.proj_stride;
