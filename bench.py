@@ -54,6 +54,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true",
                     help="skip the oracle parity check (and with it the CPU baseline)")
+    ap.add_argument("--no-config4", action="store_true",
+                    help="skip the BASELINE configs[4] leg (Q4_0 model, 32K context)")
     ap.add_argument("--cpu-budget-s", type=float, default=25.0)
     ap.add_argument("--profile", action="store_true", help="print the per-op table of one decode step")
     ap.add_argument("--turns", type=int, default=4, help="mtp workload: turns (BASELINE config 4 names 1000)")
@@ -536,12 +538,57 @@ def run_ours(args):
             line["gemv_config1"] = g1
         if cpu:
             line["cpu_baseline"] = cpu
-        print(json.dumps(line), flush=True)
     eng.close()
+    c4 = None if args.no_config4 else config4_leg(args, cfg, world, local_rank, dist, peak)
+    if rank == 0:
+        if c4:
+            line["config4"] = c4
+        print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def config4_leg(args, cfg, world, local_rank, dist, peak):
+    """the same model in Q4_0 (in_proj, embedding and LM head
+    stay Q8_0) at a 32K context, batch-1 greedy decode, on the run's N GPUs (tensor
+    parallel when N > 1). A 32,768-token prefill of uniform random ids, then `steps`
+    greedy tokens timed on the device (CUDA events, max over ranks)."""
+    import torch
+
+    from sensenova_b200.engine import Engine
+
+    prompt_n, steps, warm = 32768, 32, 4
+    tp = (int(os.environ.get("RANK", 0)), world) if world > 1 else None
+    eng = Engine.synthetic(cfg, prompt_n + warm + steps + 8, args.seed, "q4_0", device=local_rank, tp=tp)
+    prompt = np.random.default_rng(args.seed + 4).integers(0, cfg.vocab, prompt_n).tolist()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    tok = eng.forward_greedy(prompt, None, 1)[0]
+    prefill_s = time.perf_counter() - t0
+    toks, _ = eng.generate(tok, warm)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    _, ms = eng.generate(toks[-1], steps)
+    ms_t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    eng.close()
+    wb = weight_bytes_per_token(cfg, "q4_0")
+    kv = 2 * 2 * cfg.n_kv_heads * cfg.head_dim * sum(1 for l in cfg.execution_plan() if cfg.full_attention[l]) * prompt_n
+    tok_s = steps / (ms / 1000.0)
+    return {"workload": "BASELINE configs[4]: 9B-shape Q4_0 greedy decode bs1 at a 32K context "
+                        "(32768-token prefill of uniform random ids)",
+            "value": tok_s, "unit": "tok/s", "steps": steps, "warmup": warm, "ms_per_step": ms / steps,
+            "n_gpus": world, "parallelism": f"tp{world}" if world > 1 else "single",
+            "prefill_tok_s": prompt_n / prefill_s,
+            "bytes_per_token": {"weights": wb, "kv_cache_at_32k": kv},
+            "hbm_frac": (wb + kv) / world * tok_s / (peak * 1e9)}
 
 
 def run_gemv_only(args):
