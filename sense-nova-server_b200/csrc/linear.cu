@@ -464,6 +464,17 @@ struct DnScratch {
   float* chunks;  // [n_v][n_chunks][kDnChunkFloats]
 };
 
+// 16-byte asynchronous global -> shared copies (both addresses 16-byte aligned), committed
+// in groups; cp_async_wait<n> returns when at most n groups are still in flight.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // 3xTF32 tensor-core products (mma.sync m16n8k8, f32 accumulate): each f32 operand is
 // split into tf32 hi + lo and hi*hi + hi*lo + lo*hi are accumulated, which keeps about
 // fp32 accuracy (the dropped lo*lo term is below 2^-22 of the product).
@@ -482,14 +493,20 @@ __device__ __forceinline__ void mma_tf32(float d[4], const uint32_t a[4], uint32
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
-// d += A(16 x 8) B(8 x 8) in 3xTF32; a[4] / b[2] are the f32 fragment values (m16n8k8:
-// a0 (g, t), a1 (g + 8, t), a2 (g, t + 4), a3 (g + 8, t + 4); b0 (t, g), b1 (t + 4, g)).
-__device__ __forceinline__ void mma3_tf32(float d[4], const float a[4], const float b[2]) {
-  uint32_t ah[4], al[4], bh[2], bl[2];
+// Pre-split fragments: several output tiles that share their A rows (or B columns) split
+// those once per k-step, and their MMAs, into independent accumulators, interleave. Per
+// tile the MMAs run in the order of mma3_tf32, so the sums are the same bits.
+__device__ __forceinline__ void split_a(const float* ar, uint32_t sa, uint32_t ah[4], uint32_t al[4]) {
+  const float av[4] = {ar[0], ar[8 * sa], ar[4], ar[8 * sa + 4]};
 #pragma unroll
-  for (int i = 0; i < 4; i++) tf32_split(a[i], ah[i], al[i]);
-  tf32_split(b[0], bh[0], bl[0]);
-  tf32_split(b[1], bh[1], bl[1]);
+  for (int i = 0; i < 4; i++) tf32_split(av[i], ah[i], al[i]);
+}
+__device__ __forceinline__ void split_b(float b0, float b1, uint32_t bh[2], uint32_t bl[2]) {
+  tf32_split(b0, bh[0], bl[0]);
+  tf32_split(b1, bh[1], bl[1]);
+}
+__device__ __forceinline__ void mma3_split(float d[4], const uint32_t ah[4], const uint32_t al[4], const uint32_t bh[2],
+                                           const uint32_t bl[2]) {
   mma_tf32(d, al, bh[0], bh[1]);
   mma_tf32(d, ah, bl[0], bl[1]);
   mma_tf32(d, ah, bh[0], bh[1]);
@@ -500,21 +517,6 @@ __device__ __forceinline__ void mma3_tf32(float d[4], const float a[4], const fl
 // and M (64 x 68), W and U (64 x 132).
 constexpr uint32_t kPrS = 132, kPrT = 68;
 constexpr size_t kPrepSmemFloats = 5 * kDnC * kPrS + 2 * kDnC * kPrT;
-
-// 16 x 8 output tile (rows 16 mt, columns 8 nt) += A[rows][k] * B[k][cols] over k in
-// [k0, k1) (multiples of 8): A row-major with stride sa; B given by element (k, n) at
-// b[k * sbk + n * sbn].
-__device__ __forceinline__ void tile_mma3(float acc[4], const float* a, uint32_t sa, const float* b, uint32_t sbk,
-                                          uint32_t sbn, uint32_t mt, uint32_t nt, uint32_t k0, uint32_t k1, uint32_t g,
-                                          uint32_t t4) {
-  for (uint32_t k = k0; k < k1; k += 8) {
-    const float* ar = a + (16 * mt + g) * sa + k + t4;
-    const float av[4] = {ar[0], ar[8 * sa], ar[4], ar[8 * sa + 4]};
-    const float* br = b + (uint64_t)(k + t4) * sbk + (uint64_t)(8 * nt + g) * sbn;
-    const float bv[2] = {br[0], br[4 * sbk]};
-    mma3_tf32(acc, av, bv);
-  }
-}
 
 __global__ void __launch_bounds__(256) dn_prep_kernel(uint32_t m, snl_lin_p p, const float* __restrict__ proj,
                                                       const float* __restrict__ conv_out, const float* __restrict__ lw,
@@ -563,45 +565,68 @@ __global__ void __launch_bounds__(256) dn_prep_kernel(uint32_t m, snl_lin_p p, c
       kn[t * kPrS + i] *= rk;
     }
   }
-  if (tid == 0) {
+  // beta and the log decay of each token in parallel (their loads and transcendentals),
+  // then the prefix sum of the decays in token order on one thread.
+  if (tid < kDnC) {
+    const uint32_t t = tid;
     const float neg_a = -__expf(lw[(uint64_t)cd * 4 + h]);
     const float dt_bias = lw[(uint64_t)cd * 4 + p.n_v + h];
+    float bt = 0.f, lt = 0.f;
+    if (t < ce) {
+      const uint64_t prow = (uint64_t)(t0 + t) * p.proj_stride;
+      bt = 1.0f / (1.0f + __expf(-proj[prow + b_off + h]));
+      const float araw = proj[prow + a_off + h] + dt_bias;
+      const float sp = araw <= 20.0f ? log1pf(__expf(araw)) : araw;
+      lt = neg_a * sp;
+    }
+    lam[t] = lt;
+    beta[t] = bt;
+  }
+  __syncthreads();
+  if (tid == 0) {
     float acc = 0.f;
     for (uint32_t t = 0; t < kDnC; t++) {
-      float bt = 0.f, lt = 0.f;
-      if (t < ce) {
-        const uint64_t prow = (uint64_t)(t0 + t) * p.proj_stride;
-        bt = 1.0f / (1.0f + __expf(-proj[prow + b_off + h]));
-        const float araw = proj[prow + a_off + h] + dt_bias;
-        const float sp = araw <= 20.0f ? log1pf(__expf(araw)) : araw;
-        lt = neg_a * sp;
-      }
-      acc += lt;
+      acc += lam[t];
       lam[t] = acc;
-      beta[t] = bt;
-      elam[t] = __expf(acc);
     }
   }
+  __syncthreads();
+  if (tid < kDnC) elam[tid] = __expf(lam[tid]);
   __syncthreads();
   // 2. Gram matrices K K^T and Q K^T (64 x 64, K = 128): warp w takes row tile w / 2 and
   //    column tiles 4 (w % 2) .. + 3; tiles wholly above the diagonal are zero. Then
   //    L[t][s] = beta_t e^(lam_t - lam_s) k_t.k_s (s < t), M[t][s] = e^(lam_t - lam_s) q_t.k_s (s <= t).
   {
+    // The warp's 4 column tiles of both products in one k-loop: the A rows of k and q are
+    // split once per k-step, each k column once for both products.
     const uint32_t mt = warp >> 1;
-#pragma unroll 1
+    float gk[4][4] = {}, gq[4][4] = {};
+    const uint32_t nlive = min(4u, (16 * mt + 15) / 8 + 1 - min((16 * mt + 15) / 8 + 1, (warp & 1) * 4));
+#pragma unroll 2
+    for (uint32_t k = 0; k < DK; k += 8) {
+      uint32_t akh[4], akl[4], aqh[4], aql[4];
+      split_a(kn + (16 * mt + g) * kPrS + k + t4, kPrS, akh, akl);
+      split_a(qn + (16 * mt + g) * kPrS + k + t4, kPrS, aqh, aql);
+#pragma unroll
+      for (uint32_t q = 0; q < 4; q++) {
+        if (q >= nlive) break;
+        const uint32_t nt = (warp & 1) * 4 + q;
+        const float* br = kn + (8 * nt + g) * kPrS + k + t4;
+        uint32_t bh[2], bl[2];
+        split_b(br[0], br[4], bh, bl);
+        mma3_split(gk[q], akh, akl, bh, bl);
+        mma3_split(gq[q], aqh, aql, bh, bl);
+      }
+    }
+#pragma unroll
     for (uint32_t q = 0; q < 4; q++) {
       const uint32_t nt = (warp & 1) * 4 + q;
-      float gk[4] = {0.f, 0.f, 0.f, 0.f}, gq[4] = {0.f, 0.f, 0.f, 0.f};
-      if (8 * nt <= 16 * mt + 15) {
-        tile_mma3(gk, kn, kPrS, kn, 1, kPrS, mt, nt, 0, DK, g, t4);
-        tile_mma3(gq, qn, kPrS, kn, 1, kPrS, mt, nt, 0, DK, g, t4);
-      }
 #pragma unroll
       for (int r = 0; r < 4; r++) {
         const uint32_t t = 16 * mt + g + (r >= 2 ? 8 : 0), s2 = 8 * nt + 2 * t4 + (r & 1);
         const float e = s2 <= t ? __expf(lam[t] - lam[s2]) : 0.f;
-        X[t * kPrT + s2] = s2 < t ? beta[t] * e * gk[r] : 0.f;
-        Mq[t * kPrT + s2] = s2 <= t ? e * gq[r] : 0.f;
+        X[t * kPrT + s2] = s2 < t ? beta[t] * e * gk[q][r] : 0.f;
+        Mq[t * kPrT + s2] = s2 <= t ? e * gq[q][r] : 0.f;
       }
     }
   }
@@ -667,38 +692,68 @@ __global__ void __launch_bounds__(256) dn_prep_kernel(uint32_t m, snl_lin_p p, c
   // 4. W = T Gamma K, U = T V (64 x 128, K = 64, T lower triangular): warp w takes row
   //    tile w / 2 and column tiles 8 (w % 2) .. + 7.
   {
+    // The warp's 8 column tiles of W and U in one k-loop (the T rows split once per k-step).
     const uint32_t mt = warp >> 1, kend = 16 * (mt + 1);
+    float w[8][4] = {}, u[8][4] = {};
 #pragma unroll 1
+    for (uint32_t k = 0; k < kend; k += 8) {
+      uint32_t ah[4], al[4];
+      split_a(X + (16 * mt + g) * kPrT + k + t4, kPrT, ah, al);
+#pragma unroll
+      for (uint32_t q = 0; q < 8; q++) {
+        const uint32_t nt = (warp & 1) * 8 + q;
+        const float* bk = kn + (k + t4) * kPrS + 8 * nt + g;
+        const float* bv = vv + (k + t4) * kPrS + 8 * nt + g;
+        uint32_t kh[2], kl[2], vh[2], vl[2];
+        split_b(bk[0], bk[4 * kPrS], kh, kl);
+        split_b(bv[0], bv[4 * kPrS], vh, vl);
+        mma3_split(w[q], ah, al, kh, kl);
+        mma3_split(u[q], ah, al, vh, vl);
+      }
+    }
+#pragma unroll
     for (uint32_t q = 0; q < 8; q++) {
       const uint32_t nt = (warp & 1) * 8 + q;
-      float w[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
-      tile_mma3(w, X, kPrT, kn, kPrS, 1, mt, nt, 0, kend, g, t4);
-      tile_mma3(u, X, kPrT, vv, kPrS, 1, mt, nt, 0, kend, g, t4);
 #pragma unroll
       for (int r = 0; r < 4; r++) {
         const uint32_t t = 16 * mt + g + (r >= 2 ? 8 : 0), i = 8 * nt + 2 * t4 + (r & 1);
-        W[t * kPrS + i] = w[r];
-        U[t * kPrS + i] = u[r];
-        Wg[t * DK + i] = w[r];
-        Ug[t * DV + i] = u[r];
+        W[t * kPrS + i] = w[q][r];
+        U[t * kPrS + i] = u[q][r];
+        Wg[t * DK + i] = w[q][r];
+        Ug[t * DV + i] = u[q][r];
       }
     }
   }
   __syncthreads();
   // 5. P = Gamma Q - M W, R = M U (M lower triangular with diagonal).
   {
+    // The warp's 8 column tiles of M W and M U in one k-loop.
     const uint32_t mt = warp >> 1, kend = 16 * (mt + 1);
+    float pw[8][4] = {}, ru[8][4] = {};
 #pragma unroll 1
+    for (uint32_t k = 0; k < kend; k += 8) {
+      uint32_t ah[4], al[4];
+      split_a(Mq + (16 * mt + g) * kPrT + k + t4, kPrT, ah, al);
+#pragma unroll
+      for (uint32_t q = 0; q < 8; q++) {
+        const uint32_t nt = (warp & 1) * 8 + q;
+        const float* bw = W + (k + t4) * kPrS + 8 * nt + g;
+        const float* bu = U + (k + t4) * kPrS + 8 * nt + g;
+        uint32_t wh[2], wl[2], uh[2], ul[2];
+        split_b(bw[0], bw[4 * kPrS], wh, wl);
+        split_b(bu[0], bu[4 * kPrS], uh, ul);
+        mma3_split(pw[q], ah, al, wh, wl);
+        mma3_split(ru[q], ah, al, uh, ul);
+      }
+    }
+#pragma unroll
     for (uint32_t q = 0; q < 8; q++) {
       const uint32_t nt = (warp & 1) * 8 + q;
-      float pw[4] = {0.f, 0.f, 0.f, 0.f}, ru[4] = {0.f, 0.f, 0.f, 0.f};
-      tile_mma3(pw, Mq, kPrT, W, kPrS, 1, mt, nt, 0, kend, g, t4);
-      tile_mma3(ru, Mq, kPrT, U, kPrS, 1, mt, nt, 0, kend, g, t4);
 #pragma unroll
       for (int r = 0; r < 4; r++) {
         const uint32_t t = 16 * mt + g + (r >= 2 ? 8 : 0), i = 8 * nt + 2 * t4 + (r & 1);
-        Pg[t * DK + i] = fmaf(elam[t], qn[t * kPrS + i], -pw[r]);
-        Rg[t * DV + i] = ru[r];
+        Pg[t * DK + i] = fmaf(elam[t], qn[t * kPrS + i], -pw[q][r]);
+        Rg[t * DV + i] = ru[q][r];
       }
     }
   }
@@ -717,48 +772,58 @@ __global__ void __launch_bounds__(256) dn_scan_kernel(uint32_t m, uint32_t n_chu
                                                       const float* __restrict__ chunks, float* __restrict__ state,
                                                       float* __restrict__ out) {
   extern __shared__ __align__(16) float ssm[];
-  float* S = ssm;                       // [128][kScS]
-  float* A = S + DK * kScS;             // [C][kScA] P, then [C][kScKd] Kd
-  float* B = A + kDnC * kScKd;          // [C][kScA] W
-  float* D = B + kDnC * kScA;           // [C][kScS]
+  float* S = ssm;                          // [128][kScS]
+  float* Pb = S + DK * kScS;               // [2][C][kScA] P of this chunk and the next
+  float* Wb = Pb + 2 * kDnC * kScA;        // [2][C][kScA] W of this chunk and the next
+  float* Kb = Wb + 2 * kDnC * kScA;        // [C][kScKd] Kd
+  float* D = Kb + kDnC * kScKd;            // [C][kScS]
   const uint32_t slice = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
   const uint32_t warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
   const uint32_t j0 = slice * kDnCols;
   float* Sg = state + (uint64_t)h * DK * DV;
   for (uint32_t e = tid; e < DK * kDnCols; e += blockDim.x) S[(e / kDnCols) * kScS + e % kDnCols] = Sg[(e / kDnCols) * DV + j0 + e % kDnCols];
+  // The chunk records stream in with asynchronous copies, one step ahead of their use:
+  // P and W of chunk c + 1 while chunk c's state update runs, Kd of chunk c + 1 while
+  // its O and W S products run.
+  auto rec_of = [&](uint32_t c) { return chunks + ((uint64_t)h * n_chunks + c) * kDnChunkFloats; };
+  auto copy_rows = [&](float* dst, uint32_t stride, const float* src) {
+    for (uint32_t e = tid; e < kDnC * DK / 4; e += blockDim.x) {
+      const uint32_t r = e / (DK / 4), q = e % (DK / 4);
+      cp_async16(dst + r * stride + 4 * q, src + 4 * e);
+    }
+  };
+  copy_rows(Pb, kScA, rec_of(0));
+  copy_rows(Wb, kScA, rec_of(0) + 2 * kDnC * DK);
+  cp_async_commit();
+  copy_rows(Kb, kScKd, rec_of(0) + 4 * kDnC * DK);
+  cp_async_commit();
   // This warp's tiles: rows 16 * mt of the 64-token products, columns 8 * nt0 and 8 * nt0 + 8.
   const uint32_t mt = warp >> 1, nt0 = (warp & 1) * 2;
   for (uint32_t c = 0; c < n_chunks; c++) {
-    const float* rec = chunks + ((uint64_t)h * n_chunks + c) * kDnChunkFloats;
-    const float* P = rec;
-    const float* R = P + kDnC * DK;
-    const float* Wg = R + kDnC * DV;
-    const float* Ug = Wg + kDnC * DK;
-    const float* Kd = Ug + kDnC * DV;
+    const float* rec = rec_of(c);
+    const float* R = rec + kDnC * DK;
+    const float* Ug = rec + 3 * kDnC * DK;
     const float gC = rec[5 * kDnC * DK];
     const uint32_t t0 = c * kDnC, ce = min(kDnC, m - t0);
-    __syncthreads();
-    for (uint32_t e = tid; e < kDnC * DK / 4; e += blockDim.x) {
-      const uint32_t r = e / (DK / 4), q = e % (DK / 4);
-      *reinterpret_cast<float4*>(A + r * kScA + 4 * q) = reinterpret_cast<const float4*>(P)[e];
-      *reinterpret_cast<float4*>(B + r * kScA + 4 * q) = reinterpret_cast<const float4*>(Wg)[e];
-    }
+    float* A = Pb + (c & 1) * kDnC * kScA;
+    float* B = Wb + (c & 1) * kDnC * kScA;
+    cp_async_wait<1>();  // P and W of chunk c (its Kd may still be in flight)
     __syncthreads();
     // O = P S, WS = W S for the warp's two tiles.
     float o[2][4] = {}, ws[2][4] = {};
 #pragma unroll 4
     for (uint32_t ks = 0; ks < DK / 8; ks++) {
       const uint32_t kc = ks * 8 + t4;
-      const float* ar = A + (16 * mt + g) * kScA + kc;
-      const float* wr = B + (16 * mt + g) * kScA + kc;
-      const float pa[4] = {ar[0], ar[8 * kScA], ar[4], ar[8 * kScA + 4]};
-      const float wa[4] = {wr[0], wr[8 * kScA], wr[4], wr[8 * kScA + 4]};
+      uint32_t ph[4], pl[4], wh[4], wl[4];
+      split_a(A + (16 * mt + g) * kScA + kc, kScA, ph, pl);
+      split_a(B + (16 * mt + g) * kScA + kc, kScA, wh, wl);
 #pragma unroll
       for (int q = 0; q < 2; q++) {
         const uint32_t n = 8 * (nt0 + q) + g;
-        const float sb[2] = {S[kc * kScS + n], S[(kc + 4) * kScS + n]};
-        mma3_tf32(o[q], pa, sb);
-        mma3_tf32(ws[q], wa, sb);
+        uint32_t sh[2], sl[2];
+        split_b(S[kc * kScS + n], S[(kc + 4) * kScS + n], sh, sl);
+        mma3_split(o[q], ph, pl, sh, sl);
+        mma3_split(ws[q], wh, wl, sh, sl);
       }
     }
     // Outputs (+ R) and D = U - W S (c0/c1: row g, columns 2 t4, 2 t4 + 1; c2/c3: row g + 8).
@@ -771,14 +836,20 @@ __global__ void __launch_bounds__(256) dn_scan_kernel(uint32_t m, uint32_t n_chu
         if (t < ce) out[(uint64_t)(t0 + t) * p.n_v * DV + h * DV + j0 + j] = o[q][r] + R[t * DV + j0 + j];
       }
     }
-    __syncthreads();
-    for (uint32_t e = tid; e < kDnC * DK / 4; e += blockDim.x) {
-      const uint32_t r = e / (DK / 4), q = e % (DK / 4);
-      *reinterpret_cast<float4*>(A + r * kScKd + 4 * q) = reinterpret_cast<const float4*>(Kd)[e];
+    const bool more = c + 1 < n_chunks;
+    if (more) {
+      // the other buffers held chunk c - 1, finished before this chunk's first barrier
+      copy_rows(Pb + ((c + 1) & 1) * kDnC * kScA, kScA, rec_of(c + 1));
+      copy_rows(Wb + ((c + 1) & 1) * kDnC * kScA, kScA, rec_of(c + 1) + 2 * kDnC * DK);
+      cp_async_commit();
+      cp_async_wait<1>();  // Kd of chunk c
+    } else {
+      cp_async_wait<0>();
     }
     __syncthreads();
     // S = gamma_C S + Kd^T D: the warp's four tiles are state rows 16 * (warp % 8) and
     // columns 8 * nt, nt = 0..3. A(i, t) = Kd[t][i].
+    A = Kb;
     {
       const uint32_t it = warp;  // 8 row tiles of 16
       float acc[4][4];
@@ -794,11 +865,15 @@ __global__ void __launch_bounds__(256) dn_scan_kernel(uint32_t m, uint32_t n_chu
         const uint32_t kt = ks * 8 + t4;
         const float* kr = A + kt * kScKd + 16 * it + g;
         const float ka[4] = {kr[0], kr[8], kr[4 * kScKd], kr[4 * kScKd + 8]};
+        uint32_t kh[4], kl[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) tf32_split(ka[i], kh[i], kl[i]);
 #pragma unroll
         for (int q = 0; q < 4; q++) {
           const uint32_t n = 8 * q + g;
-          const float db[2] = {D[kt * kScS + n], D[(kt + 4) * kScS + n]};
-          mma3_tf32(acc[q], ka, db);
+          uint32_t dh[2], dl[2];
+          split_b(D[kt * kScS + n], D[(kt + 4) * kScS + n], dh, dl);
+          mma3_split(acc[q], kh, kl, dh, dl);
         }
       }
       __syncwarp();
@@ -809,6 +884,11 @@ __global__ void __launch_bounds__(256) dn_scan_kernel(uint32_t m, uint32_t n_chu
           const uint32_t i = 16 * it + g + (r >= 2 ? 8 : 0), j = 8 * q + 2 * t4 + (r & 1);
           S[i * kScS + j] = acc[q][r];
         }
+    }
+    if (more) {
+      __syncthreads();  // every warp has read Kd
+      copy_rows(Kb, kScKd, rec_of(c + 1) + 4 * kDnC * DK);
+      cp_async_commit();
     }
   }
   __syncthreads();
@@ -868,7 +948,7 @@ int launch_conv_delta_chunked(uint32_t m, const snl_lin_p& p, const float* proj,
   if (int rc = launch_conv(step_val(sv), p, proj, conv_out, conv_state, lw, nullptr, s)) return rc;
   const uint32_t nch = (m + kDnC - 1) / kDnC;
   const size_t prep_smem = kPrepSmemFloats * sizeof(float);
-  const size_t scan_smem = (DK * kScS + kDnC * kScKd + kDnC * kScA + kDnC * kScS) * sizeof(float);
+  const size_t scan_smem = (DK * kScS + 4 * kDnC * kScA + kDnC * kScKd + kDnC * kScS) * sizeof(float);
   static bool attr[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
