@@ -670,10 +670,13 @@ def run_deltanet(args):
         "metric": "Gated DeltaNet layer: prefill tok/s (4096 tokens) and recurrent us/token",
         "value": T / (pf_ms / 1000.0), "unit": "tok/s", "n_gpus": 1, "higher_is_better": True,
         "prefill_ms": pf_ms, "decode_us_per_token": dec_ms * 1000.0 / R, "decode_tok_s": R / (dec_ms / 1000.0),
-        "dtype": "f32", "data": "synthetic (BASELINE config 2 distributions)",
+        "dtype": "f32", "data": "synthetic (BASELINE configs[1] distributions)",
         "config": {"workload": "BASELINE configs[1]: DeltaNet 16/32 heads x 128, 4096-token prefill in 512-row steps "
-                               "then 256 single-token steps", "kernel": "conv_delta_kernel (token-sequential)"},
-        "roofline": {"bound": "latency (token-sequential recurrence)", "state_bytes_per_token": 2 * n_v * D * D * 4},
+                               "then 256 single-token steps",
+                   "kernel": "prefill: conv_kernel + chunked gated delta rule (dn_prep_kernel, dn_scan_kernel, "
+                             "dn_norm_kernel; 64-token chunks, 3xTF32 mma.sync); decode: conv_delta_split_kernel"},
+        "roofline": {"bound": "latency (chunk-sequential state carry; token-sequential recurrence in decode)",
+                     "state_bytes_per_token": 2 * n_v * D * D * 4},
         "cpu_baseline": {"value": nS / cpu_s, "unit": "tok/s", "cores": 1, "kind": "port",
                          "sample": f"oracle conv + delta over {nS} tokens"},
     }

@@ -101,6 +101,7 @@ __device__ __forceinline__ void h8_to_f(const uint4 w, float f[8]) {
 }
 
 constexpr int kAttWarps = 8;
+constexpr uint32_t kAttTcMinRows = 16;  // steps of at least this many rows use attend_tc_kernel
 constexpr int kKeysPerGroup = 8;
 constexpr uint32_t kPrefetchKeys = 64;
 
@@ -362,6 +363,231 @@ __global__ void __launch_bounds__(256) combine_kernel(StepRef sr, snl_attn_p p, 
   if (xo.planes) xout_store(xo, m, h * HD + d, o);
 }
 
+// ---- prefill attention on the tensor cores ----------------------------------------
+// Steps of many rows (prefill chunks) read every key once per 16 query tokens instead of
+// once per token. CTA (KV head kh, block of 16 step tokens), 4 warps: warp w owns query
+// head 4 kh + w for the 16 tokens, and all four share each 64-key block of K and V in
+// shared memory (GQA). Per key block, FlashAttention-style (online softmax in registers):
+//   S = Q K^T as mma.sync m16n8k16 (f16 in, f32 accumulate) with Q split into fp16 hi + lo
+//     (K is exact: the cache holds f16), so S carries Q's ~22 bits;
+//   causal and step-end masks, running max and sum per row (the S accumulator layout is
+//   the next MMA's A fragment layout);
+//   O += P V with P split into fp16 hi + lo (V exact), f32 accumulators in registers.
+// The 64-key blocks stream in with asynchronous copies one block ahead (rows past the
+// last key read as zeros). The result is the same attention as attention.wgsl:146-246
+// (sequential online softmax over 16-key tiles there), in another summation order.
+constexpr uint32_t kFaTok = 16;             // query tokens per CTA
+constexpr uint32_t kFaKeys = 64;            // keys per block
+constexpr uint32_t kFaStride = HD + 8;      // halves per smem row (528 B: ldmatrix rows on distinct banks)
+constexpr size_t kFaSmem = (size_t)(2 * G * kFaTok + 4 * kFaKeys) * kFaStride * sizeof(__half);
+
+__device__ __forceinline__ void fa_mma(float d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t r[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t r[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+// 16 bytes global -> shared, zero-filled when !valid (nothing is read then).
+__device__ __forceinline__ void fa_cp16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ uint32_t fa_h2(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+// hi / lo fp16 pairs of two floats: hi = f16(v), lo = f16(v - hi)
+__device__ __forceinline__ void fa_split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+  hi = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
+  lo = fa_h2(a - __half2float(ha), b - __half2float(hb));
+}
+
+__global__ void __launch_bounds__(128, 1) attend_tc_kernel(StepRef sr, snl_attn_p p, const float* __restrict__ proj,
+                                                           const float* __restrict__ qbuf,
+                                                           const uint32_t* __restrict__ kc,
+                                                           const uint32_t* __restrict__ vc, float* __restrict__ out) {
+  pdl_trigger();
+  extern __shared__ __align__(16) __half fsm[];
+  __half* Qh = fsm;                            // [G][16][kFaStride]
+  __half* Ql = Qh + G * kFaTok * kFaStride;    // [G][16][kFaStride]
+  __half* Kb = Ql + G * kFaTok * kFaStride;    // [2][64][kFaStride]
+  __half* Vb = Kb + 2 * kFaKeys * kFaStride;   // [2][64][kFaStride]
+  const snl_step_u st = load_step(sr);
+  const uint32_t kh = blockIdx.x, i0 = blockIdx.y * kFaTok, tid = threadIdx.x;
+  const uint32_t warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const uint32_t q_dim = p.n_heads * HD, kv_dim = p.n_kv * HD;
+  pdl_wait();
+  if (i0 >= st.m) return;
+  const uint32_t ntok = min(kFaTok, st.m - i0);
+  const uint32_t kend = st.pos0 + i0 + ntok;  // keys [0, kend) for this CTA
+  const uint32_t nblk = (kend + kFaKeys - 1) / kFaKeys;
+  const __half* kch = reinterpret_cast<const __half*>(kc);
+  const __half* vch = reinterpret_cast<const __half*>(vc);
+  auto load_block = [&](uint32_t b, uint32_t buf) {
+    __half* kd = Kb + buf * kFaKeys * kFaStride;
+    __half* vd = Vb + buf * kFaKeys * kFaStride;
+    for (uint32_t e = tid; e < kFaKeys * (HD / 8); e += blockDim.x) {
+      const uint32_t r = e / (HD / 8), c = (e % (HD / 8)) * 8;
+      const uint32_t key = b * kFaKeys + r;
+      const bool valid = key < kend;
+      const uint64_t off = (uint64_t)(valid ? key : 0) * kv_dim + kh * HD + c;
+      fa_cp16(kd + r * kFaStride + c, kch + off, valid);
+      fa_cp16(vd + r * kFaStride + c, vch + off, valid);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  load_block(0, 0);
+  // Q of the CTA's 4 heads and 16 tokens, scaled, as fp16 hi + lo (rows past the step: 0).
+  for (uint32_t e = tid; e < G * kFaTok * (HD / 2); e += blockDim.x) {
+    const uint32_t hh = e / (kFaTok * HD / 2), r = (e / (HD / 2)) % kFaTok, c = (e % (HD / 2)) * 2;
+    float a = 0.f, b = 0.f;
+    if (r < ntok) {
+      const float* qp = qbuf + (uint64_t)(i0 + r) * q_dim + (kh * G + hh) * HD + c;
+      a = qp[0] * p.scale;
+      b = qp[1] * p.scale;
+    }
+    uint32_t hi, lo;
+    fa_split2(a, b, hi, lo);
+    *reinterpret_cast<uint32_t*>(Qh + (hh * kFaTok + r) * kFaStride + c) = hi;
+    *reinterpret_cast<uint32_t*>(Ql + (hh * kFaTok + r) * kFaStride + c) = lo;
+  }
+  float o[HD / 8][4];
+#pragma unroll
+  for (int n = 0; n < (int)(HD / 8); n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float mrow[2] = {-1e30f, -1e30f}, lrow[2] = {0.f, 0.f};
+  const __half* qh = Qh + warp * kFaTok * kFaStride;
+  const __half* ql = Ql + warp * kFaTok * kFaStride;
+  // ldmatrix row addresses of this lane: A (16 x 16 of Q) and B (K: keys x dims, V: keys x dims transposed)
+  const uint32_t a_row = (lane & 7) + 8 * ((lane >> 3) & 1), a_col = 8 * (lane >> 4);
+  const uint32_t kb_row = (lane & 7) + 8 * (lane >> 4), kb_col = 8 * ((lane >> 3) & 1);
+  const uint32_t vb_row = (lane & 7) + 8 * ((lane >> 3) & 1), vb_col = 8 * (lane >> 4);
+  for (uint32_t b = 0; b < nblk; b++) {
+    const uint32_t buf = b & 1;
+    if (b + 1 < nblk) {
+      load_block(b + 1, buf ^ 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();
+    const __half* kd = Kb + buf * kFaKeys * kFaStride;
+    const __half* vd = Vb + buf * kFaKeys * kFaStride;
+    // S = Q K^T for the warp's 16 rows x 64 keys
+    float sacc[kFaKeys / 8][4];
+#pragma unroll
+    for (int j = 0; j < (int)(kFaKeys / 8); j++) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
+#pragma unroll 2
+    for (uint32_t ks = 0; ks < HD / 16; ks++) {
+      uint32_t ah[4], al[4];
+      ldsm_x4(ah, qh + a_row * kFaStride + 16 * ks + a_col);
+      ldsm_x4(al, ql + a_row * kFaStride + 16 * ks + a_col);
+#pragma unroll
+      for (int j = 0; j < (int)(kFaKeys / 8); j += 2) {
+        uint32_t kb4[4];
+        ldsm_x4(kb4, kd + (8 * j + kb_row) * kFaStride + 16 * ks + kb_col);
+        fa_mma(sacc[j], ah[0], ah[1], ah[2], ah[3], kb4[0], kb4[1]);
+        fa_mma(sacc[j], al[0], al[1], al[2], al[3], kb4[0], kb4[1]);
+        fa_mma(sacc[j + 1], ah[0], ah[1], ah[2], ah[3], kb4[2], kb4[3]);
+        fa_mma(sacc[j + 1], al[0], al[1], al[2], al[3], kb4[2], kb4[3]);
+      }
+    }
+    // masks: key k is visible to row r (step token i0 + r) iff k <= pos0 + i0 + r
+    const uint32_t key0 = b * kFaKeys;
+    float bm[2] = {-1e30f, -1e30f};
+#pragma unroll
+    for (int j = 0; j < (int)(kFaKeys / 8); j++) {
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const uint32_t r = g + (e >= 2 ? 8 : 0), key = key0 + 8 * j + 2 * t + (e & 1);
+        const bool vis = r < ntok && key <= st.pos0 + i0 + r;
+        sacc[j][e] = vis ? sacc[j][e] : -1e30f;
+        bm[e >> 1] = fmaxf(bm[e >> 1], sacc[j][e]);
+      }
+    }
+    float corr[2];
+#pragma unroll
+    for (int h2 = 0; h2 < 2; h2++) {
+      bm[h2] = fmaxf(bm[h2], __shfl_xor_sync(0xffffffffu, bm[h2], 1));
+      bm[h2] = fmaxf(bm[h2], __shfl_xor_sync(0xffffffffu, bm[h2], 2));
+      const float mn = fmaxf(mrow[h2], bm[h2]);
+      corr[h2] = __expf(mrow[h2] - mn);
+      mrow[h2] = mn;
+    }
+    float ls[2] = {0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < (int)(kFaKeys / 8); j++) {
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const float pv = sacc[j][e] <= -1e29f ? 0.f : __expf(sacc[j][e] - mrow[e >> 1]);
+        sacc[j][e] = pv;
+        ls[e >> 1] += pv;
+      }
+    }
+#pragma unroll
+    for (int h2 = 0; h2 < 2; h2++) {
+      ls[h2] += __shfl_xor_sync(0xffffffffu, ls[h2], 1);
+      ls[h2] += __shfl_xor_sync(0xffffffffu, ls[h2], 2);
+      lrow[h2] = lrow[h2] * corr[h2] + ls[h2];
+    }
+#pragma unroll
+    for (int n = 0; n < (int)(HD / 8); n++) {
+      o[n][0] *= corr[0];
+      o[n][1] *= corr[0];
+      o[n][2] *= corr[1];
+      o[n][3] *= corr[1];
+    }
+    // O += P V: P's k-step ks2 (keys 16 ks2 ..) is S tiles 2 ks2 and 2 ks2 + 1
+#pragma unroll
+    for (uint32_t ks2 = 0; ks2 < kFaKeys / 16; ks2++) {
+      uint32_t ph[4], pl[4];
+      fa_split2(sacc[2 * ks2][0], sacc[2 * ks2][1], ph[0], pl[0]);
+      fa_split2(sacc[2 * ks2][2], sacc[2 * ks2][3], ph[1], pl[1]);
+      fa_split2(sacc[2 * ks2 + 1][0], sacc[2 * ks2 + 1][1], ph[2], pl[2]);
+      fa_split2(sacc[2 * ks2 + 1][2], sacc[2 * ks2 + 1][3], ph[3], pl[3]);
+#pragma unroll
+      for (int n = 0; n < (int)(HD / 8); n += 2) {
+        uint32_t vb4[4];
+        ldsm_x4_t(vb4, vd + (16 * ks2 + vb_row) * kFaStride + 8 * n + vb_col);
+        fa_mma(o[n], ph[0], ph[1], ph[2], ph[3], vb4[0], vb4[1]);
+        fa_mma(o[n], pl[0], pl[1], pl[2], pl[3], vb4[0], vb4[1]);
+        fa_mma(o[n + 1], ph[0], ph[1], ph[2], ph[3], vb4[2], vb4[3]);
+        fa_mma(o[n + 1], pl[0], pl[1], pl[2], pl[3], vb4[2], vb4[3]);
+      }
+    }
+    __syncthreads();  // every warp is done with this buffer before it is refilled
+  }
+  // out = O / l * sigmoid(gate) (attention.wgsl:146-246)
+  const uint32_t h = kh * G + warp;
+#pragma unroll
+  for (int h2 = 0; h2 < 2; h2++) {
+    const uint32_t r = g + 8 * h2;
+    if (r >= ntok) continue;
+    const uint32_t tok = i0 + r;
+    const float inv_l = 1.0f / lrow[h2];
+    const float* gate = proj + (uint64_t)tok * p.proj_stride + h * 2 * HD + HD;
+    float* orow = out + (uint64_t)tok * q_dim + h * HD;
+#pragma unroll
+    for (int n = 0; n < (int)(HD / 8); n++) {
+      const uint32_t d = 8 * n + 2 * t;
+      const float g0 = gate[d], g1 = gate[d + 1];
+      orow[d] = o[n][2 * h2] * inv_l / (1.0f + __expf(-g0));
+      orow[d + 1] = o[n][2 * h2 + 1] * inv_l / (1.0f + __expf(-g1));
+    }
+  }
+}
+
 }  // namespace
 
 static int check_attn(const snl_attn_p& p) {
@@ -383,6 +609,20 @@ int launch_attend(StepRef st, const snl_attn_p& p, const float* proj, const floa
                   XOut xo) {
   if (int rc = check_attn(p)) return rc;
   if (m == 0 || parts_grid == 0) return SNL_OK;
+  static const bool no_tc = getenv("SNL_NO_ATTN_TC") != nullptr;
+  if (parts_grid == 1 && m >= kAttTcMinRows && !xo.planes && !no_tc) {
+    // a prefill chunk: the tiled tensor-core kernel (keys read once per 16 tokens)
+    static bool attr[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr[dev]) {
+      SNL_CUDA_TRY(cudaFuncSetAttribute(attend_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFaSmem));
+      attr[dev] = true;
+    }
+    SNL_PDL_LAUNCH("attend_tc_kernel", attend_tc_kernel, dim3(p.n_kv, (m + kFaTok - 1) / kFaTok), dim3(128), kFaSmem, s,
+                   st, p, proj, qbuf, kc, vc, out);
+    return SNL_OK;
+  }
   SNL_PDL_LAUNCH("attend_kernel", attend_kernel, dim3(dim3(p.n_kv, m, parts_grid)), dim3(kAttWarps * 32), (size_t)(0), s, st, p, proj, qbuf, kc, vc, out, partial, xo);
   return SNL_OK;
 }

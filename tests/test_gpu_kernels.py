@@ -416,7 +416,10 @@ def test_attn_prep(T, lib, orc, m, pos0):
 
 
 @pytest.mark.parametrize("m,pos0,parts", [(1, 0, 1), (1, 255, 1), (1, 1000, 4), (1, 2047, 8), (2, 5000, 20),
-                                          (4, 700, 64), (9, 50, 1), (64, 200, 1)])
+                                          (4, 700, 64), (9, 50, 1), (64, 200, 1),
+                                          # prefill chunks (16+ rows): the tiled tensor-core kernel, including
+                                          # ragged token blocks, a chunk from position 0, and 32K keys
+                                          (16, 0, 1), (37, 100, 1), (512, 0, 1), (300, 4000, 1), (64, 32000, 1)])
 def test_attend_combine(T, lib, orc, m, pos0, parts):
     rng = np.random.default_rng(pos0 + m)
     p, proj, norms, kc, vc, rpos = attn_case(rng, m, pos0)
