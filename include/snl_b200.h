@@ -304,8 +304,10 @@ int snl_engine_create(const snl_model_config* cfg, size_t ctx, int device, uint3
  *   4. set_tensor / fill_synthetic with the FULL tensors; finalize keeps this rank's
  *      shard.
  * forward_mm returns the full logits row on every rank; forward_greedy returns the same
- * token on every rank. With tp_size == 1 this is snl_engine_create. MTP is not supported
- * under tensor parallelism (finalize fails with SNL_E_UNSUPPORTED).
+ * token on every rank. With tp_size == 1 this is snl_engine_create. The MTP layer is
+ * replicated (every rank runs it in full) and its head is the vocabulary-split LM head:
+ * snl_engine_mtp returns the same draft on every rank, and every rank must make the same
+ * mtp calls in the same order as its forward calls.
  * Every cross-GPU wait is bounded: 2 s, or SNL_TP_WAIT_MS milliseconds when that
  * environment variable is set at finalize. When a peer stops taking part, the waiting
  * rank's call returns SNL_E_TIMEOUT after about one bound (later waits of the device give

@@ -118,6 +118,7 @@ struct snl_engine {
   // MTP (engine.rs:495-580)
   float *mx = nullptr, *hn = nullptr, *m_logits = nullptr;
   uint32_t *m_kc = nullptr, *m_vc = nullptr;
+  uint64_t mtp_drafts = 0;  // tensor parallel: drafts run (their argmax key sets alternate)
   // pinned host staging
   uint32_t* h_tokens = nullptr;
   uint32_t* h_rpos = nullptr;
@@ -212,12 +213,15 @@ snl_layer_p layer_p(const snl_engine* e, uint32_t mode, bool last_row) {
   return p;
 }
 
-snl_attn_p attn_p(const snl_engine* e) {
+// The attention of this rank's shard (lc), or of the whole model (cfg: the MTP layer,
+// which every rank runs in full).
+snl_attn_p attn_p(const snl_engine* e, bool whole = false) {
+  const snl_model_config& c = whole ? e->cfg : e->lc;
   snl_attn_p a;
-  a.n_heads = e->lc.n_heads;
-  a.n_kv = e->lc.n_kv_heads;
+  a.n_heads = c.n_heads;
+  a.n_kv = c.n_kv_heads;
   a.rot_dim = e->cfg.rot_dim;
-  a.proj_stride = (uint32_t)snl_synth::attn_proj_rows(e->lc);
+  a.proj_stride = (uint32_t)snl_synth::attn_proj_rows(c);
   a.rope_theta = e->cfg.rope_theta;
   a.eps = e->cfg.eps;
   a.scale = 1.0f / sqrtf((float)e->cfg.head_dim);
@@ -1002,7 +1006,8 @@ extern "C" int snl_engine_create_tp(const snl_model_config* cfg, size_t ctx, int
   t.off_bparts = al(t.off_flags + (size_t)snl::kTpSlots * snl::kTpMax * 8);
   t.off_ll = al(t.off_bparts + 2 * MAX_M * h * sizeof(float));
   t.off_llkeys = al(t.off_ll + (size_t)2 * snl::kTpMax * 4 * h * 8);
-  t.off_logits = al(t.off_llkeys + LOGIT_ROWS * snl::kTpMax * 2 * 8);
+  static_assert(LOGIT_ROWS <= snl::kTpKeyRows, "argmax key slots per set");
+  t.off_logits = al(t.off_llkeys + (size_t)snl::kTpKeySets * snl::kTpKeyRows * snl::kTpMax * 2 * 8);
   t.region_bytes = al(t.off_logits + LOGIT_ROWS * (size_t)e->vocab_l * sizeof(float));
   cudaError_t ce = cudaMalloc(&t.region, t.region_bytes);
   if (ce == cudaSuccess) ce = cudaMemset(t.region, 0, t.region_bytes);
@@ -1169,7 +1174,6 @@ extern "C" int snl_engine_finalize(snl_engine* e) {
   if (!missing.empty()) return fail(SNL_E_INVALID, "weight file is missing tensor `" + missing + "`");
   if (e->tp.size > 1) {
     if (!e->tp.connected) return fail(SNL_E_STATE, "tensor parallel engine: snl_engine_tp_connect first");
-    if (e->has_mtp) return fail(SNL_E_UNSUPPORTED, "tensor parallel engine: MTP is not supported");
     SNL_TRY(shard_weights(e));
   }
   // Tile-layout copies for the decode GEMV (embed is only gathered, not multiplied). A
@@ -1209,19 +1213,23 @@ extern "C" int snl_engine_finalize(snl_engine* e) {
     }
     e->tiles_on = true;
   }
-  const size_t proj_w = std::max({2 * I, snl_synth::lin_proj_rows(c), snl_synth::attn_proj_rows(c)});
-  const size_t act_w = std::max(I, snl_synth::conv_dim(c));
-  const size_t attn_w = std::max(snl_synth::q_dim(c), snl_synth::lin_value_dim(c));
+  // The MTP layer runs unsharded on every rank: with it, the step buffers also fit the
+  // whole model's attention and FFN (mc == c without tensor parallelism).
+  const snl_model_config& mc = e->has_mtp ? e->cfg : c;
+  const size_t proj_w = std::max({2 * I, snl_synth::lin_proj_rows(c), snl_synth::attn_proj_rows(c),
+                                  2 * (size_t)mc.intermediate, snl_synth::attn_proj_rows(mc)});
+  const size_t act_w = std::max({I, snl_synth::conv_dim(c), (size_t)mc.intermediate});
+  const size_t attn_w = std::max({snl_synth::q_dim(c), snl_synth::lin_value_dim(c), snl_synth::q_dim(mc)});
   SNL_TRY(dalloc(e, &e->x, MAX_M * 2 * h));
   SNL_TRY(dalloc(e, &e->xn, MAX_M * h));
   SNL_TRY(dalloc(e, &e->proj, MAX_M * proj_w));
   SNL_TRY(dalloc(e, &e->act, MAX_M * act_w));
   SNL_TRY(dalloc(e, &e->attn_out, MAX_M * attn_w));
   SNL_TRY(dalloc(e, &e->branch, MAX_M * h));
-  SNL_TRY(dalloc(e, &e->qbuf, MAX_M * snl_synth::q_dim(c)));
+  SNL_TRY(dalloc(e, &e->qbuf, MAX_M * std::max(snl_synth::q_dim(c), snl_synth::q_dim(mc))));
   SNL_TRY(dalloc(e, &e->coef, MAX_M * 8));
-  SNL_TRY(dalloc(e, &e->partial, std::max<size_t>((size_t)c.n_heads * MAX_M, (size_t)c.n_heads * 4 * MAX_PARTS) *
-                                         (c.head_dim + 2)));
+  const size_t heads_w = std::max(c.n_heads, mc.n_heads);
+  SNL_TRY(dalloc(e, &e->partial, std::max<size_t>(heads_w * MAX_M, heads_w * 4 * MAX_PARTS) * (c.head_dim + 2)));
   SNL_TRY(dalloc(e, &e->rpos, MAX_M * 4));
   SNL_TRY(dalloc(e, &e->tokens, MAX_M));
   SNL_TRY(dalloc(e, &e->logits, LOGIT_ROWS * (size_t)c.vocab));
@@ -1230,7 +1238,8 @@ extern "C" int snl_engine_finalize(snl_engine* e) {
   SNL_TRY(dalloc(e, &e->mhc_raw, MAX_M * 16 * 9));
   SNL_TRY(dalloc(e, &e->amax, LOGIT_ROWS));
   SNL_TRY(dalloc(e, &e->amax_part, LOGIT_ROWS * 128));
-  e->pstride = (uint32_t)((std::max({h, I, snl_synth::q_dim(c), snl_synth::lin_value_dim(c)}) + 7) / 8 * 8);
+  e->pstride = (uint32_t)((std::max({h, I, snl_synth::q_dim(c), snl_synth::lin_value_dim(c),
+                                      (size_t)mc.intermediate, snl_synth::q_dim(mc)}) + 7) / 8 * 8);
   SNL_TRY(dalloc(e, &e->xpl, (size_t)8 * e->pstride));
   SNL_TRY(dalloc(e, &e->xpl_act, (size_t)8 * e->pstride));
   SNL_TRY(dalloc(e, &e->xpl_norm, (size_t)8 * e->pstride));
@@ -1266,8 +1275,9 @@ extern "C" int snl_engine_finalize(snl_engine* e) {
     SNL_TRY(dalloc(e, &e->mx, MAX_M * 2 * h));
     SNL_TRY(dalloc(e, &e->hn, MAX_M * h));
     SNL_TRY(dalloc(e, &e->m_logits, (size_t)c.vocab));
-    SNL_TRY(dalloc(e, &e->m_kc, kv_words));
-    SNL_TRY(dalloc(e, &e->m_vc, kv_words));
+    const size_t m_kv_words = e->ctx * snl_synth::kv_dim(mc) / 2;  // the MTP layer's cache is unsharded
+    SNL_TRY(dalloc(e, &e->m_kc, m_kv_words));
+    SNL_TRY(dalloc(e, &e->m_vc, m_kv_words));
   }
   SNL_CUDA_TRY(cudaMallocHost(&e->h_tokens, MAX_M * sizeof(uint32_t)));
   SNL_CUDA_TRY(cudaMallocHost(&e->h_rpos, MAX_M * 4 * sizeof(uint32_t)));
@@ -1436,7 +1446,11 @@ extern "C" int snl_engine_sample(snl_engine* e, size_t row, const snl_sample_p* 
   return SNL_OK;
 }
 
-// mtp (engine.rs:708-774).
+// mtp (engine.rs:708-774). Under tensor parallelism every rank runs the MTP layer in
+// full on its copy of the hidden rows (the layer's weights are not sharded), so the ranks
+// need no exchange until the head: that is split by vocabulary like the model's, and the
+// draft is the argmax agreed over the ranks' shards. Each call's embedding advances the
+// step counter, so the draft's exchange has an epoch of its own.
 extern "C" int snl_engine_mtp(snl_engine* e, size_t r0, const uint32_t* tokens, size_t n, const uint32_t* pos, size_t slot0,
                               int draft, uint32_t* draft_out) {
   if (!e) return fail(SNL_E_INVALID, "null engine");
@@ -1447,7 +1461,8 @@ extern "C" int snl_engine_mtp(snl_engine* e, size_t r0, const uint32_t* tokens, 
   DeviceGuard dg(e->device);
   const size_t h = e->h();
   const auto& c = e->cfg;
-  const snl_attn_p ap = attn_p(e);
+  const snl_attn_p ap = attn_p(e, true);
+  const bool tp = e->tp.size > 1;
   for (size_t c0 = 0; c0 < n; c0 += MAX_M) {
     const size_t c1 = std::min(c0 + MAX_M, n);
     const uint32_t m = (uint32_t)(c1 - c0);
@@ -1465,8 +1480,9 @@ extern "C" int snl_engine_mtp(snl_engine* e, size_t r0, const uint32_t* tokens, 
     const bool last = c1 == n;
     const QT* emb = find_q(e, "embed");
     SNL_TRY(launch_embed(e->tokens, m, (const int8_t*)emb->q, (const float*)emb->s, (uint32_t)h, c.vocab, e->mx, nullptr,
-                         e->stream));
+                         e->stream, tp ? e->step_ctr : nullptr));
     snl_layer_p p0 = layer_p(e, 0, false);
+    p0.inter = c.intermediate;  // the MTP FFN is unsharded
     SNL_TRY(launch_branch_norm(st, p0, e->mx, e->coef, find_f(e, "mtp.norm_e"), e->xn, m, e->stream));
     snl_layer_p ph = p0;
     ph.x_stride = (uint32_t)h;
@@ -1489,8 +1505,14 @@ extern "C" int snl_engine_mtp(snl_engine* e, size_t r0, const uint32_t* tokens, 
     if (last && draft) {
       snl_layer_p pl = layer_p(e, 0, true);
       SNL_TRY(launch_branch_norm(st, pl, e->mx, e->coef, find_f(e, "mtp.norm"), e->xn, 1, e->stream));
-      SNL_TRY(mat_tile(e, st, *find_q(e, "lm_head"), e->xn, h, e->m_logits, c.vocab, 1));
-      SNL_TRY(launch_argmax_with(e->m_logits, 1, c.vocab, e->amax, e->amax_part, e->stream));
+      SNL_TRY(mat_tile(e, st, *find_q(e, "lm_head"), e->xn, h, e->m_logits, e->vocab_l, 1));
+      if (tp) {
+        const uint32_t key_set = 1 + (uint32_t)(e->mtp_drafts++ & 1);
+        SNL_TRY(launch_argmax_tp(e->m_logits, 1, e->vocab_l, e->amax, e->amax_part, e->tp.comm, e->tp_sites - 1,
+                                 e->stream, key_set));
+      } else {
+        SNL_TRY(launch_argmax_with(e->m_logits, 1, c.vocab, e->amax, e->amax_part, e->stream));
+      }
     }
     SNL_TRY(queue_error_read(e));
     SNL_CUDA_TRY(cudaStreamSynchronize(e->stream));

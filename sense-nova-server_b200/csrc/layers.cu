@@ -397,9 +397,11 @@ __global__ void argmax_pass2(const unsigned long long* __restrict__ part, uint32
 // Tensor-parallel pass 2: the row's best key over this rank's vocabulary shard, rebased
 // to the global index, is pushed into every rank's memory as two tagged words; each rank
 // then takes the largest of all ranks' keys, so all agree on the token (first index on
-// ties).
+// ties). key_set selects one of the key slot sets (kTpKeySets): each exchange kind has
+// its own, so a slot is rewritten only after an exchange that every peer joined after
+// reading it.
 __global__ void argmax_tp_pass2(const unsigned long long* __restrict__ part, uint32_t nparts, uint32_t vl, TpComm c,
-                                uint32_t site, uint32_t* __restrict__ out) {
+                                uint32_t site, uint32_t key_set, uint32_t* __restrict__ out) {
   pdl_trigger();
   pdl_wait();
   const uint32_t row = blockIdx.x;
@@ -420,14 +422,14 @@ __global__ void argmax_tp_pass2(const unsigned long long* __restrict__ part, uin
     const unsigned long long key = ((unsigned long long)ord << 32) | (unsigned long long)(~gidx);
     for (int q = 0; q < c.size; q++) {
       if (q == c.rank) continue;
-      unsigned long long* slot = c.llkeys[q] + ((uint64_t)row * kTpMax + c.rank) * 2;
+      unsigned long long* slot = c.llkeys[q] + (((uint64_t)key_set * kTpKeyRows + row) * kTpMax + c.rank) * 2;
       st_relaxed_sys_u64(slot, ll_word(tag, ord));
       st_relaxed_sys_u64(slot + 1, ll_word(tag, ~gidx));
     }
     unsigned long long g = key;
     for (int q = 0; q < c.size; q++) {
       if (q == c.rank) continue;
-      const unsigned long long* slot = c.llkeys[c.rank] + ((uint64_t)row * kTpMax + q) * 2;
+      const unsigned long long* slot = c.llkeys[c.rank] + (((uint64_t)key_set * kTpKeyRows + row) * kTpMax + q) * 2;
       const uint32_t o = ll_wait(c, slot, tag), ni = ll_wait(c, slot + 1, tag);
       const unsigned long long k = ((unsigned long long)o << 32) | ni;
       g = k > g ? k : g;
@@ -606,12 +608,13 @@ int launch_argmax_with(const float* logits, uint32_t rows, uint32_t n, uint32_t*
 }
 
 int launch_argmax_tp(const float* logits, uint32_t rows, uint32_t vl, uint32_t* out_idx, unsigned long long* part,
-                     const TpComm& c, uint32_t site, cudaStream_t s) {
+                     const TpComm& c, uint32_t site, cudaStream_t s, uint32_t key_set) {
   if (rows == 0) return SNL_OK;
+  if (rows > kTpKeyRows || key_set >= kTpKeySets) return fail(SNL_E_RANGE, "argmax_tp: rows or key set out of range");
   SNL_PDL_LAUNCH("argmax_pass1", argmax_pass1, dim3(dim3(kArgBlocks, rows)), dim3(512), (size_t)(0), s, logits, vl, part,
                  c.rank == 0 ? 1 : 0);
   SNL_PDL_LAUNCH("argmax_tp_pass2", argmax_tp_pass2, dim3(rows), dim3(32), (size_t)(0), s, part, kArgBlocks, vl, c, site,
-                 out_idx);
+                 key_set, out_idx);
   return SNL_OK;
 }
 

@@ -7,7 +7,8 @@
 //   bulk parts        [2 parities][MAX_M * hidden] f32: the prefill allreduce's input;
 //   ll                [2 parities][src][4 tokens][rows] u64: row-parallel GEMV partials
 //                     pushed by each peer, each value tagged with its exchange's epoch;
-//   llkeys            [2 rows][src][2] u64: the greedy argmax candidates, tagged alike;
+//   llkeys            [3 sets][2 rows][src][2] u64: the greedy argmax candidates, tagged
+//                     alike (set 0: forward steps; sets 1, 2: MTP drafts, alternately);
 //   logits            [2 rows][vocab / N] f32: this rank's LM-head shard.
 // The decode exchanges (GEMV partials, argmax keys) use tagged words: the writer stores
 // (epoch << 32 | value) into the peer's memory with one 64-bit system-scope store, and
@@ -21,6 +22,11 @@
 // timer (TpComm::wait_ns, 2 s unless SNL_TP_WAIT_MS says otherwise); one that runs out
 // sets bit 1 of the device error word and the kernel carries on. A wait that finds bit 1
 // already set gives up at once, so a dead peer costs one bound per step, not one per wait.
+// An MTP draft (replicated MTP layer, vocabulary-split head) is a step of its own: its
+// embedding advances the counter, and its only exchange is the argmax. Two drafts may
+// follow each other with no other exchange between them, so drafts alternate between two
+// key slot sets of their own: a set is rewritten only after the other set's exchange,
+// which every peer joins after reading the first.
 #pragma once
 #include <stdint.h>
 
@@ -31,6 +37,9 @@ namespace snl {
 constexpr int kTpMax = 8;
 constexpr uint32_t kTpSlots = 1024;  // flag slots per rank
 constexpr unsigned long long kTpWaitNs = 2000000000ull;  // default bound of one cross-GPU wait
+// Argmax key slots: [kTpKeySets][kTpKeyRows][src][2] tagged words per rank.
+constexpr uint32_t kTpKeySets = 3;
+constexpr uint32_t kTpKeyRows = 2;
 
 // Device view of the communicator (passed by value to kernels).
 struct TpComm {
@@ -153,8 +162,9 @@ constexpr uint32_t kSlotLogits = kTpSlots - 2;
 int launch_tp_allreduce(const TpComm& c, uint32_t site, uint64_t n, float* out, cudaStream_t s);
 // Copies every rank's LM-head shard [rows][vl] into full[rows][vl * size].
 int launch_tp_gather_logits(const TpComm& c, uint32_t site, uint32_t rows, uint32_t vl, float* full, cudaStream_t s);
-// Greedy argmax over an LM-head shard [rows][vl] agreed by all ranks (layers.cu).
+// Greedy argmax over an LM-head shard [rows][vl] agreed by all ranks (layers.cu), through
+// key slot set key_set (0: forward steps; 1 and 2, alternately: MTP drafts).
 int launch_argmax_tp(const float* logits, uint32_t rows, uint32_t vl, uint32_t* out_idx, unsigned long long* part,
-                     const TpComm& c, uint32_t site, cudaStream_t s);
+                     const TpComm& c, uint32_t site, cudaStream_t s, uint32_t key_set = 0);
 
 }  // namespace snl

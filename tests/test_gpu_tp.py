@@ -1,7 +1,9 @@
 """Tensor parallelism on 2, 4 and 8 GPUs of one node (needs that many GPUs; skipped
 otherwise). Each case launches tests/tp_worker.py under torchrun, one process per GPU,
 with NVLS off, and checks the rank-0 verdict: logits within 1e-3 of the unsharded oracle,
-identical greedy tokens, all ranks agreeing, no device-side wait gave up."""
+identical greedy tokens, all ranks agreeing, no device-side wait gave up; and for the
+MTP head under tensor parallelism, the oracle's drafts, accept/reject decisions, verify
+logits and committed tokens."""
 import json
 import os
 import subprocess
@@ -42,3 +44,12 @@ def test_tensor_parallel_matches_oracle(torch_cuda, tmp_path, n):
     assert max(res["decode_rel"]) < TOL, res
     assert res["first_engine_token"] == res["first_oracle_token"]
     assert res["tokens_engine"] == res["tokens_oracle"], res
+    # MTP under tensor parallelism: drafts, decisions, verify rows and committed tokens
+    mt = res["mtp"]
+    assert mt["ranks_agree"], mt
+    assert mt["drafts_engine"] == mt["drafts_oracle"], mt
+    assert mt["verified_engine"] == mt["verified_oracle"], mt
+    assert mt["accept_engine"] == mt["accept_oracle"], mt
+    assert any(mt["accept_engine"]) and not all(mt["accept_engine"]), mt
+    assert max(mt["verify_rel"]) < TOL, mt
+    assert mt["committed_engine"] == mt["committed_oracle"] == mt["greedy"][: len(mt["committed_engine"])], mt

@@ -3,7 +3,10 @@ torchrun): the TP engine on the `tp_test` model against the oracle's unsharded m
 
 Rank 0 writes a JSON verdict to $SNL_TP_RESULT: prefill and per-step logits relative
 error, greedy tokens of the engine's device decode loop and of forward_greedy, and
-whether every rank produced the same tokens.
+whether every rank produced the same tokens. A second engine of the same model with an
+MTP head (replicated on every rank, vocabulary-split head) then runs the draft-1 /
+verify-2 loop: its drafts, accept/reject decisions, verify logits and committed tokens
+go into the verdict beside the oracle's.
 """
 import datetime
 import json
@@ -20,6 +23,10 @@ import torch.distributed as dist  # noqa: E402
 
 from sensenova_b200.config import tp_test  # noqa: E402
 from sensenova_b200.engine import Engine  # noqa: E402
+from spec_loop import spec_loop  # noqa: E402
+
+MTP_PROMPT = [2, 7, 1, 8, 2, 8, 1, 8, 2, 8]
+MTP_STEPS = 10
 
 
 def rel(a, b):
@@ -46,6 +53,22 @@ def main():
     allt = [torch.empty_like(mine) for _ in range(world)]
     dist.all_gather(allt, mine)
     same = all(bool((t == mine).all()) for t in allt)
+    # MTP: the true greedy continuation (from the model without the head, same seed)
+    # is verified on odd steps, so both the accept and the reject branch run.
+    eng.reset()
+    greedy = [int(np.argmax(eng.forward(MTP_PROMPT, True)))]
+    for _ in range(2 * MTP_STEPS + 2):
+        greedy.append(int(np.argmax(eng.forward([greedy[-1]], True))))
+
+    def forced(i, committed):
+        return greedy[len(committed)] if i % 2 == 1 else None
+
+    me = Engine.synthetic(cfg, ctx, seed, "q8_0", mtp=True, device=local, tp=(rank, world))
+    mlog, mcommit = spec_loop(me, MTP_PROMPT, MTP_STEPS, forced)
+    mine = torch.tensor([x[0] for x in mlog] + mcommit, dtype=torch.int64, device="cuda")
+    allt = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(allt, mine)
+    same_mtp = all(bool((t == mine).all()) for t in allt)
     err = int(eng.lib.snl_device_error(0))
     if rank == 0:
         sys.path.insert(0, str(ROOT / "oracle"))
@@ -71,8 +94,20 @@ def main():
         res["device_error"] = err
         res["first_oracle_token"] = to
         res["first_engine_token"] = toks[0]
+        om = orc.OracleModel(cfg, ctx, seed=seed, quant=1, mtp=True)
+        olog, ocommit = spec_loop(om, MTP_PROMPT, MTP_STEPS, forced)
+        res["mtp"] = {
+            "drafts_engine": [x[0] for x in mlog], "drafts_oracle": [x[0] for x in olog],
+            "verified_engine": [x[1] for x in mlog], "verified_oracle": [x[1] for x in olog],
+            "accept_engine": [x[2] for x in mlog], "accept_oracle": [x[2] for x in olog],
+            "verify_rel": [rel(a[3], b[3]) for a, b in zip(mlog, olog)],
+            "committed_engine": mcommit, "committed_oracle": ocommit, "greedy": greedy,
+            "ranks_agree": same_mtp,
+        }
         Path(os.environ["SNL_TP_RESULT"]).write_text(json.dumps(res))
+        om.close()
         o.close()
+    me.close()
     eng.close()
     dist.barrier()
     dist.destroy_process_group()
