@@ -58,7 +58,9 @@ def parse_args():
                     help="skip the BASELINE configs[4] leg (Q4_0 model, 32K context)")
     ap.add_argument("--cpu-budget-s", type=float, default=25.0)
     ap.add_argument("--profile", action="store_true", help="print the per-op table of one decode step")
-    ap.add_argument("--turns", type=int, default=4, help="mtp workload: turns (BASELINE config 4 names 1000)")
+    ap.add_argument("--turns", type=int, default=4, help="mtp workload: turns (BASELINE configs[3] names 1000)")
+    ap.add_argument("--worker-turns", type=int, default=None,
+                    help="mtp workload: turns of the snl_worker pass (default: --turns)")
     ap.add_argument("--workload", choices=["decode", "gemv", "gemm", "deltanet", "mtp", "vision"], default="decode",
                     help="gemv: only BASELINE configs[0], the one-token Q8_0 GEMV 12288x4096; "
                          "gemm: one prefill-chunk GEMM (512 tokens x 12288 x 4096) on the tcgen05 kernel")
@@ -762,7 +764,8 @@ def run_mtp(args):
     w = Worker(eng)
     wk = {"turns": 0, "tokens": 0, "decode_s": 0.0, "prefill_s": 0.0, "drafted": 0, "accepted": 0, "cached": 0}
     cold_prefill_s = 0.0
-    for turn in range(args.turns + 1):
+    worker_turns = args.turns if args.worker_turns is None else args.worker_turns
+    for turn in range(worker_turns + 1):
         prompt = prefix_ids + rng.integers(0, cfg.vocab, full - prefix).tolist()
         _, fin = w.run(prompt, GREEDY, dec, snapshot_at=prefix)
         wk["drafted"] += fin.drafted
@@ -782,7 +785,7 @@ def run_mtp(args):
         "value": produced / dec_s, "unit": "tok/s", "n_gpus": 1, "higher_is_better": True,
         "acceptance": accepted / max(drafted, 1), "drafted": drafted, "accepted": accepted,
         "e2e_tok_s_with_feed": produced / (dec_s + feed_s), "feed_tok_s": args.turns * (full - prefix) / feed_s,
-        "prefix_prefill_s": prefix_s, "turns": args.turns, "dtype": "f32 (int8 weights)", "data": "synthetic",
+        "prefix_prefill_s": prefix_s, "turns": args.turns, "dtype": "int8 weights, x as fp16 hi+lo (~22 bits), fp32 accumulate", "data": "synthetic",
         "worker": {
             "what": "the same turns as requests to snl_worker_run (prefix cache, drafting with self-pause)",
             "decode_tok_s": wk["tokens"] / max(wk["decode_s"], 1e-9),
@@ -795,7 +798,9 @@ def run_mtp(args):
             "drafting_after": {"on": spec_on, "pause_requests_left": pause},
         },
         "config": {"workload": f"BASELINE configs[3]: 12K-token prefix snapshot, feed to 16K, {dec} tokens per turn "
-                               f"with draft-1/verify-2, {args.turns} turns (1000 named; bounded sample)",
+                               f"with draft-1/verify-2, {args.turns} turns"
+                               + ("" if args.turns >= 1000 else " (1000 named; bounded sample)")
+                               + f"; worker pass {worker_turns} turns",
                    "quant": args.quant},
     }
     print(json.dumps(line), flush=True)
