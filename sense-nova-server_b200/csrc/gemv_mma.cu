@@ -528,8 +528,8 @@ __device__ __forceinline__ void fused_norm_prologue(const GemvArgs& a, int lane,
   }
 }
 
-template <int DT, int M, int WARPS, int S, typename ST, int CPS>
-__global__ void __launch_bounds__(WARPS * 32, CPS) gemv_pg_kernel(GemvArgs a, const uint8_t* __restrict__ tiles,
+template <int DT, int M, int WARPS, int S, typename ST>
+__global__ void __launch_bounds__(WARPS * 32, WARPS >= 16 ? 2 : 3) gemv_pg_kernel(GemvArgs a, const uint8_t* __restrict__ tiles,
                                                              const ST* __restrict__ ts, uint32_t groups, int* err) {
   using G = PgGeom<DT, WARPS, S, ST>;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -696,19 +696,19 @@ uint32_t pg_grid(uint32_t groups, uint32_t slots) {
   return (groups + q - 1) / q;
 }
 
-template <int DT, int M, int WARPS, int S, typename ST, int CPS>
+template <int DT, int M, int WARPS, int S, typename ST>
 int launch_pg_cfg(const GemvArgs& a, const void* tiles, const ST* ts, uint32_t groups, int* err, cudaStream_t s) {
   using G = PgGeom<DT, WARPS, S, ST>;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
-  auto kern = gemv_pg_kernel<DT, M, WARPS, S, ST, CPS>;
+  auto kern = gemv_pg_kernel<DT, M, WARPS, S, ST>;
   if (dev >= 0 && dev < 64 && !attr[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
     if (e != cudaSuccess) return cuda_fail(e, "gemv_pg: smem attribute");
     attr[dev] = true;
   }
-  const uint32_t grid = pg_grid(groups, (uint32_t)sm_count() * (WARPS >= 16 ? kPgCtasPerSm : CPS));
+  const uint32_t grid = pg_grid(groups, (uint32_t)sm_count() * kPgCtasPerSm);
   SNL_PDL_LAUNCH("gemv_pg", kern, dim3(grid), dim3(WARPS * 32), (size_t)G::kSmem, s, a,
                  static_cast<const uint8_t*>(tiles), ts, groups, err);
   return SNL_OK;
@@ -719,12 +719,8 @@ int launch_pg_t(const GemvArgs& a, const void* tiles, const ST* ts, int* err, cu
   const uint32_t groups = (a.n + 15) / 16;
   const bool few = groups <= 2u * (uint32_t)sm_count();
   constexpr int kSA = DT == SNL_Q8_0 ? 2 : 3;  // stages per warp, 8-warp CTA
-  if (few) return launch_pg_cfg<DT, M, 16, 1, ST, 2>(a, tiles, ts, groups, err, s);
-  if constexpr (DT == SNL_Q4_0) {
-    static const bool occ4 = getenv("SNL_Q4_OCC4") != nullptr;
-    if (occ4) return launch_pg_cfg<DT, M, 8, 2, ST, 4>(a, tiles, ts, groups, err, s);
-  }
-  return launch_pg_cfg<DT, M, 8, kSA, ST, 3>(a, tiles, ts, groups, err, s);
+  if (few) return launch_pg_cfg<DT, M, 16, 1, ST>(a, tiles, ts, groups, err, s);
+  return launch_pg_cfg<DT, M, 8, kSA, ST>(a, tiles, ts, groups, err, s);
 }
 
 }  // namespace
