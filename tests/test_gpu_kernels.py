@@ -110,10 +110,12 @@ def test_mat_rows(T, lib, orc, dtype, m):
 
 
 @pytest.mark.parametrize("dtype", [SNL_Q8_0, SNL_Q4_0])
-@pytest.mark.parametrize("n,k,m", [(1000, 2048, 256), (1000, 2048, 300), (4096, 4096, 512), (333, 160, 40), (18944, 256, 300)])
+@pytest.mark.parametrize("n,k,m", [(1000, 2048, 256), (1000, 2048, 300), (4096, 4096, 512), (333, 160, 40), (18944, 256, 300),
+                                   (12288, 4096, 512)])
 def test_mat_prefill_tensor_cores(T, lib, orc, dtype, n, k, m):
     """Prefill rows (m >= 8) run on the tcgen05 GEMM: several token and row tiles, a
-    partial last K block (k = 160), against the oracle's f32 GEMM."""
+    partial last K block (k = 160), against the oracle's f32 GEMM. 12288 x 4096 at 512
+    rows is a prefill step's own shape (192-token tiles with weight planes)."""
     y, ref = run_mat(T, lib, orc, dtype, n, k, m, seed=n + m)
     assert rel(y, ref) < TOL
     # Three fp16 hi/lo products; the tensor cores' fp32 accumulation over K leaves
@@ -122,10 +124,13 @@ def test_mat_prefill_tensor_cores(T, lib, orc, dtype, n, k, m):
 
 
 @pytest.mark.parametrize("dtype", [SNL_Q8_0, SNL_Q4_0])
-@pytest.mark.parametrize("n,k,m", [(1000, 2048, 300), (4096, 4096, 512), (333, 160, 40), (18944, 256, 300)])
+@pytest.mark.parametrize("n,k,m", [(1000, 2048, 300), (4096, 4096, 512), (333, 160, 40), (18944, 256, 300),
+                                   (12288, 4096, 512), (10240, 4096, 400)])
 def test_mat_weight_planes_bitwise(T, lib, dtype, n, k, m, orc):
     """Prefill GEMM with precomputed weight planes (A by TMA) == the dequantizing GEMM,
-    bit for bit: the same operand values, tiles and MMA order."""
+    bit for bit: the same operand values and MMA order over K, whatever the token tile
+    (the planes kernel takes 192-token tiles at 12288 x 4096 x 512 and 10240 x 4096 x 400,
+    the dequantizing one 256)."""
     rng = np.random.default_rng(n + k + m)
     q, s = orc.gen_quant(n + 3, "wp", dtype, n, k)
     x = rng.standard_normal(m * k).astype(np.float32)
