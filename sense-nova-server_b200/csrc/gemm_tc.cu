@@ -35,6 +35,7 @@
 
 #include "common.cuh"
 #include "ptx.cuh"
+#include "tc.cuh"
 
 namespace snl {
 namespace {
@@ -66,32 +67,6 @@ struct TcArgs {
   uint32_t y_off, y_stride, n_off;
   int* err;
 };
-
-// Shared-memory matrix descriptor: K-major operand with rows of RB bytes (128: 128-byte
-// swizzle; 64: 64-byte swizzle), 8-row core-matrix groups 8 * RB bytes apart (SBO),
-// descriptor version 1 (sm_100).
-template <uint32_t RB>
-__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
-  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)1 << 16;                 // leading byte offset (unused with a swizzle)
-  d |= (uint64_t)((8 * RB) >> 4) << 32;   // stride byte offset
-  d |= (uint64_t)1 << 46;                 // version
-  d |= (uint64_t)(RB == 128 ? 2 : 4) << 61;  // SWIZZLE_128B / SWIZZLE_64B
-  return d;
-}
-__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc)
-      : "memory");
-}
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
   asm volatile(

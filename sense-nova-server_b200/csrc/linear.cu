@@ -11,6 +11,7 @@
 
 #include "common.cuh"
 #include "ptx.cuh"
+#include "tc.cuh"
 
 namespace snl {
 namespace {
@@ -760,6 +761,407 @@ __global__ void __launch_bounds__(256) dn_prep_kernel(uint32_t m, snl_lin_p p, c
   if (tid == 0) rec[5 * kDnC * DK] = __expf(lam_c);
 }
 
+// ---------------------------------------------------------------------------
+// dn_prep on the tcgen05 tensor cores: the same record (P, R, W, U, Kd, gamma_C) as
+// dn_prep_kernel. Its large products run as tcgen05.mma (kind::f16, M = 128, f32
+// accumulators in tensor memory) on operands split into fp16 hi + lo, accumulating
+// hi*hi + hi*lo + lo*hi (about 22 significant bits, the same scheme as the prefill
+// GEMM; the dropped lo*lo term is below 2^-22 of each product). Every operand is scaled
+// by a power of two first, so hi and lo stay normal fp16 numbers: 2^14 for the unit-norm
+// q, k and Gamma K rows, and 2^(14 - e) for T, M T and V, where 2^e bounds the block's
+// largest magnitude. The scales are exact and are taken out of the accumulators.
+//   A: [K; Q] (128 x 128) times K^T (N = 64): rows 0-63 give K K^T, rows 64-127 Q K^T.
+//   Then on the CUDA cores and mma.sync: L and M with their decays, X = (I + L)^-1,
+//   T = X diag(beta), MT = M T (64 x 64 x 64).
+//   C: [T; MT] (128 x 64) times [Gamma K | V] (N = 2 x 128): rows 0-63 give W = T Gamma K
+//   and U = T V, rows 64-127 give M W and R = M U, so P = Gamma Q - M W.
+// One thread issues the MMAs; all 8 warps split the operands before and read the
+// accumulators (tcgen05.ld) after, meeting at CTA barriers and commit mbarriers.
+// Shared memory (~101 KB, so two CTAs share an SM and a 512-row step's 256 CTAs run in
+// one wave): 16 KB tiles of [128 rows][128 B] (one K block of 64 fp16; 16-byte chunk c
+// of row r stored at c ^ (r % 8)):
+//   [0, 64K):   [K; Q] hi (2 K blocks) and lo (2); later [T; MT] hi, lo and
+//               (Gamma K)^T hi, lo;
+//   [64K, ..):  X, M (then M T) and the inverse's scratch (f32); later V^T hi and lo.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kPtTile = 128 * 128;
+constexpr uint32_t kPtF32 = 2 * kDnC * kPrT * 4 + 3 * 16 * 16 * 4;  // X, M / MT, scratch
+constexpr size_t kPrepTcSmem = 4 * kPtTile + (kPtF32 > 2 * kPtTile ? kPtF32 : 2 * kPtTile) + 1024;
+constexpr uint32_t kPtTmemCols = 256;
+constexpr float kPtUnit = 16384.0f;  // 2^14: scale of the unit-norm operands
+
+__device__ __forceinline__ float pow2f(int e) { return __int_as_float((127 + e) << 23); }
+// 2^(14 - e) with 2^e > max: the scale that brings magnitudes up to max below 2^14.
+__device__ __forceinline__ int pt_scale_exp(float amax) {
+  int e = 0;
+  if (amax > 0.f) (void)frexpf(amax, &e);
+  return min(max(14 - e, -100), 100);
+}
+__device__ __forceinline__ uint32_t ph_pair(float a, float b, bool lo) {
+  const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+  if (!lo) return (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
+  const __half la = __float2half_rn(a - __half2float(ha)), lb = __float2half_rn(b - __half2float(hb));
+  return (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
+}
+// Element k of row r of a [128 rows] x (K blocks of 64) tile set, as fp16 hi and lo.
+__device__ __forceinline__ void pt_store1(uint8_t* hi, uint8_t* lo, uint32_t r, uint32_t k, float v) {
+  const uint32_t off = (k >> 6) * kPtTile + r * 128 + (((((k & 63) >> 3) ^ (r & 7))) << 4) + ((k & 7) << 1);
+  const __half h = __float2half_rn(v);
+  *reinterpret_cast<__half*>(hi + off) = h;
+  *reinterpret_cast<__half*>(lo + off) = __float2half_rn(v - __half2float(h));
+}
+// Elements k0 .. k0 + 7 (k0 % 8 == 0) of row r: one 16-byte chunk each of hi and lo.
+__device__ __forceinline__ void pt_store8(uint8_t* hi, uint8_t* lo, uint32_t r, uint32_t k0, const float* v) {
+  const uint32_t off = (k0 >> 6) * kPtTile + r * 128 + ((((k0 & 63) >> 3) ^ (r & 7)) << 4);
+  uint4 h, l;
+  h.x = ph_pair(v[0], v[1], false);
+  h.y = ph_pair(v[2], v[3], false);
+  h.z = ph_pair(v[4], v[5], false);
+  h.w = ph_pair(v[6], v[7], false);
+  l.x = ph_pair(v[0], v[1], true);
+  l.y = ph_pair(v[2], v[3], true);
+  l.z = ph_pair(v[4], v[5], true);
+  l.w = ph_pair(v[6], v[7], true);
+  *reinterpret_cast<uint4*>(hi + off) = h;
+  *reinterpret_cast<uint4*>(lo + off) = l;
+}
+
+// One split product: kbs K blocks (64 each) of A and B into the accumulator at d.
+__device__ __forceinline__ void pt_mma(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi, uint32_t b_lo,
+                                       uint32_t kbs, uint32_t idesc) {
+  for (uint32_t kb = 0; kb < kbs; kb++) {
+#pragma unroll
+    for (uint32_t kk = 0; kk < 4; kk++) {
+      const uint32_t o = kb * kPtTile + kk * 32;  // 16 fp16 along K inside the swizzled row
+      const uint64_t ah = sdesc<128>(a_hi + o), al = sdesc<128>(a_lo + o);
+      const uint64_t bh = sdesc<128>(b_hi + o), bl = sdesc<128>(b_lo + o);
+      tc_mma(d, ah, bh, idesc, (kb | kk) != 0);
+      tc_mma(d, ah, bl, idesc, 1);
+      tc_mma(d, al, bh, idesc, 1);
+    }
+  }
+}
+
+// Largest value of v over the CTA (every thread passes its own; all get the result).
+__device__ __forceinline__ float pt_block_max(float v, float* sh8) {
+  v = warp_max(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sh8[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = sh8[0];
+#pragma unroll
+  for (int w = 1; w < 8; w++) r = fmaxf(r, sh8[w]);
+  return r;
+}
+
+__global__ void __launch_bounds__(256, 2) dn_prep_tc_kernel(uint32_t m, snl_lin_p p, const float* __restrict__ proj,
+                                                            const float* __restrict__ conv_out,
+                                                            const float* __restrict__ lw, float* __restrict__ chunks,
+                                                            int* err) {
+  extern __shared__ uint8_t pt_raw[];
+  uint8_t* RA = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(pt_raw) + 1023) & ~(uintptr_t)1023);
+  uint8_t* RB = RA + 4 * kPtTile;
+  float* X = reinterpret_cast<float*>(RB);  // [C][kPrT]: L, then X = (I + L)^-1, then T
+  float* Mq = X + kDnC * kPrT;              // [C][kPrT]: M, then M T
+  float* tmp = Mq + kDnC * kPrT;            // [3][16][16]
+  __shared__ float lam[kDnC], beta[kDnC], elam[kDnC], rq[kDnC], rk[kDnC], red[8];
+  __shared__ uint64_t bar[2];
+  __shared__ uint32_t tmem_sh;
+  const uint32_t c = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t g = lane >> 2, t4 = lane & 3;
+  const uint32_t t0 = c * kDnC, ce = min(kDnC, m - t0);
+  const uint32_t kh = h / (p.n_v / p.n_k), cd = p.conv_dim, key_dim = p.n_k * DK;
+  const uint32_t b_off = cd + p.n_v * DV, a_off = b_off + p.n_v;
+  float* rec = chunks + ((uint64_t)h * gridDim.x + c) * kDnChunkFloats;
+  float* Pg = rec;
+  float* Rg = Pg + kDnC * DK;
+  float* Wg = Rg + kDnC * DV;
+  float* Ug = Wg + kDnC * DK;
+  float* Kd = Ug + kDnC * DV;
+  const float* qsrc = conv_out + kh * DK;
+  const float* ksrc = conv_out + key_dim + kh * DK;
+  const float* vsrc = conv_out + 2 * key_dim + h * DV;
+
+  if (tid == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_sh, kPtTmemCols);
+  // beta and the log decay of each token (as dn_prep_kernel).
+  if (tid < kDnC) {
+    const uint32_t t = tid;
+    const float neg_a = -__expf(lw[(uint64_t)cd * 4 + h]);
+    const float dt_bias = lw[(uint64_t)cd * 4 + p.n_v + h];
+    float bt = 0.f, lt = 0.f;
+    if (t < ce) {
+      const uint64_t prow = (uint64_t)(t0 + t) * p.proj_stride;
+      bt = 1.0f / (1.0f + __expf(-proj[prow + b_off + h]));
+      const float araw = proj[prow + a_off + h] + dt_bias;
+      const float sp = araw <= 20.0f ? log1pf(__expf(araw)) : araw;
+      lt = neg_a * sp;
+    }
+    lam[t] = lt;
+    beta[t] = bt;
+  }
+  // 1. The chunk's k (rows 0-63) and q (rows 64-127) rows, L2-normalised (the same sums
+  //    as dn_prep_kernel), times 2^14, split into the A tiles. Warp w takes rows w + 8 i
+  //    in two batches of 8, every load of a batch in flight before the first sum.
+#pragma unroll 1
+  for (uint32_t b = 0; b < 2; b++) {
+    float x[8][4];
+#pragma unroll
+    for (uint32_t i = 0; i < 8; i++) {
+      const uint32_t r = warp + 8 * (8 * b + i), t = r & (kDnC - 1);
+      const float* src = (r >= kDnC ? qsrc : ksrc) + (uint64_t)(t0 + t) * cd;
+#pragma unroll
+      for (int u = 0; u < 4; u++) x[i][u] = t < ce ? src[lane + 32 * u] : 0.f;
+    }
+#pragma unroll
+    for (uint32_t i = 0; i < 8; i++) {
+      const uint32_t r = warp + 8 * (8 * b + i), t = r & (kDnC - 1);
+      const bool isq = r >= kDnC;
+      float sq = 0.f;
+#pragma unroll
+      for (int u = 0; u < 4; u++) sq = fmaf(x[i][u], x[i][u], sq);
+      sq = warp_sum(sq);
+      const float rn = isq ? rsqrtf(sq + 1e-6f) * rsqrtf((float)DK) : rsqrtf(sq + 1e-6f);
+      if (lane == 0) (isq ? rq : rk)[t] = rn;
+#pragma unroll
+      for (int u = 0; u < 4; u++) pt_store1(RA, RA + 2 * kPtTile, r, lane + 32 * u, x[i][u] * rn * kPtUnit);
+    }
+  }
+  fence_proxy_async_smem();  // the tiles are read by the tensor cores (async proxy)
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_sh;
+  const uint32_t a_base = smem_u32(RA);
+  if (tid == 0) {
+    pt_mma(tmem, a_base, a_base + 2 * kPtTile, a_base, a_base + 2 * kPtTile, 2, tc_idesc_f16(kDnC));
+    tc_commit(&bar[0]);
+  } else if (tid == 32) {
+    float acc = 0.f;
+    for (uint32_t t = 0; t < kDnC; t++) {
+      acc += lam[t];
+      lam[t] = acc;
+    }
+  }
+  __syncthreads();
+  if (tid < kDnC) elam[tid] = __expf(lam[tid]);
+  bool ok = __syncthreads_and(mbar_wait_bounded(&bar[0], 0));
+  tc_fence_after();
+  // 2. L[t][s] = beta_t e^(lam_t - lam_s) k_t.k_s (s < t) and M[t][s] = e^(lam_t - lam_s) q_t.k_s
+  //    (s <= t) from the accumulator: warp w reads lanes 32 (w % 4).. (the rows), columns
+  //    32 (w / 4) ..
+  if (ok) {
+    const uint32_t quarter = warp & 3, half = warp >> 2;
+    float v[32];
+    tmem_ld32(tmem + ((quarter * 32) << 16) + 32 * half, v);
+    const uint32_t row = quarter * 32 + lane, t = row & (kDnC - 1);
+    const float unscale = 1.0f / (kPtUnit * kPtUnit);
+#pragma unroll
+    for (int j = 0; j < 32; j++) {
+      const uint32_t s2 = 32 * half + j;
+      const float e = s2 <= t ? __expf(lam[t] - lam[s2]) : 0.f;
+      const float gv = v[j] * unscale;
+      if (row < kDnC) X[t * kPrT + s2] = s2 < t ? beta[t] * e * gv : 0.f;
+      else Mq[t * kPrT + s2] = s2 <= t ? e * gv : 0.f;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  // 3. X = (I + L)^-1 (as dn_prep_kernel: diagonal 16-blocks by forward substitution,
+  //    then the off-diagonal blocks row by row).
+  if (warp < 2) {
+    const uint32_t bb = warp * 2 + (lane >> 4), cc = lane & 15, o = 16 * bb;
+    float x[16];
+#pragma unroll
+    for (uint32_t r = 0; r < 16; r++) {
+      float acc = 0.f;
+#pragma unroll
+      for (uint32_t k = 0; k < r; k++) acc = fmaf(X[(o + r) * kPrT + o + k], x[k], acc);
+      x[r] = r == cc ? 1.f : (r < cc ? 0.f : -acc);
+    }
+    __syncwarp();
+#pragma unroll
+    for (uint32_t r = 0; r < 16; r++) X[(o + r) * kPrT + o + cc] = x[r];
+  }
+  __syncthreads();
+  {
+    const uint32_t r = tid >> 4, cc = tid & 15;
+    for (uint32_t i = 1; i < 4; i++) {
+      for (uint32_t j = 0; j < i; j++) {
+        float acc = 0.f;
+        for (uint32_t k = j; k < i; k++)
+#pragma unroll
+          for (uint32_t q = 0; q < 16; q++)
+            acc = fmaf(X[(16 * i + r) * kPrT + 16 * k + q], X[(16 * k + q) * kPrT + 16 * j + cc], acc);
+        tmp[(j * 16 + r) * 16 + cc] = acc;
+      }
+      __syncthreads();
+      for (uint32_t j = 0; j < i; j++) {
+        float acc = 0.f;
+#pragma unroll
+        for (uint32_t q = 0; q < 16; q++) acc = fmaf(X[(16 * i + r) * kPrT + 16 * i + q], tmp[(j * 16 + q) * 16 + cc], acc);
+        X[(16 * i + r) * kPrT + 16 * j + cc] = -acc;
+      }
+      __syncthreads();
+    }
+  }
+  float amax = 0.f;
+  for (uint32_t e = tid; e < kDnC * kDnC; e += blockDim.x) {
+    const uint32_t t = e / kDnC, s2 = e % kDnC;
+    const float tv = s2 <= t ? X[t * kPrT + s2] * beta[s2] : 0.f;
+    X[t * kPrT + s2] = tv;
+    amax = fmaxf(amax, fabsf(tv));
+  }
+  __syncthreads();
+  // 4. MT = M T (both lower triangular), 3xTF32 mma.sync: warp w takes row tile w / 2 and
+  //    column tiles 4 (w % 2) .. + 3; M T replaces M once every warp has read it.
+  {
+    const uint32_t mt = warp >> 1, kend = 16 * (mt + 1);
+    float acc[4][4] = {};
+    for (uint32_t k = 0; k < kend; k += 8) {
+      uint32_t ah[4], al[4];
+      split_a(Mq + (16 * mt + g) * kPrT + k + t4, kPrT, ah, al);
+#pragma unroll
+      for (uint32_t q = 0; q < 4; q++) {
+        const uint32_t nt = (warp & 1) * 4 + q;
+        const float* bt = X + (k + t4) * kPrT + 8 * nt + g;
+        uint32_t bh[2], bl[2];
+        split_b(bt[0], bt[4 * kPrT], bh, bl);
+        mma3_split(acc[q], ah, al, bh, bl);
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (uint32_t q = 0; q < 4; q++) {
+      const uint32_t nt = (warp & 1) * 4 + q;
+#pragma unroll
+      for (int r = 0; r < 4; r++) {
+        const uint32_t t = 16 * mt + g + (r >= 2 ? 8 : 0), u = 8 * nt + 2 * t4 + (r & 1);
+        Mq[t * kPrT + u] = acc[q][r];
+        amax = fmaxf(amax, fabsf(acc[q][r]));
+      }
+    }
+  }
+  // 5. The operands of C: [T; MT] times 2^sa (tiles 0, 1 of [0, 64K)), (Gamma K)^T times
+  //    2^14 (tiles 2, 3), and Kd to the record.
+  const int sa = pt_scale_exp(pt_block_max(amax, red));
+  {
+    const float scale = pow2f(sa);
+    for (uint32_t e = tid; e < 2 * kDnC * (kDnC / 8); e += blockDim.x) {
+      const uint32_t r = e / (kDnC / 8), k0 = 8 * (e % (kDnC / 8));
+      const float* src = r < kDnC ? X + r * kPrT + k0 : Mq + (r - kDnC) * kPrT + k0;
+      const float4 a = *reinterpret_cast<const float4*>(src), b = *reinterpret_cast<const float4*>(src + 4);
+      const float v8[8] = {a.x * scale, a.y * scale, a.z * scale, a.w * scale,
+                           b.x * scale, b.y * scale, b.z * scale, b.w * scale};
+      pt_store8(RA, RA + kPtTile, r, k0, v8);
+    }
+  }
+  const float lam_c = lam[kDnC - 1];
+  {
+    const uint32_t i = tid & (DK - 1), sh = tid >> 7;  // feature i, tokens 32 sh ..
+    float kr[32];
+#pragma unroll
+    for (uint32_t u = 0; u < 32; u++) {
+      const uint32_t s2 = 32 * sh + u;
+      kr[u] = s2 < ce ? ksrc[(uint64_t)(t0 + s2) * cd + i] : 0.f;
+    }
+#pragma unroll
+    for (uint32_t s0 = 0; s0 < 32; s0 += 8) {
+      float gk[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const uint32_t s2 = 32 * sh + s0 + u;
+        const float kv = kr[s0 + u] * rk[s2];
+        Kd[s2 * DK + i] = __expf(lam_c - lam[s2]) * kv;
+        gk[u] = kv * elam[s2] * kPtUnit;
+      }
+      pt_store8(RA + 2 * kPtTile, RA + 3 * kPtTile, i, 32 * sh + s0, gk);
+    }
+  }
+  // V rows of the chunk (registers) and their largest magnitude.
+  const uint32_t vi = tid & (DV - 1), vsh = tid >> 7;
+  float vr[32], vmax = 0.f;
+#pragma unroll
+  for (uint32_t u = 0; u < 32; u++) {
+    const uint32_t s2 = 32 * vsh + u;
+    vr[u] = s2 < ce ? vsrc[(uint64_t)(t0 + s2) * cd + vi] : 0.f;
+    vmax = fmaxf(vmax, fabsf(vr[u]));
+  }
+  fence_proxy_async_smem();
+  const int sv = pt_scale_exp(pt_block_max(vmax, red));  // its barriers also publish the tiles above
+  if (tid == 0) {
+    tc_fence_after();
+    pt_mma(tmem, a_base, a_base + kPtTile, a_base + 2 * kPtTile, a_base + 3 * kPtTile, 1, tc_idesc_f16(DK));
+  }
+  // V^T times 2^sv into [64K, 96K) (X and M T are no longer read) while W and M W run.
+  {
+    const float scale = pow2f(sv);
+#pragma unroll
+    for (uint32_t s0 = 0; s0 < 32; s0 += 8) {
+      float v8[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) v8[u] = vr[s0 + u] * scale;
+      pt_store8(RB, RB + kPtTile, vi, 32 * vsh + s0, v8);
+    }
+  }
+  fence_proxy_async_smem();
+  __syncthreads();
+  if (tid == 0) {
+    tc_fence_after();
+    pt_mma(tmem + DK, a_base, a_base + kPtTile, smem_u32(RB), smem_u32(RB) + kPtTile, 1, tc_idesc_f16(DV));
+    tc_commit(&bar[1]);
+  }
+  ok = __syncthreads_and(ok && mbar_wait_bounded(&bar[1], 0));
+  tc_fence_after();
+  // 6. Epilogue: warp w reads lanes 32 (w % 4).. and columns 128 (w / 4) ..: W and U
+  //    (rows 0-63), M W and M U (rows 64-127), each times its operands' inverse scales.
+  if (ok) {
+    const uint32_t quarter = warp & 3, half = warp >> 2;
+    const uint32_t row = quarter * 32 + lane, t = row & (kDnC - 1);
+    const bool upper = row >= kDnC;
+    const float unscale = pow2f(-sa) * (half ? pow2f(-sv) : 1.0f / kPtUnit);
+    for (uint32_t cb = 0; cb < 4; cb++) {
+      float v[32];
+      tmem_ld32(tmem + ((quarter * 32) << 16) + 128 * half + 32 * cb, v);
+#pragma unroll
+      for (int j = 0; j < 32; j++) v[j] *= unscale;
+      const uint32_t i0 = 32 * cb;
+      if (!upper) {
+        float* dst = (half ? Ug : Wg) + t * DK + i0;
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+          *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+      } else if (half) {
+        float* dst = Rg + t * DV + i0;
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+          *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+      } else {
+        const float* qr = qsrc + (uint64_t)(t0 + t) * cd + i0;
+        float* dst = Pg + t * DK + i0;
+        const float sc = rq[t], el = elam[t];
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          float4 qv = t < ce ? *reinterpret_cast<const float4*>(qr + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+          *reinterpret_cast<float4*>(dst + j) =
+              make_float4(fmaf(el, qv.x * sc, -v[j]), fmaf(el, qv.y * sc, -v[j + 1]), fmaf(el, qv.z * sc, -v[j + 2]),
+                          fmaf(el, qv.w * sc, -v[j + 3]));
+        }
+      }
+    }
+  } else if (tid == 0) {
+    report_timeout(err);
+  }
+  if (tid == 0) rec[5 * kDnC * DK] = __expf(lam_c);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kPtTmemCols);
+}
+
 // Carries one head's state slice (all 128 rows, kDnCols columns) through the chunks of
 // the step on the tensor cores, writing the pre-norm outputs O = P S0 + R of its
 // columns. 8 warps; per chunk: O and W S (64 x 32, K = 128: two 16 x 8 tiles per warp),
@@ -954,11 +1356,21 @@ int launch_conv_delta_chunked(uint32_t m, const snl_lin_p& p, const float* proj,
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr[dev]) {
     SNL_CUDA_TRY(cudaFuncSetAttribute(dn_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem));
+    SNL_CUDA_TRY(cudaFuncSetAttribute(dn_prep_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPrepTcSmem));
     SNL_CUDA_TRY(cudaFuncSetAttribute(dn_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)scan_smem));
     attr[dev] = true;
   }
-  dn_prep_kernel<<<dim3(nch, p.n_v), 256, prep_smem, s>>>(m, p, proj, conv_out, lw, scratch);
-  SNL_LAUNCH_CHECK("dn_prep");
+  // SNL_DN_PREP_MMA=1: the mma.sync form of the chunk preparation (for comparison).
+  static const bool prep_tc = getenv("SNL_DN_PREP_MMA") == nullptr;
+  if (prep_tc) {
+    int* err = nullptr;
+    if (int rc = device_error_word(&err)) return rc;
+    dn_prep_tc_kernel<<<dim3(nch, p.n_v), 256, kPrepTcSmem, s>>>(m, p, proj, conv_out, lw, scratch, err);
+    SNL_LAUNCH_CHECK("dn_prep_tc");
+  } else {
+    dn_prep_kernel<<<dim3(nch, p.n_v), 256, prep_smem, s>>>(m, p, proj, conv_out, lw, scratch);
+    SNL_LAUNCH_CHECK("dn_prep");
+  }
   dn_scan_kernel<<<dim3(DV / kDnCols, p.n_v), 256, scan_smem, s>>>(m, nch, p, scratch, state, out);
   SNL_LAUNCH_CHECK("dn_scan");
   dn_norm_kernel<<<dim3(m, p.n_v), DV, 0, s>>>(p, proj, lw, out);
