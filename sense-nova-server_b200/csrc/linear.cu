@@ -1179,6 +1179,8 @@ __global__ void __launch_bounds__(256) dn_scan_kernel(uint32_t m, uint32_t n_chu
   float* Wb = Pb + 2 * kDnC * kScA;        // [2][C][kScA] W of this chunk and the next
   float* Kb = Wb + 2 * kDnC * kScA;        // [C][kScKd] Kd
   float* D = Kb + kDnC * kScKd;            // [C][kScS]
+  float* Ub = D + kDnC * kScS;             // [C][kScS] this slice's columns of U
+  float* Rb = Ub + kDnC * kScS;            // [C][kScS] this slice's columns of R
   const uint32_t slice = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
   const uint32_t warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
   const uint32_t j0 = slice * kDnCols;
@@ -1194,8 +1196,18 @@ __global__ void __launch_bounds__(256) dn_scan_kernel(uint32_t m, uint32_t n_chu
       cp_async16(dst + r * stride + 4 * q, src + 4 * e);
     }
   };
+  // This slice's columns of U and R (single-buffered: chunk c + 1's are fetched once
+  // chunk c's outputs have read them).
+  auto copy_slice = [&](float* dst, const float* src) {
+    for (uint32_t e = tid; e < kDnC * kDnCols / 4; e += blockDim.x) {
+      const uint32_t r = e / (kDnCols / 4), q = e % (kDnCols / 4);
+      cp_async16(dst + r * kScS + 4 * q, src + r * DV + j0 + 4 * q);
+    }
+  };
   copy_rows(Pb, kScA, rec_of(0));
   copy_rows(Wb, kScA, rec_of(0) + 2 * kDnC * DK);
+  copy_slice(Ub, rec_of(0) + 3 * kDnC * DK);
+  copy_slice(Rb, rec_of(0) + kDnC * DK);
   cp_async_commit();
   copy_rows(Kb, kScKd, rec_of(0) + 4 * kDnC * DK);
   cp_async_commit();
@@ -1203,8 +1215,6 @@ __global__ void __launch_bounds__(256) dn_scan_kernel(uint32_t m, uint32_t n_chu
   const uint32_t mt = warp >> 1, nt0 = (warp & 1) * 2;
   for (uint32_t c = 0; c < n_chunks; c++) {
     const float* rec = rec_of(c);
-    const float* R = rec + kDnC * DK;
-    const float* Ug = rec + 3 * kDnC * DK;
     const float gC = rec[5 * kDnC * DK];
     const uint32_t t0 = c * kDnC, ce = min(kDnC, m - t0);
     float* A = Pb + (c & 1) * kDnC * kScA;
@@ -1234,8 +1244,8 @@ __global__ void __launch_bounds__(256) dn_scan_kernel(uint32_t m, uint32_t n_chu
 #pragma unroll
       for (int r = 0; r < 4; r++) {
         const uint32_t t = 16 * mt + g + (r >= 2 ? 8 : 0), j = 8 * (nt0 + q) + 2 * t4 + (r & 1);
-        D[t * kScS + j] = Ug[t * DV + j0 + j] - ws[q][r];
-        if (t < ce) out[(uint64_t)(t0 + t) * p.n_v * DV + h * DV + j0 + j] = o[q][r] + R[t * DV + j0 + j];
+        D[t * kScS + j] = Ub[t * kScS + j] - ws[q][r];
+        if (t < ce) out[(uint64_t)(t0 + t) * p.n_v * DV + h * DV + j0 + j] = o[q][r] + Rb[t * kScS + j];
       }
     }
     const bool more = c + 1 < n_chunks;
@@ -1249,6 +1259,11 @@ __global__ void __launch_bounds__(256) dn_scan_kernel(uint32_t m, uint32_t n_chu
       cp_async_wait<0>();
     }
     __syncthreads();
+    if (more) {  // every thread has read this chunk's U and R
+      copy_slice(Ub, rec_of(c + 1) + 3 * kDnC * DK);
+      copy_slice(Rb, rec_of(c + 1) + kDnC * DK);
+      cp_async_commit();
+    }
     // S = gamma_C S + Kd^T D: the warp's four tiles are state rows 16 * (warp % 8) and
     // columns 8 * nt, nt = 0..3. A(i, t) = Kd[t][i].
     A = Kb;
@@ -1350,7 +1365,7 @@ int launch_conv_delta_chunked(uint32_t m, const snl_lin_p& p, const float* proj,
   if (int rc = launch_conv(step_val(sv), p, proj, conv_out, conv_state, lw, nullptr, s)) return rc;
   const uint32_t nch = (m + kDnC - 1) / kDnC;
   const size_t prep_smem = kPrepSmemFloats * sizeof(float);
-  const size_t scan_smem = (DK * kScS + 4 * kDnC * kScA + kDnC * kScKd + kDnC * kScS) * sizeof(float);
+  const size_t scan_smem = (DK * kScS + 4 * kDnC * kScA + kDnC * kScKd + 3 * kDnC * kScS) * sizeof(float);
   static bool attr[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
