@@ -452,14 +452,24 @@ __global__ void __launch_bounds__(kCsThreads)
 //   o_t  = S_t^T q_t  =>  O = P S0 + R, P = Gamma Q - M W, R = M U,
 //          M[t][s] = (gamma_t/gamma_s) q_t.k_s (s <= t)
 //   S_C  = gamma_C S0 + Kd^T D,  Kd[s] = (gamma_C/gamma_s) k_s.
-// dn_prep_kernel builds P, R, W, U, Kd and gamma_C for every (head, chunk) in parallel;
-// dn_scan_kernel carries the state through the chunks (each 32-column slice of a head's
-// state is independent, so a head spans 4 CTAs); dn_norm_kernel applies the gated
-// RMSNorm of the outputs. All of it is fp32.
+// dn_prep_tc_kernel builds each (head, chunk)'s record in parallel: R and U as f32,
+// [P; W] and Kd^T already split into the fp16 hi / lo tiles that the scan's tensor-core
+// products read, gamma_C and the scale of [P; W]. dn_scan_tc_kernel carries the state
+// through the chunks (each 32-column slice of a head's state is independent, so a head
+// spans 4 CTAs); dn_norm_kernel applies the gated RMSNorm of the outputs. Products use
+// f32 accumulation of operands split into hi + lo parts.
 // ---------------------------------------------------------------------------
 constexpr uint32_t kDnC = 64;                 // tokens per chunk
 constexpr uint32_t kDnCols = 32;              // state columns per scan CTA
-constexpr uint32_t kDnChunkFloats = 5 * kDnC * DK + 4;  // P, R, W, U, Kd, gamma_C (+pad)
+// A chunk record, in floats: R [C][128] and U [C][128] (f32); [P; W] as 4 tiles of 16 KB
+// (fp16 hi K blocks 0 and 1, then lo; rows 0-63 P, 64-127 W, K = the key dimension);
+// Kd^T as 2 tiles (hi, lo; rows = the key dimension, K = token); then gamma_C and the
+// [P; W] scale exponent. The tiles are the scan's shared-memory image (128-byte rows,
+// 16-byte chunk c of row r at c ^ (r % 8)).
+constexpr uint32_t kRecTile = 128 * 128 / 4;  // floats of one 16 KB tile
+constexpr uint32_t kRecR = 0, kRecU = kDnC * DV, kRecPW = 2 * kDnC * DV, kRecKd = kRecPW + 4 * kRecTile,
+                   kRecScal = kRecKd + 2 * kRecTile;
+constexpr uint32_t kDnChunkFloats = kRecScal + 64;
 
 struct DnScratch {
   float* chunks;  // [n_v][n_chunks][kDnChunkFloats]
@@ -513,263 +523,17 @@ __device__ __forceinline__ void mma3_split(float d[4], const uint32_t ah[4], con
   mma_tf32(d, ah, bh[0], bh[1]);
 }
 
-// Per (chunk, value head): P, R, W, U, Kd and gamma_C of the WY form, on the tensor
-// cores (3xTF32). Shared memory: the chunk's q, k, v rows (row stride 132), L / X / T
-// and M (64 x 68), W and U (64 x 132).
-constexpr uint32_t kPrS = 132, kPrT = 68;
-constexpr size_t kPrepSmemFloats = 5 * kDnC * kPrS + 2 * kDnC * kPrT;
-
-__global__ void __launch_bounds__(256) dn_prep_kernel(uint32_t m, snl_lin_p p, const float* __restrict__ proj,
-                                                      const float* __restrict__ conv_out, const float* __restrict__ lw,
-                                                      float* __restrict__ chunks) {
-  extern __shared__ __align__(16) float dsm[];
-  float* kn = dsm;                 // [C][kPrS]: k, then Gamma K
-  float* qn = kn + kDnC * kPrS;    // [C][kPrS]
-  float* vv = qn + kDnC * kPrS;    // [C][kPrS]
-  float* W = vv + kDnC * kPrS;     // [C][kPrS]
-  float* U = W + kDnC * kPrS;      // [C][kPrS]
-  float* X = U + kDnC * kPrS;      // [C][kPrT]: L, then X = (I + L)^-1, then T = X diag(beta)
-  float* Mq = X + kDnC * kPrT;     // [C][kPrT]
-  __shared__ float lam[kDnC], beta[kDnC], elam[kDnC];
-  const uint32_t c = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const uint32_t g = lane >> 2, t4 = lane & 3;
-  const uint32_t t0 = c * kDnC, ce = min(kDnC, m - t0);
-  const uint32_t kh = h / (p.n_v / p.n_k), cd = p.conv_dim, key_dim = p.n_k * DK;
-  const uint32_t b_off = cd + p.n_v * DV, a_off = b_off + p.n_v;
-  float* rec = chunks + ((uint64_t)h * gridDim.x + c) * kDnChunkFloats;
-  float* Pg = rec;
-  float* Rg = Pg + kDnC * DK;
-  float* Wg = Rg + kDnC * DV;
-  float* Ug = Wg + kDnC * DK;
-  float* Kd = Ug + kDnC * DV;
-  // 1. q, k, v rows of the chunk (zero past the step's end), then per-token norms.
-  for (uint32_t e = tid; e < kDnC * DK; e += blockDim.x) {
-    const uint32_t t = e / DK, i = e % DK;
-    const bool in = t < ce;
-    const uint64_t row = (uint64_t)(t0 + t) * cd;
-    qn[t * kPrS + i] = in ? conv_out[row + kh * DK + i] : 0.f;
-    kn[t * kPrS + i] = in ? conv_out[row + key_dim + kh * DK + i] : 0.f;
-    vv[t * kPrS + i] = in ? conv_out[row + 2 * key_dim + h * DV + i] : 0.f;
-  }
-  __syncthreads();
-  for (uint32_t t = warp; t < kDnC; t += blockDim.x / 32) {
-    float sq = 0.f, sk = 0.f;
-    for (uint32_t i = lane; i < DK; i += 32) {
-      sq = fmaf(qn[t * kPrS + i], qn[t * kPrS + i], sq);
-      sk = fmaf(kn[t * kPrS + i], kn[t * kPrS + i], sk);
-    }
-    sq = warp_sum(sq);
-    sk = warp_sum(sk);
-    const float rq = rsqrtf(sq + 1e-6f) * rsqrtf((float)DK), rk = rsqrtf(sk + 1e-6f);
-    for (uint32_t i = lane; i < DK; i += 32) {
-      qn[t * kPrS + i] *= rq;
-      kn[t * kPrS + i] *= rk;
-    }
-  }
-  // beta and the log decay of each token in parallel (their loads and transcendentals),
-  // then the prefix sum of the decays in token order on one thread.
-  if (tid < kDnC) {
-    const uint32_t t = tid;
-    const float neg_a = -__expf(lw[(uint64_t)cd * 4 + h]);
-    const float dt_bias = lw[(uint64_t)cd * 4 + p.n_v + h];
-    float bt = 0.f, lt = 0.f;
-    if (t < ce) {
-      const uint64_t prow = (uint64_t)(t0 + t) * p.proj_stride;
-      bt = 1.0f / (1.0f + __expf(-proj[prow + b_off + h]));
-      const float araw = proj[prow + a_off + h] + dt_bias;
-      const float sp = araw <= 20.0f ? log1pf(__expf(araw)) : araw;
-      lt = neg_a * sp;
-    }
-    lam[t] = lt;
-    beta[t] = bt;
-  }
-  __syncthreads();
-  if (tid == 0) {
-    float acc = 0.f;
-    for (uint32_t t = 0; t < kDnC; t++) {
-      acc += lam[t];
-      lam[t] = acc;
-    }
-  }
-  __syncthreads();
-  if (tid < kDnC) elam[tid] = __expf(lam[tid]);
-  __syncthreads();
-  // 2. Gram matrices K K^T and Q K^T (64 x 64, K = 128): warp w takes row tile w / 2 and
-  //    column tiles 4 (w % 2) .. + 3; tiles wholly above the diagonal are zero. Then
-  //    L[t][s] = beta_t e^(lam_t - lam_s) k_t.k_s (s < t), M[t][s] = e^(lam_t - lam_s) q_t.k_s (s <= t).
-  {
-    // The warp's 4 column tiles of both products in one k-loop: the A rows of k and q are
-    // split once per k-step, each k column once for both products.
-    const uint32_t mt = warp >> 1;
-    float gk[4][4] = {}, gq[4][4] = {};
-    const uint32_t nlive = min(4u, (16 * mt + 15) / 8 + 1 - min((16 * mt + 15) / 8 + 1, (warp & 1) * 4));
-#pragma unroll 2
-    for (uint32_t k = 0; k < DK; k += 8) {
-      uint32_t akh[4], akl[4], aqh[4], aql[4];
-      split_a(kn + (16 * mt + g) * kPrS + k + t4, kPrS, akh, akl);
-      split_a(qn + (16 * mt + g) * kPrS + k + t4, kPrS, aqh, aql);
-#pragma unroll
-      for (uint32_t q = 0; q < 4; q++) {
-        if (q >= nlive) break;
-        const uint32_t nt = (warp & 1) * 4 + q;
-        const float* br = kn + (8 * nt + g) * kPrS + k + t4;
-        uint32_t bh[2], bl[2];
-        split_b(br[0], br[4], bh, bl);
-        mma3_split(gk[q], akh, akl, bh, bl);
-        mma3_split(gq[q], aqh, aql, bh, bl);
-      }
-    }
-#pragma unroll
-    for (uint32_t q = 0; q < 4; q++) {
-      const uint32_t nt = (warp & 1) * 4 + q;
-#pragma unroll
-      for (int r = 0; r < 4; r++) {
-        const uint32_t t = 16 * mt + g + (r >= 2 ? 8 : 0), s2 = 8 * nt + 2 * t4 + (r & 1);
-        const float e = s2 <= t ? __expf(lam[t] - lam[s2]) : 0.f;
-        X[t * kPrT + s2] = s2 < t ? beta[t] * e * gk[q][r] : 0.f;
-        Mq[t * kPrT + s2] = s2 <= t ? e * gq[q][r] : 0.f;
-      }
-    }
-  }
-  // Kd = (gamma_C / gamma_t) k_t, then k becomes Gamma K in place.
-  const float lam_c = lam[kDnC - 1];
-  for (uint32_t e = tid; e < kDnC * DK; e += blockDim.x) {
-    const uint32_t t = e / DK, i = e % DK;
-    const float kv = kn[t * kPrS + i];
-    Kd[e] = __expf(lam_c - lam[t]) * kv;
-  }
-  __syncthreads();
-  for (uint32_t e = tid; e < kDnC * DK; e += blockDim.x) {
-    const uint32_t t = e / DK, i = e % DK;
-    kn[t * kPrS + i] *= elam[t];
-  }
-  // 3. X = (I + L)^-1, blocked by 16. Diagonal blocks: warps 0 and 1, half-warp per
-  //    block, lane c owns column c (forward substitution in registers).
-  if (warp < 2) {
-    const uint32_t bb = warp * 2 + (lane >> 4), cc = lane & 15, o = 16 * bb;
-    float x[16];
-#pragma unroll
-    for (uint32_t r = 0; r < 16; r++) {
-      float acc = 0.f;
-#pragma unroll
-      for (uint32_t k = 0; k < r; k++) acc = fmaf(X[(o + r) * kPrT + o + k], x[k], acc);
-      x[r] = r == cc ? 1.f : (r < cc ? 0.f : -acc);
-    }
-    __syncwarp();
-#pragma unroll
-    for (uint32_t r = 0; r < 16; r++) X[(o + r) * kPrT + o + cc] = x[r];
-  }
-  __syncthreads();
-  //    Off-diagonal blocks, block row i = 1..3: X_ij = -X_ii sum_{k=j}^{i-1} L_ik X_kj
-  //    for all j < i at once (L_ij is read before X_ij replaces it). Thread (r, cc).
-  {
-    const uint32_t r = tid >> 4, cc = tid & 15;
-    float* tmp = W;  // scratch [3][16][16]
-    for (uint32_t i = 1; i < 4; i++) {
-      for (uint32_t j = 0; j < i; j++) {
-        float acc = 0.f;
-        for (uint32_t k = j; k < i; k++)
-#pragma unroll
-          for (uint32_t q = 0; q < 16; q++)
-            acc = fmaf(X[(16 * i + r) * kPrT + 16 * k + q], X[(16 * k + q) * kPrT + 16 * j + cc], acc);
-        tmp[(j * 16 + r) * 16 + cc] = acc;
-      }
-      __syncthreads();
-      for (uint32_t j = 0; j < i; j++) {
-        float acc = 0.f;
-#pragma unroll
-        for (uint32_t q = 0; q < 16; q++) acc = fmaf(X[(16 * i + r) * kPrT + 16 * i + q], tmp[(j * 16 + q) * 16 + cc], acc);
-        X[(16 * i + r) * kPrT + 16 * j + cc] = -acc;
-      }
-      __syncthreads();
-    }
-  }
-  //    T = X diag(beta) (X has a unit diagonal; the upper part is zero).
-  for (uint32_t e = tid; e < kDnC * kDnC; e += blockDim.x) {
-    const uint32_t t = e / kDnC, s2 = e % kDnC;
-    X[t * kPrT + s2] = s2 <= t ? X[t * kPrT + s2] * beta[s2] : 0.f;
-  }
-  __syncthreads();
-  // 4. W = T Gamma K, U = T V (64 x 128, K = 64, T lower triangular): warp w takes row
-  //    tile w / 2 and column tiles 8 (w % 2) .. + 7.
-  {
-    // The warp's 8 column tiles of W and U in one k-loop (the T rows split once per k-step).
-    const uint32_t mt = warp >> 1, kend = 16 * (mt + 1);
-    float w[8][4] = {}, u[8][4] = {};
-#pragma unroll 1
-    for (uint32_t k = 0; k < kend; k += 8) {
-      uint32_t ah[4], al[4];
-      split_a(X + (16 * mt + g) * kPrT + k + t4, kPrT, ah, al);
-#pragma unroll
-      for (uint32_t q = 0; q < 8; q++) {
-        const uint32_t nt = (warp & 1) * 8 + q;
-        const float* bk = kn + (k + t4) * kPrS + 8 * nt + g;
-        const float* bv = vv + (k + t4) * kPrS + 8 * nt + g;
-        uint32_t kh[2], kl[2], vh[2], vl[2];
-        split_b(bk[0], bk[4 * kPrS], kh, kl);
-        split_b(bv[0], bv[4 * kPrS], vh, vl);
-        mma3_split(w[q], ah, al, kh, kl);
-        mma3_split(u[q], ah, al, vh, vl);
-      }
-    }
-#pragma unroll
-    for (uint32_t q = 0; q < 8; q++) {
-      const uint32_t nt = (warp & 1) * 8 + q;
-#pragma unroll
-      for (int r = 0; r < 4; r++) {
-        const uint32_t t = 16 * mt + g + (r >= 2 ? 8 : 0), i = 8 * nt + 2 * t4 + (r & 1);
-        W[t * kPrS + i] = w[q][r];
-        U[t * kPrS + i] = u[q][r];
-        Wg[t * DK + i] = w[q][r];
-        Ug[t * DV + i] = u[q][r];
-      }
-    }
-  }
-  __syncthreads();
-  // 5. P = Gamma Q - M W, R = M U (M lower triangular with diagonal).
-  {
-    // The warp's 8 column tiles of M W and M U in one k-loop.
-    const uint32_t mt = warp >> 1, kend = 16 * (mt + 1);
-    float pw[8][4] = {}, ru[8][4] = {};
-#pragma unroll 1
-    for (uint32_t k = 0; k < kend; k += 8) {
-      uint32_t ah[4], al[4];
-      split_a(Mq + (16 * mt + g) * kPrT + k + t4, kPrT, ah, al);
-#pragma unroll
-      for (uint32_t q = 0; q < 8; q++) {
-        const uint32_t nt = (warp & 1) * 8 + q;
-        const float* bw = W + (k + t4) * kPrS + 8 * nt + g;
-        const float* bu = U + (k + t4) * kPrS + 8 * nt + g;
-        uint32_t wh[2], wl[2], uh[2], ul[2];
-        split_b(bw[0], bw[4 * kPrS], wh, wl);
-        split_b(bu[0], bu[4 * kPrS], uh, ul);
-        mma3_split(pw[q], ah, al, wh, wl);
-        mma3_split(ru[q], ah, al, uh, ul);
-      }
-    }
-#pragma unroll
-    for (uint32_t q = 0; q < 8; q++) {
-      const uint32_t nt = (warp & 1) * 8 + q;
-#pragma unroll
-      for (int r = 0; r < 4; r++) {
-        const uint32_t t = 16 * mt + g + (r >= 2 ? 8 : 0), i = 8 * nt + 2 * t4 + (r & 1);
-        Pg[t * DK + i] = fmaf(elam[t], qn[t * kPrS + i], -pw[q][r]);
-        Rg[t * DV + i] = ru[q][r];
-      }
-    }
-  }
-  if (tid == 0) rec[5 * kDnC * DK] = __expf(lam_c);
-}
+constexpr uint32_t kPrT = 68;  // row stride (floats) of the 64 x 64 f32 blocks
 
 // ---------------------------------------------------------------------------
-// dn_prep on the tcgen05 tensor cores: the same record (P, R, W, U, Kd, gamma_C) as
-// dn_prep_kernel. Its large products run as tcgen05.mma (kind::f16, M = 128, f32
+// The chunk records on the tcgen05 tensor cores (dn_prep_tc_kernel, one CTA per (chunk,
+// value head)). Its large products run as tcgen05.mma (kind::f16, M = 128, f32
 // accumulators in tensor memory) on operands split into fp16 hi + lo, accumulating
-// hi*hi + hi*lo + lo*hi (about 22 significant bits, the same scheme as the prefill
-// GEMM; the dropped lo*lo term is below 2^-22 of each product). Every operand is scaled
-// by a power of two first, so hi and lo stay normal fp16 numbers: 2^14 for the unit-norm
-// q, k and Gamma K rows, and 2^(14 - e) for T, M T and V, where 2^e bounds the block's
-// largest magnitude. The scales are exact and are taken out of the accumulators.
+// hi*hi + hi*lo + lo*hi (about 22 significant bits, the same scheme as the prefill GEMM;
+// the dropped lo*lo term is below 2^-22 of each product). Every operand is scaled by a
+// power of two first, so hi and lo stay normal fp16 numbers: 2^14 for the unit-norm
+// q, k, Gamma K and Kd rows, and 2^(14 - e) for T, M T, V, P and W, where 2^e bounds the
+// block's largest magnitude. The scales are exact and are taken out of the accumulators.
 //   A: [K; Q] (128 x 128) times K^T (N = 64): rows 0-63 give K K^T, rows 64-127 Q K^T.
 //   Then on the CUDA cores and mma.sync: L and M with their decays, X = (I + L)^-1,
 //   T = X diag(beta), MT = M T (64 x 64 x 64).
@@ -873,11 +637,10 @@ __global__ void __launch_bounds__(256, 2) dn_prep_tc_kernel(uint32_t m, snl_lin_
   const uint32_t kh = h / (p.n_v / p.n_k), cd = p.conv_dim, key_dim = p.n_k * DK;
   const uint32_t b_off = cd + p.n_v * DV, a_off = b_off + p.n_v;
   float* rec = chunks + ((uint64_t)h * gridDim.x + c) * kDnChunkFloats;
-  float* Pg = rec;
-  float* Rg = Pg + kDnC * DK;
-  float* Wg = Rg + kDnC * DV;
-  float* Ug = Wg + kDnC * DK;
-  float* Kd = Ug + kDnC * DV;
+  float* Rg = rec + kRecR;
+  float* Ug = rec + kRecU;
+  uint8_t* PWg = reinterpret_cast<uint8_t*>(rec + kRecPW);
+  uint8_t* KdTg = reinterpret_cast<uint8_t*>(rec + kRecKd);
   const float* qsrc = conv_out + kh * DK;
   const float* ksrc = conv_out + key_dim + kh * DK;
   const float* vsrc = conv_out + 2 * key_dim + h * DV;
@@ -888,7 +651,7 @@ __global__ void __launch_bounds__(256, 2) dn_prep_tc_kernel(uint32_t m, snl_lin_
     fence_mbar_init();
   }
   if (warp == 0) tmem_alloc(&tmem_sh, kPtTmemCols);
-  // beta and the log decay of each token (as dn_prep_kernel).
+  // beta and the log decay of each token.
   if (tid < kDnC) {
     const uint32_t t = tid;
     const float neg_a = -__expf(lw[(uint64_t)cd * 4 + h]);
@@ -904,8 +667,8 @@ __global__ void __launch_bounds__(256, 2) dn_prep_tc_kernel(uint32_t m, snl_lin_
     lam[t] = lt;
     beta[t] = bt;
   }
-  // 1. The chunk's k (rows 0-63) and q (rows 64-127) rows, L2-normalised (the same sums
-  //    as dn_prep_kernel), times 2^14, split into the A tiles. Warp w takes rows w + 8 i
+  // 1. The chunk's k (rows 0-63) and q (rows 64-127) rows, L2-normalised (lane l sums
+  //    elements l + 32 u), times 2^14, split into the A tiles. Warp w takes rows w + 8 i
   //    in two batches of 8, every load of a batch in flight before the first sum.
 #pragma unroll 1
   for (uint32_t b = 0; b < 2; b++) {
@@ -971,8 +734,9 @@ __global__ void __launch_bounds__(256, 2) dn_prep_tc_kernel(uint32_t m, snl_lin_
   }
   tc_fence_before();
   __syncthreads();
-  // 3. X = (I + L)^-1 (as dn_prep_kernel: diagonal 16-blocks by forward substitution,
-  //    then the off-diagonal blocks row by row).
+  // 3. X = (I + L)^-1: diagonal 16-blocks by forward substitution (half a warp per
+  //    block, lane c owns column c), then the off-diagonal blocks row by row,
+  //    X_ij = -X_ii sum_{k=j}^{i-1} L_ik X_kj for all j < i at once.
   if (warp < 2) {
     const uint32_t bb = warp * 2 + (lane >> 4), cc = lane & 15, o = 16 * bb;
     float x[16];
@@ -1047,7 +811,7 @@ __global__ void __launch_bounds__(256, 2) dn_prep_tc_kernel(uint32_t m, snl_lin_
     }
   }
   // 5. The operands of C: [T; MT] times 2^sa (tiles 0, 1 of [0, 64K)), (Gamma K)^T times
-  //    2^14 (tiles 2, 3), and Kd to the record.
+  //    2^14 (tiles 2, 3); Kd^T times 2^14 to the record.
   const int sa = pt_scale_exp(pt_block_max(amax, red));
   {
     const float scale = pow2f(sa);
@@ -1071,15 +835,16 @@ __global__ void __launch_bounds__(256, 2) dn_prep_tc_kernel(uint32_t m, snl_lin_
     }
 #pragma unroll
     for (uint32_t s0 = 0; s0 < 32; s0 += 8) {
-      float gk[8];
+      float gk[8], kd[8];
 #pragma unroll
       for (int u = 0; u < 8; u++) {
         const uint32_t s2 = 32 * sh + s0 + u;
         const float kv = kr[s0 + u] * rk[s2];
-        Kd[s2 * DK + i] = __expf(lam_c - lam[s2]) * kv;
+        kd[u] = __expf(lam_c - lam[s2]) * kv * kPtUnit;  // Kd[s] = e^(lam_C - lam_s) k_s, times 2^14
         gk[u] = kv * elam[s2] * kPtUnit;
       }
       pt_store8(RA + 2 * kPtTile, RA + 3 * kPtTile, i, 32 * sh + s0, gk);
+      pt_store8(KdTg, KdTg + kPtTile, i, 32 * sh + s0, kd);  // the scan's Kd^T tiles
     }
   }
   // V rows of the chunk (registers) and their largest magnitude.
@@ -1117,199 +882,276 @@ __global__ void __launch_bounds__(256, 2) dn_prep_tc_kernel(uint32_t m, snl_lin_
   }
   ok = __syncthreads_and(ok && mbar_wait_bounded(&bar[1], 0));
   tc_fence_after();
-  // 6. Epilogue: warp w reads lanes 32 (w % 4).. and columns 128 (w / 4) ..: W and U
-  //    (rows 0-63), M W and M U (rows 64-127), each times its operands' inverse scales.
+  // 6. Accumulators: warp w reads lanes 32 (w % 4).. and columns 128 (w / 4) ..: rows
+  //    0-63 hold W (columns 0-127) and U (128-255), rows 64-127 M W and M U = R, each
+  //    times its operands' inverse scales. U and R go to the record as f32. P = Gamma Q -
+  //    M W (rows 0-63) and W (rows 64-127) go as the scan's [P; W] tiles, times 2^spw,
+  //    where 2^spw brings their largest magnitude below 2^14 (a first read finds it).
+  const uint32_t quarter = warp & 3, half = warp >> 2;
+  const uint32_t row = quarter * 32 + lane, t = row & (kDnC - 1);
+  const bool upper = row >= kDnC;
+  const float unscale = pow2f(-sa) * (half ? pow2f(-sv) : 1.0f / kPtUnit);
+  const float qs = rq[t], el = elam[t];
+  const float* qr = qsrc + (uint64_t)(t0 + t) * cd;
+  // Column j of block cb of P (upper rows) or W, from the accumulator values v.
+  auto pw_vals = [&](uint32_t cb, float* v) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const float4 qv = upper && t < ce ? *reinterpret_cast<const float4*>(qr + 32 * cb + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float q4[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+      for (int u = 0; u < 4; u++) v[j + u] = upper ? fmaf(el, q4[u] * qs, -(v[j + u] * unscale)) : v[j + u] * unscale;
+    }
+  };
+  float pwmax = 0.f;
+  if (ok && !half) {
+    for (uint32_t cb = 0; cb < 4; cb++) {
+      float v[32];
+      tmem_ld32(tmem + ((quarter * 32) << 16) + 32 * cb, v);
+      pw_vals(cb, v);
+#pragma unroll
+      for (int j = 0; j < 32; j++) pwmax = fmaxf(pwmax, fabsf(v[j]));
+    }
+  }
+  const int spw = pt_scale_exp(pt_block_max(pwmax, red));
   if (ok) {
-    const uint32_t quarter = warp & 3, half = warp >> 2;
-    const uint32_t row = quarter * 32 + lane, t = row & (kDnC - 1);
-    const bool upper = row >= kDnC;
-    const float unscale = pow2f(-sa) * (half ? pow2f(-sv) : 1.0f / kPtUnit);
+    const float pws = pow2f(spw);
+    const uint32_t prow = upper ? t : kDnC + t;  // [P; W] row
     for (uint32_t cb = 0; cb < 4; cb++) {
       float v[32];
       tmem_ld32(tmem + ((quarter * 32) << 16) + 128 * half + 32 * cb, v);
-#pragma unroll
-      for (int j = 0; j < 32; j++) v[j] *= unscale;
       const uint32_t i0 = 32 * cb;
-      if (!upper) {
-        float* dst = (half ? Ug : Wg) + t * DK + i0;
+      if (half) {
+        float* dst = (upper ? Rg : Ug) + t * DV + i0;
 #pragma unroll
         for (int j = 0; j < 32; j += 4)
-          *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-      } else if (half) {
-        float* dst = Rg + t * DV + i0;
-#pragma unroll
-        for (int j = 0; j < 32; j += 4)
-          *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-      } else {
-        const float* qr = qsrc + (uint64_t)(t0 + t) * cd + i0;
-        float* dst = Pg + t * DK + i0;
-        const float sc = rq[t], el = elam[t];
-#pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          float4 qv = t < ce ? *reinterpret_cast<const float4*>(qr + j) : make_float4(0.f, 0.f, 0.f, 0.f);
           *reinterpret_cast<float4*>(dst + j) =
-              make_float4(fmaf(el, qv.x * sc, -v[j]), fmaf(el, qv.y * sc, -v[j + 1]), fmaf(el, qv.z * sc, -v[j + 2]),
-                          fmaf(el, qv.w * sc, -v[j + 3]));
-        }
+              make_float4(v[j] * unscale, v[j + 1] * unscale, v[j + 2] * unscale, v[j + 3] * unscale);
+      } else {
+        pw_vals(cb, v);
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] *= pws;
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) pt_store8(PWg, PWg + 2 * kPtTile, prow, i0 + j, v + j);
       }
     }
   } else if (tid == 0) {
     report_timeout(err);
   }
-  if (tid == 0) rec[5 * kDnC * DK] = __expf(lam_c);
+  if (tid == 0) {
+    rec[kRecScal] = __expf(lam_c);
+    rec[kRecScal + 1] = (float)spw;
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, kPtTmemCols);
 }
 
-// Carries one head's state slice (all 128 rows, kDnCols columns) through the chunks of
-// the step on the tensor cores, writing the pre-norm outputs O = P S0 + R of its
-// columns. 8 warps; per chunk: O and W S (64 x 32, K = 128: two 16 x 8 tiles per warp),
-// then S = gamma_C S + Kd^T D (128 x 32, K = 64: four tiles per warp). Shared-memory
-// row strides avoid bank conflicts of the fragment loads: 132 floats (= 4 mod 32) for
-// row-major A reads, 136 (= 8 mod 32) for the transposed Kd reads, 40 for S and D.
-constexpr uint32_t kScA = 132, kScKd = 136, kScS = 40;
+// Carries one head's state slice (all 128 rows, kDnCols = 32 columns) through the chunks
+// of the step on the tcgen05 tensor cores. The slice lives in registers: thread (warp
+// w, lane l) holds row 32 (w % 4) + l, columns 16 (w / 4) .. + 15, which is the tensor-
+// memory lane and column range that thread may read. Per chunk:
+//   1. S0^T times 2^ss (2^ss brings the slice's largest magnitude below 2^14) into two
+//      fp16 hi / lo B tiles; [P; W] (from the record, already split) times S0 into
+//      tensor memory columns 0-31: rows 0-63 give P S0, rows 64-127 W S0.
+//   2. O = P S0 + R to the outputs; D = U - W S0, times 2^sd, into the D^T tiles.
+//   3. Kd^T (from the record) times D into columns 32-63; S = gamma_C S0 + Kd^T D.
+// The record's [P; W] and Kd^T tiles arrive by bulk copies (one thread, mbarriers) into
+// single buffers, each refilled with the next chunk's as soon as its product completed;
+// this slice's columns of U and R arrive by cp.async while the state product runs.
+// Shared memory: [P; W] 64 KB, Kd^T 32 KB, S0^T 16 KB (32 rows x 2 K blocks, hi and lo),
+// D^T 8 KB, U and R slices 2 x 10 KB.
+constexpr uint32_t kSnTile = 16384;                  // bytes of a 128-row tile
+constexpr uint32_t kSnSmall = 32 * 128;              // bytes of a 32-row tile
+constexpr uint32_t kScS = 40;                        // row stride (floats) of the U / R slices
+constexpr uint32_t kSnPW = 0, kSnKd = 4 * kSnTile, kSnS0 = 6 * kSnTile, kSnD = kSnS0 + 4 * kSnSmall,
+                   kSnU = kSnD + 2 * kSnSmall, kSnR = kSnU + kDnC * kScS * 4;
+constexpr size_t kScanSmem = kSnR + kDnC * kScS * 4 + 1024;
 
-__global__ void __launch_bounds__(256) dn_scan_kernel(uint32_t m, uint32_t n_chunks, snl_lin_p p,
-                                                      const float* __restrict__ chunks, float* __restrict__ state,
-                                                      float* __restrict__ out) {
-  extern __shared__ __align__(16) float ssm[];
-  float* S = ssm;                          // [128][kScS]
-  float* Pb = S + DK * kScS;               // [2][C][kScA] P of this chunk and the next
-  float* Wb = Pb + 2 * kDnC * kScA;        // [2][C][kScA] W of this chunk and the next
-  float* Kb = Wb + 2 * kDnC * kScA;        // [C][kScKd] Kd
-  float* D = Kb + kDnC * kScKd;            // [C][kScS]
-  float* Ub = D + kDnC * kScS;             // [C][kScS] this slice's columns of U
-  float* Rb = Ub + kDnC * kScS;            // [C][kScS] this slice's columns of R
-  const uint32_t slice = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
-  const uint32_t warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
-  const uint32_t j0 = slice * kDnCols;
-  float* Sg = state + (uint64_t)h * DK * DV;
-  for (uint32_t e = tid; e < DK * kDnCols; e += blockDim.x) S[(e / kDnCols) * kScS + e % kDnCols] = Sg[(e / kDnCols) * DV + j0 + e % kDnCols];
-  // The chunk records stream in with asynchronous copies, one step ahead of their use:
-  // P and W of chunk c + 1 while chunk c's state update runs, Kd of chunk c + 1 while
-  // its O and W S products run.
-  auto rec_of = [&](uint32_t c) { return chunks + ((uint64_t)h * n_chunks + c) * kDnChunkFloats; };
-  auto copy_rows = [&](float* dst, uint32_t stride, const float* src) {
-    for (uint32_t e = tid; e < kDnC * DK / 4; e += blockDim.x) {
-      const uint32_t r = e / (DK / 4), q = e % (DK / 4);
-      cp_async16(dst + r * stride + 4 * q, src + 4 * e);
-    }
-  };
-  // This slice's columns of U and R (single-buffered: chunk c + 1's are fetched once
-  // chunk c's outputs have read them).
-  auto copy_slice = [&](float* dst, const float* src) {
-    for (uint32_t e = tid; e < kDnC * kDnCols / 4; e += blockDim.x) {
-      const uint32_t r = e / (kDnCols / 4), q = e % (kDnCols / 4);
-      cp_async16(dst + r * kScS + 4 * q, src + r * DV + j0 + 4 * q);
-    }
-  };
-  copy_rows(Pb, kScA, rec_of(0));
-  copy_rows(Wb, kScA, rec_of(0) + 2 * kDnC * DK);
-  copy_slice(Ub, rec_of(0) + 3 * kDnC * DK);
-  copy_slice(Rb, rec_of(0) + kDnC * DK);
-  cp_async_commit();
-  copy_rows(Kb, kScKd, rec_of(0) + 4 * kDnC * DK);
-  cp_async_commit();
-  // This warp's tiles: rows 16 * mt of the 64-token products, columns 8 * nt0 and 8 * nt0 + 8.
-  const uint32_t mt = warp >> 1, nt0 = (warp & 1) * 2;
-  for (uint32_t c = 0; c < n_chunks; c++) {
-    const float* rec = rec_of(c);
-    const float gC = rec[5 * kDnC * DK];
-    const uint32_t t0 = c * kDnC, ce = min(kDnC, m - t0);
-    float* A = Pb + (c & 1) * kDnC * kScA;
-    float* B = Wb + (c & 1) * kDnC * kScA;
-    cp_async_wait<1>();  // P and W of chunk c (its Kd may still be in flight)
-    __syncthreads();
-    // O = P S, WS = W S for the warp's two tiles.
-    float o[2][4] = {}, ws[2][4] = {};
-#pragma unroll 4
-    for (uint32_t ks = 0; ks < DK / 8; ks++) {
-      const uint32_t kc = ks * 8 + t4;
-      uint32_t ph[4], pl[4], wh[4], wl[4];
-      split_a(A + (16 * mt + g) * kScA + kc, kScA, ph, pl);
-      split_a(B + (16 * mt + g) * kScA + kc, kScA, wh, wl);
+// Element k of row r (r < 32) of the 32-row tiles, as fp16 hi and lo; K blocks of 64.
+__device__ __forceinline__ void sn_store1(uint8_t* hi, uint8_t* lo, uint32_t r, uint32_t k, float v) {
+  const uint32_t off = (k >> 6) * kSnSmall + r * 128 + ((((k & 63) >> 3) ^ (r & 7)) << 4) + ((k & 7) << 1);
+  const __half hv = __float2half_rn(v);
+  *reinterpret_cast<__half*>(hi + off) = hv;
+  *reinterpret_cast<__half*>(lo + off) = __float2half_rn(v - __half2float(hv));
+}
+// One split product with N = 32: kbs K blocks of 64; A tiles kSnTile apart, B tiles
+// kSnSmall apart.
+__device__ __forceinline__ void sn_mma(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi, uint32_t b_lo,
+                                       uint32_t kbs) {
+  constexpr uint32_t idesc = tc_idesc_f16(kDnCols);
+  for (uint32_t kb = 0; kb < kbs; kb++) {
 #pragma unroll
-      for (int q = 0; q < 2; q++) {
-        const uint32_t n = 8 * (nt0 + q) + g;
-        uint32_t sh[2], sl[2];
-        split_b(S[kc * kScS + n], S[(kc + 4) * kScS + n], sh, sl);
-        mma3_split(o[q], ph, pl, sh, sl);
-        mma3_split(ws[q], wh, wl, sh, sl);
-      }
-    }
-    // Outputs (+ R) and D = U - W S (c0/c1: row g, columns 2 t4, 2 t4 + 1; c2/c3: row g + 8).
-#pragma unroll
-    for (int q = 0; q < 2; q++) {
-#pragma unroll
-      for (int r = 0; r < 4; r++) {
-        const uint32_t t = 16 * mt + g + (r >= 2 ? 8 : 0), j = 8 * (nt0 + q) + 2 * t4 + (r & 1);
-        D[t * kScS + j] = Ub[t * kScS + j] - ws[q][r];
-        if (t < ce) out[(uint64_t)(t0 + t) * p.n_v * DV + h * DV + j0 + j] = o[q][r] + Rb[t * kScS + j];
-      }
-    }
-    const bool more = c + 1 < n_chunks;
-    if (more) {
-      // the other buffers held chunk c - 1, finished before this chunk's first barrier
-      copy_rows(Pb + ((c + 1) & 1) * kDnC * kScA, kScA, rec_of(c + 1));
-      copy_rows(Wb + ((c + 1) & 1) * kDnC * kScA, kScA, rec_of(c + 1) + 2 * kDnC * DK);
-      cp_async_commit();
-      cp_async_wait<1>();  // Kd of chunk c
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
-    if (more) {  // every thread has read this chunk's U and R
-      copy_slice(Ub, rec_of(c + 1) + 3 * kDnC * DK);
-      copy_slice(Rb, rec_of(c + 1) + kDnC * DK);
-      cp_async_commit();
-    }
-    // S = gamma_C S + Kd^T D: the warp's four tiles are state rows 16 * (warp % 8) and
-    // columns 8 * nt, nt = 0..3. A(i, t) = Kd[t][i].
-    A = Kb;
-    {
-      const uint32_t it = warp;  // 8 row tiles of 16
-      float acc[4][4];
-#pragma unroll
-      for (int q = 0; q < 4; q++)
-#pragma unroll
-        for (int r = 0; r < 4; r++) {
-          const uint32_t i = 16 * it + g + (r >= 2 ? 8 : 0), j = 8 * q + 2 * t4 + (r & 1);
-          acc[q][r] = gC * S[i * kScS + j];
-        }
-#pragma unroll 2
-      for (uint32_t ks = 0; ks < kDnC / 8; ks++) {
-        const uint32_t kt = ks * 8 + t4;
-        const float* kr = A + kt * kScKd + 16 * it + g;
-        const float ka[4] = {kr[0], kr[8], kr[4 * kScKd], kr[4 * kScKd + 8]};
-        uint32_t kh[4], kl[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) tf32_split(ka[i], kh[i], kl[i]);
-#pragma unroll
-        for (int q = 0; q < 4; q++) {
-          const uint32_t n = 8 * q + g;
-          uint32_t dh[2], dl[2];
-          split_b(D[kt * kScS + n], D[(kt + 4) * kScS + n], dh, dl);
-          mma3_split(acc[q], kh, kl, dh, dl);
-        }
-      }
-      __syncwarp();
-#pragma unroll
-      for (int q = 0; q < 4; q++)
-#pragma unroll
-        for (int r = 0; r < 4; r++) {
-          const uint32_t i = 16 * it + g + (r >= 2 ? 8 : 0), j = 8 * q + 2 * t4 + (r & 1);
-          S[i * kScS + j] = acc[q][r];
-        }
-    }
-    if (more) {
-      __syncthreads();  // every warp has read Kd
-      copy_rows(Kb, kScKd, rec_of(c + 1) + 4 * kDnC * DK);
-      cp_async_commit();
+    for (uint32_t kk = 0; kk < 4; kk++) {
+      const uint64_t ah = sdesc<128>(a_hi + kb * kSnTile + kk * 32), al = sdesc<128>(a_lo + kb * kSnTile + kk * 32);
+      const uint64_t bh = sdesc<128>(b_hi + kb * kSnSmall + kk * 32), bl = sdesc<128>(b_lo + kb * kSnSmall + kk * 32);
+      tc_mma(d, ah, bh, idesc, (kb | kk) != 0);
+      tc_mma(d, ah, bl, idesc, 1);
+      tc_mma(d, al, bh, idesc, 1);
     }
   }
+}
+
+__global__ void __launch_bounds__(256, 1) dn_scan_tc_kernel(uint32_t m, uint32_t n_chunks, snl_lin_p p,
+                                                            const float* __restrict__ chunks,
+                                                            float* __restrict__ state, float* __restrict__ out,
+                                                            int* err) {
+  extern __shared__ uint8_t sn_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sn_raw) + 1023) & ~(uintptr_t)1023);
+  float* Us = reinterpret_cast<float*>(sm + kSnU);
+  float* Rs = reinterpret_cast<float*>(sm + kSnR);
+  __shared__ float red[8];
+  __shared__ uint64_t bar[4];  // [P; W] landed, Kd^T landed, first product done, state product done
+  __shared__ uint32_t tmem_sh;
+  __shared__ int fail_sh;
+  const uint32_t slice = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t quarter = warp & 3, jc = 16 * (warp >> 2);
+  const uint32_t i = quarter * 32 + lane;  // state row = tensor-memory lane
+  const uint32_t j0 = slice * kDnCols;
+  float* Sg = state + (uint64_t)h * DK * DV;
+  float st[16];
+#pragma unroll
+  for (int jj = 0; jj < 16; jj += 4) {
+    const float4 v = *reinterpret_cast<const float4*>(Sg + (uint64_t)i * DV + j0 + jc + jj);
+    st[jj] = v.x;
+    st[jj + 1] = v.y;
+    st[jj + 2] = v.z;
+    st[jj + 3] = v.w;
+  }
+  auto rec_of = [&](uint32_t c) { return chunks + ((uint64_t)h * n_chunks + c) * kDnChunkFloats; };
+  auto load_pw = [&](uint32_t c) {
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(rec_of(c) + kRecPW);
+    mbar_arrive_expect_tx(&bar[0], 4 * kSnTile);
+    for (uint32_t q = 0; q < 4; q++) bulk_g2s_plain(sm + kSnPW + q * kSnTile, src + q * kSnTile, kSnTile, &bar[0]);
+  };
+  auto load_kd = [&](uint32_t c) {
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(rec_of(c) + kRecKd);
+    mbar_arrive_expect_tx(&bar[1], 2 * kSnTile);
+    for (uint32_t q = 0; q < 2; q++) bulk_g2s_plain(sm + kSnKd + q * kSnTile, src + q * kSnTile, kSnTile, &bar[1]);
+  };
+  auto load_ur = [&](uint32_t c) {
+    const float* rec = rec_of(c);
+    for (uint32_t e = tid; e < 2 * kDnC * (kDnCols / 4); e += blockDim.x) {
+      const uint32_t w = e / (kDnC * (kDnCols / 4)), r = (e / (kDnCols / 4)) % kDnC, q = e % (kDnCols / 4);
+      cp_async16((w ? Rs : Us) + r * kScS + 4 * q, rec + (w ? kRecR : kRecU) + r * DV + j0 + 4 * q);
+    }
+    cp_async_commit();
+  };
+  if (tid == 0) {
+    for (int b = 0; b < 4; b++) mbar_init(&bar[b], 1);
+    fail_sh = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_sh, 64);
+  tc_fence_before();
   __syncthreads();
-  for (uint32_t e = tid; e < DK * kDnCols; e += blockDim.x) Sg[(e / kDnCols) * DV + j0 + e % kDnCols] = S[(e / kDnCols) * kScS + e % kDnCols];
+  tc_fence_after();
+  const uint32_t tmem = tmem_sh, base = smem_u32(sm);
+  if (tid == 0) {
+    load_pw(0);
+    load_kd(0);
+  }
+  load_ur(0);
+  bool ok = true;
+  for (uint32_t c = 0; c < n_chunks && ok; c++) {
+    const uint32_t t0 = c * kDnC, ce = min(kDnC, m - t0), par = c & 1;
+    const bool more = c + 1 < n_chunks;
+    const float* rec = rec_of(c);
+    const float gC = rec[kRecScal];
+    const int spw = (int)rec[kRecScal + 1];
+    // 1. S0^T into the B tiles, then [P; W] S0.
+    float smax = 0.f;
+#pragma unroll
+    for (int jj = 0; jj < 16; jj++) smax = fmaxf(smax, fabsf(st[jj]));
+    const int ss = pt_scale_exp(pt_block_max(smax, red));
+    {
+      const float sc = pow2f(ss);
+#pragma unroll
+      for (int jj = 0; jj < 16; jj++) sn_store1(sm + kSnS0, sm + kSnS0 + 2 * kSnSmall, jc + jj, i, st[jj] * sc);
+    }
+    cp_async_wait<0>();  // this thread's copies of U and R
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      if (mbar_wait_bounded(&bar[0], par)) {
+        tc_fence_after();
+        sn_mma(tmem, base + kSnPW, base + kSnPW + 2 * kSnTile, base + kSnS0, base + kSnS0 + 2 * kSnSmall, 2);
+        tc_commit(&bar[2]);
+      } else {
+        fail_sh = 1;
+      }
+    }
+    __syncthreads();
+    ok = !fail_sh && __syncthreads_and(mbar_wait_bounded(&bar[2], par));
+    tc_fence_after();
+    if (!ok) break;
+    if (tid == 0 && more) load_pw(c + 1);  // the product has read [P; W]
+    // 2. O and D (rows 0-63 and 64-127 of the accumulator).
+    float v[16];
+    tmem_ld16(tmem + ((quarter * 32) << 16) + jc, v);
+    const float un1 = pow2f(-spw) * pow2f(-ss);
+    const uint32_t t = i & (kDnC - 1);
+    float dmax = 0.f;
+    if (i < kDnC) {
+      if (t < ce) {
+        float* o = out + (uint64_t)(t0 + t) * p.n_v * DV + h * DV + j0 + jc;
+#pragma unroll
+        for (int jj = 0; jj < 16; jj++) o[jj] = fmaf(v[jj], un1, Rs[t * kScS + jc + jj]);
+      }
+    } else {
+#pragma unroll
+      for (int jj = 0; jj < 16; jj++) {
+        v[jj] = Us[t * kScS + jc + jj] - v[jj] * un1;
+        dmax = fmaxf(dmax, fabsf(v[jj]));
+      }
+    }
+    const int sd = pt_scale_exp(pt_block_max(dmax, red));
+    if (i >= kDnC) {
+      const float sc = pow2f(sd);
+#pragma unroll
+      for (int jj = 0; jj < 16; jj++) sn_store1(sm + kSnD, sm + kSnD + kSnSmall, jc + jj, t, v[jj] * sc);
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (more) load_ur(c + 1);  // U and R of this chunk are read
+    // 3. S = gamma_C S0 + Kd^T D.
+    if (tid == 0) {
+      if (mbar_wait_bounded(&bar[1], par)) {
+        tc_fence_after();
+        sn_mma(tmem + 32, base + kSnKd, base + kSnKd + kSnTile, base + kSnD, base + kSnD + kSnSmall, 1);
+        tc_commit(&bar[3]);
+      } else {
+        fail_sh = 1;
+      }
+    }
+    __syncthreads();
+    ok = !fail_sh && __syncthreads_and(mbar_wait_bounded(&bar[3], par));
+    tc_fence_after();
+    if (!ok) break;
+    if (tid == 0 && more) load_kd(c + 1);
+    tmem_ld16(tmem + ((quarter * 32) << 16) + 32 + jc, v);
+    const float un2 = pow2f(-sd) * (1.0f / kPtUnit);
+#pragma unroll
+    for (int jj = 0; jj < 16; jj++) st[jj] = fmaf(gC, st[jj], v[jj] * un2);
+  }
+  if (ok) {
+#pragma unroll
+    for (int jj = 0; jj < 16; jj += 4)
+      *reinterpret_cast<float4*>(Sg + (uint64_t)i * DV + j0 + jc + jj) = make_float4(st[jj], st[jj + 1], st[jj + 2], st[jj + 3]);
+  } else {
+    // A bounded wait gave up: flag it, let the copies in flight land, stop.
+    if (tid == 0) report_timeout(err);
+    cp_async_wait<0>();
+    if (tid == 0) {
+      (void)mbar_wait_bounded(&bar[0], 0);
+      (void)mbar_wait_bounded(&bar[1], 0);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 64);
 }
 
 // Gated RMSNorm of the delta outputs (linear.wgsl's tail of `delta`), in place.
@@ -1364,30 +1206,20 @@ int launch_conv_delta_chunked(uint32_t m, const snl_lin_p& p, const float* proj,
   const snl_step_u sv{m, 0, 1, 0};
   if (int rc = launch_conv(step_val(sv), p, proj, conv_out, conv_state, lw, nullptr, s)) return rc;
   const uint32_t nch = (m + kDnC - 1) / kDnC;
-  const size_t prep_smem = kPrepSmemFloats * sizeof(float);
-  const size_t scan_smem = (DK * kScS + 4 * kDnC * kScA + kDnC * kScKd + 3 * kDnC * kScS) * sizeof(float);
   static bool attr[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr[dev]) {
-    SNL_CUDA_TRY(cudaFuncSetAttribute(dn_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem));
     SNL_CUDA_TRY(cudaFuncSetAttribute(dn_prep_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPrepTcSmem));
-    SNL_CUDA_TRY(cudaFuncSetAttribute(dn_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)scan_smem));
+    SNL_CUDA_TRY(cudaFuncSetAttribute(dn_scan_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kScanSmem));
     attr[dev] = true;
   }
-  // SNL_DN_PREP_MMA=1: the mma.sync form of the chunk preparation (for comparison).
-  static const bool prep_tc = getenv("SNL_DN_PREP_MMA") == nullptr;
-  if (prep_tc) {
-    int* err = nullptr;
-    if (int rc = device_error_word(&err)) return rc;
-    dn_prep_tc_kernel<<<dim3(nch, p.n_v), 256, kPrepTcSmem, s>>>(m, p, proj, conv_out, lw, scratch, err);
-    SNL_LAUNCH_CHECK("dn_prep_tc");
-  } else {
-    dn_prep_kernel<<<dim3(nch, p.n_v), 256, prep_smem, s>>>(m, p, proj, conv_out, lw, scratch);
-    SNL_LAUNCH_CHECK("dn_prep");
-  }
-  dn_scan_kernel<<<dim3(DV / kDnCols, p.n_v), 256, scan_smem, s>>>(m, nch, p, scratch, state, out);
-  SNL_LAUNCH_CHECK("dn_scan");
+  int* err = nullptr;
+  if (int rc = device_error_word(&err)) return rc;
+  dn_prep_tc_kernel<<<dim3(nch, p.n_v), 256, kPrepTcSmem, s>>>(m, p, proj, conv_out, lw, scratch, err);
+  SNL_LAUNCH_CHECK("dn_prep_tc");
+  dn_scan_tc_kernel<<<dim3(DV / kDnCols, p.n_v), 256, kScanSmem, s>>>(m, nch, p, scratch, state, out, err);
+  SNL_LAUNCH_CHECK("dn_scan_tc");
   dn_norm_kernel<<<dim3(m, p.n_v), DV, 0, s>>>(p, proj, lw, out);
   SNL_LAUNCH_CHECK("dn_norm");
   return SNL_OK;
