@@ -681,8 +681,9 @@ def run_deltanet(args):
         "dtype": "f32", "data": "synthetic (BASELINE configs[1] distributions)",
         "config": {"workload": "BASELINE configs[1]: DeltaNet 16/32 heads x 128, 4096-token prefill in 512-row steps "
                                "then 256 single-token steps",
-                   "kernel": "prefill: conv_kernel + chunked gated delta rule (dn_prep_kernel, dn_scan_kernel, "
-                             "dn_norm_kernel; 64-token chunks, 3xTF32 mma.sync); decode: conv_delta_split_kernel"},
+                   "kernel": "prefill: conv_kernel + chunked gated delta rule (dn_prep_tc_kernel, dn_scan_tc_kernel: "
+                             "tcgen05 fp16 hi/lo products into tensor memory; dn_norm_kernel; 64-token chunks); "
+                             "decode: conv_delta_split_kernel"},
         "roofline": {"bound": "latency (chunk-sequential state carry; token-sequential recurrence in decode)",
                      "state_bytes_per_token": 2 * n_v * D * D * 4},
         "cpu_baseline": {"value": nS / cpu_s, "unit": "tok/s", "cores": 1, "kind": "port",
