@@ -11,6 +11,7 @@
 //   * greedy callers get the argmax on the device (snl_engine_forward_greedy).
 #include <algorithm>
 #include <atomic>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -68,13 +69,14 @@ struct FT {
   size_t n = 0;
 };
 
-uint32_t parts_for(size_t m, size_t total) {
+uint32_t parts_for(size_t m, size_t total, uint32_t cap) {
   // engine.rs:827: split-K attention only for short steps. The reference splits every
   // 256 keys; here a part is 64 keys (one 8-key group per warp of attend_kernel), so short
-  // contexts spread over more CTAs. The split changes only the summation order.
+  // contexts spread over more CTAs, up to cap parts. The split changes only the
+  // summation order.
   if (m > 4) return 1;
   size_t p = (total + 63) / 64;
-  return (uint32_t)std::min<size_t>(std::max<size_t>(p, 1), MAX_PARTS);
+  return (uint32_t)std::min<size_t>(std::max<size_t>(p, 1), cap);
 }
 
 }  // namespace
@@ -88,6 +90,7 @@ struct snl_engine {
   uint32_t vocab_l = 0;  // LM-head rows on this rank
   snl::TpHost tp;
   unsigned long long* step_ctr = nullptr;  // steps run (exchange epochs), bumped by the embedding
+  uint32_t att_parts = 0;  // split-key parts of a decode step's attention (att_parts())
   float* logits_full = nullptr;            // tensor parallel: gathered logits [2][vocab]
   float* head_out = nullptr;               // where the LM head writes [rows][vocab_l]
   uint32_t tp_sites = 0;                   // exchanges per step: 2 per layer visit + 2 (head)
@@ -406,6 +409,20 @@ size_t o_proj_offset(const snl_engine* e) {
 }
 
 // The layer loop of engine.rs:389-481 for one step of m rows.
+// Part slots of a decode step's attention (the captured graphs use all of them): one
+// attend CTA per (local KV head, part) and at most one wave of them, since an attend CTA
+// holds an SM's registers (189 per thread): 37 parts for 4 KV heads on 148 SMs, against
+// 64 before (two waves at long contexts: 246.8 -> 252.4 tok/s at a 32K context).
+// SNL_ATT_PARTS overrides it; at most MAX_PARTS (the partial buffer's slots).
+uint32_t att_parts(snl_engine* e) {
+  if (!e->att_parts) {
+    const char* v = getenv("SNL_ATT_PARTS");
+    long p = v ? strtol(v, nullptr, 10) : (long)sm_count() / (long)std::max<uint32_t>(e->lc.n_kv_heads, 1);
+    e->att_parts = (uint32_t)std::min<long>(std::max<long>(p, 1), (long)MAX_PARTS);
+  }
+  return e->att_parts;
+}
+
 int run_layers(snl_engine* e, StepRef st, uint32_t m, uint32_t parts_grid) {
   const auto& c = e->lc;
   const size_t h = c.hidden;
@@ -613,7 +630,7 @@ int run_step(snl_engine* e, const snl_step_u& sh, uint32_t m, uint32_t rows, boo
   if (it == e->graphs.end()) {
     const uint64_t before = g_launches.load();
     SNL_CUDA_TRY(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
-    int rc = device_step(e, st, m, MAX_PARTS, rows, greedy);
+    int rc = device_step(e, st, m, att_parts(e), rows, greedy);
     cudaGraph_t graph = nullptr;
     cudaError_t ce = cudaStreamEndCapture(e->stream, &graph);
     if (rc) {
@@ -687,7 +704,7 @@ int forward_impl(snl_engine* e, const uint32_t* tokens, size_t n, const uint32_t
     const size_t c0 = ci * chunk;
     const size_t m = std::min(chunk, n - c0);
     const size_t total = e->pos + m;
-    snl_step_u sh = {(uint32_t)m, (uint32_t)e->pos, parts_for(m, total), (uint32_t)(ckpt ? 1 : 0)};
+    snl_step_u sh = {(uint32_t)m, (uint32_t)e->pos, parts_for(m, total, att_parts(e)), (uint32_t)(ckpt ? 1 : 0)};
     const size_t rows = (last && logit_rows > 0) ? std::min(logit_rows, m) : 0;
     if (rows) e->head_rows = rows;
     // Stage the step inputs through pinned memory.
@@ -1466,7 +1483,7 @@ extern "C" int snl_engine_mtp(snl_engine* e, size_t r0, const uint32_t* tokens, 
   for (size_t c0 = 0; c0 < n; c0 += MAX_M) {
     const size_t c1 = std::min(c0 + MAX_M, n);
     const uint32_t m = (uint32_t)(c1 - c0);
-    snl_step_u sh = {m, (uint32_t)(slot0 + c0), parts_for(m, slot0 + c1), 0};
+    snl_step_u sh = {m, (uint32_t)(slot0 + c0), parts_for(m, slot0 + c1, att_parts(e)), 0};
     *e->h_step = sh;
     memcpy(e->h_tokens, tokens + c0, m * sizeof(uint32_t));
     for (size_t i = 0; i < m; i++) {
@@ -1537,7 +1554,7 @@ extern "C" int snl_engine_generate(snl_engine* e, uint32_t first_token, size_t n
   std::vector<uint32_t> rp(4 * n);
   for (size_t i = 0; i < n; i++) {
     const size_t p = e->pos + i;
-    steps[i] = snl_step_u{1u, (uint32_t)p, parts_for(1, p + 1), 0u};
+    steps[i] = snl_step_u{1u, (uint32_t)p, parts_for(1, p + 1, att_parts(e)), 0u};
     for (int k = 0; k < 4; k++) rp[4 * i + k] = (uint32_t)p;
   }
   snl_step_u* steps_d = nullptr;
@@ -1599,7 +1616,7 @@ extern "C" int snl_engine_profile(snl_engine* e, uint32_t token, snl_op_stat* ou
   if (token >= e->cfg.vocab) return fail(SNL_E_RANGE, "token id " + std::to_string(token) + " out of range");
   DeviceGuard dg(e->device);
   std::vector<snl_engine::ProfRec> recs;
-  snl_step_u sh = {1u, (uint32_t)e->pos, parts_for(1, e->pos + 1), 0u};
+  snl_step_u sh = {1u, (uint32_t)e->pos, parts_for(1, e->pos + 1, att_parts(e)), 0u};
   *e->h_step = sh;
   *e->h_tokens = token;
   for (int k = 0; k < 4; k++) e->h_rpos[k] = (uint32_t)e->pos;
