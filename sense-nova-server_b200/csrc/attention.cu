@@ -5,6 +5,8 @@
 // then k [n_kv*256], then v [n_kv*256]; the caches hold f16 pairs packed in u32,
 // cache[(pos * kv_dim + kh*256 + d) / 2]; split-K partials are
 // [(m*n_heads + h)*parts + part][256 acc | max | sum].
+#include <cstdlib>
+
 #include "common.cuh"
 #include "ptx.cuh"
 
@@ -111,7 +113,7 @@ constexpr uint32_t kPrefetchKeys = 64;
 __global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, const float* __restrict__ proj,
                                                      const float* __restrict__ qbuf, const uint32_t* __restrict__ kc,
                                                      const uint32_t* __restrict__ vc, float* __restrict__ out,
-                                                     float* __restrict__ partial, XOut xo) {
+                                                     float* __restrict__ partial, XOut xo, int rolling_pf) {
   pdl_trigger();
   // The step descriptor is written before the step's first kernel, so the part's key
   // range is known before the wait. Every cached key before the step's own (position
@@ -185,8 +187,27 @@ __global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, c
   const int my_g = lane & 3;       // score lane -> (key lane/4, head lane%4)
   float m_run = -1e30f, l_run = 0.f;  // for head my_g (replicated over lanes with that g)
 
+  static_assert(kKeysPerGroup * 8 == 64, "lane -> (key, K or V, line) of a group's 64 lines");
+  // Parts of more than one round of key groups (long contexts) prefetch ahead.
+  const bool rpf = rolling_pf && end - start > kAttWarps * kKeysPerGroup;
   for (; t0 < end; t0 += kAttWarps * kKeysPerGroup) {
     const uint32_t nk = min((uint32_t)kKeysPerGroup, end - t0);
+    if (rpf) {
+      // The warp's next two groups' K and V rows into L2 (64 lines of 128 B per group, two
+      // per lane), so their loads later wait on L2 rather than HBM.
+#pragma unroll
+      for (uint32_t ahead = 1; ahead <= 2; ahead++) {
+        const uint32_t tg = t0 + ahead * kAttWarps * kKeysPerGroup;
+#pragma unroll
+        for (uint32_t h2 = 0; h2 < 2; h2++) {
+          const uint32_t li = lane * 2 + h2, tk = tg + (li >> 3);
+          if (tk < end) {
+            const uint32_t* base = (li & 4) ? vc : kc;
+            prefetch_l2(base + ((uint64_t)tk * kv_dim + kbase) / 2 + (li & 3) * 32);
+          }
+        }
+      }
+    }
     // The group's K and V rows are all loaded before the scores: the V loads do not wait
     // for the softmax, so the group costs one memory latency instead of nine. Rows past
     // the part's end repeat its last key and get weight 0. The first group's rows came
@@ -623,7 +644,8 @@ int launch_attend(StepRef st, const snl_attn_p& p, const float* proj, const floa
                    st, p, proj, qbuf, kc, vc, out);
     return SNL_OK;
   }
-  SNL_PDL_LAUNCH("attend_kernel", attend_kernel, dim3(dim3(p.n_kv, m, parts_grid)), dim3(kAttWarps * 32), (size_t)(0), s, st, p, proj, qbuf, kc, vc, out, partial, xo);
+  static const int rolling_pf = getenv("SNL_NO_ATT_PF") == nullptr ? 1 : 0;
+  SNL_PDL_LAUNCH("attend_kernel", attend_kernel, dim3(dim3(p.n_kv, m, parts_grid)), dim3(kAttWarps * 32), (size_t)(0), s, st, p, proj, qbuf, kc, vc, out, partial, xo, rolling_pf);
   return SNL_OK;
 }
 
