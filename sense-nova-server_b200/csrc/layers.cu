@@ -215,17 +215,19 @@ __global__ void mhc_finish_kernel(StepRef sr, snl_layer_p p, const float* __rest
 // Engine-side mHC router in two launches that use many SMs: slice s of the 2H inputs
 // of token m -> part[(m * slices + s) * 9 + o]; then one warp per token sums the
 // slices and finishes the Sinkhorn step (mhc_coef).
-constexpr int kMhcSlices = 16;
+constexpr int kMhcSlices = 4;
 // The 9 router sums (8 dots + sum of squares) of kMhcTok tokens over slice `blockIdx.x`
-// of the 2H inputs: each thread loads its router weights once per element and applies
-// them to the block's tokens; the 36 sums take one warp-shuffle and one shared-memory pass.
-constexpr uint32_t kMhcTok = 4;
+// of the 2H inputs: each thread loads the router weights of its elements once and
+// applies them to the block's 8 tokens over the whole slice before any reduction; the
+// 72 sums then take one warp-shuffle and one shared-memory pass per CTA.
+constexpr uint32_t kMhcTok = 8;
 __global__ void __launch_bounds__(256) mhc_part_kernel(snl_layer_p p, uint32_t m_rows, const float* __restrict__ x,
                                                        const float* __restrict__ w, float* __restrict__ part) {
   __shared__ float red[8][kMhcTok * 9];
   const uint32_t sl = blockIdx.x, m0 = blockIdx.y * kMhcTok, d = 2 * p.h;
   const uint32_t len = d / kMhcSlices, i0 = sl * len;
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t nt = min(kMhcTok, m_rows - m0);
   float acc[kMhcTok][9];
 #pragma unroll
   for (uint32_t t = 0; t < kMhcTok; t++)
@@ -235,12 +237,14 @@ __global__ void __launch_bounds__(256) mhc_part_kernel(snl_layer_p p, uint32_t m
     float wv[8];
 #pragma unroll
     for (int o = 0; o < 8; o++) wv[o] = __ldg(w + (uint64_t)o * d + i);
+    float xv[kMhcTok];
+#pragma unroll
+    for (uint32_t t = 0; t < kMhcTok; t++) xv[t] = t < nt ? x[(uint64_t)(m0 + t) * d + i] : 0.f;
 #pragma unroll
     for (uint32_t t = 0; t < kMhcTok; t++) {
-      const float v = m0 + t < m_rows ? x[(uint64_t)(m0 + t) * d + i] : 0.f;
 #pragma unroll
-      for (int o = 0; o < 8; o++) acc[t][o] = fmaf(wv[o], v, acc[t][o]);
-      acc[t][8] = fmaf(v, v, acc[t][8]);
+      for (int o = 0; o < 8; o++) acc[t][o] = fmaf(wv[o], xv[t], acc[t][o]);
+      acc[t][8] = fmaf(xv[t], xv[t], acc[t][8]);
     }
   }
 #pragma unroll
@@ -256,7 +260,7 @@ __global__ void __launch_bounds__(256) mhc_part_kernel(snl_layer_p p, uint32_t m
     float v = 0.f;
 #pragma unroll
     for (int wi = 0; wi < 8; wi++) v += red[wi][threadIdx.x];
-    if (m0 + t < m_rows) part[((uint64_t)(m0 + t) * kMhcSlices + sl) * 9 + o] = v;
+    if (t < nt) part[((uint64_t)(m0 + t) * kMhcSlices + sl) * 9 + o] = v;
   }
 }
 __global__ void mhc_coef_kernel(snl_layer_p p, uint32_t m_rows, const float* __restrict__ part,
