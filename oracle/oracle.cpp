@@ -11,14 +11,19 @@
 // load this library, as the checker and the timed CPU baseline. The product path
 // (libsnl_b200.so) never links or calls it.
 //
-// Parity status: the reference ships no golden vectors or tests for this path
-// (its only tests are in src/mm.rs and src/chat.rs) and cannot run here (Rust
-// toolchain absent, wgpu needs a graphics stack). This restatement is pinned by
-// tests/golden/ fixtures where those exist; everything else is parity unpinned.
+// Parity status: the reference ships no golden vectors or tests for this path (its
+// only tests are in src/mm.rs and src/chat.rs), and its host code cannot run here
+// (Rust toolchain absent, wgpu needs a graphics stack). Its kernels can: the WGSL
+// sources are translated to C++ and run on the host cores (oracle/wgsl2cpp.py,
+// oracle/wgslref.py), and every kernel restated here gives their output bit for bit
+// (tests/test_reference_shaders.py, and the committed golden vectors of
+// tests/golden/ checked by tests/test_golden.py). The op graph of engine.rs is
+// restated, not run: it is checked by the reference's own invariants (batched ==
+// stepwise, rollback == never fed, snapshot/restore) in tests/test_oracle_model.py.
 //
-// Transcendentals (exp, log, pow, sin, cos, inverseSqrt) come from the host libm;
-// WGSL leaves their precision to the implementation, so kernels using them are
-// compared within a tolerance.
+// Transcendentals (exp, log, pow, sin, cos, inverseSqrt) come from the host libm, as
+// in the translated shaders; WGSL leaves their precision to the implementation, so
+// the GPU is compared with both within a tolerance.
 #include <immintrin.h>
 #include <math.h>
 #include <omp.h>
