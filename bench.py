@@ -286,17 +286,17 @@ def gemv_config1(lib, quant: str, copies: int = 8, iters: int = 40, kernel: str 
                                           C.byref(f16), None))
             scale_mode = "fp16" if f16.value else "f32"
 
-    def run(i):
+    def run(i, stream=None):
         if kernel == "tile":  # the decode path: tile layout, tensor-core GEMV over packed x
             ffi.check(lib.snl_mat_tiles(dt, C.byref(p), 1, C.c_void_p(planes.data_ptr()), C.c_void_p(tiles[i].data_ptr()),
                                         C.c_void_p(tsc[i].data_ptr()), 1 if scale_mode == "fp16" else 0,
-                                        C.c_void_p(y.data_ptr()), None))
+                                        C.c_void_p(y.data_ptr()), stream))
         elif kernel == "tc":  # tensor-core GEMV on the file layout
             ffi.check(lib.snl_mat_xpack(dt, C.byref(p), 1, C.c_void_p(planes.data_ptr()), C.c_void_p(ws[i].data_ptr()),
-                                        C.c_void_p(ss[i].data_ptr()), C.c_void_p(y.data_ptr()), None))
+                                        C.c_void_p(ss[i].data_ptr()), C.c_void_p(y.data_ptr()), stream))
         else:  # snl_mat: the SIMT kernels of the kernel-level entry point
             ffi.check(lib.snl_mat(dt, C.byref(st), C.byref(p), C.c_void_p(x.data_ptr()), C.c_void_p(ws[i].data_ptr()),
-                                  C.c_void_p(ss[i].data_ptr()), C.c_void_p(y.data_ptr()), None))
+                                  C.c_void_p(ss[i].data_ptr()), C.c_void_p(y.data_ptr()), stream))
 
     for i in range(2 * copies):
         run(i % copies)
@@ -307,10 +307,36 @@ def gemv_config1(lib, quant: str, copies: int = 8, iters: int = 40, kernel: str 
         run(i % copies)
     b.record()
     torch.cuda.synchronize()
-    us = a.elapsed_time(b) * 1000.0 / iters
+    us_eager = a.elapsed_time(b) * 1000.0 / iters
+    # The same launches captured in one CUDA graph, as the decode step runs its kernels:
+    # no host launch cost between them, programmatic dependent launch kept. Timed with
+    # CUDA events on the graph's stream around whole replays.
+    us_graph = None
+    if kernel == "tile":
+        side = torch.cuda.Stream()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            run(0, C.c_void_p(side.cuda_stream))  # first call on this stream outside the capture
+            side.synchronize()
+            with torch.cuda.graph(graph, stream=side):
+                for i in range(iters):
+                    run(i % copies, C.c_void_p(side.cuda_stream))
+            graph.replay()
+            side.synchronize()
+            reps = 5
+            a.record(side)
+            for _ in range(reps):
+                graph.replay()
+            b.record(side)
+            side.synchronize()
+        us_graph = a.elapsed_time(b) * 1000.0 / (reps * iters)
+        del graph
+    us = us_graph if us_graph is not None else us_eager
     # Algorithmic bytes: Q8_0/Q4_0 blocks (codes + an fp16 scale per 32), x, y.
     nbytes = qb + n * k // 32 * 2 + 4 * k + 4 * n
     return {"shape": [n, k], "quant": quant, "scales": scale_mode, "kernel": kernel, "us_per_launch": us, "iters": iters,
+            "timing": "CUDA graph of the launches" if us_graph is not None else "eager launches",
+            "us_per_launch_eager": us_eager, "achieved_gbs_eager": nbytes / (us_eager * 1e3),
             "bytes_per_launch": nbytes,
             "achieved_gbs": nbytes / (us * 1e3), "copies_rotated": copies}
 
@@ -478,7 +504,9 @@ def run_ours(args):
                     "frac": g1["achieved_gbs"] / peak, "traffic": None,
                     "kernel": f"gemv_pg_kernel, BASELINE configs[0] ({args.quant.upper()} 12288x4096, one token): "
                               f"{g1['bytes_per_launch']} algorithmic bytes per launch / {g1['us_per_launch']:.2f} us "
-                              f"average over {g1['iters']} back-to-back launches (CUDA events, launching stream)",
+                              f"average over {g1['iters']} back-to-back launches captured in a CUDA graph, as in the decode "
+                              f"step (CUDA events around the replays on the graph's stream; eager launches: "
+                              f"{g1['us_per_launch_eager']:.2f} us)",
                     "peak_kind": f"{peak_kind} hbm_gbs (burst)"}
 
     # Parity on this configuration, after the timed legs (the CPU oracle runs only now): the
