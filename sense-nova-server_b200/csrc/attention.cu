@@ -102,24 +102,32 @@ __device__ __forceinline__ void h8_to_f(const uint4 w, float f[8]) {
   }
 }
 
-constexpr int kAttWarps = 8;
+constexpr int kAttWarps = 12;
 constexpr uint32_t kAttTcMinRows = 16;  // steps of at least this many rows use attend_tc_kernel
 constexpr int kKeysPerGroup = 8;
-constexpr uint32_t kPrefetchKeys = 64;
+constexpr uint32_t kAttStages = 2;  // key groups in flight per warp
+constexpr uint32_t kAttGroupBytes = kKeysPerGroup * 2 * HD * 2;  // 8 keys x (K row, V row) x 512 B
+constexpr size_t kAttSmem = (size_t)kAttWarps * kAttStages * kAttGroupBytes;  // 192 KB
 
-// attend: CTA (KV head, token, part); 8 warps each take 8-key groups round-robin and
+// attend: CTA (KV head, token, part); 12 warps each take 8-key groups round-robin and
 // keep their own online softmax for the G = 4 query heads; lane l owns head dims
 // [8l, 8l+8). The warps' states are merged at the end.
-__global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, const float* __restrict__ proj,
-                                                     const float* __restrict__ qbuf, const uint32_t* __restrict__ kc,
-                                                     const uint32_t* __restrict__ vc, float* __restrict__ out,
-                                                     float* __restrict__ partial, XOut xo, int rolling_pf) {
+// Each warp streams its groups' K and V rows (16 rows of 512 contiguous bytes) into a
+// ring of kAttStages groups in shared memory with bulk copies completing on one mbarrier
+// per stage, so two groups per warp (192 KB per SM, one CTA) are in flight while it
+// computes, instead of one load latency per group. Groups whose
+// rows all precede this step's keys were written by earlier steps and are requested
+// before the dependency wait; the others (the step's own keys, which the prep kernel
+// writes) after it.
+__global__ void __launch_bounds__(kAttWarps * 32, 1) attend_kernel(StepRef sr, snl_attn_p p, const float* __restrict__ proj,
+                                                        const float* __restrict__ qbuf, const uint32_t* __restrict__ kc,
+                                                        const uint32_t* __restrict__ vc, float* __restrict__ out,
+                                                        float* __restrict__ partial, XOut xo, int* err) {
   pdl_trigger();
-  // The step descriptor is written before the step's first kernel, so the part's key
-  // range is known before the wait. Every cached key before the step's own (position
-  // pos0 on) was written by earlier steps: the warp's first 8-key group of K and V rows is
-  // loaded into registers here, and its rows of the step's own keys (which the prep
-  // kernel writes meanwhile) again after the wait. Later groups' rows go to L2 here.
+  extern __shared__ __align__(128) uint8_t att_ring[];  // [warp][stage][K rows 4 KB | V rows 4 KB]
+  __shared__ uint64_t bars[kAttWarps][kAttStages];
+  __shared__ float s_ml[kAttWarps][G][2];
+  __shared__ float s_p[kAttWarps][32];
   const snl_step_u st = load_step(sr);
   const uint32_t kh = blockIdx.x, m = blockIdx.y, part = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -130,35 +138,36 @@ __global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, c
   const uint32_t start = min(total, part * chunk);
   const uint32_t end = min(total, start + chunk);
   const uint64_t kbase = (uint64_t)kh * HD;  // in halves
-  uint4 kw[kKeysPerGroup], vw[kKeysPerGroup];
-  uint32_t t0 = start + warp * kKeysPerGroup;
-  bool preloaded = false;
-  if (live) {
-    if (t0 < end) {
-      const uint32_t nk = min((uint32_t)kKeysPerGroup, end - t0);
-#pragma unroll
-      for (int j = 0; j < kKeysPerGroup; j++) {
-        const uint64_t row = ((uint64_t)(t0 + min((uint32_t)j, nk - 1)) * kv_dim + kbase) / 2 + lane * 4;
-        kw[j] = *reinterpret_cast<const uint4*>(kc + row);
-        vw[j] = *reinterpret_cast<const uint4*>(vc + row);
-      }
-      preloaded = true;
+  // warp-local group jj holds keys start + 8 (warp + 8 jj) ..; the part has ceil((end - start) / 8) groups
+  const uint32_t ngroups = live ? (end - start + kKeysPerGroup - 1) / kKeysPerGroup : 0;
+  const uint32_t my_groups = ngroups > (uint32_t)warp ? (ngroups - warp + kAttWarps - 1) / kAttWarps : 0;
+  uint8_t* ring = att_ring + (size_t)warp * kAttStages * kAttGroupBytes;
+  if (lane == 0)
+    for (uint32_t s2 = 0; s2 < kAttStages; s2++) mbar_init(&bars[warp][s2], 1);
+  fence_mbar_init();
+  __syncwarp();
+  auto group_key0 = [&](uint32_t jj) { return start + (warp + jj * kAttWarps) * kKeysPerGroup; };
+  // Rows past the part's end repeat its last key (weight 0 later), so every group is 8 KB.
+  auto issue = [&](uint32_t jj) {
+    const uint32_t t0 = group_key0(jj), nk = min((uint32_t)kKeysPerGroup, end - t0);
+    uint64_t* bar = &bars[warp][jj % kAttStages];
+    uint8_t* stg = ring + (jj % kAttStages) * kAttGroupBytes;
+    if (lane == 0) mbar_arrive_expect_tx(bar, kAttGroupBytes);
+    __syncwarp();
+    if (lane < 2 * kKeysPerGroup) {
+      const uint32_t j = lane % kKeysPerGroup, t = t0 + min(j, nk - 1);
+      const uint32_t* src = (lane < kKeysPerGroup ? kc : vc) + ((uint64_t)t * kv_dim + kbase) / 2;
+      bulk_g2s_plain(stg + (lane / kKeysPerGroup) * (kAttGroupBytes / 2) + j * (HD * 2), src, HD * 2, bar);
     }
-    // 4 lines of 128 B per row, K and V, of the part's rows after the first 64 (at most
-    // kPrefetchKeys more): a long context's whole KV (134 MB per layer at 32K) would
-    // overflow L2.
-    const uint32_t a0 = start + kAttWarps * kKeysPerGroup;
-    const uint32_t lines = a0 < end ? min(end - a0, kPrefetchKeys) * 8 : 0;
-    for (uint32_t i = threadIdx.x; i < lines; i += blockDim.x) {
-      const uint32_t t = a0 + (i >> 3), l = i & 3;
-      const uint32_t* base = (i & 4) ? vc : kc;
-      prefetch_l2(base + ((uint64_t)t * kv_dim + kbase) / 2 + l * 32);
-    }
+  };
+  // Requested before the wait: the leading groups whose rows all precede the step's keys.
+  uint32_t issued = 0;
+  while (issued < min(my_groups, kAttStages)) {
+    const uint32_t t0 = group_key0(issued), last = t0 + min((uint32_t)kKeysPerGroup, end - t0) - 1;
+    if (last >= st.pos0) break;
+    issue(issued++);
   }
   pdl_wait();
-  __shared__ float s_acc[kAttWarps][G][HD];  // 32 KB
-  __shared__ float s_ml[kAttWarps][G][2];
-  __shared__ float s_p[kAttWarps][32];
   if (m >= st.m) return;
   if (part >= st.parts) {
     // An unused part slot of a captured step (the grid has the largest part count): a
@@ -170,6 +179,7 @@ __global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, c
     }
     return;
   }
+  for (; issued < min(my_groups, kAttStages); issued++) issue(issued);
 
   float q[G][8];
 #pragma unroll
@@ -184,48 +194,22 @@ __global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, c
   for (int g = 0; g < (int)G; g++)
 #pragma unroll
     for (int e = 0; e < 8; e++) acc[g][e] = 0.f;
-  const int my_g = lane & 3;       // score lane -> (key lane/4, head lane%4)
-  float m_run = -1e30f, l_run = 0.f;  // for head my_g (replicated over lanes with that g)
+  float m_run = -1e30f, l_run = 0.f;  // for head lane % 4 (replicated over lanes with that head)
 
-  static_assert(kKeysPerGroup * 8 == 64, "lane -> (key, K or V, line) of a group's 64 lines");
-  // Parts of more than one round of key groups (long contexts) prefetch ahead.
-  const bool rpf = rolling_pf && end - start > kAttWarps * kKeysPerGroup;
-  for (; t0 < end; t0 += kAttWarps * kKeysPerGroup) {
-    const uint32_t nk = min((uint32_t)kKeysPerGroup, end - t0);
-    if (rpf) {
-      // The warp's next two groups' K and V rows into L2 (64 lines of 128 B per group, two
-      // per lane), so their loads later wait on L2 rather than HBM.
-#pragma unroll
-      for (uint32_t ahead = 1; ahead <= 2; ahead++) {
-        const uint32_t tg = t0 + ahead * kAttWarps * kKeysPerGroup;
-#pragma unroll
-        for (uint32_t h2 = 0; h2 < 2; h2++) {
-          const uint32_t li = lane * 2 + h2, tk = tg + (li >> 3);
-          if (tk < end) {
-            const uint32_t* base = (li & 4) ? vc : kc;
-            prefetch_l2(base + ((uint64_t)tk * kv_dim + kbase) / 2 + (li & 3) * 32);
-          }
-        }
-      }
+  bool ok = true;
+  uint32_t jj = 0;
+  for (; jj < my_groups; jj++) {
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&bars[warp][jj % kAttStages], (jj / kAttStages) & 1))) {
+      ok = false;
+      break;
     }
-    // The group's K and V rows are all loaded before the scores: the V loads do not wait
-    // for the softmax, so the group costs one memory latency instead of nine. Rows past
-    // the part's end repeat its last key and get weight 0. The first group's rows came
-    // before the wait; only its rows of this step's keys are read again.
-#pragma unroll
-    for (int j = 0; j < kKeysPerGroup; j++) {
-      const uint32_t t = t0 + min((uint32_t)j, nk - 1);
-      if (preloaded && t < st.pos0) continue;
-      const uint64_t row = ((uint64_t)t * kv_dim + kbase) / 2 + lane * 4;
-      kw[j] = *reinterpret_cast<const uint4*>(kc + row);
-      vw[j] = *reinterpret_cast<const uint4*>(vc + row);
-    }
-    preloaded = false;
+    const uint32_t t0 = group_key0(jj), nk = min((uint32_t)kKeysPerGroup, end - t0);
+    const uint8_t* stg = ring + (jj % kAttStages) * kAttGroupBytes;
     float part_s[32];
 #pragma unroll
     for (int j = 0; j < kKeysPerGroup; j++) {
       float k8[8];
-      h8_to_f(kw[j], k8);
+      h8_to_f(*reinterpret_cast<const uint4*>(stg + j * (HD * 2) + lane * 16), k8);
 #pragma unroll
       for (int g = 0; g < (int)G; g++) {
         float s = 0.f;
@@ -262,7 +246,7 @@ __global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, c
 #pragma unroll
     for (int j = 0; j < kKeysPerGroup; j++) {
       float v8[8];
-      h8_to_f(vw[j], v8);
+      h8_to_f(*reinterpret_cast<const uint4*>(stg + kAttGroupBytes / 2 + j * (HD * 2) + lane * 16), v8);
       const float4 pj = *reinterpret_cast<const float4*>(&s_p[warp][j * 4]);
       const float pg[G] = {pj.x, pj.y, pj.z, pj.w};
 #pragma unroll
@@ -270,13 +254,27 @@ __global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, c
 #pragma unroll
         for (int e = 0; e < 8; e++) acc[g][e] = fmaf(pg[g], v8[e], acc[g][e]);
     }
+    // The stage's rows were read by this warp's generic loads; the next bulk copy into it
+    // is ordered after them.
+    fence_proxy_async_smem();
     __syncwarp();
+    if (jj + kAttStages < my_groups) issue(jj + kAttStages);
   }
+  if (!ok) {
+    // A bounded wait gave up: flag it and let this warp's copies still in flight land
+    // before its ring is reused below (the CTA still meets at the merge barrier).
+    if (lane == 0) report_timeout(err);
+    for (uint32_t k2 = jj; k2 < min(my_groups, jj + kAttStages); k2++)
+      (void)mbar_wait_bounded(&bars[warp][k2 % kAttStages], (k2 / kAttStages) & 1);
+  }
+  // This warp's accumulators go to the start of its own ring (its copies have all landed).
+  float (*s_acc_w)[HD] = reinterpret_cast<float (*)[HD]>(ring);
+  auto s_acc = [&](int w, int g) { return reinterpret_cast<float*>(att_ring + (size_t)w * kAttStages * kAttGroupBytes) + g * HD; };
   // Publish this warp's state.
 #pragma unroll
   for (int g = 0; g < (int)G; g++) {
 #pragma unroll
-    for (int e = 0; e < 8; e++) s_acc[warp][g][lane * 8 + e] = acc[g][e];
+    for (int e = 0; e < 8; e++) s_acc_w[g][lane * 8 + e] = acc[g][e];
   }
   if (lane < (int)G) {
     s_ml[warp][lane][0] = m_run;
@@ -285,6 +283,7 @@ __global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, c
   __syncthreads();
   // Merge: thread d owns head dim d for the G heads.
   const uint32_t d = threadIdx.x;
+  if (d >= HD) return;
 #pragma unroll
   for (int g = 0; g < (int)G; g++) {
     float M = -1e30f;
@@ -295,7 +294,7 @@ __global__ void __launch_bounds__(256) attend_kernel(StepRef sr, snl_attn_p p, c
     for (int w = 0; w < kAttWarps; w++) {
       const float f = __expf(s_ml[w][g][0] - M);
       L = fmaf(s_ml[w][g][1], f, L);
-      A = fmaf(s_acc[w][g][d], f, A);
+      A = fmaf(s_acc(w, g)[d], f, A);
     }
     const uint32_t h = kh * G + g;
     if (gridDim.z == 1) {
@@ -644,8 +643,17 @@ int launch_attend(StepRef st, const snl_attn_p& p, const float* proj, const floa
                    st, p, proj, qbuf, kc, vc, out);
     return SNL_OK;
   }
-  static const int rolling_pf = getenv("SNL_NO_ATT_PF") == nullptr ? 1 : 0;
-  SNL_PDL_LAUNCH("attend_kernel", attend_kernel, dim3(dim3(p.n_kv, m, parts_grid)), dim3(kAttWarps * 32), (size_t)(0), s, st, p, proj, qbuf, kc, vc, out, partial, xo, rolling_pf);
+  int* err = nullptr;
+  if (int rc = device_error_word(&err)) return rc;
+  static bool ring_attr[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !ring_attr[dev]) {
+    SNL_CUDA_TRY(cudaFuncSetAttribute(attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttSmem));
+    ring_attr[dev] = true;
+  }
+  SNL_PDL_LAUNCH("attend_kernel", attend_kernel, dim3(dim3(p.n_kv, m, parts_grid)), dim3(kAttWarps * 32), kAttSmem, s, st,
+                 p, proj, qbuf, kc, vc, out, partial, xo, err);
   return SNL_OK;
 }
 
