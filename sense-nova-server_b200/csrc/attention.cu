@@ -106,6 +106,7 @@ constexpr int kAttWarps = 12;
 constexpr uint32_t kAttTcMinRows = 16;  // steps of at least this many rows use attend_tc_kernel
 constexpr int kKeysPerGroup = 8;
 constexpr uint32_t kAttStages = 2;  // key groups in flight per warp
+static_assert(kAttKeysPerPart == kAttWarps * kKeysPerGroup, "a decode part is one key group per warp");
 constexpr uint32_t kAttGroupBytes = kKeysPerGroup * 2 * HD * 2;  // 8 keys x (K row, V row) x 512 B
 constexpr size_t kAttSmem = (size_t)kAttWarps * kAttStages * kAttGroupBytes;  // 192 KB
 

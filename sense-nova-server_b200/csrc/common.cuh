@@ -177,6 +177,9 @@ int launch_swiglu(StepRef st, const snl_layer_p& p, const float* gu, float* act,
                   XOut xo = XOut());
 int launch_attn_prep(StepRef st, const snl_attn_p& p, const float* proj, float* qbuf, uint32_t* kc, uint32_t* vc,
                      const float* norms, const uint32_t* rpos, uint32_t m, cudaStream_t s);
+// Keys of one split-key part of a decode step's attention: one 8-key group per warp of
+// attend_kernel (12 warps).
+constexpr uint32_t kAttKeysPerPart = 96;
 int launch_attend(StepRef st, const snl_attn_p& p, const float* proj, const float* qbuf, const uint32_t* kc,
                   const uint32_t* vc, float* out, float* partial, uint32_t m, uint32_t parts_grid, cudaStream_t s,
                   XOut xo = XOut());

@@ -71,11 +71,11 @@ struct FT {
 
 uint32_t parts_for(size_t m, size_t total, uint32_t cap) {
   // engine.rs:827: split-K attention only for short steps. The reference splits every
-  // 256 keys; here a part is 64 keys (one 8-key group per warp of attend_kernel), so short
-  // contexts spread over more CTAs, up to cap parts. The split changes only the
-  // summation order.
+  // 256 keys; here a part is kAttKeysPerPart keys (one 8-key group per warp of
+  // attend_kernel), so short contexts spread over more CTAs, up to cap parts. The split
+  // changes only the summation order.
   if (m > 4) return 1;
-  size_t p = (total + 63) / 64;
+  size_t p = (total + kAttKeysPerPart - 1) / kAttKeysPerPart;
   return (uint32_t)std::min<size_t>(std::max<size_t>(p, 1), cap);
 }
 
