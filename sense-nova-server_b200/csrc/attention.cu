@@ -76,30 +76,43 @@ __global__ void __launch_bounds__(256) prep_kernel(StepRef sr, snl_attn_p p, con
   }
 }
 
-// 32 per-lane values -> lane L holds the warp-wide sum of value L (butterfly
-// reduce-scatter, 31 shuffles).
-__device__ __forceinline__ float reduce_scatter32(float v[32], int lane) {
-#pragma unroll
-  for (int o = 16, n = 16; o > 0; o >>= 1, n >>= 1) {
-    const bool up = (lane & o) != 0;
-#pragma unroll
-    for (int i = 0; i < n; i++) {
-      const float send = up ? v[i] : v[i + n];
-      const float keep = up ? v[i + n] : v[i];
-      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-    }
-  }
-  return v[0];
+__device__ __forceinline__ void fa_mma(float d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t r[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t r[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+// 16 bytes global -> shared, zero-filled when !valid (nothing is read then).
+__device__ __forceinline__ void fa_cp16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ uint32_t fa_h2(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+// hi / lo fp16 pairs of two floats: hi = f16(v), lo = f16(v - hi)
+__device__ __forceinline__ void fa_split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+  hi = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
+  lo = fa_h2(a - __half2float(ha), b - __half2float(hb));
 }
 
-__device__ __forceinline__ void h8_to_f(const uint4 w, float f[8]) {
-  const __half2* h = reinterpret_cast<const __half2*>(&w);
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const float2 t = __half22float2(h[i]);
-    f[2 * i] = t.x;
-    f[2 * i + 1] = t.y;
-  }
+__device__ __forceinline__ void mma16808(float d[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+               : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+               : "r"(a0), "r"(a1), "r"(b0));
 }
 
 constexpr int kAttWarps = 12;
@@ -107,12 +120,16 @@ constexpr uint32_t kAttTcMinRows = 16;  // steps of at least this many rows use 
 constexpr int kKeysPerGroup = 8;
 constexpr uint32_t kAttStages = 2;  // key groups in flight per warp
 static_assert(kAttKeysPerPart == kAttWarps * kKeysPerGroup, "a decode part is one key group per warp");
-constexpr uint32_t kAttGroupBytes = kKeysPerGroup * 2 * HD * 2;  // 8 keys x (K row, V row) x 512 B
-constexpr size_t kAttSmem = (size_t)kAttWarps * kAttStages * kAttGroupBytes;  // 192 KB
+constexpr uint32_t kAttRowBytes = HD * 2 + 16;  // a cached K or V row (512 B) padded so ldmatrix rows hit distinct banks
+constexpr uint32_t kAttGroupBytes = kKeysPerGroup * 2 * HD * 2;  // bytes copied per group: 8 keys x (K row, V row)
+constexpr uint32_t kAttStageBytes = kKeysPerGroup * 2 * kAttRowBytes;
+constexpr size_t kAttSmem = (size_t)kAttWarps * kAttStages * kAttStageBytes;  // 198 KB
 
 // attend: CTA (KV head, token, part); 12 warps each take 8-key groups round-robin and
-// keep their own online softmax for the G = 4 query heads; lane l owns head dims
-// [8l, 8l+8). The warps' states are merged at the end.
+// keep their own online softmax for the G = 4 query heads. Per group, the scores
+// S = Q K^T are 16 mma.sync m16n8k16 over the 256 dims (the 4 heads' queries as fp16
+// hi and lo rows, K exact), and O^T += V^T P^T is 16 m16n8k8 (V exact, P as hi and lo
+// columns), accumulated in f32 registers. The warps' states are merged at the end.
 // Each warp streams its groups' K and V rows (16 rows of 512 contiguous bytes) into a
 // ring of kAttStages groups in shared memory with bulk copies completing on one mbarrier
 // per stage, so two groups per warp (192 KB per SM, one CTA) are in flight while it
@@ -125,10 +142,10 @@ __global__ void __launch_bounds__(kAttWarps * 32, 1) attend_kernel(StepRef sr, s
                                                         const uint32_t* __restrict__ vc, float* __restrict__ out,
                                                         float* __restrict__ partial, XOut xo, int* err) {
   pdl_trigger();
-  extern __shared__ __align__(128) uint8_t att_ring[];  // [warp][stage][K rows 4 KB | V rows 4 KB]
+  extern __shared__ __align__(128) uint8_t att_ring[];  // [warp][stage][8 K rows | 8 V rows], rows kAttRowBytes apart
   __shared__ uint64_t bars[kAttWarps][kAttStages];
   __shared__ float s_ml[kAttWarps][G][2];
-  __shared__ float s_p[kAttWarps][32];
+  __shared__ __align__(16) __half q_tile[2 * G][HD + 8];  // rows of 528 B: ldmatrix rows on distinct banks
   const snl_step_u st = load_step(sr);
   const uint32_t kh = blockIdx.x, m = blockIdx.y, part = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -142,7 +159,7 @@ __global__ void __launch_bounds__(kAttWarps * 32, 1) attend_kernel(StepRef sr, s
   // warp-local group jj holds keys start + 8 (warp + 8 jj) ..; the part has ceil((end - start) / 8) groups
   const uint32_t ngroups = live ? (end - start + kKeysPerGroup - 1) / kKeysPerGroup : 0;
   const uint32_t my_groups = ngroups > (uint32_t)warp ? (ngroups - warp + kAttWarps - 1) / kAttWarps : 0;
-  uint8_t* ring = att_ring + (size_t)warp * kAttStages * kAttGroupBytes;
+  uint8_t* ring = att_ring + (size_t)warp * kAttStages * kAttStageBytes;
   if (lane == 0)
     for (uint32_t s2 = 0; s2 < kAttStages; s2++) mbar_init(&bars[warp][s2], 1);
   fence_mbar_init();
@@ -152,13 +169,13 @@ __global__ void __launch_bounds__(kAttWarps * 32, 1) attend_kernel(StepRef sr, s
   auto issue = [&](uint32_t jj) {
     const uint32_t t0 = group_key0(jj), nk = min((uint32_t)kKeysPerGroup, end - t0);
     uint64_t* bar = &bars[warp][jj % kAttStages];
-    uint8_t* stg = ring + (jj % kAttStages) * kAttGroupBytes;
+    uint8_t* stg = ring + (jj % kAttStages) * kAttStageBytes;
     if (lane == 0) mbar_arrive_expect_tx(bar, kAttGroupBytes);
     __syncwarp();
-    if (lane < 2 * kKeysPerGroup) {
+    if (lane < 2 * kKeysPerGroup) {  // lanes 0-7: K rows, 8-15: V rows
       const uint32_t j = lane % kKeysPerGroup, t = t0 + min(j, nk - 1);
       const uint32_t* src = (lane < kKeysPerGroup ? kc : vc) + ((uint64_t)t * kv_dim + kbase) / 2;
-      bulk_g2s_plain(stg + (lane / kKeysPerGroup) * (kAttGroupBytes / 2) + j * (HD * 2), src, HD * 2, bar);
+      bulk_g2s_plain(stg + lane * kAttRowBytes, src, HD * 2, bar);
     }
   };
   // Requested before the wait: the leading groups whose rows all precede the step's keys.
@@ -182,20 +199,32 @@ __global__ void __launch_bounds__(kAttWarps * 32, 1) attend_kernel(StepRef sr, s
   }
   for (; issued < min(my_groups, kAttStages); issued++) issue(issued);
 
-  float q[G][8];
-#pragma unroll
-  for (int g = 0; g < (int)G; g++) {
-    const float4* qp = reinterpret_cast<const float4*>(qbuf + (uint64_t)m * q_dim + (kh * G + g) * HD + lane * 8);
-    const float4 a = qp[0], b = qp[1];
-    q[g][0] = a.x * p.scale; q[g][1] = a.y * p.scale; q[g][2] = a.z * p.scale; q[g][3] = a.w * p.scale;
-    q[g][4] = b.x * p.scale; q[g][5] = b.y * p.scale; q[g][6] = b.z * p.scale; q[g][7] = b.w * p.scale;
+  // The GQA group's scores and outputs as mma.sync tiles. Q is the A operand of S = Q K^T:
+  // row 2h + e of the CTA's Q tile holds head h's scaled query as fp16 hi (e = 0) or lo
+  // (e = 1); rows 8-15 of the MMA are zero. K and V are exact fp16 operands; all three are
+  // read from shared memory with ldmatrix.
+  for (uint32_t i = threadIdx.x; i < G * HD / 2; i += blockDim.x) {
+    const uint32_t hq = i / (HD / 2), d2 = (i % (HD / 2)) * 2;
+    const float2 x = *reinterpret_cast<const float2*>(qbuf + (uint64_t)m * q_dim + (kh * G + hq) * HD + d2);
+    uint32_t hi, lo;
+    fa_split2(x.x * p.scale, x.y * p.scale, hi, lo);
+    *reinterpret_cast<uint32_t*>(&q_tile[2 * hq][d2]) = hi;
+    *reinterpret_cast<uint32_t*>(&q_tile[2 * hq + 1][d2]) = lo;
   }
-  float acc[G][8];
+  __syncthreads();
+  const uint32_t g = lane >> 2, t = lane & 3, qh = g >> 1, qhl = g & 1;
+  // O^T = V^T P^T accumulators: lane (g, t) holds head t's dims 16c + g (o[c][0] from P's
+  // hi half, o[c][1] from its lo half) and 16c + g + 8 (o[c][2], o[c][3]).
+  float o[16][4];
 #pragma unroll
-  for (int g = 0; g < (int)G; g++)
+  for (int c = 0; c < 16; c++)
 #pragma unroll
-    for (int e = 0; e < 8; e++) acc[g][e] = 0.f;
-  float m_run = -1e30f, l_run = 0.f;  // for head lane % 4 (replicated over lanes with that head)
+    for (int e = 0; e < 4; e++) o[c][e] = 0.f;
+  float m_run = -1e30f, l_run = 0.f;  // head qh's online softmax (equal in its 8 lanes)
+  // ldmatrix x4: lane L addresses row L % 8 of matrix L / 8 = (chunk c + L / 16, dims + 8 (L / 8 % 2))
+  const uint32_t lrow = lane & 7, lsel = lane >> 3;
+  const uint32_t lcol = (16 * (lsel >> 1) + 8 * (lsel & 1)) * 2;
+  const uint8_t* qst = reinterpret_cast<const uint8_t*>(&q_tile[lrow][0]) + lcol;
 
   bool ok = true;
   uint32_t jj = 0;
@@ -205,58 +234,55 @@ __global__ void __launch_bounds__(kAttWarps * 32, 1) attend_kernel(StepRef sr, s
       break;
     }
     const uint32_t t0 = group_key0(jj), nk = min((uint32_t)kKeysPerGroup, end - t0);
-    const uint8_t* stg = ring + (jj % kAttStages) * kAttGroupBytes;
-    float part_s[32];
+    const uint8_t* kst = ring + (jj % kAttStages) * kAttStageBytes + lrow * kAttRowBytes + lcol;
+    const uint8_t* vst = kst + kKeysPerGroup * kAttRowBytes;
+    // S for the group's 8 keys (two accumulator chains over the 16 chunks).
+    float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int j = 0; j < kKeysPerGroup; j++) {
-      float k8[8];
-      h8_to_f(*reinterpret_cast<const uint4*>(stg + j * (HD * 2) + lane * 16), k8);
-#pragma unroll
-      for (int g = 0; g < (int)G; g++) {
-        float s = 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; e++) s = fmaf(q[g][e], k8[e], s);
-        part_s[j * 4 + g] = s;
-      }
+    for (int c = 0; c < 16; c += 2) {
+      uint32_t qa[4], kb[4];
+      ldsm_x4(qa, qst + 32 * c);
+      ldsm_x4(kb, kst + 32 * c);
+      fa_mma(s0, qa[0], 0u, qa[1], 0u, kb[0], kb[1]);
+      fa_mma(s1, qa[2], 0u, qa[3], 0u, kb[2], kb[3]);
     }
-    float sc = reduce_scatter32(part_s, lane);
-    const uint32_t my_key = lane >> 2;
-    if (my_key >= nk) sc = -1e30f;
-    float mx = sc;
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+    // Head qh's scores of keys 2t and 2t + 1: its hi and lo rows (lanes g, g ^ 1) added.
+    float sa = s0[0] + s1[0], sb = s0[1] + s1[1];
+    sa += __shfl_xor_sync(0xffffffffu, sa, 4);
+    sb += __shfl_xor_sync(0xffffffffu, sb, 4);
+    const bool va_ok = 2 * t < nk, vb_ok = 2 * t + 1 < nk;
+    if (!va_ok) sa = -1e30f;
+    if (!vb_ok) sb = -1e30f;
+    float mx = fmaxf(sa, sb);
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
     const float m_new = fmaxf(m_run, mx);
-    const float pe = my_key < nk ? __expf(sc - m_new) : 0.f;
-    float ls = pe;
-    ls += __shfl_xor_sync(0xffffffffu, ls, 4);
-    ls += __shfl_xor_sync(0xffffffffu, ls, 8);
-    ls += __shfl_xor_sync(0xffffffffu, ls, 16);
+    const float pa = va_ok ? __expf(sa - m_new) : 0.f;
+    const float pb = vb_ok ? __expf(sb - m_new) : 0.f;
+    float ls = pa + pb;
+    ls += __shfl_xor_sync(0xffffffffu, ls, 1);
+    ls += __shfl_xor_sync(0xffffffffu, ls, 2);
     const float corr = __expf(m_run - m_new);
     l_run = l_run * corr + ls;
     m_run = m_new;
-    s_p[warp][lane] = pe;
-    float cg[G];
+    // P^T as the B operand: column 2h + e = head h's probabilities, fp16 hi (e = 0) or lo.
+    uint32_t phi, plo;
+    fa_split2(pa, pb, phi, plo);
+    const uint32_t pfrag = qhl ? plo : phi;
+    const float ct = __shfl_sync(0xffffffffu, corr, 8 * t);  // head t's correction (lane 8t: g = 2t)
 #pragma unroll
-    for (int g = 0; g < (int)G; g++) cg[g] = __shfl_sync(0xffffffffu, corr, g);
-    __syncwarp();
+    for (int c = 0; c < 16; c++)
 #pragma unroll
-    for (int g = 0; g < (int)G; g++)
+      for (int e = 0; e < 4; e++) o[c][e] *= ct;
 #pragma unroll
-      for (int e = 0; e < 8; e++) acc[g][e] *= cg[g];
-#pragma unroll
-    for (int j = 0; j < kKeysPerGroup; j++) {
-      float v8[8];
-      h8_to_f(*reinterpret_cast<const uint4*>(stg + kAttGroupBytes / 2 + j * (HD * 2) + lane * 16), v8);
-      const float4 pj = *reinterpret_cast<const float4*>(&s_p[warp][j * 4]);
-      const float pg[G] = {pj.x, pj.y, pj.z, pj.w};
-#pragma unroll
-      for (int g = 0; g < (int)G; g++)
-#pragma unroll
-        for (int e = 0; e < 8; e++) acc[g][e] = fmaf(pg[g], v8[e], acc[g][e]);
+    for (int c = 0; c < 16; c += 2) {
+      uint32_t va[4];
+      ldsm_x4_t(va, vst + 32 * c);
+      mma16808(o[c], va[0], va[1], pfrag);
+      mma16808(o[c + 1], va[2], va[3], pfrag);
     }
-    // The stage's rows were read by this warp's generic loads; the next bulk copy into it
-    // is ordered after them.
+    // The stage's rows were read by this warp's loads; the next bulk copy into it is
+    // ordered after them.
     fence_proxy_async_smem();
     __syncwarp();
     if (jj + kAttStages < my_groups) issue(jj + kAttStages);
@@ -270,16 +296,16 @@ __global__ void __launch_bounds__(kAttWarps * 32, 1) attend_kernel(StepRef sr, s
   }
   // This warp's accumulators go to the start of its own ring (its copies have all landed).
   float (*s_acc_w)[HD] = reinterpret_cast<float (*)[HD]>(ring);
-  auto s_acc = [&](int w, int g) { return reinterpret_cast<float*>(att_ring + (size_t)w * kAttStages * kAttGroupBytes) + g * HD; };
-  // Publish this warp's state.
+  auto s_acc = [&](int w, int h) { return reinterpret_cast<float*>(att_ring + (size_t)w * kAttStages * kAttStageBytes) + h * HD; };
+  // Publish this warp's state: head t's dims from the hi and lo halves summed.
 #pragma unroll
-  for (int g = 0; g < (int)G; g++) {
-#pragma unroll
-    for (int e = 0; e < 8; e++) s_acc_w[g][lane * 8 + e] = acc[g][e];
+  for (int c = 0; c < 16; c++) {
+    s_acc_w[t][16 * c + g] = o[c][0] + o[c][1];
+    s_acc_w[t][16 * c + g + 8] = o[c][2] + o[c][3];
   }
-  if (lane < (int)G) {
-    s_ml[warp][lane][0] = m_run;
-    s_ml[warp][lane][1] = l_run;
+  if (t == 0 && qhl == 0) {
+    s_ml[warp][qh][0] = m_run;
+    s_ml[warp][qh][1] = l_run;
   }
   __syncthreads();
   // Merge: thread d owns head dim d for the G heads.
@@ -401,39 +427,6 @@ constexpr uint32_t kFaTok = 16;             // query tokens per CTA
 constexpr uint32_t kFaKeys = 64;            // keys per block
 constexpr uint32_t kFaStride = HD + 8;      // halves per smem row (528 B: ldmatrix rows on distinct banks)
 constexpr size_t kFaSmem = (size_t)(2 * G * kFaTok + 4 * kFaKeys) * kFaStride * sizeof(__half);
-
-__device__ __forceinline__ void fa_mma(float d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                       uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void ldsm_x4(uint32_t r[4], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t r[4], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_u32(p)));
-}
-// 16 bytes global -> shared, zero-filled when !valid (nothing is read then).
-__device__ __forceinline__ void fa_cp16(void* dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0)
-               : "memory");
-}
-__device__ __forceinline__ uint32_t fa_h2(float a, float b) {
-  const __half2 h = __floats2half2_rn(a, b);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
-// hi / lo fp16 pairs of two floats: hi = f16(v), lo = f16(v - hi)
-__device__ __forceinline__ void fa_split2(float a, float b, uint32_t& hi, uint32_t& lo) {
-  const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
-  hi = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
-  lo = fa_h2(a - __half2float(ha), b - __half2float(hb));
-}
 
 __global__ void __launch_bounds__(128, 1) attend_tc_kernel(StepRef sr, snl_attn_p p, const float* __restrict__ proj,
                                                            const float* __restrict__ qbuf,
