@@ -17,7 +17,7 @@ import hashlib
 
 import numpy as np
 
-from sensenova_b200.ffi import AttnP, LayerP, LinP, MatP, StepU
+from sensenova_b200.ffi import AttnP, LayerP, LinP, MatP, StepU, VisP
 
 Q8, Q4 = 1, 2
 HD = 256
@@ -69,6 +69,11 @@ CASES = [
     ("attend_3parts", "attend", dict(m=1, pos0=40, parts=3, ctx=44)),
     ("conv", "conv", dict(m=5, ckpt=2)),
     ("delta", "delta", dict(m=3, ckpt=2)),
+    # vision.wgsl (the tower's kernels around its matrix products)
+    ("vis_layer_norm", "vis_layer_norm", dict(rows=5, cols=300)),
+    *[(f"vis_epilogue_mode{md}_act{ac}", "vis_epilogue", dict(rows=5, cols=300, mode=md, act=ac))
+      for md, ac in ((0, 1), (0, 2), (1, 0), (2, 0))],
+    ("vis_rope_attend", "vis_rope_attend", dict(n=24, grid_w=6, heads=3)),
 ]
 
 
@@ -127,6 +132,15 @@ def inputs(name: str, kernel: str, a: dict) -> dict:
             d.update(qbuf=hashed(t("q"), m * p.n_heads * HD, 2.0), out=np.zeros(m * p.n_heads * HD, np.float32),
                      partial=np.zeros(m * p.n_heads * a["parts"] * (HD + 2), np.float32))
         return d
+    if kernel == "vis_layer_norm":
+        r, c = a["rows"], a["cols"]
+        return dict(a=hashed(t("a"), r * c, 3.0, 0.5), w=np.concatenate([hashed(t("w"), c, 0.2, 1.0), hashed(t("b"), c, 0.2)]))
+    if kernel == "vis_epilogue":
+        r, c = a["rows"], a["cols"]
+        return dict(a=hashed(t("a"), r * c, 4.0), b=hashed(t("b"), r * c, 2.0), w=hashed(t("w"), c, 0.5),
+                    e=hashed(t("e"), r * c, 2.0))
+    if kernel == "vis_rope_attend":
+        return dict(qkv=hashed(t("qkv"), a["n"] * 3 * a["heads"] * 72, 2.0))
     lp = lin_p()
     m = a["m"]
     lw = np.concatenate([hashed(t("cw"), lp.conv_dim * 4, 0.9), hashed(t("al"), lp.n_v, 0.2),
@@ -153,13 +167,20 @@ def params(kernel: str, a: dict):
         return StepU(a["m"], 0, 1, 0), layer_p(64, inter=a["inter"])
     if kernel in ("attn_prep", "attend"):
         return StepU(a["m"], a["pos0"], a.get("parts", 1), 0), attn_p()
+    if kernel == "vis_layer_norm":
+        return None, VisP(a["rows"], a["cols"], 0, 0, 1e-6, 0, 0, 0)
+    if kernel == "vis_epilogue":
+        return None, VisP(a["rows"], a["cols"], a["mode"], a["act"], 0, 0, 0, 0)
+    if kernel == "vis_rope_attend":
+        return None, VisP(a["n"], 0, 0, 0, 0, a["grid_w"], a["heads"], 0)
     return StepU(a["m"], 0, 1, a["ckpt"]), lin_p()
 
 
 # Outputs each case records (buffers after the call).
 OUTPUTS = {"mat": ["y"], "branch_norm": ["out"], "mhc": ["raw", "coef"], "merge": ["x"], "swiglu": ["act"],
            "attn_prep": ["qbuf", "kc", "vc"], "attend": ["out", "partial"], "conv": ["conv_out", "conv_state", "conv_ckpt"],
-           "delta": ["out", "state", "state_ckpt"]}
+           "delta": ["out", "state", "state_ckpt"], "vis_layer_norm": ["b"], "vis_epilogue": ["a", "b"],
+           "vis_rope_attend": ["qkv", "out"]}
 
 
 def run(name: str, kernel: str, a: dict, impl) -> dict:
@@ -187,4 +208,11 @@ def run(name: str, kernel: str, a: dict, impl) -> dict:
         impl.conv(st, p, d["proj"], d["conv_out"], d["conv_state"], d["lw"], d["conv_ckpt"])
     elif kernel == "delta":
         impl.delta(st, p, d["proj"], d["conv_out"], d["state"], d["lw"], d["out"], d["state_ckpt"])
+    elif kernel == "vis_layer_norm":
+        d["b"] = impl.vis_layer_norm(p, d["a"], d["w"])
+    elif kernel == "vis_epilogue":
+        impl.vis_epilogue(p, d["a"], None if a["mode"] == 0 else d["b"], d["w"], d["e"] if a["mode"] == 2 else None)
+    elif kernel == "vis_rope_attend":
+        impl.vis_rope(p, d["qkv"])
+        d["out"] = impl.vis_attend(p, d["qkv"])
     return {k: d[k] for k in OUTPUTS[kernel]}

@@ -85,6 +85,22 @@ class Cuda:
     def delta(self, st, p, proj, conv_out, state, lw, out, state_ckpt):
         self._run(self.lib.snl_delta, C.byref(st), C.byref(p), proj, conv_out, state, lw, out, state_ckpt)
 
+    def vis_layer_norm(self, p, a, w):
+        b = np.zeros_like(a)
+        self._run(self.lib.snl_vis_layer_norm, C.byref(p), a, b, w)
+        return b
+
+    def vis_epilogue(self, p, a, b, w, e=None):
+        self._run(self.lib.snl_vis_epilogue, C.byref(p), a, b, w, e)
+
+    def vis_rope(self, p, qkv):
+        self._run(self.lib.snl_vis_rope, C.byref(p), qkv)
+
+    def vis_attend(self, p, qkv):
+        out = np.zeros((p.rows * p.heads * 72,), np.float32)
+        self._run(self.lib.snl_vis_attend, C.byref(p), qkv, out)
+        return out
+
 
 @pytest.fixture(scope="module")
 def cuda(torch_cuda, lib):
