@@ -464,14 +464,21 @@ def build(ref: Path = DEFAULT_REF, out: Path = OUT, force: bool = False) -> Path
     deps = [HERE / "wgsl_rt.h", Path(__file__)] + sorted((ref / "src" / "shaders").glob("*.wgsl")) + [ref / "src" / "gpu.rs"]
     if not force and lib.exists() and all(lib.stat().st_mtime >= d.stat().st_mtime for d in deps):
         return lib
+    return compile_modules(module_sources(ref), out, lib.name)
+
+
+def compile_modules(srcs: dict[str, str], out: Path, lib_name: str) -> Path:
+    """Translate WGSL modules {name: source} and link them into out/lib_name; module
+    `name` exports wr_<name>_dispatch and wr_<name>_entries."""
     out.mkdir(parents=True, exist_ok=True)
     cpps = []
-    for name, src in module_sources(ref).items():
+    for name, src in srcs.items():
         m = Module(name, src)
         m.translate()
         p = out / f"wgsl_{name}.cpp"
         p.write_text(m.cpp())
         cpps.append(p)
+    lib = out / lib_name
     cxx = os.environ.get("SNL_CXX") or shutil.which("g++") or "g++"
     cmd = [cxx, "-O2", "-std=c++20", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-shared", "-pthread",
            "-I", str(HERE), *map(str, cpps), "-o", str(lib)]

@@ -29,26 +29,32 @@ def available() -> bool:
     return (wgsl2cpp.DEFAULT_REF / "src" / "shaders").is_dir()
 
 
+def load(path, modules) -> C.CDLL:
+    """A library of translated modules (wgsl2cpp.compile_modules) with its dispatchers typed."""
+    L = C.CDLL(str(path))
+    for m in modules:
+        f = getattr(L, f"wr_{m}_dispatch")
+        f.restype = C.c_int64
+        f.argtypes = [C.c_char_p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_int, C.POINTER(C.c_int),
+                      C.POINTER(C.c_void_p), C.POINTER(C.c_uint64)]
+    return L
+
+
 def lib() -> C.CDLL:
     global _lib
     if _lib is None:
         path = wgsl2cpp.build()
         if path is None:
             raise FileNotFoundError("reference tree absent: the reference shaders cannot be built")
-        L = C.CDLL(str(path))
-        for m in wgsl2cpp.MODULES:
-            f = getattr(L, f"wr_{m}_dispatch")
-            f.restype = C.c_int64
-            f.argtypes = [C.c_char_p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_int, C.POINTER(C.c_int),
-                          C.POINTER(C.c_void_p), C.POINTER(C.c_uint64)]
-        _lib = L
+        _lib = load(path, wgsl2cpp.MODULES)
     return _lib
 
 
-def dispatch(module: str, entry: str, grid: tuple[int, int, int], bindings: dict) -> None:
+def dispatch(module: str, entry: str, grid: tuple[int, int, int], bindings: dict, library: C.CDLL | None = None) -> None:
     """Run one entry point over grid; bindings maps binding index -> numpy array (storage,
     bound over its whole extent) or ctypes struct (uniform). Raises on an out-of-bounds
-    access or a binding the module does not have."""
+    access or a binding the module does not have. library: the reference's modules unless
+    given."""
     keep, ids, ptrs, sizes = [], [], [], []
     for b, v in sorted(bindings.items()):
         if isinstance(v, np.ndarray):
@@ -63,7 +69,7 @@ def dispatch(module: str, entry: str, grid: tuple[int, int, int], bindings: dict
         ids.append(b)
         keep.append(v)
     n = len(ids)
-    rc = getattr(lib(), f"wr_{module}_dispatch")(
+    rc = getattr(library if library is not None else lib(), f"wr_{module}_dispatch")(
         entry.encode(), *[int(g) for g in grid], n, (C.c_int * n)(*ids), (C.c_void_p * n)(*ptrs),
         (C.c_uint64 * n)(*sizes))
     if rc == -1:
