@@ -366,7 +366,9 @@ def run_reference(args):
     v, n = oracle_decode(m, orc, first, args.warmup, args.steps, budget)
     thr = orc.threads()
     m.close()
-    sample = (f"9B-shape {args.quant} greedy decode after a {len(prompt)}-token prompt, {args.warmup} warm-up and "
+    sample = (f"oracle/ (the reference's kernels restated in C++, bit-identical to its WGSL translated and run on the "
+              f"host, tests/test_reference_shaders.py): "
+              f"9B-shape {args.quant} greedy decode after a {len(prompt)}-token prompt, {args.warmup} warm-up and "
               f"{n} timed tokens (of --steps {args.steps}; capped at ~{budget:.0f} s of CPU work), {thr} OpenMP "
               f"threads, weights generated in {build_s:.0f} s. The prompt is short because a 2048-token prefill "
               f"costs ~54 TFLOP on the CPU; the KV reads at 2K context are <1% of a decode step's bytes")
@@ -535,7 +537,8 @@ def run_ours(args):
         # the oracle model of the parity check, decoding on from where it stopped
         v, n = oracle_decode(om, orc, parity["tokens_oracle"][-1], 0, 32, args.cpu_budget_s)
         cpu = {"value": v, "unit": "tok/s", "cores": orc.threads(), "kind": "port",
-               "sample": f"oracle/ (C++ restatement of the WGSL kernels, OpenMP, AVX2) greedy decode of the same "
+               "sample": f"oracle/ (C++ restatement of the WGSL kernels, bit-identical to the reference's WGSL "
+                         f"translated and run on the host; OpenMP, AVX2) greedy decode of the same "
                          f"9B-shape {args.quant} model after a {len(pprompt)}-token prompt, {n} tokens timed; KV "
                          f"reads at 2K context are <1% of the 13.9 GB weight stream, so a short context stands in"}
     if om is not None:
