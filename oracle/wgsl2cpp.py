@@ -408,8 +408,8 @@ class Module:
         out += self.structs
         for b, n, kind, ty in self.bindings:
             out.append(f"static {ty} {n};" if kind == "uniform" else f"static Buf<{ty}> {n};")
-        for n, ty in self.wg_vars:
-            out.append(f"static {ty} {n};")
+        for n, ty in self.wg_vars:  # one copy per host thread: each thread runs its own workgroup
+            out.append(f"static thread_local {ty} {n};")
         out.append("static void zero_wg() {" + " ".join(f"{n} = {ty}{{}};" for n, ty in self.wg_vars) + "}")
         out += self.protos
         out += self.bodies

@@ -8,14 +8,18 @@
 //     Buf<T> for runtime-sized storage arrays, with the WGSL operators;
 //   * the builtins the translated shaders call (W_exp, W_inverseSqrt, W_pack2x16float ...);
 //     transcendentals come from the host libm in f32, as in oracle/oracle.cpp;
-//   * a dispatcher: one host thread per invocation of a workgroup, workgroupBarrier() as
-//     a std::barrier over those threads, workgroups run one after another (workgroup
-//     memory is zeroed before each one, as WGSL zero-initializes it).
+//   * a dispatcher: the invocations of a workgroup run as fibers on one host thread,
+//     workgroupBarrier() as a switch back to a scheduler that releases them together;
+//     workgroups run on several host threads at once (workgroup memory is per thread and
+//     zeroed before each workgroup, as WGSL zero-initializes it).
 // Out-of-bounds array or buffer accesses, which WGSL would clamp or discard, are
 // recorded (the dispatch then fails) so a harness mistake is never mistaken for a result.
 #pragma once
 #include <atomic>
-#include <barrier>
+#include <ucontext.h>
+
+#include <algorithm>
+#include <memory>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -191,39 +195,86 @@ struct Builtins {
   u32 local_invocation_index;
 };
 
-inline thread_local std::barrier<>* tl_barrier = nullptr;
-inline void W_workgroupBarrier() { tl_barrier->arrive_and_wait(); }
-inline void W_storageBarrier() { tl_barrier->arrive_and_wait(); }
+// The invocations of one workgroup run as fibers (ucontext) on one host thread:
+// workgroupBarrier() switches back to the scheduler, which resumes every invocation only
+// after all of them have reached the barrier (or returned). Workgroup variables are
+// thread_local, so host threads run different workgroups at the same time, as a GPU does.
+struct FiberSet {
+  static constexpr size_t kStack = 64 * 1024;
+  u32 W = 0, cur = 0;
+  std::vector<ucontext_t> ctx;
+  std::vector<std::unique_ptr<char[]>> stk;
+  std::vector<uint8_t> done;
+  std::vector<Builtins> bi;
+  ucontext_t main{};
+  const std::function<void(const Builtins&)>* entry = nullptr;
+  explicit FiberSet(u32 w) : W(w), ctx(w), done(w), bi(w) {
+    for (u32 i = 0; i < w; i++) stk.emplace_back(new char[kStack]);
+  }
+};
+inline thread_local FiberSet* tl_fs = nullptr;
+inline void fiber_main() {
+  FiberSet* fs = tl_fs;
+  const u32 i = fs->cur;
+  (*fs->entry)(fs->bi[i]);
+  fs->done[i] = 1;  // uc_link returns to the scheduler
+}
+inline void W_workgroupBarrier() {
+  FiberSet* fs = tl_fs;
+  swapcontext(&fs->ctx[fs->cur], &fs->main);
+}
+inline void W_storageBarrier() { W_workgroupBarrier(); }
 
-// Runs entry over the grid; zero_wg clears the module's workgroup variables. Returns
-// the number of out-of-bounds accesses seen (0 on success).
+// Runs entry over the grid; zero_wg clears the calling thread's workgroup variables.
+// Returns the number of out-of-bounds accesses seen (0 on success).
 inline uint64_t dispatch(const std::function<void(const Builtins&)>& entry, const std::function<void()>& zero_wg,
                          u32 gx, u32 gy, u32 gz, u32 wx, u32 wy, u32 wz) {
   g_oob.store(0);
   const u32 W = wx * wy * wz;
-  std::barrier<> bar((std::ptrdiff_t)W);
-  auto body = [&](u32 li) {
-    tl_barrier = &bar;
-    Builtins b{};
-    b.local_invocation_index = li;
-    b.local_invocation_id = vec3<u32>(li % wx, (li / wx) % wy, li / (wx * wy));
-    b.num_workgroups = vec3<u32>(gx, gy, gz);
-    for (u32 z = 0; z < gz; z++)
-      for (u32 y = 0; y < gy; y++)
-        for (u32 x = 0; x < gx; x++) {
-          if (li == 0) zero_wg();
-          bar.arrive_and_wait();
-          b.workgroup_id = vec3<u32>(x, y, z);
-          b.global_invocation_id = vec3<u32>(x * wx + b.local_invocation_id.x, y * wy + b.local_invocation_id.y,
-                                             z * wz + b.local_invocation_id.z);
-          entry(b);
-          bar.arrive_and_wait();
+  const uint64_t nwg = (uint64_t)gx * gy * gz;
+  std::atomic<uint64_t> next{0};
+  auto worker = [&]() {
+    FiberSet fs(W);
+    fs.entry = &entry;
+    tl_fs = &fs;
+    for (;;) {
+      const uint64_t g = next.fetch_add(1);
+      if (g >= nwg) break;
+      const u32 x = (u32)(g % gx), y = (u32)((g / gx) % gy), z = (u32)(g / ((uint64_t)gx * gy));
+      zero_wg();
+      for (u32 i = 0; i < W; i++) {
+        Builtins& b = fs.bi[i];
+        b.local_invocation_index = i;
+        b.local_invocation_id = vec3<u32>(i % wx, (i / wx) % wy, i / (wx * wy));
+        b.num_workgroups = vec3<u32>(gx, gy, gz);
+        b.workgroup_id = vec3<u32>(x, y, z);
+        b.global_invocation_id = vec3<u32>(x * wx + b.local_invocation_id.x, y * wy + b.local_invocation_id.y,
+                                           z * wz + b.local_invocation_id.z);
+        getcontext(&fs.ctx[i]);
+        fs.ctx[i].uc_stack.ss_sp = fs.stk[i].get();
+        fs.ctx[i].uc_stack.ss_size = FiberSet::kStack;
+        fs.ctx[i].uc_link = &fs.main;
+        makecontext(&fs.ctx[i], fiber_main, 0);
+        fs.done[i] = 0;
+      }
+      // One pass runs every live invocation to its next barrier or its end.
+      for (bool live = true; live;) {
+        live = false;
+        for (u32 i = 0; i < W; i++) {
+          if (fs.done[i]) continue;
+          fs.cur = i;
+          swapcontext(&fs.main, &fs.ctx[i]);
+          live = true;
         }
-    tl_barrier = nullptr;
+      }
+    }
+    tl_fs = nullptr;
   };
+  const u32 hw = std::max(1u, std::thread::hardware_concurrency());
+  const u32 T = (u32)std::min<uint64_t>(std::min<u32>(hw, 16), nwg);
   std::vector<std::thread> th;
-  th.reserve(W);
-  for (u32 i = 0; i < W; i++) th.emplace_back(body, i);
+  for (u32 t = 1; t < T; t++) th.emplace_back(worker);
+  worker();
   for (auto& t : th) t.join();
   return g_oob.load();
 }

@@ -1,0 +1,148 @@
+"""The reference's forward pass from its own kernels - TEST INFRASTRUCTURE ONLY.
+
+The op list that src/engine.rs:383-493 records (and forward_mm, :801-936, runs per
+prefill chunk), restated in Python over the reference's WGSL kernels translated to C++
+(oracle/wgslref.py), with the weights of an oracle model (oracle/oracle.py) so both run
+on the same tensors. A test compares its logits with the oracle model's: the same graph,
+one side built from the reference's kernel code.
+
+Steps of at most one prefill chunk (512 rows) per call; Q8_0 weights (the oracle model's
+default quantization).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+if str(HERE) not in sys.path:
+    sys.path.insert(0, str(HERE))
+import wgslref as wr  # noqa: E402
+from sensenova_b200.ffi import AttnP, LayerP, LinP, MatP, StepU  # noqa: E402
+
+Q8 = 1
+CHUNK = 512  # engine.rs prefill_chunk
+
+
+class RefModel:
+    def __init__(self, cfg, ctx: int, weights):
+        self.cfg, self.ctx, self.w = cfg, ctx, weights
+        self.plan = cfg.execution_plan()
+        self.pos = 0
+        h = cfg.hidden
+        self.hlast = np.zeros(h, np.float32)
+        n_full = sum(1 for li in self.plan if cfg.full_attention[li])
+        n_lin = len(self.plan) - n_full
+        kv_words = ctx * cfg.kv_dim // 2
+        self.kc = [np.zeros(kv_words, np.uint32) for _ in range(n_full)]
+        self.vc = [np.zeros(kv_words, np.uint32) for _ in range(n_full)]
+        self.conv = [np.zeros(3 * cfg.conv_dim, np.float32) for _ in range(n_lin)]
+        self.state = [np.zeros(cfg.lin_v_heads * 128 * 128, np.float32) for _ in range(n_lin)]
+
+    # -- weights of the oracle model --
+    def q(self, name: str):
+        ptr, rows, cols, s = self.w.tensor(name)
+        q = np.ctypeslib.as_array((C.c_uint8 * (rows * cols)).from_address(ptr)).copy()
+        sc = np.ctypeslib.as_array((C.c_float * (rows * cols // 32)).from_address(s)).copy()
+        return q, sc, rows, cols
+
+    def f(self, name: str) -> np.ndarray:
+        ptr, _, n, _ = self.w.tensor(name)
+        return np.ctypeslib.as_array((C.c_float * n).from_address(ptr)).copy()
+
+    def layer_p(self, mode: int, last_row: bool = False) -> LayerP:
+        c = self.cfg
+        return LayerP(c.hidden, mode, 1 if last_row else 0, c.eps, 1.0, c.mhc.iterations if c.mhc else 0,
+                      c.intermediate, 0)
+
+    def mat(self, st, name, x, x_stride, y, y_stride, m_one=0, x_off=0):
+        """engine.rs:336-363 (one chunk: n_off 0)."""
+        q, s, rows, cols = self.q(name)
+        wr.mat(Q8, st, MatP(rows, cols, x_off, x_stride, 0, y_stride, 0, m_one), x, q, s, y)
+
+    def forward(self, tokens, want_logits: bool):
+        c, h = self.cfg, self.cfg.hidden
+        m = len(tokens)
+        assert 0 < m <= CHUNK and self.pos + m <= self.ctx
+        total = self.pos + m
+        parts = min(max(-(-total // 256), 1), 64) if m <= 4 else 1  # engine.rs:827
+        st = StepU(m, self.pos, parts, 0)
+        # embed (engine.rs:777-790): stream 0 the dequantized row, stream 1 zero
+        eq, es, _, _ = self.q("embed")
+        x = np.zeros(m * 2 * h, np.float32)
+        codes = eq.view(np.int8).astype(np.float32)
+        for i, t in enumerate(tokens):
+            x[i * 2 * h:i * 2 * h + h] = codes[t * h:(t + 1) * h] * np.repeat(es[t * h // 32:(t + 1) * h // 32], 32)
+        rpos = np.repeat(np.arange(self.pos, self.pos + m, dtype=np.uint32)[:, None], 4, 1).reshape(-1).copy()
+        coef = np.zeros(m * 8, np.float32)
+        xn = np.zeros(m * h, np.float32)
+        proj = np.zeros(m * max(c.attn_proj_rows, c.lin_proj_rows, 2 * c.intermediate), np.float32)
+        act = np.zeros(m * max(c.intermediate, c.conv_dim), np.float32)
+        attn_out = np.zeros(m * max(c.q_dim, c.lin_value_dim), np.float32)
+        branch = np.zeros(m * h, np.float32)
+        qbuf = np.zeros(m * c.q_dim, np.float32)
+        partial = np.zeros(m * c.n_heads * parts * 258, np.float32)
+        raw = np.zeros(m * 9, np.float32)
+
+        def push_norm(router, norm_w):
+            if router is not None:
+                wr.mhc_dots(st, self.layer_p(0), x, router, raw)
+                wr.mhc_finish(st, self.layer_p(0), raw, router, coef)
+            wr.branch_norm(st, self.layer_p(1 if router is not None else 0), x, coef, norm_w, xn, m)
+
+        lin_slot = full_slot = 0
+        mhc_start = c.mhc.start if c.mhc else None
+        mhc_end = c.mhc.end if c.mhc else None
+        for li in self.plan:
+            L = f"l{li}."
+            mhc = c.is_mhc(li)
+            if mhc and li == mhc_start:
+                wr.merge(st, self.layer_p(3), x, coef, branch)
+            push_norm(self.f(L + "mhc_attn") if mhc else None, self.f(L + "in_ln"))
+            if c.full_attention[li]:
+                stride = c.attn_proj_rows
+                self.mat(st, L + "qkv", xn, h, proj, stride)
+                ap = AttnP(c.n_heads, c.n_kv_heads, c.rot_dim, stride, c.rope_theta, c.eps,
+                           float(np.float32(1.0) / np.sqrt(np.float32(c.head_dim))),
+                           ((3 * c.mrope_section[1]) << 16) | (3 * c.mrope_section[2]))
+                kc, vc = self.kc[full_slot], self.vc[full_slot]
+                wr.attn_prep(st, ap, proj, qbuf, kc, vc, self.f(L + "qk_norm"), rpos)
+                wr.attend(st, ap, proj, qbuf, kc, vc, attn_out, partial)
+                if parts > 1:
+                    wr.attn_combine(st, ap, proj, partial, attn_out)
+                self.mat(st, L + "o_proj", attn_out, c.q_dim, branch, h)
+                full_slot += 1
+            else:
+                stride = c.lin_proj_rows
+                self.mat(st, L + "in_proj", xn, h, proj, stride)
+                lp = LinP(c.conv_dim, stride, c.lin_k_heads, c.lin_v_heads, c.eps, (0, 0, 0))
+                lw = self.f(L + "lin")
+                ck = np.zeros_like(self.conv[lin_slot])
+                sk = np.zeros_like(self.state[lin_slot])
+                wr.conv(st, lp, proj, act, self.conv[lin_slot], lw, ck)
+                wr.delta(st, lp, proj, act, self.state[lin_slot], lw, attn_out, sk)
+                self.mat(st, L + "out_proj", attn_out, c.lin_value_dim, branch, h)
+                lin_slot += 1
+            wr.merge(st, self.layer_p(1 if mhc else 0), x, coef, branch)
+            push_norm(self.f(L + "mhc_ffn") if mhc else None, self.f(L + "post_ln"))
+            self.mat(st, L + "gate_up", xn, h, proj, 2 * c.intermediate)
+            wr.swiglu(st, self.layer_p(0), proj, act)
+            self.mat(st, L + "down", act, c.intermediate, branch, h)
+            mode = 0 if not mhc else (2 if li + 1 == mhc_end else 1)
+            wr.merge(st, self.layer_p(mode), x, coef, branch)
+        # final norm into rows 1..m of hid (row 0: the previous step's last hidden row), head
+        hid = np.zeros((m + 1) * h, np.float32)
+        hid[:h] = self.hlast
+        out_rows = np.zeros(m * h, np.float32)
+        wr.branch_norm(st, self.layer_p(0), x, coef, self.f("norm"), out_rows, m)
+        hid[h:] = out_rows
+        logits = None
+        if want_logits:
+            logits = np.zeros(c.vocab, np.float32)
+            self.mat(st, "lm_head", hid, h, logits, c.vocab, m_one=1, x_off=m * h)
+        self.hlast = hid[m * h:(m + 1) * h].copy()
+        self.pos += m
+        return logits

@@ -1,0 +1,37 @@
+"""The whole forward pass from the reference's own kernels against the oracle model.
+
+oracle/wgslref_model.py composes the reference's WGSL kernels (translated to C++ and run
+on the host cores) in the op order of src/engine.rs:383-493 and forward_mm (:801-936),
+on the oracle model's weights. Every kernel call of the reduced model's graph (DeltaNet
+and attention layers, the mHC loop, split-key attention with several parts, the LM head)
+must give the oracle's bits, through a prefill and greedy decode steps.
+"""
+import numpy as np
+import pytest
+
+import oracle as orc
+import wgslref as wr
+from sensenova_b200.config import small
+
+pytestmark = pytest.mark.skipif(not wr.available(), reason="reference tree absent")
+
+
+def test_reference_kernels_forward_matches_oracle_model():
+    from wgslref_model import RefModel
+
+    cfg = small()
+    ctx = 320
+    om = orc.OracleModel(cfg, ctx, seed=3)
+    rm = RefModel(cfg, ctx, om)
+    prompt = [(17 + 7919 * i) % cfg.vocab for i in range(258)]  # one tiled-matmul chunk
+    lo, lr = om.forward(prompt, True), rm.forward(prompt, True)
+    # decode steps past 256 keys: the split-key attention runs with two parts and combine
+    steps = 0
+    while True:
+        assert np.array_equal(lo.view(np.uint32), lr.view(np.uint32)), f"logits differ at step {steps}"
+        tok = int(np.argmax(lo))
+        steps += 1
+        if steps > 3:
+            break
+        lo, lr = om.forward([tok], True), rm.forward([tok], True)
+    om.close()
