@@ -7,7 +7,8 @@ on the same tensors. A test compares its logits with the oracle model's: the sam
 one side built from the reference's kernel code.
 
 Steps of at most one prefill chunk (512 rows) per call; Q8_0 weights (the oracle model's
-default quantization).
+default quantization). `mtp` restates Engine::mtp (engine.rs:700-774) over the MTP layer
+that engine.rs:495-580 builds, when the oracle model has one.
 """
 from __future__ import annotations
 
@@ -41,6 +42,10 @@ class RefModel:
         self.vc = [np.zeros(kv_words, np.uint32) for _ in range(n_full)]
         self.conv = [np.zeros(3 * cfg.conv_dim, np.float32) for _ in range(n_lin)]
         self.state = [np.zeros(cfg.lin_v_heads * 128 * 128, np.float32) for _ in range(n_lin)]
+        self.mkc = np.zeros(kv_words, np.uint32)  # the MTP layer's own cache
+        self.mvc = np.zeros(kv_words, np.uint32)
+        self.hid = np.zeros(h, np.float32)
+        self.hid_rows = 0
 
     # -- weights of the oracle model --
     def q(self, name: str):
@@ -63,6 +68,22 @@ class RefModel:
         q, s, rows, cols = self.q(name)
         wr.mat(Q8, st, MatP(rows, cols, x_off, x_stride, 0, y_stride, 0, m_one), x, q, s, y)
 
+    def embed(self, tokens) -> np.ndarray:
+        """engine.rs:777-790: stream 0 the dequantized row, stream 1 zero."""
+        h = self.cfg.hidden
+        eq, es, _, _ = self.q("embed")
+        x = np.zeros(len(tokens) * 2 * h, np.float32)
+        codes = eq.view(np.int8).astype(np.float32)
+        for i, t in enumerate(tokens):
+            x[i * 2 * h:i * 2 * h + h] = codes[t * h:(t + 1) * h] * np.repeat(es[t * h // 32:(t + 1) * h // 32], 32)
+        return x
+
+    def attn_p(self) -> AttnP:
+        c = self.cfg
+        return AttnP(c.n_heads, c.n_kv_heads, c.rot_dim, c.attn_proj_rows, c.rope_theta, c.eps,
+                     float(np.float32(1.0) / np.sqrt(np.float32(c.head_dim))),
+                     ((3 * c.mrope_section[1]) << 16) | (3 * c.mrope_section[2]))
+
     def forward(self, tokens, want_logits: bool):
         c, h = self.cfg, self.cfg.hidden
         m = len(tokens)
@@ -70,12 +91,7 @@ class RefModel:
         total = self.pos + m
         parts = min(max(-(-total // 256), 1), 64) if m <= 4 else 1  # engine.rs:827
         st = StepU(m, self.pos, parts, 0)
-        # embed (engine.rs:777-790): stream 0 the dequantized row, stream 1 zero
-        eq, es, _, _ = self.q("embed")
-        x = np.zeros(m * 2 * h, np.float32)
-        codes = eq.view(np.int8).astype(np.float32)
-        for i, t in enumerate(tokens):
-            x[i * 2 * h:i * 2 * h + h] = codes[t * h:(t + 1) * h] * np.repeat(es[t * h // 32:(t + 1) * h // 32], 32)
+        x = self.embed(tokens)
         rpos = np.repeat(np.arange(self.pos, self.pos + m, dtype=np.uint32)[:, None], 4, 1).reshape(-1).copy()
         coef = np.zeros(m * 8, np.float32)
         xn = np.zeros(m * h, np.float32)
@@ -105,9 +121,7 @@ class RefModel:
             if c.full_attention[li]:
                 stride = c.attn_proj_rows
                 self.mat(st, L + "qkv", xn, h, proj, stride)
-                ap = AttnP(c.n_heads, c.n_kv_heads, c.rot_dim, stride, c.rope_theta, c.eps,
-                           float(np.float32(1.0) / np.sqrt(np.float32(c.head_dim))),
-                           ((3 * c.mrope_section[1]) << 16) | (3 * c.mrope_section[2]))
+                ap = self.attn_p()
                 kc, vc = self.kc[full_slot], self.vc[full_slot]
                 wr.attn_prep(st, ap, proj, qbuf, kc, vc, self.f(L + "qk_norm"), rpos)
                 wr.attend(st, ap, proj, qbuf, kc, vc, attn_out, partial)
@@ -144,5 +158,60 @@ class RefModel:
             logits = np.zeros(c.vocab, np.float32)
             self.mat(st, "lm_head", hid, h, logits, c.vocab, m_one=1, x_off=m * h)
         self.hlast = hid[m * h:(m + 1) * h].copy()
+        self.hid, self.hid_rows = hid, m
         self.pos += m
+        return logits
+
+    def mtp(self, r0: int, tokens, pos, slot0: int, draft: bool):
+        """Engine::mtp: pairs (hidden row r0 + i of the last step, tokens[i]) into MTP cache
+        slots slot0.., rotary positions pos [n][3]; with draft, the MTP's logits and argmax."""
+        c, h = self.cfg, self.cfg.hidden
+        n = len(tokens)
+        assert n and r0 + n <= self.hid_rows + 1
+        logits = None
+        for c0 in range(0, n, CHUNK):
+            c1 = min(c0 + CHUNK, n)
+            m = c1 - c0
+            total = slot0 + c1
+            parts = min(max(-(-total // 256), 1), 64) if m <= 4 else 1
+            st = StepU(m, slot0 + c0, parts, 0)
+            mx = self.embed(tokens[c0:c1])
+            rpos = np.array([[p[0], p[1], p[2], 0] for p in pos[c0:c1]], np.uint32).reshape(-1).copy()
+            p0 = self.layer_p(0)
+            coef = np.zeros(m * 8, np.float32)
+            xn = np.zeros(m * h, np.float32)
+            hn = np.zeros(m * h, np.float32)
+            branch = np.zeros(m * h, np.float32)
+            proj = np.zeros(m * max(c.attn_proj_rows, 2 * c.intermediate), np.float32)
+            act = np.zeros(m * c.intermediate, np.float32)
+            qbuf = np.zeros(m * c.q_dim, np.float32)
+            attn_out = np.zeros(m * c.q_dim, np.float32)
+            partial = np.zeros(m * c.n_heads * parts * 258, np.float32)
+            wr.branch_norm(st, p0, mx, coef, self.f("mtp.norm_e"), xn, m)  # pre (engine.rs:527)
+            ph = self.layer_p(0)
+            ph.x_stride = h
+            rows = np.ascontiguousarray(self.hid[(r0 + c0) * h:(r0 + c0 + m) * h])
+            wr.branch_norm(st, ph, rows, coef, self.f("mtp.norm_h"), hn, m)  # norm_h (engine.rs:736-747)
+            # engine.rs:549-566
+            self.mat(st, "mtp.fc_e", xn, h, mx, 2 * h)
+            self.mat(st, "mtp.fc_h", hn, h, branch, h)
+            wr.merge(st, p0, mx, coef, branch)
+            wr.branch_norm(st, p0, mx, coef, self.f("mtp.in_ln"), xn, m)
+            self.mat(st, "mtp.qkv", xn, h, proj, c.attn_proj_rows)
+            ap = self.attn_p()
+            wr.attn_prep(st, ap, proj, qbuf, self.mkc, self.mvc, self.f("mtp.qk_norm"), rpos)
+            wr.attend(st, ap, proj, qbuf, self.mkc, self.mvc, attn_out, partial)
+            if parts > 1:
+                wr.attn_combine(st, ap, proj, partial, attn_out)
+            self.mat(st, "mtp.o_proj", attn_out, c.q_dim, branch, h)
+            wr.merge(st, p0, mx, coef, branch)
+            wr.branch_norm(st, p0, mx, coef, self.f("mtp.post_ln"), xn, m)
+            self.mat(st, "mtp.gate_up", xn, h, proj, 2 * c.intermediate)
+            wr.swiglu(st, p0, proj, act)
+            self.mat(st, "mtp.down", act, c.intermediate, branch, h)
+            wr.merge(st, p0, mx, coef, branch)
+            if c1 == n and draft:  # head (engine.rs:567-570): the last row, lm_head
+                wr.branch_norm(st, self.layer_p(0, True), mx, coef, self.f("mtp.norm"), xn, 1)
+                logits = np.zeros(c.vocab, np.float32)
+                self.mat(st, "lm_head", xn, h, logits, c.vocab, m_one=1)
         return logits

@@ -35,3 +35,27 @@ def test_reference_kernels_forward_matches_oracle_model():
             break
         lo, lr = om.forward([tok], True), rm.forward([tok], True)
     om.close()
+
+
+def test_reference_kernels_mtp_matches_oracle_model():
+    """Engine::mtp (engine.rs:700-774) from the reference's kernels: the MTP layer over a
+    prompt's hidden rows, then a one-pair draft, logits bit-identical to the oracle's."""
+    from wgslref_model import RefModel
+
+    cfg = small()
+    ctx = 64
+    om = orc.OracleModel(cfg, ctx, seed=4, mtp=True)
+    rm = RefModel(cfg, ctx, om)
+    prompt = [(29 + 104729 * i) % cfg.vocab for i in range(9)]
+    lo, lr = om.forward(prompt, True), rm.forward(prompt, True)
+    assert np.array_equal(lo, lr)
+    nxt = int(np.argmax(lo))
+    # pairs (hidden row i + 1, token i + 1): the prompt's rows with the tokens that follow them
+    toks = prompt[1:] + [nxt]
+    pos = [[i, i, i] for i in range(len(toks))]
+    d_o = om.mtp(1, toks, pos, 0, True)
+    lr_m = rm.mtp(1, toks, pos, 0, True)
+    lo_m = om.mtp_logits()
+    assert np.array_equal(lo_m.view(np.uint32), lr_m.view(np.uint32))
+    assert d_o == int(np.argmax(lr_m))
+    om.close()
