@@ -1283,6 +1283,13 @@ ORC_API const void* orc_model_tensor(void* hm, const char* name, size_t* rows, s
   return nullptr;
 }
 
+// The quantization of a named matrix (SNL_Q8_0 / SNL_Q4_0), or -1.
+ORC_API int orc_model_tensor_dtype(void* hm, const char* name) {
+  const Model& M = *(const Model*)hm;
+  auto it = M.qw.find(name);
+  return it == M.qw.end() ? -1 : it->second.dtype;
+}
+
 // forward_mm (engine.rs:801-936).
 ORC_API int orc_model_forward_mm(void* hm, const uint32_t* tokens, size_t n, const uint32_t* pos3,
                                  const uint32_t* embed_idx, const float* embeds, size_t n_embeds, size_t logit_rows,

@@ -51,6 +51,7 @@ _SIG = {
     "orc_model_hid_rows": (sz, [vp]),
     "orc_model_read_hidden": (i32, [vp, sz, sz, vp]),
     "orc_model_tensor": (vp, [vp, C.c_char_p, P(sz), P(sz), P(vp)]),
+    "orc_model_tensor_dtype": (i32, [vp, C.c_char_p]),
     "orc_model_forward_mm": (i32, [vp, vp, sz, vp, vp, vp, sz, sz, i32, vp]),
     "orc_model_mtp": (i32, [vp, sz, vp, sz, vp, sz, i32, vp]),
     "orc_model_mtp_logits": (vp, [vp]),
@@ -264,6 +265,10 @@ class OracleModel:
         if not ptr:
             raise KeyError(name)
         return ptr, int(r.value), int(c.value), s.value
+
+    def tensor_dtype(self, name: str) -> int:
+        """SNL_Q8_0 / SNL_Q4_0 of a matrix, -1 for a vector or an unknown name."""
+        return int(lib().orc_model_tensor_dtype(self._h, name.encode()))
 
     def forward_mm(self, tokens, pos=None, logit_rows=0, ckpt=False, embeds=()):
         toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32))

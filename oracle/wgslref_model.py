@@ -6,8 +6,8 @@ prefill chunk), restated in Python over the reference's WGSL kernels translated 
 on the same tensors. A test compares its logits with the oracle model's: the same graph,
 one side built from the reference's kernel code.
 
-Steps of at most one prefill chunk (512 rows) per call; Q8_0 weights (the oracle model's
-default quantization). `mtp` restates Engine::mtp (engine.rs:700-774) over the MTP layer
+Steps of at most one prefill chunk (512 rows) per call; each matrix in the oracle model's
+quantization (Q8_0, or Q4_0 for the matrices a Q4_0 conversion quantizes). `mtp` restates Engine::mtp (engine.rs:700-774) over the MTP layer
 that engine.rs:495-580 builds, when the oracle model has one.
 """
 from __future__ import annotations
@@ -50,9 +50,11 @@ class RefModel:
     # -- weights of the oracle model --
     def q(self, name: str):
         ptr, rows, cols, s = self.w.tensor(name)
-        q = np.ctypeslib.as_array((C.c_uint8 * (rows * cols)).from_address(ptr)).copy()
+        dt = self.w.tensor_dtype(name)
+        nbytes = rows * cols if dt == Q8 else rows * cols // 2
+        q = np.ctypeslib.as_array((C.c_uint8 * nbytes).from_address(ptr)).copy()
         sc = np.ctypeslib.as_array((C.c_float * (rows * cols // 32)).from_address(s)).copy()
-        return q, sc, rows, cols
+        return q, sc, rows, cols, dt
 
     def f(self, name: str) -> np.ndarray:
         ptr, _, n, _ = self.w.tensor(name)
@@ -65,13 +67,14 @@ class RefModel:
 
     def mat(self, st, name, x, x_stride, y, y_stride, m_one=0, x_off=0):
         """engine.rs:336-363 (one chunk: n_off 0)."""
-        q, s, rows, cols = self.q(name)
-        wr.mat(Q8, st, MatP(rows, cols, x_off, x_stride, 0, y_stride, 0, m_one), x, q, s, y)
+        q, s, rows, cols, dt = self.q(name)
+        wr.mat(dt, st, MatP(rows, cols, x_off, x_stride, 0, y_stride, 0, m_one), x, q, s, y)
 
     def embed(self, tokens) -> np.ndarray:
         """engine.rs:777-790: stream 0 the dequantized row, stream 1 zero."""
         h = self.cfg.hidden
-        eq, es, _, _ = self.q("embed")
+        eq, es, _, _, dt = self.q("embed")
+        assert dt == Q8, "the embedding stays Q8_0 (convert.rs)"
         x = np.zeros(len(tokens) * 2 * h, np.float32)
         codes = eq.view(np.int8).astype(np.float32)
         for i, t in enumerate(tokens):

@@ -2,7 +2,7 @@
 
 oracle/wgslref_model.py composes the reference's WGSL kernels (translated to C++ and run
 on the host cores) in the op order of src/engine.rs:383-493 and forward_mm (:801-936),
-on the oracle model's weights. Every kernel call of the reduced model's graph (DeltaNet
+on the oracle model's weights (Q8_0, and the Q4_0 model of BASELINE configs[4]). Every kernel call of the reduced model's graph (DeltaNet
 and attention layers, the mHC loop, split-key attention with several parts, the LM head)
 must give the oracle's bits, through a prefill and greedy decode steps.
 """
@@ -16,12 +16,13 @@ from sensenova_b200.config import small
 pytestmark = pytest.mark.skipif(not wr.available(), reason="reference tree absent")
 
 
-def test_reference_kernels_forward_matches_oracle_model():
+@pytest.mark.parametrize("quant", [1, 2], ids=["q8_0", "q4_0"])
+def test_reference_kernels_forward_matches_oracle_model(quant):
     from wgslref_model import RefModel
 
     cfg = small()
     ctx = 320
-    om = orc.OracleModel(cfg, ctx, seed=3)
+    om = orc.OracleModel(cfg, ctx, seed=3, quant=quant)
     rm = RefModel(cfg, ctx, om)
     prompt = [(17 + 7919 * i) % cfg.vocab for i in range(258)]  # one tiled-matmul chunk
     lo, lr = om.forward(prompt, True), rm.forward(prompt, True)
