@@ -22,7 +22,7 @@ HERE = Path(__file__).resolve().parent
 if str(HERE) not in sys.path:
     sys.path.insert(0, str(HERE))
 import wgslref as wr  # noqa: E402
-from sensenova_b200.ffi import AttnP, LayerP, LinP, MatP, StepU  # noqa: E402
+from sensenova_b200.ffi import AttnP, LayerP, LinP, MatP, StepU, VisP  # noqa: E402
 
 Q8 = 1
 CHUNK = 512  # engine.rs prefill_chunk
@@ -218,3 +218,93 @@ class RefModel:
                 logits = np.zeros(c.vocab, np.float32)
                 self.mat(st, "lm_head", xn, h, logits, c.vocab, m_one=1)
         return logits
+
+
+class RefVision:
+    """Vision::encode (src/vision.rs:195-343) over the reference's vision.wgsl and matmul
+    kernels (translated), on an oracle vision tower's weights: the op order of
+    vision.rs:252-290 per frame, the position embedding of :160-193 on the host in f32."""
+
+    EPS, GELU_TANH, GELU_ERF = 1e-6, 1, 2  # vision.rs:53-55
+
+    def __init__(self, cfg, tower):
+        self.cfg, self.t = cfg, tower
+
+    def f(self, name):
+        return self.t.tensor(name)[1]
+
+    def mat(self, name, x, rows, y, y_stride):
+        """mat_ops (vision.rs:345-380): x_stride = the weight's k, one chunk."""
+        dt, q, s, n, k = self.t.tensor(name)
+        wr.mat(dt, StepU(rows, 0, 1, 0), MatP(n, k, 0, k, 0, y_stride, 0, 0), x, q.view(np.uint8), s, y)
+
+    def pos_embed(self, h, w):
+        c = self.cfg
+        side, hid, m = c.pos_side, c.hidden, c.merge
+        f32 = np.float32
+
+        def lin(n):
+            return [f32(0) if n == 1 else f32(f32(side - 1) * f32(i)) / f32(n - 1) for i in range(n)]
+
+        hs, ws = lin(h), lin(w)
+        pos = self.f("v.pos")
+        out = np.zeros((h * w, hid), np.float32)
+        for token in range(h * w):
+            blk, intra = token // (m * m), token % (m * m)
+            r = (blk // (w // m)) * m + intra // m
+            cc = (blk % (w // m)) * m + intra % m
+            fh, fw = int(hs[r]), int(ws[cc])
+            ch, cw = min(fh + 1, side - 1), min(fw + 1, side - 1)
+            dh, dw = f32(hs[r] - f32(fh)), f32(ws[cc] - f32(fw))
+            one = f32(1)
+            corners = [(fh * side + fw, f32((one - dh) * (one - dw))), (fh * side + cw, f32((one - dh) * dw)),
+                       (ch * side + fw, f32(dh * (one - dw))), (ch * side + cw, f32(dh * dw))]
+            for idx, wt in corners:
+                out[token] = out[token] + pos[idx * hid:(idx + 1) * hid] * wt
+        return out.reshape(-1)
+
+    def encode(self, patches, frames, h, w):
+        c = self.cfg
+        n, hid = h * w, c.hidden
+        nq = n // (c.merge * c.merge)
+        pd = 3 * c.temporal_patch * c.patch * c.patch
+        md, ip = hid * c.merge * c.merge, c.intermediate_padded
+        pos = self.pos_embed(h, w)
+        x = np.zeros(n * hid, np.float32)
+        xn, tmp, att = np.zeros_like(x), np.zeros_like(x), np.zeros_like(x)
+        qkv = np.zeros(max(n * 3 * hid, nq * c.out_hidden), np.float32)
+        mlp = np.zeros(max(n * ip, nq * md), np.float32)
+
+        def norm(wname):
+            xn[:] = wr.vis_layer_norm(VisP(n, hid, 0, 0, self.EPS, 0, 0, 0), x, self.f(wname))
+
+        def epi(a, b, bname, e, rows, cols, mode, act):
+            wr.vis_epilogue(VisP(rows, cols, mode, act, 0.0, 0, 0, 0), a, b, self.f(bname), e)
+
+        out = []
+        for fr in range(frames):
+            pin = np.ascontiguousarray(patches.reshape(-1)[fr * n * pd:(fr + 1) * n * pd], np.float32)
+            self.mat("v.patch", pin, n, tmp, hid)
+            epi(tmp, x, "v.patch_b", pos, n, hid, 2, 0)
+            for i in range(c.depth):
+                b = f"v{i}."
+                norm(b + "n1")
+                self.mat(b + "qkv", xn, n, qkv, 3 * hid)
+                epi(qkv, None, b + "qkv_b", None, n, 3 * hid, 0, 0)
+                rp = VisP(n, 0, 0, 0, 0.0, w, c.n_heads, 0)
+                wr.vis_rope(rp, qkv)
+                att[:] = wr.vis_attend(rp, qkv[:n * 3 * hid]).reshape(-1)
+                self.mat(b + "proj", att, n, tmp, hid)
+                epi(tmp, x, b + "proj_b", None, n, hid, 1, 0)
+                norm(b + "n2")
+                self.mat(b + "fc1", xn, n, mlp, ip)
+                epi(mlp, None, b + "fc1_b", None, n, ip, 0, self.GELU_TANH)
+                self.mat(b + "fc2", mlp, n, tmp, hid)
+                epi(tmp, x, b + "fc2_b", None, n, hid, 1, 0)
+            norm("vm.norm")
+            self.mat("vm.fc1", xn, nq, mlp, md)
+            epi(mlp, None, "vm.fc1_b", None, nq, md, 0, self.GELU_ERF)
+            self.mat("vm.fc2", mlp, nq, qkv, c.out_hidden)
+            epi(qkv, None, "vm.fc2_b", None, nq, c.out_hidden, 0, 0)
+            out.append(qkv[:nq * c.out_hidden].copy())
+        return np.concatenate(out).reshape(frames * nq, c.out_hidden)

@@ -60,3 +60,19 @@ def test_reference_kernels_mtp_matches_oracle_model():
     assert np.array_equal(lo_m.view(np.uint32), lr_m.view(np.uint32))
     assert d_o == int(np.argmax(lr_m))
     om.close()
+
+
+@pytest.mark.parametrize("frames,h,w", [(1, 4, 6), (2, 4, 4)])
+def test_reference_kernels_vision_encode_matches_oracle(frames, h, w):
+    """Vision::encode (vision.rs:195-343) from the reference's vision and matmul kernels on
+    the oracle tower's weights: output rows bit-identical to the oracle's encode."""
+    from sensenova_b200.vision import small_vision
+    from wgslref_model import RefVision
+
+    cfg = small_vision()
+    ov = orc.OracleVision(cfg, seed=5)
+    patches = np.random.default_rng(h * w + frames).standard_normal((frames, h * w, cfg.patch_dim())).astype(np.float32)
+    want = ov.encode(patches, frames, h, w)
+    got = RefVision(cfg, ov).encode(patches, frames, h, w)
+    assert np.array_equal(want.view(np.uint32), got.view(np.uint32))
+    ov.close()
